@@ -1,0 +1,209 @@
+"""CPU oracle for the attention / Gated-DeltaNet hot path -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs import this package, and only as the checker
+(or as the timed CPU arm). The product package larder_b200 never imports it and has no CPU path.
+
+Two layers:
+  * liboracle.so (oracle.cpp): a C++ restatement of the reference's CPU kernels CpuAttn and CpuGdn
+    (cpu_ext/cpu_kern.cpp:404-485, :493-659), OpenMP-threaded over all host cores, f32 arithmetic in the
+    reference's order. This is the f32 oracle the GPU kernels are graded against and the timed CPU baseline.
+  * attn_ref64 / gdn_ref64: float64 numpy restatements of the reference tests' own oracles
+    (tests/test_cpu_kern.py:141-149 for attention, tests/test_gdn_cuda.py:29-45 for the recurrence), used to pin
+    liboracle.so against the reference's tolerances (tests/test_cpu_kern.py:25, :129-133, :167-169).
+
+Arrays are numpy. bf16 has no numpy dtype, so bf16 data travels as uint16 bit patterns (`BF16` marks them);
+helpers convert with round-to-nearest-even as the reference does (cpu_kern.cpp:48-55).
+"""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+
+F32, BF16, F16 = 0, 1, 2
+MASK_NONE, MASK_CAUSAL, MASK_ARRAY = 0, 1, 2
+
+_lib = None
+
+
+def build(force=False):
+    """Compile liboracle.so with oracle/Makefile (g++ + OpenMP)."""
+    if force or not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < os.path.getmtime(
+            os.path.join(HERE, "oracle.cpp")):
+        subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        p, i, f, i64p = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.POINTER(ctypes.c_int64)
+        L.orc_attn.argtypes = [p, i64p, i, p, i64p, i, p, i64p, i, p, i64p, p, i, i, i, i, i, i, i, i, f, i, i]
+        L.orc_attn.restype = i
+        L.orc_gdn.argtypes = [p, p, i, p, i, p, i, i, p, i, p, p, p, i, p, i, i, i, i, i, i, i]
+        L.orc_gdn.restype = i
+        L.orc_default_threads.restype = i
+        _lib = L
+    return _lib
+
+
+def default_threads():
+    """Threads the oracle uses by default: every host core it can see (the reference uses physical cores,
+    cpu_kernels.py:14-22, :91)."""
+    return int(lib().orc_default_threads())
+
+
+# ---------------------------------------------------------------------------------------------- dtype helpers
+
+def f32_to_bf16(x):
+    """float32 array -> uint16 bf16 bit patterns, round to nearest even (NaN kept quiet)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    return np.where(nan, ((u >> 16) | 0x40).astype(np.uint16), r)
+
+
+def bf16_to_f32(h):
+    return (np.asarray(h, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def to_f32(a, dt):
+    if dt == F32:
+        return np.asarray(a, dtype=np.float32)
+    if dt == BF16:
+        return bf16_to_f32(a)
+    return np.asarray(a).view(np.float16).astype(np.float32)
+
+
+def from_f32(x, dt):
+    """float32 -> the storage of dtype code dt (uint16 bits for bf16 and f16)."""
+    if dt == F32:
+        return np.ascontiguousarray(x, dtype=np.float32)
+    if dt == BF16:
+        return f32_to_bf16(x)
+    return np.ascontiguousarray(x, dtype=np.float32).astype(np.float16).view(np.uint16)
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _strides(a, n=3):
+    """Element strides of the first n axes of a numpy array."""
+    return (ctypes.c_int64 * n)(*[s // a.itemsize for s in a.strides[:n]])
+
+
+# ---------------------------------------------------------------------------------------------- f32 oracle
+
+def attn(q, k, v, scale, dt, mask_kind=MASK_NONE, mask=None, out_dt=None, threads=0):
+    """softmax(scale q k^T + mask) v through liboracle.so (CpuAttn's arithmetic).
+
+    q [B, Hq, T, D], k [B, Hkv, N, D], v [B, Hkv, N, Dv] numpy arrays in storage dtype `dt` (uint16 bits for
+    bf16/f16); any strides with a unit last stride (slices of a longer cache buffer are fine). mask: bool [T, N]
+    (kind 2). Returns [B, Hq, T, Dv] in storage dtype out_dt (default dt)."""
+    out_dt = dt if out_dt is None else out_dt
+    for a in (q, k, v):
+        assert a.strides[-1] == a.itemsize, "last axis must have unit stride"
+    B, Hq, T, D = q.shape
+    Hkv, N, Dv = k.shape[1], k.shape[2], v.shape[3]
+    o = np.zeros((B, Hq, T, Dv), dtype=np.float32 if out_dt == F32 else np.uint16)
+    m8 = None
+    ms = (ctypes.c_int64 * 2)(0, 0)
+    if mask_kind == MASK_ARRAY:
+        m8 = np.ascontiguousarray(mask, dtype=np.uint8).reshape(T, N)
+        ms = (ctypes.c_int64 * 2)(N, 1)
+    rc = lib().orc_attn(_ptr(q), _strides(q), dt, _ptr(k), _strides(k), dt, _ptr(v), _strides(v), dt, _ptr(m8), ms,
+                        _ptr(o), out_dt, B, Hq, T, D, Hkv, N, Dv, float(scale), int(mask_kind), int(threads))
+    if rc != 0:
+        raise ValueError(f"oracle attn: unsupported shape {q.shape} {k.shape}")
+    return o
+
+
+def gdn(q, k, v, g, beta, state, dt, v_dt=None, g_dt=F32, b_dt=None, mask=None, threads=0):
+    """The gated delta recurrence through liboracle.so (CpuGdn's arithmetic): returns (y, state_out).
+
+    q, k [B, T, Hk, Dk] and v [B, T, Hv, Dv] in storage dtypes dt / v_dt; g [B, T, Hv] or [B, T, Hv, Dk] (g_dt);
+    beta [B, T, Hv] (b_dt); state [B, Hv, Dv, Dk] float32; mask [B, T] bool or None. y comes back in dt."""
+    v_dt = dt if v_dt is None else v_dt
+    b_dt = dt if b_dt is None else b_dt
+    q, k, v, g, beta = (np.ascontiguousarray(a) for a in (q, k, v, g, beta))
+    state = np.ascontiguousarray(state, dtype=np.float32)
+    B, T, Hk, Dk = q.shape
+    Hv, Dv = v.shape[2], v.shape[3]
+    y = np.zeros((B, T, Hv, Dv), dtype=np.float32 if dt == F32 else np.uint16)
+    s = np.zeros_like(state)
+    m8 = None if mask is None else np.ascontiguousarray(mask, dtype=np.uint8)
+    rc = lib().orc_gdn(_ptr(q), _ptr(k), dt, _ptr(v), v_dt, _ptr(g), g_dt, int(g.ndim == 4), _ptr(beta), b_dt,
+                       _ptr(m8), _ptr(state), _ptr(y), dt, _ptr(s), B, T, Hk, Dk, Hv, Dv, int(threads))
+    if rc != 0:
+        raise ValueError(f"oracle gdn: unsupported shape {q.shape} {v.shape}")
+    return y, s
+
+
+# ---------------------------------------------------------------------------------------------- float64 references
+
+def attn_ref64(q, k, v, scale, mask=None):
+    """tests/test_cpu_kern.py:141-149 in float64: q, k, v float arrays, mask bool [T, N] or None."""
+    q, k, v = (np.asarray(a, dtype=np.float64) for a in (q, k, v))
+    G = q.shape[1] // k.shape[1]
+    k, v = np.repeat(k, G, 1), np.repeat(v, G, 1)
+    s = scale * q @ np.swapaxes(k, -1, -2)
+    if mask is not None:
+        s = np.where(mask, s, -np.inf)
+    mx = s.max(-1, keepdims=True)
+    p = np.exp(s - np.where(np.isfinite(mx), mx, 0.0))
+    den = p.sum(-1, keepdims=True)
+    return (p / np.where(den > 0, den, 1.0)) @ v
+
+
+def causal_mask(T, N):
+    """Bottom-right causal: row t sees keys 0 .. N - T + t (tests/test_cpu_kern.py:159)."""
+    return np.arange(T)[:, None] + N - T >= np.arange(N)[None, :]
+
+
+def gdn_ref64(q, k, v, g, beta, state, mask=None):
+    """tests/test_gdn_cuda.py:29-45 in float64: masked steps skipped (y = 0, state kept)."""
+    q, k, v, g, beta, s = (np.asarray(x, dtype=np.float64) for x in (q, k, v, g, beta, state))
+    B, T, Hk, Dk = q.shape
+    r = v.shape[2] // Hk
+    q, k = np.repeat(q, r, axis=2), np.repeat(k, r, axis=2)
+    m = np.ones((B, T), bool) if mask is None else np.asarray(mask, bool)
+    ys = np.zeros(v.shape)
+    for t in range(T):
+        gt = g[:, t]
+        sn = s * (gt[..., None, None] if gt.ndim == 2 else gt[..., None, :])
+        kv = (sn * k[:, t, :, None, :]).sum(-1)
+        sn = sn + k[:, t, :, None, :] * ((v[:, t] - kv) * beta[:, t, :, None])[..., None]
+        y = (sn * q[:, t, :, None, :]).sum(-1)
+        s = np.where(m[:, t, None, None, None], sn, s)
+        ys[:, t] = np.where(m[:, t, None, None], y, 0.0)
+    return ys, s
+
+
+# ---------------------------------------------------------------------------------------------- seeded inputs
+
+def rms_norm(x, eps=1e-6):
+    """mx.fast.rms_norm(x, None, eps) over the last axis, float32."""
+    x = np.asarray(x, dtype=np.float32)
+    return x / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + np.float32(eps))
+
+
+def softplus(x):
+    x = np.asarray(x, dtype=np.float64)
+    return np.where(x > 20, x, np.log1p(np.exp(np.minimum(x, 20))))
+
+
+def compute_g(A_log, a, dt_bias):
+    """mlx_lm's compute_g, g = exp(-exp(A_log) * softplus(a + dt_bias)) (spelled out in gdn_cuda.py:146-149)."""
+    return np.exp(-np.exp(np.asarray(A_log, np.float64)) * softplus(np.asarray(a, np.float64) +
+                                                                      np.asarray(dt_bias, np.float64))).astype(np.float32)
+
+
+def sigmoid(x):
+    return (1.0 / (1.0 + np.exp(-np.asarray(x, dtype=np.float64)))).astype(np.float32)

@@ -1,0 +1,88 @@
+"""The CPU oracle (oracle/liboracle.so) pinned against the golden vectors: the reference tests' float64 oracles on
+the reference tests' own seeded inputs, with the reference tests' tolerances. Also: the generated inputs still hash
+to the digests stored with the goldens, and a mistake planted in the oracle is caught."""
+import numpy as np
+import pytest
+
+import cases
+import checks
+import oracle
+
+
+@pytest.fixture(scope="module")
+def g():
+    return checks.golden()
+
+
+def test_digests_match(g):
+    for c in cases.attn_cases():
+        assert str(g[f"attn{c['case']}.digest"]) == cases.digest(c["q"], c["kc"], c["vc"], c["rnd"])
+    c = cases.gdn_cpu_case()
+    assert str(g["gdncpu.digest"]) == cases.digest(c["q"], c["k"], c["v"], c["g"], c["beta"], c["state"])
+    for i in range(len(cases.GDN_CUDA_CASES)):
+        c = cases.gdn_cuda_case(i)
+        assert str(g[f"gdncuda{i}.digest"]) == cases.digest(c["q"], c["k"], c["v"], c["g"], c["beta"], c["state"],
+                                                            c["mask"])
+
+
+@pytest.mark.parametrize("kind", ["none", "causal", "array"])
+def test_oracle_attn_golden(kind):
+    """tests/test_cpu_kern.py:151-169 against liboracle.so: decode (split keys), causal rows, array mask, K/V as
+    slices of a longer cache buffer."""
+    for c in cases.attn_cases():
+        mk = {"none": oracle.MASK_NONE, "causal": oracle.MASK_CAUSAL, "array": oracle.MASK_ARRAY}[kind]
+        for threads in (2, 0):
+            o = oracle.attn(c["q"], c["k"], c["v"], c["scale"], c["dt"], mk, c["rnd"], threads=threads)
+            got = oracle.to_f32(o, c["dt"])
+            checks.golden_close(got, f"attn{c['case']}.{kind}", 1e-5, ulp=checks.ULP[c["dt"]],
+                                what=f"case {c['case']} threads {threads}")
+
+
+def test_oracle_gdn_cpu_golden():
+    """tests/test_cpu_kern.py:103-134: state rel err < 1e-5, y within 2^-8 |Y| + 1e-5 max|Y|."""
+    c = cases.gdn_cpu_case()
+    y, s = oracle.gdn(c["q"], c["k"], c["v"], c["g"], c["beta"], c["state"], c["dt"], g_dt=c["g_dt"], b_dt=c["b_dt"])
+    checks.golden_close(oracle.to_f32(y, c["dt"]), "gdncpu.y", 1e-5, ulp=2.0 ** -8, what="y")
+    checks.golden_close(s, "gdncpu.s", 1e-5, what="state")
+
+
+@pytest.mark.parametrize("i", range(len(cases.GDN_CUDA_CASES)))
+def test_oracle_gdn_cuda_cases_golden(i):
+    """tests/test_gdn_cuda.py:95-99's cases (scalar and per-Dk gate, masks, GQA) against the float64 recurrence,
+    with the CPU kernel's bar; a masked position writes y = 0."""
+    c = cases.gdn_cuda_case(i)
+    y, s = oracle.gdn(c["q"], c["k"], c["v"], c["g"], c["beta"], c["state"], c["dt"], g_dt=c["g_dt"],
+                      b_dt=c["b_dt"], mask=c["mask"])
+    yf = oracle.to_f32(y, c["dt"])
+    checks.golden_close(yf, f"gdncuda{i}.y", 1e-5, ulp=2.0 ** -8, what=f"case {i} y")
+    checks.golden_close(s, f"gdncuda{i}.s", 1e-5, what=f"case {i} state")
+    if c["mask"] is not None:
+        assert not yf[~c["mask"]].any(), "a masked position wrote y"
+
+
+def test_planted_mistake_is_caught():
+    """A mistake planted in the oracle (scale off by 1%, then the GQA head map shifted) fails the golden check."""
+    c = next(cases.attn_cases())
+    o = oracle.attn(c["q"], c["k"], c["v"], c["scale"] * 1.01, c["dt"], oracle.MASK_NONE)
+    with pytest.raises(AssertionError):
+        checks.golden_close(oracle.to_f32(o, c["dt"]), "attn0.none", 1e-5, ulp=checks.ULP[c["dt"]])
+    k2 = np.ascontiguousarray(c["k"][:, ::-1])
+    v2 = np.ascontiguousarray(c["v"][:, ::-1])
+    o = oracle.attn(c["q"], k2, v2, c["scale"], c["dt"], oracle.MASK_NONE)
+    with pytest.raises(AssertionError):
+        checks.golden_close(oracle.to_f32(o, c["dt"]), "attn0.none", 1e-5, ulp=checks.ULP[c["dt"]])
+
+
+def test_fully_masked_leading_block_is_finite():
+    """A key range whose first 32-key block is fully masked: the oracle adds nothing for it (the reference's
+    CpuAttn would carry -inf into its accumulator there, cpu_kern.cpp:583, :601)."""
+    rng = np.random.default_rng(7)
+    q = rng.normal(0, 1, (1, 2, 2, 64)).astype(np.float32)
+    k = rng.normal(0, 1, (1, 1, 96, 64)).astype(np.float32)
+    v = rng.normal(0, 1, (1, 1, 96, 64)).astype(np.float32)
+    m = np.zeros((2, 96), bool)
+    m[:, 40:] = True
+    o = oracle.attn(q, k, v, 0.125, oracle.F32, oracle.MASK_ARRAY, m, threads=1)
+    ref = oracle.attn_ref64(q, k, v, 0.125, m)
+    assert np.isfinite(o).all()
+    checks.attn_close(o, ref, oracle.F32)
