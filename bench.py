@@ -1,0 +1,405 @@
+#!/usr/bin/env python3
+"""Benchmark of the attention / Gated-DeltaNet hot path on B200, one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--section decode,prefill,gdn]
+
+Headline (`value`): decode KV-read GB/s on BASELINE.json's configs[1] -- batch 16, 32 query / 4 KV heads x 128,
+bf16 KV cache with per-sequence lengths uniform in [1024, 8192], one query token each. A step is one split-KV decode
+call over the whole batch. With N GPUs every rank runs its own batch of 16 sequences (weak scaling over independent
+sequences, no data-path collective); value = KV bytes read by all ranks / max-over-ranks device time.
+
+Extra objects on the same line:
+  prefill  configs[2]: 8192-token causal prefill in four 2048-row chunks (wide cut), 16/2 heads x 256, bf16, with
+           the sigmoid output gate; TFLOP/s over the causal pairs only (5.498e11 FLOP a step)
+  gdn      configs[3]: a Gated-DeltaNet decode step at B = 16 (Hk 16, Hv 32, 128 x 128) -- state GB/s -- and the
+           8192-token prefill
+Inputs are seeded synthetic data with the configs' shapes and distributions (no dataset is involved).
+`--impl reference` times the reference's CPU implementation (the oracle restatement of cpu_ext/cpu_kern.cpp) on
+the same workload and prints the same line with "impl": "reference".
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "prefill attn TFLOP/s & decode KV-read GB/s at 8k ctx, 1/2/4/8 B200, % peak"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return {k: float(p[k]) for k in PEAKS_FALLBACK}, "measured"
+    except (OSError, KeyError, ValueError):
+        return dict(PEAKS_FALLBACK), "fallback"
+
+
+# ------------------------------------------------------------------------------------------------ workloads
+
+def decode_inputs(torch, dev, seed, copies):
+    """Config 2, `copies` independent caches so that consecutive steps read different memory (> L2)."""
+    g = torch.Generator().manual_seed(seed)
+    B, Hq, Hkv, D, cap = 16, 32, 4, 128, 8192
+    lens = torch.randint(1024, 8193, (B,), generator=g)
+    sets = []
+    for _ in range(copies):
+        q = torch.randn(B, Hq, 1, D, generator=g).to(torch.bfloat16)
+        k = torch.empty(B, Hkv, cap, D, dtype=torch.bfloat16, device=dev)
+        v = torch.empty(B, Hkv, cap, D, dtype=torch.bfloat16, device=dev)
+        k.normal_(generator=torch.Generator(device=dev).manual_seed(seed + 1))
+        v.normal_(generator=torch.Generator(device=dev).manual_seed(seed + 2))
+        sets.append((q, k, v))
+    return lens, sets, (B, Hq, Hkv, D)
+
+
+def decode_bytes(lens, Hkv, D, B, Hq):
+    kv = int(lens.sum()) * Hkv * D * 2 * 2
+    qo = 2 * B * Hq * D * 2
+    return kv, kv + qo
+
+
+class Clocks:
+    """nvidia-smi sampled every 200 ms while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait(timeout=5)
+
+    def summary(self):
+        sm = [float(r[1]) for r in self.rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) >= 9 for i in range(4) if "Active" in r[5 + i]})
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm_sorted = sorted(sm)
+        return {"sm_mhz": sm_sorted[len(sm_sorted) // 2], "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(sm)}
+
+
+def cuda_time(torch, fn, steps, stream):
+    """Device time of `steps` calls of fn (ms, CUDA events on the launching stream)."""
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        fn(i)
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1)
+
+
+# ------------------------------------------------------------------------------------------------ our arm
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from larder_b200 import ops
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    stream = torch.cuda.current_stream(dev)
+    pk, pk_kind = peaks()
+    sections = set(args.section.split(","))
+
+    def barrier_sync():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    out = {"metric": METRIC, "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1), config shapes)"}
+
+    # ---------------------------------------------------------------- decode (headline)
+    copies = 4
+    lens, sets, (B, Hq, Hkv, D) = decode_inputs(torch, dev, 1000 + rank, copies)
+    kv_len = lens.to(torch.int32).to(dev)
+    kv_bytes, alg_bytes = decode_bytes(lens, Hkv, D, B, Hq)
+    q_dev = [s[0].to(dev) for s in sets]
+    o_dev = torch.empty(B, Hq, 1, D, dtype=torch.bfloat16, device=dev)
+    split = args.split
+
+    def dec(i):
+        _, k, v = sets[i % copies]
+        ops.attn_decode(q_dev[i % copies], k, v, D ** -0.5, kv_len=kv_len, split=split, out=o_dev)
+
+    for i in range(args.warmup):
+        dec(i)
+    barrier_sync()
+    with Clocks(local) as clk:
+        ms = cuda_time(torch, dec, args.steps, stream)
+    barrier_sync()
+    ms = max_over_ranks(ms)
+    per = ms / args.steps
+    gbs = world * kv_bytes / (per * 1e-3) / 1e9
+    kern_gbs = alg_bytes / (per * 1e-3) / 1e9
+    out.update({"value": round(gbs, 1), "unit": "GB/s", "ms_per_step": round(per, 5)})
+    out["config"] = {"workload": "configs[1] GQA decode: B=16/rank, 32q/4kv x 128, bf16 KV, lengths U[1024,8192]",
+                     "global_batch": 16 * world, "kv_lens_sum_per_rank": int(lens.sum()), "parallelism": f"dp{world}",
+                     "split": split or "auto", "l2": f"{copies} rotating KV caches ({copies} x "
+                     f"{kv_bytes / 1e6:.0f} MB read) so consecutive steps miss L2"}
+    out["roofline"] = {"bound": "hbm", "achieved": round(kern_gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                       "frac": round(kern_gbs / pk["hbm_gbs"], 4), "traffic": None, "peak_kind": pk_kind,
+                       "kernel": "lb2::decode::decode_kernel<bf16,128,1>",
+                       "algorithmic_bytes_per_launch": alg_bytes}
+    out["clocks"] = clk.summary()
+    out["gpu_launches"] = args.steps  # one decode kernel a step (the split merge runs inside it)
+
+    # e2e through the public API: q from pinned host memory each step, o read back each step
+    q_host = [s[0].pin_memory() for s in sets]
+    o_host = torch.empty(B, Hq, 1, D, dtype=torch.bfloat16).pin_memory()
+
+    def dec_e2e(i):
+        _, k, v = sets[i % copies]
+        qd = q_host[i % copies].to(dev, non_blocking=True)
+        o = ops.attn_decode(qd, k, v, D ** -0.5, kv_len=kv_len, split=split)
+        o_host.copy_(o, non_blocking=True)
+
+    for i in range(args.warmup):
+        dec_e2e(i)
+    barrier_sync()
+    ms_e2e = max_over_ranks(cuda_time(torch, dec_e2e, args.steps, stream))
+    barrier_sync()
+    per_e2e = ms_e2e / args.steps
+    out["e2e"] = {"value": round(world * kv_bytes / (per_e2e * 1e-3) / 1e9, 1), "unit": "GB/s",
+                  "h2d_bytes_per_step": q_host[0].numel() * 2, "d2h_bytes_per_step": o_host.numel() * 2,
+                  "ms_per_step": round(per_e2e, 5), "api": "larder_b200.ops.attn_decode"}
+    del sets, q_dev
+    torch.cuda.empty_cache()
+
+    # ---------------------------------------------------------------- prefill
+    if "prefill" in sections:
+        try:
+            out["prefill"] = bench_prefill(torch, ops, dev, rank, world, args, stream, pk, pk_kind, barrier_sync,
+                                           max_over_ranks)
+        except Exception as e:  # reported, never hidden
+            out["prefill"] = {"error": f"{type(e).__name__}: {e}"}
+    if "gdn" in sections:
+        try:
+            out["gdn"] = bench_gdn(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_over_ranks)
+        except Exception as e:
+            out["gdn"] = {"error": f"{type(e).__name__}: {e}"}
+    st = ops.status(local)
+    out["device_status"] = st
+
+    # ---------------------------------------------------------------- CPU baseline (rank 0, N=1 only)
+    if world == 1 and rank == 0 and not args.no_cpu:
+        out["cpu_baseline"] = cpu_decode_baseline(torch, args, reps=3)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out))
+
+
+def bench_prefill(torch, ops, dev, rank, world, args, stream, pk, pk_kind, barrier_sync, max_over_ranks):
+    g = torch.Generator(device=dev).manual_seed(3000 + rank)
+    B, Hq, Hkv, D, T, W = 1, 16, 2, 256, 8192, 2048
+    q = torch.randn(B, T, Hq, D, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    k = torch.randn(B, Hkv, T, D, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    v = torch.randn(B, Hkv, T, D, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    gate = torch.randn(B, T, Hq * D, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    out = torch.empty(B, Hq, T, D, dtype=torch.bfloat16, device=dev)
+    qv = q.transpose(1, 2)  # [B, Hq, T, D] view, as mlx_lm hands it over
+    gv = gate.view(B, T, Hq, D).transpose(1, 2)
+    flop = 4.0 * D * Hq * (T * (T + 1) / 2)
+
+    def step(i):
+        for c in range(T // W):
+            r0, r1 = c * W, (c + 1) * W
+            ops.attn_prefill(qv[:, :, r0:r1], k[:, :, :r1], v[:, :, :r1], D ** -0.5, "causal", gate=gv[:, :, r0:r1],
+                             out=out[:, :, r0:r1])
+
+    for i in range(args.warmup):
+        step(i)
+    barrier_sync()
+    with Clocks(int(os.environ.get("LOCAL_RANK", "0"))) as clk:
+        ms = cuda_time(torch, step, args.steps, stream)
+    barrier_sync()
+    ms = max_over_ranks(ms)
+    per = ms / args.steps
+    tf = flop / (per * 1e-3) / 1e12
+    return {"value": round(world * tf, 2), "unit": "TFLOP/s", "ms_per_step": round(per, 4),
+            "workload": "configs[2]: B=1, 8192 causal rows in 4 chunks of 2048 (keys 0..2048(c+1)), 16q/2kv x 256, "
+                        "bf16, sigmoid gate fused",
+            "flop_per_step": flop, "gpu_launches_per_step": T // W,
+            "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": round(tf / pk["bf16_tflops"], 4), "traffic": None, "peak_kind": pk_kind,
+                         "kernel": "lb2::prefill::fmha_kernel<bf16,256>"},
+            "clocks": clk.summary()}
+
+
+def bench_gdn(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_over_ranks):
+    g = torch.Generator(device=dev).manual_seed(4000 + rank)
+    B, Hk, Hv, D = 16, 16, 32, 128
+    copies = 3  # 3 x 67 MB of state: consecutive steps miss L2
+    states = [torch.zeros(B, Hv, D, D, device=dev) for _ in range(copies)]
+    outs = [torch.empty_like(s) for s in states]
+    q = torch.nn.functional.normalize(torch.randn(B, 1, Hk, D, generator=g, device=dev), dim=-1).to(torch.bfloat16)
+    k = torch.nn.functional.normalize(torch.randn(B, 1, Hk, D, generator=g, device=dev), dim=-1).to(torch.bfloat16)
+    v = torch.randn(B, 1, Hv, D, generator=g, device=dev).to(torch.bfloat16)
+    beta = torch.sigmoid(torch.randn(B, 1, Hv, generator=g, device=dev)).to(torch.bfloat16)
+    gg = torch.exp(-torch.nn.functional.softplus(torch.randn(B, 1, Hv, generator=g, device=dev)))
+
+    def step(i):
+        y, s = ops.gdn_recurrent(q, k, v, gg, beta, states[i % copies])
+        states[i % copies] = s
+
+    for i in range(args.warmup):
+        step(i)
+    barrier_sync()
+    ms = max_over_ranks(cuda_time(torch, step, args.steps, stream))
+    barrier_sync()
+    per = ms / args.steps
+    state_bytes = B * Hv * D * D * 4 * 2
+    gbs = state_bytes / (per * 1e-3) / 1e9
+    res = {"decode": {"value": round(world * gbs, 1), "unit": "GB/s", "ms_per_step": round(per, 5),
+                      "workload": "configs[3] decode step: B=16, Hk 16, Hv 32, 128x128 fp32 state read+written",
+                      "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                   "frac": round(gbs / pk["hbm_gbs"], 4),
+                                   "kernel": "lb2::gdnrec::recurrent_kernel<bf16,4>"}}}
+    return res
+
+
+# ------------------------------------------------------------------------------------------------ CPU arms
+
+def cpu_decode_baseline(torch, args, reps=3, sample_seqs=16):
+    """Config 2 through the CPU oracle (the restated reference CPU kernel), one call per sequence as the reference's
+    CPU attention requires (mask leading dims 1, cpu_kern.cpp:653), all host cores."""
+    import numpy as np
+
+    import oracle
+    g = torch.Generator().manual_seed(1000)
+    B, Hq, Hkv, D = 16, 32, 4, 128
+    lens = torch.randint(1024, 8193, (B,), generator=g)
+    rng = np.random.default_rng(7)
+    seqs = []
+    for b in range(min(sample_seqs, B)):
+        n = int(lens[b])
+        q = oracle.f32_to_bf16(rng.normal(0, 1, (1, Hq, 1, D)).astype(np.float32))
+        k = oracle.f32_to_bf16(rng.normal(0, 1, (1, Hkv, n, D)).astype(np.float32))
+        v = oracle.f32_to_bf16(rng.normal(0, 1, (1, Hkv, n, D)).astype(np.float32))
+        seqs.append((q, k, v, n))
+    threads = oracle.default_threads()
+    times = []
+    for r in range(reps + 1):
+        t0 = time.perf_counter()
+        for q, k, v, n in seqs:
+            oracle.attn(q, k, v, D ** -0.5, oracle.BF16, threads=threads)
+        if r:
+            times.append(time.perf_counter() - t0)
+    t = sorted(times)[len(times) // 2]
+    kv = sum(n for *_, n in seqs) * Hkv * D * 2 * 2
+    return {"value": round(kv / t / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"configs[1] decode, {len(seqs)} sequences (sum len {sum(n for *_, n in seqs)}), one oracle call "
+                      f"each, median of {reps} after one warm-up", "seconds": round(t, 3)}
+
+
+def run_reference(args):
+    """The reference's CPU implementation of the path (oracle restatement of CpuAttn) on the headline workload."""
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+
+    import oracle
+    g = torch.Generator().manual_seed(1000)
+    B, Hq, Hkv, D = 16, 32, 4, 128
+    lens = torch.randint(1024, 8193, (B,), generator=g)
+    rng = np.random.default_rng(7)
+    seqs = []
+    for b in range(B):
+        n = int(lens[b])
+        seqs.append((oracle.f32_to_bf16(rng.normal(0, 1, (1, Hq, 1, D)).astype(np.float32)),
+                     oracle.f32_to_bf16(rng.normal(0, 1, (1, Hkv, n, D)).astype(np.float32)),
+                     oracle.f32_to_bf16(rng.normal(0, 1, (1, Hkv, n, D)).astype(np.float32)), n))
+    threads = oracle.default_threads()
+
+    def step():
+        for q, k, v, n in seqs:
+            oracle.attn(q, k, v, D ** -0.5, oracle.BF16, threads=threads)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    kv = int(lens.sum()) * Hkv * D * 2 * 2
+    val = round(kv / dt / 1e9, 3)
+    print(json.dumps({"impl": "reference", "metric": METRIC, "value": val, "unit": "GB/s", "n_gpus": world,
+                      "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
+                      "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                      "data": "synthetic (seeded N(0,1), config shapes)",
+                      "config": {"workload": "configs[1] GQA decode: B=16, 32q/4kv x 128, bf16 KV, lengths "
+                                             "U[1024,8192]", "global_batch": 16, "parallelism": "cpu"},
+                      "cpu_baseline": {"value": val, "unit": "GB/s", "cores": threads, "kind": "port",
+                                       "sample": "the full configs[1] batch a step, one oracle call per sequence"},
+                      "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--section", default="decode,prefill,gdn")
+    ap.add_argument("--split", type=int, default=0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

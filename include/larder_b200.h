@@ -1,0 +1,140 @@
+/* larder_b200: B200 (sm_100a) kernels for Larder's attention / Gated-DeltaNet hot path, behind a plain C ABI.
+ *
+ * Every entry point takes raw device pointers, element strides (int64, in elements of the tensor's own dtype),
+ * shapes, dtype codes and a cudaStream_t passed as void*. Launches are asynchronous on that stream; the return
+ * value is a status code (LB2_OK or an error), and lb2_error() gives the calling thread's last message. The caller
+ * owns every buffer: outputs and workspaces are allocated by the caller (the Python layer uses torch) and the
+ * library never allocates or frees device memory on these paths. Device-side waits are time-bounded; a wait that
+ * gives up records itself in a device status word read (and cleared) by lb2_status().
+ *
+ * Reference interfaces each entry replaces are cited per function (paths within IamCooller/larder).
+ */
+#ifndef LARDER_B200_H
+#define LARDER_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* dtype codes (cpu_ext/cpu_kern.cpp:32's DT enum, same values) */
+#define LB2_F32 0
+#define LB2_BF16 1
+#define LB2_F16 2
+
+/* attention mask kinds (cpu_ext/cpu_kern.cpp:634: 0 none, 1 causal bottom-right, 2 boolean [T, N] array) */
+#define LB2_MASK_NONE 0
+#define LB2_MASK_CAUSAL 1
+#define LB2_MASK_ARRAY 2
+
+/* status codes */
+#define LB2_OK 0
+#define LB2_EINVAL 1   /* unsupported shape, dtype, stride or alignment */
+#define LB2_ECUDA 2    /* a CUDA runtime call or launch failed */
+#define LB2_ETIMEOUT 3 /* a bounded device wait gave up (lb2_status) */
+
+/* Version of this ABI; bumped on any signature change. */
+int lb2_abi_version(void);
+
+/* The calling thread's last error message ("" when none). Mirrors native/moe_pipe_cuda.cpp:1658-1690's
+ * mpc_error(): one message slot, entry points return a status. */
+const char* lb2_error(void);
+
+/* Synchronises `stream`, then returns and clears the current device's status word: LB2_OK, or
+ * LB2_ETIMEOUT | (where << 8) for the first device wait that gave up since the last call. */
+int lb2_status(void* stream);
+
+/* ------------------------------------------------------------------------------------------------------------
+ * Prefill / multi-row attention (tcgen05 tensor cores, TMEM accumulators, TMA-staged tiles).
+ *
+ * o = softmax(scale * q k^T + mask) v, optionally times sigmoid(gate).
+ *   q    [B, Hq, T, D]   strides q_st[0..2] for B, H, T; unit stride on D
+ *   k, v [B, Hkv, N, D]  strides k_st / v_st; unit stride on D (K/V may be slices of a longer cache buffer)
+ *   o    [B, Hq, T, D]   strides o_st
+ *   gate [B, Hq, T, D]   strides g_st, or NULL (the gated-attention epilogue of qwen4_exp_vendor.py:397-401:
+ *                        out * sigmoid(gate), gate being [B, T, Hq * D] seen through these strides)
+ *   mask uint8 [T, N]    strides m_st[0..1], only for LB2_MASK_ARRAY
+ * Causal is bottom-right: row t sees keys 0 .. N - T + t. GQA: q head h reads KV head h / (Hq / Hkv).
+ * dtype LB2_BF16 or LB2_F16 for q, k, v, o, gate alike; D in {64, 128, 256}; row strides multiples of 8 elements
+ * and every base 16-byte aligned (TMA).
+ * Replaces: the patched scaled_dot_product_attention's prefill route (chunkattn.py:451-537) and each chunk of
+ * chunkattn.chunked (chunkattn.py:359-423), qsa_tiles.chunked's array-masked chunk (qsa_tiles.py:266-292), and
+ * the stock mx.fast.scaled_dot_product_attention they call (chunkattn.py:419-420). */
+int lb2_attn_prefill(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
+                     const int64_t* v_st, void* o, const int64_t* o_st, const void* gate, const int64_t* g_st,
+                     const uint8_t* mask, const int64_t* m_st, int B, int Hq, int Hkv, int T, int N, int D, int dtype,
+                     float scale, int mask_kind, void* stream);
+
+/* ------------------------------------------------------------------------------------------------------------
+ * Split-KV decode attention (few query rows over a long KV cache; HBM-bandwidth bound).
+ *
+ * The G*T query rows that share a KV head are folded into one tile (foldattn.py:230-259); keys are cut into
+ * splits of `split` keys (a multiple of 64, or 0 to let the library choose), each split computes an fp32
+ * partial (o, max, sum) with an online softmax, and the last split of each (b, kv head) to finish merges them by
+ * log-sum-exp (foldattn.py:188-211, cpu_kern.cpp:607-628) and writes o.
+ *   q [B, Hq, T, D], k/v [B, Hkv, N, D] (N = capacity), o [B, Hq, T, D]: strides as in lb2_attn_prefill
+ *   kv_len int32 [B] device array of per-sequence key counts (<= N), or NULL for N everywhere
+ *   causal: 1 for bottom-right causal over each sequence's own length (T >= 2 verify rows), else 0
+ *   workspace: lb2_attn_decode_workspace_size() bytes, 256-byte aligned, ZEROED before its first use (the
+ *   kernel returns its counters to zero, so one zeroing lasts the workspace's life). Calls that share a
+ *   workspace must be ordered on one stream.
+ * Limits: G*T <= 32 for D <= 128, G*T <= 16 for D = 256; dtype LB2_BF16 or LB2_F16; D in {64, 128, 256}.
+ * Replaces: decode SDPA (chunkattn.gqa_sdpa + _gqa_route, chunkattn.py:638-657, :679-696; stream_fast.py's
+ * _sdpa_parts / two-pass vector SDPA, :5952-6098), foldattn.fold (foldattn.py:230-259) and the stock decode SDPA
+ * attn_cuda calls (stream_fast.py:6439). */
+size_t lb2_attn_decode_workspace_size(int B, int Hq, int Hkv, int T, int N, int D, int split);
+int lb2_attn_decode(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
+                    const int64_t* v_st, void* o, const int64_t* o_st, const int32_t* kv_len, int B, int Hq, int Hkv,
+                    int T, int N, int D, int dtype, float scale, int causal, int split, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/* The same decode over this rank's KV range only, emitting the range's normalised partial output and its
+ * log-sum-exp instead of the final o: part_o fp32 [B, Hq, T, D] contiguous, part_lse fp32 [B, Hq, T] (natural
+ * log; -inf for a row with no visible key). For KV-range shards across GPUs merged by lb2_attn_combine.
+ * kv_len / workspace as lb2_attn_decode. Every query row sees every key of the range (decode rows: the range
+ * lies wholly before the query position). */
+int lb2_attn_decode_partial(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
+                            const int64_t* v_st, float* part_o, float* part_lse, const int32_t* kv_len, int B, int Hq,
+                            int Hkv, int T, int N, int D, int dtype, float scale, int split, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
+/* Merges R partials: o[row] = sum_r w_r part_o[r][row] / sum_r w_r, w_r = exp(part_lse[r][row] - max_r lse),
+ * rows = B * Hq * T (row-major [B, Hq, T]), o [B, Hq, T, D] with strides o_st in dtype. An all -inf row gives 0.
+ * Replaces the LSE merge of foldattn_merge (foldattn.py:188-211) / cpu_kern.cpp:607-628, across ranks. */
+int lb2_attn_combine(const float* part_o, const float* part_lse, int R, int B, int Hq, int T, int D, void* o,
+                     const int64_t* o_st, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------------------------------------------
+ * Gated-DeltaNet recurrence, one position at a time (decode steps, short verify passes).
+ *
+ * For each (b, v head hv, value row dv), over t: s <- s * g_t; kv = s . k_t; delta = (v_t[dv] - kv) * beta_t;
+ * s <- s + k_t * delta; y_t[dv] = s . q_t (gdn_cuda.py:18-66). v head hv reads k head hv / (Hv / Hk).
+ *   q, k [B, T, Hk, Dk] (qdt), v [B, T, Hv, Dv] (vdt), g [B, T, Hv] or, with g_vec, [B, T, Hv, Dk] (gdt),
+ *   beta [B, T, Hv] (bdt), state_in / state_out fp32 [B, Hv, Dv, Dk] (may alias), y [B, T, Hv, Dv] (qdt),
+ *   mask uint8 [B, T] or NULL (a masked position writes y = 0 and keeps the state). All contiguous.
+ * Dk in {32, 64, 128, 256}; dtypes LB2_F32 / LB2_BF16 / LB2_F16.
+ * Replaces: gdn_cuda.recurrence (gdn_cuda.py:88-99) and, with the gating done by the caller, the patched
+ * gated_delta_update (gdn_cuda.py:336-353). */
+int lb2_gdn_recurrent(const void* q, const void* k, int qdt, const void* v, int vdt, const void* g, int gdt,
+                      int g_vec, const void* beta, int bdt, const uint8_t* mask, const float* state_in,
+                      float* state_out, void* y, int B, int T, int Hk, int Dk, int Hv, int Dv, void* stream);
+
+/* ------------------------------------------------------------------------------------------------------------
+ * Gated-DeltaNet chunked prefill: the same recurrence and result as lb2_gdn_recurrent, computed in chunks of 64
+ * positions (intra-chunk products on tensor cores, the chunk's triangular system solved in fp32, the state
+ * carried chunk to chunk). Scalar gate only (g [B, T, Hv]), no mask; Dk = Dv = 128; q/k/v bf16 or f16, g f32,
+ * beta in q's dtype or f32. workspace: lb2_gdn_chunked_workspace_size() bytes.
+ * Replaces: gdn_cuda.recurrence's prefill calls (one launch for all T, gdn_cuda.py:88-99) via the patched
+ * gated_delta_update (gdn_cuda.py:336-353). */
+size_t lb2_gdn_chunked_workspace_size(int B, int T, int Hk, int Hv, int Dk, int Dv);
+int lb2_gdn_chunked(const void* q, const void* k, int qdt, const void* v, int vdt, const void* g, int gdt,
+                    const void* beta, int bdt, const float* state_in, float* state_out, void* y, int B, int T, int Hk,
+                    int Dk, int Hv, int Dv, void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LARDER_B200_H */

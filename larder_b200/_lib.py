@@ -1,0 +1,70 @@
+"""Loader for liblarder_b200.so, the C-ABI library of this package's CUDA kernels.
+
+There is no CPU or PyTorch fallback anywhere in larder_b200: if the library is missing, or the tensors are not on a
+CUDA device, calls raise. The library is built in-tree by larder_b200.build (nvcc, sm_100a) so that it travels with
+the repository.
+"""
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liblarder_b200.so")
+
+F32, BF16, F16 = 0, 1, 2
+MASK_NONE, MASK_CAUSAL, MASK_ARRAY = 0, 1, 2
+OK, EINVAL, ECUDA, ETIMEOUT = 0, 1, 2, 3
+
+# Every symbol include/larder_b200.h declares, with its ctypes signature.
+_p, _i, _f, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
+_i64p = ctypes.POINTER(ctypes.c_int64)
+SIGNATURES = {
+    "lb2_abi_version": ([], _i),
+    "lb2_error": ([], ctypes.c_char_p),
+    "lb2_status": ([_p], _i),
+    "lb2_attn_prefill": ([_p, _i64p, _p, _i64p, _p, _i64p, _p, _i64p, _p, _i64p, _p, _i64p,
+                          _i, _i, _i, _i, _i, _i, _i, _f, _i, _p], _i),
+    "lb2_attn_decode_workspace_size": ([_i, _i, _i, _i, _i, _i, _i], _sz),
+    "lb2_attn_decode": ([_p, _i64p, _p, _i64p, _p, _i64p, _p, _i64p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _i, _i,
+                         _p, _sz, _p], _i),
+    "lb2_attn_decode_partial": ([_p, _i64p, _p, _i64p, _p, _i64p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _i,
+                                 _p, _sz, _p], _i),
+    "lb2_attn_combine": ([_p, _p, _i, _i, _i, _i, _i, _p, _i64p, _i, _p], _i),
+    "lb2_gdn_recurrent": ([_p, _p, _i, _p, _i, _p, _i, _i, _p, _i, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p], _i),
+    "lb2_gdn_chunked_workspace_size": ([_i, _i, _i, _i, _i, _i], _sz),
+    "lb2_gdn_chunked": ([_p, _p, _i, _p, _i, _p, _i, _p, _i, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p, _sz, _p], _i),
+}
+
+_lib = None
+
+
+class LarderError(RuntimeError):
+    """A CUDA-side failure reported by liblarder_b200 (launch error or a device wait that gave up)."""
+
+
+def lib():
+    """The loaded library; raises ImportError when it was not built (no fallback exists)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: build it with `python -m larder_b200.build` "
+                              "(larder_b200 has no CPU or PyTorch fallback)")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (args, res) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = L
+    return _lib
+
+
+def check(rc, what):
+    if rc == OK:
+        return
+    msg = lib().lb2_error().decode(errors="replace")
+    if rc == EINVAL:
+        raise ValueError(f"{what}: {msg}")
+    raise LarderError(f"{what}: {msg} (status {rc})")
+
+
+def i64(*vals):
+    return (ctypes.c_int64 * len(vals))(*[int(v) for v in vals])

@@ -1,0 +1,390 @@
+// larder_b200: the C-ABI library. One translation unit (so the device status word is one symbol) that includes
+// every kernel header and implements the entry points declared in include/larder_b200.h.
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+#include "attn_decode.cuh"
+#include "gdn_recurrent.cuh"
+#include "attn_prefill.cuh"
+
+namespace lb2 {
+
+static thread_local std::string t_error;
+
+void set_error(const std::string& msg) { t_error = msg; }
+
+int fail(int code, const std::string& msg) {
+  t_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  t_error = std::string(what) + ": " + cudaGetErrorString(e);
+  return LB2_ECUDA;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  });
+  return fn;
+}
+
+int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
+                      const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(LB2_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if (reinterpret_cast<uintptr_t>(base) & 15) return fail(LB2_EINVAL, "TMA base address is not 16-byte aligned");
+  for (int i = 0; i < rank - 1; ++i)
+    if (strides_bytes[i] % 16) return fail(LB2_EINVAL, "TMA stride is not a multiple of 16 bytes");
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = fn(map, dtype, cuuint32_t(rank), const_cast<void*>(base), reinterpret_cast<const cuuint64_t*>(dims),
+                  reinterpret_cast<const cuuint64_t*>(strides_bytes), reinterpret_cast<const cuuint32_t*>(box), estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(LB2_EINVAL, "cuTensorMapEncodeTiled failed (code " + std::to_string(r) + ")");
+  return LB2_OK;
+}
+
+int sm_count(int device) {
+  static int cached[64] = {0};
+  if (device < 0 || device >= 64) return 148;
+  if (!cached[device]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0) n = 148;
+    cached[device] = n;
+  }
+  return cached[device];
+}
+
+static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// ------------------------------------------------------------------------------------------------ decode
+
+namespace decode {
+
+static int pick_split(int B, int Hkv, int N, int split) {
+  if (split > 0) return (split + BK - 1) / BK * BK;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  // Aim at about eight CTAs per SM over the whole call (two resident at a time), never under two tiles a split.
+  const int64_t target = int64_t(sm_count(dev)) * 8;
+  int64_t s = (int64_t(B) * Hkv * N + target - 1) / target;
+  s = (s + BK - 1) / BK * BK;
+  if (s < 2 * BK) s = 2 * BK;
+  if (s > N) s = (N + BK - 1) / BK * BK;
+  return int(s < BK ? BK : s);
+}
+
+static int rows_tiles(int G, int T) { return (G * T + 15) / 16; }
+
+struct WsLayout {
+  size_t cnt, ml, o, total;
+};
+
+static WsLayout ws_layout(int B, int Hkv, int rp, int D, int nsplit) {
+  WsLayout w;
+  w.cnt = 0;
+  w.ml = align_up(size_t(B) * Hkv * sizeof(int), 256);
+  w.o = w.ml + align_up(size_t(B) * Hkv * nsplit * rp * 2 * sizeof(float), 256);
+  w.total = w.o + size_t(B) * Hkv * nsplit * rp * D * sizeof(float);
+  return w;
+}
+
+template <typename T, int D, int MT>
+static int launch_t(const CUtensorMap& km, const CUtensorMap& vm, const Params& p, cudaStream_t st) {
+  auto kern = decode_kernel<T, D, MT>;
+  static bool attr_set = false;  // per instantiation; the attribute is per device but idempotent
+  const int smem = Cfg<D>::SMEM_BYTES;
+  if (!attr_set) {
+    LB2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr_set = true;
+  }
+  dim3 grid(p.nsplit, p.Hkv, p.B);
+  kern<<<grid, THREADS, smem, st>>>(km, vm, p);
+  LB2_CUDA(cudaGetLastError());
+  return LB2_OK;
+}
+
+template <typename T>
+static int launch_d(int D, int MT, const CUtensorMap& km, const CUtensorMap& vm, const Params& p, cudaStream_t st) {
+  if (D == 64) return MT == 1 ? launch_t<T, 64, 1>(km, vm, p, st) : launch_t<T, 64, 2>(km, vm, p, st);
+  if (D == 128) return MT == 1 ? launch_t<T, 128, 1>(km, vm, p, st) : launch_t<T, 128, 2>(km, vm, p, st);
+  return launch_t<T, 256, 1>(km, vm, p, st);
+}
+
+static int kv_map(CUtensorMap* m, const void* base, const int64_t* st, int B, int H, int N, int D, int dtype) {
+  const uint64_t dims[4] = {uint64_t(D), uint64_t(N), uint64_t(H), uint64_t(B)};
+  const uint64_t strides[3] = {uint64_t(st[2]) * 2, uint64_t(st[1]) * 2, uint64_t(st[0]) * 2};
+  const uint32_t box[4] = {64, uint32_t(BK), 1, 1};
+  return encode_tensor_map(m, dtype == LB2_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                           4, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+static int run(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
+               const int64_t* v_st, void* o, const int64_t* o_st, float* part_o, float* part_lse,
+               const int32_t* kv_len, int B, int Hq, int Hkv, int T, int N, int D, int dtype, float scale, int causal,
+               int split, void* workspace, size_t workspace_bytes, void* stream) {
+  LB2_CHECK_ARG(B > 0 && Hq > 0 && Hkv > 0 && T > 0 && N > 0, "decode: empty shape");
+  LB2_CHECK_ARG(Hq % Hkv == 0, "decode: Hq must be a multiple of Hkv");
+  LB2_CHECK_ARG(D == 64 || D == 128 || D == 256, "decode: head dim must be 64, 128 or 256");
+  LB2_CHECK_ARG(dtype == LB2_BF16 || dtype == LB2_F16, "decode: dtype must be bf16 or f16");
+  const int G = Hq / Hkv, rows = G * T;
+  LB2_CHECK_ARG(rows <= (D == 256 ? 16 : 32), "decode: too many folded rows (G*T) for the split-KV kernel");
+  for (int i = 0; i < 3; ++i)
+    LB2_CHECK_ARG(q_st[i] % 8 == 0 && k_st[i] % 8 == 0 && v_st[i] % 8 == 0,
+                  "decode: q/k/v strides must be multiples of 8 elements");
+  LB2_CHECK_ARG((reinterpret_cast<uintptr_t>(q) & 15) == 0, "decode: q must be 16-byte aligned");
+  const int MT = rows_tiles(G, T);
+  const int sp = pick_split(B, Hkv, N, split);
+  const int nsplit = (N + sp - 1) / sp;
+  const WsLayout w = ws_layout(B, Hkv, MT * 16, D, nsplit);
+  LB2_CHECK_ARG(workspace != nullptr && workspace_bytes >= w.total, "decode: workspace too small");
+  LB2_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "decode: workspace must be 256-byte aligned");
+  CUtensorMap km, vm;
+  int rc = kv_map(&km, k, k_st, B, Hkv, N, D, dtype);
+  if (rc) return rc;
+  rc = kv_map(&vm, v, v_st, B, Hkv, N, D, dtype);
+  if (rc) return rc;
+  Params p{};
+  p.q = q;
+  for (int i = 0; i < 3; ++i) {
+    p.q_st[i] = q_st[i];
+    p.o_st[i] = o_st ? o_st[i] : 0;
+  }
+  p.o = o;
+  p.part_o = part_o;
+  p.part_lse = part_lse;
+  p.emit = part_o != nullptr;
+  p.kv_len = kv_len;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  p.ws_cnt = reinterpret_cast<int*>(ws + w.cnt);
+  p.ws_ml = reinterpret_cast<float*>(ws + w.ml);
+  p.ws_o = reinterpret_cast<float*>(ws + w.o);
+  p.B = B;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.T = T;
+  p.N = N;
+  p.G = G;
+  p.rows = rows;
+  p.split = sp;
+  p.nsplit = nsplit;
+  p.causal = causal && T > 1;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return dtype == LB2_BF16 ? launch_d<__nv_bfloat16>(D, MT, km, vm, p, st) : launch_d<__half>(D, MT, km, vm, p, st);
+}
+
+}  // namespace decode
+
+// ------------------------------------------------------------------------------------------------ prefill
+
+namespace prefill {
+
+template <typename T, int D>
+static int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const Params& p,
+                  cudaStream_t st) {
+  auto kern = fmha_kernel<T, D>;
+  static int attr_dev = -1;
+  int dev = 0;
+  LB2_CUDA(cudaGetDevice(&dev));
+  if (attr_dev != dev) {
+    LB2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM_BYTES));
+    attr_dev = dev;
+  }
+  dim3 grid(unsigned(p.B * p.Hq * p.mtiles));
+  kern<<<grid, THREADS, Cfg<D>::SMEM_BYTES, st>>>(qm, km, vm, p);
+  LB2_CUDA(cudaGetLastError());
+  return LB2_OK;
+}
+
+static int map4(CUtensorMap* m, const void* base, const int64_t* st, int B, int H, int L, int D, int dtype,
+                int box_rows) {
+  const uint64_t dims[4] = {uint64_t(D), uint64_t(L), uint64_t(H), uint64_t(B)};
+  const uint64_t strides[3] = {uint64_t(st[2]) * 2, uint64_t(st[1]) * 2, uint64_t(st[0]) * 2};
+  const uint32_t box[4] = {64, uint32_t(box_rows), 1, 1};
+  return encode_tensor_map(m, dtype == LB2_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                           4, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+}  // namespace prefill
+}  // namespace lb2
+
+using namespace lb2;
+
+extern "C" {
+
+int lb2_abi_version(void) { return 1; }
+
+const char* lb2_error(void) { return t_error.c_str(); }
+
+int lb2_status(void* stream) {
+  LB2_CUDA(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  int v = 0, zero = 0;
+  LB2_CUDA(cudaMemcpyFromSymbol(&v, g_status, sizeof(int)));
+  if (v) LB2_CUDA(cudaMemcpyToSymbol(g_status, &zero, sizeof(int)));
+  if (v) set_error("a device wait gave up (where " + std::to_string(v >> 8) + ")");
+  return v;
+}
+
+size_t lb2_attn_decode_workspace_size(int B, int Hq, int Hkv, int T, int N, int D, int split) {
+  if (B <= 0 || Hkv <= 0 || Hq % Hkv || N <= 0 || T <= 0) return 0;
+  const int MT = decode::rows_tiles(Hq / Hkv, T);
+  const int sp = decode::pick_split(B, Hkv, N, split);
+  return decode::ws_layout(B, Hkv, MT * 16, D, (N + sp - 1) / sp).total;
+}
+
+int lb2_attn_decode(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
+                    const int64_t* v_st, void* o, const int64_t* o_st, const int32_t* kv_len, int B, int Hq, int Hkv,
+                    int T, int N, int D, int dtype, float scale, int causal, int split, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  LB2_CHECK_ARG(o != nullptr && o_st != nullptr, "decode: output missing");
+  return decode::run(q, q_st, k, k_st, v, v_st, o, o_st, nullptr, nullptr, kv_len, B, Hq, Hkv, T, N, D, dtype, scale,
+                     causal, split, workspace, workspace_bytes, stream);
+}
+
+int lb2_attn_decode_partial(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
+                            const int64_t* v_st, float* part_o, float* part_lse, const int32_t* kv_len, int B, int Hq,
+                            int Hkv, int T, int N, int D, int dtype, float scale, int split, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  LB2_CHECK_ARG(part_o != nullptr && part_lse != nullptr, "decode_partial: outputs missing");
+  return decode::run(q, q_st, k, k_st, v, v_st, nullptr, nullptr, part_o, part_lse, kv_len, B, Hq, Hkv, T, N, D,
+                     dtype, scale, 0, split, workspace, workspace_bytes, stream);
+}
+
+int lb2_attn_combine(const float* part_o, const float* part_lse, int R, int B, int Hq, int T, int D, void* o,
+                     const int64_t* o_st, int dtype, void* stream) {
+  LB2_CHECK_ARG(R > 0 && B > 0 && Hq > 0 && T > 0 && D > 0, "combine: empty shape");
+  const int rows = B * Hq * T;
+  const int warps = 8;
+  dim3 grid((rows + warps - 1) / warps);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == LB2_BF16)
+    decode::combine_kernel<__nv_bfloat16><<<grid, warps * 32, 0, st>>>(part_o, part_lse, R, rows, Hq, T, D, o,
+                                                                       o_st[0], o_st[1], o_st[2]);
+  else if (dtype == LB2_F16)
+    decode::combine_kernel<__half><<<grid, warps * 32, 0, st>>>(part_o, part_lse, R, rows, Hq, T, D, o, o_st[0],
+                                                                o_st[1], o_st[2]);
+  else if (dtype == LB2_F32)
+    decode::combine_kernel<float><<<grid, warps * 32, 0, st>>>(part_o, part_lse, R, rows, Hq, T, D, o, o_st[0],
+                                                               o_st[1], o_st[2]);
+  else
+    return fail(LB2_EINVAL, "combine: dtype");
+  LB2_CUDA(cudaGetLastError());
+  return LB2_OK;
+}
+
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int lb2_attn_prefill(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
+                     const int64_t* v_st, void* o, const int64_t* o_st, const void* gate, const int64_t* g_st,
+                     const uint8_t* mask, const int64_t* m_st, int B, int Hq, int Hkv, int T, int N, int D, int dtype,
+                     float scale, int mask_kind, void* stream) {
+  LB2_CHECK_ARG(B > 0 && Hq > 0 && Hkv > 0 && T > 0 && N > 0, "prefill: empty shape");
+  LB2_CHECK_ARG(Hq % Hkv == 0, "prefill: Hq must be a multiple of Hkv");
+  LB2_CHECK_ARG(D == 64 || D == 128 || D == 256, "prefill: head dim must be 64, 128 or 256");
+  LB2_CHECK_ARG(dtype == LB2_BF16 || dtype == LB2_F16, "prefill: dtype must be bf16 or f16");
+  LB2_CHECK_ARG(mask_kind >= LB2_MASK_NONE && mask_kind <= LB2_MASK_ARRAY, "prefill: mask kind");
+  LB2_CHECK_ARG(mask_kind != LB2_MASK_ARRAY || (mask != nullptr && m_st != nullptr), "prefill: array mask missing");
+  for (int i = 0; i < 3; ++i) {
+    LB2_CHECK_ARG(q_st[i] % 8 == 0 && k_st[i] % 8 == 0 && v_st[i] % 8 == 0 && o_st[i] % 8 == 0,
+                  "prefill: strides must be multiples of 8 elements");
+    LB2_CHECK_ARG(!gate || g_st[i] % 8 == 0, "prefill: gate strides must be multiples of 8 elements");
+  }
+  LB2_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o) && (!gate || aligned16(gate)),
+                "prefill: tensors must be 16-byte aligned");
+  CUtensorMap qm, km, vm;
+  const int BN = D == 256 ? prefill::Cfg<256>::BN : prefill::Cfg<128>::BN;
+  int rc = prefill::map4(&qm, q, q_st, B, Hq, T, D, dtype, prefill::BM);
+  if (!rc) rc = prefill::map4(&km, k, k_st, B, Hkv, N, D, dtype, BN);
+  if (!rc) rc = prefill::map4(&vm, v, v_st, B, Hkv, N, D, dtype, BN);
+  if (rc) return rc;
+  prefill::Params p{};
+  p.o = o;
+  p.gate = gate;
+  for (int i = 0; i < 3; ++i) {
+    p.o_st[i] = o_st[i];
+    p.g_st[i] = gate ? g_st[i] : 0;
+  }
+  p.mask = mask_kind == LB2_MASK_ARRAY ? mask : nullptr;
+  p.m_st[0] = p.mask ? m_st[0] : 0;
+  p.m_st[1] = p.mask ? m_st[1] : 0;
+  p.B = B;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.T = T;
+  p.N = N;
+  p.G = Hq / Hkv;
+  p.mask_kind = mask_kind;
+  p.mtiles = (T + prefill::BM - 1) / prefill::BM;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == LB2_BF16) {
+    if (D == 64) return prefill::launch<__nv_bfloat16, 64>(qm, km, vm, p, st);
+    if (D == 128) return prefill::launch<__nv_bfloat16, 128>(qm, km, vm, p, st);
+    return prefill::launch<__nv_bfloat16, 256>(qm, km, vm, p, st);
+  }
+  if (D == 64) return prefill::launch<__half, 64>(qm, km, vm, p, st);
+  if (D == 128) return prefill::launch<__half, 128>(qm, km, vm, p, st);
+  return prefill::launch<__half, 256>(qm, km, vm, p, st);
+}
+
+size_t lb2_gdn_chunked_workspace_size(int B, int T, int Hk, int Hv, int Dk, int Dv) {
+  (void)B; (void)T; (void)Hk; (void)Hv; (void)Dk; (void)Dv;
+  return 256;
+}
+
+int lb2_gdn_chunked(const void* q, const void* k, int qdt, const void* v, int vdt, const void* g, int gdt,
+                    const void* beta, int bdt, const float* state_in, float* state_out, void* y, int B, int T, int Hk,
+                    int Dk, int Hv, int Dv, void* workspace, size_t workspace_bytes, void* stream) {
+  (void)q; (void)k; (void)qdt; (void)v; (void)vdt; (void)g; (void)gdt; (void)beta; (void)bdt; (void)state_in;
+  (void)state_out; (void)y; (void)B; (void)T; (void)Hk; (void)Dk; (void)Hv; (void)Dv; (void)workspace;
+  (void)workspace_bytes; (void)stream;
+  return fail(LB2_EINVAL, "gdn_chunked: the chunked kernel is not built into this library yet");
+}
+
+int lb2_gdn_recurrent(const void* q, const void* k, int qdt, const void* v, int vdt, const void* g, int gdt,
+                      int g_vec, const void* beta, int bdt, const uint8_t* mask, const float* state_in,
+                      float* state_out, void* y, int B, int T, int Hk, int Dk, int Hv, int Dv, void* stream) {
+  LB2_CHECK_ARG(B > 0 && T >= 0 && Hk > 0 && Hv > 0 && Dv > 0, "gdn: empty shape");
+  LB2_CHECK_ARG(Hv % Hk == 0, "gdn: Hv must be a multiple of Hk");
+  LB2_CHECK_ARG(Dk == 32 || Dk == 64 || Dk == 128 || Dk == 256, "gdn: Dk must be 32, 64, 128 or 256");
+  for (int dt : {qdt, vdt, gdt, bdt}) LB2_CHECK_ARG(dt >= LB2_F32 && dt <= LB2_F16, "gdn: dtype");
+  gdnrec::Params p{q, k, v, g, beta, mask, state_in, state_out, y, qdt, vdt, gdt, bdt, g_vec, B, T, Hk, Dk, Hv, Dv};
+  const int64_t rows = int64_t(B) * Hv * Dv;
+  const int warps = 4;
+  dim3 grid(unsigned((rows + warps - 1) / warps));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define LB2_GDN_LAUNCH(QT)                                                                           \
+  switch (Dk) {                                                                                      \
+    case 32: gdnrec::recurrent_kernel<QT, 1><<<grid, warps * 32, 0, st>>>(p); break;                 \
+    case 64: gdnrec::recurrent_kernel<QT, 2><<<grid, warps * 32, 0, st>>>(p); break;                 \
+    case 128: gdnrec::recurrent_kernel<QT, 4><<<grid, warps * 32, 0, st>>>(p); break;                \
+    default: gdnrec::recurrent_kernel<QT, 8><<<grid, warps * 32, 0, st>>>(p); break;                 \
+  }
+  if (qdt == LB2_BF16) {
+    LB2_GDN_LAUNCH(__nv_bfloat16)
+  } else if (qdt == LB2_F16) {
+    LB2_GDN_LAUNCH(__half)
+  } else {
+    LB2_GDN_LAUNCH(float)
+  }
+#undef LB2_GDN_LAUNCH
+  LB2_CUDA(cudaGetLastError());
+  return LB2_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,207 @@
+"""torch-facing wrappers of the C-ABI entry points: shape/dtype/stride checks, output and workspace allocation,
+the caller's current CUDA stream. Every function here runs a CUDA kernel of liblarder_b200; none has a CPU path.
+
+Tensors follow the reference's layouts (mlx_lm's): attention q [B, Hq, T, D] (often a transposed view of
+[B, T, Hq, D]), k / v [B, Hkv, N, D] (often slices of a capacity-padded cache buffer); Gated-DeltaNet q / k
+[B, T, Hk, Dk], v [B, T, Hv, Dv], state [B, Hv, Dv, Dk] fp32.
+"""
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import check, i64, lib
+
+_DT = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16: _lib.F16}
+_WS = {}  # (device index, tag) -> zeroed uint8 workspace, grown on demand
+
+
+def dtype_code(t):
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {t.dtype}") from None
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("larder_b200 runs on CUDA tensors only (no CPU path)")
+
+
+def _stream(t):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _ptr(t):
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _unit_last(t, name):
+    if t.stride(-1) != 1:
+        raise ValueError(f"{name}: the last axis must have unit stride")
+
+
+def workspace(device, nbytes, tag):
+    """A zeroed, 256-byte aligned uint8 buffer of at least nbytes on device, kept per (device, tag). The decode
+    kernels leave their ticket counters at zero, so one zeroing lasts the buffer's life."""
+    key = (device.index if device.index is not None else torch.cuda.current_device(), tag)
+    buf = _WS.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(max(int(nbytes), 256) + 256, dtype=torch.uint8, device=device)
+        _WS[key] = buf
+    off = (-buf.data_ptr()) % 256
+    return buf[off:]
+
+
+def status(device=None):
+    """Synchronise the current stream and return (and clear) the library's device status word (0 = ok)."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+    return lib().lb2_status(ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream))
+
+
+# ---------------------------------------------------------------------------------------------------- attention
+
+def attn_prefill(q, k, v, scale, mask=None, gate=None, out=None):
+    """softmax(scale q k^T + mask) v [* sigmoid(gate)] on tcgen05 tensor cores.
+
+    mask: None, "causal" (bottom-right) or a bool tensor broadcastable from [T, N] (leading dims of 1)."""
+    _cuda(q, k, v, gate)
+    for t, n in ((q, "q"), (k, "k"), (v, "v")):
+        _unit_last(t, n)
+    B, Hq, T, D = q.shape
+    Hkv, N = k.shape[1], k.shape[2]
+    if k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("q, k, v must share a dtype")
+    if v.shape[-1] != D:
+        raise ValueError("v's head dim must equal q's")
+    if out is None:
+        out = torch.empty((B, Hq, T, D), dtype=q.dtype, device=q.device)
+    kind, m, mst = _lib.MASK_NONE, None, i64(0, 0)
+    if isinstance(mask, str):
+        if mask != "causal":
+            raise ValueError(f"unsupported mask {mask!r}")
+        kind = _lib.MASK_CAUSAL
+    elif mask is not None:
+        if mask.dtype != torch.bool or tuple(mask.shape[-2:]) != (T, N) or any(d != 1 for d in mask.shape[:-2]):
+            raise ValueError("array masks must be bool [..., T, N] with leading dims of 1")
+        m = mask.reshape(T, N).to(torch.uint8)
+        kind, mst = _lib.MASK_ARRAY, i64(m.stride(0), m.stride(1))
+    gst = i64(0, 0, 0)
+    if gate is not None:
+        if gate.shape != (B, Hq, T, D) or gate.dtype != q.dtype:
+            raise ValueError("gate must be [B, Hq, T, D] in q's dtype")
+        _unit_last(gate, "gate")
+        gst = i64(*gate.stride()[:3])
+    rc = lib().lb2_attn_prefill(_ptr(q), i64(*q.stride()[:3]), _ptr(k), i64(*k.stride()[:3]), _ptr(v),
+                                i64(*v.stride()[:3]), _ptr(out), i64(*out.stride()[:3]), _ptr(gate), gst,
+                                _ptr(m), mst, B, Hq, Hkv, T, N, D, dtype_code(q), float(scale), kind, _stream(q))
+    check(rc, "attn_prefill")
+    return out
+
+
+def decode_rows_limit(D):
+    """Folded rows (G*T) the split-KV decode kernel takes at head dim D."""
+    return 16 if D == 256 else 32
+
+
+def attn_decode(q, k, v, scale, causal=False, kv_len=None, split=0, out=None):
+    """Split-KV decode attention: q [B, Hq, T, D] with few rows over k / v [B, Hkv, N, D]; kv_len int32 [B]
+    (on the device) gives each sequence's key count, else all N."""
+    _cuda(q, k, v, kv_len)
+    for t, n in ((q, "q"), (k, "k"), (v, "v")):
+        _unit_last(t, n)
+    B, Hq, T, D = q.shape
+    Hkv, N = k.shape[1], k.shape[2]
+    if out is None:
+        out = torch.empty((B, Hq, T, D), dtype=q.dtype, device=q.device)
+    nbytes = lib().lb2_attn_decode_workspace_size(B, Hq, Hkv, T, N, D, split)
+    ws = workspace(q.device, nbytes, "decode")
+    if kv_len is not None and (kv_len.dtype != torch.int32 or kv_len.numel() != B):
+        raise ValueError("kv_len must be int32 [B]")
+    rc = lib().lb2_attn_decode(_ptr(q), i64(*q.stride()[:3]), _ptr(k), i64(*k.stride()[:3]), _ptr(v),
+                               i64(*v.stride()[:3]), _ptr(out), i64(*out.stride()[:3]), _ptr(kv_len), B, Hq, Hkv, T,
+                               N, D, dtype_code(q), float(scale), int(bool(causal)), int(split), _ptr(ws), ws.numel(),
+                               _stream(q))
+    check(rc, "attn_decode")
+    return out
+
+
+def attn_decode_partial(q, k, v, scale, kv_len=None, split=0):
+    """This KV range's normalised partial output (fp32 [B, Hq, T, D]) and log-sum-exp (fp32 [B, Hq, T])."""
+    _cuda(q, k, v, kv_len)
+    B, Hq, T, D = q.shape
+    Hkv, N = k.shape[1], k.shape[2]
+    part_o = torch.empty((B, Hq, T, D), dtype=torch.float32, device=q.device)
+    part_lse = torch.empty((B, Hq, T), dtype=torch.float32, device=q.device)
+    nbytes = lib().lb2_attn_decode_workspace_size(B, Hq, Hkv, T, N, D, split)
+    ws = workspace(q.device, nbytes, "decode_partial")
+    rc = lib().lb2_attn_decode_partial(_ptr(q), i64(*q.stride()[:3]), _ptr(k), i64(*k.stride()[:3]), _ptr(v),
+                                       i64(*v.stride()[:3]), _ptr(part_o), _ptr(part_lse), _ptr(kv_len), B, Hq, Hkv,
+                                       T, N, D, dtype_code(q), float(scale), int(split), _ptr(ws), ws.numel(),
+                                       _stream(q))
+    check(rc, "attn_decode_partial")
+    return part_o, part_lse
+
+
+def attn_combine(part_o, part_lse, dtype, out=None):
+    """Merge R partials part_o [R, B, Hq, T, D], part_lse [R, B, Hq, T] (fp32) by log-sum-exp."""
+    _cuda(part_o, part_lse)
+    R, B, Hq, T, D = part_o.shape
+    part_o, part_lse = part_o.contiguous(), part_lse.contiguous()
+    if out is None:
+        out = torch.empty((B, Hq, T, D), dtype=dtype, device=part_o.device)
+    rc = lib().lb2_attn_combine(_ptr(part_o), _ptr(part_lse), R, B, Hq, T, D, _ptr(out), i64(*out.stride()[:3]),
+                                dtype_code(out), _stream(part_o))
+    check(rc, "attn_combine")
+    return out
+
+
+# ---------------------------------------------------------------------------------------------------- GDN
+
+def _gdn_common(q, k, v, g, beta, state):
+    _cuda(q, k, v, g, beta, state)
+    B, T, Hk, Dk = q.shape
+    Hv, Dv = v.shape[2], v.shape[3]
+    if k.shape != q.shape or k.dtype != q.dtype:
+        raise ValueError("q and k must share shape and dtype")
+    if state is None:
+        state = torch.zeros((B, Hv, Dv, Dk), dtype=torch.float32, device=q.device)
+    if state.dtype != torch.float32 or tuple(state.shape) != (B, Hv, Dv, Dk):
+        raise ValueError("state must be fp32 [B, Hv, Dv, Dk]")
+    q, k, v, g, beta, state = (t.contiguous() for t in (q, k, v, g, beta, state))
+    return q, k, v, g, beta, state, (B, T, Hk, Dk, Hv, Dv)
+
+
+def gdn_recurrent(q, k, v, g, beta, state=None, mask=None):
+    """The gated delta recurrence position by position: returns (y [B, T, Hv, Dv] in q's dtype, new state)."""
+    q, k, v, g, beta, state, (B, T, Hk, Dk, Hv, Dv) = _gdn_common(q, k, v, g, beta, state)
+    y = torch.empty((B, T, Hv, Dv), dtype=q.dtype, device=q.device)
+    s_out = torch.empty_like(state)
+    m = None
+    if mask is not None:
+        m = mask.reshape(B, T).to(torch.uint8).contiguous()
+    rc = lib().lb2_gdn_recurrent(_ptr(q), _ptr(k), dtype_code(q), _ptr(v), dtype_code(v), _ptr(g), dtype_code(g),
+                                 int(g.dim() == 4), _ptr(beta), dtype_code(beta), _ptr(m), _ptr(state), _ptr(s_out),
+                                 _ptr(y), B, T, Hk, Dk, Hv, Dv, _stream(q))
+    check(rc, "gdn_recurrent")
+    return y, s_out
+
+
+def gdn_chunked_supported(q, v, g, mask):
+    return (mask is None and g.dim() == 3 and q.shape[-1] == 128 and v.shape[-1] == 128
+            and q.dtype in (torch.bfloat16, torch.float16))
+
+
+def gdn_chunked(q, k, v, g, beta, state=None):
+    """The same recurrence in chunks of 64 positions on tensor cores (scalar gate, no mask, Dk = Dv = 128)."""
+    q, k, v, g, beta, state, (B, T, Hk, Dk, Hv, Dv) = _gdn_common(q, k, v, g, beta, state)
+    y = torch.empty((B, T, Hv, Dv), dtype=q.dtype, device=q.device)
+    s_out = torch.empty_like(state)
+    nbytes = lib().lb2_gdn_chunked_workspace_size(B, T, Hk, Hv, Dk, Dv)
+    ws = workspace(q.device, nbytes, "gdn_chunked")
+    rc = lib().lb2_gdn_chunked(_ptr(q), _ptr(k), dtype_code(q), _ptr(v), dtype_code(v), _ptr(g), dtype_code(g),
+                               _ptr(beta), dtype_code(beta), _ptr(state), _ptr(s_out), _ptr(y), B, T, Hk, Dk, Hv, Dv,
+                               _ptr(ws), ws.numel(), _stream(q))
+    check(rc, "gdn_chunked")
+    return y, s_out
