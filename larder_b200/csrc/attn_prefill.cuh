@@ -40,7 +40,7 @@ struct Cfg {
   static constexpr int K_OFF = Q_OFF + QBYTES;
   static constexpr int V_OFF = K_OFF + STAGES * KBYTES;
   static constexpr int P_OFF = V_OFF + STAGES * KBYTES;
-  static constexpr int BAR_OFF = P_OFF + PBYTES;
+  static constexpr int BAR_OFF = P_OFF + 2 * PBYTES;  // P double-buffered: P_j is written while PV_{j-1} runs
   // at least ~120 KB so that one CTA holds an SM (its TMEM allocation is all 512 columns)
   static constexpr int SMEM_RAW = BAR_OFF + 256;
   static constexpr int SMEM_BYTES = (SMEM_RAW < 120 * 1024 ? 120 * 1024 : SMEM_RAW) + 1024;
@@ -173,11 +173,11 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_kernel(const __grid_constant_
   uint64_t* v_empty = bars + 7;  // [2]
   uint64_t* s_full = bars + 9;   // [2]
   uint64_t* s_free = bars + 11;  // [2]
-  uint64_t* p_full = bars + 13;
-  uint64_t* o_done = bars + 14;
-  uint64_t* drain = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 17);
+  uint64_t* p_full = bars + 13;  // [2] P_j written into buffer j & 1
+  uint64_t* o_done = bars + 15;  // [2] PV_j complete, committed to o_done[j & 1]
+  uint64_t* drain = bars + 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 19);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -190,8 +190,10 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_kernel(const __grid_constant_
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], SOFTMAX_WARPS * 32);
     }
-    mbar_init(p_full, SOFTMAX_WARPS * 32);
-    mbar_init(o_done, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&p_full[i], SOFTMAX_WARPS * 32);
+      mbar_init(&o_done[i], 1);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -256,16 +258,17 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_kernel(const __grid_constant_
       auto issue_pv = [&](int i) -> bool {
         const int st = i & 1;
         if (!mbar_wait(&v_full[st], (i >> 1) & 1, 22)) return false;
-        if (!mbar_wait(p_full, i & 1, 23)) return false;
+        if (!mbar_wait(&p_full[st], (i >> 1) & 1, 23)) return false;
         tc_fence_after();
         const uint32_t v_addr = smem_u32(sm + C::V_OFF + st * C::KBYTES);
+        const uint32_t pb = p_addr + st * C::PBYTES;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t a = sdesc(p_addr + (kk >> 2) * BM * 128 + (kk & 3) * 32, 16, 1024);
+          const uint64_t a = sdesc(pb + (kk >> 2) * BM * 128 + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = sdesc(v_addr + kk * 16 * 128, BN * 128, 1024);
           umma_ss(tmem + C::O_COL, a, bd, IDESC_PV, (i > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(o_done);
+        umma_commit(&o_done[st]);
         umma_commit(&v_empty[st]);
         return true;
       };
@@ -328,33 +331,32 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_kernel(const __grid_constant_
 
       const int key0 = j * BN;
       const bool full_tile = key0 + BN - 1 <= lim && key0 + BN <= p.N && !mrow;
-      float tmax = -INFINITY;
+      float tmax = -INFINITY;  // in raw score units (scale > 0 keeps the order)
+      if (full_tile) {
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
-        float x = s[c] * p.scale_log2;
-        if (!full_tile) {
+        for (int c = 0; c < BN; ++c) tmax = fmaxf(tmax, s[c]);
+      } else {
+#pragma unroll
+        for (int c = 0; c < BN; ++c) {
           const int key = key0 + c;
           bool vis = key <= lim && key < p.N;
           if (mrow && vis) vis = mrow[int64_t(key) * p.m_st[1]] != 0;
-          x = vis ? x : -INFINITY;
+          s[c] = vis ? s[c] : -INFINITY;
+          tmax = fmaxf(tmax, s[c]);
         }
-        s[c] = x;
-        tmax = fmaxf(tmax, x);
       }
-      // PV_{j-1} must be done before P is rewritten (one P buffer) and before O may be rescaled.
-      if (j > 0) {
-        if (!mbar_wait(o_done, (j - 1) & 1, 32)) {
+      const float tmax2 = tmax * p.scale_log2;  // base-2 units
+      // The running max moves only when it grew by more than 2^8 (fp32 O and the 16-bit P absorb the rest); O is
+      // rescaled in TMEM then, after PV_{j-1} has completed. tcgen05.ld / st are warp-collective, so a warp rescales
+      // when any of its rows must (factor 1 for the others).
+      const bool move = tmax2 > m_run + 8.f;
+      const float factor = move ? ex2f(m_run - tmax2) : 1.f;
+      if (__any_sync(0xffffffffu, move && j > 0 && l_run > 0.f)) {
+        if (!mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, 32)) {
           ok = false;
           break;
         }
         tc_fence_after();
-      }
-      // The running max moves only when it grew by more than 2^8 (fp32 O and the 16-bit P absorb the rest); O is
-      // rescaled in TMEM then. tcgen05.ld / st are warp-collective, so a warp rescales when any of its rows must
-      // (factor 1 for the others).
-      const bool move = tmax > m_run + 8.f;
-      const float factor = move ? ex2f(m_run - tmax) : 1.f;
-      if (__any_sync(0xffffffffu, move && j > 0 && l_run > 0.f)) {
 #pragma unroll 1
         for (int c = 0; c < D; c += 32) {
           float ov[32];
@@ -368,16 +370,24 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_kernel(const __grid_constant_
       }
       if (move) {
         l_run *= factor;
-        m_run = tmax;
+        m_run = tmax2;
       }
-      const float mu = m_run == -INFINITY ? 0.f : m_run;
+      // P buffer j & 1 was last read by PV_{j-2}.
+      if (j >= 2) {
+        if (!mbar_wait(&o_done[j & 1], ((j >> 1) - 1) & 1, 34)) {
+          ok = false;
+          break;
+        }
+      }
+      const float nm = m_run == -INFINITY ? 0.f : -m_run;
+      uint8_t* pbuf = prow + (j & 1) * C::PBYTES;
       float ls = 0.f;
 #pragma unroll
       for (int c = 0; c < BN; c += 8) {
         float e[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-          e[u] = ex2f(s[c + u] - mu);
+          e[u] = ex2f(fmaf(s[c + u], p.scale_log2, nm));
           ls += e[u];
         }
         uint4 pk;
@@ -386,15 +396,15 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_kernel(const __grid_constant_
         pk.z = pack2<T>(e[4], e[5]);
         pk.w = pack2<T>(e[6], e[7]);
         const int box = c >> 6, ch = (c & 63) >> 3;
-        *reinterpret_cast<uint4*>(prow + box * BM * 128 + r * 128 + ((ch ^ (r & 7)) << 4)) = pk;
+        *reinterpret_cast<uint4*>(pbuf + box * BM * 128 + r * 128 + ((ch ^ (r & 7)) << 4)) = pk;
       }
       l_run += ls;
       fence_proxy_async_shared();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[j & 1]);
     }
     if (ok && ntiles > 0) {
-      if (!mbar_wait(o_done, (ntiles - 1) & 1, 33)) ok = false;
+      if (!mbar_wait(&o_done[(ntiles - 1) & 1], ((ntiles - 1) >> 1) & 1, 33)) ok = false;
       tc_fence_after();
     }
     // ---------------------------------------------------------------------------------- epilogue

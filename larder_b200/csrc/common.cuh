@@ -1,8 +1,8 @@
 // Shared device/host helpers of the larder_b200 kernels (sm_100a only).
 //
-// Every device-side wait in this library is bounded: an mbarrier poll gives up after a fixed number of tries
-// (several seconds of polling at the sleep hint used), records where it gave up in the library's device status
-// word and lets the kernel return. The host reads the word with lb2_status(); nothing traps or spins forever.
+// Every device-side wait in this library is bounded: an mbarrier poll gives up after kWaitNs of %globaltimer time,
+// records where it gave up in the library's device status word and lets the kernel return. The host reads the word
+// with lb2_status(); nothing traps or spins forever.
 #pragma once
 
 #include <cuda.h>
@@ -80,10 +80,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
+      : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
 }
@@ -98,17 +98,23 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // tile load queued behind a few hundred others, microseconds), short enough that a broken phase ends the launch.
 constexpr uint64_t kWaitNs = 2000000000ull;
 
-// Waits for the phase with this parity; false (and the status word set) when the time bound ran out.
+// Waits for the phase with this parity by polling try_wait (no suspend hint: a hand-off between warps is on the
+// critical path of every tile), reading the global timer only every 1024 polls; false (and the status word set)
+// when the time bound ran out.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int where) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer_ns() - t0 > kWaitNs) {
-      report_timeout(where);
-      return false;
+  uint64_t t0 = 0;
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 1023u) == 0) {
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitNs) {
+        report_timeout(where);
+        return false;
+      }
     }
   }
-  return true;
 }
 
 // 1-D bulk copy global -> shared, completing on an mbarrier (both addresses 16-byte aligned, bytes % 16 == 0).
