@@ -1,14 +1,15 @@
 // Prefill / multi-row causal GQA attention on the 5th-generation tensor cores (tcgen05, TMEM accumulators).
 //
 // One CTA computes one 128-row query tile of one head: O = softmax(scale Q K^T + mask) V [* sigmoid(gate)].
-// Warp roles (192 threads):
-//   warps 0-3  softmax + epilogue: thread i owns query row i, which is TMEM lane i of S and O; reads S with
-//              tcgen05.ld, keeps the running max / sum in base 2, writes P (bf16/f16) into a 128-byte swizzled
-//              shared tile, rescales its O row in TMEM only when its max grew by more than 2^8, and finally
-//              normalises O, applies the optional sigmoid gate and stores the row.
-//   warp 4     TMA producer: Q once, then K and V tiles (128-byte swizzled boxes of 64 head-dim elements) into
+// Warp roles (320 threads):
+//   warps 0-7  softmax + epilogue: query row r = 32 (w % 4) + lane is TMEM lane r of S and O; warps w and w + 4
+//              split the row's columns, exchanging the row max through shared memory. They read S with
+//              tcgen05.ld, keep the running max / sum in base 2, write P (bf16/f16) into a double-buffered
+//              128-byte swizzled shared tile, rescale the O row in TMEM only when the max grew by more than 2^8,
+//              and finally normalise O, apply the optional sigmoid gate and store the row.
+//   warp 8     TMA producer: Q once, then K and V tiles (128-byte swizzled boxes of 64 head-dim elements) into
 //              two-stage rings.
-//   warp 5     MMA issuer (one elected thread): S_j = Q K_j^T (SS operands, M=128, N=BN) into one of two S
+//   warp 9     MMA issuer (one elected thread): S_j = Q K_j^T (SS operands, M=128, N=BN) into one of two S
 //              buffers in TMEM, then O += P_{j-1} V_{j-1} (M=128, N=D, V read MN-major), so S_{j+1} runs while
 //              the softmax warps work on S_j. Completion is signalled with tcgen05.commit on mbarriers.
 // Causal is bottom-right (row t sees keys 0 .. N - T + t, chunkattn.py:359-365); a tile reads only the KV tiles
@@ -23,10 +24,10 @@ namespace lb2 {
 namespace prefill {
 
 constexpr int BM = 128;
-constexpr int THREADS = 192;
-constexpr int SOFTMAX_WARPS = 4;
-constexpr int PRODUCER_WARP = 4;
-constexpr int MMA_WARP = 5;
+constexpr int THREADS = 320;
+constexpr int SOFTMAX_WARPS = 8;  // two per SM sub-partition: warps w and w + 4 share rows, split the columns
+constexpr int PRODUCER_WARP = 8;
+constexpr int MMA_WARP = 9;
 constexpr int TMEM_COLS = 512;
 
 template <int D>
@@ -42,7 +43,8 @@ struct Cfg {
   static constexpr int P_OFF = V_OFF + STAGES * KBYTES;
   static constexpr int BAR_OFF = P_OFF + 2 * PBYTES;  // P double-buffered: P_j is written while PV_{j-1} runs
   // at least ~120 KB so that one CTA holds an SM (its TMEM allocation is all 512 columns)
-  static constexpr int SMEM_RAW = BAR_OFF + 256;
+  static constexpr int RED_OFF = BAR_OFF + 256;  // [2 halves][128 rows] fp32: a row's partial max / sum
+  static constexpr int SMEM_RAW = RED_OFF + 2 * BM * 4;
   static constexpr int SMEM_BYTES = (SMEM_RAW < 120 * 1024 ? 120 * 1024 : SMEM_RAW) + 1024;
   static constexpr int S_COL = 0;       // S buffers at columns [0, BN) and [BN, 2 BN)
   static constexpr int O_COL = 2 * BN;  // O at [2 BN, 2 BN + D)
@@ -307,9 +309,14 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_kernel(const __grid_constant_
     }
   } else {
     // ------------------------------------------------------------------------------------ softmax warps
-    const int r = threadIdx.x;  // row in the tile == TMEM lane
+    constexpr int HC = BN / 2;  // S columns a thread owns
+    constexpr int HD = D / 2;   // O columns a thread owns
+    const int r = 32 * (warp & 3) + lane;  // row in the tile == TMEM lane
+    const int hf = warp >> 2;              // which half of the columns
     const int row = r0 + r;
-    const uint32_t lane_base = tmem + (uint32_t(warp * 32) << 16);
+    const uint32_t lane_base = tmem + (uint32_t(32 * (warp & 3)) << 16);
+    const uint32_t pair_bar = 2 + (warp & 3);  // named barrier of warps w and w + 4 (ids 2..5)
+    float* red = reinterpret_cast<float*>(sm + C::RED_OFF);
     const int lim = p.mask_kind == LB2_MASK_CAUSAL ? p.N - p.T + row : p.N - 1;
     const uint8_t* mrow = (p.mask_kind == LB2_MASK_ARRAY && row < p.T) ? p.mask + int64_t(row) * p.m_st[0] : nullptr;
     float m_run = -INFINITY, l_run = 0.f;
@@ -317,54 +324,72 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_kernel(const __grid_constant_
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
       const int st = j & 1;
-      if (*abort_flag || !mbar_wait(&s_full[st], (j >> 1) & 1, 31)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      float s[BN];
+      // A failed wait never leaves a warp alone at a barrier: the decision to stop is made warp-uniform before
+      // the warp-collective TMEM loads and pair-uniform at the max exchange (bar.red.and), where both warps of a
+      // row pair leave the loop together.
+      bool okj = ok && !*abort_flag && mbar_wait(&s_full[st], (j >> 1) & 1, 31);
+      okj = __all_sync(0xffffffffu, okj);
+      float s[HC];
+      if (okj) {
+        tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < BN; c += 32) tmem_ld32(lane_base + C::S_COL + st * BN + c, s + c);
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&s_free[st]);
-
-      const int key0 = j * BN;
-      const bool full_tile = key0 + BN - 1 <= lim && key0 + BN <= p.N && !mrow;
-      float tmax = -INFINITY;  // in raw score units (scale > 0 keeps the order)
-      if (full_tile) {
-#pragma unroll
-        for (int c = 0; c < BN; ++c) tmax = fmaxf(tmax, s[c]);
+        for (int c = 0; c < HC; c += 32) tmem_ld32(lane_base + C::S_COL + st * BN + hf * HC + c, s + c);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&s_free[st]);
       } else {
 #pragma unroll
-        for (int c = 0; c < BN; ++c) {
+        for (int c = 0; c < HC; ++c) s[c] = -INFINITY;
+      }
+
+      const int key0 = j * BN + hf * HC;
+      const bool full_tile = j * BN + BN - 1 <= lim && j * BN + BN <= p.N && !mrow;
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (full_tile) {
+#pragma unroll
+        for (int c = 0; c < HC; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
+      } else {
+#pragma unroll
+        for (int c = 0; c < HC; ++c) {
           const int key = key0 + c;
           bool vis = key <= lim && key < p.N;
           if (mrow && vis) vis = mrow[int64_t(key) * p.m_st[1]] != 0;
           s[c] = vis ? s[c] : -INFINITY;
-          tmax = fmaxf(tmax, s[c]);
+          mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
         }
+      }
+      float tmax = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));  // raw score units (scale > 0)
+      red[hf * BM + r] = tmax;
+      uint32_t pair_ok;
+      asm volatile(
+          "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+          "bar.red.and.pred q, %2, 64, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+          : "=r"(pair_ok)
+          : "r"(uint32_t(okj)), "r"(pair_bar)
+          : "memory");
+      tmax = fmaxf(tmax, red[(1 - hf) * BM + r]);
+      asm volatile("bar.sync %0, 64;" ::"r"(pair_bar));  // both read before the next tile rewrites
+      if (!pair_ok) {
+        ok = false;
+        break;
       }
       const float tmax2 = tmax * p.scale_log2;  // base-2 units
       // The running max moves only when it grew by more than 2^8 (fp32 O and the 16-bit P absorb the rest); O is
       // rescaled in TMEM then, after PV_{j-1} has completed. tcgen05.ld / st are warp-collective, so a warp rescales
-      // when any of its rows must (factor 1 for the others).
+      // when any of its rows must (factor 1 for the others); both warps of a row pair decide alike.
       const bool move = tmax2 > m_run + 8.f;
       const float factor = move ? ex2f(m_run - tmax2) : 1.f;
       if (__any_sync(0xffffffffu, move && j > 0 && l_run > 0.f)) {
-        if (!mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, 32)) {
-          ok = false;
-          break;
-        }
+        if (!mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, 32)) ok = false;
         tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < D; c += 32) {
+        for (int c = 0; c < HD; c += 32) {
           float ov[32];
-          tmem_ld32(lane_base + C::O_COL + c, ov);
+          tmem_ld32(lane_base + C::O_COL + hf * HD + c, ov);
           tmem_wait_ld();
 #pragma unroll
           for (int e = 0; e < 32; ++e) ov[e] *= factor;
-          tmem_st32(lane_base + C::O_COL + c, ov);
+          tmem_st32(lane_base + C::O_COL + hf * HD + c, ov);
         }
         tmem_wait_st();
       }
@@ -373,32 +398,28 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_kernel(const __grid_constant_
         m_run = tmax2;
       }
       // P buffer j & 1 was last read by PV_{j-2}.
-      if (j >= 2) {
-        if (!mbar_wait(&o_done[j & 1], ((j >> 1) - 1) & 1, 34)) {
-          ok = false;
-          break;
-        }
-      }
+      if (j >= 2 && !mbar_wait(&o_done[j & 1], ((j >> 1) - 1) & 1, 34)) ok = false;
       const float nm = m_run == -INFINITY ? 0.f : -m_run;
       uint8_t* pbuf = prow + (j & 1) * C::PBYTES;
-      float ls = 0.f;
+      float ls4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < BN; c += 8) {
+      for (int c = 0; c < HC; c += 8) {
         float e[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           e[u] = ex2f(fmaf(s[c + u], p.scale_log2, nm));
-          ls += e[u];
+          ls4[u & 3] += e[u];
         }
         uint4 pk;
         pk.x = pack2<T>(e[0], e[1]);
         pk.y = pack2<T>(e[2], e[3]);
         pk.z = pack2<T>(e[4], e[5]);
         pk.w = pack2<T>(e[6], e[7]);
-        const int box = c >> 6, ch = (c & 63) >> 3;
+        const int cc = hf * HC + c;
+        const int box = cc >> 6, ch = (cc & 63) >> 3;
         *reinterpret_cast<uint4*>(pbuf + box * BM * 128 + r * 128 + ((ch ^ (r & 7)) << 4)) = pk;
       }
-      l_run += ls;
+      l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
       fence_proxy_async_shared();
       tc_fence_before();
       mbar_arrive(&p_full[j & 1]);
@@ -408,20 +429,24 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_kernel(const __grid_constant_
       tc_fence_after();
     }
     // ---------------------------------------------------------------------------------- epilogue
-    // Warp-uniform from here on: every lane takes part in the TMEM loads, only rows inside T store.
+    // Warp-uniform from here on: every lane takes part in the TMEM loads, only rows inside T store. The row sum is
+    // the two halves' partial sums.
     ok = __all_sync(0xffffffffu, ok);
+    red[hf * BM + r] = l_run;
+    asm volatile("bar.sync %0, 64;" ::"r"(pair_bar));
+    const float l_tot = l_run + red[(1 - hf) * BM + r];
     const bool have_o = ntiles > 0 && ok;
     const bool store = row < p.T;
-    T* orow = reinterpret_cast<T*>(p.o) + b * p.o_st[0] + int64_t(h) * p.o_st[1] + int64_t(row) * p.o_st[2];
+    T* orow = reinterpret_cast<T*>(p.o) + b * p.o_st[0] + int64_t(h) * p.o_st[1] + int64_t(row) * p.o_st[2] + hf * HD;
     const T* grow = p.gate ? reinterpret_cast<const T*>(p.gate) + b * p.g_st[0] + int64_t(h) * p.g_st[1] +
-                                 int64_t(row) * p.g_st[2]
+                                 int64_t(row) * p.g_st[2] + hf * HD
                            : nullptr;
-    const float inv = (have_o && l_run > 0.f) ? 1.f / l_run : 0.f;
+    const float inv = (have_o && l_tot > 0.f) ? 1.f / l_tot : 0.f;
 #pragma unroll 1
-    for (int c = 0; c < D; c += 32) {
+    for (int c = 0; c < HD; c += 32) {
       float ov[32];
       if (have_o) {
-        tmem_ld32(lane_base + C::O_COL + c, ov);
+        tmem_ld32(lane_base + C::O_COL + hf * HD + c, ov);
         tmem_wait_ld();
       } else {
 #pragma unroll
