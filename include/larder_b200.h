@@ -100,6 +100,25 @@ int lb2_attn_decode_partial(const void* q, const int64_t* q_st, const void* k, c
                             int Hkv, int T, int N, int D, int dtype, float scale, int split, void* workspace,
                             size_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of lb2_attn_decode, for callers that cannot call cudaMalloc: an engine whose device
+ * memory is owned and budgeted by its own allocator (every byte counted against a memory budget, so a library-side
+ * allocation would break the budget), or a caller on a latency-critical path where cudaMalloc's implicit device
+ * synchronisation is not acceptable. This entry has no counterpart in the reference (whose decode runs inside MLX's
+ * allocator); it exists for such callers of this library.
+ * Arguments and results as lb2_attn_decode, without the workspace: the split partials and ticket counters live in a
+ * file-scope device array of LB2_NOALLOC_SCRATCH_BYTES (8 MiB) that every GPU loading this library holds until the
+ * process exits. A call whose workspace (lb2_attn_decode_workspace_size) exceeds that size returns LB2_EINVAL;
+ * choose a larger `split` or use lb2_attn_decode. The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current); make that first call before any stream capture. Each call
+ * clears the counters it needs with cudaMemsetAsync on `stream`; it calls no cudaMalloc / cudaFree. All calls share
+ * the one array, which keeps the last call's contents: calls that overlap on the GPU (different streams, or
+ * different host threads on one device) race on it and must be ordered by the caller. */
+#define LB2_NOALLOC_SCRATCH_BYTES (8u << 20)
+int lb2_attn_decode_noalloc(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
+                            const int64_t* v_st, void* o, const int64_t* o_st, const int32_t* kv_len, int B, int Hq,
+                            int Hkv, int T, int N, int D, int dtype, float scale, int causal, int split,
+                            void* stream);
+
 /* Merges R partials: o[row] = sum_r w_r part_o[r][row] / sum_r w_r, w_r = exp(part_lse[r][row] - max_r lse),
  * rows = B * Hq * T (row-major [B, Hq, T]), o [B, Hq, T, D] with strides o_st in dtype. An all -inf row gives 0.
  * Replaces the LSE merge of foldattn_merge (foldattn.py:188-211) / cpu_kern.cpp:607-628, across ranks. */

@@ -28,6 +28,8 @@ SIGNATURES = {
                          _p, _sz, _p], _i),
     "lb2_attn_decode_partial": ([_p, _i64p, _p, _i64p, _p, _i64p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _i,
                                  _p, _sz, _p], _i),
+    "lb2_attn_decode_noalloc": ([_p, _i64p, _p, _i64p, _p, _i64p, _p, _i64p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _i,
+                                 _i, _p], _i),
     "lb2_attn_combine": ([_p, _p, _i, _i, _i, _i, _i, _p, _i64p, _i, _p], _i),
     "lb2_gdn_recurrent": ([_p, _p, _i, _p, _i, _p, _i, _i, _p, _i, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p], _i),
     "lb2_gdn_chunked_workspace_size": ([_i, _i, _i, _i, _i, _i], _sz),

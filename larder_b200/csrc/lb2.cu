@@ -220,6 +220,35 @@ static int map4(CUtensorMap* m, const void* base, const int64_t* st, int B, int 
 }
 
 }  // namespace prefill
+// ------------------------------------------------------------------------------------------------ allocation-free decode
+
+// The scratch of lb2_attn_decode_noalloc (split partials and ticket counters): a file-scope device array, so that
+// the entry point never allocates. Host code must not pass this name to a kernel (in host code it is a host-side
+// stand-in); its device address comes from cudaGetSymbolAddress, once per device.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[LB2_NOALLOC_SCRATCH_BYTES];
+
+namespace noalloc {
+
+static std::mutex g_mu;
+static void* g_addr[64];  // device address of g_noalloc_scratch, per device
+
+// The array's device address on the current device, looked up on the first call there (with that device current).
+static int scratch(void** out) {
+  int dev = 0;
+  LB2_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(LB2_EINVAL, "decode_noalloc: device index out of range");
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (!g_addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+    g_addr[dev] = p;
+  }
+  *out = g_addr[dev];
+  return LB2_OK;
+}
+
+}  // namespace noalloc
 }  // namespace lb2
 
 using namespace lb2;
@@ -262,6 +291,27 @@ int lb2_attn_decode_partial(const void* q, const int64_t* q_st, const void* k, c
   LB2_CHECK_ARG(part_o != nullptr && part_lse != nullptr, "decode_partial: outputs missing");
   return decode::run(q, q_st, k, k_st, v, v_st, nullptr, nullptr, part_o, part_lse, kv_len, B, Hq, Hkv, T, N, D,
                      dtype, scale, 0, split, workspace, workspace_bytes, stream);
+}
+
+int lb2_attn_decode_noalloc(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
+                            const int64_t* v_st, void* o, const int64_t* o_st, const int32_t* kv_len, int B, int Hq,
+                            int Hkv, int T, int N, int D, int dtype, float scale, int causal, int split,
+                            void* stream) {
+  LB2_CHECK_ARG(o != nullptr && o_st != nullptr, "decode_noalloc: output missing");
+  const size_t need = lb2_attn_decode_workspace_size(B, Hq, Hkv, T, N, D, split);
+  LB2_CHECK_ARG(need > 0, "decode_noalloc: empty or unsupported shape");
+  if (need > LB2_NOALLOC_SCRATCH_BYTES)
+    return fail(LB2_EINVAL, "decode_noalloc: this call needs " + std::to_string(need) + " bytes of scratch, more than "
+                            "the " + std::to_string(LB2_NOALLOC_SCRATCH_BYTES) + "-byte static array; use a larger "
+                            "split or lb2_attn_decode with a caller workspace");
+  void* ws = nullptr;
+  int rc = noalloc::scratch(&ws);
+  if (rc) return rc;
+  // The ticket counters must start at zero; the array keeps whatever the last call left.
+  const size_t counters = decode::ws_layout(B, Hkv, 16, D, 1).ml;
+  LB2_CUDA(cudaMemsetAsync(ws, 0, counters, static_cast<cudaStream_t>(stream)));
+  return decode::run(q, q_st, k, k_st, v, v_st, o, o_st, nullptr, nullptr, kv_len, B, Hq, Hkv, T, N, D, dtype, scale,
+                     causal, split, ws, LB2_NOALLOC_SCRATCH_BYTES, stream);
 }
 
 int lb2_attn_combine(const float* part_o, const float* part_lse, int R, int B, int Hq, int T, int D, void* o,
