@@ -1,0 +1,75 @@
+"""Gated-DeltaNet on B200: the drop-in for the reference's gdn_cuda.py (gdn_cuda.py:88-99, :318-360).
+
+recurrence(q, k, v, g, beta, state, mask=None) keeps the reference's contract: q, k [B, T, Hk, Dk], v [B, T, Hv, Dv],
+g [B, T, Hv] (one gate a head) or [B, T, Hv, Dk] (per-Dk gate), beta [B, T, Hv], state [B, Hv, Dv, Dk] fp32, mask
+[B, T] or None -> (y [B, T, Hv, Dv] in q's dtype, the new state). g is the multiplicative decay (the state is
+multiplied by g, gdn_cuda.py:43). Long passes with a scalar gate and no mask run the chunked tensor-core scan
+(lb2_gdn_chunked, chunks of 64 positions); everything else -- decode steps, short verify passes, vector gates,
+masks -- runs the position-by-position kernel (lb2_gdn_recurrent). Both are CUDA; there is no ops-loop fallback.
+
+gated_delta_update keeps mlx_lm 0.32's parameter list (gdn_cuda.py:318-319) and its gating: beta = sigmoid(b)
+(doubled with allow_neg_eigval), g = compute_g(A_log, a, dt_bias) = exp(-exp(A_log) * softplus(a + dt_bias))
+(the expression gdn_cuda.py:146-149 spells out), a zero state when none is given.
+"""
+import inspect
+import sys
+
+import torch
+
+from . import ops
+
+_PARAMS = ["q", "k", "v", "a", "b", "A_log", "dt_bias", "state", "mask", "use_kernel", "lower_bound",
+           "allow_neg_eigval"]
+CHUNK_MIN_T = 64  # passes at least this long (scalar gate, no mask, Dk = Dv = 128) take the chunked scan
+
+
+def recurrence(q, k, v, g, beta, state, mask=None):
+    """The gated delta recurrence over all T positions in one launch (gdn_cuda.py:88-99's contract)."""
+    if q.shape[1] >= CHUNK_MIN_T and ops.gdn_chunked_supported(q, v, g, mask):
+        return ops.gdn_chunked(q, k, v, g, beta, state)
+    return ops.gdn_recurrent(q, k, v, g, beta, state, mask)
+
+
+def compute_g(A_log, a, dt_bias):
+    """g = exp(-exp(A_log) * softplus(a + dt_bias)) in fp32 (mlx_lm's compute_g, as gdn_cuda.py:146-149 spells it)."""
+    return torch.exp(-torch.exp(A_log.float()) * torch.nn.functional.softplus(a.float() + dt_bias.float()))
+
+
+def gated_delta_update(q, k, v, a, b, A_log, dt_bias, state=None, mask=None, *, use_kernel=True, lower_bound=None,
+                       allow_neg_eigval=False):
+    """mlx_lm's gated_delta_update with this package's kernels (gdn_cuda.py:336-353)."""
+    if lower_bound is not None:
+        raise NotImplementedError("gated_delta_update: lower_bound gating (compute_lower_bound_g) is not built")
+    beta = torch.sigmoid(b.float())
+    if allow_neg_eigval:
+        beta = beta * 2.0
+    g = compute_g(A_log, a, dt_bias)
+    if state is None:
+        B, _, Hk, Dk = q.shape
+        Hv, Dv = v.shape[-2:]
+        state = torch.zeros((B, Hv, Dv, Dk), dtype=torch.float32, device=q.device)
+    return recurrence(q, k, v, g, beta, state, mask)
+
+
+gated_delta_update._gdn_cuda = True
+
+
+def install(modules=None):
+    """Route `gated_delta_update` to this package wherever a module holds the name, as the reference rebinds it in
+    gated_delta and in every model module that already imported it (gdn_cuda.py:322-360). `modules` defaults to
+    every loaded module whose attribute of that name takes mlx_lm's parameter list; returns the modules rebound."""
+    done = []
+    cands = modules if modules is not None else [m for m in list(sys.modules.values()) if m is not None]
+    for mod in cands:
+        fn = getattr(mod, "gated_delta_update", None)
+        if fn is None or fn is gated_delta_update or getattr(fn, "_gdn_cuda", False):
+            continue
+        try:
+            params = list(inspect.signature(fn).parameters)
+        except (TypeError, ValueError):
+            continue
+        if params != _PARAMS:
+            continue
+        mod.gated_delta_update = gated_delta_update
+        done.append(mod)
+    return done
