@@ -7,6 +7,7 @@
 #include "attn_decode.cuh"
 #include "gdn_recurrent.cuh"
 #include "attn_prefill.cuh"
+#include "gdn_chunked.cuh"
 
 namespace lb2 {
 
@@ -393,17 +394,50 @@ int lb2_attn_prefill(const void* q, const int64_t* q_st, const void* k, const in
 }
 
 size_t lb2_gdn_chunked_workspace_size(int B, int T, int Hk, int Hv, int Dk, int Dv) {
-  (void)B; (void)T; (void)Hk; (void)Hv; (void)Dk; (void)Dv;
-  return 256;
+  (void)Hk;
+  if (B <= 0 || T < 0 || Hv <= 0 || Dk != gdnchunk::DK || Dv != gdnchunk::DV) return 0;
+  const int64_t nchunks = (int64_t(T) + gdnchunk::C - 1) / gdnchunk::C;
+  return size_t(int64_t(B) * Hv * nchunks * gdnchunk::UNIT * int64_t(sizeof(float))) + 256;
 }
 
 int lb2_gdn_chunked(const void* q, const void* k, int qdt, const void* v, int vdt, const void* g, int gdt,
                     const void* beta, int bdt, const float* state_in, float* state_out, void* y, int B, int T, int Hk,
                     int Dk, int Hv, int Dv, void* workspace, size_t workspace_bytes, void* stream) {
-  (void)q; (void)k; (void)qdt; (void)v; (void)vdt; (void)g; (void)gdt; (void)beta; (void)bdt; (void)state_in;
-  (void)state_out; (void)y; (void)B; (void)T; (void)Hk; (void)Dk; (void)Hv; (void)Dv; (void)workspace;
-  (void)workspace_bytes; (void)stream;
-  return fail(LB2_EINVAL, "gdn_chunked: the chunked kernel is not built into this library yet");
+  LB2_CHECK_ARG(B > 0 && T >= 0 && Hk > 0 && Hv > 0, "gdn_chunked: empty shape");
+  LB2_CHECK_ARG(Hv % Hk == 0, "gdn_chunked: Hv must be a multiple of Hk");
+  LB2_CHECK_ARG(Dk == gdnchunk::DK && Dv == gdnchunk::DV, "gdn_chunked: Dk = Dv = 128 only");
+  LB2_CHECK_ARG(qdt == LB2_BF16 || qdt == LB2_F16, "gdn_chunked: q/k must be bf16 or f16");
+  for (int dt : {vdt, gdt, bdt}) LB2_CHECK_ARG(dt >= LB2_F32 && dt <= LB2_F16, "gdn_chunked: dtype");
+  LB2_CHECK_ARG(vdt == qdt, "gdn_chunked: v must share q's dtype (y is written in it)");
+  LB2_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(workspace), "gdn_chunked: q, k and workspace 16-byte aligned");
+  LB2_CHECK_ARG(workspace_bytes >= lb2_gdn_chunked_workspace_size(B, T, Hk, Hv, Dk, Dv), "gdn_chunked: workspace too small");
+  gdnchunk::Params p{q, k, v, g, beta, qdt, vdt, gdt, bdt, state_in, state_out, y, B, T, Hk, Hv,
+                     (T + gdnchunk::C - 1) / gdnchunk::C, static_cast<float*>(workspace)};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  static int attr_dev = -1;
+  int dev = 0;
+  LB2_CUDA(cudaGetDevice(&dev));
+  if (attr_dev != dev) {
+    LB2_CUDA(cudaFuncSetAttribute(gdnchunk::prep_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  gdnchunk::PrepSmem::BYTES));
+    LB2_CUDA(cudaFuncSetAttribute(gdnchunk::prep_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  gdnchunk::PrepSmem::BYTES));
+    LB2_CUDA(cudaFuncSetAttribute(gdnchunk::scan_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  gdnchunk::ScanSmem::BYTES));
+    LB2_CUDA(cudaFuncSetAttribute(gdnchunk::scan_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  gdnchunk::ScanSmem::BYTES));
+    attr_dev = dev;
+  }
+  const dim3 gp(unsigned(p.nchunks), unsigned(Hv), unsigned(B)), gs(gdnchunk::DV / gdnchunk::DVB, Hv, B);
+  if (qdt == LB2_BF16) {
+    if (p.nchunks > 0) gdnchunk::prep_kernel<__nv_bfloat16><<<gp, 128, gdnchunk::PrepSmem::BYTES, st>>>(p);
+    gdnchunk::scan_kernel<__nv_bfloat16><<<gs, 128, gdnchunk::ScanSmem::BYTES, st>>>(p);
+  } else {
+    if (p.nchunks > 0) gdnchunk::prep_kernel<__half><<<gp, 128, gdnchunk::PrepSmem::BYTES, st>>>(p);
+    gdnchunk::scan_kernel<__half><<<gs, 128, gdnchunk::ScanSmem::BYTES, st>>>(p);
+  }
+  LB2_CUDA(cudaGetLastError());
+  return LB2_OK;
 }
 
 int lb2_gdn_recurrent(const void* q, const void* k, int qdt, const void* v, int vdt, const void* g, int gdt,
