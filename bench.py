@@ -232,7 +232,7 @@ def bench_decode(torch, ops, dev, rank, world, args, stream, pk, pk_kind, barrie
                        "kernel": "lb2::decode::decode_kernel<bf16,128,1>",
                        "algorithmic_bytes_per_launch": alg_bytes}
     out["clocks"] = clk.summary()
-    out["gpu_launches"] = args.steps  # one decode kernel a step (the split merge runs inside it)
+    out["gpu_launches"] = 2 * args.steps  # a step: the persistent split-KV kernel and the split combine
 
     # e2e through the public API: q from pinned host memory each step, o read back each step
     q_host = [s[0].pin_memory() for s in sets]
@@ -300,6 +300,7 @@ def bench_prefill(torch, ops, dev, rank, world, args, stream, pk, pk_kind, barri
 
 
 def bench_gdn(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_over_ranks):
+    """the GDN decode step at B = 16 (state GB/s) and the 8192-token chunked prefill."""
     g = torch.Generator(device=dev).manual_seed(4000 + rank)
     B, Hk, Hv, D = 16, 16, 32, 128
     copies = 3  # 3 x 67 MB of state: consecutive steps miss L2
@@ -326,7 +327,40 @@ def bench_gdn(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_
     per = ms / args.steps
     state_bytes = B * Hv * D * D * 4 * 2
     gbs = state_bytes / (per * 1e-3) / 1e9
-    res = {"decode": {"value": round(world * gbs, 1), "unit": "GB/s", "ms_per_step": round(per, 5),
+    # prefill: configs[3], B=1, T=8192 through the chunked scan (two launches), and the position-by-position kernel
+    T = 8192
+    pq = torch.nn.functional.normalize(torch.randn(1, T, Hk, D, generator=g, device=dev), dim=-1).to(torch.bfloat16)
+    pk_ = torch.nn.functional.normalize(torch.randn(1, T, Hk, D, generator=g, device=dev), dim=-1).to(torch.bfloat16)
+    pv = torch.randn(1, T, Hv, D, generator=g, device=dev).to(torch.bfloat16)
+    pb = torch.sigmoid(torch.randn(1, T, Hv, generator=g, device=dev)).to(torch.bfloat16)
+    pg = torch.exp(-torch.nn.functional.softplus(torch.randn(1, T, Hv, generator=g, device=dev)))
+    s0 = torch.zeros(1, Hv, D, D, device=dev)
+
+    def pre(i):
+        ops.gdn_chunked(pq, pk_, pv, pg, pb, s0)
+
+    def pre_rec(i):
+        ops.gdn_recurrent(pq, pk_, pv, pg, pb, s0)
+
+    for i in range(args.warmup):
+        pre(i)
+    barrier_sync()
+    ms_p = max_over_ranks(cuda_time(torch, pre, args.steps, stream)) / args.steps
+    pre_rec(0)
+    barrier_sync()
+    ms_r = max_over_ranks(cuda_time(torch, pre_rec, max(2, args.steps // 10), stream)) / max(2, args.steps // 10)
+    flop = 7.0 * T * Hv * D * D
+    pbytes = 2 * T * Hk * D * 2 + 2 * T * Hv * D * 2 + 2 * T * Hv * 4 + 2 * Hv * D * D * 4
+    t_roof = max(flop / (pk["bf16_tflops"] * 1e12), pbytes / (pk["hbm_gbs"] * 1e9))
+    prefill = {"value": round(world * flop / (ms_p * 1e-3) / 1e12, 2), "unit": "TFLOP/s (recurrence FLOP)",
+               "ms_per_step": round(ms_p, 4), "recurrent_kernel_ms": round(ms_r, 4),
+               "workload": "configs[3] prefill: B=1, T=8192, Hk 16, Hv 32, 128x128, chunk 64, zero state",
+               "flop_per_step": flop, "algorithmic_bytes": pbytes, "gpu_launches_per_step": 2,
+               "roofline": {"bound": "max(tensor, hbm)", "roof_ms": round(t_roof * 1e3, 4),
+                            "frac": round(t_roof * 1e3 / ms_p, 4), "unit": "time",
+                            "kernel": "lb2::gdnchunk::{prep_kernel, scan_kernel}"}}
+    res = {"prefill": prefill,
+           "decode": {"value": round(world * gbs, 1), "unit": "GB/s", "ms_per_step": round(per, 5),
                       "workload": "configs[3] decode step: B=16, Hk 16, Hv 32, 128x128 fp32 state read+written",
                       "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                                    "frac": round(gbs / pk["hbm_gbs"], 4),

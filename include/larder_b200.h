@@ -71,15 +71,15 @@ int lb2_attn_prefill(const void* q, const int64_t* q_st, const void* k, const in
  * Split-KV decode attention (few query rows over a long KV cache; HBM-bandwidth bound).
  *
  * The G*T query rows that share a KV head are folded into one tile (foldattn.py:230-259); keys are cut into
- * splits of `split` keys (a multiple of 64, or 0 to let the library choose), each split computes an fp32
- * partial (o, max, sum) with an online softmax, and the last split of each (b, kv head) to finish merges them by
- * log-sum-exp (foldattn.py:188-211, cpu_kern.cpp:607-628) and writes o.
+ * splits of `split` keys (a multiple of 64, or 0 to let the library choose; raised so that a sequence has at most
+ * 2 D splits), each split computes an fp32 partial (o, max, sum) with an online softmax in a persistent kernel,
+ * and a second kernel merges the splits of each (b, kv head) by log-sum-exp (foldattn.py:188-211,
+ * cpu_kern.cpp:607-628) and writes o.
  *   q [B, Hq, T, D], k/v [B, Hkv, N, D] (N = capacity), o [B, Hq, T, D]: strides as in lb2_attn_prefill
  *   kv_len int32 [B] device array of per-sequence key counts (<= N), or NULL for N everywhere
  *   causal: 1 for bottom-right causal over each sequence's own length (T >= 2 verify rows), else 0
- *   workspace: lb2_attn_decode_workspace_size() bytes, 256-byte aligned, ZEROED before its first use (the
- *   kernel returns its counters to zero, so one zeroing lasts the workspace's life). Calls that share a
- *   workspace must be ordered on one stream.
+ *   workspace: lb2_attn_decode_workspace_size() bytes, 256-byte aligned, any contents (a call writes every
+ *   partial it reads). Calls that share a workspace must be ordered on one stream.
  * Limits: G*T <= 32 for D <= 128, G*T <= 16 for D = 256; dtype LB2_BF16 or LB2_F16; D in {64, 128, 256}.
  * Replaces: decode SDPA (chunkattn.gqa_sdpa + _gqa_route, chunkattn.py:638-657, :679-696; stream_fast.py's
  * _sdpa_parts / two-pass vector SDPA, :5952-6098), foldattn.fold (foldattn.py:230-259) and the stock decode SDPA
@@ -105,14 +105,14 @@ int lb2_attn_decode_partial(const void* q, const int64_t* q_st, const void* k, c
  * allocation would break the budget), or a caller on a latency-critical path where cudaMalloc's implicit device
  * synchronisation is not acceptable. This entry has no counterpart in the reference (whose decode runs inside MLX's
  * allocator); it exists for such callers of this library.
- * Arguments and results as lb2_attn_decode, without the workspace: the split partials and ticket counters live in a
+ * Arguments and results as lb2_attn_decode, without the workspace: the split partials live in a
  * file-scope device array of LB2_NOALLOC_SCRATCH_BYTES (8 MiB) that every GPU loading this library holds until the
  * process exits. A call whose workspace (lb2_attn_decode_workspace_size) exceeds that size returns LB2_EINVAL;
  * choose a larger `split` or use lb2_attn_decode. The first call on a device looks up the array's device address
- * (cudaGetSymbolAddress, with that device current); make that first call before any stream capture. Each call
- * clears the counters it needs with cudaMemsetAsync on `stream`; it calls no cudaMalloc / cudaFree. All calls share
- * the one array, which keeps the last call's contents: calls that overlap on the GPU (different streams, or
- * different host threads on one device) race on it and must be ordered by the caller. */
+ * (cudaGetSymbolAddress, with that device current); make that first call before any stream capture. It calls no
+ * cudaMalloc / cudaFree. All calls share the one array, which keeps the last call's contents (harmless: a call
+ * writes every partial it reads before reading it); calls that overlap on the GPU (different streams, or different
+ * host threads on one device) race on it and must be ordered by the caller. */
 #define LB2_NOALLOC_SCRATCH_BYTES (8u << 20)
 int lb2_attn_decode_noalloc(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
                             const int64_t* v_st, void* o, const int64_t* o_st, const int32_t* kv_len, int B, int Hq,

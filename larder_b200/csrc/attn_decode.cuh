@@ -1,13 +1,17 @@
 // Split-KV decode attention for a few query rows over a long KV cache (HBM-bandwidth bound).
 //
-// Work unit: one CTA per (key split s, KV head hk, sequence b). The G*T query rows sharing KV head hk are folded
-// into 16-row tiles (the fold of foldattn.py:230-259), so every K/V byte is read from HBM once per decode call.
-// A producer warp streams 64-key K and V tiles with TMA (128-byte swizzled boxes of 64 head-dim elements) into a
-// STAGES-deep mbarrier ring; four consumer warps each take 16 of a tile's 64 keys and run S = Q K^T and O += P V
-// on mma.sync m16n8k16 (fp32 accumulate) with an fp32 online softmax in base 2. The four warps' (max, sum, O) are
-// merged in shared memory, and the split's partial is merged with the other splits of (b, hk) by log-sum-exp in
-// the last CTA to finish (an atomic ticket per (b, hk)), the same combine as foldattn_merge (foldattn.py:188-211)
-// and CpuAttn's range merge (cpu_ext/cpu_kern.cpp:607-628).
+// Persistent kernel: one CTA per SM walks a static round-robin share of equal-sized work units, a unit being
+// (sequence b, one `split`-key range of it, KV head hk). The G*T query rows sharing KV head hk are folded into
+// 16-row tiles (the fold of foldattn.py:230-259), so every K/V byte is read from HBM once per call.
+// A producer warp streams, unit after unit without a pause, the unit's folded Q tile (a 2-slot ring) and its
+// 64-key K and V tiles (a STAGES-deep ring), all with TMA into 128-byte swizzled boxes of 64 head-dim elements;
+// four consumer warps each take 16 of a tile's 64 keys and run S = Q K^T and O += P V on mma.sync m16n8k16 (fp32
+// accumulate) with an fp32 online softmax in base 2. At a unit's end the four warps' (max, sum, O) are merged in
+// shared memory while the producer already prefetches the next unit. A sequence that fits one split writes its
+// output directly; otherwise each split writes its partial (max, sum, unnormalised O) to the workspace and
+// split_combine_kernel, launched right behind as a programmatic dependent, merges the splits of every (b, hk, row)
+// by log-sum-exp -- the combine of foldattn_merge (foldattn.py:188-211) and CpuAttn's range merge
+// (cpu_ext/cpu_kern.cpp:607-628).
 #pragma once
 
 #include "common.cuh"
@@ -18,27 +22,35 @@ namespace decode {
 constexpr int BK = 64;         // keys per tile
 constexpr int CONSUMERS = 4;   // consumer warps, 16 keys of each tile apiece
 constexpr int THREADS = (CONSUMERS + 1) * 32;
+constexpr int MAX_B = 1024;    // sequences a call (the per-CTA unit table)
 
-template <int D>
+template <int D, int MT>
 struct Cfg {
-  static constexpr int STAGES = D == 64 ? 4 : D == 128 ? 3 : 2;
-  static constexpr int TILE_BYTES = BK * D * 2;             // one K (or V) tile, bf16/f16
-  static constexpr int STAGE_BYTES = 2 * TILE_BYTES;        // K + V
+  static constexpr int RP = MT * 16;                          // folded rows, padded
+  static constexpr int STAGES = D == 64 ? 6 : D == 128 ? 4 : 2;
+  static constexpr int TILE_BYTES = BK * D * 2;               // one K (or V) tile, bf16/f16
+  static constexpr int STAGE_BYTES = 2 * TILE_BYTES;          // K + V
   static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
-  static constexpr int SMEM_BYTES = RING_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int QSLOT = (D / 64) * RP * 128;           // one folded Q tile
+  static constexpr int Q_OFF = RING_BYTES;
+  static constexpr int MERGE_OFF = Q_OFF + 2 * QSLOT;         // [CONSUMERS][RP][D] O + [CONSUMERS][RP][2] (m, l)
+  static constexpr int MERGE_BYTES = CONSUMERS * RP * D * 4 + CONSUMERS * RP * 2 * 4;
+  static constexpr int PREFIX_OFF = MERGE_OFF + MERGE_BYTES;  // [MAX_B + 1] ints
+  static constexpr int LENS_OFF = PREFIX_OFF + (MAX_B + 1) * 4;  // [MAX_B] ints
+  static constexpr int META_OFF = LENS_OFF + MAX_B * 4;
+  static constexpr int BAR_OFF = (META_OFF + 2 * 32 + 15) / 16 * 16;
+  static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024 /*align*/;
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
 struct Params {
-  const void* q;
-  int64_t q_st[3];
   void* o;
   int64_t o_st[3];
   float* part_o;    // emit mode: normalised fp32 o, [B, Hq, T, D] contiguous
   float* part_lse;  // emit mode: natural-log lse, [B, Hq, T]
   const int32_t* kv_len;
-  float* ws_o;      // [B, Hkv, nsplit, rows_pad, D] unnormalised partial O
-  float* ws_ml;     // [B, Hkv, nsplit, rows_pad, 2] (max in log2 units, sum)
-  int* ws_cnt;      // [B * Hkv] tickets, zero between calls
+  float* ws_o;      // [B, Hkv, nsplit, RP, D] unnormalised partial O
+  float* ws_ml;     // [B, Hkv, nsplit, RP, 2] (max in log2 units, sum)
   int B, Hq, Hkv, T, N, G, rows;
   int split, nsplit;
   int causal, emit;
@@ -87,314 +99,408 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// AND of `pred` over the four consumer warps (named barrier 1, 128 threads); also orders their shared-memory use.
+__device__ __forceinline__ bool consumers_all(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(uint32_t(pred)), "r"(CONSUMERS * 32)
+      : "memory");
+  return r != 0;
+}
+
+// Unit u of the call -> (b, s, hk) through the prefix table of per-sequence split counts.
+__device__ __forceinline__ void unit_coords(const int* prefix, int B, int Hkv, int u, int& b, int& s, int& hk) {
+  const int pidx = u / Hkv;
+  hk = u - pidx * Hkv;
+  int lo = 0, hi = B;  // largest b with prefix[b] <= pidx
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (prefix[mid] <= pidx) lo = mid; else hi = mid;
+  }
+  b = lo;
+  s = pidx - prefix[b];
+}
+
 template <typename T, int D, int MT>
-__global__ void __launch_bounds__(THREADS) decode_kernel(const __grid_constant__ CUtensorMap kmap,
-                                                          const __grid_constant__ CUtensorMap vmap, const Params p) {
-  using C = Cfg<D>;
+__global__ void __launch_bounds__(THREADS, 1) decode_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                             const __grid_constant__ CUtensorMap kmap,
+                                                             const __grid_constant__ CUtensorMap vmap,
+                                                             const Params p) {
+  using C = Cfg<D, MT>;
   constexpr int STAGES = C::STAGES;
-  constexpr int ND = D / 8;  // 8-wide head-dim tiles of the output
-  constexpr int KD = D / 16; // 16-wide k-steps of Q K^T
-  const int s = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
-  const int len = p.kv_len ? min(max(p.kv_len[b], 0), p.N) : p.N;
-  const int nsplit_b = max(1, (len + p.split - 1) / p.split);
-  if (s >= nsplit_b) return;  // the whole CTA: nothing of this sequence lies in this split
-  const int n0 = s * p.split, n1 = min(len, n0 + p.split);
-  const int ntiles = n1 > n0 ? (n1 - n0 + BK - 1) / BK : 0;
+  constexpr int RP = C::RP;
+  constexpr int ND = D / 8;   // 8-wide head-dim tiles of the output
+  constexpr int KD = D / 16;  // 16-wide k-steps of Q K^T
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(ring + C::RING_BYTES);
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  int* prefix = reinterpret_cast<int*>(sm + C::PREFIX_OFF);
+  int* meta = reinterpret_cast<int*>(sm + C::META_OFF);  // [2 slots][8]: b, hk, s, n0, n1, len
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + C::BAR_OFF);
   uint64_t* empty = full + STAGES;
-  __shared__ int s_last;
+  uint64_t* q_full = empty + STAGES;
+  uint64_t* q_empty = q_full + 2;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* lens = reinterpret_cast<int*>(sm + C::LENS_OFF);
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], CONSUMERS);
     }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], CONSUMERS);
+    }
     fence_barrier_init();
   }
+  // per-sequence lengths and split counts (loaded in parallel), then warp 0 scans the counts into a prefix table
+  for (int b = threadIdx.x; b < p.B; b += THREADS) {
+    const int len = p.kv_len ? min(max(p.kv_len[b], 0), p.N) : p.N;
+    lens[b] = len;
+    prefix[b + 1] = max(1, (len + p.split - 1) / p.split);
+  }
   __syncthreads();
+  if (warp == 0) {
+    int run = 0;
+    for (int base = 0; base < p.B; base += 32) {
+      int x = base + lane < p.B ? prefix[base + lane + 1] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      if (base + lane < p.B) prefix[base + lane + 1] = run + x;
+      run += __shfl_sync(0xffffffffu, x, 31);
+    }
+    if (lane == 0) prefix[0] = 0;
+  }
+  __syncthreads();
+  const int units = prefix[p.B] * p.Hkv;
+  // The split combine (launched as this grid's programmatic dependent) may start its prologue now; it waits for
+  // this grid's completion before reading any partial.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-  // ------------------------------------------------------------------ producer warp: TMA K/V tiles into the ring
+  // ------------------------------------------------------------------ producer warp: Q tiles and K/V tiles
   if (warp == CONSUMERS) {
     if (lane == 0) {
+      prefetch_tensormap(&qmap);
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
-      int issued = 0;
-      for (int i = 0; i < ntiles; ++i) {
-        const int st = i % STAGES;
-        if (i >= STAGES && !mbar_wait(&empty[st], ((i / STAGES) - 1) & 1, 1)) break;
-        uint8_t* kt = ring + st * C::STAGE_BYTES;
-        uint8_t* vt = kt + C::TILE_BYTES;
-        mbar_arrive_expect_tx(&full[st], C::STAGE_BYTES);
-        const int key0 = n0 + i * BK;
+      int gt = 0, uc = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++uc) {
+        int b, s, hk;
+        unit_coords(prefix, p.B, p.Hkv, u, b, s, hk);
+        const int len = lens[b];
+        const int n0 = s * p.split, n1 = min(len, n0 + p.split);
+        const int ntiles = n1 > n0 ? (n1 - n0 + BK - 1) / BK : 0;
+        const int qs = uc & 1;
+        if (uc >= 2 && !mbar_wait(&q_empty[qs], ((uc >> 1) - 1) & 1, 1)) break;
+        int* m = meta + qs * 8;
+        m[0] = b; m[1] = hk; m[2] = s; m[3] = n0; m[4] = n1; m[5] = len;
+        mbar_arrive_expect_tx(&q_full[qs], (D / 64) * p.rows * 128);
 #pragma unroll
-        for (int db = 0; db < D / 64; ++db) {
-          tma_load_4d(kt + db * BK * 128, &kmap, db * 64, key0, hk, b, &full[st]);
-          tma_load_4d(vt + db * BK * 128, &vmap, db * 64, key0, hk, b, &full[st]);
+        for (int db = 0; db < D / 64; ++db)
+          tma_load_4d(sm + C::Q_OFF + qs * C::QSLOT + db * RP * 128, &qmap, db * 64, 0, hk * p.G, b, &q_full[qs]);
+        for (int i = 0; i < ntiles; ++i, ++gt) {
+          const int st = gt % STAGES;
+          if (gt >= STAGES && !mbar_wait(&empty[st], ((gt / STAGES) - 1) & 1, 2)) {
+            ok = false;
+            break;
+          }
+          uint8_t* kt = sm + st * C::STAGE_BYTES;
+          uint8_t* vt = kt + C::TILE_BYTES;
+          mbar_arrive_expect_tx(&full[st], C::STAGE_BYTES);
+          const int key0 = n0 + i * BK;
+#pragma unroll
+          for (int db = 0; db < D / 64; ++db) {
+            tma_load_4d(kt + db * BK * 128, &kmap, db * 64, key0, hk, b, &full[st]);
+            tma_load_4d(vt + db * BK * 128, &vmap, db * 64, key0, hk, b, &full[st]);
+          }
         }
-        issued = i + 1;
       }
-      // Before the CTA may exit: the last tiles issued have landed (normally already consumed; bounded).
-      for (int i = max(0, issued - STAGES); i < issued; ++i) mbar_wait(&full[i % STAGES], (i / STAGES) & 1, 2);
+      // Drain: the last loads issued have landed before the CTA may finish (normally already consumed).
+      for (int g2 = max(0, gt - STAGES); g2 < gt; ++g2) mbar_wait(&full[g2 % STAGES], (g2 / STAGES) & 1, 3);
+      for (int q2 = max(0, uc - 2); q2 < uc; ++q2) mbar_wait(&q_full[q2 & 1], (q2 >> 1) & 1, 4);
     }
-    __syncthreads();
-    __syncthreads();
-    if (p.nsplit > 1 && nsplit_b > 1) __syncthreads();
-    return;
+    return;  // the producer takes part in no block-wide barrier after the setup
   }
 
   // ------------------------------------------------------------------ consumer warps
   const int quad = lane >> 2, qid = lane & 3;
-  // Q fragments (A operand, row-major 16 x 16 per k-step): rows are folded (g, t) pairs, row = g * T + t.
-  uint32_t qa[MT][KD][4];
-#pragma unroll
-  for (int mt = 0; mt < MT; ++mt) {
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const int r = mt * 16 + quad + 8 * hh;
-      const bool live = r < p.rows;
-      const int g = live ? r / p.T : 0, t = live ? r % p.T : 0;
-      const T* qrow = reinterpret_cast<const T*>(p.q) + b * p.q_st[0] + int64_t(hk * p.G + g) * p.q_st[1] +
-                      int64_t(t) * p.q_st[2];
-#pragma unroll
-      for (int kk = 0; kk < KD; ++kk) {
-        const int d = kk * 16 + 2 * qid;
-        qa[mt][kk][hh] = live ? *reinterpret_cast<const uint32_t*>(qrow + d) : 0u;
-        qa[mt][kk][hh + 2] = live ? *reinterpret_cast<const uint32_t*>(qrow + d + 8) : 0u;
-      }
-    }
-  }
-  // Causal limit of each of this thread's rows: the last visible key (bottom-right over this sequence's length).
-  int lim[MT][2];
-#pragma unroll
-  for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const int r = mt * 16 + quad + 8 * hh;
-      lim[mt][hh] = r >= p.rows ? -1 : (p.causal ? len - p.T + (r % p.T) : len - 1);
-    }
-
-  float m_run[MT][2], l_run[MT][2];
-  float acc[MT][ND][4];
-#pragma unroll
-  for (int mt = 0; mt < MT; ++mt) {
-    m_run[mt][0] = m_run[mt][1] = -INFINITY;
-    l_run[mt][0] = l_run[mt][1] = 0.f;
-#pragma unroll
-    for (int j = 0; j < ND; ++j) acc[mt][j][0] = acc[mt][j][1] = acc[mt][j][2] = acc[mt][j][3] = 0.f;
-  }
-
+  float* wo = reinterpret_cast<float*>(sm + C::MERGE_OFF);  // [CONSUMERS][RP][D]
+  float* wml = wo + CONSUMERS * RP * D;                      // [CONSUMERS][RP][2]
+  int gt = 0, uc = 0;
   bool ok = true;
-  for (int i = 0; i < ntiles && ok; ++i) {
-    const int st = i % STAGES;
-    if (!mbar_wait(&full[st], (i / STAGES) & 1, 3)) {
-      ok = false;
-      break;
-    }
-    const uint32_t kt = smem_u32(ring + st * C::STAGE_BYTES);
-    const uint32_t vt = kt + C::TILE_BYTES;
-    const int kbase = n0 + i * BK + warp * 16;  // this warp's first key
-    // Rows of this warp's 16 keys that lie past the sequence (capacity padding may hold anything): zero V there
-    // so that P = 0 never meets a non-finite value.
-    const int nvalid = min(16, max(0, n1 - kbase));
-    if (nvalid < 16) {
-      uint8_t* vrow = ring + st * C::STAGE_BYTES + C::TILE_BYTES;
-      for (int e = lane; e < (16 - nvalid) * (D / 8); e += 32) {
-        const int r = warp * 16 + nvalid + e / (D / 8), c = e % (D / 8);
-        *reinterpret_cast<uint4*>(vrow + swz(c / 8, r, c % 8)) = make_uint4(0, 0, 0, 0);
-      }
-      __syncwarp();
-    }
-
-    // S = Q K^T over this warp's 16 keys: two 8-key n-tiles.
-    float sc[MT][2][4];
+  for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++uc) {
+    const int qs = uc & 1;
+    // The four consumer warps leave the unit loop together: a failed wait anywhere ends it for all of them, so no
+    // warp is ever left alone at the consumers' named barrier.
+    ok = mbar_wait(&q_full[qs], (uc >> 1) & 1, 5) && ok;
+    if (!consumers_all(ok)) break;
+    const int* m = meta + qs * 8;
+    const int b = m[0], hk = m[1], s = m[2], n0 = m[3], n1 = m[4], len = m[5];
+    const int ntiles = n1 > n0 ? (n1 - n0 + BK - 1) / BK : 0;
+    const int nsplit_b = max(1, (len + p.split - 1) / p.split);
+    // Q fragments (A operand, row-major 16 x 16 a k-step) from the swizzled Q tile; rows are folded (g, t).
+    uint32_t qa[MT][KD][4];
+    const uint32_t qaddr = smem_u32(sm + C::Q_OFF + qs * C::QSLOT);
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt) sc[mt][nt][0] = sc[mt][nt][1] = sc[mt][nt][2] = sc[mt][nt][3] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < KD; ++kk) {
-      uint32_t kb[4];
-      const int r = warp * 16 + (lane & 7) + 8 * (lane >> 4);
-      const int c = (kk * 16) / 8 + ((lane >> 3) & 1);
-      ldsm_x4(kt + swz(c / 8, r, c % 8), kb);
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        mma16816<T>(sc[mt][0], qa[mt][kk], kb[0], kb[1]);
-        mma16816<T>(sc[mt][1], qa[mt][kk], kb[2], kb[3]);
+      for (int kk = 0; kk < KD; ++kk) {
+        const int r = mt * 16 + (lane & 15), c = kk * 2 + (lane >> 4);
+        ldsm_x4(qaddr + (c / 8) * RP * 128 + swz(0, r, c % 8), qa[mt][kk]);
       }
-    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&q_empty[qs]);
 
-    // Online softmax (base 2) per row; each thread holds rows quad and quad + 8 of every m-tile.
-    uint32_t pa[MT][4];
+    int lim[MT][2];
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt) {
+    for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
-        float mx = -INFINITY;
+        const int r = mt * 16 + quad + 8 * hh;
+        lim[mt][hh] = r >= p.rows ? -1 : (p.causal ? len - p.T + (r % p.T) : len - 1);
+      }
+    float m_run[MT][2], l_run[MT][2];
+    float acc[MT][ND][4];
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
+    for (int mt = 0; mt < MT; ++mt) {
+      m_run[mt][0] = m_run[mt][1] = -INFINITY;
+      l_run[mt][0] = l_run[mt][1] = 0.f;
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int key = kbase + nt * 8 + 2 * qid + e;
-            float& x = sc[mt][nt][2 * hh + e];
-            x = (key < n1 && key <= lim[mt][hh]) ? x * p.scale_log2 : -INFINITY;
-            mx = fmaxf(mx, x);
-          }
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        const float m_new = fmaxf(m_run[mt][hh], mx);
-        const float m_use = m_new == -INFINITY ? 0.f : m_new;
-        const float corr = ex2(m_run[mt][hh] - m_use);
-        m_run[mt][hh] = m_new;
-        float ls = 0.f;
+      for (int j = 0; j < ND; ++j) acc[mt][j][0] = acc[mt][j][1] = acc[mt][j][2] = acc[mt][j][3] = 0.f;
+    }
+
+    for (int i = 0; i < ntiles; ++i, ++gt) {
+      const int st = gt % STAGES;
+      if (!mbar_wait(&full[st], (gt / STAGES) & 1, 6)) {
+        ok = false;
+        break;
+      }
+      const uint32_t kt = smem_u32(sm + st * C::STAGE_BYTES);
+      const uint32_t vt = kt + C::TILE_BYTES;
+      const int kbase = n0 + i * BK + warp * 16;  // this warp's first key
+      // Rows of this warp's 16 keys past the sequence (capacity padding may hold anything): zero V there so that
+      // P = 0 never meets a non-finite value.
+      const int nvalid = min(16, max(0, n1 - kbase));
+      if (nvalid < 16) {
+        uint8_t* vrow = sm + st * C::STAGE_BYTES + C::TILE_BYTES;
+        for (int e = lane; e < (16 - nvalid) * (D / 8); e += 32) {
+          const int r = warp * 16 + nvalid + e / (D / 8), c = e % (D / 8);
+          *reinterpret_cast<uint4*>(vrow + swz(c / 8, r, c % 8)) = make_uint4(0, 0, 0, 0);
+        }
+        __syncwarp();
+      }
+      float sc[MT][2][4];
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
+      for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            float& x = sc[mt][nt][2 * hh + e];
-            x = ex2(x - m_use);
-            ls += x;
-          }
-        l_run[mt][hh] = l_run[mt][hh] * corr + ls;
+        for (int nt = 0; nt < 2; ++nt) sc[mt][nt][0] = sc[mt][nt][1] = sc[mt][nt][2] = sc[mt][nt][3] = 0.f;
 #pragma unroll
-        for (int j = 0; j < ND; ++j) {
-          acc[mt][j][2 * hh] *= corr;
-          acc[mt][j][2 * hh + 1] *= corr;
+      for (int kk = 0; kk < KD; ++kk) {
+        uint32_t kb[4];
+        const int r = warp * 16 + (lane & 7) + 8 * (lane >> 4);
+        const int c = kk * 2 + ((lane >> 3) & 1);
+        ldsm_x4(kt + swz(c / 8, r, c % 8), kb);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          mma16816<T>(sc[mt][0], qa[mt][kk], kb[0], kb[1]);
+          mma16816<T>(sc[mt][1], qa[mt][kk], kb[2], kb[3]);
         }
       }
-      pa[mt][0] = pack2<T>(sc[mt][0][0], sc[mt][0][1]);
-      pa[mt][1] = pack2<T>(sc[mt][0][2], sc[mt][0][3]);
-      pa[mt][2] = pack2<T>(sc[mt][1][0], sc[mt][1][1]);
-      pa[mt][3] = pack2<T>(sc[mt][1][2], sc[mt][1][3]);
-    }
-
-    // O += P V over this warp's 16 keys: V^T fragments by transposed ldmatrix, two 8-wide d-tiles a load.
-#pragma unroll
-    for (int j = 0; j < ND; j += 2) {
-      uint32_t vb[4];
-      const int r = warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
-      const int c = j + (lane >> 4);
-      ldsm_x4_t(vt + swz(c / 8, r, c % 8), vb);
+      uint32_t pa[MT][4];
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
-        mma16816<T>(acc[mt][j], pa[mt], vb[0], vb[1]);
-        mma16816<T>(acc[mt][j + 1], pa[mt], vb[2], vb[3]);
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          float mx = -INFINITY;
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int key = kbase + nt * 8 + 2 * qid + e;
+              float& x = sc[mt][nt][2 * hh + e];
+              x = (key < n1 && key <= lim[mt][hh]) ? x * p.scale_log2 : -INFINITY;
+              mx = fmaxf(mx, x);
+            }
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+          const float m_new = fmaxf(m_run[mt][hh], mx);
+          const float m_use = m_new == -INFINITY ? 0.f : m_new;
+          const float corr = ex2(m_run[mt][hh] - m_use);
+          m_run[mt][hh] = m_new;
+          float ls = 0.f;
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              float& x = sc[mt][nt][2 * hh + e];
+              x = ex2(x - m_use);
+              ls += x;
+            }
+          l_run[mt][hh] = l_run[mt][hh] * corr + ls;
+#pragma unroll
+          for (int j = 0; j < ND; ++j) {
+            acc[mt][j][2 * hh] *= corr;
+            acc[mt][j][2 * hh + 1] *= corr;
+          }
+        }
+        pa[mt][0] = pack2<T>(sc[mt][0][0], sc[mt][0][1]);
+        pa[mt][1] = pack2<T>(sc[mt][0][2], sc[mt][0][3]);
+        pa[mt][2] = pack2<T>(sc[mt][1][0], sc[mt][1][1]);
+        pa[mt][3] = pack2<T>(sc[mt][1][2], sc[mt][1][3]);
       }
+#pragma unroll
+      for (int j = 0; j < ND; j += 2) {
+        uint32_t vb[4];
+        const int r = warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+        const int c = j + (lane >> 4);
+        ldsm_x4_t(vt + swz(c / 8, r, c % 8), vb);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          mma16816<T>(acc[mt][j], pa[mt], vb[0], vb[1]);
+          mma16816<T>(acc[mt][j + 1], pa[mt], vb[2], vb[3]);
+        }
+      }
+      if (nvalid < 16) fence_proxy_async_shared();  // generic writes above precede the next TMA into this stage
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
     }
-    if (nvalid < 16) fence_proxy_async_shared();  // generic writes above precede the next TMA into this stage
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[st]);
-  }
 
-  // ------------------------------------------------------------------ merge the four warps (shared memory)
+    // -------------------------------------------------------------- unit epilogue: merge the four warps
 #pragma unroll
-  for (int mt = 0; mt < MT; ++mt)
+    for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      l_run[mt][hh] += __shfl_xor_sync(0xffffffffu, l_run[mt][hh], 1);
-      l_run[mt][hh] += __shfl_xor_sync(0xffffffffu, l_run[mt][hh], 2);
-    }
-  __syncthreads();  // (1) every warp is done with the ring: reuse it for the merge
-  constexpr int RP = MT * 16;  // padded rows
-  float* wo = reinterpret_cast<float*>(ring);          // [CONSUMERS][RP][D]
-  float* wml = wo + CONSUMERS * RP * D;                // [CONSUMERS][RP][2]
-#pragma unroll
-  for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const int r = mt * 16 + quad + 8 * hh;
-      if (qid == 0) {
-        wml[(warp * RP + r) * 2] = m_run[mt][hh];
-        wml[(warp * RP + r) * 2 + 1] = l_run[mt][hh];
+      for (int hh = 0; hh < 2; ++hh) {
+        l_run[mt][hh] += __shfl_xor_sync(0xffffffffu, l_run[mt][hh], 1);
+        l_run[mt][hh] += __shfl_xor_sync(0xffffffffu, l_run[mt][hh], 2);
       }
 #pragma unroll
-      for (int j = 0; j < ND; ++j)
-        *reinterpret_cast<float2*>(&wo[(warp * RP + r) * D + j * 8 + 2 * qid]) =
-            make_float2(acc[mt][j][2 * hh], acc[mt][j][2 * hh + 1]);
-    }
-  // named barrier over the consumer warps only (the producer waits at the block barriers below)
-  asm volatile("bar.sync 1, %0;" ::"r"(CONSUMERS * 32));
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int r = mt * 16 + quad + 8 * hh;
+        if (qid == 0) {
+          wml[(warp * RP + r) * 2] = m_run[mt][hh];
+          wml[(warp * RP + r) * 2 + 1] = l_run[mt][hh];
+        }
+#pragma unroll
+        for (int j = 0; j < ND; ++j)
+          *reinterpret_cast<float2*>(&wo[(warp * RP + r) * D + j * 8 + 2 * qid]) =
+              make_float2(acc[mt][j][2 * hh], acc[mt][j][2 * hh + 1]);
+      }
+    asm volatile("bar.sync 1, %0;" ::"r"(CONSUMERS * 32));
 
-  const int ct = threadIdx.x;  // 0 .. 127
-  const bool single = nsplit_b == 1;
-  float* so = p.ws_o + ((size_t(b) * p.Hkv + hk) * p.nsplit + s) * RP * D;
-  float* sml = p.ws_ml + ((size_t(b) * p.Hkv + hk) * p.nsplit + s) * RP * 2;
-  for (int e = ct; e < p.rows * D; e += CONSUMERS * 32) {
-    const int r = e / D, d = e % D;
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < CONSUMERS; ++w) M = fmaxf(M, wml[(w * RP + r) * 2]);
-    const float Mu = M == -INFINITY ? 0.f : M;
-    float L = 0.f, O = 0.f;
-#pragma unroll
-    for (int w = 0; w < CONSUMERS; ++w) {
-      const float wgt = ex2(wml[(w * RP + r) * 2] - Mu);
-      L += wml[(w * RP + r) * 2 + 1] * wgt;
-      O += wo[(w * RP + r) * D + d] * wgt;
-    }
-    if (single) {
-      const int g = r / p.T, t = r % p.T, h = hk * p.G + g;
-      const float val = L > 0.f ? O / L : 0.f;
-      if (p.emit) {
-        const size_t ro = (size_t(b) * p.Hq + h) * p.T + t;
-        p.part_o[ro * D + d] = val;
-        if (d == 0) p.part_lse[ro] = L > 0.f ? (M + __log2f(L)) * 0.69314718055994531f : -INFINITY;
-      } else {
-        reinterpret_cast<T*>(p.o)[b * p.o_st[0] + int64_t(h) * p.o_st[1] + int64_t(t) * p.o_st[2] + d] =
-            from_f<T>(val);
-      }
-    } else {
-      so[r * D + d] = O;
-      if (d == 0) {
-        sml[r * 2] = M;
-        sml[r * 2 + 1] = L;
-      }
-    }
-  }
-  __syncthreads();  // (2)
-  if (p.nsplit > 1 && nsplit_b > 1) {
-    // ---------------------------------------------------------------- the last split of (b, hk) merges them all
-    if (threadIdx.x == 0) {
-      __threadfence();
-      const int prev = atomicAdd(&p.ws_cnt[b * p.Hkv + hk], 1);
-      s_last = prev == nsplit_b - 1;
-      if (s_last) {
-        p.ws_cnt[b * p.Hkv + hk] = 0;  // ready for the next call
-        __threadfence();
-      }
-    }
-    __syncthreads();  // (3)
-    if (!s_last) return;
-    const float* bo = p.ws_o + (size_t(b) * p.Hkv + hk) * p.nsplit * RP * D;
-    const float* bml = p.ws_ml + (size_t(b) * p.Hkv + hk) * p.nsplit * RP * 2;
+    const int ct = threadIdx.x;  // 0 .. 127
+    const bool single = nsplit_b == 1;
+    float* so = p.ws_o + ((size_t(b) * p.Hkv + hk) * p.nsplit + s) * RP * D;
+    float* sml = p.ws_ml + ((size_t(b) * p.Hkv + hk) * p.nsplit + s) * RP * 2;
     for (int e = ct; e < p.rows * D; e += CONSUMERS * 32) {
       const int r = e / D, d = e % D;
       float M = -INFINITY;
-      for (int w = 0; w < nsplit_b; ++w) M = fmaxf(M, __ldcg(&bml[(w * RP + r) * 2]));
+#pragma unroll
+      for (int w = 0; w < CONSUMERS; ++w) M = fmaxf(M, wml[(w * RP + r) * 2]);
       const float Mu = M == -INFINITY ? 0.f : M;
       float L = 0.f, O = 0.f;
-      for (int w = 0; w < nsplit_b; ++w) {
-        const float wgt = ex2(__ldcg(&bml[(w * RP + r) * 2]) - Mu);
-        L += __ldcg(&bml[(w * RP + r) * 2 + 1]) * wgt;
-        O += __ldcg(&bo[(size_t(w) * RP + r) * D + d]) * wgt;
+#pragma unroll
+      for (int w = 0; w < CONSUMERS; ++w) {
+        const float wgt = ex2(wml[(w * RP + r) * 2] - Mu);
+        L += wml[(w * RP + r) * 2 + 1] * wgt;
+        O += wo[(w * RP + r) * D + d] * wgt;
       }
-      const int g = r / p.T, t = r % p.T, h = hk * p.G + g;
-      const float val = L > 0.f ? O / L : 0.f;
-      if (p.emit) {
-        const size_t ro = (size_t(b) * p.Hq + h) * p.T + t;
-        p.part_o[ro * D + d] = val;
-        if (d == 0) p.part_lse[ro] = L > 0.f ? (M + __log2f(L)) * 0.69314718055994531f : -INFINITY;
+      if (single) {
+        const int g = r / p.T, t = r % p.T, h = hk * p.G + g;
+        const float val = L > 0.f ? O / L : 0.f;
+        if (p.emit) {
+          const size_t ro = (size_t(b) * p.Hq + h) * p.T + t;
+          p.part_o[ro * D + d] = val;
+          if (d == 0) p.part_lse[ro] = L > 0.f ? (M + __log2f(L)) * 0.69314718055994531f : -INFINITY;
+        } else {
+          reinterpret_cast<T*>(p.o)[b * p.o_st[0] + int64_t(h) * p.o_st[1] + int64_t(t) * p.o_st[2] + d] =
+              from_f<T>(val);
+        }
       } else {
-        reinterpret_cast<T*>(p.o)[b * p.o_st[0] + int64_t(h) * p.o_st[1] + int64_t(t) * p.o_st[2] + d] =
-            from_f<T>(val);
+        so[r * D + d] = O;
+        if (d == 0) {
+          sml[r * 2] = M;
+          sml[r * 2 + 1] = L;
+        }
+      }
+    }
+    // the split's partial is now in the workspace; split_combine_kernel merges the splits of (b, hk)
+    // the merge area is free again; a failed tile wait in any warp ends the loop for all
+    if (!consumers_all(ok)) break;
+  }
+}
+
+// Merges the splits of every (b, hk, folded row) of a decode call: one warp per row, lanes across the head dim
+// (float4 loads), several splits' loads in flight at once. Rows of single-split sequences were written by the
+// decode kernel and are skipped.
+template <typename T, int D, int RP>
+__global__ void __launch_bounds__(256) split_combine_kernel(const Params p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the decode grid has completed and its writes are visible
+  const int wid = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int r = wid % p.rows, bh = wid / p.rows;
+  if (bh >= p.B * p.Hkv) return;
+  const int b = bh / p.Hkv, hk = bh % p.Hkv;
+  const int len = p.kv_len ? min(max(p.kv_len[b], 0), p.N) : p.N;
+  const int nsplit_b = max(1, (len + p.split - 1) / p.split);
+  if (nsplit_b == 1) return;
+  const float* bo = p.ws_o + size_t(bh) * p.nsplit * RP * D;
+  const float* bml = p.ws_ml + size_t(bh) * p.nsplit * RP * 2;
+  float M = -INFINITY;
+  for (int w = lane; w < nsplit_b; w += 32) M = fmaxf(M, __ldcg(&bml[(w * RP + r) * 2]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  const float Mu = M == -INFINITY ? 0.f : M;
+  float L = 0.f;
+  for (int w = lane; w < nsplit_b; w += 32) {
+    const float2 ml = __ldcg(reinterpret_cast<const float2*>(&bml[(w * RP + r) * 2]));
+    L += ml.y * ex2(ml.x - Mu);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+  constexpr int V = D / 32;  // head-dim elements a lane
+  float acc[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) acc[i] = 0.f;
+#pragma unroll 4
+  for (int w = 0; w < nsplit_b; ++w) {
+    const float wgt = ex2(__ldcg(&bml[(w * RP + r) * 2]) - Mu);
+    const float* src = bo + (size_t(w) * RP + r) * D + lane * V;
+    if constexpr (V == 4) {
+      const float4 x = __ldcg(reinterpret_cast<const float4*>(src));
+      acc[0] += wgt * x.x;
+      acc[1] += wgt * x.y;
+      acc[2] += wgt * x.z;
+      acc[3] += wgt * x.w;
+    } else {
+#pragma unroll
+      for (int i = 0; i < V; i += 2) {
+        const float2 x = __ldcg(reinterpret_cast<const float2*>(src + i));
+        acc[i] += wgt * x.x;
+        acc[i + 1] += wgt * x.y;
       }
     }
   }
-  (void)ok;
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  const int g = r / p.T, t = r % p.T, h = hk * p.G + g;
+  if (p.emit) {
+    const size_t ro = (size_t(b) * p.Hq + h) * p.T + t;
+#pragma unroll
+    for (int i = 0; i < V; ++i) p.part_o[ro * D + lane * V + i] = acc[i] * inv;
+    if (lane == 0) p.part_lse[ro] = L > 0.f ? (M + __log2f(L)) * 0.69314718055994531f : -INFINITY;
+  } else {
+    T* orow = reinterpret_cast<T*>(p.o) + b * p.o_st[0] + int64_t(h) * p.o_st[1] + int64_t(t) * p.o_st[2];
+#pragma unroll
+    for (int i = 0; i < V; ++i) orow[lane * V + i] = from_f<T>(acc[i] * inv);
+  }
 }
 
 // Merges R rank partials (normalised o, natural-log lse) row by row: one warp per row.

@@ -1,5 +1,6 @@
 // larder_b200: the C-ABI library. One translation unit (so the device status word is one symbol) that includes
 // every kernel header and implements the entry points declared in include/larder_b200.h.
+#include <algorithm>
 #include <mutex>
 #include <string>
 
@@ -75,54 +76,81 @@ static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 namespace decode {
 
-static int pick_split(int B, int Hkv, int N, int split) {
-  if (split > 0) return (split + BK - 1) / BK * BK;
+// The final merge keeps two floats per (split, row) in the merge area of CONSUMERS x RP x D floats, so a sequence
+// has at most 2 D splits; a smaller requested split is raised to respect that.
+static int min_split(int N, int D) {
+  const int per = (N + 2 * D - 1) / (2 * D);
+  return (per + BK - 1) / BK * BK;
+}
+
+static int pick_split(int B, int Hkv, int N, int D, int split) {
+  if (split > 0) return std::max((split + BK - 1) / BK * BK, min_split(N, D));
   int dev = 0;
   cudaGetDevice(&dev);
-  // Aim at about eight CTAs per SM over the whole call (two resident at a time), never under two tiles a split.
-  const int64_t target = int64_t(sm_count(dev)) * 8;
-  int64_t s = (int64_t(B) * Hkv * N + target - 1) / target;
+  // About four units a CTA (one CTA an SM) when sequences fill half the capacity on average, never under two
+  // tiles a unit: long enough units that the per-unit epilogue stays small, enough of them to balance.
+  const int64_t target = int64_t(sm_count(dev)) * 4;
+  int64_t s = (int64_t(B) * Hkv * (N / 2 + 1) + target - 1) / target;
   s = (s + BK - 1) / BK * BK;
   if (s < 2 * BK) s = 2 * BK;
   if (s > N) s = (N + BK - 1) / BK * BK;
-  return int(s < BK ? BK : s);
+  return std::max(int(s < BK ? BK : s), min_split(N, D));
 }
 
 static int rows_tiles(int G, int T) { return (G * T + 15) / 16; }
 
 struct WsLayout {
-  size_t cnt, ml, o, total;
+  size_t ml, o, total;
 };
 
+// Split partials: (max, sum) pairs then unnormalised O rows, [B, Hkv, nsplit, rp] each. Every value a call reads
+// was written earlier in the same call, so nothing in the workspace needs to start at zero.
 static WsLayout ws_layout(int B, int Hkv, int rp, int D, int nsplit) {
   WsLayout w;
-  w.cnt = 0;
-  w.ml = align_up(size_t(B) * Hkv * sizeof(int), 256);
+  w.ml = 0;
   w.o = w.ml + align_up(size_t(B) * Hkv * nsplit * rp * 2 * sizeof(float), 256);
   w.total = w.o + size_t(B) * Hkv * nsplit * rp * D * sizeof(float);
   return w;
 }
 
 template <typename T, int D, int MT>
-static int launch_t(const CUtensorMap& km, const CUtensorMap& vm, const Params& p, cudaStream_t st) {
+static int launch_t(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const Params& p,
+                    cudaStream_t st) {
   auto kern = decode_kernel<T, D, MT>;
-  static bool attr_set = false;  // per instantiation; the attribute is per device but idempotent
-  const int smem = Cfg<D>::SMEM_BYTES;
-  if (!attr_set) {
+  const int smem = Cfg<D, MT>::SMEM_BYTES;
+  static int attr_dev = -1;
+  int dev = 0;
+  LB2_CUDA(cudaGetDevice(&dev));
+  if (attr_dev != dev) {
     LB2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr_set = true;
+    attr_dev = dev;
   }
-  dim3 grid(p.nsplit, p.Hkv, p.B);
-  kern<<<grid, THREADS, smem, st>>>(km, vm, p);
+  dim3 grid(unsigned(sm_count(dev)));
+  kern<<<grid, THREADS, smem, st>>>(qm, km, vm, p);
   LB2_CUDA(cudaGetLastError());
+  if (p.nsplit > 1) {
+    // the split combine as a programmatic dependent: its launch overlaps the decode grid's tail
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned((int64_t(p.B) * p.Hkv * p.rows + 7) / 8));
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    LB2_CUDA(cudaLaunchKernelEx(&cfg, split_combine_kernel<T, D, Cfg<D, MT>::RP>, p));
+  }
   return LB2_OK;
 }
 
 template <typename T>
-static int launch_d(int D, int MT, const CUtensorMap& km, const CUtensorMap& vm, const Params& p, cudaStream_t st) {
-  if (D == 64) return MT == 1 ? launch_t<T, 64, 1>(km, vm, p, st) : launch_t<T, 64, 2>(km, vm, p, st);
-  if (D == 128) return MT == 1 ? launch_t<T, 128, 1>(km, vm, p, st) : launch_t<T, 128, 2>(km, vm, p, st);
-  return launch_t<T, 256, 1>(km, vm, p, st);
+static int launch_d(int D, int MT, const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
+                    const Params& p, cudaStream_t st) {
+  if (D == 64) return MT == 1 ? launch_t<T, 64, 1>(qm, km, vm, p, st) : launch_t<T, 64, 2>(qm, km, vm, p, st);
+  if (D == 128) return MT == 1 ? launch_t<T, 128, 1>(qm, km, vm, p, st) : launch_t<T, 128, 2>(qm, km, vm, p, st);
+  return launch_t<T, 256, 1>(qm, km, vm, p, st);
 }
 
 static int kv_map(CUtensorMap* m, const void* base, const int64_t* st, int B, int H, int N, int D, int dtype) {
@@ -148,29 +176,33 @@ static int run(const void* q, const int64_t* q_st, const void* k, const int64_t*
                   "decode: q/k/v strides must be multiples of 8 elements");
   LB2_CHECK_ARG((reinterpret_cast<uintptr_t>(q) & 15) == 0, "decode: q must be 16-byte aligned");
   const int MT = rows_tiles(G, T);
-  const int sp = pick_split(B, Hkv, N, split);
+  const int sp = pick_split(B, Hkv, N, D, split);
   const int nsplit = (N + sp - 1) / sp;
   const WsLayout w = ws_layout(B, Hkv, MT * 16, D, nsplit);
   LB2_CHECK_ARG(workspace != nullptr && workspace_bytes >= w.total, "decode: workspace too small");
   LB2_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "decode: workspace must be 256-byte aligned");
-  CUtensorMap km, vm;
+  LB2_CHECK_ARG(B <= MAX_B, "decode: at most 1024 sequences a call");
+  CUtensorMap qm, km, vm;
   int rc = kv_map(&km, k, k_st, B, Hkv, N, D, dtype);
   if (rc) return rc;
   rc = kv_map(&vm, v, v_st, B, Hkv, N, D, dtype);
   if (rc) return rc;
-  Params p{};
-  p.q = q;
-  for (int i = 0; i < 3; ++i) {
-    p.q_st[i] = q_st[i];
-    p.o_st[i] = o_st ? o_st[i] : 0;
+  {  // the folded Q tile of one KV head: a (64, T, G, 1) box of the (D, T, Hq, B) view of q
+    const uint64_t dims[4] = {uint64_t(D), uint64_t(T), uint64_t(Hq), uint64_t(B)};
+    const uint64_t strides[3] = {uint64_t(q_st[2]) * 2, uint64_t(q_st[1]) * 2, uint64_t(q_st[0]) * 2};
+    const uint32_t box[4] = {64, uint32_t(T), uint32_t(G), 1};
+    rc = encode_tensor_map(&qm, dtype == LB2_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                           4, q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
   }
+  Params p{};
+  for (int i = 0; i < 3; ++i) p.o_st[i] = o_st ? o_st[i] : 0;
   p.o = o;
   p.part_o = part_o;
   p.part_lse = part_lse;
   p.emit = part_o != nullptr;
   p.kv_len = kv_len;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  p.ws_cnt = reinterpret_cast<int*>(ws + w.cnt);
   p.ws_ml = reinterpret_cast<float*>(ws + w.ml);
   p.ws_o = reinterpret_cast<float*>(ws + w.o);
   p.B = B;
@@ -185,7 +217,8 @@ static int run(const void* q, const int64_t* q_st, const void* k, const int64_t*
   p.causal = causal && T > 1;
   p.scale_log2 = scale * 1.4426950408889634f;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return dtype == LB2_BF16 ? launch_d<__nv_bfloat16>(D, MT, km, vm, p, st) : launch_d<__half>(D, MT, km, vm, p, st);
+  return dtype == LB2_BF16 ? launch_d<__nv_bfloat16>(D, MT, qm, km, vm, p, st)
+                           : launch_d<__half>(D, MT, qm, km, vm, p, st);
 }
 
 }  // namespace decode
@@ -223,7 +256,7 @@ static int map4(CUtensorMap* m, const void* base, const int64_t* st, int B, int 
 }  // namespace prefill
 // ------------------------------------------------------------------------------------------------ allocation-free decode
 
-// The scratch of lb2_attn_decode_noalloc (split partials and ticket counters): a file-scope device array, so that
+// The scratch of lb2_attn_decode_noalloc (split partials): a file-scope device array, so that
 // the entry point never allocates. Host code must not pass this name to a kernel (in host code it is a host-side
 // stand-in); its device address comes from cudaGetSymbolAddress, once per device.
 static __device__ __align__(256) uint8_t g_noalloc_scratch[LB2_NOALLOC_SCRATCH_BYTES];
@@ -272,7 +305,7 @@ int lb2_status(void* stream) {
 size_t lb2_attn_decode_workspace_size(int B, int Hq, int Hkv, int T, int N, int D, int split) {
   if (B <= 0 || Hkv <= 0 || Hq % Hkv || N <= 0 || T <= 0) return 0;
   const int MT = decode::rows_tiles(Hq / Hkv, T);
-  const int sp = decode::pick_split(B, Hkv, N, split);
+  const int sp = decode::pick_split(B, Hkv, N, D, split);
   return decode::ws_layout(B, Hkv, MT * 16, D, (N + sp - 1) / sp).total;
 }
 
@@ -308,9 +341,8 @@ int lb2_attn_decode_noalloc(const void* q, const int64_t* q_st, const void* k, c
   void* ws = nullptr;
   int rc = noalloc::scratch(&ws);
   if (rc) return rc;
-  // The ticket counters must start at zero; the array keeps whatever the last call left.
-  const size_t counters = decode::ws_layout(B, Hkv, 16, D, 1).ml;
-  LB2_CUDA(cudaMemsetAsync(ws, 0, counters, static_cast<cudaStream_t>(stream)));
+  // The array keeps whatever the last call left; every partial this call reads is written by this call first, so
+  // nothing needs clearing.
   return decode::run(q, q_st, k, k_st, v, v_st, o, o_st, nullptr, nullptr, kv_len, B, Hq, Hkv, T, N, D, dtype, scale,
                      causal, split, ws, LB2_NOALLOC_SCRATCH_BYTES, stream);
 }

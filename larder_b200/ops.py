@@ -13,7 +13,7 @@ from . import _lib
 from ._lib import check, i64, lib
 
 _DT = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16: _lib.F16}
-_WS = {}  # (device index, tag) -> zeroed uint8 workspace, grown on demand
+_WS = {}  # (device index, tag) -> uint8 workspace, grown on demand
 
 
 def dtype_code(t):
@@ -43,8 +43,8 @@ def _unit_last(t, name):
 
 
 def workspace(device, nbytes, tag):
-    """A zeroed, 256-byte aligned uint8 buffer of at least nbytes on device, kept per (device, tag). The decode
-    kernels leave their ticket counters at zero, so one zeroing lasts the buffer's life."""
+    """A 256-byte aligned uint8 buffer of at least nbytes on device, kept per (device, tag) and reused by later
+    calls on the same stream."""
     key = (device.index if device.index is not None else torch.cuda.current_device(), tag)
     buf = _WS.get(key)
     if buf is None or buf.numel() < nbytes:
