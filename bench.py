@@ -177,6 +177,12 @@ def run_ours(args):
                                            max_over_ranks)
         except Exception as e:  # reported, never hidden
             out["prefill"] = {"error": f"{type(e).__name__}: {e}"}
+    if "sharded" in sections:
+        try:
+            out["sharded"] = bench_sharded(torch, ops, dev, rank, world, args, stream, pk, barrier_sync,
+                                           max_over_ranks)
+        except Exception as e:
+            out["sharded"] = {"error": f"{type(e).__name__}: {e}"}
     if "gdn" in sections:
         try:
             out["gdn"] = bench_gdn(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_over_ranks)
@@ -297,6 +303,64 @@ def bench_prefill(torch, ops, dev, rank, world, args, stream, pk, pk_kind, barri
                          "frac": round(tf / pk["bf16_tflops"], 4), "traffic": None, "peak_kind": pk_kind,
                          "kernel": "lb2::prefill::fmha_kernel<bf16,256>"},
             "clocks": clk.summary()}
+
+
+def bench_sharded(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_over_ranks):
+    """configs[4] per rank (weak scaling: the 8-GPU share of each rank fixed): 8 independent 8192-token causal
+    prefills (32q/4kv x 128), and a batch-64 decode over this rank's 4096-key range of every sequence merged across
+    ranks (NCCL all-gather of packed (o, lse), then the log-sum-exp combine). At 8 GPUs that is configs[4]."""
+    from larder_b200 import sharded
+    g = torch.Generator(device=dev).manual_seed(5000 + rank)
+    # prefill: 8 sequences a rank
+    S, Hq, Hkv, D, T = 8, 32, 4, 128, 8192
+    q = torch.randn(S, T, Hq, D, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16).transpose(1, 2)
+    k = torch.randn(S, Hkv, T, D, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    v = torch.randn(S, Hkv, T, D, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    o = torch.empty(S, Hq, T, D, dtype=torch.bfloat16, device=dev)
+
+    def pre(i):
+        ops.attn_prefill(q, k, v, D ** -0.5, "causal", out=o)
+
+    for i in range(args.warmup):
+        pre(i)
+    barrier_sync()
+    ms_p = max_over_ranks(cuda_time(torch, pre, args.steps, stream)) / args.steps
+    flop = 4.0 * D * Hq * (T * (T + 1) / 2) * S
+    del q, k, v, o
+    torch.cuda.empty_cache()
+    # decode: B=64, 4096 keys of each sequence on this rank, merged across ranks
+    B, n_local = 64, 4096
+    dq = torch.randn(B, Hq, 1, D, generator=torch.Generator(device=dev).manual_seed(77), device=dev).to(torch.bfloat16)
+    copies = 2  # 2 x 268 MB of local KV: consecutive steps miss L2
+    kvs = [(torch.randn(B, Hkv, n_local, D, generator=g, device=dev).to(torch.bfloat16),
+            torch.randn(B, Hkv, n_local, D, generator=g, device=dev).to(torch.bfloat16)) for _ in range(copies)]
+
+    def dec(i):
+        kk, vv = kvs[i % copies]
+        if world > 1:
+            sharded.kv_sharded_decode(dq, kk, vv, D ** -0.5)
+        else:
+            ops.attn_decode(dq, kk, vv, D ** -0.5)
+
+    for i in range(args.warmup):
+        dec(i)
+    barrier_sync()
+    ms_d = max_over_ranks(cuda_time(torch, dec, args.steps, stream)) / args.steps
+    kv_bytes = B * n_local * Hkv * D * 2 * 2
+    return {"prefill": {"value": round(world * flop / (ms_p * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                        "ms_per_step": round(ms_p, 4), "per_rank": "8 x 8192 causal, 32q/4kv x 128, bf16",
+                        "roofline": {"bound": "tensor", "achieved": round(flop / (ms_p * 1e-3) / 1e12, 2),
+                                     "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                                     "frac": round(flop / (ms_p * 1e-3) / 1e12 / pk["bf16_tflops_sustained"], 4),
+                                     "peak_kind": "sustained (long step)"}},
+            "decode": {"value": round(world * kv_bytes / (ms_d * 1e-3) / 1e9, 1), "unit": "GB/s",
+                       "ms_per_step": round(ms_d, 5), "context": n_local * world,
+                       "per_rank": f"B=64 x {n_local} local keys; partial (o, lse) all-gathered over NCCL",
+                       "merge_bytes_per_rank": B * Hq * (D + 1) * 4,
+                       "roofline": {"bound": "hbm", "achieved": round(kv_bytes / (ms_d * 1e-3) / 1e9, 1),
+                                    "peak": pk["hbm_gbs"], "frac": round(kv_bytes / (ms_d * 1e-3) / 1e9 /
+                                                                         pk["hbm_gbs"], 4)}},
+            "scaling": "weak", "workload": "configs[4] share of one rank (exactly configs[4] at 8 GPUs)"}
 
 
 def bench_gdn(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_over_ranks):
@@ -454,7 +518,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--section", default="decode,prefill,gdn")
+    ap.add_argument("--section", default="decode,prefill,gdn,sharded")
     ap.add_argument("--split", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()

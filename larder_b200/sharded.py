@@ -1,0 +1,86 @@
+"""Multi-GPU layer: one process per GPU, torch.distributed (NCCL over NVLink / NVSwitch) for the plumbing.
+
+The reference is single-process and single-GPU (no collective exists in it); the hot path partitions two ways:
+
+  * prefill by independent sequences: rank r of R takes its contiguous share of the batch and runs the prefill
+    kernel on it locally -- no exchange at all (weak scaling). `sequence_shard` gives the share.
+  * long-context decode by KV range: each sequence's KV cache is cut into R contiguous ranges, one per rank,
+    resident on that rank. Each rank computes its range's normalised partial output and log-sum-exp
+    (lb2_attn_decode_partial), the ranks exchange them with one all-gather of a packed [o | lse] buffer (about
+    B * Hq * T * (D + 1) * 4 bytes a rank), and every rank merges them with the log-sum-exp combine kernel
+    (lb2_attn_combine): o = sum_r exp(lse_r - lse*) o_r / sum_r exp(lse_r - lse*), the merge of foldattn_merge
+    (foldattn.py:188-211) and cpu_kern.cpp:607-628 taken across GPUs.
+
+`partial_fn` / `combine_fn` default to this package's CUDA entry points; tests on CPU ranks (gloo) pass the CPU
+oracle instead, as the checker of the exchange itself.
+"""
+import datetime
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+
+
+def init(backend="nccl", timeout_s=60, device=None):
+    """Initialise the process group from the torchrun environment with a short timeout, so that ranks waiting on a
+    rank that died end with an error instead of waiting for good. Returns (rank, world)."""
+    if not dist.is_initialized():
+        kw = {"timeout": datetime.timedelta(seconds=timeout_s)}
+        if backend == "nccl" and device is not None:
+            kw["device_id"] = device
+        dist.init_process_group(backend, **kw)
+    return dist.get_rank(), dist.get_world_size()
+
+
+def sequence_shard(n_seq, rank, world):
+    """[start, stop) of the sequences rank `rank` of `world` prefills: contiguous blocks, the first n_seq % world
+    ranks one longer."""
+    base, extra = divmod(n_seq, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def kv_range(n_keys, rank, world):
+    """[start, stop) of the keys of a sequence rank `rank` holds: contiguous ranges (config 5's 8 x 4096 of 32768)."""
+    return sequence_shard(n_keys, rank, world)
+
+
+def _cuda_partial(q, k, v, scale, kv_len):
+    return ops.attn_decode_partial(q, k, v, scale, kv_len=kv_len)
+
+
+def _cuda_combine(part_o, part_lse, dtype):
+    return ops.attn_combine(part_o, part_lse, dtype)
+
+
+def kv_sharded_decode(q, k_local, v_local, scale, kv_len_local=None, group=None, partial_fn=None, combine_fn=None,
+                      out_dtype=None):
+    """Decode attention over a KV cache whose key range is split across the ranks of `group`.
+
+    q [B, Hq, T, D] (the same on every rank), k_local / v_local [B, Hkv, n_local, D] this rank's contiguous range,
+    kv_len_local int32 [B] (keys of the range each sequence fills, or None). Every query row must see every key of
+    every range (decode rows lie after the whole cache). Returns o [B, Hq, T, D] on every rank."""
+    partial_fn = partial_fn or _cuda_partial
+    combine_fn = combine_fn or _cuda_combine
+    world = dist.get_world_size(group)
+    B, Hq, T, D = q.shape
+    part_o, part_lse = partial_fn(q, k_local, v_local, scale, kv_len_local)
+    rows = B * Hq * T
+    packed = torch.cat([part_o.reshape(rows, D), part_lse.reshape(rows, 1)], dim=1).contiguous()
+    gathered = torch.empty((world * rows, D + 1), dtype=packed.dtype, device=packed.device)
+    dist.all_gather_into_tensor(gathered, packed, group=group)
+    gathered = gathered.view(world, rows, D + 1)
+    go = gathered[:, :, :D].reshape(world, B, Hq, T, D)
+    gl = gathered[:, :, D].reshape(world, B, Hq, T)
+    return combine_fn(go, gl, out_dtype or q.dtype)
+
+
+def sharded_prefill(q, k, v, scale, mask="causal", gate=None, rank=None, world=None):
+    """Prefill of a batch of independent sequences, this rank's share only: q [B, Hq, T, D], k / v [B, Hkv, N, D]
+    (the whole batch's views; only this rank's rows are read). Returns (start, stop, o_local)."""
+    rank = dist.get_rank() if rank is None else rank
+    world = dist.get_world_size() if world is None else world
+    s0, s1 = sequence_shard(q.shape[0], rank, world)
+    g = None if gate is None else gate[s0:s1]
+    return s0, s1, ops.attn_prefill(q[s0:s1], k[s0:s1], v[s0:s1], scale, mask, gate=g)
