@@ -58,7 +58,8 @@ int lb2_status(void* stream);
  *   mask uint8 [T, N]    strides m_st[0..1], only for LB2_MASK_ARRAY
  * Causal is bottom-right: row t sees keys 0 .. N - T + t. GQA: q head h reads KV head h / (Hq / Hkv).
  * dtype LB2_BF16 or LB2_F16 for q, k, v, o, gate alike; D in {64, 128, 256}; row strides multiples of 8 elements
- * and every base 16-byte aligned (TMA).
+ * and every base 16-byte aligned (TMA). dtype LB2_F32 (the reference's CPU-runnable fp32 configuration) runs an
+ * exact fp32 CUDA-core kernel instead (D in {32, 64, 128, 256}, any strides with a unit last stride).
  * Replaces: the patched scaled_dot_product_attention's prefill route (chunkattn.py:451-537) and each chunk of
  * chunkattn.chunked (chunkattn.py:359-423), qsa_tiles.chunked's array-masked chunk (qsa_tiles.py:266-292), and
  * the stock mx.fast.scaled_dot_product_attention they call (chunkattn.py:419-420). */
@@ -81,6 +82,7 @@ int lb2_attn_prefill(const void* q, const int64_t* q_st, const void* k, const in
  *   workspace: lb2_attn_decode_workspace_size() bytes, 256-byte aligned, any contents (a call writes every
  *   partial it reads). Calls that share a workspace must be ordered on one stream.
  * Limits: G*T <= 32 for D <= 128, G*T <= 16 for D = 256; dtype LB2_BF16 or LB2_F16; D in {64, 128, 256}.
+ * dtype LB2_F32 runs the exact fp32 CUDA-core kernel (no workspace used).
  * Replaces: decode SDPA (chunkattn.gqa_sdpa + _gqa_route, chunkattn.py:638-657, :679-696; stream_fast.py's
  * _sdpa_parts / two-pass vector SDPA, :5952-6098), foldattn.fold (foldattn.py:230-259) and the stock decode SDPA
  * attn_cuda calls (stream_fast.py:6439). */

@@ -9,6 +9,7 @@
 #include "gdn_recurrent.cuh"
 #include "attn_prefill.cuh"
 #include "gdn_chunked.cuh"
+#include "attn_f32.cuh"
 
 namespace lb2 {
 
@@ -254,6 +255,56 @@ static int map4(CUtensorMap* m, const void* base, const int64_t* st, int B, int 
 }
 
 }  // namespace prefill
+
+// ------------------------------------------------------------------------------------------------ fp32 attention
+
+namespace f32attn {
+
+static int run(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
+               const int64_t* v_st, void* o, const int64_t* o_st, const void* gate, const int64_t* g_st,
+               const uint8_t* mask, const int64_t* m_st, const int32_t* kv_len, int B, int Hq, int Hkv, int T, int N,
+               int D, float scale, int mask_kind, void* stream) {
+  LB2_CHECK_ARG(D == 32 || D == 64 || D == 128 || D == 256, "fp32 attention: head dim 32, 64, 128 or 256");
+  Params p{};
+  p.q = static_cast<const float*>(q);
+  p.k = static_cast<const float*>(k);
+  p.v = static_cast<const float*>(v);
+  p.o = static_cast<float*>(o);
+  p.gate = static_cast<const float*>(gate);
+  p.mask = mask_kind == LB2_MASK_ARRAY ? mask : nullptr;
+  for (int i = 0; i < 3; ++i) {
+    p.q_st[i] = q_st[i];
+    p.k_st[i] = k_st[i];
+    p.v_st[i] = v_st[i];
+    p.o_st[i] = o_st[i];
+    p.g_st[i] = gate ? g_st[i] : 0;
+  }
+  p.m_st[0] = p.mask ? m_st[0] : 0;
+  p.m_st[1] = p.mask ? m_st[1] : 0;
+  p.kv_len = kv_len;
+  p.B = B;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.T = T;
+  p.N = N;
+  p.G = Hq / Hkv;
+  p.mask_kind = mask_kind;
+  p.scale = scale;
+  const int64_t warps = int64_t(B) * Hq * T;
+  dim3 grid(unsigned((warps + 3) / 4));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (D) {
+    case 32: attn_f32_kernel<32><<<grid, 128, 0, st>>>(p); break;
+    case 64: attn_f32_kernel<64><<<grid, 128, 0, st>>>(p); break;
+    case 128: attn_f32_kernel<128><<<grid, 128, 0, st>>>(p); break;
+    default: attn_f32_kernel<256><<<grid, 128, 0, st>>>(p); break;
+  }
+  LB2_CUDA(cudaGetLastError());
+  return LB2_OK;
+}
+
+}  // namespace f32attn
+
 // ------------------------------------------------------------------------------------------------ allocation-free decode
 
 // The scratch of lb2_attn_decode_noalloc (split partials): a file-scope device array, so that
@@ -314,6 +365,11 @@ int lb2_attn_decode(const void* q, const int64_t* q_st, const void* k, const int
                     int T, int N, int D, int dtype, float scale, int causal, int split, void* workspace,
                     size_t workspace_bytes, void* stream) {
   LB2_CHECK_ARG(o != nullptr && o_st != nullptr, "decode: output missing");
+  if (dtype == LB2_F32) {  // exact fp32 on CUDA cores; needs no workspace
+    LB2_CHECK_ARG(B > 0 && Hq > 0 && Hkv > 0 && T > 0 && N > 0 && Hq % Hkv == 0, "decode: shape");
+    return f32attn::run(q, q_st, k, k_st, v, v_st, o, o_st, nullptr, nullptr, nullptr, nullptr, kv_len, B, Hq, Hkv,
+                        T, N, D, scale, causal && T > 1 ? LB2_MASK_CAUSAL : LB2_MASK_NONE, stream);
+  }
   return decode::run(q, q_st, k, k_st, v, v_st, o, o_st, nullptr, nullptr, kv_len, B, Hq, Hkv, T, N, D, dtype, scale,
                      causal, split, workspace, workspace_bytes, stream);
 }
@@ -378,6 +434,9 @@ int lb2_attn_prefill(const void* q, const int64_t* q_st, const void* k, const in
                      float scale, int mask_kind, void* stream) {
   LB2_CHECK_ARG(B > 0 && Hq > 0 && Hkv > 0 && T > 0 && N > 0, "prefill: empty shape");
   LB2_CHECK_ARG(Hq % Hkv == 0, "prefill: Hq must be a multiple of Hkv");
+  if (dtype == LB2_F32)  // exact fp32 on CUDA cores (the tensor-core kernel takes 16-bit operands)
+    return f32attn::run(q, q_st, k, k_st, v, v_st, o, o_st, gate, g_st, mask, m_st, nullptr, B, Hq, Hkv, T, N, D,
+                        scale, mask_kind, stream);
   LB2_CHECK_ARG(D == 64 || D == 128 || D == 256, "prefill: head dim must be 64, 128 or 256");
   LB2_CHECK_ARG(dtype == LB2_BF16 || dtype == LB2_F16, "prefill: dtype must be bf16 or f16");
   LB2_CHECK_ARG(mask_kind >= LB2_MASK_NONE && mask_kind <= LB2_MASK_ARRAY, "prefill: mask kind");
