@@ -14,8 +14,8 @@
 // Two launches:
 //   prep (grid: chunks x v-heads x batch, independent): K K^T and Q K^T on bf16 mma.sync (fp32 accumulate), the
 //        decay / beta weighting, T by blocked inversion (16 x 16 diagonal blocks by substitution, then 32 and 64
-//        by the 2 x 2 block formula) in fp32, and W, U' on TF32 mma.sync; writes W, U', M, gamma, Gam to the
-//        workspace.
+//        by the 2 x 2 block formula) in fp32, and W, U' on TF32 mma.sync with their B operands (beta Gam K,
+//        beta V) formed from the 16-bit tiles on the fly; writes W, U', M, gamma, Gam to the workspace.
 //   scan (grid: Dv / 32 value-row blocks x v-heads x batch): the state slice S[32 x 128] in fp32 shared memory,
 //        chunks in order, each chunk's workspace tiles prefetched with cp.async while the previous chunk computes;
 //        U, Y and the state update on TF32 mma.sync with fp32 accumulation.
@@ -115,10 +115,9 @@ __device__ __forceinline__ float* unit_ptr(const Params& p, int b, int h, int c)
 struct PrepSmem {
   static constexpr int KB = 0;                              // bf16 [C][KP]
   static constexpr int QB = KB + C * KP * 2;                // bf16 [C][KP]
-  static constexpr int AF = QB + C * KP * 2;                // f32 [C][AP]  A, then T
-  static constexpr int RK = AF + C * AP * 4;                // f32 [C][RP]  beta Gam K
-  static constexpr int RV = RK + C * RP * 4;                // f32 [C][RP]  beta V
-  static constexpr int XS = RV + C * RP * 4;                // f32 [32][33] inversion scratch
+  static constexpr int VB = QB + C * KP * 2;                // bf16 [C][KP]
+  static constexpr int AF = VB + C * KP * 2;                // f32 [C][AP]  A, then T
+  static constexpr int XS = AF + C * AP * 4;                // f32 [32][33] inversion scratch
   static constexpr int GAM = XS + 32 * 33 * 4;              // f32 [C] gamma, [C] Gam, [C] beta
   static constexpr int BYTES = GAM + 3 * C * 4;
 };
@@ -132,9 +131,8 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
   extern __shared__ __align__(16) uint8_t sm[];
   T* Kb = reinterpret_cast<T*>(sm + PrepSmem::KB);
   T* Qb = reinterpret_cast<T*>(sm + PrepSmem::QB);
+  T* Vb = reinterpret_cast<T*>(sm + PrepSmem::VB);
   float* Af = reinterpret_cast<float*>(sm + PrepSmem::AF);
-  float* Rk = reinterpret_cast<float*>(sm + PrepSmem::RK);
-  float* Rv = reinterpret_cast<float*>(sm + PrepSmem::RV);
   float* Xs = reinterpret_cast<float*>(sm + PrepSmem::XS);
   float* gam = reinterpret_cast<float*>(sm + PrepSmem::GAM);
   float* Gam = gam + C;
@@ -166,21 +164,25 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
       bet[lane + 32 * u] = bt[u];
     }
   }
-  // 2. K and Q tiles (bf16/f16), zero past T
+  // 2. K, Q and V tiles (16-bit, vector loads), zero past T
   {
     const T* kg = static_cast<const T*>(p.k);
     const T* qg = static_cast<const T*>(p.q);
+    const T* vg = static_cast<const T*>(p.v);
+#pragma unroll 4
     for (int e = tid; e < C * (DK / 8); e += 128) {
       const int r = e / (DK / 8), u = e % (DK / 8);
       const int pos = t0 + r;
-      uint4 kv = make_uint4(0, 0, 0, 0), qv = make_uint4(0, 0, 0, 0);
+      uint4 kv = make_uint4(0, 0, 0, 0), qv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
       if (pos < p.T) {
         const int64_t off = ((int64_t(b) * p.T + pos) * p.Hk + hk) * DK + u * 8;
         kv = *reinterpret_cast<const uint4*>(kg + off);
         qv = *reinterpret_cast<const uint4*>(qg + off);
+        vv = *reinterpret_cast<const uint4*>(vg + ((int64_t(b) * p.T + pos) * p.Hv + h) * DV + u * 8);
       }
       *reinterpret_cast<uint4*>(Kb + r * KP + u * 8) = kv;
       *reinterpret_cast<uint4*>(Qb + r * KP + u * 8) = qv;
+      *reinterpret_cast<uint4*>(Vb + r * KP + u * 8) = vv;
     }
   }
   __syncthreads();
@@ -287,25 +289,16 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
       Af[(32 + r) * AP + cc] = -s;
     }
   }
-  // 5. right-hand sides: beta Gam K and beta V (fp32)
-  {
-    const T* vg = static_cast<const T*>(p.v);
-    for (int e = tid; e < C * DK; e += 128) {
-      const int r = e / DK, d = e % DK;
-      const int pos = t0 + r;
-      Rk[r * RP + d] = bet[r] * Gam[r] * to_f<T>(Kb[r * KP + d]);
-      Rv[r * RP + d] = pos < p.T ? bet[r] * ldf(vg, ((int64_t(b) * p.T + pos) * p.Hv + h) * DV + d, p.vdt) : 0.f;
-    }
-  }
   __syncthreads();
-  // 6. W = T Rk and U' = T Rv (TF32 mma), rows 16 w .. 16 w + 15; T is lower triangular, so k < 16 (w + 1)
+  // 5. W = T diag(beta Gam) K and U' = T diag(beta) V (TF32 mma), rows 16 w .. 16 w + 15; the B fragments are
+  // formed from the 16-bit tiles on the fly. T is lower triangular, so only k < 16 (w + 1) contributes.
   {
     float* Wg = unit_ptr(p, b, h, c);
     float* Ug = Wg + C * DK;
     const int r = lane >> 2, cq = lane & 3, m0 = warp * 16;
 #pragma unroll 1
     for (int which = 0; which < 2; ++which) {
-      const float* R = which ? Rv : Rk;
+      const T* R = which ? Vb : Kb;
       float* G = which ? Ug : Wg;
 #pragma unroll 1
       for (int nh = 0; nh < 2; ++nh) {  // two halves of 64 columns, to bound registers
@@ -315,10 +308,13 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
         for (int k0 = 0; k0 < 16 * (warp + 1); k0 += 8) {
           const uint32_t a0 = tf32(Af[(m0 + r) * AP + k0 + cq]), a1 = tf32(Af[(m0 + r + 8) * AP + k0 + cq]);
           const uint32_t a2 = tf32(Af[(m0 + r) * AP + k0 + cq + 4]), a3 = tf32(Af[(m0 + r + 8) * AP + k0 + cq + 4]);
+          const float s0 = which ? bet[k0 + cq] : bet[k0 + cq] * Gam[k0 + cq];
+          const float s1 = which ? bet[k0 + cq + 4] : bet[k0 + cq + 4] * Gam[k0 + cq + 4];
 #pragma unroll
           for (int n = 0; n < 8; ++n) {
             const int n0 = nh * 64 + n * 8;
-            mma_tf32(acc[n], a0, a1, a2, a3, tf32(R[(k0 + cq) * RP + n0 + r]), tf32(R[(k0 + cq + 4) * RP + n0 + r]));
+            mma_tf32(acc[n], a0, a1, a2, a3, tf32(s0 * to_f<T>(R[(k0 + cq) * KP + n0 + r])),
+                     tf32(s1 * to_f<T>(R[(k0 + cq + 4) * KP + n0 + r])));
           }
         }
 #pragma unroll

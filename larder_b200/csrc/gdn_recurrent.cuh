@@ -1,7 +1,8 @@
 // Gated-DeltaNet recurrence, position by position (decode steps and short passes).
 //
-// One warp per (sequence b, value head hv, value row dv), lane l holding state[dv][l*NPT, (l+1)*NPT) in fp32
-// registers, as the reference's CUDA recurrence lays it out (gdn_cuda.py:18-66); per position:
+// One warp per R consecutive value rows of one (sequence b, value head hv), lane l holding state[dv][l*NPT,
+// (l+1)*NPT) of each row in fp32 registers, as the reference's CUDA recurrence lays a row out (gdn_cuda.py:18-66);
+// per position:
 //   s <- s * g; kv = sum(s * k); delta = (v[dv] - kv) * beta; s <- s + k * delta; y[dv] = sum(s * q).
 // Consecutive warps take consecutive value rows of one head, so a block's state rows are one contiguous stretch
 // of HBM and its q / k loads are shared through L1. For a decode step (T = 1) the kernel is a streaming pass over
@@ -41,31 +42,41 @@ __device__ __forceinline__ void ld_vec(const QT* p, float* out) {
   for (int i = 0; i < NPT; ++i) out[i] = to_f<QT>(p[i]);
 }
 
-template <typename QT, int NPT>
+// R value rows a warp (consecutive rows of one head, so q / k loads are shared and R state rows are in flight at
+// once); lane l holds elements [l * NPT, (l + 1) * NPT) of each row.
+template <typename QT, int NPT, int R>
 __global__ void __launch_bounds__(128) recurrent_kernel(const Params p) {
   const int lane = threadIdx.x & 31;
-  const int64_t row = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int64_t rows = int64_t(p.B) * p.Hv * p.Dv;
-  if (row >= rows) return;
-  const int dv = int(row % p.Dv);
-  const int64_t bh = row / p.Dv;
+  const int64_t wid = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int groups = p.Dv / R;  // warps a head
+  if (wid >= int64_t(p.B) * p.Hv * groups) return;
+  const int dv0 = int(wid % groups) * R;
+  const int64_t bh = wid / groups;
   const int hv = int(bh % p.Hv), b = int(bh / p.Hv);
   const int hk = hv / (p.Hv / p.Hk);
   const int Dk = p.Dk;
 
-  float s[NPT];
-  const int64_t so = (bh * p.Dv + dv) * Dk + lane * NPT;
+  float s[R][NPT];
 #pragma unroll
-  for (int i = 0; i < NPT; ++i) s[i] = p.s_in[so + i];
+  for (int r = 0; r < R; ++r) {
+    const int64_t so = (bh * p.Dv + dv0 + r) * Dk + lane * NPT;
+    if constexpr (NPT == 4) {
+      const float4 x = *reinterpret_cast<const float4*>(p.s_in + so);
+      s[r][0] = x.x; s[r][1] = x.y; s[r][2] = x.z; s[r][3] = x.w;
+    } else {
+#pragma unroll
+      for (int i = 0; i < NPT; ++i) s[r][i] = p.s_in[so + i];
+    }
+  }
 
   const QT* qb = static_cast<const QT*>(p.q);
   const QT* kb = static_cast<const QT*>(p.k);
   QT* yb = static_cast<QT*>(p.y);
   for (int t = 0; t < p.T; ++t) {
     const int64_t bt = int64_t(b) * p.T + t;
-    const int64_t vo = (bt * p.Hv + hv) * p.Dv + dv;
+    const int64_t vo = (bt * p.Hv + hv) * p.Dv + dv0;
     if (p.mask && !p.mask[bt]) {
-      if (lane == 0) yb[vo] = from_f<QT>(0.f);
+      if (lane < R) yb[vo + lane] = from_f<QT>(0.f);
       continue;
     }
     const int64_t qo = (bt * p.Hk + hk) * Dk + lane * NPT;
@@ -82,28 +93,52 @@ __global__ void __launch_bounds__(128) recurrent_kernel(const Params p) {
       for (int i = 0; i < NPT; ++i) gf[i] = gs;
     }
     const float bt_ = ld_any(p.beta, go, p.bdt);
-    const float vv = ld_any(p.v, vo, p.vdt);
-    float kv = 0.f;
+    float vv[R];
 #pragma unroll
-    for (int i = 0; i < NPT; ++i) {
-      s[i] = s[i] * gf[i];
-      kv = fmaf(s[i], kf[i], kv);
+    for (int r = 0; r < R; ++r) vv[r] = ld_any(p.v, vo + r, p.vdt);
+    float kv[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      kv[r] = 0.f;
+#pragma unroll
+      for (int i = 0; i < NPT; ++i) {
+        s[r][i] = s[r][i] * gf[i];
+        kv[r] = fmaf(s[r][i], kf[i], kv[r]);
+      }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) kv += __shfl_xor_sync(0xffffffffu, kv, o);
-    const float delta = (vv - kv) * bt_;
-    float out = 0.f;
+    for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-    for (int i = 0; i < NPT; ++i) {
-      s[i] = fmaf(kf[i], delta, s[i]);
-      out = fmaf(s[i], qf[i], out);
+      for (int r = 0; r < R; ++r) kv[r] += __shfl_xor_sync(0xffffffffu, kv[r], o);
+    float out[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const float delta = (vv[r] - kv[r]) * bt_;
+      out[r] = 0.f;
+#pragma unroll
+      for (int i = 0; i < NPT; ++i) {
+        s[r][i] = fmaf(kf[i], delta, s[r][i]);
+        out[r] = fmaf(s[r][i], qf[i], out[r]);
+      }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) out += __shfl_xor_sync(0xffffffffu, out, o);
-    if (lane == 0) yb[vo] = from_f<QT>(out);
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int r = 0; r < R; ++r) out[r] += __shfl_xor_sync(0xffffffffu, out[r], o);
+    if (lane == 0)
+#pragma unroll
+      for (int r = 0; r < R; ++r) yb[vo + r] = from_f<QT>(out[r]);
   }
 #pragma unroll
-  for (int i = 0; i < NPT; ++i) p.s_out[so + i] = s[i];
+  for (int r = 0; r < R; ++r) {
+    const int64_t so = (bh * p.Dv + dv0 + r) * Dk + lane * NPT;
+    if constexpr (NPT == 4) {
+      *reinterpret_cast<float4*>(p.s_out + so) = make_float4(s[r][0], s[r][1], s[r][2], s[r][3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < NPT; ++i) p.s_out[so + i] = s[r][i];
+    }
+  }
 }
 
 }  // namespace gdnrec

@@ -500,7 +500,8 @@ int lb2_gdn_chunked(const void* q, const void* k, int qdt, const void* v, int vd
   LB2_CHECK_ARG(qdt == LB2_BF16 || qdt == LB2_F16, "gdn_chunked: q/k must be bf16 or f16");
   for (int dt : {vdt, gdt, bdt}) LB2_CHECK_ARG(dt >= LB2_F32 && dt <= LB2_F16, "gdn_chunked: dtype");
   LB2_CHECK_ARG(vdt == qdt, "gdn_chunked: v must share q's dtype (y is written in it)");
-  LB2_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(workspace), "gdn_chunked: q, k and workspace 16-byte aligned");
+  LB2_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(workspace),
+                "gdn_chunked: q, k, v and workspace 16-byte aligned");
   LB2_CHECK_ARG(workspace_bytes >= lb2_gdn_chunked_workspace_size(B, T, Hk, Hv, Dk, Dv), "gdn_chunked: workspace too small");
   gdnchunk::Params p{q, k, v, g, beta, qdt, vdt, gdt, bdt, state_in, state_out, y, B, T, Hk, Hv,
                      (T + gdnchunk::C - 1) / gdnchunk::C, static_cast<float*>(workspace)};
@@ -539,16 +540,30 @@ int lb2_gdn_recurrent(const void* q, const void* k, int qdt, const void* v, int 
   LB2_CHECK_ARG(Dk == 32 || Dk == 64 || Dk == 128 || Dk == 256, "gdn: Dk must be 32, 64, 128 or 256");
   for (int dt : {qdt, vdt, gdt, bdt}) LB2_CHECK_ARG(dt >= LB2_F32 && dt <= LB2_F16, "gdn: dtype");
   gdnrec::Params p{q, k, v, g, beta, mask, state_in, state_out, y, qdt, vdt, gdt, bdt, g_vec, B, T, Hk, Dk, Hv, Dv};
-  const int64_t rows = int64_t(B) * Hv * Dv;
+  LB2_CHECK_ARG(Dv % 4 == 0, "gdn: Dv must be a multiple of 4");
+  LB2_CHECK_ARG((reinterpret_cast<uintptr_t>(state_in) & 15) == 0 && (reinterpret_cast<uintptr_t>(state_out) & 15) == 0,
+                "gdn: state buffers must be 16-byte aligned");
   const int warps = 4;
-  dim3 grid(unsigned((rows + warps - 1) / warps));
+  // value rows a warp: several for a decode step (more state in flight), one for longer passes (more warps)
+  const int R = T > 1 ? 1 : (Dk == 256 ? 2 : 4);
+  const int64_t nw = int64_t(B) * Hv * (Dv / R);
+  dim3 grid(unsigned((nw + warps - 1) / warps));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 #define LB2_GDN_LAUNCH(QT)                                                                           \
-  switch (Dk) {                                                                                      \
-    case 32: gdnrec::recurrent_kernel<QT, 1><<<grid, warps * 32, 0, st>>>(p); break;                 \
-    case 64: gdnrec::recurrent_kernel<QT, 2><<<grid, warps * 32, 0, st>>>(p); break;                 \
-    case 128: gdnrec::recurrent_kernel<QT, 4><<<grid, warps * 32, 0, st>>>(p); break;                \
-    default: gdnrec::recurrent_kernel<QT, 8><<<grid, warps * 32, 0, st>>>(p); break;                 \
+  if (R == 1) {                                                                                      \
+    switch (Dk) {                                                                                    \
+      case 32: gdnrec::recurrent_kernel<QT, 1, 1><<<grid, warps * 32, 0, st>>>(p); break;            \
+      case 64: gdnrec::recurrent_kernel<QT, 2, 1><<<grid, warps * 32, 0, st>>>(p); break;            \
+      case 128: gdnrec::recurrent_kernel<QT, 4, 1><<<grid, warps * 32, 0, st>>>(p); break;           \
+      default: gdnrec::recurrent_kernel<QT, 8, 1><<<grid, warps * 32, 0, st>>>(p); break;            \
+    }                                                                                                \
+  } else {                                                                                           \
+    switch (Dk) {                                                                                    \
+      case 32: gdnrec::recurrent_kernel<QT, 1, 4><<<grid, warps * 32, 0, st>>>(p); break;            \
+      case 64: gdnrec::recurrent_kernel<QT, 2, 4><<<grid, warps * 32, 0, st>>>(p); break;            \
+      case 128: gdnrec::recurrent_kernel<QT, 4, 4><<<grid, warps * 32, 0, st>>>(p); break;           \
+      default: gdnrec::recurrent_kernel<QT, 8, 2><<<grid, warps * 32, 0, st>>>(p); break;            \
+    }                                                                                                \
   }
   if (qdt == LB2_BF16) {
     LB2_GDN_LAUNCH(__nv_bfloat16)
