@@ -30,6 +30,9 @@ sys.path.insert(0, ROOT)
 
 METRIC = "prefill attn TFLOP/s & decode KV-read GB/s at 8k ctx, 1/2/4/8 B200, % peak"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# dram__bytes_read.sum + dram__bytes_write.sum of one decode_kernel launch on this workload, from the ncu capture in
+# profiles/decode_kernel_config2.md (148.3 MB read + 4.5 MB written).
+DECODE_TRAFFIC_BYTES = 152.8e6
 
 
 def peaks():
@@ -234,7 +237,8 @@ def bench_decode(torch, ops, dev, rank, world, args, stream, pk, pk_kind, barrie
                      "split": split or "auto", "l2": f"{copies} rotating KV caches ({copies} x "
                      f"{kv_bytes / 1e6:.0f} MB read) so consecutive steps miss L2"}
     out["roofline"] = {"bound": "hbm", "achieved": round(kern_gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                       "frac": round(kern_gbs / pk["hbm_gbs"], 4), "traffic": None, "peak_kind": pk_kind,
+                       "frac": round(kern_gbs / pk["hbm_gbs"], 4), "traffic": DECODE_TRAFFIC_BYTES,
+                       "traffic_source": "ncu, profiles/decode_kernel_config2.md", "peak_kind": pk_kind,
                        "kernel": "lb2::decode::decode_kernel<bf16,128,1>",
                        "algorithmic_bytes_per_launch": alg_bytes}
     out["clocks"] = clk.summary()
