@@ -154,6 +154,44 @@ int lb2_gdn_chunked(const void* q, const void* k, int qdt, const void* v, int vd
                     const void* beta, int bdt, const float* state_in, float* state_out, void* y, int B, int T, int Hk,
                     int Dk, int Hv, int Dv, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------------------------------------------------
+ * QSA decode over picked KV blocks and the paged KV home.
+ *
+ * Gathers the rows the reference's QSA decode attends to: the sorted picked blocks tb (int32 [nsel], block size cr)
+ * and the sequence's trailing partial block; row r < nsel*cr is position tb[r/cr]*cr + r%cr, row r >= nsel*cr is
+ * position own0 + r - nsel*cr with own0 = n/cr*cr, m = nsel*cr + n - own0 rows. kg / vg [Hk, m, D] contiguous.
+ * k / v: [Hk, n, D] views (one sequence) with strides k_st / v_st (head, position, dim).
+ * Replaces: stream_fast._qsa_gather (stream_fast.py:6448-6491); attn_cuda then runs the decode over kg / vg
+ * (stream_fast.py:6411-6441), here lb2_attn_decode. */
+int lb2_kv_gather_picks(const void* k, const int64_t* k_st, const void* v, const int64_t* v_st, const int32_t* tb,
+                        int nsel, int cr, int n, void* kg, void* vg, int Hk, int D, int dtype, void* stream);
+
+/* The paged home: positions in chunks of 2^logc, each chunk [K/V][Hk][2^logc][D] contiguous, chunk addresses in a
+ * uint64 device table (device memory or pinned, GPU-mapped host memory). put writes s new positions pos0.. of
+ * k / v [Hk, s, D] (strides) into the home; gather reads the picked rows (as lb2_kv_gather_picks) from it, with
+ * cache-bypassing loads. Replaces: kv_host's layout and its put / gather kernels (kv_host.py:17-18, :36-41,
+ * :64-291, decode :612-648) without the VRAM LRU. */
+int lb2_kvh_put(const uint64_t* table, const void* k, const int64_t* k_st, const void* v, const int64_t* v_st,
+                int64_t pos0, int s, int Hk, int D, int dtype, int logc, void* stream);
+int lb2_kvh_gather(const uint64_t* table, const int32_t* tb, int nsel, int cr, int n, void* kg, void* vg, int Hk,
+                   int D, int dtype, int logc, void* stream);
+
+/* ------------------------------------------------------------------------------------------------------------
+ * Gated-DeltaNet decode-row glue.
+ *
+ * step_glue: NR positions of one sequence from the conv output before silu, conv [NR, 2 Hk Dk + Hv Dv] (dtype), a / b
+ * [NR, Hv] (dtype), A_log / dt_bias [Hv] fp32, state [Hv, Dv, Dk] fp32 (in / out may alias) -> y [NR, Hv, Dv]
+ * (dtype): silu, q / k RMSNorm (eps) scaled by sq / sk (the 16-bit-rounded Dk^-1 and Dk^-0.5), sigmoid(b),
+ * compute_g and one recurrence step a position. Dk in {64, 128}. Replaces gdn_cuda.step_glue (gdn_cuda.py:118-198,
+ * :235-254).
+ * norm_gate: out = silu(z) * (w * rms_norm(x)), rows of D elements. Replaces gdn_cuda.norm_gate
+ * (gdn_cuda.py:200-222, :257-268). */
+int lb2_gdn_step_glue(const void* conv, const void* a, const void* b, const float* A_log, const float* dt_bias,
+                      const float* state_in, float* state_out, void* y, int NR, int Hk, int Dk, int Hv, int Dv,
+                      int dtype, float sq, float sk, float eps, void* stream);
+int lb2_gdn_norm_gate(const void* x, const void* z, const void* w, void* out, int64_t R, int D, int dtype, float eps,
+                      void* stream);
+
 #ifdef __cplusplus
 }
 #endif

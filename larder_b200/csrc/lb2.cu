@@ -10,6 +10,8 @@
 #include "attn_prefill.cuh"
 #include "gdn_chunked.cuh"
 #include "attn_f32.cuh"
+#include "kv_gather.cuh"
+#include "gdn_glue.cuh"
 
 namespace lb2 {
 
@@ -573,6 +575,124 @@ int lb2_gdn_recurrent(const void* q, const void* k, int qdt, const void* v, int 
     LB2_GDN_LAUNCH(float)
   }
 #undef LB2_GDN_LAUNCH
+  LB2_CUDA(cudaGetLastError());
+  return LB2_OK;
+}
+
+// ------------------------------------------------------------------------------------------------ gathers
+
+int lb2_kv_gather_picks(const void* k, const int64_t* k_st, const void* v, const int64_t* v_st, const int32_t* tb,
+                        int nsel, int cr, int n, void* kg, void* vg, int Hk, int D, int dtype, void* stream) {
+  LB2_CHECK_ARG(nsel >= 0 && cr > 0 && n >= 0 && Hk > 0 && D > 0, "kv_gather_picks: shape");
+  LB2_CHECK_ARG(dtype >= LB2_F32 && dtype <= LB2_F16, "kv_gather_picks: dtype");
+  const int m = nsel * cr + n - n / cr * cr;
+  if (m == 0) return LB2_OK;
+  dim3 grid(unsigned((int64_t(m) * 32 + 255) / 256), unsigned(Hk), 2);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == LB2_BF16)
+    kvg::gather_picks_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(k), k_st[0], k_st[1], k_st[2], static_cast<const __nv_bfloat16*>(v),
+        v_st[0], v_st[1], v_st[2], tb, nsel, cr, n, static_cast<__nv_bfloat16*>(kg), static_cast<__nv_bfloat16*>(vg),
+        Hk, D);
+  else if (dtype == LB2_F16)
+    kvg::gather_picks_kernel<__half><<<grid, 256, 0, st>>>(
+        static_cast<const __half*>(k), k_st[0], k_st[1], k_st[2], static_cast<const __half*>(v), v_st[0], v_st[1],
+        v_st[2], tb, nsel, cr, n, static_cast<__half*>(kg), static_cast<__half*>(vg), Hk, D);
+  else
+    kvg::gather_picks_kernel<float><<<grid, 256, 0, st>>>(
+        static_cast<const float*>(k), k_st[0], k_st[1], k_st[2], static_cast<const float*>(v), v_st[0], v_st[1],
+        v_st[2], tb, nsel, cr, n, static_cast<float*>(kg), static_cast<float*>(vg), Hk, D);
+  LB2_CUDA(cudaGetLastError());
+  return LB2_OK;
+}
+
+int lb2_kvh_put(const uint64_t* table, const void* k, const int64_t* k_st, const void* v, const int64_t* v_st,
+                int64_t pos0, int s, int Hk, int D, int dtype, int logc, void* stream) {
+  LB2_CHECK_ARG(s >= 0 && pos0 >= 0 && Hk > 0 && D > 0 && logc > 0 && logc < 31, "kvh_put: shape");
+  LB2_CHECK_ARG(dtype >= LB2_F32 && dtype <= LB2_F16, "kvh_put: dtype");
+  if (s == 0) return LB2_OK;
+  dim3 grid(unsigned((int64_t(s) * 32 + 255) / 256), unsigned(Hk), 2);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == LB2_BF16)
+    kvg::home_put_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(table, static_cast<const __nv_bfloat16*>(k), k_st[0],
+                                                              k_st[1], k_st[2], static_cast<const __nv_bfloat16*>(v),
+                                                              v_st[0], v_st[1], v_st[2], pos0, s, Hk, D, logc);
+  else if (dtype == LB2_F16)
+    kvg::home_put_kernel<__half><<<grid, 256, 0, st>>>(table, static_cast<const __half*>(k), k_st[0], k_st[1],
+                                                       k_st[2], static_cast<const __half*>(v), v_st[0], v_st[1],
+                                                       v_st[2], pos0, s, Hk, D, logc);
+  else
+    kvg::home_put_kernel<float><<<grid, 256, 0, st>>>(table, static_cast<const float*>(k), k_st[0], k_st[1], k_st[2],
+                                                      static_cast<const float*>(v), v_st[0], v_st[1], v_st[2], pos0, s,
+                                                      Hk, D, logc);
+  LB2_CUDA(cudaGetLastError());
+  return LB2_OK;
+}
+
+int lb2_kvh_gather(const uint64_t* table, const int32_t* tb, int nsel, int cr, int n, void* kg, void* vg, int Hk,
+                   int D, int dtype, int logc, void* stream) {
+  LB2_CHECK_ARG(nsel >= 0 && cr > 0 && n >= 0 && Hk > 0 && D > 0 && logc > 0 && logc < 31, "kvh_gather: shape");
+  LB2_CHECK_ARG(dtype >= LB2_F32 && dtype <= LB2_F16, "kvh_gather: dtype");
+  const int m = nsel * cr + n - n / cr * cr;
+  if (m == 0) return LB2_OK;
+  dim3 grid(unsigned((int64_t(m) * 32 + 255) / 256), unsigned(Hk), 2);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == LB2_BF16)
+    kvg::home_gather_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(table, tb, nsel, cr, n,
+                                                                 static_cast<__nv_bfloat16*>(kg),
+                                                                 static_cast<__nv_bfloat16*>(vg), Hk, D, logc);
+  else if (dtype == LB2_F16)
+    kvg::home_gather_kernel<__half><<<grid, 256, 0, st>>>(table, tb, nsel, cr, n, static_cast<__half*>(kg),
+                                                          static_cast<__half*>(vg), Hk, D, logc);
+  else
+    kvg::home_gather_kernel<float><<<grid, 256, 0, st>>>(table, tb, nsel, cr, n, static_cast<float*>(kg),
+                                                         static_cast<float*>(vg), Hk, D, logc);
+  LB2_CUDA(cudaGetLastError());
+  return LB2_OK;
+}
+
+// ------------------------------------------------------------------------------------------------ GDN glue
+
+int lb2_gdn_step_glue(const void* conv, const void* a, const void* b, const float* A_log, const float* dt_bias,
+                      const float* state_in, float* state_out, void* y, int NR, int Hk, int Dk, int Hv, int Dv,
+                      int dtype, float sq, float sk, float eps, void* stream) {
+  LB2_CHECK_ARG(NR >= 0 && Hk > 0 && Hv > 0 && Dv > 0 && Hv % Hk == 0, "gdn_step_glue: shape");
+  LB2_CHECK_ARG(Dk == 64 || Dk == 128, "gdn_step_glue: Dk must be 64 or 128");
+  LB2_CHECK_ARG(dtype == LB2_BF16 || dtype == LB2_F16, "gdn_step_glue: dtype must be bf16 or f16");
+  glue::StepParams p{conv, a, b, A_log, dt_bias, state_in, state_out, y, NR, Hk, Hv, Dv, sq, sk, eps};
+  constexpr int RB = 16;
+  dim3 grid(unsigned((Dv + RB - 1) / RB), unsigned(Hv));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == LB2_BF16) {
+    if (Dk == 128) glue::step_glue_kernel<__nv_bfloat16, 4, RB><<<grid, RB * 32, 0, st>>>(p);
+    else glue::step_glue_kernel<__nv_bfloat16, 2, RB><<<grid, RB * 32, 0, st>>>(p);
+  } else {
+    if (Dk == 128) glue::step_glue_kernel<__half, 4, RB><<<grid, RB * 32, 0, st>>>(p);
+    else glue::step_glue_kernel<__half, 2, RB><<<grid, RB * 32, 0, st>>>(p);
+  }
+  LB2_CUDA(cudaGetLastError());
+  return LB2_OK;
+}
+
+int lb2_gdn_norm_gate(const void* x, const void* z, const void* w, void* out, int64_t R, int D, int dtype, float eps,
+                      void* stream) {
+  LB2_CHECK_ARG(R >= 0 && D > 0, "gdn_norm_gate: shape");
+  LB2_CHECK_ARG(dtype >= LB2_F32 && dtype <= LB2_F16, "gdn_norm_gate: dtype");
+  if (R == 0) return LB2_OK;
+  dim3 grid(unsigned((R + 3) / 4));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == LB2_BF16)
+    glue::norm_gate_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(z),
+        static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(out), R, D, eps);
+  else if (dtype == LB2_F16)
+    glue::norm_gate_kernel<__half><<<grid, 128, 0, st>>>(static_cast<const __half*>(x), static_cast<const __half*>(z),
+                                                          static_cast<const __half*>(w), static_cast<__half*>(out), R,
+                                                          D, eps);
+  else
+    glue::norm_gate_kernel<float><<<grid, 128, 0, st>>>(static_cast<const float*>(x), static_cast<const float*>(z),
+                                                        static_cast<const float*>(w), static_cast<float*>(out), R, D,
+                                                        eps);
   LB2_CUDA(cudaGetLastError());
   return LB2_OK;
 }

@@ -54,6 +54,23 @@ def gated_delta_update(q, k, v, a, b, A_log, dt_bias, state=None, mask=None, *, 
 gated_delta_update._gdn_cuda = True
 
 
+def step_glue(conv, a, b, A_log, dt_bias, state, Hk, Dk, Hv, Dv):
+    """T positions of qwen3_5's GatedDeltaNet from the conv output (before silu): conv [1, T, 2 Hk Dk + Hv Dv], a / b
+    [1, T, Hv], A_log / dt_bias [Hv], state [1, Hv, Dv, Dk] -> (y [1, T, Hv, Dv] in conv's dtype, the new state)
+    (gdn_cuda.py:235-254's contract), one fused kernel."""
+    if conv.shape[0] != 1 or Dk not in (64, 128) or Hv % Hk:
+        raise ValueError("step_glue: B = 1, Dk in {64, 128}, Hv a multiple of Hk")
+    y, s = ops.gdn_step_glue(conv, a, b, A_log, dt_bias, state.reshape(Hv, Dv, Dk), Hk, Dk, Hv, Dv)
+    return y, s.reshape(state.shape)
+
+
+def norm_gate(x, z, weight, eps):
+    """Qwen3NextRMSNormGated(x, z): rms_norm with `weight`, then silu(z) times it (gdn_cuda.py:257-268)."""
+    if z.shape != x.shape or weight.dtype != x.dtype:
+        raise ValueError("norm_gate: z must match x and weight x's dtype")
+    return ops.gdn_norm_gate(x, z, weight, eps)
+
+
 def install(modules=None):
     """Route `gated_delta_update` to this package wherever a module holds the name, as the reference rebinds it in
     gated_delta and in every model module that already imported it (gdn_cuda.py:322-360). `modules` defaults to

@@ -205,3 +205,86 @@ def gdn_chunked(q, k, v, g, beta, state=None):
                                _ptr(ws), ws.numel(), _stream(q))
     check(rc, "gdn_chunked")
     return y, s_out
+
+
+# ---------------------------------------------------------------------------------------------------- gathers
+
+def kv_gather_picks(k, v, tb, cr, n=None):
+    """Rows of one sequence's k / v [Hk, n, D] (or [1, Hk, n, D]) that QSA decode attends to: the sorted picked
+    blocks tb (int32, block size cr) and the trailing partial block. Returns kg, vg [1, Hk, m, D]."""
+    _cuda(k, v, tb)
+    if k.dim() == 4:
+        k, v = k[0], v[0]
+    Hk, N, D = k.shape
+    n = N if n is None else int(n)
+    tb = tb.reshape(-1)
+    if tb.dtype != torch.int32:
+        raise ValueError("tb must be int32")
+    nsel = tb.numel()
+    m = nsel * cr + n - n // cr * cr
+    kg = torch.empty((1, Hk, m, D), dtype=k.dtype, device=k.device)
+    vg = torch.empty_like(kg)
+    rc = lib().lb2_kv_gather_picks(_ptr(k), i64(*k.stride()), _ptr(v), i64(*v.stride()), _ptr(tb), nsel, int(cr), n,
+                                   _ptr(kg), _ptr(vg), Hk, D, dtype_code(k), _stream(k))
+    check(rc, "kv_gather_picks")
+    return kg, vg
+
+
+def kvh_put(table, k, v, pos0, logc):
+    """Write k / v [Hk, s, D] (or [1, Hk, s, D]) as positions pos0 .. pos0 + s - 1 of the paged home `table`."""
+    _cuda(table, k, v)
+    if k.dim() == 4:
+        k, v = k[0], v[0]
+    Hk, s, D = k.shape
+    rc = lib().lb2_kvh_put(_ptr(table), _ptr(k), i64(*k.stride()), _ptr(v), i64(*v.stride()), int(pos0), s, Hk, D,
+                           dtype_code(k), int(logc), _stream(k))
+    check(rc, "kvh_put")
+
+
+def kvh_gather(table, tb, cr, n, Hk, D, dtype, logc, device):
+    """The QSA picks of a sequence of n positions read from the paged home: kg, vg [1, Hk, m, D]."""
+    tb = tb.reshape(-1)
+    nsel = tb.numel()
+    m = nsel * cr + n - n // cr * cr
+    kg = torch.empty((1, Hk, m, D), dtype=dtype, device=device)
+    vg = torch.empty_like(kg)
+    rc = lib().lb2_kvh_gather(_ptr(table), _ptr(tb), nsel, int(cr), int(n), _ptr(kg), _ptr(vg), Hk, D,
+                              dtype_code(kg), int(logc), _stream(kg))
+    check(rc, "kvh_gather")
+    return kg, vg
+
+
+# ---------------------------------------------------------------------------------------------------- GDN glue
+
+def _rounded(x, dtype):
+    """A Python float rounded to `dtype` (the scalar an op on that dtype applies)."""
+    return float(torch.tensor(float(x), dtype=dtype).item())
+
+
+def gdn_step_glue(conv, a, b, A_log, dt_bias, state, Hk, Dk, Hv, Dv):
+    """Fused GDN decode rows (silu, q/k RMSNorm and scales, sigmoid(b), compute_g, recurrence) for B = 1."""
+    _cuda(conv, a, b, A_log, dt_bias, state)
+    NR = conv.shape[-2]
+    conv, a, b = conv.reshape(NR, -1).contiguous(), a.reshape(NR, Hv).contiguous(), b.reshape(NR, Hv).contiguous()
+    A_log, dt_bias = A_log.float().contiguous(), dt_bias.float().contiguous()
+    state = state.contiguous()
+    y = torch.empty((1, NR, Hv, Dv), dtype=conv.dtype, device=conv.device)
+    s_out = torch.empty_like(state)
+    inv = Dk ** -0.5
+    rc = lib().lb2_gdn_step_glue(_ptr(conv), _ptr(a), _ptr(b), _ptr(A_log), _ptr(dt_bias), _ptr(state), _ptr(s_out),
+                                 _ptr(y), NR, Hk, Dk, Hv, Dv, dtype_code(conv), _rounded(inv * inv, conv.dtype),
+                                 _rounded(inv, conv.dtype), float(1e-6 * inv * inv), _stream(conv))
+    check(rc, "gdn_step_glue")
+    return y, s_out
+
+
+def gdn_norm_gate(x, z, weight, eps):
+    """silu(z) * (weight * rms_norm(x)) over the last axis."""
+    _cuda(x, z, weight)
+    D = x.shape[-1]
+    xc, zc = x.contiguous(), z.contiguous()
+    out = torch.empty_like(xc)
+    rc = lib().lb2_gdn_norm_gate(_ptr(xc), _ptr(zc), _ptr(weight.contiguous()), _ptr(out), xc.numel() // D, D,
+                                 dtype_code(xc), float(eps), _stream(xc))
+    check(rc, "gdn_norm_gate")
+    return out
