@@ -6,12 +6,11 @@
 // A producer warp streams, unit after unit without a pause, the unit's folded Q tile (a 2-slot ring) and its
 // 64-key K and V tiles (a STAGES-deep ring), all with TMA into 128-byte swizzled boxes of 64 head-dim elements;
 // four consumer warps each take 16 of a tile's 64 keys and run S = Q K^T and O += P V on mma.sync m16n8k16 (fp32
-// accumulate) with an fp32 online softmax in base 2. At a unit's end the four warps' (max, sum, O) are merged in
-// shared memory while the producer already prefetches the next unit. A sequence that fits one split writes its
-// output directly; otherwise each split writes its partial (max, sum, unnormalised O) to the workspace and
-// split_combine_kernel, launched right behind as a programmatic dependent, merges the splits of every (b, hk, row)
-// by log-sum-exp -- the combine of foldattn_merge (foldattn.py:188-211) and CpuAttn's range merge
-// (cpu_ext/cpu_kern.cpp:607-628).
+// accumulate) with an fp32 online softmax in base 2. At a unit's end each consumer warp drops its partial (max, sum,
+// unnormalised O) into shared memory and goes on to the next unit while the producer keeps streaming; a merger warp
+// folds the four into the unit's partial in the workspace; split_combine_kernel, launched right behind as a
+// programmatic dependent, merges the splits of each (b, hk, row) by log-sum-exp -- the combine of foldattn_merge
+// (foldattn.py:188-211) and CpuAttn's range merge (cpu_ext/cpu_kern.cpp:607-628).
 #pragma once
 
 #include "common.cuh"
@@ -21,7 +20,9 @@ namespace decode {
 
 constexpr int BK = 64;         // keys per tile
 constexpr int CONSUMERS = 4;   // consumer warps, 16 keys of each tile apiece
-constexpr int THREADS = (CONSUMERS + 1) * 32;
+constexpr int PRODUCER = CONSUMERS;     // warp index of the TMA producer
+constexpr int MERGER = CONSUMERS + 1;   // warp index of the partial merger
+constexpr int THREADS = (CONSUMERS + 2) * 32;
 constexpr int MAX_B = 1024;    // sequences a call (the per-CTA unit table)
 
 template <int D, int MT>
@@ -33,12 +34,13 @@ struct Cfg {
   static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
   static constexpr int QSLOT = (D / 64) * RP * 128;           // one folded Q tile
   static constexpr int Q_OFF = RING_BYTES;
-  static constexpr int MERGE_OFF = Q_OFF + 2 * QSLOT;         // [CONSUMERS][RP][D] O + [CONSUMERS][RP][2] (m, l)
-  static constexpr int MERGE_BYTES = CONSUMERS * RP * D * 4 + CONSUMERS * RP * 2 * 4;
-  static constexpr int PREFIX_OFF = MERGE_OFF + MERGE_BYTES;  // [MAX_B + 1] ints
+  static constexpr int PART_OFF = Q_OFF + 2 * QSLOT;         // [CONSUMERS][RP][D] O + [CONSUMERS][RP][2] (m, l)
+  static constexpr int PART_BYTES = CONSUMERS * RP * D * 4 + CONSUMERS * RP * 2 * 4;
+  static constexpr int PREFIX_OFF = PART_OFF + PART_BYTES;   // [MAX_B + 1] ints
   static constexpr int LENS_OFF = PREFIX_OFF + (MAX_B + 1) * 4;  // [MAX_B] ints
   static constexpr int META_OFF = LENS_OFF + MAX_B * 4;
-  static constexpr int BAR_OFF = (META_OFF + 2 * 32 + 15) / 16 * 16;
+  static constexpr int PMETA_OFF = META_OFF + 2 * 32;        // (b, hk, s, nsplit_b) of the unit in the part area
+  static constexpr int BAR_OFF = (PMETA_OFF + 16 + 15) / 16 * 16;
   static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024 /*align*/;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
@@ -49,8 +51,8 @@ struct Params {
   float* part_o;    // emit mode: normalised fp32 o, [B, Hq, T, D] contiguous
   float* part_lse;  // emit mode: natural-log lse, [B, Hq, T]
   const int32_t* kv_len;
-  float* ws_o;      // [B, Hkv, nsplit, RP, D] unnormalised partial O
-  float* ws_ml;     // [B, Hkv, nsplit, RP, 2] (max in log2 units, sum)
+  float* ws_o;      // [B, Hkv, nsplit, rows, D] unnormalised partial O of each split
+  float* ws_ml;     // [B, Hkv, nsplit, rows, 2] (max in log2 units, sum)
   int B, Hq, Hkv, T, N, G, rows;
   int split, nsplit;
   int causal, emit;
@@ -99,18 +101,6 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// AND of `pred` over the four consumer warps (named barrier 1, 128 threads); also orders their shared-memory use.
-__device__ __forceinline__ bool consumers_all(bool pred) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, 1, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"(uint32_t(pred)), "r"(CONSUMERS * 32)
-      : "memory");
-  return r != 0;
-}
-
 // Unit u of the call -> (b, s, hk) through the prefix table of per-sequence split counts.
 __device__ __forceinline__ void unit_coords(const int* prefix, int B, int Hkv, int u, int& b, int& s, int& hk) {
   const int pidx = u / Hkv;
@@ -143,6 +133,11 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const __grid_constan
   uint64_t* empty = full + STAGES;
   uint64_t* q_full = empty + STAGES;
   uint64_t* q_empty = q_full + 2;
+  uint64_t* part_full = q_empty + 2;   // the four consumer warps' partials of a unit are in the part area
+  uint64_t* part_empty = part_full + 1;  // the merger has read them
+  int* pmeta = reinterpret_cast<int*>(sm + C::PMETA_OFF);
+  float* pwo = reinterpret_cast<float*>(sm + C::PART_OFF);  // [CONSUMERS][RP][D]
+  float* pwml = pwo + CONSUMERS * RP * D;                  // [CONSUMERS][RP][2]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int* lens = reinterpret_cast<int*>(sm + C::LENS_OFF);
@@ -155,6 +150,8 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const __grid_constan
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], CONSUMERS);
     }
+    mbar_init(part_full, CONSUMERS);
+    mbar_init(part_empty, 1);
     fence_barrier_init();
   }
   // per-sequence lengths and split counts (loaded in parallel), then warp 0 scans the counts into a prefix table
@@ -185,7 +182,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const __grid_constan
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   // ------------------------------------------------------------------ producer warp: Q tiles and K/V tiles
-  if (warp == CONSUMERS) {
+  if (warp == PRODUCER) {
     if (lane == 0) {
       prefetch_tensormap(&qmap);
       prefetch_tensormap(&kmap);
@@ -230,18 +227,44 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const __grid_constan
     return;  // the producer takes part in no block-wide barrier after the setup
   }
 
+  // ------------------------------------------------------------------ merger warp: one partial per unit
+  if (warp == MERGER) {
+    int uc = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++uc) {
+      if (!mbar_wait(part_full, uc & 1, 7)) break;
+      const int b = pmeta[0], hk = pmeta[1], s = pmeta[2];
+      const size_t part = ((size_t(b) * p.Hkv + hk) * p.nsplit + s) * p.rows;
+      for (int e = lane; e < p.rows * D; e += 32) {
+        const int r = e / D, d = e % D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < CONSUMERS; ++w) M = fmaxf(M, pwml[(w * RP + r) * 2]);
+        const float Mu = M == -INFINITY ? 0.f : M;
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int w = 0; w < CONSUMERS; ++w) {
+          const float wgt = ex2(pwml[(w * RP + r) * 2] - Mu);
+          L += pwml[(w * RP + r) * 2 + 1] * wgt;
+          O += pwo[(w * RP + r) * D + d] * wgt;
+        }
+        p.ws_o[(part + r) * D + d] = O;
+        if (d == 0) *reinterpret_cast<float2*>(&p.ws_ml[(part + r) * 2]) = make_float2(M, L);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(part_empty);
+    }
+    return;
+  }
+
   // ------------------------------------------------------------------ consumer warps
   const int quad = lane >> 2, qid = lane & 3;
-  float* wo = reinterpret_cast<float*>(sm + C::MERGE_OFF);  // [CONSUMERS][RP][D]
-  float* wml = wo + CONSUMERS * RP * D;                      // [CONSUMERS][RP][2]
   int gt = 0, uc = 0;
   bool ok = true;
   for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++uc) {
     const int qs = uc & 1;
-    // The four consumer warps leave the unit loop together: a failed wait anywhere ends it for all of them, so no
-    // warp is ever left alone at the consumers' named barrier.
-    ok = mbar_wait(&q_full[qs], (uc >> 1) & 1, 5) && ok;
-    if (!consumers_all(ok)) break;
+    // No named barrier joins the consumer warps: a warp whose (time-bounded) wait gives up leaves the loop, the
+    // producer then stops at its own bounded waits, and the other warps' waits end the same way.
+    if (!mbar_wait(&q_full[qs], (uc >> 1) & 1, 5)) break;
     const int* m = meta + qs * 8;
     const int b = m[0], hk = m[1], s = m[2], n0 = m[3], n1 = m[4], len = m[5];
     const int ntiles = n1 > n0 ? (n1 - n0 + BK - 1) / BK : 0;
@@ -373,7 +396,10 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const __grid_constan
       if (lane == 0) mbar_arrive(&empty[st]);
     }
 
-    // -------------------------------------------------------------- unit epilogue: merge the four warps
+    // -------------------------------------------------------------- unit epilogue: this warp's partial
+    // Each warp drops its (max, sum, unnormalised O) for the unit's rows into the part area and goes on to the next
+    // unit while the producer keeps streaming; the merger warp folds the four into the unit's one partial in the
+    // workspace (split_combine_kernel then merges the splits of each (b, hk, row)).
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -381,125 +407,111 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const __grid_constan
         l_run[mt][hh] += __shfl_xor_sync(0xffffffffu, l_run[mt][hh], 1);
         l_run[mt][hh] += __shfl_xor_sync(0xffffffffu, l_run[mt][hh], 2);
       }
+    if (uc >= 1 && !mbar_wait(part_empty, (uc - 1) & 1, 8)) break;  // the merger has read the previous unit's
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const int r = mt * 16 + quad + 8 * hh;
+        if (r >= p.rows) continue;
         if (qid == 0) {
-          wml[(warp * RP + r) * 2] = m_run[mt][hh];
-          wml[(warp * RP + r) * 2 + 1] = l_run[mt][hh];
+          pwml[(warp * RP + r) * 2] = m_run[mt][hh];
+          pwml[(warp * RP + r) * 2 + 1] = l_run[mt][hh];
         }
 #pragma unroll
         for (int j = 0; j < ND; ++j)
-          *reinterpret_cast<float2*>(&wo[(warp * RP + r) * D + j * 8 + 2 * qid]) =
+          *reinterpret_cast<float2*>(&pwo[(warp * RP + r) * D + j * 8 + 2 * qid]) =
               make_float2(acc[mt][j][2 * hh], acc[mt][j][2 * hh + 1]);
       }
-    asm volatile("bar.sync 1, %0;" ::"r"(CONSUMERS * 32));
-
-    const int ct = threadIdx.x;  // 0 .. 127
-    const bool single = nsplit_b == 1;
-    float* so = p.ws_o + ((size_t(b) * p.Hkv + hk) * p.nsplit + s) * RP * D;
-    float* sml = p.ws_ml + ((size_t(b) * p.Hkv + hk) * p.nsplit + s) * RP * 2;
-    for (int e = ct; e < p.rows * D; e += CONSUMERS * 32) {
-      const int r = e / D, d = e % D;
-      float M = -INFINITY;
-#pragma unroll
-      for (int w = 0; w < CONSUMERS; ++w) M = fmaxf(M, wml[(w * RP + r) * 2]);
-      const float Mu = M == -INFINITY ? 0.f : M;
-      float L = 0.f, O = 0.f;
-#pragma unroll
-      for (int w = 0; w < CONSUMERS; ++w) {
-        const float wgt = ex2(wml[(w * RP + r) * 2] - Mu);
-        L += wml[(w * RP + r) * 2 + 1] * wgt;
-        O += wo[(w * RP + r) * D + d] * wgt;
-      }
-      if (single) {
-        const int g = r / p.T, t = r % p.T, h = hk * p.G + g;
-        const float val = L > 0.f ? O / L : 0.f;
-        if (p.emit) {
-          const size_t ro = (size_t(b) * p.Hq + h) * p.T + t;
-          p.part_o[ro * D + d] = val;
-          if (d == 0) p.part_lse[ro] = L > 0.f ? (M + __log2f(L)) * 0.69314718055994531f : -INFINITY;
-        } else {
-          reinterpret_cast<T*>(p.o)[b * p.o_st[0] + int64_t(h) * p.o_st[1] + int64_t(t) * p.o_st[2] + d] =
-              from_f<T>(val);
-        }
-      } else {
-        so[r * D + d] = O;
-        if (d == 0) {
-          sml[r * 2] = M;
-          sml[r * 2 + 1] = L;
-        }
-      }
+    if (warp == 0 && lane == 0) {
+      pmeta[0] = b;
+      pmeta[1] = hk;
+      pmeta[2] = s;
     }
-    // the split's partial is now in the workspace; split_combine_kernel merges the splits of (b, hk)
-    // the merge area is free again; a failed tile wait in any warp ends the loop for all
-    if (!consumers_all(ok)) break;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(part_full);
   }
 }
 
 // Merges the splits of every (b, hk, folded row) of a decode call: one warp per row, lanes across the head dim
 // (float4 loads), several splits' loads in flight at once. Rows of single-split sequences were written by the
 // decode kernel and are skipped.
-template <typename T, int D, int RP>
+template <typename T, int D>
 __global__ void __launch_bounds__(256) split_combine_kernel(const Params p) {
+  // One block per (b, hk, folded row): the row's nsplit_b partials (one per split). Pass 1: every (max, sum) pair, the
+  // block max and the total sum, and each partial's weight in shared memory. Pass 2: threads split the head dim into
+  // float4 groups and the partials into interleaved sets, so every thread has its few loads in flight at once; the
+  // sets are summed in shared memory.
   asm volatile("griddepcontrol.wait;" ::: "memory");  // the decode grid has completed and its writes are visible
-  const int wid = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  const int r = wid % p.rows, bh = wid / p.rows;
-  if (bh >= p.B * p.Hkv) return;
+  constexpr int CG = D / 4;          // float4 column groups
+  constexpr int PG = 256 / CG;       // partial sets
+  __shared__ float wts[2 * D];  // a sequence has at most 2 D splits
+  __shared__ float red[PG][D];
+  __shared__ float s_red[8];
+  const int r = blockIdx.x % p.rows;
+  const int bh = blockIdx.x / p.rows;
   const int b = bh / p.Hkv, hk = bh % p.Hkv;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int len = p.kv_len ? min(max(p.kv_len[b], 0), p.N) : p.N;
-  const int nsplit_b = max(1, (len + p.split - 1) / p.split);
-  if (nsplit_b == 1) return;
-  const float* bo = p.ws_o + size_t(bh) * p.nsplit * RP * D;
-  const float* bml = p.ws_ml + size_t(bh) * p.nsplit * RP * 2;
+  const int nparts = max(1, (len + p.split - 1) / p.split);
+  const size_t base = size_t(bh) * p.nsplit * p.rows;  // partial index of (b, hk, split 0, row 0)
+  // pass 1
   float M = -INFINITY;
-  for (int w = lane; w < nsplit_b; w += 32) M = fmaxf(M, __ldcg(&bml[(w * RP + r) * 2]));
+  for (int q = tid; q < nparts; q += 256) {
+    const float m = __ldcg(&p.ws_ml[(base + size_t(q) * p.rows + r) * 2]);
+    wts[q] = m;
+    M = fmaxf(M, m);
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  if (lane == 0) s_red[w] = M;
+  __syncthreads();
+  M = s_red[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) M = fmaxf(M, s_red[i]);
   const float Mu = M == -INFINITY ? 0.f : M;
+  __syncthreads();
   float L = 0.f;
-  for (int w = lane; w < nsplit_b; w += 32) {
-    const float2 ml = __ldcg(reinterpret_cast<const float2*>(&bml[(w * RP + r) * 2]));
-    L += ml.y * ex2(ml.x - Mu);
+  for (int q = tid; q < nparts; q += 256) {
+    const float wq = ex2(wts[q] - Mu);
+    wts[q] = wq;
+    L += wq * __ldcg(&p.ws_ml[(base + size_t(q) * p.rows + r) * 2 + 1]);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-  constexpr int V = D / 32;  // head-dim elements a lane
-  float acc[V];
+  if (lane == 0) s_red[w] = L;
+  __syncthreads();
+  L = 0.f;
 #pragma unroll
-  for (int i = 0; i < V; ++i) acc[i] = 0.f;
-#pragma unroll 4
-  for (int w = 0; w < nsplit_b; ++w) {
-    const float wgt = ex2(__ldcg(&bml[(w * RP + r) * 2]) - Mu);
-    const float* src = bo + (size_t(w) * RP + r) * D + lane * V;
-    if constexpr (V == 4) {
-      const float4 x = __ldcg(reinterpret_cast<const float4*>(src));
-      acc[0] += wgt * x.x;
-      acc[1] += wgt * x.y;
-      acc[2] += wgt * x.z;
-      acc[3] += wgt * x.w;
-    } else {
-#pragma unroll
-      for (int i = 0; i < V; i += 2) {
-        const float2 x = __ldcg(reinterpret_cast<const float2*>(src + i));
-        acc[i] += wgt * x.x;
-        acc[i + 1] += wgt * x.y;
-      }
-    }
+  for (int i = 0; i < 8; ++i) L += s_red[i];
+  // pass 2
+  const int cg = tid % CG, pg = tid / CG;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+  for (int q = pg; q < nparts; q += PG) {
+    const float wq = wts[q];
+    const float4 x = __ldcg(reinterpret_cast<const float4*>(p.ws_o + (base + size_t(q) * p.rows + r) * D) + cg);
+    acc.x += wq * x.x;
+    acc.y += wq * x.y;
+    acc.z += wq * x.z;
+    acc.w += wq * x.w;
   }
-  const float inv = L > 0.f ? 1.f / L : 0.f;
-  const int g = r / p.T, t = r % p.T, h = hk * p.G + g;
-  if (p.emit) {
-    const size_t ro = (size_t(b) * p.Hq + h) * p.T + t;
+  *reinterpret_cast<float4*>(&red[pg][cg * 4]) = acc;
+  __syncthreads();
+  if (tid < D) {
+    float o = 0.f;
 #pragma unroll
-    for (int i = 0; i < V; ++i) p.part_o[ro * D + lane * V + i] = acc[i] * inv;
-    if (lane == 0) p.part_lse[ro] = L > 0.f ? (M + __log2f(L)) * 0.69314718055994531f : -INFINITY;
-  } else {
-    T* orow = reinterpret_cast<T*>(p.o) + b * p.o_st[0] + int64_t(h) * p.o_st[1] + int64_t(t) * p.o_st[2];
-#pragma unroll
-    for (int i = 0; i < V; ++i) orow[lane * V + i] = from_f<T>(acc[i] * inv);
+    for (int i = 0; i < PG; ++i) o += red[i][tid];
+    const float val = L > 0.f ? o / L : 0.f;
+    const int g = r / p.T, t = r % p.T, h = hk * p.G + g;
+    if (p.emit) {
+      const size_t ro = (size_t(b) * p.Hq + h) * p.T + t;
+      p.part_o[ro * D + tid] = val;
+      if (tid == 0) p.part_lse[ro] = L > 0.f ? (M + __log2f(L)) * 0.69314718055994531f : -INFINITY;
+    } else {
+      reinterpret_cast<T*>(p.o)[b * p.o_st[0] + int64_t(h) * p.o_st[1] + int64_t(t) * p.o_st[2] + tid] =
+          from_f<T>(val);
+    }
   }
 }
 

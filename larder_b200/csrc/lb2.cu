@@ -90,9 +90,9 @@ static int pick_split(int B, int Hkv, int N, int D, int split) {
   if (split > 0) return std::max((split + BK - 1) / BK * BK, min_split(N, D));
   int dev = 0;
   cudaGetDevice(&dev);
-  // About four units a CTA (one CTA an SM) when sequences fill half the capacity on average, never under two
+  // About 3.5 units a CTA (one CTA an SM) when sequences fill half the capacity on average, never under two
   // tiles a unit: long enough units that the per-unit epilogue stays small, enough of them to balance.
-  const int64_t target = int64_t(sm_count(dev)) * 4;
+  const int64_t target = int64_t(sm_count(dev)) * 7 / 2;
   int64_t s = (int64_t(B) * Hkv * (N / 2 + 1) + target - 1) / target;
   s = (s + BK - 1) / BK * BK;
   if (s < 2 * BK) s = 2 * BK;
@@ -106,13 +106,14 @@ struct WsLayout {
   size_t ml, o, total;
 };
 
-// Split partials: (max, sum) pairs then unnormalised O rows, [B, Hkv, nsplit, rp] each. Every value a call reads
+// Split partials, one per (b, hk, split, row): (max, sum) pairs, then unnormalised O rows. Every value a call reads
 // was written earlier in the same call, so nothing in the workspace needs to start at zero.
-static WsLayout ws_layout(int B, int Hkv, int rp, int D, int nsplit) {
+static WsLayout ws_layout(int B, int Hkv, int rows, int D, int nsplit) {
   WsLayout w;
+  const size_t parts = size_t(B) * Hkv * nsplit * rows;
   w.ml = 0;
-  w.o = w.ml + align_up(size_t(B) * Hkv * nsplit * rp * 2 * sizeof(float), 256);
-  w.total = w.o + size_t(B) * Hkv * nsplit * rp * D * sizeof(float);
+  w.o = align_up(parts * 2 * sizeof(float), 256);
+  w.total = w.o + parts * D * sizeof(float);
   return w;
 }
 
@@ -131,10 +132,10 @@ static int launch_t(const CUtensorMap& qm, const CUtensorMap& km, const CUtensor
   dim3 grid(unsigned(sm_count(dev)));
   kern<<<grid, THREADS, smem, st>>>(qm, km, vm, p);
   LB2_CUDA(cudaGetLastError());
-  if (p.nsplit > 1) {
+  {
     // the split combine as a programmatic dependent: its launch overlaps the decode grid's tail
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(unsigned((int64_t(p.B) * p.Hkv * p.rows + 7) / 8));
+    cfg.gridDim = dim3(unsigned(int64_t(p.B) * p.Hkv * p.rows));
     cfg.blockDim = dim3(256);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = st;
@@ -143,7 +144,7 @@ static int launch_t(const CUtensorMap& qm, const CUtensorMap& km, const CUtensor
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    LB2_CUDA(cudaLaunchKernelEx(&cfg, split_combine_kernel<T, D, Cfg<D, MT>::RP>, p));
+    LB2_CUDA(cudaLaunchKernelEx(&cfg, split_combine_kernel<T, D>, p));
   }
   return LB2_OK;
 }
@@ -181,7 +182,7 @@ static int run(const void* q, const int64_t* q_st, const void* k, const int64_t*
   const int MT = rows_tiles(G, T);
   const int sp = pick_split(B, Hkv, N, D, split);
   const int nsplit = (N + sp - 1) / sp;
-  const WsLayout w = ws_layout(B, Hkv, MT * 16, D, nsplit);
+  const WsLayout w = ws_layout(B, Hkv, rows, D, nsplit);
   LB2_CHECK_ARG(workspace != nullptr && workspace_bytes >= w.total, "decode: workspace too small");
   LB2_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "decode: workspace must be 256-byte aligned");
   LB2_CHECK_ARG(B <= MAX_B, "decode: at most 1024 sequences a call");
@@ -357,9 +358,8 @@ int lb2_status(void* stream) {
 
 size_t lb2_attn_decode_workspace_size(int B, int Hq, int Hkv, int T, int N, int D, int split) {
   if (B <= 0 || Hkv <= 0 || Hq % Hkv || N <= 0 || T <= 0) return 0;
-  const int MT = decode::rows_tiles(Hq / Hkv, T);
   const int sp = decode::pick_split(B, Hkv, N, D, split);
-  return decode::ws_layout(B, Hkv, MT * 16, D, (N + sp - 1) / sp).total;
+  return decode::ws_layout(B, Hkv, (Hq / Hkv) * T, D, (N + sp - 1) / sp).total;
 }
 
 int lb2_attn_decode(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
