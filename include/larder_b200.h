@@ -71,11 +71,12 @@ int lb2_attn_prefill(const void* q, const int64_t* q_st, const void* k, const in
 /* ------------------------------------------------------------------------------------------------------------
  * Split-KV decode attention (few query rows over a long KV cache; HBM-bandwidth bound).
  *
- * The G*T query rows that share a KV head are folded into one tile (foldattn.py:230-259); keys are cut into
- * splits of `split` keys (a multiple of 64, or 0 to let the library choose; raised so that a sequence has at most
- * 2 D splits), each split computes an fp32 partial (o, max, sum) with an online softmax in a persistent kernel,
- * and a second kernel merges the splits of each (b, kv head) by log-sum-exp (foldattn.py:188-211,
- * cpu_kern.cpp:607-628) and writes o.
+ * The G*T query rows that share a KV head are folded into one tile (foldattn.py:230-259). A persistent kernel
+ * (one CTA an SM) computes fp32 partials (o, max, sum) with an online softmax over key ranges, and a second kernel
+ * merges the partials of each (b, kv head) by log-sum-exp (foldattn.py:188-211, cpu_kern.cpp:607-628) and writes o.
+ * split = 0: balanced schedule -- the call's 64-key tiles are cut into equal runs, one a CTA, whatever the
+ * per-sequence lengths; split > 0: key ranges of `split` keys (rounded up to a multiple of 64, and raised so that a
+ * sequence has at most 512 of them) dealt to the CTAs round-robin.
  *   q [B, Hq, T, D], k/v [B, Hkv, N, D] (N = capacity), o [B, Hq, T, D]: strides as in lb2_attn_prefill
  *   kv_len int32 [B] device array of per-sequence key counts (<= N), or NULL for N everywhere
  *   causal: 1 for bottom-right causal over each sequence's own length (T >= 2 verify rows), else 0

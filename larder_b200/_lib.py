@@ -73,5 +73,9 @@ def check(rc, what):
     raise LarderError(f"{what}: {msg} (status {rc})")
 
 
+_I64N = [ctypes.c_int64 * n for n in range(5)]
+
+
 def i64(*vals):
-    return (ctypes.c_int64 * len(vals))(*[int(v) for v in vals])
+    """An int64 array argument (strides, shapes) from Python ints."""
+    return _I64N[len(vals)](*vals) if len(vals) < 5 else (ctypes.c_int64 * len(vals))(*vals)

@@ -1,15 +1,20 @@
 // Split-KV decode attention for a few query rows over a long KV cache (HBM-bandwidth bound).
 //
-// Persistent kernel: one CTA per SM walks a static round-robin share of equal-sized work units, a unit being
-// (sequence b, one `split`-key range of it, KV head hk). The G*T query rows sharing KV head hk are folded into
-// 16-row tiles (the fold of foldattn.py:230-259), so every K/V byte is read from HBM once per call.
-// A producer warp streams, unit after unit without a pause, the unit's folded Q tile (a 2-slot ring) and its
-// 64-key K and V tiles (a STAGES-deep ring), all with TMA into 128-byte swizzled boxes of 64 head-dim elements;
-// four consumer warps each take 16 of a tile's 64 keys and run S = Q K^T and O += P V on mma.sync m16n8k16 (fp32
-// accumulate) with an fp32 online softmax in base 2. At a unit's end each consumer warp drops its partial (max, sum,
-// unnormalised O) into shared memory and goes on to the next unit while the producer keeps streaming; a merger warp
-// folds the four into the unit's partial in the workspace; split_combine_kernel, launched right behind as a
-// programmatic dependent, merges the splits of each (b, hk, row) by log-sum-exp -- the combine of foldattn_merge
+// Persistent kernel: one CTA per SM walks its share of the call's work items, an item being (sequence b, KV head hk,
+// a key range of b). The G*T query rows sharing KV head hk are folded into 16-row tiles (the fold of
+// foldattn.py:230-259), so every K/V byte is read from HBM once per call. Two schedules:
+//  - balanced (split = 0): the call's 64-key tiles, ordered (b, hk, tile), are cut into gridDim.x equal runs and CTA c
+//    takes run c, cut again where a (b, hk) pair ends. Every CTA streams the same number of tiles whatever the
+//    per-sequence lengths, and CTA c's item of pair p writes partial slot c + p: unique (a later CTA starts at or
+//    after an earlier CTA's last pair) and contiguous per pair, so the combine finds a pair's partials by arithmetic;
+//  - split (split > 0): equal `split`-key units (b, s, hk) dealt round-robin, partial slot (b Hkv + hk) nsplit + s.
+// A producer warp streams, item after item without a pause, the item's folded Q tile (a 2-slot ring) and its 64-key
+// K and V tiles (a STAGES-deep ring), all with TMA into 128-byte swizzled boxes of 64 head-dim elements; four
+// consumer warps each take 16 of a tile's 64 keys and run S = Q K^T and O += P V on mma.sync m16n8k16 (fp32
+// accumulate) with an fp32 online softmax in base 2. At an item's end each consumer warp drops its partial (max, sum,
+// unnormalised O) into shared memory and goes on to the next item while the producer keeps streaming; a merger warp
+// folds the four into the item's partial in the workspace; split_combine_kernel, launched right behind as a
+// programmatic dependent, merges the partials of each (b, hk, row) by log-sum-exp -- the combine of foldattn_merge
 // (foldattn.py:188-211) and CpuAttn's range merge (cpu_ext/cpu_kern.cpp:607-628).
 #pragma once
 
@@ -19,30 +24,40 @@ namespace lb2 {
 namespace decode {
 
 constexpr int BK = 64;         // keys per tile
-constexpr int CONSUMERS = 4;   // consumer warps, 16 keys of each tile apiece
-constexpr int PRODUCER = CONSUMERS;     // warp index of the TMA producer
-constexpr int MERGER = CONSUMERS + 1;   // warp index of the partial merger
-constexpr int THREADS = (CONSUMERS + 2) * 32;
-constexpr int MAX_B = 1024;    // sequences a call (the per-CTA unit table)
+constexpr int MAX_B = 1024;    // sequences a call (the per-CTA prefix table)
+constexpr int MAX_PARTS = 512; // partials of one (b, hk) pair the combine can merge
 
-template <int D, int MT>
+// NT: 8-row tiles of folded query rows (rows <= 8 NT). With one row tile, two groups of four consumer warps take
+// alternate K/V tiles (eight consumer warps, two a scheduler, so one hides the other's latency); otherwise one
+// group of four. The K/V ring gets as many stages as shared memory holds (at most 8).
+template <int D, int NT>
 struct Cfg {
-  static constexpr int RP = MT * 16;                          // folded rows, padded
-  static constexpr int STAGES = D == 64 ? 6 : D == 128 ? 4 : 2;
+  static constexpr int RP = NT * 8;                           // folded rows, padded
+  static constexpr int GROUPS = NT == 1 ? 2 : 1;
+  static constexpr int CONSUMERS = 4 * GROUPS;                // consumer warps, 16 keys of a tile apiece
+  static constexpr int PRODUCER = CONSUMERS;                  // warp index of the TMA producer
+  static constexpr int MERGER = CONSUMERS + 1;                // warp index of the partial merger
+  static constexpr int THREADS = (CONSUMERS + 2) * 32;
+  static constexpr bool Q_REGS = NT * (D / 16) <= 16;         // Q^T fragments held in registers for the item
   static constexpr int TILE_BYTES = BK * D * 2;               // one K (or V) tile, bf16/f16
   static constexpr int STAGE_BYTES = 2 * TILE_BYTES;          // K + V
-  static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
   static constexpr int QSLOT = (D / 64) * RP * 128;           // one folded Q tile
+  static constexpr int PART_BYTES = CONSUMERS * RP * D * 4 + CONSUMERS * RP * 2 * 4;
+  static constexpr int FIXED = 2 * QSLOT + PART_BYTES + (2 * MAX_B + 1) * 4 + 16 + 256 + 1024;
+  static constexpr int STAGES_FIT = (232448 - FIXED) / STAGE_BYTES;
+  // With two groups the stage count is even, so that stage st only ever holds tiles of group st % 2: a warp then waits
+  // on every phase of its stages in order. (With an odd count the tile STAGES back in the same stage is the other
+  // group's; a wait for phase k could run while phase k - 1 is still open, and parity k & 1 would match phase k - 2.)
+  static constexpr int STAGES = (STAGES_FIT > 8 ? 8 : STAGES_FIT) / GROUPS * GROUPS;
+  static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
   static constexpr int Q_OFF = RING_BYTES;
   static constexpr int PART_OFF = Q_OFF + 2 * QSLOT;         // [CONSUMERS][RP][D] O + [CONSUMERS][RP][2] (m, l)
-  static constexpr int PART_BYTES = CONSUMERS * RP * D * 4 + CONSUMERS * RP * 2 * 4;
   static constexpr int PREFIX_OFF = PART_OFF + PART_BYTES;   // [MAX_B + 1] ints
   static constexpr int LENS_OFF = PREFIX_OFF + (MAX_B + 1) * 4;  // [MAX_B] ints
-  static constexpr int META_OFF = LENS_OFF + MAX_B * 4;
-  static constexpr int PMETA_OFF = META_OFF + 2 * 32;        // (b, hk, s, nsplit_b) of the unit in the part area
-  static constexpr int BAR_OFF = (PMETA_OFF + 16 + 15) / 16 * 16;
+  static constexpr int BAR_OFF = (LENS_OFF + MAX_B * 4 + 15) / 16 * 16;
   static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024 /*align*/;
-  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+  static_assert(STAGES >= 2 && STAGES % GROUPS == 0 && SMEM_BYTES <= 232448, "shared memory budget");
+  static_assert((2 * STAGES + 6) * 8 <= 256, "barrier area");
 };
 
 struct Params {
@@ -51,10 +66,12 @@ struct Params {
   float* part_o;    // emit mode: normalised fp32 o, [B, Hq, T, D] contiguous
   float* part_lse;  // emit mode: natural-log lse, [B, Hq, T]
   const int32_t* kv_len;
-  float* ws_o;      // [B, Hkv, nsplit, rows, D] unnormalised partial O of each split
-  float* ws_ml;     // [B, Hkv, nsplit, rows, 2] (max in log2 units, sum)
+  float* ws_o;      // [slots, rows, D] unnormalised partial O of each item
+  float* ws_ml;     // [slots, rows, 2] (max in log2 units, sum)
   int B, Hq, Hkv, T, N, G, rows;
-  int split, nsplit;
+  int balanced;     // 1: balanced tile runs; 0: split units
+  int split, nsplit;  // split mode: keys a unit, slots a (b, hk) pair
+  int grid;         // CTAs of the decode grid (the balanced schedule's run count)
   int causal, emit;
   float scale_log2;  // softmax scale * log2(e)
 };
@@ -101,41 +118,94 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// Unit u of the call -> (b, s, hk) through the prefix table of per-sequence split counts.
-__device__ __forceinline__ void unit_coords(const int* prefix, int B, int Hkv, int u, int& b, int& s, int& hk) {
-  const int pidx = u / Hkv;
-  hk = u - pidx * Hkv;
-  int lo = 0, hi = B;  // largest b with prefix[b] <= pidx
-  while (hi - lo > 1) {
-    const int mid = (lo + hi) >> 1;
-    if (prefix[mid] <= pidx) lo = mid; else hi = mid;
-  }
-  b = lo;
-  s = pidx - prefix[b];
+// Transposes an 8 x 8 matrix of 16-bit values held a row pair a lane (lane l: row l / 4, columns 2 (l % 4) and
+// 2 (l % 4) + 1) across the warp, in the same layout.
+__device__ __forceinline__ uint32_t movm_t(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
 }
 
-template <typename T, int D, int MT>
-__global__ void __launch_bounds__(THREADS, 1) decode_kernel(const __grid_constant__ CUtensorMap qmap,
-                                                             const __grid_constant__ CUtensorMap kmap,
-                                                             const __grid_constant__ CUtensorMap vmap,
-                                                             const Params p) {
-  using C = Cfg<D, MT>;
+// One work item: KV head hk of sequence b (length len), keys [n0, n1), partial slot `slot`.
+struct Item {
+  int b, hk, n0, n1, len, slot;
+};
+
+// The CTA's work items in order. prefix[b] counts, for one head, the split units (split mode) or the key tiles
+// (balanced mode) of sequences before b; lens[b] is b's length. Every role of the CTA walks the same sequence.
+struct Sched {
+  const int* prefix;
+  const int* lens;
+  int B, Hkv, split, nsplit, balanced;
+  int cur, end, step;
+
+  __device__ __forceinline__ Sched(const Params& p, const int* prefix_, const int* lens_)
+      : prefix(prefix_), lens(lens_), B(p.B), Hkv(p.Hkv), split(p.split), nsplit(p.nsplit), balanced(p.balanced) {
+    const int total = prefix[p.B] * p.Hkv;  // units or tiles of the call
+    if (balanced) {
+      cur = int(int64_t(blockIdx.x) * total / gridDim.x);
+      end = int(int64_t(blockIdx.x + 1) * total / gridDim.x);
+      step = 0;
+    } else {
+      cur = blockIdx.x;
+      end = total;
+      step = gridDim.x;
+    }
+  }
+
+  __device__ __forceinline__ bool next(Item& it) {
+    if (cur >= end) return false;
+    const int key = cur / Hkv;
+    int lo = 0, hi = B;  // the largest b with prefix[b] <= key, i.e. prefix[b] * Hkv <= cur
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (prefix[mid] <= key) lo = mid; else hi = mid;
+    }
+    const int b = lo;
+    it.b = b;
+    it.len = lens[b];
+    if (balanced) {  // tiles ordered (b, hk, tile); b has nt >= 1 tiles, since cur < the call's total
+      const int base = prefix[b] * Hkv, nt = prefix[b + 1] - prefix[b];
+      const int hk = (cur - base) / nt, i0 = cur - base - hk * nt;
+      const int seg_end = min(end, base + (hk + 1) * nt);
+      it.hk = hk;
+      it.n0 = i0 * BK;
+      it.n1 = min(it.len, (i0 + seg_end - cur) * BK);
+      it.slot = int(blockIdx.x) + b * Hkv + hk;
+      cur = seg_end;
+    } else {  // units ordered (b, s, hk)
+      const int hk = cur - key * Hkv, s = key - prefix[b];
+      it.hk = hk;
+      it.n0 = s * split;
+      it.n1 = min(it.len, it.n0 + split);
+      it.slot = (b * Hkv + hk) * nsplit + s;
+      cur += step;
+    }
+    return true;
+  }
+};
+
+template <typename T, int D, int NT>
+__global__ void __launch_bounds__(Cfg<D, NT>::THREADS, 1) decode_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                                       const __grid_constant__ CUtensorMap kmap,
+                                                                       const __grid_constant__ CUtensorMap vmap,
+                                                                       const Params p) {
+  using C = Cfg<D, NT>;
   constexpr int STAGES = C::STAGES;
   constexpr int RP = C::RP;
-  constexpr int ND = D / 8;   // 8-wide head-dim tiles of the output
-  constexpr int KD = D / 16;  // 16-wide k-steps of Q K^T
+  constexpr int CONSUMERS = C::CONSUMERS;
+  constexpr int THREADS = C::THREADS;
+  constexpr int KD = D / 16;  // 16-wide k-steps of K Q^T, and 16-row head-dim blocks of O^T
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   int* prefix = reinterpret_cast<int*>(sm + C::PREFIX_OFF);
-  int* meta = reinterpret_cast<int*>(sm + C::META_OFF);  // [2 slots][8]: b, hk, s, n0, n1, len
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + C::BAR_OFF);
   uint64_t* empty = full + STAGES;
   uint64_t* q_full = empty + STAGES;
   uint64_t* q_empty = q_full + 2;
-  uint64_t* part_full = q_empty + 2;   // the four consumer warps' partials of a unit are in the part area
+  uint64_t* part_full = q_empty + 2;   // the consumer warps' partials of an item are in the part area
   uint64_t* part_empty = part_full + 1;  // the merger has read them
-  int* pmeta = reinterpret_cast<int*>(sm + C::PMETA_OFF);
   float* pwo = reinterpret_cast<float*>(sm + C::PART_OFF);  // [CONSUMERS][RP][D]
   float* pwml = pwo + CONSUMERS * RP * D;                  // [CONSUMERS][RP][2]
 
@@ -144,7 +214,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const __grid_constan
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], CONSUMERS);
+      mbar_init(&empty[i], 4);  // the four warps of the group that takes the tile
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&q_full[i], 1);
@@ -154,11 +224,12 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const __grid_constan
     mbar_init(part_empty, 1);
     fence_barrier_init();
   }
-  // per-sequence lengths and split counts (loaded in parallel), then warp 0 scans the counts into a prefix table
+  // per-sequence lengths and unit or tile counts (loaded in parallel), then warp 0 scans the counts into a prefix
+  // table
   for (int b = threadIdx.x; b < p.B; b += THREADS) {
     const int len = p.kv_len ? min(max(p.kv_len[b], 0), p.N) : p.N;
     lens[b] = len;
-    prefix[b + 1] = max(1, (len + p.split - 1) / p.split);
+    prefix[b + 1] = p.balanced ? (len + BK - 1) / BK : max(1, (len + p.split - 1) / p.split);
   }
   __syncthreads();
   if (warp == 0) {
@@ -176,29 +247,25 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const __grid_constan
     if (lane == 0) prefix[0] = 0;
   }
   __syncthreads();
-  const int units = prefix[p.B] * p.Hkv;
   // The split combine (launched as this grid's programmatic dependent) may start its prologue now; it waits for
   // this grid's completion before reading any partial.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   // ------------------------------------------------------------------ producer warp: Q tiles and K/V tiles
-  if (warp == PRODUCER) {
+  if (warp == C::PRODUCER) {
     if (lane == 0) {
       prefetch_tensormap(&qmap);
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
       int gt = 0, uc = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++uc) {
-        int b, s, hk;
-        unit_coords(prefix, p.B, p.Hkv, u, b, s, hk);
-        const int len = lens[b];
-        const int n0 = s * p.split, n1 = min(len, n0 + p.split);
-        const int ntiles = n1 > n0 ? (n1 - n0 + BK - 1) / BK : 0;
+      Sched sched(p, prefix, lens);
+      Item it;
+      for (; ok && sched.next(it); ++uc) {
+        const int b = it.b, hk = it.hk, n0 = it.n0;
+        const int ntiles = it.n1 > n0 ? (it.n1 - n0 + BK - 1) / BK : 0;
         const int qs = uc & 1;
         if (uc >= 2 && !mbar_wait(&q_empty[qs], ((uc >> 1) - 1) & 1, 1)) break;
-        int* m = meta + qs * 8;
-        m[0] = b; m[1] = hk; m[2] = s; m[3] = n0; m[4] = n1; m[5] = len;
         mbar_arrive_expect_tx(&q_full[qs], (D / 64) * p.rows * 128);
 #pragma unroll
         for (int db = 0; db < D / 64; ++db)
@@ -227,28 +294,38 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const __grid_constan
     return;  // the producer takes part in no block-wide barrier after the setup
   }
 
-  // ------------------------------------------------------------------ merger warp: one partial per unit
-  if (warp == MERGER) {
+  // ------------------------------------------------------------------ merger warp: one partial per item
+  if (warp == C::MERGER) {
     int uc = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x, ++uc) {
+    Sched sched(p, prefix, lens);
+    Item it;
+    for (; sched.next(it); ++uc) {
       if (!mbar_wait(part_full, uc & 1, 7)) break;
-      const int b = pmeta[0], hk = pmeta[1], s = pmeta[2];
-      const size_t part = ((size_t(b) * p.Hkv + hk) * p.nsplit + s) * p.rows;
-      for (int e = lane; e < p.rows * D; e += 32) {
-        const int r = e / D, d = e % D;
+      const size_t part = size_t(it.slot) * p.rows;
+      for (int r = 0; r < p.rows; ++r) {
         float M = -INFINITY;
 #pragma unroll
         for (int w = 0; w < CONSUMERS; ++w) M = fmaxf(M, pwml[(w * RP + r) * 2]);
         const float Mu = M == -INFINITY ? 0.f : M;
-        float L = 0.f, O = 0.f;
+        float wgt[CONSUMERS], L = 0.f;
 #pragma unroll
         for (int w = 0; w < CONSUMERS; ++w) {
-          const float wgt = ex2(pwml[(w * RP + r) * 2] - Mu);
-          L += pwml[(w * RP + r) * 2 + 1] * wgt;
-          O += pwo[(w * RP + r) * D + d] * wgt;
+          wgt[w] = ex2(pwml[(w * RP + r) * 2] - Mu);
+          L += pwml[(w * RP + r) * 2 + 1] * wgt[w];
         }
-        p.ws_o[(part + r) * D + d] = O;
-        if (d == 0) *reinterpret_cast<float2*>(&p.ws_ml[(part + r) * 2]) = make_float2(M, L);
+        for (int c = lane; c < D / 4; c += 32) {
+          float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int w = 0; w < CONSUMERS; ++w) {
+            const float4 x = *reinterpret_cast<const float4*>(&pwo[(w * RP + r) * D + 4 * c]);
+            o.x += wgt[w] * x.x;
+            o.y += wgt[w] * x.y;
+            o.z += wgt[w] * x.z;
+            o.w += wgt[w] * x.w;
+          }
+          reinterpret_cast<float4*>(&p.ws_o[(part + r) * D])[c] = o;
+        }
+        if (lane == 0) *reinterpret_cast<float2*>(&p.ws_ml[(part + r) * 2]) = make_float2(M, L);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(part_empty);
@@ -257,50 +334,61 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const __grid_constan
   }
 
   // ------------------------------------------------------------------ consumer warps
+  // Keys sit in the M dimension of the MMAs: S^T = K Q^T (m16n8k16: 16 keys x 8 folded rows, k over the head dim)
+  // and O^T += V^T P^T (16 head-dim rows x 8 folded rows, k over the keys), so a tile of 8 rows wastes no MMA rows.
+  // The S^T accumulators turn into the B operand of the second product with one movmatrix transpose each.
   const int quad = lane >> 2, qid = lane & 3;
+  const int grp = warp >> 2, wq = warp & 3;  // group (takes tiles gt with gt % GROUPS == grp), warp in the group
   int gt = 0, uc = 0;
   bool ok = true;
-  for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++uc) {
+  Sched sched(p, prefix, lens);
+  Item it;
+  for (; ok && sched.next(it); ++uc) {
     const int qs = uc & 1;
     // No named barrier joins the consumer warps: a warp whose (time-bounded) wait gives up leaves the loop, the
     // producer then stops at its own bounded waits, and the other warps' waits end the same way.
-    if (!mbar_wait(&q_full[qs], (uc >> 1) & 1, 5)) break;
-    const int* m = meta + qs * 8;
-    const int b = m[0], hk = m[1], s = m[2], n0 = m[3], n1 = m[4], len = m[5];
+    if (!mbar_wait(&q_full[qs], (uc >> 1) & 1, 5)) {
+      ok = false;
+      break;
+    }
+    const int n0 = it.n0, n1 = it.n1, len = it.len;
     const int ntiles = n1 > n0 ? (n1 - n0 + BK - 1) / BK : 0;
-    const int nsplit_b = max(1, (len + p.split - 1) / p.split);
-    // Q fragments (A operand, row-major 16 x 16 a k-step) from the swizzled Q tile; rows are folded (g, t).
-    uint32_t qa[MT][KD][4];
+    // Q^T fragments (B operand, 16 head-dim x 8 rows a k-step): one ldmatrix.x4 gives two k-steps of a row tile.
     const uint32_t qaddr = smem_u32(sm + C::Q_OFF + qs * C::QSLOT);
+    auto q_frag = [&](int nt, int k2, uint32_t* x) {
+      const int r = nt * 8 + (lane & 7), c = k2 * 4 + (lane >> 3);
+      ldsm_x4(qaddr + (c / 8) * RP * 128 + swz(0, r, c % 8), x);
+    };
+    uint32_t qb[C::Q_REGS ? NT : 1][C::Q_REGS ? KD / 2 : 1][4];
+    if constexpr (C::Q_REGS) {
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int kk = 0; kk < KD; ++kk) {
-        const int r = mt * 16 + (lane & 15), c = kk * 2 + (lane >> 4);
-        ldsm_x4(qaddr + (c / 8) * RP * 128 + swz(0, r, c % 8), qa[mt][kk]);
-      }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&q_empty[qs]);
+        for (int k2 = 0; k2 < KD / 2; ++k2) q_frag(nt, k2, qb[nt][k2]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&q_empty[qs]);
+    }
 
-    int lim[MT][2];
+    int lim[NT][2];  // last visible key of rows nt 8 + 2 qid + e; -1 for padding rows
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
+    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int r = mt * 16 + quad + 8 * hh;
-        lim[mt][hh] = r >= p.rows ? -1 : (p.causal ? len - p.T + (r % p.T) : len - 1);
+      for (int e = 0; e < 2; ++e) {
+        const int r = nt * 8 + 2 * qid + e;
+        lim[nt][e] = r >= p.rows ? -1 : (p.causal ? len - p.T + (r % p.T) : len - 1);
       }
-    float m_run[MT][2], l_run[MT][2];
-    float acc[MT][ND][4];
+    float m_run[NT][2], l_run[NT][2];
+    float acc[NT][KD][4];  // O^T: (head dim 16 j + quad (+8), rows nt 8 + 2 qid (+1))
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt) {
-      m_run[mt][0] = m_run[mt][1] = -INFINITY;
-      l_run[mt][0] = l_run[mt][1] = 0.f;
+    for (int nt = 0; nt < NT; ++nt) {
+      m_run[nt][0] = m_run[nt][1] = -INFINITY;
+      l_run[nt][0] = l_run[nt][1] = 0.f;
 #pragma unroll
-      for (int j = 0; j < ND; ++j) acc[mt][j][0] = acc[mt][j][1] = acc[mt][j][2] = acc[mt][j][3] = 0.f;
+      for (int j = 0; j < KD; ++j) acc[nt][j][0] = acc[nt][j][1] = acc[nt][j][2] = acc[nt][j][3] = 0.f;
     }
 
     for (int i = 0; i < ntiles; ++i, ++gt) {
+      if (C::GROUPS > 1 && (gt & 1) != grp) continue;  // the other group's tile
       const int st = gt % STAGES;
       if (!mbar_wait(&full[st], (gt / STAGES) & 1, 6)) {
         ok = false;
@@ -308,153 +396,190 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const __grid_constan
       }
       const uint32_t kt = smem_u32(sm + st * C::STAGE_BYTES);
       const uint32_t vt = kt + C::TILE_BYTES;
-      const int kbase = n0 + i * BK + warp * 16;  // this warp's first key
+      const int kbase = n0 + i * BK + wq * 16;  // this warp's first key
       // Rows of this warp's 16 keys past the sequence (capacity padding may hold anything): zero V there so that
       // P = 0 never meets a non-finite value.
       const int nvalid = min(16, max(0, n1 - kbase));
       if (nvalid < 16) {
         uint8_t* vrow = sm + st * C::STAGE_BYTES + C::TILE_BYTES;
         for (int e = lane; e < (16 - nvalid) * (D / 8); e += 32) {
-          const int r = warp * 16 + nvalid + e / (D / 8), c = e % (D / 8);
+          const int r = wq * 16 + nvalid + e / (D / 8), c = e % (D / 8);
           *reinterpret_cast<uint4*>(vrow + swz(c / 8, r, c % 8)) = make_uint4(0, 0, 0, 0);
         }
         __syncwarp();
       }
-      float sc[MT][2][4];
+      // S^T = K Q^T: (keys quad, quad + 8) x (rows 2 qid, 2 qid + 1) a lane
+      float sc[NT][4];
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) sc[mt][nt][0] = sc[mt][nt][1] = sc[mt][nt][2] = sc[mt][nt][3] = 0.f;
+      for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
 #pragma unroll
       for (int kk = 0; kk < KD; ++kk) {
-        uint32_t kb[4];
-        const int r = warp * 16 + (lane & 7) + 8 * (lane >> 4);
-        const int c = kk * 2 + ((lane >> 3) & 1);
-        ldsm_x4(kt + swz(c / 8, r, c % 8), kb);
+        uint32_t ka[4];
+        const int r = wq * 16 + (lane & 15), c = kk * 2 + (lane >> 4);
+        ldsm_x4(kt + swz(c / 8, r, c % 8), ka);
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          mma16816<T>(sc[mt][0], qa[mt][kk], kb[0], kb[1]);
-          mma16816<T>(sc[mt][1], qa[mt][kk], kb[2], kb[3]);
-        }
-      }
-      uint32_t pa[MT][4];
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          float mx = -INFINITY;
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int key = kbase + nt * 8 + 2 * qid + e;
-              float& x = sc[mt][nt][2 * hh + e];
-              x = (key < n1 && key <= lim[mt][hh]) ? x * p.scale_log2 : -INFINITY;
-              mx = fmaxf(mx, x);
-            }
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-          const float m_new = fmaxf(m_run[mt][hh], mx);
-          const float m_use = m_new == -INFINITY ? 0.f : m_new;
-          const float corr = ex2(m_run[mt][hh] - m_use);
-          m_run[mt][hh] = m_new;
-          float ls = 0.f;
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              float& x = sc[mt][nt][2 * hh + e];
-              x = ex2(x - m_use);
-              ls += x;
-            }
-          l_run[mt][hh] = l_run[mt][hh] * corr + ls;
-#pragma unroll
-          for (int j = 0; j < ND; ++j) {
-            acc[mt][j][2 * hh] *= corr;
-            acc[mt][j][2 * hh + 1] *= corr;
+        for (int nt = 0; nt < NT; ++nt) {
+          if constexpr (C::Q_REGS) {
+            mma16816<T>(sc[nt], ka, qb[nt][kk >> 1][2 * (kk & 1)], qb[nt][kk >> 1][2 * (kk & 1) + 1]);
+          } else {
+            uint32_t x[4];
+            q_frag(nt, kk >> 1, x);
+            mma16816<T>(sc[nt], ka, x[2 * (kk & 1)], x[2 * (kk & 1) + 1]);
           }
         }
-        pa[mt][0] = pack2<T>(sc[mt][0][0], sc[mt][0][1]);
-        pa[mt][1] = pack2<T>(sc[mt][0][2], sc[mt][0][3]);
-        pa[mt][2] = pack2<T>(sc[mt][1][0], sc[mt][1][1]);
-        pa[mt][3] = pack2<T>(sc[mt][1][2], sc[mt][1][3]);
       }
+      // online softmax over this warp's 16 keys (a row's keys are spread over the lanes of equal qid)
+      uint32_t pb[NT][2];
+      const int key0 = kbase + quad, key1 = key0 + 8;
 #pragma unroll
-      for (int j = 0; j < ND; j += 2) {
-        uint32_t vb[4];
-        const int r = warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
-        const int c = j + (lane >> 4);
-        ldsm_x4_t(vt + swz(c / 8, r, c % 8), vb);
+      for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          mma16816<T>(acc[mt][j], pa[mt], vb[0], vb[1]);
-          mma16816<T>(acc[mt][j + 1], pa[mt], vb[2], vb[3]);
+        for (int e = 0; e < 2; ++e) {
+          float& x0 = sc[nt][e];
+          float& x1 = sc[nt][2 + e];
+          x0 = (key0 < n1 && key0 <= lim[nt][e]) ? x0 * p.scale_log2 : -INFINITY;
+          x1 = (key1 < n1 && key1 <= lim[nt][e]) ? x1 * p.scale_log2 : -INFINITY;
+          float mx = fmaxf(x0, x1);
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+          const float m_new = fmaxf(m_run[nt][e], mx);
+          const float m_use = m_new == -INFINITY ? 0.f : m_new;
+          const float corr = ex2(m_run[nt][e] - m_use);
+          m_run[nt][e] = m_new;
+          x0 = ex2(x0 - m_use);
+          x1 = ex2(x1 - m_use);
+          l_run[nt][e] = l_run[nt][e] * corr + x0 + x1;
+#pragma unroll
+          for (int j = 0; j < KD; ++j) {
+            acc[nt][j][e] *= corr;
+            acc[nt][j][2 + e] *= corr;
+          }
         }
+        // P^T as the B operand (16 keys x 8 rows): transpose the two 8 x 8 (key, row) blocks
+        pb[nt][0] = movm_t(pack2<T>(sc[nt][0], sc[nt][1]));
+        pb[nt][1] = movm_t(pack2<T>(sc[nt][2], sc[nt][3]));
+      }
+      // O^T += V^T P^T: V^T fragments (A operand, 16 head-dim x 16 keys) by transposing loads of V rows
+#pragma unroll
+      for (int j = 0; j < KD; ++j) {
+        uint32_t va[4];
+        const int r = wq * 16 + (lane & 7) + 8 * (lane >> 4);
+        const int c = 2 * j + ((lane >> 3) & 1);
+        ldsm_x4_t(vt + swz(c / 8, r, c % 8), va);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma16816<T>(acc[nt][j], va, pb[nt][0], pb[nt][1]);
       }
       if (nvalid < 16) fence_proxy_async_shared();  // generic writes above precede the next TMA into this stage
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
     }
-
-    // -------------------------------------------------------------- unit epilogue: this warp's partial
-    // Each warp drops its (max, sum, unnormalised O) for the unit's rows into the part area and goes on to the next
-    // unit while the producer keeps streaming; the merger warp folds the four into the unit's one partial in the
-    // workspace (split_combine_kernel then merges the splits of each (b, hk, row)).
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        l_run[mt][hh] += __shfl_xor_sync(0xffffffffu, l_run[mt][hh], 1);
-        l_run[mt][hh] += __shfl_xor_sync(0xffffffffu, l_run[mt][hh], 2);
-      }
-    if (uc >= 1 && !mbar_wait(part_empty, (uc - 1) & 1, 8)) break;  // the merger has read the previous unit's
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int r = mt * 16 + quad + 8 * hh;
-        if (r >= p.rows) continue;
-        if (qid == 0) {
-          pwml[(warp * RP + r) * 2] = m_run[mt][hh];
-          pwml[(warp * RP + r) * 2 + 1] = l_run[mt][hh];
-        }
-#pragma unroll
-        for (int j = 0; j < ND; ++j)
-          *reinterpret_cast<float2*>(&pwo[(warp * RP + r) * D + j * 8 + 2 * qid]) =
-              make_float2(acc[mt][j][2 * hh], acc[mt][j][2 * hh + 1]);
-      }
-    if (warp == 0 && lane == 0) {
-      pmeta[0] = b;
-      pmeta[1] = hk;
-      pmeta[2] = s;
+    if constexpr (!C::Q_REGS) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&q_empty[qs]);
     }
+
+    // -------------------------------------------------------------- item epilogue: this warp's partial
+    // Each warp drops its (max, sum, unnormalised O) for the item's rows into the part area and goes on to the next
+    // item while the producer keeps streaming; the merger warp folds them into the item's one partial in the
+    // workspace (split_combine_kernel then merges the partials of each (b, hk, row)).
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        l_run[nt][e] += __shfl_xor_sync(0xffffffffu, l_run[nt][e], 4);
+        l_run[nt][e] += __shfl_xor_sync(0xffffffffu, l_run[nt][e], 8);
+        l_run[nt][e] += __shfl_xor_sync(0xffffffffu, l_run[nt][e], 16);
+      }
+    if (!ok) break;
+    if (uc >= 1 && !mbar_wait(part_empty, (uc - 1) & 1, 8)) {  // the merger has read the previous item's
+      ok = false;
+      break;
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int r = nt * 8 + 2 * qid + e;
+        if (r >= p.rows) continue;
+        if (quad == 0) {
+          pwml[(warp * RP + r) * 2] = m_run[nt][e];
+          pwml[(warp * RP + r) * 2 + 1] = l_run[nt][e];
+        }
+        float* orow = pwo + (warp * RP + r) * D + quad;
+#pragma unroll
+        for (int j = 0; j < KD; ++j) {
+          orow[16 * j] = acc[nt][j][e];
+          orow[16 * j + 8] = acc[nt][j][2 + e];
+        }
+      }
     __syncwarp();
     if (lane == 0) mbar_arrive(part_full);
   }
 }
 
-// Merges the splits of every (b, hk, folded row) of a decode call: one warp per row, lanes across the head dim
-// (float4 loads), several splits' loads in flight at once. Rows of single-split sequences were written by the
-// decode kernel and are skipped.
+// Merges the partials of every (b, hk, folded row) of a decode call by log-sum-exp.
 template <typename T, int D>
 __global__ void __launch_bounds__(256) split_combine_kernel(const Params p) {
-  // One block per (b, hk, folded row): the row's nsplit_b partials (one per split). Pass 1: every (max, sum) pair, the
-  // block max and the total sum, and each partial's weight in shared memory. Pass 2: threads split the head dim into
-  // float4 groups and the partials into interleaved sets, so every thread has its few loads in flight at once; the
-  // sets are summed in shared memory.
-  asm volatile("griddepcontrol.wait;" ::: "memory");  // the decode grid has completed and its writes are visible
+  // One block per (b, hk, folded row). Its partials sit in consecutive slots: split mode, (b Hkv + hk) nsplit + s
+  // for the nsplit_b splits of b; balanced mode, c + (b Hkv + hk) for the CTAs c whose tile runs meet the pair, found
+  // from the pair's first and last tile. Pass 1: every (max, sum) pair, the block max and the total sum, and each
+  // partial's weight in shared memory. Pass 2: threads split the head dim into float4 groups and the partials into
+  // interleaved sets, so every thread has its few loads in flight at once; the sets are summed in shared memory.
   constexpr int CG = D / 4;          // float4 column groups
   constexpr int PG = 256 / CG;       // partial sets
-  __shared__ float wts[2 * D];  // a sequence has at most 2 D splits
+  __shared__ float wts[MAX_PARTS];
   __shared__ float red[PG][D];
   __shared__ float s_red[8];
+  __shared__ int s_tiles[2][8];
   const int r = blockIdx.x % p.rows;
   const int bh = blockIdx.x / p.rows;
   const int b = bh / p.Hkv, hk = bh % p.Hkv;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int len = p.kv_len ? min(max(p.kv_len[b], 0), p.N) : p.N;
-  const int nparts = max(1, (len + p.split - 1) / p.split);
-  const size_t base = size_t(bh) * p.nsplit * p.rows;  // partial index of (b, hk, split 0, row 0)
+  int first, nparts;
+  if (p.balanced) {
+    // tiles (one head) of the sequences before b and of all sequences; kv_len is an input of the call, so this
+    // runs before the wait for the decode grid
+    int before = 0, total = 0;
+    for (int i = tid; i < p.B; i += 256) {
+      const int li = p.kv_len ? min(max(p.kv_len[i], 0), p.N) : p.N;
+      const int t = (li + BK - 1) / BK;
+      total += t;
+      if (i < b) before += t;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      before += __shfl_xor_sync(0xffffffffu, before, o);
+      total += __shfl_xor_sync(0xffffffffu, total, o);
+    }
+    if (lane == 0) {
+      s_tiles[0][w] = before;
+      s_tiles[1][w] = total;
+    }
+    __syncthreads();
+    before = total = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      before += s_tiles[0][i];
+      total += s_tiles[1][i];
+    }
+    const int nt = (len + BK - 1) / BK;
+    if (nt == 0) {
+      first = 0;
+      nparts = 0;
+    } else {  // CTA of tile t: the largest c with floor(c total / grid) <= t, i.e. ((t + 1) grid - 1) / total
+      const int64_t tt = int64_t(total) * p.Hkv, t0 = int64_t(before) * p.Hkv + int64_t(hk) * nt;
+      const int c0 = int(((t0 + 1) * p.grid - 1) / tt), c1 = int(((t0 + nt) * p.grid - 1) / tt);
+      first = c0 + bh;
+      nparts = c1 - c0 + 1;
+    }
+  } else {
+    first = bh * p.nsplit;
+    nparts = max(1, (len + p.split - 1) / p.split);
+  }
+  const size_t base = size_t(first) * p.rows;  // partial index of (first slot, row 0)
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the decode grid has completed and its writes are visible
   // pass 1
   float M = -INFINITY;
   for (int q = tid; q < nparts; q += 256) {

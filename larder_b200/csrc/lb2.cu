@@ -79,58 +79,72 @@ static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 namespace decode {
 
-// The final merge keeps two floats per (split, row) in the merge area of CONSUMERS x RP x D floats, so a sequence
-// has at most 2 D splits; a smaller requested split is raised to respect that.
-static int min_split(int N, int D) {
-  const int per = (N + 2 * D - 1) / (2 * D);
+// The combine keeps one weight per partial of a (b, hk) pair in shared memory, so a sequence has at most MAX_PARTS
+// splits; a smaller requested split is raised to respect that.
+static int min_split(int N) {
+  const int per = (N + MAX_PARTS - 1) / MAX_PARTS;
   return (per + BK - 1) / BK * BK;
 }
 
-static int pick_split(int B, int Hkv, int N, int D, int split) {
-  if (split > 0) return std::max((split + BK - 1) / BK * BK, min_split(N, D));
+// How a call is scheduled: split = 0 asks for the balanced schedule (equal tile runs, one CTA an SM, never fewer than
+// two tiles a CTA at full capacity); split > 0 for split units of that many keys (rounded up to whole tiles).
+struct Plan {
+  int balanced, split, nsplit, grid;
+  int64_t slots;  // partial slots the workspace holds
+};
+
+static Plan plan(int B, int Hkv, int N, int D, int split) {
   int dev = 0;
   cudaGetDevice(&dev);
-  // About 3.5 units a CTA (one CTA an SM) when sequences fill half the capacity on average, never under two
-  // tiles a unit: long enough units that the per-unit epilogue stays small, enough of them to balance.
-  const int64_t target = int64_t(sm_count(dev)) * 7 / 2;
-  int64_t s = (int64_t(B) * Hkv * (N / 2 + 1) + target - 1) / target;
-  s = (s + BK - 1) / BK * BK;
-  if (s < 2 * BK) s = 2 * BK;
-  if (s > N) s = (N + BK - 1) / BK * BK;
-  return std::max(int(s < BK ? BK : s), min_split(N, D));
+  const int sms = sm_count(dev);
+  Plan pl{};
+  if (split > 0) {
+    pl.balanced = 0;
+    pl.split = std::max((split + BK - 1) / BK * BK, min_split(N));
+    pl.nsplit = (N + pl.split - 1) / pl.split;
+    pl.grid = sms;
+    pl.slots = int64_t(B) * Hkv * pl.nsplit;
+  } else {
+    const int64_t tiles = int64_t(B) * Hkv * ((N + BK - 1) / BK);
+    pl.balanced = 1;
+    pl.split = 0;
+    pl.nsplit = 0;
+    pl.grid = int(std::max<int64_t>(1, std::min<int64_t>({int64_t(sms), int64_t(MAX_PARTS), tiles / 2})));
+    pl.slots = int64_t(pl.grid) + int64_t(B) * Hkv;
+  }
+  return pl;
 }
 
-static int rows_tiles(int G, int T) { return (G * T + 15) / 16; }
+static int rows_tiles(int G, int T) { return G * T <= 8 ? 1 : G * T <= 16 ? 2 : 4; }
 
 struct WsLayout {
   size_t ml, o, total;
 };
 
-// Split partials, one per (b, hk, split, row): (max, sum) pairs, then unnormalised O rows. Every value a call reads
-// was written earlier in the same call, so nothing in the workspace needs to start at zero.
-static WsLayout ws_layout(int B, int Hkv, int rows, int D, int nsplit) {
+// Item partials, one per (slot, row): (max, sum) pairs, then unnormalised O rows. Every value a call reads was
+// written earlier in the same call, so nothing in the workspace needs to start at zero.
+static WsLayout ws_layout(int64_t slots, int rows, int D) {
   WsLayout w;
-  const size_t parts = size_t(B) * Hkv * nsplit * rows;
+  const size_t parts = size_t(slots) * rows;
   w.ml = 0;
   w.o = align_up(parts * 2 * sizeof(float), 256);
   w.total = w.o + parts * D * sizeof(float);
   return w;
 }
 
-template <typename T, int D, int MT>
+template <typename T, int D, int NT>
 static int launch_t(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const Params& p,
                     cudaStream_t st) {
-  auto kern = decode_kernel<T, D, MT>;
-  const int smem = Cfg<D, MT>::SMEM_BYTES;
+  using C = Cfg<D, NT>;
+  auto kern = decode_kernel<T, D, NT>;
   static int attr_dev = -1;
   int dev = 0;
   LB2_CUDA(cudaGetDevice(&dev));
   if (attr_dev != dev) {
-    LB2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    LB2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
     attr_dev = dev;
   }
-  dim3 grid(unsigned(sm_count(dev)));
-  kern<<<grid, THREADS, smem, st>>>(qm, km, vm, p);
+  kern<<<dim3(unsigned(p.grid)), C::THREADS, C::SMEM_BYTES, st>>>(qm, km, vm, p);
   LB2_CUDA(cudaGetLastError());
   {
     // the split combine as a programmatic dependent: its launch overlaps the decode grid's tail
@@ -149,12 +163,17 @@ static int launch_t(const CUtensorMap& qm, const CUtensorMap& km, const CUtensor
   return LB2_OK;
 }
 
+// NT: 8-row tiles of folded rows (1, 2 or 4; D = 256 takes at most 2).
 template <typename T>
-static int launch_d(int D, int MT, const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
+static int launch_d(int D, int NT, const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
                     const Params& p, cudaStream_t st) {
-  if (D == 64) return MT == 1 ? launch_t<T, 64, 1>(qm, km, vm, p, st) : launch_t<T, 64, 2>(qm, km, vm, p, st);
-  if (D == 128) return MT == 1 ? launch_t<T, 128, 1>(qm, km, vm, p, st) : launch_t<T, 128, 2>(qm, km, vm, p, st);
-  return launch_t<T, 256, 1>(qm, km, vm, p, st);
+  if (D == 64)
+    return NT == 1 ? launch_t<T, 64, 1>(qm, km, vm, p, st)
+                   : NT == 2 ? launch_t<T, 64, 2>(qm, km, vm, p, st) : launch_t<T, 64, 4>(qm, km, vm, p, st);
+  if (D == 128)
+    return NT == 1 ? launch_t<T, 128, 1>(qm, km, vm, p, st)
+                   : NT == 2 ? launch_t<T, 128, 2>(qm, km, vm, p, st) : launch_t<T, 128, 4>(qm, km, vm, p, st);
+  return NT == 1 ? launch_t<T, 256, 1>(qm, km, vm, p, st) : launch_t<T, 256, 2>(qm, km, vm, p, st);
 }
 
 static int kv_map(CUtensorMap* m, const void* base, const int64_t* st, int B, int H, int N, int D, int dtype) {
@@ -179,10 +198,10 @@ static int run(const void* q, const int64_t* q_st, const void* k, const int64_t*
     LB2_CHECK_ARG(q_st[i] % 8 == 0 && k_st[i] % 8 == 0 && v_st[i] % 8 == 0,
                   "decode: q/k/v strides must be multiples of 8 elements");
   LB2_CHECK_ARG((reinterpret_cast<uintptr_t>(q) & 15) == 0, "decode: q must be 16-byte aligned");
-  const int MT = rows_tiles(G, T);
-  const int sp = pick_split(B, Hkv, N, D, split);
-  const int nsplit = (N + sp - 1) / sp;
-  const WsLayout w = ws_layout(B, Hkv, rows, D, nsplit);
+  const int NT = rows_tiles(G, T);
+  LB2_CHECK_ARG(int64_t(B) * Hkv * ((N + BK - 1) / BK) < (int64_t(1) << 30), "decode: too many key tiles a call");
+  const Plan pl = plan(B, Hkv, N, D, split);
+  const WsLayout w = ws_layout(pl.slots, rows, D);
   LB2_CHECK_ARG(workspace != nullptr && workspace_bytes >= w.total, "decode: workspace too small");
   LB2_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "decode: workspace must be 256-byte aligned");
   LB2_CHECK_ARG(B <= MAX_B, "decode: at most 1024 sequences a call");
@@ -216,13 +235,15 @@ static int run(const void* q, const int64_t* q_st, const void* k, const int64_t*
   p.N = N;
   p.G = G;
   p.rows = rows;
-  p.split = sp;
-  p.nsplit = nsplit;
+  p.balanced = pl.balanced;
+  p.split = pl.split;
+  p.nsplit = pl.nsplit;
+  p.grid = pl.grid;
   p.causal = causal && T > 1;
   p.scale_log2 = scale * 1.4426950408889634f;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return dtype == LB2_BF16 ? launch_d<__nv_bfloat16>(D, MT, qm, km, vm, p, st)
-                           : launch_d<__half>(D, MT, qm, km, vm, p, st);
+  return dtype == LB2_BF16 ? launch_d<__nv_bfloat16>(D, NT, qm, km, vm, p, st)
+                           : launch_d<__half>(D, NT, qm, km, vm, p, st);
 }
 
 }  // namespace decode
@@ -358,8 +379,7 @@ int lb2_status(void* stream) {
 
 size_t lb2_attn_decode_workspace_size(int B, int Hq, int Hkv, int T, int N, int D, int split) {
   if (B <= 0 || Hkv <= 0 || Hq % Hkv || N <= 0 || T <= 0) return 0;
-  const int sp = decode::pick_split(B, Hkv, N, D, split);
-  return decode::ws_layout(B, Hkv, (Hq / Hkv) * T, D, (N + sp - 1) / sp).total;
+  return decode::ws_layout(decode::plan(B, Hkv, N, D, split).slots, (Hq / Hkv) * T, D).total;
 }
 
 int lb2_attn_decode(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,

@@ -29,7 +29,13 @@ def _cuda(*ts):
             raise ValueError("larder_b200 runs on CUDA tensors only (no CPU path)")
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(t):
+    """The caller's current CUDA stream on t's device, as the cudaStream_t handle the C ABI takes."""
+    if _raw_stream is not None:
+        return ctypes.c_void_p(_raw_stream(t.device.index))
     return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
 
 
@@ -46,12 +52,12 @@ def workspace(device, nbytes, tag):
     """A 256-byte aligned uint8 buffer of at least nbytes on device, kept per (device, tag) and reused by later
     calls on the same stream."""
     key = (device.index if device.index is not None else torch.cuda.current_device(), tag)
-    buf = _WS.get(key)
-    if buf is None or buf.numel() < nbytes:
+    ws = _WS.get(key)
+    if ws is None or ws.numel() < nbytes:
         buf = torch.zeros(max(int(nbytes), 256) + 256, dtype=torch.uint8, device=device)
-        _WS[key] = buf
-    off = (-buf.data_ptr()) % 256
-    return buf[off:]
+        ws = buf[(-buf.data_ptr()) % 256:]
+        _WS[key] = ws
+    return ws
 
 
 def status(device=None):
@@ -105,6 +111,17 @@ def decode_rows_limit(D):
     return 16 if D == 256 else 32
 
 
+_DECODE_WS = {}  # (B, Hq, Hkv, T, N, D, split, device) -> workspace bytes
+
+
+def _decode_ws_bytes(B, Hq, Hkv, T, N, D, split):
+    key = (B, Hq, Hkv, T, N, D, split, torch.cuda.current_device())
+    n = _DECODE_WS.get(key)
+    if n is None:
+        n = _DECODE_WS[key] = lib().lb2_attn_decode_workspace_size(B, Hq, Hkv, T, N, D, split)
+    return n
+
+
 def attn_decode(q, k, v, scale, causal=False, kv_len=None, split=0, out=None):
     """Split-KV decode attention: q [B, Hq, T, D] with few rows over k / v [B, Hkv, N, D]; kv_len int32 [B]
     (on the device) gives each sequence's key count, else all N."""
@@ -115,8 +132,7 @@ def attn_decode(q, k, v, scale, causal=False, kv_len=None, split=0, out=None):
     Hkv, N = k.shape[1], k.shape[2]
     if out is None:
         out = torch.empty((B, Hq, T, D), dtype=q.dtype, device=q.device)
-    nbytes = lib().lb2_attn_decode_workspace_size(B, Hq, Hkv, T, N, D, split)
-    ws = workspace(q.device, nbytes, "decode")
+    ws = workspace(q.device, _decode_ws_bytes(B, Hq, Hkv, T, N, D, split), "decode")
     if kv_len is not None and (kv_len.dtype != torch.int32 or kv_len.numel() != B):
         raise ValueError("kv_len must be int32 [B]")
     rc = lib().lb2_attn_decode(_ptr(q), i64(*q.stride()[:3]), _ptr(k), i64(*k.stride()[:3]), _ptr(v),
@@ -134,8 +150,7 @@ def attn_decode_partial(q, k, v, scale, kv_len=None, split=0):
     Hkv, N = k.shape[1], k.shape[2]
     part_o = torch.empty((B, Hq, T, D), dtype=torch.float32, device=q.device)
     part_lse = torch.empty((B, Hq, T), dtype=torch.float32, device=q.device)
-    nbytes = lib().lb2_attn_decode_workspace_size(B, Hq, Hkv, T, N, D, split)
-    ws = workspace(q.device, nbytes, "decode_partial")
+    ws = workspace(q.device, _decode_ws_bytes(B, Hq, Hkv, T, N, D, split), "decode_partial")
     rc = lib().lb2_attn_decode_partial(_ptr(q), i64(*q.stride()[:3]), _ptr(k), i64(*k.stride()[:3]), _ptr(v),
                                        i64(*v.stride()[:3]), _ptr(part_o), _ptr(part_lse), _ptr(kv_len), B, Hq, Hkv,
                                        T, N, D, dtype_code(q), float(scale), int(split), _ptr(ws), ws.numel(),
@@ -173,11 +188,18 @@ def _gdn_common(q, k, v, g, beta, state):
     return q, k, v, g, beta, state, (B, T, Hk, Dk, Hv, Dv)
 
 
-def gdn_recurrent(q, k, v, g, beta, state=None, mask=None):
-    """The gated delta recurrence position by position: returns (y [B, T, Hv, Dv] in q's dtype, new state)."""
+def gdn_recurrent(q, k, v, g, beta, state=None, mask=None, state_out=None):
+    """The gated delta recurrence position by position: returns (y [B, T, Hv, Dv] in q's dtype, new state). The new
+    state goes to `state_out` when given (fp32, the state's shape, contiguous, not the input state itself)."""
     q, k, v, g, beta, state, (B, T, Hk, Dk, Hv, Dv) = _gdn_common(q, k, v, g, beta, state)
     y = torch.empty((B, T, Hv, Dv), dtype=q.dtype, device=q.device)
-    s_out = torch.empty_like(state)
+    if state_out is None:
+        s_out = torch.empty_like(state)
+    else:
+        if (state_out.shape != state.shape or state_out.dtype != torch.float32 or not state_out.is_contiguous()
+                or state_out.data_ptr() == state.data_ptr()):
+            raise ValueError("gdn_recurrent: state_out must be a separate contiguous fp32 tensor of the state's shape")
+        s_out = state_out
     m = None
     if mask is not None:
         m = mask.reshape(B, T).to(torch.uint8).contiguous()

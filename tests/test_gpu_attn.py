@@ -60,11 +60,12 @@ def test_decode_config2_ragged():
         checks.grading_close(out[b:b + 1], ref, what=f"seq {b} len {n}")
 
 
-@pytest.mark.parametrize("T", [2, 3, 4])
-def test_decode_causal_verify_rows(T):
-    """foldattn's multi-row verify semantics: T rows, bottom-right causal, G*T rows folded; q a transposed view."""
-    gen = torch.Generator().manual_seed(10 + T)
-    B, Hq, Hkv, D, N = 2, 32, 8, 128, 4100
+@pytest.mark.parametrize("T,Hkv", [(2, 8), (3, 8), (4, 8), (3, 4), (4, 4)])
+def test_decode_causal_verify_rows(T, Hkv):
+    """foldattn's multi-row verify semantics: T rows, bottom-right causal, G*T rows folded (8 to 32 of them); q a
+    transposed view."""
+    gen = torch.Generator().manual_seed(10 + T + Hkv)
+    B, Hq, D, N = 2, 32, 128, 4100
     q = randn((B, T, Hq, D), oracle.BF16, gen).transpose(1, 2)
     kb = randn((B, Hkv, N + 200, D), oracle.BF16, gen)
     vb = randn((B, Hkv, N + 200, D), oracle.BF16, gen)
@@ -76,13 +77,15 @@ def test_decode_causal_verify_rows(T):
 
 @pytest.mark.parametrize("D,dt", [(64, oracle.F16), (128, oracle.BF16), (256, oracle.BF16)])
 def test_decode_head_dims(D, dt):
+    """Each head dim with 8 and 16 folded rows (one and two 8-row tiles), both schedules."""
     gen = torch.Generator().manual_seed(D)
-    q = randn((1, 16, 1, D), dt, gen)
-    k = randn((1, 2, 3000, D), dt, gen)
-    v = randn((1, 2, 3000, D), dt, gen)
-    for split in (0, 64, 1024):
-        out = f32(ops.attn_decode(q, k, v, D ** -0.5, split=split))
-        checks.grading_close(out, oracle_ref(q, k, v, D ** -0.5), what=f"D={D} split={split}")
+    for Hq in (16, 32):
+        q = randn((1, Hq, 1, D), dt, gen)
+        k = randn((1, 2, 3000, D), dt, gen)
+        v = randn((1, 2, 3000, D), dt, gen)
+        for split in (0, 64, 1024):
+            out = f32(ops.attn_decode(q, k, v, D ** -0.5, split=split))
+            checks.grading_close(out, oracle_ref(q, k, v, D ** -0.5), what=f"D={D} Hq={Hq} split={split}")
 
 
 def test_decode_partial_combine_equals_whole():
@@ -100,6 +103,77 @@ def test_decode_partial_combine_equals_whole():
     whole = f32(ops.attn_decode(q, k, v, D ** -0.5))
     checks.grading_close(out, oracle_ref(q, k, v, D ** -0.5), what="combined shards")
     assert np.abs(out - whole).max() <= 2e-2
+
+
+def test_decode_balanced_runs_cross_pairs():
+    """The balanced schedule (split = 0) on many short, ragged sequences (zero-length and sub-tile ones among them):
+    a CTA's tile run crosses many (b, hk) pairs and a long pair spans many CTAs; both modes match the oracle."""
+    gen = torch.Generator().manual_seed(8)
+    B, Hq, Hkv, D, cap = 300, 8, 2, 128, 704
+    lens = torch.randint(0, cap + 1, (B,), generator=gen)
+    lens[:5] = torch.tensor([0, 1, 63, 64, 65])
+    lens[-1] = cap
+    q = randn((B, Hq, 1, D), oracle.BF16, gen)
+    k = randn((B, Hkv, cap, D), oracle.BF16, gen)
+    v = randn((B, Hkv, cap, D), oracle.BF16, gen)
+    kv_len = lens.to(torch.int32).to(DEV)
+    bal = f32(ops.attn_decode(q, k, v, D ** -0.5, kv_len=kv_len))
+    spl = f32(ops.attn_decode(q, k, v, D ** -0.5, kv_len=kv_len, split=128))
+    for b in range(B):
+        n = int(lens[b])
+        if n == 0:
+            assert np.all(bal[b] == 0) and np.all(spl[b] == 0), f"seq {b}: zero length must give zeros"
+            continue
+        ref = oracle_ref(q[b:b + 1], k[b:b + 1, :, :n], v[b:b + 1, :, :n], D ** -0.5)
+        checks.grading_close(bal[b:b + 1], ref, what=f"balanced seq {b} len {n}")
+        checks.grading_close(spl[b:b + 1], ref, what=f"split seq {b} len {n}")
+    # one long sequence over few heads: the pair's tiles spread over many CTAs (many partials a row)
+    q1 = randn((1, 8, 1, D), oracle.BF16, gen)
+    k1 = randn((1, 1, 8192, D), oracle.BF16, gen)
+    v1 = randn((1, 1, 8192, D), oracle.BF16, gen)
+    checks.grading_close(f32(ops.attn_decode(q1, k1, v1, D ** -0.5)), oracle_ref(q1, k1, v1, D ** -0.5),
+                         what="one pair over many CTAs")
+
+
+def test_decode_repeated_shapes_and_graph_replay():
+    """Calls of different shapes (and grid sizes) in turn on one shared workspace, then the decode (persistent kernel
+    and its programmatically dependent combine) captured in a CUDA graph and replayed with new inputs: all match the
+    oracle."""
+    gen = torch.Generator().manual_seed(9)
+    D = 128
+    shapes = [(16, 32, 4, 4096), (1, 8, 1, 300), (16, 32, 4, 4096), (3, 16, 2, 2000)]
+    for B, Hq, Hkv, N in shapes:
+        q = randn((B, Hq, 1, D), oracle.BF16, gen)
+        k = randn((B, Hkv, N, D), oracle.BF16, gen)
+        v = randn((B, Hkv, N, D), oracle.BF16, gen)
+        checks.grading_close(f32(ops.attn_decode(q, k, v, D ** -0.5)), oracle_ref(q, k, v, D ** -0.5),
+                             what=f"B={B} Hkv={Hkv} N={N}")
+    B, Hq, Hkv, N = 8, 32, 4, 3000
+    q = randn((B, Hq, 1, D), oracle.BF16, gen)
+    k = randn((B, Hkv, N, D), oracle.BF16, gen)
+    v = randn((B, Hkv, N, D), oracle.BF16, gen)
+    lens = torch.randint(1, N + 1, (B,), generator=gen).to(torch.int32).to(DEV)
+    out = torch.empty_like(q)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        ops.attn_decode(q, k, v, D ** -0.5, kv_len=lens, out=out)  # workspace allocated outside the capture
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        ops.attn_decode(q, k, v, D ** -0.5, kv_len=lens, out=out)
+    ln = lens.cpu()
+    for rep in range(3):
+        q.copy_(randn((B, Hq, 1, D), oracle.BF16, gen))
+        graph.replay()
+        torch.cuda.synchronize()
+        got = f32(out)
+        for b in range(B):
+            n = int(ln[b])
+            ref = oracle_ref(q[b:b + 1], k[b:b + 1, :, :n], v[b:b + 1, :, :n], D ** -0.5)
+            checks.grading_close(got[b:b + 1], ref, what=f"replay {rep} seq {b}")
+    del graph
 
 
 def test_decode_empty_and_short_sequences():

@@ -54,7 +54,7 @@ def test_recurrent_cpu_case():
 
 def test_recurrent_decode_batch16_config4():
     """Config 4's decode: 64 recurrent steps at B=16 (Hk 16, Hv 32, 128 x 128) from a random state, one call a step,
-    the state carried in place; checked after the 64 steps."""
+    the state ping-ponged between two caller buffers (state_out); checked after the 64 steps."""
     gen = torch.Generator().manual_seed(4)
     B, Hk, Hv, D, steps = 16, 16, 32, 128, 64
     q = torch.nn.functional.normalize(torch.randn(B, steps, Hk, D, generator=gen), dim=-1).to(torch.bfloat16)
@@ -64,10 +64,11 @@ def test_recurrent_decode_batch16_config4():
     g = torch.exp(-torch.nn.functional.softplus(torch.randn(B, steps, Hv, generator=gen)))
     s0 = torch.randn(B, Hv, D, D, generator=gen) * 0.1
     s = s0.cuda()
+    bufs = [torch.empty_like(s), torch.empty_like(s)]
     ys = []
     for t in range(steps):
         y, s = ops.gdn_recurrent(q[:, t:t + 1].cuda(), k[:, t:t + 1].cuda(), v[:, t:t + 1].cuda(),
-                                 g[:, t:t + 1].cuda(), beta[:, t:t + 1].cuda(), s)
+                                 g[:, t:t + 1].cuda(), beta[:, t:t + 1].cuda(), s, state_out=bufs[t % 2])
         ys.append(f32(y))
     from gpu_util import to_np
     yr, sr = oracle.gdn(to_np(q), to_np(k), to_np(v), g.numpy(), to_np(beta), s0.numpy(), oracle.BF16,
