@@ -153,6 +153,8 @@ struct Sched {
     }
   }
 
+  __device__ __forceinline__ bool more() const { return cur < end; }
+
   __device__ __forceinline__ bool next(Item& it) {
     if (cur >= end) return false;
     const int key = cur / Hkv;
@@ -223,7 +225,13 @@ __global__ void __launch_bounds__(Cfg<D, NT>::THREADS, 1) decode_kernel(const __
     mbar_init(part_full, CONSUMERS);
     mbar_init(part_empty, 1);
     fence_barrier_init();
+    prefetch_tensormap(&qmap);  // kernel parameters: no dependency on the previous kernel
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
   }
+  // Launched as a programmatic dependent of the previous kernel in the stream: everything above touched only this
+  // CTA's shared memory; every global read below waits for that kernel to complete.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   // per-sequence lengths and unit or tile counts (loaded in parallel), then warp 0 scans the counts into a prefix
   // table
   for (int b = threadIdx.x; b < p.B; b += THREADS) {
@@ -254,9 +262,6 @@ __global__ void __launch_bounds__(Cfg<D, NT>::THREADS, 1) decode_kernel(const __
   // ------------------------------------------------------------------ producer warp: Q tiles and K/V tiles
   if (warp == C::PRODUCER) {
     if (lane == 0) {
-      prefetch_tensormap(&qmap);
-      prefetch_tensormap(&kmap);
-      prefetch_tensormap(&vmap);
       int gt = 0, uc = 0;
       bool ok = true;
       Sched sched(p, prefix, lens);
@@ -295,11 +300,12 @@ __global__ void __launch_bounds__(Cfg<D, NT>::THREADS, 1) decode_kernel(const __
   }
 
   // ------------------------------------------------------------------ merger warp: one partial per item
+  // (all but the CTA's last item, which the consumer warps merge themselves, a row each, once the stream has ended)
   if (warp == C::MERGER) {
     int uc = 0;
     Sched sched(p, prefix, lens);
     Item it;
-    for (; sched.next(it); ++uc) {
+    for (; sched.next(it) && sched.more(); ++uc) {
       if (!mbar_wait(part_full, uc & 1, 7)) break;
       const size_t part = size_t(it.slot) * p.rows;
       for (int r = 0; r < p.rows; ++r) {
@@ -515,25 +521,56 @@ __global__ void __launch_bounds__(Cfg<D, NT>::THREADS, 1) decode_kernel(const __
       }
     __syncwarp();
     if (lane == 0) mbar_arrive(part_full);
+    if (!sched.more()) {
+      // the CTA's last item: every consumer warp's partial is in the part area once part_full completes; the
+      // consumer warps merge them, warp w the rows w, w + CONSUMERS, ...
+      if (!mbar_wait(part_full, uc & 1, 11)) {
+        ok = false;
+        break;
+      }
+      const size_t part = size_t(it.slot) * p.rows;
+      for (int r = warp; r < p.rows; r += CONSUMERS) {
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < CONSUMERS; ++w) M = fmaxf(M, pwml[(w * RP + r) * 2]);
+        const float Mu = M == -INFINITY ? 0.f : M;
+        float wgt[CONSUMERS], L = 0.f;
+#pragma unroll
+        for (int w = 0; w < CONSUMERS; ++w) {
+          wgt[w] = ex2(pwml[(w * RP + r) * 2] - Mu);
+          L += pwml[(w * RP + r) * 2 + 1] * wgt[w];
+        }
+        for (int c = lane; c < D / 4; c += 32) {
+          float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int w = 0; w < CONSUMERS; ++w) {
+            const float4 x = *reinterpret_cast<const float4*>(&pwo[(w * RP + r) * D + 4 * c]);
+            o.x += wgt[w] * x.x;
+            o.y += wgt[w] * x.y;
+            o.z += wgt[w] * x.z;
+            o.w += wgt[w] * x.w;
+          }
+          reinterpret_cast<float4*>(&p.ws_o[(part + r) * D])[c] = o;
+        }
+        if (lane == 0) *reinterpret_cast<float2*>(&p.ws_ml[(part + r) * 2]) = make_float2(M, L);
+      }
+    }
   }
 }
 
 // Merges the partials of every (b, hk, folded row) of a decode call by log-sum-exp.
 template <typename T, int D>
 __global__ void __launch_bounds__(256) split_combine_kernel(const Params p) {
-  // One block per (b, hk, folded row). Its partials sit in consecutive slots: split mode, (b Hkv + hk) nsplit + s
-  // for the nsplit_b splits of b; balanced mode, c + (b Hkv + hk) for the CTAs c whose tile runs meet the pair, found
-  // from the pair's first and last tile. Pass 1: every (max, sum) pair, the block max and the total sum, and each
-  // partial's weight in shared memory. Pass 2: threads split the head dim into float4 groups and the partials into
-  // interleaved sets, so every thread has its few loads in flight at once; the sets are summed in shared memory.
-  constexpr int CG = D / 4;          // float4 column groups
-  constexpr int PG = 256 / CG;       // partial sets
-  __shared__ float wts[MAX_PARTS];
-  __shared__ float red[PG][D];
-  __shared__ float s_red[8];
+  // One block per (b, hk); warp w merges folded rows w, w + 8, ..., lane l the float4 columns l, l + 32, ... Its
+  // partials sit in consecutive slots: split mode, (b Hkv + hk) nsplit + s for the nsplit_b splits of b; balanced
+  // mode, c + (b Hkv + hk) for the CTAs c whose tile runs meet the pair, found from the pair's first and last tile.
+  // After the grid dependency, each lane issues its (max, sum) load and the O loads of the first HELD partials at
+  // once (one round trip to L2); a longer span loads the rest once the weights are known.
+  constexpr int CW = D / 4;  // float4 columns of a row
+  constexpr int CL = (CW + 31) / 32;  // columns a lane
+  constexpr int HELD = 8;
   __shared__ int s_tiles[2][8];
-  const int r = blockIdx.x % p.rows;
-  const int bh = blockIdx.x / p.rows;
+  const int bh = blockIdx.x;
   const int b = bh / p.Hkv, hk = bh % p.Hkv;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int len = p.kv_len ? min(max(p.kv_len[b], 0), p.N) : p.N;
@@ -578,64 +615,85 @@ __global__ void __launch_bounds__(256) split_combine_kernel(const Params p) {
     first = bh * p.nsplit;
     nparts = max(1, (len + p.split - 1) / p.split);
   }
-  const size_t base = size_t(first) * p.rows;  // partial index of (first slot, row 0)
+  // the next kernel of the stream (the next decode, a programmatic dependent) may begin its launch now
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");  // the decode grid has completed and its writes are visible
-  // pass 1
-  float M = -INFINITY;
-  for (int q = tid; q < nparts; q += 256) {
-    const float m = __ldcg(&p.ws_ml[(base + size_t(q) * p.rows + r) * 2]);
-    wts[q] = m;
-    M = fmaxf(M, m);
-  }
+  const float2* ml = reinterpret_cast<const float2*>(p.ws_ml);
+  const float4* wo = reinterpret_cast<const float4*>(p.ws_o);
+  for (int r = w; r < p.rows; r += 8) {
+    const size_t base = size_t(first) * p.rows + r;  // partial index of (first slot, row r); slot stride p.rows
+    float4 xs[HELD][CL];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-  if (lane == 0) s_red[w] = M;
-  __syncthreads();
-  M = s_red[0];
+    for (int k = 0; k < HELD; ++k)
 #pragma unroll
-  for (int i = 1; i < 8; ++i) M = fmaxf(M, s_red[i]);
-  const float Mu = M == -INFINITY ? 0.f : M;
-  __syncthreads();
-  float L = 0.f;
-  for (int q = tid; q < nparts; q += 256) {
-    const float wq = ex2(wts[q] - Mu);
-    wts[q] = wq;
-    L += wq * __ldcg(&p.ws_ml[(base + size_t(q) * p.rows + r) * 2 + 1]);
-  }
+      for (int j = 0; j < CL; ++j) {
+        const int c = lane + 32 * j;
+        xs[k][j] = (k < nparts && c < CW) ? __ldcg(wo + (base + size_t(k) * p.rows) * CW + c)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    float2 mine = make_float2(-INFINITY, 0.f);  // lane q < 32: partial q's (max, sum)
+    if (lane < nparts) mine = __ldcg(ml + base + size_t(lane) * p.rows);
+    float M = mine.x;
+    for (int q = lane + 32; q < nparts; q += 32) M = fmaxf(M, __ldcg(ml + base + size_t(q) * p.rows).x);
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-  if (lane == 0) s_red[w] = L;
-  __syncthreads();
-  L = 0.f;
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float Mu = M == -INFINITY ? 0.f : M;
+    float L = lane < nparts ? mine.y * ex2(mine.x - Mu) : 0.f;
+    for (int q = lane + 32; q < nparts; q += 32) {
+      const float2 x = __ldcg(ml + base + size_t(q) * p.rows);
+      L += x.y * ex2(x.x - Mu);
+    }
 #pragma unroll
-  for (int i = 0; i < 8; ++i) L += s_red[i];
-  // pass 2
-  const int cg = tid % CG, pg = tid / CG;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-  for (int q = pg; q < nparts; q += PG) {
-    const float wq = wts[q];
-    const float4 x = __ldcg(reinterpret_cast<const float4*>(p.ws_o + (base + size_t(q) * p.rows + r) * D) + cg);
-    acc.x += wq * x.x;
-    acc.y += wq * x.y;
-    acc.z += wq * x.z;
-    acc.w += wq * x.w;
-  }
-  *reinterpret_cast<float4*>(&red[pg][cg * 4]) = acc;
-  __syncthreads();
-  if (tid < D) {
-    float o = 0.f;
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    float4 acc[CL];
 #pragma unroll
-    for (int i = 0; i < PG; ++i) o += red[i][tid];
-    const float val = L > 0.f ? o / L : 0.f;
+    for (int j = 0; j < CL; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < HELD; ++k) {
+      const float mk = __shfl_sync(0xffffffffu, mine.x, k);
+      if (k < nparts) {
+        const float wk = ex2(mk - Mu);
+#pragma unroll
+        for (int j = 0; j < CL; ++j) {
+          acc[j].x += wk * xs[k][j].x;
+          acc[j].y += wk * xs[k][j].y;
+          acc[j].z += wk * xs[k][j].z;
+          acc[j].w += wk * xs[k][j].w;
+        }
+      }
+    }
+    for (int q = HELD; q < nparts; ++q) {
+      const float wq = ex2(__ldcg(ml + base + size_t(q) * p.rows).x - Mu);
+#pragma unroll
+      for (int j = 0; j < CL; ++j) {
+        const int c = lane + 32 * j;
+        if (c < CW) {
+          const float4 x = __ldcg(wo + (base + size_t(q) * p.rows) * CW + c);
+          acc[j].x += wq * x.x;
+          acc[j].y += wq * x.y;
+          acc[j].z += wq * x.z;
+          acc[j].w += wq * x.w;
+        }
+      }
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
     const int g = r / p.T, t = r % p.T, h = hk * p.G + g;
-    if (p.emit) {
-      const size_t ro = (size_t(b) * p.Hq + h) * p.T + t;
-      p.part_o[ro * D + tid] = val;
-      if (tid == 0) p.part_lse[ro] = L > 0.f ? (M + __log2f(L)) * 0.69314718055994531f : -INFINITY;
-    } else {
-      reinterpret_cast<T*>(p.o)[b * p.o_st[0] + int64_t(h) * p.o_st[1] + int64_t(t) * p.o_st[2] + tid] =
-          from_f<T>(val);
+#pragma unroll
+    for (int j = 0; j < CL; ++j) {
+      const int c = lane + 32 * j;
+      if (c >= CW) continue;
+      const float4 v = make_float4(acc[j].x * inv, acc[j].y * inv, acc[j].z * inv, acc[j].w * inv);
+      if (p.emit) {
+        const size_t ro = (size_t(b) * p.Hq + h) * p.T + t;
+        reinterpret_cast<float4*>(p.part_o + ro * D)[c] = v;
+        if (c == 0) p.part_lse[ro] = L > 0.f ? (M + __log2f(L)) * 0.69314718055994531f : -INFINITY;
+      } else {
+        T* dst = reinterpret_cast<T*>(p.o) + b * p.o_st[0] + int64_t(h) * p.o_st[1] + int64_t(t) * p.o_st[2] + 4 * c;
+        dst[0] = from_f<T>(v.x);
+        dst[1] = from_f<T>(v.y);
+        dst[2] = from_f<T>(v.z);
+        dst[3] = from_f<T>(v.w);
+      }
     }
   }
 }

@@ -144,12 +144,25 @@ static int launch_t(const CUtensorMap& qm, const CUtensorMap& km, const CUtensor
     LB2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
     attr_dev = dev;
   }
-  kern<<<dim3(unsigned(p.grid)), C::THREADS, C::SMEM_BYTES, st>>>(qm, km, vm, p);
-  LB2_CUDA(cudaGetLastError());
+  cudaLaunchAttribute pdl[1];
+  pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  pdl[0].val.programmaticStreamSerializationAllowed = 1;
+  {
+    // a programmatic dependent of the stream's previous kernel: its launch and shared-memory set-up overlap that
+    // kernel's tail (the kernel waits on the grid dependency before its first global read)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(p.grid));
+    cfg.blockDim = dim3(C::THREADS);
+    cfg.dynamicSmemBytes = C::SMEM_BYTES;
+    cfg.stream = st;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    LB2_CUDA(cudaLaunchKernelEx(&cfg, kern, qm, km, vm, p));
+  }
   {
     // the split combine as a programmatic dependent: its launch overlaps the decode grid's tail
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(unsigned(int64_t(p.B) * p.Hkv * p.rows));
+    cfg.gridDim = dim3(unsigned(int64_t(p.B) * p.Hkv));
     cfg.blockDim = dim3(256);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = st;
