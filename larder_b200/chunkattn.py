@@ -6,10 +6,11 @@ The drop-in for the reference's chunkattn.py surface: `chunked`, `install`, `cal
 
 What changes on B200: the prefill kernel (lb2_attn_prefill, tcgen05 tensor cores with TMEM accumulators) is a
 fused flash-style kernel, so no [Hq, T, N] score buffer ever exists and query-row chunking is a scheduling choice,
-not a memory bound. `chunked()` still cuts the rows as the reference does (_bounds: `rows` apart, a short tail
-folded into the chunk before it) and still trims each chunk's keys to its causal horizon, but a chunk reads exactly
-the keys its last row can see (offset + c1), because a fused kernel has no bit-exactness reason to round the cut up
-to KEY_ALIGN or to the LOOPED floor; `_cut` keeps the reference's rounding for callers that use it to size things.
+not a memory bound. The reference cuts the rows only to bound MLX's score buffer (chunkattn.py:359-405: "same
+result as" one causal SDPA); `chunked()` here runs all T rows as ONE launch, whose row tiles are ordered heaviest
+first across the whole pass, so no chunk leaves its own partial last wave. Each row still reads the keys its causal
+horizon allows, in the same 64-key tiles and the same order as a chunk-by-chunk cut would, so the result is the
+same. `_bounds` and `_cut` keep the reference's arithmetic for callers that use them to size things.
 Few-row calls (decode, verify passes) go to the split-KV decode kernel instead (lb2_attn_decode).
 
 There is no stock fallback: an unsupported call (attention sinks, a quantised cache, an additive mask, fp32 on the
@@ -46,29 +47,18 @@ def _bounds(T, rows, min_rows):
 
 
 def chunked(q, k, v, scale, rows, min_rows, floor=0, mask=None, fused=False, gate=None):
-    """Causal SDPA of q's T rows, the last T of k/v's N positions (row r sees keys 0 .. N - T + r), cut into row
-    chunks of `rows` (chunkattn.py:359-423). `mask`: a bool [..., T, N] array instead of the causal rule; each chunk
-    takes its rows of it. `fused` is accepted for the reference's signature (every chunk here is fused). `gate`
-    ([B, Hq, T, D] view, optional): the output is multiplied by sigmoid(gate) inside the kernel. Returns
-    [B, Hq, T, D] in q's dtype."""
+    """Causal SDPA of q's T rows, the last T of k/v's N positions (row r sees keys 0 .. N - T + r), the result of
+    the reference's row-chunked pass (chunkattn.py:359-423) in one launch. `rows`, `min_rows` and `floor` are the
+    reference's chunking knobs (kept for its signature; here they change no result and no work). `mask`: a bool
+    [..., T, N] array instead of the causal rule. `fused` is accepted for the reference's signature (the kernel is
+    fused). `gate` ([B, Hq, T, D] view, optional): the output is multiplied by sigmoid(gate) inside the kernel.
+    Returns [B, Hq, T, D] in q's dtype."""
     B, Hq, T, D = q.shape
     N = k.shape[2]
-    offset = N - T
     out = torch.empty((B, Hq, T, D), dtype=q.dtype, device=q.device)
-    for c0, c1 in zip(_bounds(T, rows, min_rows), _bounds(T, rows, min_rows)[1:]):
-        g = None if gate is None else gate[:, :, c0:c1]
-        if mask is None:
-            nk = min(N, max(0, offset + c1))  # the chunk's causal horizon, exactly
-            if nk == 0:
-                out[:, :, c0:c1].zero_()
-                continue
-            ops.attn_prefill(q[:, :, c0:c1], k[:, :, :nk], v[:, :, :nk], scale, "causal", gate=g,
-                             out=out[:, :, c0:c1])
-        else:
-            nk = _cut(offset + c1, N, floor) if floor else N
-            m = mask.reshape(T, N)[c0:c1, :nk]
-            ops.attn_prefill(q[:, :, c0:c1], k[:, :, :nk], v[:, :, :nk], scale, m, gate=g, out=out[:, :, c0:c1])
-    return out
+    if mask is None:
+        return ops.attn_prefill(q, k, v, scale, "causal", gate=gate, out=out)
+    return ops.attn_prefill(q, k, v, scale, mask.reshape(T, N), gate=gate, out=out)
 
 
 def _arr_mask(mask, T, N):

@@ -72,14 +72,15 @@ def test_wrapper_refuses_what_it_cannot_serve(spy):
     assert spy.calls == []
 
 
-def test_chunked_cuts_each_chunk_at_its_causal_horizon(spy):
+def test_chunked_runs_all_rows_in_one_launch(spy):
+    """The fused kernel keeps no score buffer, so the wide cut's row chunks become one launch over all T rows and
+    all N keys (bottom-right causal), whatever `rows`, `min_rows` and `floor` say."""
     B, Hq, Hkv, D, T, N = 1, 16, 2, 256, 300, 1000
     q = torch.zeros(B, Hq, T, D, dtype=torch.bfloat16)
     k = torch.zeros(B, Hkv, N, D, dtype=torch.bfloat16)
-    chunkattn.chunked(q, k, k, 0.0625, 128, 128)
-    cuts = [(c[1][0].shape[2], c[1][1].shape[2]) for c in spy.calls]
-    # chunks [0,128) and [128,300) (tail folded); keys up to N - T + c1
-    assert cuts == [(128, 828), (172, 1000)]
+    chunkattn.chunked(q, k, k, 0.0625, 128, 128, floor=512)
+    calls = [(c[0], c[1][0].shape[2], c[1][1].shape[2], c[1][4]) for c in spy.calls]
+    assert calls == [("prefill", T, N, "causal")]
 
 
 def test_install_rebinds_module_attribute():
