@@ -3,15 +3,19 @@
 // One CTA computes one 128-row query tile of one head: O = softmax(scale Q K^T + mask) V [* sigmoid(gate)].
 // Warp roles (320 threads):
 //   warps 0-7  softmax + epilogue: query row r = 32 (w % 4) + lane is TMEM lane r of S and O; warps w and w + 4
-//              split the row's columns, exchanging the row max through shared memory. They read S with
-//              tcgen05.ld, keep the running max / sum in base 2, write P (bf16/f16) into a double-buffered
-//              128-byte swizzled shared tile, rescale the O row in TMEM only when the max grew by more than 2^8,
-//              and finally normalise O, apply the optional sigmoid gate and store the row.
-//   warp 8     TMA producer: Q once, then K and V tiles (128-byte swizzled boxes of 64 head-dim elements) into
-//              two-stage rings.
-//   warp 9     MMA issuer (one elected thread): S_j = Q K_j^T (SS operands, M=128, N=BN) into one of two S
-//              buffers in TMEM, then O += P_{j-1} V_{j-1} (M=128, N=D, V read MN-major), so S_{j+1} runs while
-//              the softmax warps work on S_j. Completion is signalled with tcgen05.commit on mbarriers.
+//              split the row's columns, exchanging the row max through shared memory. They read S_j with
+//              tcgen05.ld, keep the running max / sum in base 2, write P_j (bf16/f16, key pairs packed a column) into
+//              TMEM buffer j % 2 once PV_{j-2} has finished reading it, rescale the O row in TMEM only when the max
+//              grew by more than 2^8, and finally normalise O, apply the optional sigmoid gate and store the row.
+//   warp 8     TMA producers: lane 0 loads Q once, then K tiles into a three-stage ring; lane 1 loads V tiles into
+//              a two-stage ring (128-byte swizzled boxes of 64 head-dim elements). Each ring refills as soon as its
+//              own stage frees.
+//   warp 9     MMA issuer (one elected thread): S_j = Q K_j^T (SS operands, M=128, N=BN) into S buffer j % 2, and
+//              O += P_j V_j (A = P_j from TMEM, B = V_j MN-major from shared memory, M=128, N=D). It polls the
+//              barriers and issues whichever is ready: S_{j+2} as soon as K_{j+2} has landed and the softmax warps
+//              have loaded S_j, so the next scores are computed while the softmax of tile j still runs; PV_j as soon
+//              as P_j and V_j are in. Completion is signalled with tcgen05.commit on mbarriers. S and P have separate
+//              TMEM buffers, so no MMA writes TMEM that an earlier one may still be reading.
 // Causal is bottom-right (row t sees keys 0 .. N - T + t, chunkattn.py:359-365); a tile reads only the KV tiles
 // up to its last row's limit, and only tiles crossing a row's limit are masked element by element. Every mbarrier
 // wait is time-bounded; a wait that gives up sets the CTA's abort flag, every role drains what it issued, TMEM is
@@ -35,19 +39,20 @@ struct Cfg {
   static constexpr int BN = D == 256 ? 64 : 128;
   static constexpr int QBYTES = BM * D * 2;
   static constexpr int KBYTES = BN * D * 2;  // one K tile; a V tile is the same size
-  static constexpr int PBYTES = BM * BN * 2;
-  static constexpr int STAGES = 2;
+  static constexpr int KSTAGES = 3;  // K_{j+3} loads while S_j.. S_{j+2} are still ahead of it
+  static constexpr int VSTAGES = 2;
+  static constexpr int SBUF = 2;  // S buffers in TMEM (fp32), and as many P buffers (16-bit, BN / 2 columns each)
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_OFF + QBYTES;
-  static constexpr int V_OFF = K_OFF + STAGES * KBYTES;
-  static constexpr int P_OFF = V_OFF + STAGES * KBYTES;
-  static constexpr int BAR_OFF = P_OFF + 2 * PBYTES;  // P double-buffered: P_j is written while PV_{j-1} runs
+  static constexpr int V_OFF = K_OFF + KSTAGES * KBYTES;
+  static constexpr int BAR_OFF = V_OFF + VSTAGES * KBYTES;
   // at least ~120 KB so that one CTA holds an SM (its TMEM allocation is all 512 columns)
   static constexpr int RED_OFF = BAR_OFF + 256;  // [2 halves][128 rows] fp32: a row's partial max / sum
   static constexpr int SMEM_RAW = RED_OFF + 2 * BM * 4;
   static constexpr int SMEM_BYTES = (SMEM_RAW < 120 * 1024 ? 120 * 1024 : SMEM_RAW) + 1024;
-  static constexpr int S_COL = 0;       // S buffers at columns [0, BN) and [BN, 2 BN)
-  static constexpr int O_COL = 2 * BN;  // O at [2 BN, 2 BN + D)
+  static constexpr int S_COL = 0;                // S buffers at columns [b BN, (b + 1) BN)
+  static constexpr int P_COL = SBUF * BN;        // P buffers at [P_COL + b BN / 2, ...)
+  static constexpr int O_COL = P_COL + SBUF * BN / 2;  // O at [3 BN, 3 BN + D)
   static_assert(O_COL + D <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
@@ -93,6 +98,14 @@ __device__ __forceinline__ void umma_ss(uint32_t tmem_d, uint64_t a, uint64_t b,
       "l"(a), "l"(b), "r"(idesc), "r"(acc));
 }
 
+// D (TMEM) [+]= A (TMEM, M rows x 16 elements a column pair) x B (shared memory descriptor).
+__device__ __forceinline__ void umma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc));
+}
+
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
@@ -125,6 +138,15 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -153,6 +175,7 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_kernel(const __grid_constant_
                                                            const Params p) {
   using C = Cfg<D>;
   constexpr int BN = C::BN;
+  constexpr int KS = C::KSTAGES, VS = C::VSTAGES, SB = C::SBUF;
   constexpr int AB = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
   constexpr uint32_t IDESC_S = idesc_f16(AB, 0, 0, BM, BN);
   constexpr uint32_t IDESC_PV = idesc_f16(AB, 0, 1, BM, D);
@@ -168,34 +191,37 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_kernel(const __grid_constant_
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::BAR_OFF);
-  uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [2]
-  uint64_t* s_free = bars + 11;  // [2]
-  uint64_t* p_full = bars + 13;  // [2] P_j written into buffer j & 1
-  uint64_t* o_done = bars + 15;  // [2] PV_j complete, committed to o_done[j & 1]
-  uint64_t* drain = bars + 17;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 19);
+  uint64_t* q_full = bars;               // [1]
+  uint64_t* k_full = q_full + 1;         // [KS]
+  uint64_t* k_empty = k_full + KS;       // [KS]
+  uint64_t* v_full = k_empty + KS;       // [VS]
+  uint64_t* v_empty = v_full + VS;       // [VS]
+  uint64_t* s_full = v_empty + VS;       // [SB] S_j complete in S buffer j % SB
+  uint64_t* s_free = s_full + SB;        // [SB] the softmax warps have loaded S_j
+  uint64_t* p_full = s_free + SB;        // [SB] P_j written into P buffer j % SB
+  uint64_t* o_done = p_full + SB;        // [SB] PV_j complete (P buffer j % SB read), committed to o_done[j % SB]
+  uint64_t* drain = o_done + SB;         // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(drain + 2);
+  static_assert((1 + 2 * KS + 2 * VS + 4 * SB + 1) * 8 + 16 <= 256, "barrier area");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < KS; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < VS; ++i) {
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < SB; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], SOFTMAX_WARPS * 32);
-    }
-    for (int i = 0; i < 2; ++i) {
       mbar_init(&p_full[i], SOFTMAX_WARPS * 32);
-      mbar_init(&o_done[i], 1);
     }
+    for (int i = 0; i < SB; ++i) mbar_init(&o_done[i], 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -211,95 +237,109 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_kernel(const __grid_constant_
   const uint32_t tmem = *tmem_slot;
 
   if (warp == PRODUCER_WARP) {
-    // ------------------------------------------------------------------------------------ TMA producer
-    if (lane == 0 && ntiles > 0) {
-      prefetch_tensormap(&qmap);
-      prefetch_tensormap(&kmap);
-      prefetch_tensormap(&vmap);
-      mbar_arrive_expect_tx(q_full, C::QBYTES);
+    // ------------------------------------------------------------------------------------ TMA producers
+    // Lane 0 loads Q, then K tiles; lane 1 loads V tiles. Each ring refills as soon as its own stage frees, so K_{j+2}
+    // (needed for S_{j+2}, which the MMA issuer runs before PV_j) never waits behind a V tile.
+    if (lane < 2 && ntiles > 0) {
+      if (lane == 0) {
+        prefetch_tensormap(&qmap);
+        prefetch_tensormap(&kmap);
+        mbar_arrive_expect_tx(q_full, C::QBYTES);
 #pragma unroll
-      for (int db = 0; db < D / 64; ++db)
-        tma_load_4d(sm + C::Q_OFF + db * BM * 128, &qmap, db * 64, r0, h, b, q_full);
+        for (int db = 0; db < D / 64; ++db)
+          tma_load_4d(sm + C::Q_OFF + db * BM * 128, &qmap, db * 64, r0, h, b, q_full);
+      } else {
+        prefetch_tensormap(&vmap);
+      }
+      const int NS = lane == 0 ? KS : VS;
+      uint64_t* fullb = lane == 0 ? k_full : v_full;
+      uint64_t* emptyb = lane == 0 ? k_empty : v_empty;
+      const CUtensorMap* map = lane == 0 ? &kmap : &vmap;
+      const int off = lane == 0 ? C::K_OFF : C::V_OFF;
       int issued = 0;
       for (int j = 0; j < ntiles && !*abort_flag; ++j) {
-        const int st = j & 1;
-        if (j >= 2 && !mbar_wait(&k_empty[st], ((j >> 1) - 1) & 1, 11)) {
+        const int st = j % NS;
+        if (j >= NS && !mbar_wait(&emptyb[st], ((j / NS) - 1) & 1, 11 + lane)) {
           *abort_flag = 1;
           break;
         }
-        mbar_arrive_expect_tx(&k_full[st], C::KBYTES);
+        mbar_arrive_expect_tx(&fullb[st], C::KBYTES);
 #pragma unroll
         for (int db = 0; db < D / 64; ++db)
-          tma_load_4d(sm + C::K_OFF + st * C::KBYTES + db * BN * 128, &kmap, db * 64, j * BN, hk, b, &k_full[st]);
-        if (j >= 2 && !mbar_wait(&v_empty[st], ((j >> 1) - 1) & 1, 12)) {
-          *abort_flag = 1;
-          issued = 2 * j + 1;
-          break;
-        }
-        mbar_arrive_expect_tx(&v_full[st], C::KBYTES);
-#pragma unroll
-        for (int db = 0; db < D / 64; ++db)
-          tma_load_4d(sm + C::V_OFF + st * C::KBYTES + db * BN * 128, &vmap, db * 64, j * BN, hk, b, &v_full[st]);
-        issued = 2 * j + 2;
+          tma_load_4d(sm + off + st * C::KBYTES + db * BN * 128, map, db * 64, j * BN, hk, b, &fullb[st]);
+        issued = j + 1;
       }
-      // Drain: every load issued has landed before the CTA may finish (already true on the normal path).
-      mbar_wait(q_full, 0, 13);
-      for (int u = max(0, issued - 4); u < issued; ++u) {
-        const int j = u >> 1;
-        mbar_wait((u & 1) ? &v_full[j & 1] : &k_full[j & 1], (j >> 1) & 1, 14);
-      }
+      // Drain: every load this lane issued has landed before the CTA may finish (already true normally).
+      if (lane == 0) mbar_wait(q_full, 0, 13);
+      for (int j = max(0, issued - NS); j < issued; ++j) mbar_wait(&fullb[j % NS], (j / NS) & 1, 14);
     }
   } else if (warp == MMA_WARP) {
     // ------------------------------------------------------------------------------------ MMA issuer
     if (ntiles > 0) {
       const bool leader = elect_one();
       const uint32_t q_addr = smem_u32(sm + C::Q_OFF);
-      const uint32_t p_addr = smem_u32(sm + C::P_OFF);
       bool ok = !leader || mbar_wait(q_full, 0, 21);
-      int pv_done = 0;
-      auto issue_pv = [&](int i) -> bool {
-        const int st = i & 1;
-        if (!mbar_wait(&v_full[st], (i >> 1) & 1, 22)) return false;
-        if (!mbar_wait(&p_full[st], (i >> 1) & 1, 23)) return false;
+      // S_j = Q K_j^T into S buffer j % SB (K_j landed; the softmax warps have loaded S_{j-SB}).
+      auto issue_s = [&](int j) {
+        const int st = j % KS, sb = j % SB;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sm + C::K_OFF + st * C::KBYTES);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t a = sdesc(q_addr + (kk >> 2) * BM * 128 + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sdesc(k_addr + (kk >> 2) * BN * 128 + (kk & 3) * 32, 16, 1024);
+          umma_ss(tmem + C::S_COL + sb * BN, a, bd, IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[sb]);
+        umma_commit(&k_empty[st]);
+      };
+      // O += P_i V_i: A = P_i from TMEM (16 keys = 8 columns a k-step), B = V_i MN-major.
+      auto issue_pv = [&](int i) {
+        const int st = i % VS, sb = i % SB;
         tc_fence_after();
         const uint32_t v_addr = smem_u32(sm + C::V_OFF + st * C::KBYTES);
-        const uint32_t pb = p_addr + st * C::PBYTES;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t a = sdesc(pb + (kk >> 2) * BM * 128 + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = sdesc(v_addr + kk * 16 * 128, BN * 128, 1024);
-          umma_ss(tmem + C::O_COL, a, bd, IDESC_PV, (i > 0 || kk > 0) ? 1u : 0u);
+          umma_ts(tmem + C::O_COL, tmem + C::P_COL + sb * (BN / 2) + kk * 8, bd, IDESC_PV, (i > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&o_done[st]);
+        umma_commit(&o_done[i % SB]);
         umma_commit(&v_empty[st]);
-        return true;
       };
       if (leader) {
-        for (int j = 0; j < ntiles && ok; ++j) {
-          const int st = j & 1;
-          if (!mbar_wait(&k_full[st], (j >> 1) & 1, 24) || (j >= 2 && !mbar_wait(&s_free[st], ((j >> 1) - 1) & 1, 25))) {
-            ok = false;
-            break;
+        // Issue whichever of S_js and PV_jp is ready first (PV first when both are), polling the barriers without
+        // blocking: a late K tile then never holds back a PV whose P and V are in, nor a late V tile the next S.
+        // PV_jp needs S_jp issued. The whole loop is time-bounded.
+        int js = 0, jp = 0;
+        uint64_t t0 = 0;
+        for (uint32_t it = 1; ok && jp < ntiles; ++it) {
+          if (jp < js && mbar_test_wait(&v_full[jp % VS], (jp / VS) & 1) &&
+              mbar_test_wait(&p_full[jp % SB], (jp / SB) & 1)) {
+            issue_pv(jp++);
+            t0 = 0;
+            continue;
           }
-          tc_fence_after();
-          const uint32_t k_addr = smem_u32(sm + C::K_OFF + st * C::KBYTES);
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint64_t a = sdesc(q_addr + (kk >> 2) * BM * 128 + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd = sdesc(k_addr + (kk >> 2) * BN * 128 + (kk & 3) * 32, 16, 1024);
-            umma_ss(tmem + C::S_COL + st * BN, a, bd, IDESC_S, kk > 0 ? 1u : 0u);
+          if (js < ntiles && mbar_test_wait(&k_full[js % KS], (js / KS) & 1) &&
+              (js < SB || mbar_test_wait(&s_free[js % SB], ((js / SB) - 1) & 1))) {
+            issue_s(js++);
+            t0 = 0;
+            continue;
           }
-          umma_commit(&s_full[st]);
-          umma_commit(&k_empty[st]);
-          if (j >= 1) {
-            if (!issue_pv(j - 1)) {
+          if ((it & 255) == 0) {
+            if (*abort_flag) {
               ok = false;
               break;
             }
-            pv_done = j;
+            const uint64_t now = globaltimer_ns();
+            if (t0 == 0) {
+              t0 = now;
+            } else if (now - t0 > kWaitNs) {
+              report_timeout(27);
+              ok = false;
+              break;
+            }
           }
         }
-        if (ok && pv_done < ntiles) ok = issue_pv(ntiles - 1);
         if (!ok) *abort_flag = 1;
         // Drain: everything this thread issued has completed before TMEM may be released.
         umma_commit(drain);
@@ -320,23 +360,23 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_kernel(const __grid_constant_
     const int lim = p.mask_kind == LB2_MASK_CAUSAL ? p.N - p.T + row : p.N - 1;
     const uint8_t* mrow = (p.mask_kind == LB2_MASK_ARRAY && row < p.T) ? p.mask + int64_t(row) * p.m_st[0] : nullptr;
     float m_run = -INFINITY, l_run = 0.f;
-    uint8_t* prow = sm + C::P_OFF;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
-      const int st = j & 1;
+      const int sb = j % SB;
+      const uint32_t scol = C::S_COL + sb * BN;
       // A failed wait never leaves a warp alone at a barrier: the decision to stop is made warp-uniform before
       // the warp-collective TMEM loads and pair-uniform at the max exchange (bar.red.and), where both warps of a
       // row pair leave the loop together.
-      bool okj = ok && !*abort_flag && mbar_wait(&s_full[st], (j >> 1) & 1, 31);
+      bool okj = ok && !*abort_flag && mbar_wait(&s_full[sb], (j / SB) & 1, 31);
       okj = __all_sync(0xffffffffu, okj);
       float s[HC];
       if (okj) {
         tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < HC; c += 32) tmem_ld32(lane_base + C::S_COL + st * BN + hf * HC + c, s + c);
+        for (int c = 0; c < HC; c += 32) tmem_ld32(lane_base + scol + hf * HC + c, s + c);
         tmem_wait_ld();
         tc_fence_before();
-        mbar_arrive(&s_free[st]);
+        mbar_arrive(&s_free[sb]);
       } else {
 #pragma unroll
         for (int c = 0; c < HC; ++c) s[c] = -INFINITY;
@@ -368,7 +408,8 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_kernel(const __grid_constant_
           : "r"(uint32_t(okj)), "r"(pair_bar)
           : "memory");
       tmax = fmaxf(tmax, red[(1 - hf) * BM + r]);
-      asm volatile("bar.sync %0, 64;" ::"r"(pair_bar));  // both read before the next tile rewrites
+      // both read before the next tile rewrites red
+      asm volatile("bar.sync %0, 64;" ::"r"(pair_bar));
       if (!pair_ok) {
         ok = false;
         break;
@@ -380,7 +421,7 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_kernel(const __grid_constant_
       const bool move = tmax2 > m_run + 8.f;
       const float factor = move ? ex2f(m_run - tmax2) : 1.f;
       if (__any_sync(0xffffffffu, move && j > 0 && l_run > 0.f)) {
-        if (!mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, 32)) ok = false;
+        if (!mbar_wait(&o_done[(j - 1) % SB], ((j - 1) / SB) & 1, 32)) ok = false;
         tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < HD; c += 32) {
@@ -397,35 +438,30 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_kernel(const __grid_constant_
         l_run *= factor;
         m_run = tmax2;
       }
-      // P buffer j & 1 was last read by PV_{j-2}.
-      if (j >= 2 && !mbar_wait(&o_done[j & 1], ((j >> 1) - 1) & 1, 34)) ok = false;
+      // P_j (16-bit, key pairs packed a 32-bit column) into P buffer j % SB, this half's HC keys at columns
+      // hf HC / 2 ...; the buffer was last read by PV_{j-SB}.
+      if (j >= SB && !mbar_wait(&o_done[sb], ((j / SB) - 1) & 1, 34)) ok = false;
+      tc_fence_after();
       const float nm = m_run == -INFINITY ? 0.f : -m_run;
-      uint8_t* pbuf = prow + (j & 1) * C::PBYTES;
       float ls4[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[HC / 2];
 #pragma unroll
-      for (int c = 0; c < HC; c += 8) {
-        float e[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          e[u] = ex2f(fmaf(s[c + u], p.scale_log2, nm));
-          ls4[u & 3] += e[u];
-        }
-        uint4 pk;
-        pk.x = pack2<T>(e[0], e[1]);
-        pk.y = pack2<T>(e[2], e[3]);
-        pk.z = pack2<T>(e[4], e[5]);
-        pk.w = pack2<T>(e[6], e[7]);
-        const int cc = hf * HC + c;
-        const int box = cc >> 6, ch = (cc & 63) >> 3;
-        *reinterpret_cast<uint4*>(pbuf + box * BM * 128 + r * 128 + ((ch ^ (r & 7)) << 4)) = pk;
+      for (int c = 0; c < HC; c += 2) {
+        const float e0 = ex2f(fmaf(s[c], p.scale_log2, nm));
+        const float e1 = ex2f(fmaf(s[c + 1], p.scale_log2, nm));
+        ls4[c & 3] += e0;
+        ls4[(c + 1) & 3] += e1;
+        pk[c / 2] = pack2<T>(e0, e1);
       }
+#pragma unroll
+      for (int c = 0; c < HC / 2; c += 16) tmem_st16(lane_base + C::P_COL + sb * (BN / 2) + hf * (HC / 2) + c, pk + c);
       l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
-      fence_proxy_async_shared();
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_full[j & 1]);
+      mbar_arrive(&p_full[sb]);
     }
     if (ok && ntiles > 0) {
-      if (!mbar_wait(&o_done[(ntiles - 1) & 1], ((ntiles - 1) >> 1) & 1, 33)) ok = false;
+      if (!mbar_wait(&o_done[(ntiles - 1) % SB], ((ntiles - 1) / SB) & 1, 33)) ok = false;
       tc_fence_after();
     }
     // ---------------------------------------------------------------------------------- epilogue

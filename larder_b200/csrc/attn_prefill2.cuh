@@ -1,0 +1,535 @@
+// Prefill attention on a pair of CTAs (a 2-CTA cluster sharing each MMA: tcgen05 cta_group::2), head dim 256.
+//
+// The single-CTA kernel (attn_prefill.cuh) reads every K and V byte once per 128 query rows; at head dim 256 each
+// SM then streams 64 KB of K/V from L2 per 64-key tile and the L2 -> shared memory transfer, not the tensor cores,
+// sets the pace. Here the two CTAs of a cluster take 256 consecutive rows of one head (128 each) and one MMA
+// instruction covers both (M = 256): matrix A (Q for the scores, P for the output) stays split by rows, one half in
+// each CTA, and matrix B is split along N, so each CTA loads only HALF of every K tile (32 of its 64 keys) and HALF
+// of every V tile (128 of its 256 columns). Per SM that halves the K/V bytes per FLOP.
+//
+// Roles (320 threads a CTA, as in the single-CTA kernel):
+//   warps 0-7  softmax + epilogue on the CTA's own 128 rows (TMEM lane r = row r of its S, P and O); warps w and
+//              w + 4 split a row's 64 keys and exchange the row max through shared memory. After loading S_j and
+//              after writing P_j each warp arrives once on the LEADER CTA's s_free / p_full barrier.
+//   warp 8     TMA producers of the CTA's halves: lane 0 Q then K, lane 1 V. Loads complete on the leader's
+//              barriers (the 2-CTA form of the bulk tensor copy); the leader's lanes announce the byte counts of both
+//              halves. Each CTA refills a stage when its own k_empty / v_empty says the pair's MMA has finished it.
+//   warp 9     in the leader (rank 0) only, one elected thread issues every MMA of the pair: S_j = Q K_j^T into S
+//              buffer j % 2 and O += P_j V_j (A = P_j from TMEM), whichever is ready first, and commits completion to
+//              the barriers of both CTAs (one commit each). In both CTAs warp 9 allocates and frees the TMEM.
+// Causal is bottom-right as in the single-CTA kernel; the pair loops over the KV tiles its later rows need, the
+// earlier CTA's rows masking the last tile or two. Every wait is time-bounded; a wait that gives up sets the CTA's
+// abort flag, the roles drain what they issued, and both CTAs meet at a final cluster barrier before TMEM is freed.
+#pragma once
+
+#include "attn_prefill.cuh"
+
+namespace lb2 {
+namespace prefill2 {
+
+using prefill::BM;
+using prefill::MMA_WARP;
+using prefill::PRODUCER_WARP;
+using prefill::SOFTMAX_WARPS;
+using prefill::THREADS;
+using prefill::TMEM_COLS;
+using prefill::Params;
+
+template <int D>
+struct Cfg {
+  static constexpr int BN = 64;                 // keys a tile (the pair)
+  static constexpr int HN = BN / 2;             // K rows (keys) a CTA holds
+  static constexpr int HD = D / 2;              // V columns a CTA holds
+  static constexpr int QBYTES = BM * D * 2;
+  static constexpr int KHBYTES = HN * D * 2;    // a CTA's half of a K tile
+  static constexpr int VHBYTES = BN * HD * 2;   // a CTA's half of a V tile
+  static constexpr int KS = 4;
+  static constexpr int VS = 4;
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = Q_OFF + QBYTES;
+  static constexpr int V_OFF = K_OFF + KS * KHBYTES;
+  static constexpr int BAR_OFF = V_OFF + VS * VHBYTES;
+  static constexpr int RED_OFF = BAR_OFF + 256;  // [2 halves][128 rows] fp32
+  static constexpr int SMEM_BYTES = RED_OFF + 2 * BM * 4 + 1024;
+  static constexpr int PB = 3;                    // P buffers
+  static constexpr int S_COL = 0;                 // S buffers [b BN, (b + 1) BN), b < 2
+  static constexpr int P_COL = 2 * BN;            // P buffers [P_COL + b BN / 2, ...), b < PB
+  static constexpr int O_COL = P_COL + PB * BN / 2;  // O [O_COL, O_COL + D)
+  static_assert(O_COL + D <= TMEM_COLS, "TMEM budget");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+  static_assert(D == 256, "the pair kernel is built for head dim 256");
+};
+
+// ---------------------------------------------------------------------------------------------- cluster helpers
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory word in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrive on an mbarrier anywhere in the cluster. The arriving warps order their tcgen05 loads / stores before it
+// with tcgen05.fence::before_thread_sync, the MMA thread orders its MMAs after the wait with
+// tcgen05.fence::after_thread_sync.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_test_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int where) {
+  uint64_t t0 = 0;
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_test_wait_cluster(bar, parity)) return true;
+    if ((i & 1023) == 0) {
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitNs) {
+        report_timeout(where);
+        return false;
+      }
+    }
+  }
+}
+
+// 4-D tiled TMA load into this CTA's shared memory, completing on the leader CTA's copy of the mbarrier (the 2-CTA
+// form of the copy, whose barrier may sit in either CTA of the pair).
+__device__ __forceinline__ void tma_load_4d_pair(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                                 uint64_t* bar) {
+  const uint32_t b = mapa(smem_u32(bar), 0);
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(b), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma2_ss(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0u));
+}
+
+__device__ __forceinline__ void umma2_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}" ::"r"(
+          tmem_d),
+      "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc), "r"(0u));
+}
+
+// Completion of this thread's prior pair MMAs, signalled on the barrier at this shared-memory offset in both CTAs
+// (one commit a CTA).
+__device__ __forceinline__ void umma2_commit_both(uint64_t* bar) {
+  const uint32_t local = smem_u32(bar);
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(local) : "memory");
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mapa(local, 1))
+               : "memory");
+}
+
+// Number of BN-key tiles the pair of row tiles mt2 (rows [256 mt2, 256 mt2 + 256)) reads.
+template <int D>
+__device__ __forceinline__ int kv_tiles2(const Params& p, int mt2) {
+  constexpr int BN = Cfg<D>::BN;
+  int last = p.N;
+  if (p.mask_kind == LB2_MASK_CAUSAL) {
+    const int rmax = min(p.T, (mt2 + 1) * 2 * BM) - 1;
+    last = min(p.N, p.N - p.T + rmax + 1);
+  }
+  return last <= 0 ? 0 : (last + BN - 1) / BN;
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                            const __grid_constant__ CUtensorMap kmap,
+                                                            const __grid_constant__ CUtensorMap vmap,
+                                                            const Params p) {
+  using C = Cfg<D>;
+  constexpr int BN = C::BN, HN = C::HN, HD = C::HD;
+  constexpr int KS = C::KS, VS = C::VS;
+  constexpr int AB = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+  constexpr uint32_t IDESC_S = prefill::idesc_f16(AB, 0, 0, 2 * BM, BN);
+  constexpr uint32_t IDESC_PV = prefill::idesc_f16(AB, 0, 1, 2 * BM, D);
+
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  // Heaviest pairs first; heads vary fastest so that neighbouring clusters share their KV head's tiles in L2.
+  const int pair = blockIdx.x >> 1;
+  const int bh = pair % (p.B * p.Hq);
+  const int mt2 = p.mtiles - 1 - pair / (p.B * p.Hq);
+  const int b = bh / p.Hq, h = bh % p.Hq, hk = h / p.G;
+  const int r0 = mt2 * 2 * BM + int(rank) * BM;  // this CTA's first row
+  const int ntiles = kv_tiles2<D>(p, mt2);
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::BAR_OFF);
+  uint64_t* q_full = bars;            // [1]  leader: both Q halves landed
+  uint64_t* k_full = q_full + 1;      // [KS] leader: both K halves of the stage landed
+  uint64_t* k_empty = k_full + KS;    // [KS] both CTAs: the pair's MMA has read the stage
+  uint64_t* v_full = k_empty + KS;    // [VS] leader
+  uint64_t* v_empty = v_full + VS;    // [VS] both CTAs
+  uint64_t* s_full = v_empty + VS;    // [2]  both CTAs: S_j complete in S buffer j % 2
+  uint64_t* s_free = s_full + 2;      // [2]  leader: all 16 softmax warps of the pair have loaded S_j
+  uint64_t* p_full = s_free + 2;      // [PB] leader: all 16 softmax warps have written P_j into P buffer j % PB
+  uint64_t* o_done = p_full + C::PB;  // [PB] both CTAs: PV_j complete (P buffer j % PB read)
+  uint64_t* drain = o_done + C::PB;   // [1]  leader
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(drain + 2);
+  static_assert((1 + 2 * KS + 2 * VS + 4 + 2 * C::PB + 1) * 8 + 16 <= 256, "barrier area");
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < KS; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < VS; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 2 * SOFTMAX_WARPS);
+    }
+    for (int i = 0; i < C::PB; ++i) {
+      mbar_init(&p_full[i], 2 * SOFTMAX_WARPS);
+      mbar_init(&o_done[i], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == MMA_WARP) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  prefill::tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers are initialised before any remote arrive or load completion
+  prefill::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == PRODUCER_WARP) {
+    // ------------------------------------------------------------------------------------ TMA producers
+    if (lane < 2 && ntiles > 0) {
+      if (lane == 0) {
+        prefetch_tensormap(&qmap);
+        prefetch_tensormap(&kmap);
+        if (leader) mbar_arrive_expect_tx(q_full, 2 * C::QBYTES);
+#pragma unroll
+        for (int db = 0; db < D / 64; ++db)
+          tma_load_4d_pair(sm + C::Q_OFF + db * BM * 128, &qmap, db * 64, r0, h, b, q_full);
+      } else {
+        prefetch_tensormap(&vmap);
+      }
+      const int NS = lane == 0 ? KS : VS;
+      const int bytes = lane == 0 ? C::KHBYTES : C::VHBYTES;
+      uint64_t* fullb = lane == 0 ? k_full : v_full;
+      uint64_t* emptyb = lane == 0 ? k_empty : v_empty;
+      int issued = 0;
+      for (int j = 0; j < ntiles && !*abort_flag; ++j) {
+        const int st = j % NS;
+        if (j >= NS && !mbar_wait(&emptyb[st], ((j / NS) - 1) & 1, 41 + lane)) {
+          *abort_flag = 1;
+          break;
+        }
+        if (leader) mbar_arrive_expect_tx(&fullb[st], 2 * bytes);
+        if (lane == 0) {  // keys [j BN + rank HN, + HN), all D columns: D / 64 boxes of (64, HN)
+          uint8_t* dst = sm + C::K_OFF + st * C::KHBYTES;
+#pragma unroll
+          for (int db = 0; db < D / 64; ++db)
+            tma_load_4d_pair(dst + db * HN * 128, &kmap, db * 64, j * BN + int(rank) * HN, hk, b, &fullb[st]);
+        } else {  // keys [j BN, + BN), columns [rank HD, + HD): HD / 64 boxes of (64, BN)
+          uint8_t* dst = sm + C::V_OFF + st * C::VHBYTES;
+#pragma unroll
+          for (int db = 0; db < HD / 64; ++db)
+            tma_load_4d_pair(dst + db * BN * 128, &vmap, int(rank) * HD + db * 64, j * BN, hk, b, &fullb[st]);
+        }
+        issued = j + 1;
+      }
+      // Drain (leader only: the loads of both CTAs complete on its barriers): everything issued has landed.
+      if (leader) {
+        if (lane == 0) mbar_wait(q_full, 0, 43);
+        for (int j = max(0, issued - NS); j < issued; ++j) mbar_wait(&fullb[j % NS], (j / NS) & 1, 44);
+      }
+    }
+  } else if (warp == MMA_WARP) {
+    // ------------------------------------------------------------------------------------ MMA issuer (leader)
+    if (leader && ntiles > 0) {
+      const bool elected = elect_one();
+      if (elected) {
+        const uint32_t q_addr = smem_u32(sm + C::Q_OFF);
+        bool ok = mbar_wait(q_full, 0, 51);
+        auto issue_s = [&](int j) {
+          const int st = j % KS, sb = j & 1;
+          prefill::tc_fence_after();
+          const uint32_t k_addr = smem_u32(sm + C::K_OFF + st * C::KHBYTES);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint64_t a = prefill::sdesc(q_addr + (kk >> 2) * BM * 128 + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = prefill::sdesc(k_addr + (kk >> 2) * HN * 128 + (kk & 3) * 32, 16, 1024);
+            umma2_ss(tmem + C::S_COL + sb * BN, a, bd, IDESC_S, kk > 0 ? 1u : 0u);
+          }
+          umma2_commit_both(&s_full[sb]);
+          umma2_commit_both(&k_empty[st]);
+        };
+        auto issue_pv = [&](int i) {
+          const int st = i % VS, pb = i % C::PB;
+          prefill::tc_fence_after();
+          const uint32_t v_addr = smem_u32(sm + C::V_OFF + st * C::VHBYTES);
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const uint64_t bd = prefill::sdesc(v_addr + kk * 16 * 128, BN * 128, 1024);
+            umma2_ts(tmem + C::O_COL, tmem + C::P_COL + pb * (BN / 2) + kk * 8, bd, IDESC_PV,
+                     (i > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma2_commit_both(&o_done[pb]);  // PV_i read P buffer i % PB
+          umma2_commit_both(&v_empty[st]);
+        };
+        int js = 0, jp = 0;
+        uint64_t t0 = 0;
+        for (uint32_t it = 1; ok && jp < ntiles; ++it) {
+          if (jp < js && mbar_test_wait_cluster(&v_full[jp % VS], (jp / VS) & 1) &&
+              mbar_test_wait_cluster(&p_full[jp % C::PB], (jp / C::PB) & 1)) {
+            issue_pv(jp++);
+            t0 = 0;
+            continue;
+          }
+          if (js < ntiles && mbar_test_wait_cluster(&k_full[js % KS], (js / KS) & 1) &&
+              (js < 2 || mbar_test_wait_cluster(&s_free[js & 1], ((js >> 1) - 1) & 1))) {
+            issue_s(js++);
+            t0 = 0;
+            continue;
+          }
+          if ((it & 255) == 0) {
+            if (*abort_flag) {
+              ok = false;
+              break;
+            }
+            const uint64_t now = globaltimer_ns();
+            if (t0 == 0) {
+              t0 = now;
+            } else if (now - t0 > kWaitNs) {
+              report_timeout(52);
+              ok = false;
+              break;
+            }
+          }
+        }
+        if (!ok) *abort_flag = 1;
+        asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         smem_u32(drain))
+                     : "memory");
+        mbar_wait(drain, 0, 53);
+      }
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------------------------------------------------------------ softmax warps
+    constexpr int HC = BN / 2;  // S columns a thread owns
+    constexpr int DH = D / 2;   // O columns a thread owns
+    const int r = 32 * (warp & 3) + lane;
+    const int hf = warp >> 2;
+    const int row = r0 + r;
+    const uint32_t lane_base = tmem + (uint32_t(32 * (warp & 3)) << 16);
+    const uint32_t pair_bar = 2 + (warp & 3);
+    float* red = reinterpret_cast<float*>(sm + C::RED_OFF);
+    const uint32_t s_free_l = mapa(smem_u32(s_free), 0), p_full_l = mapa(smem_u32(p_full), 0);
+    const int lim = p.mask_kind == LB2_MASK_CAUSAL ? p.N - p.T + row : p.N - 1;
+    const uint8_t* mrow = (p.mask_kind == LB2_MASK_ARRAY && row < p.T) ? p.mask + int64_t(row) * p.m_st[0] : nullptr;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int sb = j & 1;
+      bool okj = ok && !*abort_flag && mbar_wait(&s_full[sb], (j >> 1) & 1, 61);
+      okj = __all_sync(0xffffffffu, okj);
+      float s[HC];
+      if (okj) {
+        prefill::tc_fence_after();
+        prefill::tmem_ld32(lane_base + C::S_COL + sb * BN + hf * HC, s);
+        prefill::tmem_wait_ld();
+        prefill::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(s_free_l + 8u * sb);
+      } else {
+#pragma unroll
+        for (int c = 0; c < HC; ++c) s[c] = -INFINITY;
+      }
+      const int key0 = j * BN + hf * HC;
+      const bool full_tile = j * BN + BN - 1 <= lim && j * BN + BN <= p.N && !mrow;
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (full_tile) {
+#pragma unroll
+        for (int c = 0; c < HC; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
+      } else {
+#pragma unroll
+        for (int c = 0; c < HC; ++c) {
+          const int key = key0 + c;
+          bool vis = key <= lim && key < p.N;
+          if (mrow && vis) vis = mrow[int64_t(key) * p.m_st[1]] != 0;
+          s[c] = vis ? s[c] : -INFINITY;
+          mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
+        }
+      }
+      float tmax = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      // The running max moves only when a half's tile max exceeds it by more than 2^8 (rare after the first tile):
+      // one barrier tells both halves of the 32 rows whether any of them wants to (or a wait failed); only then do
+      // the halves swap their maxima.
+      const bool want = !okj || tmax * p.scale_log2 > m_run + 8.f;
+      uint32_t any_want;
+      asm volatile(
+          "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+          "bar.red.or.pred q, %2, 64, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+          : "=r"(any_want)
+          : "r"(uint32_t(want)), "r"(pair_bar)
+          : "memory");
+      bool move = false;
+      float tmax2 = 0.f;
+      if (any_want) {
+        red[hf * BM + r] = tmax;
+        uint32_t pair_ok;
+        asm volatile(
+            "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+            "bar.red.and.pred q, %2, 64, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+            : "=r"(pair_ok)
+            : "r"(uint32_t(okj)), "r"(pair_bar)
+            : "memory");
+        tmax = fmaxf(tmax, red[(1 - hf) * BM + r]);
+        asm volatile("bar.sync %0, 64;" ::"r"(pair_bar));
+        if (!pair_ok) {
+          ok = false;
+          break;
+        }
+        tmax2 = tmax * p.scale_log2;
+        move = tmax2 > m_run + 8.f;
+      }
+      const float factor = move ? prefill::ex2f(m_run - tmax2) : 1.f;
+      if (__any_sync(0xffffffffu, move && j > 0 && l_run > 0.f)) {
+        if (!mbar_wait(&o_done[(j - 1) % C::PB], ((j - 1) / C::PB) & 1, 62)) ok = false;
+        prefill::tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < DH; c += 32) {
+          float ov[32];
+          prefill::tmem_ld32(lane_base + C::O_COL + hf * DH + c, ov);
+          prefill::tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] *= factor;
+          prefill::tmem_st32(lane_base + C::O_COL + hf * DH + c, ov);
+        }
+        prefill::tmem_wait_st();
+      }
+      if (move) {
+        l_run *= factor;
+        m_run = tmax2;
+      }
+      // P_j into P buffer j % PB (last read by PV_{j-PB}): this half's HC keys at columns hf HC / 2 ...
+      const int pbuf = j % C::PB;
+      if (j >= C::PB && !mbar_wait(&o_done[pbuf], ((j / C::PB) - 1) & 1, 64)) ok = false;
+      prefill::tc_fence_after();
+      const float nm = m_run == -INFINITY ? 0.f : -m_run;
+      float ls4[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[HC / 2];
+#pragma unroll
+      for (int c = 0; c < HC; c += 2) {
+        const float e0 = prefill::ex2f(fmaf(s[c], p.scale_log2, nm));
+        const float e1 = prefill::ex2f(fmaf(s[c + 1], p.scale_log2, nm));
+        ls4[c & 3] += e0;
+        ls4[(c + 1) & 3] += e1;
+        pk[c / 2] = pack2<T>(e0, e1);
+      }
+      prefill::tmem_st16(lane_base + C::P_COL + pbuf * (BN / 2) + hf * (HC / 2), pk);
+      l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
+      prefill::tmem_wait_st();
+      prefill::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(p_full_l + 8u * pbuf);
+    }
+    if (ok && ntiles > 0) {
+      if (!mbar_wait(&o_done[(ntiles - 1) % C::PB], ((ntiles - 1) / C::PB) & 1, 63)) ok = false;
+      prefill::tc_fence_after();
+    }
+    // ---------------------------------------------------------------------------------- epilogue
+    ok = __all_sync(0xffffffffu, ok);
+    red[hf * BM + r] = l_run;
+    asm volatile("bar.sync %0, 64;" ::"r"(pair_bar));
+    const float l_tot = l_run + red[(1 - hf) * BM + r];
+    const bool have_o = ntiles > 0 && ok;
+    const bool store = row < p.T;
+    T* orow = reinterpret_cast<T*>(p.o) + b * p.o_st[0] + int64_t(h) * p.o_st[1] + int64_t(row) * p.o_st[2] + hf * DH;
+    const T* grow = p.gate ? reinterpret_cast<const T*>(p.gate) + b * p.g_st[0] + int64_t(h) * p.g_st[1] +
+                                 int64_t(row) * p.g_st[2] + hf * DH
+                           : nullptr;
+    const float inv = (have_o && l_tot > 0.f) ? 1.f / l_tot : 0.f;
+#pragma unroll 1
+    for (int c = 0; c < DH; c += 32) {
+      float ov[32];
+      if (have_o) {
+        prefill::tmem_ld32(lane_base + C::O_COL + hf * DH + c, ov);
+        prefill::tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) ov[e] = 0.f;
+      }
+      if (!store) continue;
+#pragma unroll
+      for (int e = 0; e < 32; e += 8) {
+        float x[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) x[u] = ov[e + u] * inv;
+        if (grow) {
+          const uint4 gv = *reinterpret_cast<const uint4*>(grow + c + e);
+          const T* gh = reinterpret_cast<const T*>(&gv);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const float z = to_f<T>(gh[u]);
+            x[u] = x[u] / (1.f + __expf(-z));
+          }
+        }
+        uint4 pk4;
+        pk4.x = pack2<T>(x[0], x[1]);
+        pk4.y = pack2<T>(x[2], x[3]);
+        pk4.z = pack2<T>(x[4], x[5]);
+        pk4.w = pack2<T>(x[6], x[7]);
+        *reinterpret_cast<uint4*>(orow + c + e) = pk4;
+      }
+    }
+  }
+
+  // The leader's MMAs read this CTA's shared memory and TMEM: neither CTA frees anything before both are done.
+  prefill::tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == MMA_WARP) {
+    prefill::tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+  }
+}
+
+}  // namespace prefill2
+}  // namespace lb2

@@ -8,6 +8,7 @@
 #include "attn_decode.cuh"
 #include "gdn_recurrent.cuh"
 #include "attn_prefill.cuh"
+#include "attn_prefill2.cuh"
 #include "gdn_chunked.cuh"
 #include "attn_f32.cuh"
 #include "kv_gather.cuh"
@@ -293,6 +294,38 @@ static int map4(CUtensorMap* m, const void* base, const int64_t* st, int B, int 
 
 }  // namespace prefill
 
+namespace prefill2 {
+
+// Clusters of two CTAs (one 256-row pair each), heaviest pairs first.
+template <typename T, int D>
+static int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const Params& p,
+                  cudaStream_t st) {
+  auto kern = fmha2_kernel<T, D>;
+  static int attr_dev = -1;
+  int dev = 0;
+  LB2_CUDA(cudaGetDevice(&dev));
+  if (attr_dev != dev) {
+    LB2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM_BYTES));
+    attr_dev = dev;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(2 * p.B * p.Hq * p.mtiles));
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = Cfg<D>::SMEM_BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  LB2_CUDA(cudaLaunchKernelEx(&cfg, kern, qm, km, vm, p));
+  return LB2_OK;
+}
+
+}  // namespace prefill2
+
 // ------------------------------------------------------------------------------------------------ fp32 attention
 
 namespace f32attn {
@@ -483,10 +516,12 @@ int lb2_attn_prefill(const void* q, const int64_t* q_st, const void* k, const in
   }
   LB2_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o) && (!gate || aligned16(gate)),
                 "prefill: tensors must be 16-byte aligned");
+  // Head dim 256 over more than one row tile runs on CTA pairs (each CTA loads half of every K and V tile).
+  const bool pair = D == 256 && T > prefill::BM;
   CUtensorMap qm, km, vm;
   const int BN = D == 256 ? prefill::Cfg<256>::BN : prefill::Cfg<128>::BN;
   int rc = prefill::map4(&qm, q, q_st, B, Hq, T, D, dtype, prefill::BM);
-  if (!rc) rc = prefill::map4(&km, k, k_st, B, Hkv, N, D, dtype, BN);
+  if (!rc) rc = prefill::map4(&km, k, k_st, B, Hkv, N, D, dtype, pair ? prefill2::Cfg<256>::HN : BN);
   if (!rc) rc = prefill::map4(&vm, v, v_st, B, Hkv, N, D, dtype, BN);
   if (rc) return rc;
   prefill::Params p{};
@@ -506,9 +541,12 @@ int lb2_attn_prefill(const void* q, const int64_t* q_st, const void* k, const in
   p.N = N;
   p.G = Hq / Hkv;
   p.mask_kind = mask_kind;
-  p.mtiles = (T + prefill::BM - 1) / prefill::BM;
+  p.mtiles = pair ? (T + 2 * prefill::BM - 1) / (2 * prefill::BM) : (T + prefill::BM - 1) / prefill::BM;
   p.scale_log2 = scale * 1.4426950408889634f;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (pair)
+    return dtype == LB2_BF16 ? prefill2::launch<__nv_bfloat16, 256>(qm, km, vm, p, st)
+                             : prefill2::launch<__half, 256>(qm, km, vm, p, st);
   if (dtype == LB2_BF16) {
     if (D == 64) return prefill::launch<__nv_bfloat16, 64>(qm, km, vm, p, st);
     if (D == 128) return prefill::launch<__nv_bfloat16, 128>(qm, km, vm, p, st);
