@@ -7,16 +7,19 @@
 // each CTA, and matrix B is split along N, so each CTA loads only HALF of every K tile (32 of its 64 keys) and HALF
 // of every V tile (128 of its 256 columns). Per SM that halves the K/V bytes per FLOP.
 //
-// Roles (320 threads a CTA, as in the single-CTA kernel):
-//   warps 0-7  softmax + epilogue on the CTA's own 128 rows (TMEM lane r = row r of its S, P and O); warps w and
-//              w + 4 split a row's 64 keys and exchange the row max through shared memory. After loading S_j and
-//              after writing P_j each warp arrives once on the LEADER CTA's s_free / p_full barrier.
-//   warp 8     TMA producers of the CTA's halves: lane 0 Q then K, lane 1 V. Loads complete on the leader's
+// Roles (576 threads a CTA):
+//   warps 0-15 softmax + epilogue on the CTA's own 128 rows (TMEM lane r = row r of its S, P and O): warp w serves
+//              the rows of lane quarter w % 4 and the key group w / 4 (16 of a tile's 64 keys, 64 of O's columns),
+//              so four warps share each row. The running max moves only when a group's tile max exceeds it by more
+//              than 2^8: one barrier of the four warps checks that, and only then do they swap maxima through shared
+//              memory. After loading S_j and after writing P_j each warp arrives once on the LEADER CTA's s_free /
+//              p_full barrier.
+//   warp 16    TMA producers of the CTA's halves: lane 0 Q then K, lane 1 V. Loads complete on the leader's
 //              barriers (the 2-CTA form of the bulk tensor copy); the leader's lanes announce the byte counts of both
 //              halves. Each CTA refills a stage when its own k_empty / v_empty says the pair's MMA has finished it.
-//   warp 9     in the leader (rank 0) only, one elected thread issues every MMA of the pair: S_j = Q K_j^T into S
+//   warp 17    in the leader (rank 0) only, one elected thread issues every MMA of the pair: S_j = Q K_j^T into S
 //              buffer j % 2 and O += P_j V_j (A = P_j from TMEM), whichever is ready first, and commits completion to
-//              the barriers of both CTAs (one commit each). In both CTAs warp 9 allocates and frees the TMEM.
+//              the barriers of both CTAs (one commit each). In both CTAs warp 17 allocates and frees the TMEM.
 // Causal is bottom-right as in the single-CTA kernel; the pair loops over the KV tiles its later rows need, the
 // earlier CTA's rows masking the last tile or two. Every wait is time-bounded; a wait that gives up sets the CTA's
 // abort flag, the roles drain what they issued, and both CTAs meet at a final cluster barrier before TMEM is freed.
@@ -28,12 +31,14 @@ namespace lb2 {
 namespace prefill2 {
 
 using prefill::BM;
-using prefill::MMA_WARP;
-using prefill::PRODUCER_WARP;
-using prefill::SOFTMAX_WARPS;
-using prefill::THREADS;
 using prefill::TMEM_COLS;
 using prefill::Params;
+
+constexpr int NG = 4;                         // softmax warps a lane quarter (key / O column groups)
+constexpr int SOFTMAX_WARPS = 4 * NG;
+constexpr int PRODUCER_WARP = SOFTMAX_WARPS;
+constexpr int MMA_WARP = SOFTMAX_WARPS + 1;
+constexpr int THREADS = (SOFTMAX_WARPS + 2) * 32;
 
 template <int D>
 struct Cfg {
@@ -49,8 +54,8 @@ struct Cfg {
   static constexpr int K_OFF = Q_OFF + QBYTES;
   static constexpr int V_OFF = K_OFF + KS * KHBYTES;
   static constexpr int BAR_OFF = V_OFF + VS * VHBYTES;
-  static constexpr int RED_OFF = BAR_OFF + 256;  // [2 halves][128 rows] fp32
-  static constexpr int SMEM_BYTES = RED_OFF + 2 * BM * 4 + 1024;
+  static constexpr int RED_OFF = BAR_OFF + 256;  // [NG groups][128 rows] fp32
+  static constexpr int SMEM_BYTES = RED_OFF + NG * BM * 4 + 1024;
   static constexpr int PB = 3;                    // P buffers
   static constexpr int S_COL = 0;                 // S buffers [b BN, (b + 1) BN), b < 2
   static constexpr int P_COL = 2 * BN;            // P buffers [P_COL + b BN / 2, ...), b < PB
@@ -147,6 +152,21 @@ __device__ __forceinline__ void umma2_commit_both(uint64_t* bar) {
   const uint32_t local = smem_u32(bar);
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(local) : "memory");
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mapa(local, 1))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
                : "memory");
 }
 
@@ -352,13 +372,13 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
     }
   } else {
     // ------------------------------------------------------------------------------------ softmax warps
-    constexpr int HC = BN / 2;  // S columns a thread owns
-    constexpr int DH = D / 2;   // O columns a thread owns
+    constexpr int HC = BN / NG;  // S columns (keys) a thread owns
+    constexpr int DH = D / NG;   // O columns a thread owns
     const int r = 32 * (warp & 3) + lane;
-    const int hf = warp >> 2;
+    const int grp = warp >> 2;
     const int row = r0 + r;
     const uint32_t lane_base = tmem + (uint32_t(32 * (warp & 3)) << 16);
-    const uint32_t pair_bar = 2 + (warp & 3);
+    const uint32_t grp_bar = 2 + (warp & 3);  // named barrier of the NG warps of a lane quarter (ids 2..5)
     float* red = reinterpret_cast<float*>(sm + C::RED_OFF);
     const uint32_t s_free_l = mapa(smem_u32(s_free), 0), p_full_l = mapa(smem_u32(p_full), 0);
     const int lim = p.mask_kind == LB2_MASK_CAUSAL ? p.N - p.T + row : p.N - 1;
@@ -372,7 +392,7 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
       float s[HC];
       if (okj) {
         prefill::tc_fence_after();
-        prefill::tmem_ld32(lane_base + C::S_COL + sb * BN + hf * HC, s);
+        tmem_ld16(lane_base + C::S_COL + sb * BN + grp * HC, s);
         prefill::tmem_wait_ld();
         prefill::tc_fence_before();
         __syncwarp();
@@ -381,7 +401,7 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
 #pragma unroll
         for (int c = 0; c < HC; ++c) s[c] = -INFINITY;
       }
-      const int key0 = j * BN + hf * HC;
+      const int key0 = j * BN + grp * HC;
       const bool full_tile = j * BN + BN - 1 <= lim && j * BN + BN <= p.N && !mrow;
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
       if (full_tile) {
@@ -398,31 +418,30 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
         }
       }
       float tmax = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-      // The running max moves only when a half's tile max exceeds it by more than 2^8 (rare after the first tile):
-      // one barrier tells both halves of the 32 rows whether any of them wants to (or a wait failed); only then do
-      // the halves swap their maxima.
+      // one barrier of the quarter's NG warps: does any of their rows want to move its max (or did a wait fail)?
       const bool want = !okj || tmax * p.scale_log2 > m_run + 8.f;
       uint32_t any_want;
       asm volatile(
           "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
-          "bar.red.or.pred q, %2, 64, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+          "bar.red.or.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
           : "=r"(any_want)
-          : "r"(uint32_t(want)), "r"(pair_bar)
+          : "r"(uint32_t(want)), "r"(grp_bar), "n"(NG * 32)
           : "memory");
       bool move = false;
       float tmax2 = 0.f;
       if (any_want) {
-        red[hf * BM + r] = tmax;
-        uint32_t pair_ok;
+        red[grp * BM + r] = tmax;
+        uint32_t all_ok;
         asm volatile(
             "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
-            "bar.red.and.pred q, %2, 64, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
-            : "=r"(pair_ok)
-            : "r"(uint32_t(okj)), "r"(pair_bar)
+            "bar.red.and.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+            : "=r"(all_ok)
+            : "r"(uint32_t(okj)), "r"(grp_bar), "n"(NG * 32)
             : "memory");
-        tmax = fmaxf(tmax, red[(1 - hf) * BM + r]);
-        asm volatile("bar.sync %0, 64;" ::"r"(pair_bar));
-        if (!pair_ok) {
+#pragma unroll
+        for (int g2 = 0; g2 < NG; ++g2) tmax = fmaxf(tmax, red[g2 * BM + r]);
+        asm volatile("bar.sync %0, %1;" ::"r"(grp_bar), "n"(NG * 32));
+        if (!all_ok) {
           ok = false;
           break;
         }
@@ -436,11 +455,11 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
 #pragma unroll 1
         for (int c = 0; c < DH; c += 32) {
           float ov[32];
-          prefill::tmem_ld32(lane_base + C::O_COL + hf * DH + c, ov);
+          prefill::tmem_ld32(lane_base + C::O_COL + grp * DH + c, ov);
           prefill::tmem_wait_ld();
 #pragma unroll
           for (int e = 0; e < 32; ++e) ov[e] *= factor;
-          prefill::tmem_st32(lane_base + C::O_COL + hf * DH + c, ov);
+          prefill::tmem_st32(lane_base + C::O_COL + grp * DH + c, ov);
         }
         prefill::tmem_wait_st();
       }
@@ -448,7 +467,7 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
         l_run *= factor;
         m_run = tmax2;
       }
-      // P_j into P buffer j % PB (last read by PV_{j-PB}): this half's HC keys at columns hf HC / 2 ...
+      // P_j into P buffer j % PB (last read by PV_{j-PB}): this group's HC keys at columns grp HC / 2 ...
       const int pbuf = j % C::PB;
       if (j >= C::PB && !mbar_wait(&o_done[pbuf], ((j / C::PB) - 1) & 1, 64)) ok = false;
       prefill::tc_fence_after();
@@ -463,7 +482,7 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
         ls4[(c + 1) & 3] += e1;
         pk[c / 2] = pack2<T>(e0, e1);
       }
-      prefill::tmem_st16(lane_base + C::P_COL + pbuf * (BN / 2) + hf * (HC / 2), pk);
+      tmem_st8(lane_base + C::P_COL + pbuf * (BN / 2) + grp * (HC / 2), pk);
       l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
       prefill::tmem_wait_st();
       prefill::tc_fence_before();
@@ -476,21 +495,23 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
     }
     // ---------------------------------------------------------------------------------- epilogue
     ok = __all_sync(0xffffffffu, ok);
-    red[hf * BM + r] = l_run;
-    asm volatile("bar.sync %0, 64;" ::"r"(pair_bar));
-    const float l_tot = l_run + red[(1 - hf) * BM + r];
+    red[grp * BM + r] = l_run;
+    asm volatile("bar.sync %0, %1;" ::"r"(grp_bar), "n"(NG * 32));
+    float l_tot = 0.f;
+#pragma unroll
+    for (int g2 = 0; g2 < NG; ++g2) l_tot += red[g2 * BM + r];
     const bool have_o = ntiles > 0 && ok;
     const bool store = row < p.T;
-    T* orow = reinterpret_cast<T*>(p.o) + b * p.o_st[0] + int64_t(h) * p.o_st[1] + int64_t(row) * p.o_st[2] + hf * DH;
+    T* orow = reinterpret_cast<T*>(p.o) + b * p.o_st[0] + int64_t(h) * p.o_st[1] + int64_t(row) * p.o_st[2] + grp * DH;
     const T* grow = p.gate ? reinterpret_cast<const T*>(p.gate) + b * p.g_st[0] + int64_t(h) * p.g_st[1] +
-                                 int64_t(row) * p.g_st[2] + hf * DH
+                                 int64_t(row) * p.g_st[2] + grp * DH
                            : nullptr;
     const float inv = (have_o && l_tot > 0.f) ? 1.f / l_tot : 0.f;
 #pragma unroll 1
     for (int c = 0; c < DH; c += 32) {
       float ov[32];
       if (have_o) {
-        prefill::tmem_ld32(lane_base + C::O_COL + hf * DH + c, ov);
+        prefill::tmem_ld32(lane_base + C::O_COL + grp * DH + c, ov);
         prefill::tmem_wait_ld();
       } else {
 #pragma unroll
