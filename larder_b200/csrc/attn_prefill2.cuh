@@ -347,7 +347,10 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
             t0 = 0;
             continue;
           }
-          if ((it & 255) == 0) {
+          // Nothing ready: back off briefly, so that this polling thread does not take issue slots and MIO
+          // bandwidth from the softmax warps that share its SM sub-partition.
+          __nanosleep(20);
+          if ((it & 15) == 0) {
             if (*abort_flag) {
               ok = false;
               break;
