@@ -32,7 +32,7 @@ METRIC = "prefill attn TFLOP/s & decode KV-read GB/s at 8k ctx, 1/2/4/8 B200, % 
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode_kernel launch on this workload, from the ncu capture in
 # profiles/decode_kernel_config2.md (148.3 MB read + 4.5 MB written).
-DECODE_TRAFFIC_BYTES = 152.8e6
+DECODE_TRAFFIC_BYTES = 152.1e6
 
 
 def peaks():
@@ -331,7 +331,7 @@ def bench_prefill(torch, ops, dev, rank, world, args, stream, pk, pk_kind, barri
             "flop_per_step": flop, "gpu_launches_per_step": 1,
             "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": round(tf / pk["bf16_tflops"], 4), "traffic": None, "peak_kind": pk_kind,
-                         "kernel": "lb2::prefill::fmha_kernel<bf16,256>"},
+                         "kernel": "lb2::prefill2::fmha2_kernel<bf16,256>"},
             "clocks": clk.summary()}
 
 
