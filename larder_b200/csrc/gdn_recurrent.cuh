@@ -36,23 +36,36 @@ __device__ __forceinline__ float ld_any(const void* p, int64_t i, int dt) {
   }
 }
 
+// NPT consecutive 16-bit values (one 8-byte load for NPT = 4, 16-byte for 8) widened to fp32.
 template <typename QT, int NPT>
 __device__ __forceinline__ void ld_vec(const QT* p, float* out) {
+  if constexpr (NPT == 4) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const QT* h = reinterpret_cast<const QT*>(&u);
 #pragma unroll
-  for (int i = 0; i < NPT; ++i) out[i] = to_f<QT>(p[i]);
+    for (int i = 0; i < 4; ++i) out[i] = to_f<QT>(h[i]);
+  } else if constexpr (NPT == 8) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const QT* h = reinterpret_cast<const QT*>(&u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[i] = to_f<QT>(h[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < NPT; ++i) out[i] = to_f<QT>(p[i]);
+  }
 }
 
 // R value rows a warp (consecutive rows of one head, so q / k loads are shared and R state rows are in flight at
-// once); lane l holds elements [l * NPT, (l + 1) * NPT) of each row.
+// once); lane l holds elements [l * NPT, (l + 1) * NPT) of each row. Grid: x = groups of R rows (four warps a
+// block), y = (b, hv): no index division.
 template <typename QT, int NPT, int R>
 __global__ void __launch_bounds__(128) recurrent_kernel(const Params p) {
   const int lane = threadIdx.x & 31;
-  const int64_t wid = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int groups = p.Dv / R;  // warps a head
-  if (wid >= int64_t(p.B) * p.Hv * groups) return;
-  const int dv0 = int(wid % groups) * R;
-  const int64_t bh = wid / groups;
-  const int hv = int(bh % p.Hv), b = int(bh / p.Hv);
+  const int grp = int(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (grp * R >= p.Dv) return;
+  const int dv0 = grp * R;
+  const int64_t bh = blockIdx.y;
+  const int hv = int(blockIdx.y) % p.Hv, b = int(blockIdx.y) / p.Hv;
   const int hk = hv / (p.Hv / p.Hk);
   const int Dk = p.Dk;
 

@@ -614,13 +614,19 @@ int lb2_gdn_recurrent(const void* q, const void* k, int qdt, const void* v, int 
   for (int dt : {qdt, vdt, gdt, bdt}) LB2_CHECK_ARG(dt >= LB2_F32 && dt <= LB2_F16, "gdn: dtype");
   gdnrec::Params p{q, k, v, g, beta, mask, state_in, state_out, y, qdt, vdt, gdt, bdt, g_vec, B, T, Hk, Dk, Hv, Dv};
   LB2_CHECK_ARG(Dv % 4 == 0, "gdn: Dv must be a multiple of 4");
+  {  // q / k rows are read as 8-byte (Dk = 128) or 16-byte (Dk = 256) vectors
+    const uintptr_t need = Dk == 256 ? 15 : Dk == 128 ? 7 : 0;
+    LB2_CHECK_ARG(((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k)) & need) == 0,
+                  "gdn: q and k must be 8-byte aligned (16-byte at Dk = 256)");
+  }
   LB2_CHECK_ARG((reinterpret_cast<uintptr_t>(state_in) & 15) == 0 && (reinterpret_cast<uintptr_t>(state_out) & 15) == 0,
                 "gdn: state buffers must be 16-byte aligned");
   const int warps = 4;
-  // value rows a warp: several for a decode step (more state in flight), one for longer passes (more warps)
-  const int R = T > 1 ? 1 : (Dk == 256 ? 2 : 4);
-  const int64_t nw = int64_t(B) * Hv * (Dv / R);
-  dim3 grid(unsigned((nw + warps - 1) / warps));
+  // value rows a warp: several for a decode step (more state in flight, 32 fp32 values a lane), one for longer
+  // passes (more warps)
+  const int R = T > 1 ? 1 : (Dk == 256 ? 4 : (Dv % 8 == 0 ? 8 : 4));
+  LB2_CHECK_ARG(int64_t(B) * Hv < 65536, "gdn: at most 65535 (sequence, head) pairs a call");
+  dim3 grid(unsigned((Dv / R + warps - 1) / warps), unsigned(B * Hv));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 #define LB2_GDN_LAUNCH(QT)                                                                           \
   if (R == 1) {                                                                                      \
@@ -630,12 +636,18 @@ int lb2_gdn_recurrent(const void* q, const void* k, int qdt, const void* v, int 
       case 128: gdnrec::recurrent_kernel<QT, 4, 1><<<grid, warps * 32, 0, st>>>(p); break;           \
       default: gdnrec::recurrent_kernel<QT, 8, 1><<<grid, warps * 32, 0, st>>>(p); break;            \
     }                                                                                                \
-  } else {                                                                                           \
+  } else if (R == 4) {                                                                              \
     switch (Dk) {                                                                                    \
       case 32: gdnrec::recurrent_kernel<QT, 1, 4><<<grid, warps * 32, 0, st>>>(p); break;            \
       case 64: gdnrec::recurrent_kernel<QT, 2, 4><<<grid, warps * 32, 0, st>>>(p); break;            \
       case 128: gdnrec::recurrent_kernel<QT, 4, 4><<<grid, warps * 32, 0, st>>>(p); break;           \
-      default: gdnrec::recurrent_kernel<QT, 8, 2><<<grid, warps * 32, 0, st>>>(p); break;            \
+      default: gdnrec::recurrent_kernel<QT, 8, 4><<<grid, warps * 32, 0, st>>>(p); break;            \
+    }                                                                                                \
+  } else {                                                                                           \
+    switch (Dk) {                                                                                    \
+      case 32: gdnrec::recurrent_kernel<QT, 1, 8><<<grid, warps * 32, 0, st>>>(p); break;            \
+      case 64: gdnrec::recurrent_kernel<QT, 2, 8><<<grid, warps * 32, 0, st>>>(p); break;            \
+      default: gdnrec::recurrent_kernel<QT, 4, 8><<<grid, warps * 32, 0, st>>>(p); break;            \
     }                                                                                                \
   }
   if (qdt == LB2_BF16) {
