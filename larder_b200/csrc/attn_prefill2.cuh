@@ -4,12 +4,14 @@
 // SM then streams 64 KB of K/V from L2 per 64-key tile and the L2 -> shared memory transfer, not the tensor cores,
 // sets the pace. Here the two CTAs of a cluster take 256 consecutive rows of one head (128 each) and one MMA
 // instruction covers both (M = 256): matrix A (Q for the scores, P for the output) stays split by rows, one half in
-// each CTA, and matrix B is split along N, so each CTA loads only HALF of every K tile (32 of its 64 keys) and HALF
-// of every V tile (128 of its 256 columns). Per SM that halves the K/V bytes per FLOP.
+// each CTA, and matrix B is split along N, so each CTA loads only HALF of every K tile (64 of its 128 keys) and HALF
+// of every V tile (128 of its 256 columns). Per SM that halves the K/V bytes per FLOP. Tiles of 128 keys make the
+// score MMAs N = 128 wide and halve the per-tile handshakes of the softmax; TMEM then holds one S buffer (128
+// columns), two P buffers (64 each) and O (256).
 //
 // Roles (576 threads a CTA):
 //   warps 0-15 softmax + epilogue on the CTA's own 128 rows (TMEM lane r = row r of its S, P and O): warp w serves
-//              the rows of lane quarter w % 4 and the key group w / 4 (16 of a tile's 64 keys, 64 of O's columns),
+//              the rows of lane quarter w % 4 and the key group w / 4 (32 of a tile's 128 keys, 64 of O's columns),
 //              so four warps share each row. The running max moves only when a group's tile max exceeds it by more
 //              than 2^8: one barrier of the four warps checks that, and only then do they swap maxima through shared
 //              memory. After loading S_j and after writing P_j each warp arrives once on the LEADER CTA's s_free /
@@ -17,8 +19,8 @@
 //   warp 16    TMA producers of the CTA's halves: lane 0 Q then K, lane 1 V. Loads complete on the leader's
 //              barriers (the 2-CTA form of the bulk tensor copy); the leader's lanes announce the byte counts of both
 //              halves. Each CTA refills a stage when its own k_empty / v_empty says the pair's MMA has finished it.
-//   warp 17    in the leader (rank 0) only, one elected thread issues every MMA of the pair: S_j = Q K_j^T into S
-//              buffer j % 2 and O += P_j V_j (A = P_j from TMEM), whichever is ready first, and commits completion to
+//   warp 17    in the leader (rank 0) only, one elected thread issues every MMA of the pair: S_j = Q K_j^T into the S
+//              buffer and O += P_j V_j (A = P_j from TMEM), whichever is ready first, and commits completion to
 //              the barriers of both CTAs (one commit each). In both CTAs warp 17 allocates and frees the TMEM.
 // Causal is bottom-right as in the single-CTA kernel; the pair loops over the KV tiles its later rows need, the
 // earlier CTA's rows masking the last tile or two. Every wait is time-bounded; a wait that gives up sets the CTA's
@@ -42,23 +44,25 @@ constexpr int THREADS = (SOFTMAX_WARPS + 2) * 32;
 
 template <int D>
 struct Cfg {
-  static constexpr int BN = 64;                 // keys a tile (the pair)
+  static constexpr int BN = 128;                // keys a tile (the pair)
   static constexpr int HN = BN / 2;             // K rows (keys) a CTA holds
   static constexpr int HD = D / 2;              // V columns a CTA holds
   static constexpr int QBYTES = BM * D * 2;
   static constexpr int KHBYTES = HN * D * 2;    // a CTA's half of a K tile
   static constexpr int VHBYTES = BN * HD * 2;   // a CTA's half of a V tile
-  static constexpr int KS = 4;
-  static constexpr int VS = 4;
+  static constexpr int KS = 2;
+  static constexpr int VS = 2;
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_OFF + QBYTES;
   static constexpr int V_OFF = K_OFF + KS * KHBYTES;
   static constexpr int BAR_OFF = V_OFF + VS * VHBYTES;
   static constexpr int RED_OFF = BAR_OFF + 256;  // [NG groups][128 rows] fp32
   static constexpr int SMEM_BYTES = RED_OFF + NG * BM * 4 + 1024;
-  static constexpr int PB = 3;                    // P buffers
-  static constexpr int S_COL = 0;                 // S buffers [b BN, (b + 1) BN), b < 2
-  static constexpr int P_COL = 2 * BN;            // P buffers [P_COL + b BN / 2, ...), b < PB
+  static constexpr int SB = 1;                    // S buffers: the softmax copies S_j to registers at once, so
+                                                  // S_{j+1} can overwrite it while P_j is still being formed
+  static constexpr int PB = 2;                    // P buffers
+  static constexpr int S_COL = 0;                 // S buffers [b BN, (b + 1) BN), b < SB
+  static constexpr int P_COL = SB * BN;           // P buffers [P_COL + b BN / 2, ...), b < PB
   static constexpr int O_COL = P_COL + PB * BN / 2;  // O [O_COL, O_COL + D)
   static_assert(O_COL + D <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -212,14 +216,14 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
   uint64_t* k_empty = k_full + KS;    // [KS] both CTAs: the pair's MMA has read the stage
   uint64_t* v_full = k_empty + KS;    // [VS] leader
   uint64_t* v_empty = v_full + VS;    // [VS] both CTAs
-  uint64_t* s_full = v_empty + VS;    // [2]  both CTAs: S_j complete in S buffer j % 2
-  uint64_t* s_free = s_full + 2;      // [2]  leader: all 16 softmax warps of the pair have loaded S_j
-  uint64_t* p_full = s_free + 2;      // [PB] leader: all 16 softmax warps have written P_j into P buffer j % PB
+  uint64_t* s_full = v_empty + VS;    // [SB] both CTAs: S_j complete in S buffer j % SB
+  uint64_t* s_free = s_full + C::SB;  // [SB] leader: all softmax warps of the pair have loaded S_j
+  uint64_t* p_full = s_free + C::SB;  // [PB] leader: all softmax warps have written P_j into P buffer j % PB
   uint64_t* o_done = p_full + C::PB;  // [PB] both CTAs: PV_j complete (P buffer j % PB read)
   uint64_t* drain = o_done + C::PB;   // [1]  leader
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(drain + 2);
-  static_assert((1 + 2 * KS + 2 * VS + 4 + 2 * C::PB + 1) * 8 + 16 <= 256, "barrier area");
+  static_assert((1 + 2 * KS + 2 * VS + 2 * C::SB + 2 * C::PB + 1) * 8 + 16 <= 256, "barrier area");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -232,7 +236,7 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < C::SB; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 2 * SOFTMAX_WARPS);
     }
@@ -307,7 +311,7 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
         const uint32_t q_addr = smem_u32(sm + C::Q_OFF);
         bool ok = mbar_wait(q_full, 0, 51);
         auto issue_s = [&](int j) {
-          const int st = j % KS, sb = j & 1;
+          const int st = j % KS, sb = j % C::SB;
           prefill::tc_fence_after();
           const uint32_t k_addr = smem_u32(sm + C::K_OFF + st * C::KHBYTES);
 #pragma unroll
@@ -342,7 +346,7 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
             continue;
           }
           if (js < ntiles && mbar_test_wait_cluster(&k_full[js % KS], (js / KS) & 1) &&
-              (js < 2 || mbar_test_wait_cluster(&s_free[js & 1], ((js >> 1) - 1) & 1))) {
+              (js < C::SB || mbar_test_wait_cluster(&s_free[js % C::SB], ((js / C::SB) - 1) & 1))) {
             issue_s(js++);
             t0 = 0;
             continue;
@@ -389,13 +393,14 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
-      const int sb = j & 1;
-      bool okj = ok && !*abort_flag && mbar_wait(&s_full[sb], (j >> 1) & 1, 61);
+      const int sb = j % C::SB;
+      bool okj = ok && !*abort_flag && mbar_wait(&s_full[sb], (j / C::SB) & 1, 61);
       okj = __all_sync(0xffffffffu, okj);
       float s[HC];
       if (okj) {
         prefill::tc_fence_after();
-        tmem_ld16(lane_base + C::S_COL + sb * BN + grp * HC, s);
+        static_assert(HC == 32, "a softmax thread loads 32 S columns");
+        prefill::tmem_ld32(lane_base + C::S_COL + sb * BN + grp * HC, s);
         prefill::tmem_wait_ld();
         prefill::tc_fence_before();
         __syncwarp();
@@ -485,7 +490,7 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
         ls4[(c + 1) & 3] += e1;
         pk[c / 2] = pack2<T>(e0, e1);
       }
-      tmem_st8(lane_base + C::P_COL + pbuf * (BN / 2) + grp * (HC / 2), pk);
+      prefill::tmem_st16(lane_base + C::P_COL + pbuf * (BN / 2) + grp * (HC / 2), pk);
       l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
       prefill::tmem_wait_st();
       prefill::tc_fence_before();

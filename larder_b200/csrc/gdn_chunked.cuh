@@ -16,9 +16,10 @@
 //        decay / beta weighting, T by blocked inversion (16 x 16 diagonal blocks by substitution, then 32 and 64
 //        by the 2 x 2 block formula) in fp32, and W, U' on TF32 mma.sync with their B operands (beta Gam K,
 //        beta V) formed from the 16-bit tiles on the fly; writes W, U', M, gamma, Gam to the workspace.
-//   scan (grid: Dv / 32 value-row blocks x v-heads x batch): the state slice S[32 x 128] in fp32 shared memory,
-//        chunks in order, each chunk's workspace tiles prefetched with cp.async while the previous chunk computes;
-//        U, Y and the state update on TF32 mma.sync with fp32 accumulation.
+//   scan (grid: Dv / 32 value-row blocks x v-heads x batch, 8 warps): the state slice S[32 x 128] in fp32
+//        registers (a TF32 copy in shared memory for the products that read all of it), chunks in order, each
+//        chunk's workspace tiles prefetched with cp.async while the previous chunk computes; U, Y and the state
+//        update on TF32 mma.sync with fp32 accumulation. W and M are stored already rounded to TF32 by prep.
 #pragma once
 
 #include "common.cuh"
@@ -221,7 +222,7 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
         const int j = n * 8 + 2 * (lane & 3) + (e & 1);
         const float dec = j <= t ? __expf(gam[t] - gam[j]) : 0.f;
         Af[t * AP + j] = j < t ? bet[t] * dec * kk[n][e] : 0.f;
-        Mg[t * C + j] = dec * qk[n][e];
+        Mg[t * C + j] = __uint_as_float(tf32(dec * qk[n][e]));  // an MMA operand of the scan: rounded once here
       }
   }
   __syncthreads();
@@ -317,6 +318,11 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
                      tf32(s1 * to_f<T>(R[(k0 + cq + 4) * KP + n0 + r])));
           }
         }
+        if (!which)  // W is an MMA operand of the scan: stored rounded to TF32; U' stays fp32
+#pragma unroll
+          for (int n = 0; n < 8; ++n)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[n][e] = __uint_as_float(tf32(acc[n][e]));
 #pragma unroll
         for (int n = 0; n < 8; ++n) {
           const int col = nh * 64 + n * 8 + 2 * cq;
@@ -336,21 +342,31 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
 
 // ------------------------------------------------------------------------------------------------ scan
 
+constexpr int SCAN_THREADS = 256;  // warps 0-3: U = U' - W S^T; warps 4-7: Q S^T and M U; all 8: the state update
+constexpr int UQ = 40;             // u32 row stride of the U tiles read as MMA operands (conflict-free fragments)
+
 struct ScanSmem {
   // one prefetch buffer
-  static constexpr int W = 0;                         // f32 [C][WP]
+  static constexpr int W = 0;                         // tf32 [C][WP]
   static constexpr int U = W + C * WP * 4;            // f32 [C][UP]   U' columns of this block
-  static constexpr int M = U + C * UP * 4;            // f32 [C][AP]
-  static constexpr int Q = M + C * AP * 4;            // bf16 [C][KP]
-  static constexpr int K = Q + C * KP * 2;            // bf16 [C][KP]
+  static constexpr int M = U + C * UP * 4;            // tf32 [C][AP]
+  static constexpr int Q = M + C * AP * 4;            // 16-bit [C][KP]
+  static constexpr int K = Q + C * KP * 2;            // 16-bit [C][KP]
   static constexpr int G = K + C * KP * 2;            // f32 [C] gamma, [C] Gam
   static constexpr int BUF = G + 2 * C * 4;
   // persistent
-  static constexpr int S = 2 * BUF;                   // f32 [DVB][WP] the state slice
-  static constexpr int UB = S + DVB * WP * 4;         // f32 [C][UP] this chunk's U
-  static constexpr int DEC = UB + C * UP * 4;         // f32 [C] exp(gamma_C - gamma_j)
-  static constexpr int BYTES = DEC + C * 4;
+  static constexpr int ST = 2 * BUF;                  // tf32 [DVB][WP] the state slice, rounded for the MMAs
+  static constexpr int UB = ST + DVB * WP * 4;        // tf32 [C][UQ] this chunk's U
+  static constexpr int UD = UB + C * UQ * 4;          // tf32 [C][UQ] diag(exp(gamma_C - gamma)) U
+  static constexpr int BYTES = UD + C * UQ * 4;
 };
+static_assert(ScanSmem::BYTES <= 232448, "scan shared memory");
+
+// A 16-bit value's exact TF32 bit pattern (bf16 and fp16 mantissas fit TF32's 10 bits).
+template <typename T>
+__device__ __forceinline__ uint32_t tf32_of(T x) {
+  return __float_as_uint(to_f<T>(x));
+}
 
 template <typename T>
 __device__ __forceinline__ void scan_prefetch(const Params& p, uint8_t* buf, int b, int h, int hk, int c, int dv0,
@@ -362,22 +378,26 @@ __device__ __forceinline__ void scan_prefetch(const Params& p, uint8_t* buf, int
   T* Q = reinterpret_cast<T*>(buf + ScanSmem::Q);
   T* K = reinterpret_cast<T*>(buf + ScanSmem::K);
   float* G = reinterpret_cast<float*>(buf + ScanSmem::G);
-  for (int e = tid; e < C * (DK / 4); e += 128) {  // W: 64 rows x 32 chunks of 16 B
+#pragma unroll
+  for (int e = tid; e < C * (DK / 4); e += SCAN_THREADS) {  // W: 64 rows x 32 pieces of 16 B
     const int r = e >> 5, q = e & 31;
     cp_async16(W + r * WP + q * 4, u + r * DK + q * 4);
   }
-  for (int e = tid; e < C * (DVB / 4); e += 128) {  // U' columns dv0 .. dv0 + 31
+#pragma unroll
+  for (int e = tid; e < C * (DVB / 4); e += SCAN_THREADS) {  // U' columns dv0 .. dv0 + 31
     const int r = e >> 3, q = e & 7;
     cp_async16(U + r * UP + q * 4, u + C * DK + r * DV + dv0 + q * 4);
   }
-  for (int e = tid; e < C * (C / 4); e += 128) {  // M
+#pragma unroll
+  for (int e = tid; e < C * (C / 4); e += SCAN_THREADS) {  // M
     const int r = e >> 4, q = e & 15;
     cp_async16(M + r * AP + q * 4, u + C * DK + C * DV + r * C + q * 4);
   }
   if (tid < 2 * C / 4) cp_async16(G + tid * 4, u + C * DK + C * DV + C * C + tid * 4);
   const T* qg = static_cast<const T*>(p.q);
   const T* kg = static_cast<const T*>(p.k);
-  for (int e = tid; e < C * (DK / 8); e += 128) {  // Q, K rows (zero past T)
+#pragma unroll
+  for (int e = tid; e < C * (DK / 8); e += SCAN_THREADS) {  // Q, K rows (zero past T)
     const int r = e >> 4, q = e & 15;
     const int pos = c * C + r;
     if (pos < p.T) {
@@ -391,22 +411,39 @@ __device__ __forceinline__ void scan_prefetch(const Params& p, uint8_t* buf, int
   }
 }
 
+// One CTA: value rows dv0 .. dv0 + 31 of one (batch, v-head), all chunks in order. The fp32 state slice lives in
+// registers, warp w owning key columns 16 w .. 16 w + 15 of all 32 rows; a TF32 copy in shared memory feeds the
+// products that read the whole slice. Per chunk: (1) warps 0-3 form U = U' - W S^T (16 positions each) while warps
+// 4-7 form Gam Q S^T; (2) all warps update their state columns with U^T diag(exp(gamma_C - gamma)) K while warps
+// 4-7 add M U to Y and store it.
 template <typename T>
-__global__ void __launch_bounds__(128, 1) scan_kernel(const Params p) {
+__global__ void __launch_bounds__(SCAN_THREADS, 1) scan_kernel(const Params p) {
   const int blk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int hk = h / (p.Hv / p.Hk);
   const int dv0 = blk * DVB;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int r = lane >> 2, cq = lane & 3;
   extern __shared__ __align__(16) uint8_t sm[];
-  float* S = reinterpret_cast<float*>(sm + ScanSmem::S);
-  float* Ub = reinterpret_cast<float*>(sm + ScanSmem::UB);
-  float* dec = reinterpret_cast<float*>(sm + ScanSmem::DEC);
+  uint32_t* St = reinterpret_cast<uint32_t*>(sm + ScanSmem::ST);
+  uint32_t* Ub = reinterpret_cast<uint32_t*>(sm + ScanSmem::UB);
+  uint32_t* Ud = reinterpret_cast<uint32_t*>(sm + ScanSmem::UD);
 
-  for (int e = tid; e < DVB * DK; e += 128) {
-    const int i = e / DK, d = e % DK;
-    S[i * WP + d] = p.s_in[((int64_t(b) * p.Hv + h) * DV + dv0 + i) * DK + d];
-  }
+  // the state tile of this warp: rows mt * 16 + r (+ 8), columns 16 warp + 8 n + 2 cq (+ 1)
+  float sreg[2][2][4];
+  const float* sin = p.s_in + (int64_t(b) * p.Hv + h) * DV * DK;
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int i = mt * 16 + r + 8 * hh, d = warp * 16 + n * 8 + 2 * cq;
+        const float2 v = *reinterpret_cast<const float2*>(sin + int64_t(dv0 + i) * DK + d);
+        sreg[mt][n][2 * hh] = v.x;
+        sreg[mt][n][2 * hh + 1] = v.y;
+        St[i * WP + d] = tf32(v.x);
+        St[i * WP + d + 1] = tf32(v.y);
+      }
   scan_prefetch<T>(p, sm, b, h, hk, 0, dv0, tid);
   cp_async_commit();
 
@@ -416,61 +453,109 @@ __global__ void __launch_bounds__(128, 1) scan_kernel(const Params p) {
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
-    const float* W = reinterpret_cast<const float*>(buf + ScanSmem::W);
+    const uint32_t* W = reinterpret_cast<const uint32_t*>(buf + ScanSmem::W);
     const float* U = reinterpret_cast<const float*>(buf + ScanSmem::U);
-    const float* M = reinterpret_cast<const float*>(buf + ScanSmem::M);
+    const uint32_t* M = reinterpret_cast<const uint32_t*>(buf + ScanSmem::M);
     const T* Q = reinterpret_cast<const T*>(buf + ScanSmem::Q);
     const T* K = reinterpret_cast<const T*>(buf + ScanSmem::K);
     const float* G = reinterpret_cast<const float*>(buf + ScanSmem::G);
-    const int m0 = warp * 16;
+    const int m0 = (warp & 3) * 16;
 
-    // U = U' - W S^T and QS = Q S^T for rows m0 .. m0 + 15, all 32 value columns
-    float uacc[4][4], yacc[4][4];
+    // (1) warps 0-3: acc = W S^T; warps 4-7: acc = Q S^T. Rows m0 .. m0 + 15, all 32 value columns.
+    float acc[4][4];
 #pragma unroll
     for (int n = 0; n < 4; ++n)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) uacc[n][e] = yacc[n][e] = 0.f;
+      for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
+    if (warp < 4) {
 #pragma unroll 4
-    for (int k0 = 0; k0 < DK; k0 += 8) {
-      const uint32_t a0 = tf32(W[(m0 + r) * WP + k0 + cq]), a1 = tf32(W[(m0 + r + 8) * WP + k0 + cq]);
-      const uint32_t a2 = tf32(W[(m0 + r) * WP + k0 + cq + 4]), a3 = tf32(W[(m0 + r + 8) * WP + k0 + cq + 4]);
-      const uint32_t q0 = tf32(to_f<T>(Q[(m0 + r) * KP + k0 + cq])), q1 = tf32(to_f<T>(Q[(m0 + r + 8) * KP + k0 + cq]));
-      const uint32_t q2 = tf32(to_f<T>(Q[(m0 + r) * KP + k0 + cq + 4]));
-      const uint32_t q3 = tf32(to_f<T>(Q[(m0 + r + 8) * KP + k0 + cq + 4]));
+      for (int k0 = 0; k0 < DK; k0 += 8) {
+        const uint32_t a0 = W[(m0 + r) * WP + k0 + cq], a1 = W[(m0 + r + 8) * WP + k0 + cq];
+        const uint32_t a2 = W[(m0 + r) * WP + k0 + cq + 4], a3 = W[(m0 + r + 8) * WP + k0 + cq + 4];
 #pragma unroll
-      for (int n = 0; n < 4; ++n) {
-        const uint32_t b0 = tf32(S[(n * 8 + r) * WP + k0 + cq]), b1 = tf32(S[(n * 8 + r) * WP + k0 + cq + 4]);
-        mma_tf32(uacc[n], a0, a1, a2, a3, b0, b1);
-        mma_tf32(yacc[n], q0, q1, q2, q3, b0, b1);
+        for (int n = 0; n < 4; ++n)
+          mma_tf32(acc[n], a0, a1, a2, a3, St[(n * 8 + r) * WP + k0 + cq], St[(n * 8 + r) * WP + k0 + cq + 4]);
       }
-    }
-#pragma unroll
-    for (int n = 0; n < 4; ++n) {
-      const int col = n * 8 + 2 * cq;
-      Ub[(m0 + r) * UP + col] = U[(m0 + r) * UP + col] - uacc[n][0];
-      Ub[(m0 + r) * UP + col + 1] = U[(m0 + r) * UP + col + 1] - uacc[n][1];
-      Ub[(m0 + r + 8) * UP + col] = U[(m0 + r + 8) * UP + col] - uacc[n][2];
-      Ub[(m0 + r + 8) * UP + col + 1] = U[(m0 + r + 8) * UP + col + 1] - uacc[n][3];
-    }
-    if (tid < C) dec[tid] = __expf(G[C - 1] - G[tid]);
-    __syncthreads();
-    // Y = diag(Gam) Q S^T + M U  (M lower triangular: k < 16 (w + 1))
-#pragma unroll
-    for (int n = 0; n < 4; ++n) {
-      yacc[n][0] *= G[C + m0 + r];
-      yacc[n][1] *= G[C + m0 + r];
-      yacc[n][2] *= G[C + m0 + r + 8];
-      yacc[n][3] *= G[C + m0 + r + 8];
-    }
-    for (int k0 = 0; k0 < 16 * (warp + 1); k0 += 8) {
-      const uint32_t a0 = tf32(M[(m0 + r) * AP + k0 + cq]), a1 = tf32(M[(m0 + r + 8) * AP + k0 + cq]);
-      const uint32_t a2 = tf32(M[(m0 + r) * AP + k0 + cq + 4]), a3 = tf32(M[(m0 + r + 8) * AP + k0 + cq + 4]);
+      // U = U' - W S^T, stored rounded for the products that read it, plain and scaled by exp(gamma_C - gamma_t)
+      const float gl = G[C - 1];
+      const float dl = __expf(gl - G[m0 + r]), dh = __expf(gl - G[m0 + r + 8]);
 #pragma unroll
       for (int n = 0; n < 4; ++n)
-        mma_tf32(yacc[n], a0, a1, a2, a3, tf32(Ub[(k0 + cq) * UP + n * 8 + r]),
-                 tf32(Ub[(k0 + cq + 4) * UP + n * 8 + r]));
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int t = m0 + r + 8 * (e >> 1), col = n * 8 + 2 * cq + (e & 1);
+          const float u = U[t * UP + col] - acc[n][e];
+          Ub[t * UQ + col] = tf32(u);
+          Ud[t * UQ + col] = tf32((e >> 1 ? dh : dl) * u);
+        }
+    } else {
+#pragma unroll 4
+      for (int k0 = 0; k0 < DK; k0 += 8) {
+        const uint32_t a0 = tf32_of(Q[(m0 + r) * KP + k0 + cq]), a1 = tf32_of(Q[(m0 + r + 8) * KP + k0 + cq]);
+        const uint32_t a2 = tf32_of(Q[(m0 + r) * KP + k0 + cq + 4]);
+        const uint32_t a3 = tf32_of(Q[(m0 + r + 8) * KP + k0 + cq + 4]);
+#pragma unroll
+        for (int n = 0; n < 4; ++n)
+          mma_tf32(acc[n], a0, a1, a2, a3, St[(n * 8 + r) * WP + k0 + cq], St[(n * 8 + r) * WP + k0 + cq + 4]);
+      }
+      const float gl = G[C + m0 + r], gh = G[C + m0 + r + 8];
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        acc[n][0] *= gl;
+        acc[n][1] *= gl;
+        acc[n][2] *= gh;
+        acc[n][3] *= gh;
+      }
     }
+    __syncthreads();  // U complete; every read of the state copy done
+
+    // (2) S <- Gam_C S + (diag(dec) U)^T K on this warp's 16 key columns (all 32 value rows)
     {
+      const float gc = G[C + C - 1];
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int n = 0; n < 2; ++n)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) sreg[mt][n][e] *= gc;
+#pragma unroll 2
+      for (int k0 = 0; k0 < C; k0 += 8) {
+        uint32_t a[2][4];
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          a[mt][0] = Ud[(k0 + cq) * UQ + mt * 16 + r];
+          a[mt][1] = Ud[(k0 + cq) * UQ + mt * 16 + r + 8];
+          a[mt][2] = Ud[(k0 + cq + 4) * UQ + mt * 16 + r];
+          a[mt][3] = Ud[(k0 + cq + 4) * UQ + mt * 16 + r + 8];
+        }
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+          const int col = warp * 16 + n * 8 + r;
+          const uint32_t b0 = tf32_of(K[(k0 + cq) * KP + col]), b1 = tf32_of(K[(k0 + cq + 4) * KP + col]);
+#pragma unroll
+          for (int mt = 0; mt < 2; ++mt) mma_tf32(sreg[mt][n], a[mt][0], a[mt][1], a[mt][2], a[mt][3], b0, b1);
+        }
+      }
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int n = 0; n < 2; ++n)
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const int i = mt * 16 + r + 8 * hh, d = warp * 16 + n * 8 + 2 * cq;
+            St[i * WP + d] = tf32(sreg[mt][n][2 * hh]);
+            St[i * WP + d + 1] = tf32(sreg[mt][n][2 * hh + 1]);
+          }
+    }
+    // (3) warps 4-7: Y = Gam Q S^T + M U (M lower triangular: k < m0 + 16), stored
+    if (warp >= 4) {
+      for (int k0 = 0; k0 < m0 + 16; k0 += 8) {
+        const uint32_t a0 = M[(m0 + r) * AP + k0 + cq], a1 = M[(m0 + r + 8) * AP + k0 + cq];
+        const uint32_t a2 = M[(m0 + r) * AP + k0 + cq + 4], a3 = M[(m0 + r + 8) * AP + k0 + cq + 4];
+#pragma unroll
+        for (int n = 0; n < 4; ++n)
+          mma_tf32(acc[n], a0, a1, a2, a3, Ub[(k0 + cq) * UQ + n * 8 + r], Ub[(k0 + cq + 4) * UQ + n * 8 + r]);
+      }
       T* yg = static_cast<T*>(p.y);
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
@@ -479,64 +564,25 @@ __global__ void __launch_bounds__(128, 1) scan_kernel(const Params p) {
           T* yr = yg + ((int64_t(b) * p.T + pos) * p.Hv + h) * DV + dv0;
 #pragma unroll
           for (int n = 0; n < 4; ++n) {
-            yr[n * 8 + 2 * cq] = from_f<T>(yacc[n][2 * hh]);
-            yr[n * 8 + 2 * cq + 1] = from_f<T>(yacc[n][2 * hh + 1]);
+            yr[n * 8 + 2 * cq] = from_f<T>(acc[n][2 * hh]);
+            yr[n * 8 + 2 * cq + 1] = from_f<T>(acc[n][2 * hh + 1]);
           }
         }
       }
     }
-    // S <- Gam_C S + U^T diag(dec) K: value rows 0 .. 31 (two m-tiles), key columns 32 w .. 32 w + 31
-    {
-      const float gc = G[C + C - 1];
-      float sacc[2][4][4];
+    __syncthreads();  // the state copy complete and this chunk's buffer free before the next prefetch
+  }
+  float* sout = p.s_out + (int64_t(b) * p.Hv + h) * DV * DK;
 #pragma unroll
-      for (int mt = 0; mt < 2; ++mt)
+  for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-        for (int n = 0; n < 4; ++n) {
-          const int i0 = mt * 16 + r, d0 = warp * 32 + n * 8 + 2 * cq;
-          sacc[mt][n][0] = gc * S[i0 * WP + d0];
-          sacc[mt][n][1] = gc * S[i0 * WP + d0 + 1];
-          sacc[mt][n][2] = gc * S[(i0 + 8) * WP + d0];
-          sacc[mt][n][3] = gc * S[(i0 + 8) * WP + d0 + 1];
-        }
-#pragma unroll 2
-      for (int k0 = 0; k0 < C; k0 += 8) {
-        uint32_t a[2][4];
+    for (int n = 0; n < 2; ++n)
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-          a[mt][0] = tf32(Ub[(k0 + cq) * UP + mt * 16 + r]);
-          a[mt][1] = tf32(Ub[(k0 + cq) * UP + mt * 16 + r + 8]);
-          a[mt][2] = tf32(Ub[(k0 + cq + 4) * UP + mt * 16 + r]);
-          a[mt][3] = tf32(Ub[(k0 + cq + 4) * UP + mt * 16 + r + 8]);
-        }
-        const float d0 = dec[k0 + cq], d1 = dec[k0 + cq + 4];
-#pragma unroll
-        for (int n = 0; n < 4; ++n) {
-          const int col = warp * 32 + n * 8 + r;
-          const uint32_t b0 = tf32(d0 * to_f<T>(K[(k0 + cq) * KP + col]));
-          const uint32_t b1 = tf32(d1 * to_f<T>(K[(k0 + cq + 4) * KP + col]));
-#pragma unroll
-          for (int mt = 0; mt < 2; ++mt) mma_tf32(sacc[mt][n], a[mt][0], a[mt][1], a[mt][2], a[mt][3], b0, b1);
-        }
+      for (int hh = 0; hh < 2; ++hh) {
+        const int i = mt * 16 + r + 8 * hh, d = warp * 16 + n * 8 + 2 * cq;
+        *reinterpret_cast<float2*>(sout + int64_t(dv0 + i) * DK + d) =
+            make_float2(sreg[mt][n][2 * hh], sreg[mt][n][2 * hh + 1]);
       }
-      __syncthreads();  // every warp's reads of S (U and QS above) precede the update
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-        for (int n = 0; n < 4; ++n) {
-          const int i0 = mt * 16 + r, d0 = warp * 32 + n * 8 + 2 * cq;
-          S[i0 * WP + d0] = sacc[mt][n][0];
-          S[i0 * WP + d0 + 1] = sacc[mt][n][1];
-          S[(i0 + 8) * WP + d0] = sacc[mt][n][2];
-          S[(i0 + 8) * WP + d0 + 1] = sacc[mt][n][3];
-        }
-    }
-    __syncthreads();  // the state and U are complete before the next chunk reads them
-  }
-  for (int e = tid; e < DVB * DK; e += 128) {
-    const int i = e / DK, d = e % DK;
-    p.s_out[((int64_t(b) * p.Hv + h) * DV + dv0 + i) * DK + d] = S[i * WP + d];
-  }
 }
 
 }  // namespace gdnchunk

@@ -522,7 +522,7 @@ int lb2_attn_prefill(const void* q, const int64_t* q_st, const void* k, const in
   const int BN = D == 256 ? prefill::Cfg<256>::BN : prefill::Cfg<128>::BN;
   int rc = prefill::map4(&qm, q, q_st, B, Hq, T, D, dtype, prefill::BM);
   if (!rc) rc = prefill::map4(&km, k, k_st, B, Hkv, N, D, dtype, pair ? prefill2::Cfg<256>::HN : BN);
-  if (!rc) rc = prefill::map4(&vm, v, v_st, B, Hkv, N, D, dtype, BN);
+  if (!rc) rc = prefill::map4(&vm, v, v_st, B, Hkv, N, D, dtype, pair ? prefill2::Cfg<256>::BN : BN);
   if (rc) return rc;
   prefill::Params p{};
   p.o = o;
@@ -576,6 +576,7 @@ int lb2_gdn_chunked(const void* q, const void* k, int qdt, const void* v, int vd
   LB2_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(workspace),
                 "gdn_chunked: q, k, v and workspace 16-byte aligned");
   LB2_CHECK_ARG(workspace_bytes >= lb2_gdn_chunked_workspace_size(B, T, Hk, Hv, Dk, Dv), "gdn_chunked: workspace too small");
+  LB2_CHECK_ARG(((uintptr_t(state_in) | uintptr_t(state_out)) & 7) == 0, "gdn_chunked: states 8-byte aligned");
   gdnchunk::Params p{q, k, v, g, beta, qdt, vdt, gdt, bdt, state_in, state_out, y, B, T, Hk, Hv,
                      (T + gdnchunk::C - 1) / gdnchunk::C, static_cast<float*>(workspace)};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -596,10 +597,10 @@ int lb2_gdn_chunked(const void* q, const void* k, int qdt, const void* v, int vd
   const dim3 gp(unsigned(p.nchunks), unsigned(Hv), unsigned(B)), gs(gdnchunk::DV / gdnchunk::DVB, Hv, B);
   if (qdt == LB2_BF16) {
     if (p.nchunks > 0) gdnchunk::prep_kernel<__nv_bfloat16><<<gp, 128, gdnchunk::PrepSmem::BYTES, st>>>(p);
-    gdnchunk::scan_kernel<__nv_bfloat16><<<gs, 128, gdnchunk::ScanSmem::BYTES, st>>>(p);
+    gdnchunk::scan_kernel<__nv_bfloat16><<<gs, gdnchunk::SCAN_THREADS, gdnchunk::ScanSmem::BYTES, st>>>(p);
   } else {
     if (p.nchunks > 0) gdnchunk::prep_kernel<__half><<<gp, 128, gdnchunk::PrepSmem::BYTES, st>>>(p);
-    gdnchunk::scan_kernel<__half><<<gs, 128, gdnchunk::ScanSmem::BYTES, st>>>(p);
+    gdnchunk::scan_kernel<__half><<<gs, gdnchunk::SCAN_THREADS, gdnchunk::ScanSmem::BYTES, st>>>(p);
   }
   LB2_CUDA(cudaGetLastError());
   return LB2_OK;
