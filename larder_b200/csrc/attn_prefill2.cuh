@@ -22,6 +22,8 @@
 //   warp 17    in the leader (rank 0) only, one elected thread issues every MMA of the pair: S_j = Q K_j^T into the S
 //              buffer and O += P_j V_j (A = P_j from TMEM), whichever is ready first, and commits completion to
 //              the barriers of both CTAs (one commit each). In both CTAs warp 17 allocates and frees the TMEM.
+// The grid is persistent: as many clusters as fit at once, each taking 256-row items (heaviest first) in turn; the
+// next item's Q, K and V loads and its first score MMA overlap the current item's last tiles and epilogue.
 // Causal is bottom-right as in the single-CTA kernel; the pair loops over the KV tiles its later rows need, the
 // earlier CTA's rows masking the last tile or two. Every wait is time-bounded; a wait that gives up sets the CTA's
 // abort flag, the roles drain what they issued, and both CTAs meet at a final cluster barrier before TMEM is freed.
@@ -186,6 +188,34 @@ __device__ __forceinline__ int kv_tiles2(const Params& p, int mt2) {
   return last <= 0 ? 0 : (last + BN - 1) / BN;
 }
 
+// Work item k of a pass, heaviest first; heads vary fastest so that neighbouring clusters share their KV head's
+// tiles in L2: the 256-row pair mt2 of (batch, query head) b, h.
+struct Item {
+  int b, h, hk, r0, ntiles;
+};
+
+template <int D>
+__device__ __forceinline__ Item item_of(const Params& p, int k, uint32_t rank) {
+  Item it;
+  const int bh = k % (p.B * p.Hq);
+  const int mt2 = p.mtiles - 1 - k / (p.B * p.Hq);
+  it.b = bh / p.Hq;
+  it.h = bh % p.Hq;
+  it.hk = it.h / p.G;
+  it.r0 = mt2 * 2 * BM + int(rank) * BM;  // this CTA's first row
+  it.ntiles = kv_tiles2<D>(p, mt2);
+  return it;
+}
+
+// The items of cluster c of nc: round r takes item r nc + c, every other round in reverse order (a snake over the
+// heaviest-first list), so that the clusters' totals even out.
+__device__ __forceinline__ int item_index(int r, int c, int nc) { return r * nc + ((r & 1) ? nc - 1 - c : c); }
+
+// Persistent: the grid holds as many clusters as fit at once, each looping over its items. Every role walks the same
+// item sequence; the K / V stage rings, the S and P buffers and their barriers run on counters that continue across
+// items. Two barriers hand resources from one item to the next: q_empty (the item's last score MMA has read Q, so
+// the next Q may land) and o_free (the epilogue has read O out of TMEM, so the next item's first PV may overwrite
+// it). Both count only items that have keys, so that no waiter can fall two phases behind.
 template <typename T, int D>
 __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant__ CUtensorMap qmap,
                                                             const __grid_constant__ CUtensorMap kmap,
@@ -200,19 +230,15 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
 
   const uint32_t rank = cluster_rank();
   const bool leader = rank == 0;
-  // Heaviest pairs first; heads vary fastest so that neighbouring clusters share their KV head's tiles in L2.
-  const int pair = blockIdx.x >> 1;
-  const int bh = pair % (p.B * p.Hq);
-  const int mt2 = p.mtiles - 1 - pair / (p.B * p.Hq);
-  const int b = bh / p.Hq, h = bh % p.Hq, hk = h / p.G;
-  const int r0 = mt2 * 2 * BM + int(rank) * BM;  // this CTA's first row
-  const int ntiles = kv_tiles2<D>(p, mt2);
+  const int cl = blockIdx.x >> 1, ncl = gridDim.x >> 1;
+  const int total = p.B * p.Hq * p.mtiles;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::BAR_OFF);
-  uint64_t* q_full = bars;            // [1]  leader: both Q halves landed
-  uint64_t* k_full = q_full + 1;      // [KS] leader: both K halves of the stage landed
+  uint64_t* q_full = bars;            // [1]  leader: both Q halves of the item landed
+  uint64_t* q_empty = q_full + 1;     // [1]  both CTAs: the item's score MMAs are done with Q
+  uint64_t* k_full = q_empty + 1;     // [KS] leader: both K halves of the stage landed
   uint64_t* k_empty = k_full + KS;    // [KS] both CTAs: the pair's MMA has read the stage
   uint64_t* v_full = k_empty + KS;    // [VS] leader
   uint64_t* v_empty = v_full + VS;    // [VS] both CTAs
@@ -220,14 +246,16 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
   uint64_t* s_free = s_full + C::SB;  // [SB] leader: all softmax warps of the pair have loaded S_j
   uint64_t* p_full = s_free + C::SB;  // [PB] leader: all softmax warps have written P_j into P buffer j % PB
   uint64_t* o_done = p_full + C::PB;  // [PB] both CTAs: PV_j complete (P buffer j % PB read)
-  uint64_t* drain = o_done + C::PB;   // [1]  leader
+  uint64_t* o_free = o_done + C::PB;  // [1]  leader: all softmax warps of the pair have read the item's O
+  uint64_t* drain = o_free + 1;       // [1]  leader
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(drain + 2);
-  static_assert((1 + 2 * KS + 2 * VS + 2 * C::SB + 2 * C::PB + 1) * 8 + 16 <= 256, "barrier area");
+  static_assert((2 + 2 * KS + 2 * VS + 2 * C::SB + 2 * C::PB + 2) * 8 + 16 <= 256, "barrier area");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int i = 0; i < KS; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
@@ -244,6 +272,7 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
       mbar_init(&p_full[i], 2 * SOFTMAX_WARPS);
       mbar_init(&o_done[i], 1);
     }
+    mbar_init(o_free, 2 * SOFTMAX_WARPS);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -261,14 +290,10 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
 
   if (warp == PRODUCER_WARP) {
     // ------------------------------------------------------------------------------------ TMA producers
-    if (lane < 2 && ntiles > 0) {
+    if (lane < 2) {
       if (lane == 0) {
         prefetch_tensormap(&qmap);
         prefetch_tensormap(&kmap);
-        if (leader) mbar_arrive_expect_tx(q_full, 2 * C::QBYTES);
-#pragma unroll
-        for (int db = 0; db < D / 64; ++db)
-          tma_load_4d_pair(sm + C::Q_OFF + db * BM * 128, &qmap, db * 64, r0, h, b, q_full);
       } else {
         prefetch_tensormap(&vmap);
       }
@@ -276,42 +301,66 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
       const int bytes = lane == 0 ? C::KHBYTES : C::VHBYTES;
       uint64_t* fullb = lane == 0 ? k_full : v_full;
       uint64_t* emptyb = lane == 0 ? k_empty : v_empty;
-      int issued = 0;
-      for (int j = 0; j < ntiles && !*abort_flag; ++j) {
-        const int st = j % NS;
-        if (j >= NS && !mbar_wait(&emptyb[st], ((j / NS) - 1) & 1, 41 + lane)) {
-          *abort_flag = 1;
-          break;
-        }
-        if (leader) mbar_arrive_expect_tx(&fullb[st], 2 * bytes);
-        if (lane == 0) {  // keys [j BN + rank HN, + HN), all D columns: D / 64 boxes of (64, HN)
-          uint8_t* dst = sm + C::K_OFF + st * C::KHBYTES;
+      int jg = 0, qi = 0, q_issued = -1;  // tiles issued on this lane's ring; items with keys so far; last Q item
+      bool stop = false;
+      for (int rr = 0; rr * ncl < total && !stop; ++rr) {
+        const int kidx = item_index(rr, cl, ncl);
+        if (kidx >= total) continue;
+        const Item itm = item_of<D>(p, kidx, rank);
+        if (itm.ntiles == 0) continue;
+        if (lane == 0) {  // Q of this item, once the previous item's score MMAs are done with the buffer
+          if (qi > 0 && !mbar_wait(q_empty, (qi - 1) & 1, 45)) {
+            *abort_flag = 1;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(q_full, 2 * C::QBYTES);
 #pragma unroll
           for (int db = 0; db < D / 64; ++db)
-            tma_load_4d_pair(dst + db * HN * 128, &kmap, db * 64, j * BN + int(rank) * HN, hk, b, &fullb[st]);
-        } else {  // keys [j BN, + BN), columns [rank HD, + HD): HD / 64 boxes of (64, BN)
-          uint8_t* dst = sm + C::V_OFF + st * C::VHBYTES;
-#pragma unroll
-          for (int db = 0; db < HD / 64; ++db)
-            tma_load_4d_pair(dst + db * BN * 128, &vmap, int(rank) * HD + db * 64, j * BN, hk, b, &fullb[st]);
+            tma_load_4d_pair(sm + C::Q_OFF + db * BM * 128, &qmap, db * 64, itm.r0, itm.h, itm.b, q_full);
+          q_issued = qi;
         }
-        issued = j + 1;
+        for (int j = 0; j < itm.ntiles; ++j, ++jg) {
+          if (*abort_flag) {
+            stop = true;
+            break;
+          }
+          const int st = jg % NS;
+          if (jg >= NS && !mbar_wait(&emptyb[st], ((jg / NS) - 1) & 1, 41 + lane)) {
+            *abort_flag = 1;
+            stop = true;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&fullb[st], 2 * bytes);
+          if (lane == 0) {  // keys [j BN + rank HN, + HN), all D columns: D / 64 boxes of (64, HN)
+            uint8_t* dst = sm + C::K_OFF + st * C::KHBYTES;
+#pragma unroll
+            for (int db = 0; db < D / 64; ++db)
+              tma_load_4d_pair(dst + db * HN * 128, &kmap, db * 64, j * BN + int(rank) * HN, itm.hk, itm.b,
+                               &fullb[st]);
+          } else {  // keys [j BN, + BN), columns [rank HD, + HD): HD / 64 boxes of (64, BN)
+            uint8_t* dst = sm + C::V_OFF + st * C::VHBYTES;
+#pragma unroll
+            for (int db = 0; db < HD / 64; ++db)
+              tma_load_4d_pair(dst + db * BN * 128, &vmap, int(rank) * HD + db * 64, j * BN, itm.hk, itm.b,
+                               &fullb[st]);
+          }
+        }
+        ++qi;
       }
       // Drain (leader only: the loads of both CTAs complete on its barriers): everything issued has landed.
       if (leader) {
-        if (lane == 0) mbar_wait(q_full, 0, 43);
-        for (int j = max(0, issued - NS); j < issued; ++j) mbar_wait(&fullb[j % NS], (j / NS) & 1, 44);
+        if (lane == 0 && q_issued >= 0) mbar_wait(q_full, q_issued & 1, 43);
+        for (int g = max(0, jg - NS); g < jg; ++g) mbar_wait(&fullb[g % NS], (g / NS) & 1, 44);
       }
     }
   } else if (warp == MMA_WARP) {
     // ------------------------------------------------------------------------------------ MMA issuer (leader)
-    if (leader && ntiles > 0) {
+    if (leader) {
       const bool elected = elect_one();
       if (elected) {
         const uint32_t q_addr = smem_u32(sm + C::Q_OFF);
-        bool ok = mbar_wait(q_full, 0, 51);
-        auto issue_s = [&](int j) {
-          const int st = j % KS, sb = j % C::SB;
+        auto issue_s = [&](int g) {
+          const int st = g % KS, sb = g % C::SB;
           prefill::tc_fence_after();
           const uint32_t k_addr = smem_u32(sm + C::K_OFF + st * C::KHBYTES);
 #pragma unroll
@@ -323,51 +372,64 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
           umma2_commit_both(&s_full[sb]);
           umma2_commit_both(&k_empty[st]);
         };
-        auto issue_pv = [&](int i) {
-          const int st = i % VS, pb = i % C::PB;
+        auto issue_pv = [&](int g, bool first) {
+          const int st = g % VS, pb = g % C::PB;
           prefill::tc_fence_after();
           const uint32_t v_addr = smem_u32(sm + C::V_OFF + st * C::VHBYTES);
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk) {
             const uint64_t bd = prefill::sdesc(v_addr + kk * 16 * 128, BN * 128, 1024);
             umma2_ts(tmem + C::O_COL, tmem + C::P_COL + pb * (BN / 2) + kk * 8, bd, IDESC_PV,
-                     (i > 0 || kk > 0) ? 1u : 0u);
+                     (!first || kk > 0) ? 1u : 0u);
           }
-          umma2_commit_both(&o_done[pb]);  // PV_i read P buffer i % PB
+          umma2_commit_both(&o_done[pb]);  // PV_g read P buffer g % PB
           umma2_commit_both(&v_empty[st]);
         };
-        int js = 0, jp = 0;
-        uint64_t t0 = 0;
-        for (uint32_t it = 1; ok && jp < ntiles; ++it) {
-          if (jp < js && mbar_test_wait_cluster(&v_full[jp % VS], (jp / VS) & 1) &&
-              mbar_test_wait_cluster(&p_full[jp % C::PB], (jp / C::PB) & 1)) {
-            issue_pv(jp++);
-            t0 = 0;
-            continue;
-          }
-          if (js < ntiles && mbar_test_wait_cluster(&k_full[js % KS], (js / KS) & 1) &&
-              (js < C::SB || mbar_test_wait_cluster(&s_free[js % C::SB], ((js / C::SB) - 1) & 1))) {
-            issue_s(js++);
-            t0 = 0;
-            continue;
-          }
-          // Nothing ready: back off briefly, so that this polling thread does not take issue slots and MIO
-          // bandwidth from the softmax warps that share its SM sub-partition.
-          __nanosleep(20);
-          if ((it & 15) == 0) {
-            if (*abort_flag) {
-              ok = false;
-              break;
+        bool ok = true;
+        int js_g = 0, jp_g = 0, qi = 0;  // S and PV tiles issued; items with keys so far
+        for (int rr = 0; ok && rr * ncl < total; ++rr) {
+          const int kidx = item_index(rr, cl, ncl);
+          if (kidx >= total) continue;
+          const int nt = kv_tiles2<D>(p, p.mtiles - 1 - kidx / (p.B * p.Hq));
+          if (nt == 0) continue;
+          ok = mbar_wait(q_full, qi & 1, 51);
+          bool o_ok = qi == 0;  // O may be overwritten by this item's first PV
+          int js = 0, jp = 0;
+          uint64_t t0 = 0;
+          for (uint32_t it = 1; ok && jp < nt; ++it) {
+            if (jp < js && (jp > 0 || o_ok || (o_ok = mbar_test_wait_cluster(o_free, (qi - 1) & 1))) &&
+                mbar_test_wait_cluster(&v_full[jp_g % VS], (jp_g / VS) & 1) &&
+                mbar_test_wait_cluster(&p_full[jp_g % C::PB], (jp_g / C::PB) & 1)) {
+              issue_pv(jp_g++, jp++ == 0);
+              t0 = 0;
+              continue;
             }
-            const uint64_t now = globaltimer_ns();
-            if (t0 == 0) {
-              t0 = now;
-            } else if (now - t0 > kWaitNs) {
-              report_timeout(52);
-              ok = false;
-              break;
+            if (js < nt && mbar_test_wait_cluster(&k_full[js_g % KS], (js_g / KS) & 1) &&
+                (js_g < C::SB || mbar_test_wait_cluster(&s_free[js_g % C::SB], ((js_g / C::SB) - 1) & 1))) {
+              issue_s(js_g++);
+              if (++js == nt) umma2_commit_both(q_empty);  // the item's score MMAs are done with Q
+              t0 = 0;
+              continue;
+            }
+            // Nothing ready: back off briefly, so that this polling thread does not take issue slots and MIO
+            // bandwidth from the softmax warps that share its SM sub-partition.
+            __nanosleep(20);
+            if ((it & 15) == 0) {
+              if (*abort_flag) {
+                ok = false;
+                break;
+              }
+              const uint64_t now = globaltimer_ns();
+              if (t0 == 0) {
+                t0 = now;
+              } else if (now - t0 > kWaitNs) {
+                report_timeout(52);
+                ok = false;
+                break;
+              }
             }
           }
+          ++qi;
         }
         if (!ok) *abort_flag = 1;
         asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -381,173 +443,212 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
     // ------------------------------------------------------------------------------------ softmax warps
     constexpr int HC = BN / NG;  // S columns (keys) a thread owns
     constexpr int DH = D / NG;   // O columns a thread owns
+    static_assert(HC == 32, "a softmax thread loads 32 S columns");
     const int r = 32 * (warp & 3) + lane;
     const int grp = warp >> 2;
-    const int row = r0 + r;
     const uint32_t lane_base = tmem + (uint32_t(32 * (warp & 3)) << 16);
     const uint32_t grp_bar = 2 + (warp & 3);  // named barrier of the NG warps of a lane quarter (ids 2..5)
     float* red = reinterpret_cast<float*>(sm + C::RED_OFF);
     const uint32_t s_free_l = mapa(smem_u32(s_free), 0), p_full_l = mapa(smem_u32(p_full), 0);
-    const int lim = p.mask_kind == LB2_MASK_CAUSAL ? p.N - p.T + row : p.N - 1;
-    const uint8_t* mrow = (p.mask_kind == LB2_MASK_ARRAY && row < p.T) ? p.mask + int64_t(row) * p.m_st[0] : nullptr;
-    float m_run = -INFINITY, l_run = 0.f;
+    const uint32_t o_free_l = mapa(smem_u32(o_free), 0);
     bool ok = true;
-    for (int j = 0; j < ntiles; ++j) {
-      const int sb = j % C::SB;
-      bool okj = ok && !*abort_flag && mbar_wait(&s_full[sb], (j / C::SB) & 1, 61);
-      okj = __all_sync(0xffffffffu, okj);
-      float s[HC];
-      if (okj) {
+    int jg = 0;  // S tiles consumed so far (the MMA issuer's S and PV counters follow the same sequence)
+    for (int rr = 0; ok && rr * ncl < total; ++rr) {
+      const int kidx = item_index(rr, cl, ncl);
+      if (kidx >= total) continue;
+      const Item itm = item_of<D>(p, kidx, rank);
+      const int ntiles = itm.ntiles;
+      const int row = itm.r0 + r;
+      const int lim = p.mask_kind == LB2_MASK_CAUSAL ? p.N - p.T + row : p.N - 1;
+      const uint8_t* mrow =
+          (p.mask_kind == LB2_MASK_ARRAY && row < p.T) ? p.mask + int64_t(row) * p.m_st[0] : nullptr;
+      float m_run = -INFINITY, l_run = 0.f;
+      for (int j = 0; j < ntiles; ++j) {
+        const int g = jg + j;
+        const int sb = g % C::SB;
+        bool okj = ok && !*abort_flag && mbar_wait(&s_full[sb], (g / C::SB) & 1, 61);
+        okj = __all_sync(0xffffffffu, okj);
+        float s[HC];
+        if (okj) {
+          prefill::tc_fence_after();
+          prefill::tmem_ld32(lane_base + C::S_COL + sb * BN + grp * HC, s);
+          prefill::tmem_wait_ld();
+          prefill::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(s_free_l + 8u * sb);
+        } else {
+#pragma unroll
+          for (int c = 0; c < HC; ++c) s[c] = -INFINITY;
+        }
+        const int key0 = j * BN + grp * HC;
+        const bool full_tile = j * BN + BN - 1 <= lim && j * BN + BN <= p.N && !mrow;
+        if (!full_tile) {
+#pragma unroll
+          for (int c = 0; c < HC; ++c) {
+            const int key = key0 + c;
+            bool vis = key <= lim && key < p.N;
+            if (mrow && vis) vis = mrow[int64_t(key) * p.m_st[1]] != 0;
+            s[c] = vis ? s[c] : -INFINITY;
+          }
+        }
+        // P_j with the running max, in the same pass as the tile max: the running max moves only when a row's tile
+        // max exceeds it by more than 2^8, so these are the final values unless the check below says otherwise
+        // (then the rows that move recompute theirs).
+        float nm = m_run == -INFINITY ? 0.f : -m_run;
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        float ls4[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t pk[HC / 2];
+#pragma unroll
+        for (int c = 0; c < HC; c += 2) {
+          mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
+          mx4[(c + 1) & 3] = fmaxf(mx4[(c + 1) & 3], s[c + 1]);
+          const float e0 = prefill::ex2f(fmaf(s[c], p.scale_log2, nm));
+          const float e1 = prefill::ex2f(fmaf(s[c + 1], p.scale_log2, nm));
+          ls4[c & 3] += e0;
+          ls4[(c + 1) & 3] += e1;
+          pk[c / 2] = pack2<T>(e0, e1);
+        }
+        float tmax = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+        // one barrier of the quarter's NG warps: does any of their rows want to move its max (or did a wait fail)?
+        const bool want = !okj || tmax * p.scale_log2 > m_run + 8.f;
+        uint32_t any_want;
+        asm volatile(
+            "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+            "bar.red.or.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+            : "=r"(any_want)
+            : "r"(uint32_t(want)), "r"(grp_bar), "n"(NG * 32)
+            : "memory");
+        if (any_want) {
+          red[grp * BM + r] = tmax;
+          uint32_t all_ok;
+          asm volatile(
+              "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+              "bar.red.and.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+              : "=r"(all_ok)
+              : "r"(uint32_t(okj)), "r"(grp_bar), "n"(NG * 32)
+              : "memory");
+#pragma unroll
+          for (int g2 = 0; g2 < NG; ++g2) tmax = fmaxf(tmax, red[g2 * BM + r]);
+          asm volatile("bar.sync %0, %1;" ::"r"(grp_bar), "n"(NG * 32));
+          if (!all_ok) {
+            ok = false;
+            break;
+          }
+          const float tmax2 = tmax * p.scale_log2;
+          const bool move = tmax2 > m_run + 8.f;
+          const float factor = move ? prefill::ex2f(m_run - tmax2) : 1.f;
+          if (__any_sync(0xffffffffu, move && j > 0 && l_run > 0.f)) {
+            if (!mbar_wait(&o_done[(g - 1) % C::PB], ((g - 1) / C::PB) & 1, 62)) ok = false;
+            prefill::tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < DH; c += 16) {  // (16 columns at a time: S and P stay in registers meanwhile)
+              float ov[16];
+              tmem_ld16(lane_base + C::O_COL + grp * DH + c, ov);
+              prefill::tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 16; ++e) ov[e] *= factor;
+              prefill::tmem_st16(lane_base + C::O_COL + grp * DH + c, reinterpret_cast<const uint32_t*>(ov));
+            }
+            prefill::tmem_wait_st();
+          }
+          if (move) {  // this row's P with its new max
+            l_run *= factor;
+            m_run = tmax2;
+            nm = -m_run;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) ls4[c] = 0.f;
+#pragma unroll
+            for (int c = 0; c < HC; c += 2) {
+              const float e0 = prefill::ex2f(fmaf(s[c], p.scale_log2, nm));
+              const float e1 = prefill::ex2f(fmaf(s[c + 1], p.scale_log2, nm));
+              ls4[c & 3] += e0;
+              ls4[(c + 1) & 3] += e1;
+              pk[c / 2] = pack2<T>(e0, e1);
+            }
+          }
+        }
+        // P_j into P buffer g % PB (last read by PV_{g-PB}): this group's HC keys at columns grp HC / 2 ...
+        const int pbuf = g % C::PB;
+        if (g >= C::PB && !mbar_wait(&o_done[pbuf], ((g / C::PB) - 1) & 1, 64)) ok = false;
         prefill::tc_fence_after();
-        static_assert(HC == 32, "a softmax thread loads 32 S columns");
-        prefill::tmem_ld32(lane_base + C::S_COL + sb * BN + grp * HC, s);
-        prefill::tmem_wait_ld();
+        prefill::tmem_st16(lane_base + C::P_COL + pbuf * (BN / 2) + grp * (HC / 2), pk);
+        l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
+        prefill::tmem_wait_st();
         prefill::tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(s_free_l + 8u * sb);
-      } else {
-#pragma unroll
-        for (int c = 0; c < HC; ++c) s[c] = -INFINITY;
+        if (lane == 0) mbar_arrive_cluster(p_full_l + 8u * pbuf);
       }
-      const int key0 = j * BN + grp * HC;
-      const bool full_tile = j * BN + BN - 1 <= lim && j * BN + BN <= p.N && !mrow;
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      if (full_tile) {
-#pragma unroll
-        for (int c = 0; c < HC; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
-      } else {
-#pragma unroll
-        for (int c = 0; c < HC; ++c) {
-          const int key = key0 + c;
-          bool vis = key <= lim && key < p.N;
-          if (mrow && vis) vis = mrow[int64_t(key) * p.m_st[1]] != 0;
-          s[c] = vis ? s[c] : -INFINITY;
-          mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
-        }
+      if (ok && ntiles > 0) {
+        const int gl = jg + ntiles - 1;  // the item's last PV
+        if (!mbar_wait(&o_done[gl % C::PB], (gl / C::PB) & 1, 63)) ok = false;
+        prefill::tc_fence_after();
       }
-      float tmax = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-      // one barrier of the quarter's NG warps: does any of their rows want to move its max (or did a wait fail)?
-      const bool want = !okj || tmax * p.scale_log2 > m_run + 8.f;
-      uint32_t any_want;
-      asm volatile(
-          "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
-          "bar.red.or.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
-          : "=r"(any_want)
-          : "r"(uint32_t(want)), "r"(grp_bar), "n"(NG * 32)
-          : "memory");
-      bool move = false;
-      float tmax2 = 0.f;
-      if (any_want) {
-        red[grp * BM + r] = tmax;
+      // -------------------------------------------------------------------------------- epilogue of the item
+      ok = __all_sync(0xffffffffu, ok);
+      float l_tot = 0.f;
+      if (ntiles > 0) {  // (an item without keys skips the exchange, whose buffer the quarter may still be reading)
+        red[grp * BM + r] = l_run;
+        // the quarter's warps agree on ok, so that all of them leave the item loop together or none does
         uint32_t all_ok;
         asm volatile(
             "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
             "bar.red.and.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
             : "=r"(all_ok)
-            : "r"(uint32_t(okj)), "r"(grp_bar), "n"(NG * 32)
+            : "r"(uint32_t(ok)), "r"(grp_bar), "n"(NG * 32)
             : "memory");
+        ok = all_ok != 0;
 #pragma unroll
-        for (int g2 = 0; g2 < NG; ++g2) tmax = fmaxf(tmax, red[g2 * BM + r]);
-        asm volatile("bar.sync %0, %1;" ::"r"(grp_bar), "n"(NG * 32));
-        if (!all_ok) {
-          ok = false;
-          break;
-        }
-        tmax2 = tmax * p.scale_log2;
-        move = tmax2 > m_run + 8.f;
+        for (int g2 = 0; g2 < NG; ++g2) l_tot += red[g2 * BM + r];
       }
-      const float factor = move ? prefill::ex2f(m_run - tmax2) : 1.f;
-      if (__any_sync(0xffffffffu, move && j > 0 && l_run > 0.f)) {
-        if (!mbar_wait(&o_done[(j - 1) % C::PB], ((j - 1) / C::PB) & 1, 62)) ok = false;
-        prefill::tc_fence_after();
+      const bool have_o = ntiles > 0 && ok;
+      const bool store = row < p.T;
+      T* orow = reinterpret_cast<T*>(p.o) + itm.b * p.o_st[0] + int64_t(itm.h) * p.o_st[1] + int64_t(row) * p.o_st[2] +
+                grp * DH;
+      const T* grow = p.gate ? reinterpret_cast<const T*>(p.gate) + itm.b * p.g_st[0] + int64_t(itm.h) * p.g_st[1] +
+                                   int64_t(row) * p.g_st[2] + grp * DH
+                             : nullptr;
+      const float inv = (have_o && l_tot > 0.f) ? 1.f / l_tot : 0.f;
 #pragma unroll 1
-        for (int c = 0; c < DH; c += 32) {
-          float ov[32];
+      for (int c = 0; c < DH; c += 32) {
+        float ov[32];
+        if (have_o) {
           prefill::tmem_ld32(lane_base + C::O_COL + grp * DH + c, ov);
           prefill::tmem_wait_ld();
+        } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) ov[e] *= factor;
-          prefill::tmem_st32(lane_base + C::O_COL + grp * DH + c, ov);
+          for (int e = 0; e < 32; ++e) ov[e] = 0.f;
         }
-        prefill::tmem_wait_st();
-      }
-      if (move) {
-        l_run *= factor;
-        m_run = tmax2;
-      }
-      // P_j into P buffer j % PB (last read by PV_{j-PB}): this group's HC keys at columns grp HC / 2 ...
-      const int pbuf = j % C::PB;
-      if (j >= C::PB && !mbar_wait(&o_done[pbuf], ((j / C::PB) - 1) & 1, 64)) ok = false;
-      prefill::tc_fence_after();
-      const float nm = m_run == -INFINITY ? 0.f : -m_run;
-      float ls4[4] = {0.f, 0.f, 0.f, 0.f};
-      uint32_t pk[HC / 2];
+        if (!store) continue;
 #pragma unroll
-      for (int c = 0; c < HC; c += 2) {
-        const float e0 = prefill::ex2f(fmaf(s[c], p.scale_log2, nm));
-        const float e1 = prefill::ex2f(fmaf(s[c + 1], p.scale_log2, nm));
-        ls4[c & 3] += e0;
-        ls4[(c + 1) & 3] += e1;
-        pk[c / 2] = pack2<T>(e0, e1);
-      }
-      prefill::tmem_st16(lane_base + C::P_COL + pbuf * (BN / 2) + grp * (HC / 2), pk);
-      l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
-      prefill::tmem_wait_st();
-      prefill::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(p_full_l + 8u * pbuf);
-    }
-    if (ok && ntiles > 0) {
-      if (!mbar_wait(&o_done[(ntiles - 1) % C::PB], ((ntiles - 1) / C::PB) & 1, 63)) ok = false;
-      prefill::tc_fence_after();
-    }
-    // ---------------------------------------------------------------------------------- epilogue
-    ok = __all_sync(0xffffffffu, ok);
-    red[grp * BM + r] = l_run;
-    asm volatile("bar.sync %0, %1;" ::"r"(grp_bar), "n"(NG * 32));
-    float l_tot = 0.f;
+        for (int e = 0; e < 32; e += 8) {
+          float x[8];
 #pragma unroll
-    for (int g2 = 0; g2 < NG; ++g2) l_tot += red[g2 * BM + r];
-    const bool have_o = ntiles > 0 && ok;
-    const bool store = row < p.T;
-    T* orow = reinterpret_cast<T*>(p.o) + b * p.o_st[0] + int64_t(h) * p.o_st[1] + int64_t(row) * p.o_st[2] + grp * DH;
-    const T* grow = p.gate ? reinterpret_cast<const T*>(p.gate) + b * p.g_st[0] + int64_t(h) * p.g_st[1] +
-                                 int64_t(row) * p.g_st[2] + grp * DH
-                           : nullptr;
-    const float inv = (have_o && l_tot > 0.f) ? 1.f / l_tot : 0.f;
-#pragma unroll 1
-    for (int c = 0; c < DH; c += 32) {
-      float ov[32];
-      if (have_o) {
-        prefill::tmem_ld32(lane_base + C::O_COL + grp * DH + c, ov);
-        prefill::tmem_wait_ld();
-      } else {
+          for (int u = 0; u < 8; ++u) x[u] = ov[e + u] * inv;
+          if (grow) {
+            const uint4 gv = *reinterpret_cast<const uint4*>(grow + c + e);
+            const T* gh = reinterpret_cast<const T*>(&gv);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) ov[e] = 0.f;
-      }
-      if (!store) continue;
-#pragma unroll
-      for (int e = 0; e < 32; e += 8) {
-        float x[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) x[u] = ov[e + u] * inv;
-        if (grow) {
-          const uint4 gv = *reinterpret_cast<const uint4*>(grow + c + e);
-          const T* gh = reinterpret_cast<const T*>(&gv);
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const float z = to_f<T>(gh[u]);
-            x[u] = x[u] / (1.f + __expf(-z));
+            for (int u = 0; u < 8; ++u) {
+              const float z = to_f<T>(gh[u]);
+              x[u] = x[u] / (1.f + __expf(-z));
+            }
           }
+          uint4 pk4;
+          pk4.x = pack2<T>(x[0], x[1]);
+          pk4.y = pack2<T>(x[2], x[3]);
+          pk4.z = pack2<T>(x[4], x[5]);
+          pk4.w = pack2<T>(x[6], x[7]);
+          *reinterpret_cast<uint4*>(orow + c + e) = pk4;
         }
-        uint4 pk4;
-        pk4.x = pack2<T>(x[0], x[1]);
-        pk4.y = pack2<T>(x[2], x[3]);
-        pk4.z = pack2<T>(x[4], x[5]);
-        pk4.w = pack2<T>(x[6], x[7]);
-        *reinterpret_cast<uint4*>(orow + c + e) = pk4;
       }
+      if (ntiles > 0) {  // O is read: the next item's first PV may overwrite it
+        prefill::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(o_free_l);
+      }
+      jg += ntiles;
     }
+    if (!ok) *abort_flag = 1;
   }
 
   // The leader's MMAs read this CTA's shared memory and TMEM: neither CTA frees anything before both are done.

@@ -296,20 +296,13 @@ static int map4(CUtensorMap* m, const void* base, const int64_t* st, int B, int 
 
 namespace prefill2 {
 
-// Clusters of two CTAs (one 256-row pair each), heaviest pairs first.
+// Persistent clusters of two CTAs: as many as fit on the device at once (at most one a 256-row item), each looping
+// over its items.
 template <typename T, int D>
 static int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const Params& p,
                   cudaStream_t st) {
   auto kern = fmha2_kernel<T, D>;
-  static int attr_dev = -1;
-  int dev = 0;
-  LB2_CUDA(cudaGetDevice(&dev));
-  if (attr_dev != dev) {
-    LB2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM_BYTES));
-    attr_dev = dev;
-  }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(unsigned(2 * p.B * p.Hq * p.mtiles));
   cfg.blockDim = dim3(THREADS);
   cfg.dynamicSmemBytes = Cfg<D>::SMEM_BYTES;
   cfg.stream = st;
@@ -320,6 +313,18 @@ static int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMa
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  static int attr_dev = -1, max_clusters = 0;
+  int dev = 0;
+  LB2_CUDA(cudaGetDevice(&dev));
+  if (attr_dev != dev) {
+    LB2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM_BYTES));
+    cfg.gridDim = dim3(2);
+    LB2_CUDA(cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg));
+    if (max_clusters < 1) return fail(LB2_ECUDA, "prefill: no 2-CTA cluster of the pair kernel fits the device");
+    attr_dev = dev;
+  }
+  const int64_t items = int64_t(p.B) * p.Hq * p.mtiles;
+  cfg.gridDim = dim3(unsigned(2 * std::min<int64_t>(items, max_clusters)));
   LB2_CUDA(cudaLaunchKernelEx(&cfg, kern, qm, km, vm, p));
   return LB2_OK;
 }
