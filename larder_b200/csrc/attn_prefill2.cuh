@@ -1,13 +1,13 @@
-// Prefill attention on a pair of CTAs (a 2-CTA cluster sharing each MMA: tcgen05 cta_group::2), head dim 256.
+// Prefill attention on a pair of CTAs (a 2-CTA cluster sharing each MMA: tcgen05 cta_group::2), head dims 128, 256.
 //
 // The single-CTA kernel (attn_prefill.cuh) reads every K and V byte once per 128 query rows; at head dim 256 each
 // SM then streams 64 KB of K/V from L2 per 64-key tile and the L2 -> shared memory transfer, not the tensor cores,
 // sets the pace. Here the two CTAs of a cluster take 256 consecutive rows of one head (128 each) and one MMA
 // instruction covers both (M = 256): matrix A (Q for the scores, P for the output) stays split by rows, one half in
 // each CTA, and matrix B is split along N, so each CTA loads only HALF of every K tile (64 of its 128 keys) and HALF
-// of every V tile (128 of its 256 columns). Per SM that halves the K/V bytes per FLOP. Tiles of 128 keys make the
-// score MMAs N = 128 wide and halve the per-tile handshakes of the softmax; TMEM then holds one S buffer (128
-// columns), two P buffers (64 each) and O (256).
+// of every V tile (D / 2 of its D columns). Per SM that halves the K/V bytes per FLOP. Tiles of 128 keys make the
+// score MMAs N = 128 wide and halve the per-tile handshakes of the softmax; at head dim 256 TMEM then holds one S
+// buffer (128 columns), two P buffers (64 each) and O (256); at head dim 128, two S buffers, two P buffers and O.
 //
 // Roles (576 threads a CTA):
 //   warps 0-15 softmax + epilogue on the CTA's own 128 rows (TMEM lane r = row r of its S, P and O): warp w serves
@@ -52,23 +52,24 @@ struct Cfg {
   static constexpr int QBYTES = BM * D * 2;
   static constexpr int KHBYTES = HN * D * 2;    // a CTA's half of a K tile
   static constexpr int VHBYTES = BN * HD * 2;   // a CTA's half of a V tile
-  static constexpr int KS = 2;
-  static constexpr int VS = 2;
+  static constexpr int KS = D == 256 ? 2 : 4;   // K / V stages (32 KB halves at head dim 256, 16 KB at 128)
+  static constexpr int VS = KS;
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_OFF + QBYTES;
   static constexpr int V_OFF = K_OFF + KS * KHBYTES;
   static constexpr int BAR_OFF = V_OFF + VS * VHBYTES;
   static constexpr int RED_OFF = BAR_OFF + 256;  // [NG groups][128 rows] fp32
   static constexpr int SMEM_BYTES = RED_OFF + NG * BM * 4 + 1024;
-  static constexpr int SB = 1;                    // S buffers: the softmax copies S_j to registers at once, so
-                                                  // S_{j+1} can overwrite it while P_j is still being formed
+  // S buffers: the softmax copies S_j to registers at once, so S_{j+1} can overwrite it while P_j is still being
+  // formed; at head dim 128 O leaves TMEM room for a second buffer, and S_{j+1} no longer waits for that copy.
+  static constexpr int SB = D == 256 ? 1 : 2;
   static constexpr int PB = 2;                    // P buffers
   static constexpr int S_COL = 0;                 // S buffers [b BN, (b + 1) BN), b < SB
   static constexpr int P_COL = SB * BN;           // P buffers [P_COL + b BN / 2, ...), b < PB
   static constexpr int O_COL = P_COL + PB * BN / 2;  // O [O_COL, O_COL + D)
   static_assert(O_COL + D <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
-  static_assert(D == 256, "the pair kernel is built for head dim 256");
+  static_assert(D == 128 || D == 256, "the pair kernel is built for head dims 128 and 256");
 };
 
 // ---------------------------------------------------------------------------------------------- cluster helpers
@@ -411,9 +412,20 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
               t0 = 0;
               continue;
             }
-            // Nothing ready: back off briefly, so that this polling thread does not take issue slots and MIO
-            // bandwidth from the softmax warps that share its SM sub-partition.
-            __nanosleep(20);
+            // Nothing ready: sleep on the barrier that gates the next MMA in the usual order (S_{j+SB} needs the
+            // softmax to have loaded S_j, which precedes P_j), so that this thread takes no issue slots from the
+            // softmax warps sharing its SM sub-partition and still wakes the moment that barrier completes.
+            if (jp < js && (js >= nt || js - jp > C::SB)) {
+              if (!mbar_test_wait_cluster(&p_full[jp_g % C::PB], (jp_g / C::PB) & 1))
+                mbar_try_wait_hint(&p_full[jp_g % C::PB], (jp_g / C::PB) & 1, 1000);
+              else
+                mbar_try_wait_hint(&v_full[jp_g % VS], (jp_g / VS) & 1, 1000);
+            } else if (js < nt) {
+              if (js_g >= C::SB && !mbar_test_wait_cluster(&s_free[js_g % C::SB], ((js_g / C::SB) - 1) & 1))
+                mbar_try_wait_hint(&s_free[js_g % C::SB], ((js_g / C::SB) - 1) & 1, 1000);
+              else
+                mbar_try_wait_hint(&k_full[js_g % KS], (js_g / KS) & 1, 1000);
+            }
             if ((it & 15) == 0) {
               if (*abort_flag) {
                 ok = false;
@@ -491,26 +503,23 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
             s[c] = vis ? s[c] : -INFINITY;
           }
         }
-        // P_j with the running max, in the same pass as the tile max: the running max moves only when a row's tile
-        // max exceeds it by more than 2^8, so these are the final values unless the check below says otherwise
-        // (then the rows that move recompute theirs).
+        // P_j with the running max. The running max moves only when a row's tile max exceeds it by more than 2^8,
+        // i.e. when some P of the row exceeds 2^8; P >= 0, so a thread whose P sum is at most 2^8 has no such
+        // element and skips the max altogether. Otherwise (or before the row's first key) the exact check below
+        // runs, and the rows that move recompute their P.
         float nm = m_run == -INFINITY ? 0.f : -m_run;
-        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         float ls4[4] = {0.f, 0.f, 0.f, 0.f};
         uint32_t pk[HC / 2];
 #pragma unroll
         for (int c = 0; c < HC; c += 2) {
-          mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
-          mx4[(c + 1) & 3] = fmaxf(mx4[(c + 1) & 3], s[c + 1]);
           const float e0 = prefill::ex2f(fmaf(s[c], p.scale_log2, nm));
           const float e1 = prefill::ex2f(fmaf(s[c + 1], p.scale_log2, nm));
           ls4[c & 3] += e0;
           ls4[(c + 1) & 3] += e1;
           pk[c / 2] = pack2<T>(e0, e1);
         }
-        float tmax = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
         // one barrier of the quarter's NG warps: does any of their rows want to move its max (or did a wait fail)?
-        const bool want = !okj || tmax * p.scale_log2 > m_run + 8.f;
+        const bool want = !okj || m_run == -INFINITY || !((ls4[0] + ls4[1]) + (ls4[2] + ls4[3]) <= 256.f);
         uint32_t any_want;
         asm volatile(
             "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
@@ -519,6 +528,10 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
             : "r"(uint32_t(want)), "r"(grp_bar), "n"(NG * 32)
             : "memory");
         if (any_want) {
+          float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+          for (int c = 0; c < HC; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
+          float tmax = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
           red[grp * BM + r] = tmax;
           uint32_t all_ok;
           asm volatile(
@@ -607,7 +620,7 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
       const T* grow = p.gate ? reinterpret_cast<const T*>(p.gate) + itm.b * p.g_st[0] + int64_t(itm.h) * p.g_st[1] +
                                    int64_t(row) * p.g_st[2] + grp * DH
                              : nullptr;
-      const float inv = (have_o && l_tot > 0.f) ? 1.f / l_tot : 0.f;
+      const float inv = (have_o && m_run != -INFINITY && l_tot > 0.f) ? 1.f / l_tot : 0.f;
 #pragma unroll 1
       for (int c = 0; c < DH; c += 32) {
         float ov[32];

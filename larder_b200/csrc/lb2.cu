@@ -521,8 +521,10 @@ int lb2_attn_prefill(const void* q, const int64_t* q_st, const void* k, const in
   }
   LB2_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o) && (!gate || aligned16(gate)),
                 "prefill: tensors must be 16-byte aligned");
-  // Head dim 256 over more than one row tile runs on CTA pairs (each CTA loads half of every K and V tile).
-  const bool pair = D == 256 && T > prefill::BM;
+  // Head dims 128 and 256 over more than one row tile run on CTA pairs (each CTA loads half of every K and V tile).
+  const bool pair = (D == 128 || D == 256) && T > prefill::BM;
+  static_assert(prefill2::Cfg<128>::HN == prefill2::Cfg<256>::HN && prefill2::Cfg<128>::BN == prefill2::Cfg<256>::BN,
+                "one K / V box height for both pair head dims");
   CUtensorMap qm, km, vm;
   const int BN = D == 256 ? prefill::Cfg<256>::BN : prefill::Cfg<128>::BN;
   int rc = prefill::map4(&qm, q, q_st, B, Hq, T, D, dtype, prefill::BM);
@@ -549,9 +551,13 @@ int lb2_attn_prefill(const void* q, const int64_t* q_st, const void* k, const in
   p.mtiles = pair ? (T + 2 * prefill::BM - 1) / (2 * prefill::BM) : (T + prefill::BM - 1) / prefill::BM;
   p.scale_log2 = scale * 1.4426950408889634f;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (pair)
+  if (pair) {
+    if (D == 128)
+      return dtype == LB2_BF16 ? prefill2::launch<__nv_bfloat16, 128>(qm, km, vm, p, st)
+                               : prefill2::launch<__half, 128>(qm, km, vm, p, st);
     return dtype == LB2_BF16 ? prefill2::launch<__nv_bfloat16, 256>(qm, km, vm, p, st)
                              : prefill2::launch<__half, 256>(qm, km, vm, p, st);
+  }
   if (dtype == LB2_BF16) {
     if (D == 64) return prefill::launch<__nv_bfloat16, 64>(qm, km, vm, p, st);
     if (D == 128) return prefill::launch<__nv_bfloat16, 128>(qm, km, vm, p, st);
