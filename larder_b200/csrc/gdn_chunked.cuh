@@ -18,8 +18,9 @@
 //        beta V) formed from the 16-bit tiles on the fly; writes W, U', M, gamma, Gam to the workspace.
 //   scan (grid: Dv / 32 value-row blocks x v-heads x batch, 8 warps): the state slice S[32 x 128] in fp32
 //        registers (a TF32 copy in shared memory for the products that read all of it), chunks in order, each
-//        chunk's workspace tiles prefetched with cp.async while the previous chunk computes; U, Y and the state
-//        update on TF32 mma.sync with fp32 accumulation. W and M are stored already rounded to TF32 by prep.
+//        chunk's tiles prefetched by bulk copies (the workspace is laid out as the shared-memory tiles) while the
+//        previous chunk computes; U, Y and the state update on TF32 mma.sync with fp32 accumulation. W and M are
+//        stored already rounded to TF32 by prep.
 #pragma once
 
 #include "common.cuh"
@@ -31,12 +32,21 @@ constexpr int C = 64;
 constexpr int DK = 128;
 constexpr int DV = 128;
 constexpr int DVB = 32;   // value rows a scan CTA owns
-constexpr int UNIT = C * DK + C * DV + C * C + 2 * C;  // workspace floats a (batch, head, chunk)
 constexpr int KP = 136;   // bf16 row stride of K / Q tiles (conflict-free ldmatrix and scalar reads)
 constexpr int AP = 68;    // fp32 row stride of A / T / M tiles
 constexpr int RP = 136;   // fp32 row stride of 128-wide fp32 tiles (B operands)
 constexpr int WP = 132;   // fp32 row stride of W / S tiles (A operands and S^T reads)
 constexpr int UP = 36;    // fp32 row stride of 32-wide U tiles
+// Workspace of one (batch, head, chunk) in floats, laid out as the scan's shared-memory tiles (padded rows included)
+// so that a scan CTA fetches a chunk with two bulk copies: W [C][WP] and M [C][AP] (TF32 values) and gamma, Gam
+// [2 C] as one block, then U' as DV / DVB slices [C][UP] of 32 value columns each.
+constexpr int WS_W = 0;
+constexpr int WS_M = WS_W + C * WP;
+constexpr int WS_G = WS_M + C * AP;
+constexpr int WS_U = WS_G + 2 * C;
+constexpr int UNIT = WS_U + (DV / DVB) * C * UP;
+constexpr int WMG_BYTES = WS_U * 4;  // W, M and the gates: one copy
+static_assert(WS_M % 4 == 0 && WS_G % 4 == 0 && WS_U % 4 == 0 && UNIT % 4 == 0, "16-byte aligned workspace tiles");
 
 struct Params {
   const void* q;
@@ -64,6 +74,12 @@ __device__ __forceinline__ uint32_t tf32(float x) {
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
   return r;
+}
+
+// A 16-bit value's exact TF32 bit pattern (bf16 and fp16 mantissas fit TF32's 10 bits).
+template <typename T>
+__device__ __forceinline__ uint32_t tf32_of(T x) {
+  return __float_as_uint(to_f<T>(x));
 }
 
 __device__ __forceinline__ void mma_tf32(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
@@ -97,13 +113,38 @@ __device__ __forceinline__ void ldsm4(uint32_t addr, uint32_t* r) {
                : "r"(addr));
 }
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+// 16-byte cp.async, zero-filling the destination when `in` is false (nothing is read then).
+__device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, bool in) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(in ? 16 : 0)
+               : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+
+// acc (a 16 x 8 m16n8k8 accumulator) += L R over K = 8 ksteps, with L's rows at Lp (row stride ldl, columns from
+// Lp) and R's rows k at Rp + k ldr, in three TF32 products per step (hi hi + hi lo + lo hi of each fp32 operand
+// split into TF32 high and low parts), so that the block products of the inversion keep close to fp32 accuracy.
+__device__ __forceinline__ void mma3_tile(const float* Lp, int ldl, const float* Rp, int ldr, int ksteps, float* acc,
+                                          int lane) {
+  const int r = lane >> 2, cq = lane & 3;
+  for (int ks = 0; ks < ksteps; ++ks) {
+    const int k0 = ks * 8;
+    const float a[4] = {Lp[r * ldl + k0 + cq], Lp[(r + 8) * ldl + k0 + cq], Lp[r * ldl + k0 + cq + 4],
+                        Lp[(r + 8) * ldl + k0 + cq + 4]};
+    const float bb[2] = {Rp[(k0 + cq) * ldr + r], Rp[(k0 + cq + 4) * ldr + r]};
+    uint32_t ah[4], al[4], bh[2], bl[2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      ah[i] = tf32(a[i]);
+      al[i] = tf32(a[i] - __uint_as_float(ah[i]));
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      bh[i] = tf32(bb[i]);
+      bl[i] = tf32(bb[i] - __uint_as_float(bh[i]));
+    }
+    mma_tf32(acc, al[0], al[1], al[2], al[3], bh[0], bh[1]);
+    mma_tf32(acc, ah[0], ah[1], ah[2], ah[3], bl[0], bl[1]);
+    mma_tf32(acc, ah[0], ah[1], ah[2], ah[3], bh[0], bh[1]);
+  }
 }
 
 // Workspace tiles of one (batch, head, chunk).
@@ -118,8 +159,8 @@ struct PrepSmem {
   static constexpr int QB = KB + C * KP * 2;                // bf16 [C][KP]
   static constexpr int VB = QB + C * KP * 2;                // bf16 [C][KP]
   static constexpr int AF = VB + C * KP * 2;                // f32 [C][AP]  A, then T
-  static constexpr int XS = AF + C * AP * 4;                // f32 [32][33] inversion scratch
-  static constexpr int GAM = XS + 32 * 33 * 4;              // f32 [C] gamma, [C] Gam, [C] beta
+  static constexpr int XS = AF + C * AP * 4;                // f32 [32][XP] inversion scratch
+  static constexpr int GAM = XS + 32 * 40 * 4;              // f32 [C] gamma, [C] Gam, [C] beta
   static constexpr int BYTES = GAM + 3 * C * 4;
 };
 
@@ -139,7 +180,23 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
   float* Gam = gam + C;
   float* bet = Gam + C;
 
-  // 1. gates: gamma = inclusive prefix sum of log g over the chunk (positions past T: g = 1, beta = 0)
+  // 1. K, Q and V tiles (16-bit) by cp.async, zero past T: they land while the gates are formed
+  {
+    const T* kg = static_cast<const T*>(p.k);
+    const T* qg = static_cast<const T*>(p.q);
+    const T* vg = static_cast<const T*>(p.v);
+#pragma unroll
+    for (int i = 0; i < C * (DK / 8) / 128; ++i) {
+      const int e = tid + 128 * i, r = e / (DK / 8), u = e % (DK / 8);
+      const bool in = t0 + r < p.T;
+      const int64_t row = int64_t(b) * p.T + (in ? t0 + r : 0);  // (a row of the sequence even when not read)
+      cp_async16_zfill(Kb + r * KP + u * 8, kg + (row * p.Hk + hk) * DK + u * 8, in);
+      cp_async16_zfill(Qb + r * KP + u * 8, qg + (row * p.Hk + hk) * DK + u * 8, in);
+      cp_async16_zfill(Vb + r * KP + u * 8, vg + (row * p.Hv + h) * DV + u * 8, in);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  // 2. gates: gamma = inclusive prefix sum of log g over the chunk (positions past T: g = 1, beta = 0)
   if (warp == 0) {
     float x[2], bt[2];
 #pragma unroll
@@ -165,27 +222,7 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
       bet[lane + 32 * u] = bt[u];
     }
   }
-  // 2. K, Q and V tiles (16-bit, vector loads), zero past T
-  {
-    const T* kg = static_cast<const T*>(p.k);
-    const T* qg = static_cast<const T*>(p.q);
-    const T* vg = static_cast<const T*>(p.v);
-#pragma unroll 4
-    for (int e = tid; e < C * (DK / 8); e += 128) {
-      const int r = e / (DK / 8), u = e % (DK / 8);
-      const int pos = t0 + r;
-      uint4 kv = make_uint4(0, 0, 0, 0), qv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-      if (pos < p.T) {
-        const int64_t off = ((int64_t(b) * p.T + pos) * p.Hk + hk) * DK + u * 8;
-        kv = *reinterpret_cast<const uint4*>(kg + off);
-        qv = *reinterpret_cast<const uint4*>(qg + off);
-        vv = *reinterpret_cast<const uint4*>(vg + ((int64_t(b) * p.T + pos) * p.Hv + h) * DV + u * 8);
-      }
-      *reinterpret_cast<uint4*>(Kb + r * KP + u * 8) = kv;
-      *reinterpret_cast<uint4*>(Qb + r * KP + u * 8) = qv;
-      *reinterpret_cast<uint4*>(Vb + r * KP + u * 8) = vv;
-    }
-  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
 
   // 3. K K^T and Q K^T for rows 16 w .. 16 w + 15 (bf16 mma, fp32 accumulate), then decay / beta weighting
@@ -213,16 +250,19 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
         mma_16816<T>(qk[2 * np + 1], aq, bk[2], bk[3]);
       }
     }
-    float* Mg = unit_ptr(p, b, h, c) + C * DK + C * DV;
+    float* Mg = unit_ptr(p, b, h, c) + WS_M;
 #pragma unroll
     for (int n = 0; n < 8; ++n)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int t = warp * 16 + (lane >> 2) + 8 * (e >> 1);
-        const int j = n * 8 + 2 * (lane & 3) + (e & 1);
-        const float dec = j <= t ? __expf(gam[t] - gam[j]) : 0.f;
-        Af[t * AP + j] = j < t ? bet[t] * dec * kk[n][e] : 0.f;
-        Mg[t * C + j] = __uint_as_float(tf32(dec * qk[n][e]));  // an MMA operand of the scan: rounded once here
+      for (int hh = 0; hh < 2; ++hh) {  // columns j, j + 1 of row t
+        const int t = warp * 16 + (lane >> 2) + 8 * hh;
+        const int j = n * 8 + 2 * (lane & 3);
+        const float d0 = j <= t ? __expf(gam[t] - gam[j]) : 0.f, d1 = j + 1 <= t ? __expf(gam[t] - gam[j + 1]) : 0.f;
+        *reinterpret_cast<float2*>(&Af[t * AP + j]) =
+            make_float2(j < t ? bet[t] * d0 * kk[n][2 * hh] : 0.f, j + 1 < t ? bet[t] * d1 * kk[n][2 * hh + 1] : 0.f);
+        // an MMA operand of the scan: rounded once here
+        *reinterpret_cast<float2*>(&Mg[t * AP + j]) = make_float2(__uint_as_float(tf32(d0 * qk[n][2 * hh])),
+                                                                  __uint_as_float(tf32(d1 * qk[n][2 * hh + 1])));
       }
   }
   __syncthreads();
@@ -246,61 +286,76 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
       for (int r = 0; r < 16; ++r) Af[(base + r) * AP + base + i] = tc[r];
   }
   __syncthreads();
-  // level 1: T[hi][lo] = -T[hi][hi] A[hi][lo] T[lo][lo] for block pairs (0, 1) and (2, 3)
+  // level 1: T[hi][lo] = -T[hi][hi] A[hi][lo] T[lo][lo] for the block pairs (0, 1) and (2, 3) (16 x 16 blocks):
+  // warp w takes pair w / 2 and output columns 8 (w % 2) .. + 7, first of X = A[hi][lo] T[lo][lo], then of the block
+  constexpr int XP = 40;  // row stride of the scratch X (conflict-free B fragment reads)
   {
-    const int pr = tid >> 6, t = tid & 63;  // 64 threads a pair, 4 outputs each
+    const int pr = warp >> 1, n0 = (warp & 1) * 8;
     const int lo = 32 * pr, hi = lo + 16;
-    float* X = Xs + pr * 16 * 17;
+    float* X = Xs + pr * 16 * XP;
+    const int r = lane >> 2, cq = lane & 3;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    mma3_tile(Af + hi * AP + lo, AP, Af + lo * AP + lo + n0, AP, 2, acc, lane);
+    X[r * XP + n0 + 2 * cq] = acc[0];
+    X[r * XP + n0 + 2 * cq + 1] = acc[1];
+    X[(r + 8) * XP + n0 + 2 * cq] = acc[2];
+    X[(r + 8) * XP + n0 + 2 * cq + 1] = acc[3];
+    __syncthreads();
+    float t[4] = {0.f, 0.f, 0.f, 0.f};
+    mma3_tile(Af + hi * AP + hi, AP, X + n0, XP, 2, t, lane);
+    Af[(hi + r) * AP + lo + n0 + 2 * cq] = -t[0];
+    Af[(hi + r) * AP + lo + n0 + 2 * cq + 1] = -t[1];
+    Af[(hi + r + 8) * AP + lo + n0 + 2 * cq] = -t[2];
+    Af[(hi + r + 8) * AP + lo + n0 + 2 * cq + 1] = -t[3];
+  }
+  __syncthreads();
+  // level 2: T[32:64][0:32] = -T[32:64][32:64] A[32:64][0:32] T[0:32][0:32] (32 x 32 blocks): warp w takes the two
+  // 16 x 8 output tiles 2 w, 2 w + 1 (row tile = index / 4, column tile = index % 4) of each product
+  {
+    const int r = lane >> 2, cq = lane & 3;
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int o = t + 64 * u, r = o >> 4, cc = o & 15;
-      float s = 0.f;
-#pragma unroll
-      for (int j = 0; j < 16; ++j) s = fmaf(Af[(hi + r) * AP + lo + j], Af[(lo + j) * AP + lo + cc], s);
-      X[r * 17 + cc] = s;
+    for (int u = 0; u < 2; ++u) {
+      const int ti = warp * 2 + u, m0 = (ti >> 2) * 16, n0 = (ti & 3) * 8;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      mma3_tile(Af + (32 + m0) * AP, AP, Af + n0, AP, 4, acc, lane);
+      Xs[(m0 + r) * XP + n0 + 2 * cq] = acc[0];
+      Xs[(m0 + r) * XP + n0 + 2 * cq + 1] = acc[1];
+      Xs[(m0 + r + 8) * XP + n0 + 2 * cq] = acc[2];
+      Xs[(m0 + r + 8) * XP + n0 + 2 * cq + 1] = acc[3];
     }
     __syncthreads();
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int o = t + 64 * u, r = o >> 4, cc = o & 15;
-      float s = 0.f;
-#pragma unroll
-      for (int j = 0; j < 16; ++j) s = fmaf(Af[(hi + r) * AP + hi + j], X[j * 17 + cc], s);
-      Af[(hi + r) * AP + lo + cc] = -s;
+    for (int u = 0; u < 2; ++u) {
+      const int ti = warp * 2 + u, m0 = (ti >> 2) * 16, n0 = (ti & 3) * 8;
+      float t[4] = {0.f, 0.f, 0.f, 0.f};
+      mma3_tile(Af + (32 + m0) * AP + 32, AP, Xs + n0, XP, 4, t, lane);
+      Af[(32 + m0 + r) * AP + n0 + 2 * cq] = -t[0];
+      Af[(32 + m0 + r) * AP + n0 + 2 * cq + 1] = -t[1];
+      Af[(32 + m0 + r + 8) * AP + n0 + 2 * cq] = -t[2];
+      Af[(32 + m0 + r + 8) * AP + n0 + 2 * cq + 1] = -t[3];
     }
   }
   __syncthreads();
-  // level 2: T[32:64][0:32] = -T[32:64][32:64] A[32:64][0:32] T[0:32][0:32]
+  // 5. U' = T diag(beta) V, then W = T diag(beta Gam) K (TF32 mma), rows 16 w .. 16 w + 15: warp w scales its own
+  // rows of T by the column factors (beta, then Gam on top), so the B fragments are the 16-bit tiles' exact TF32
+  // values. T is lower triangular, so only k < 16 (w + 1) contributes.
   {
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int o = tid + 128 * u, r = o >> 5, cc = o & 31;
-      float s = 0.f;
-#pragma unroll 8
-      for (int j = 0; j < 32; ++j) s = fmaf(Af[(32 + r) * AP + j], Af[j * AP + cc], s);
-      Xs[r * 33 + cc] = s;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int o = tid + 128 * u, r = o >> 5, cc = o & 31;
-      float s = 0.f;
-#pragma unroll 8
-      for (int j = 0; j < 32; ++j) s = fmaf(Af[(32 + r) * AP + 32 + j], Xs[j * 33 + cc], s);
-      Af[(32 + r) * AP + cc] = -s;
-    }
-  }
-  __syncthreads();
-  // 5. W = T diag(beta Gam) K and U' = T diag(beta) V (TF32 mma), rows 16 w .. 16 w + 15; the B fragments are
-  // formed from the 16-bit tiles on the fly. T is lower triangular, so only k < 16 (w + 1) contributes.
-  {
-    float* Wg = unit_ptr(p, b, h, c);
-    float* Ug = Wg + C * DK;
+    float* Wg = unit_ptr(p, b, h, c) + WS_W;
+    float* Ug = unit_ptr(p, b, h, c) + WS_U;
     const int r = lane >> 2, cq = lane & 3, m0 = warp * 16;
 #pragma unroll 1
-    for (int which = 0; which < 2; ++which) {
+    for (int which = 1; which >= 0; --which) {
       const T* R = which ? Vb : Kb;
-      float* G = which ? Ug : Wg;
+      __syncwarp();
+      {  // lane l scales columns l and l + 32 of the warp's rows (the lower triangle: columns < m0 + 16)
+        const float f0 = which ? bet[lane] : Gam[lane], f1 = which ? bet[lane + 32] : Gam[lane + 32];
+#pragma unroll
+        for (int rr = 0; rr < 16; ++rr) {
+          Af[(m0 + rr) * AP + lane] *= f0;
+          if (m0 >= 16) Af[(m0 + rr) * AP + lane + 32] *= f1;
+        }
+      }
+      __syncwarp();
 #pragma unroll 1
       for (int nh = 0; nh < 2; ++nh) {  // two halves of 64 columns, to bound registers
         float acc[8][4];
@@ -309,13 +364,11 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
         for (int k0 = 0; k0 < 16 * (warp + 1); k0 += 8) {
           const uint32_t a0 = tf32(Af[(m0 + r) * AP + k0 + cq]), a1 = tf32(Af[(m0 + r + 8) * AP + k0 + cq]);
           const uint32_t a2 = tf32(Af[(m0 + r) * AP + k0 + cq + 4]), a3 = tf32(Af[(m0 + r + 8) * AP + k0 + cq + 4]);
-          const float s0 = which ? bet[k0 + cq] : bet[k0 + cq] * Gam[k0 + cq];
-          const float s1 = which ? bet[k0 + cq + 4] : bet[k0 + cq + 4] * Gam[k0 + cq + 4];
 #pragma unroll
           for (int n = 0; n < 8; ++n) {
             const int n0 = nh * 64 + n * 8;
-            mma_tf32(acc[n], a0, a1, a2, a3, tf32(s0 * to_f<T>(R[(k0 + cq) * KP + n0 + r])),
-                     tf32(s1 * to_f<T>(R[(k0 + cq + 4) * KP + n0 + r])));
+            mma_tf32(acc[n], a0, a1, a2, a3, tf32_of(R[(k0 + cq) * KP + n0 + r]),
+                     tf32_of(R[(k0 + cq + 4) * KP + n0 + r]));
           }
         }
         if (!which)  // W is an MMA operand of the scan: stored rounded to TF32; U' stays fp32
@@ -324,17 +377,19 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
 #pragma unroll
             for (int e = 0; e < 4; ++e) acc[n][e] = __uint_as_float(tf32(acc[n][e]));
 #pragma unroll
-        for (int n = 0; n < 8; ++n) {
+        for (int n = 0; n < 8; ++n) {  // W rows of stride WP; U' in slices of DVB columns, rows of stride UP
           const int col = nh * 64 + n * 8 + 2 * cq;
-          *reinterpret_cast<float2*>(&G[(m0 + r) * DK + col]) = make_float2(acc[n][0], acc[n][1]);
-          *reinterpret_cast<float2*>(&G[(m0 + r + 8) * DK + col]) = make_float2(acc[n][2], acc[n][3]);
+          float* g0 = which ? Ug + ((col / DVB) * C + m0 + r) * UP + col % DVB : Wg + (m0 + r) * WP + col;
+          float* g1 = g0 + 8 * (which ? UP : WP);
+          *reinterpret_cast<float2*>(g0) = make_float2(acc[n][0], acc[n][1]);
+          *reinterpret_cast<float2*>(g1) = make_float2(acc[n][2], acc[n][3]);
         }
       }
     }
   }
   // 7. gamma and Gam for the scan
   if (tid < C) {
-    float* gg = unit_ptr(p, b, h, c) + C * DK + C * DV + C * C;
+    float* gg = unit_ptr(p, b, h, c) + WS_G;
     gg[tid] = gam[tid];
     gg[C + tid] = Gam[tid];
   }
@@ -343,71 +398,65 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
 // ------------------------------------------------------------------------------------------------ scan
 
 constexpr int SCAN_THREADS = 256;  // warps 0-3: U = U' - W S^T; warps 4-7: Q S^T and M U; all 8: the state update
-constexpr int UQ = 40;             // u32 row stride of the U tiles read as MMA operands (conflict-free fragments)
+constexpr int UQ = 68;             // u32 row stride of the transposed U tiles [DVB][C] (conflict-free ldmatrix)
 
 struct ScanSmem {
-  // one prefetch buffer
+  // one prefetch buffer; W, M and G in the workspace's order (one bulk copy)
   static constexpr int W = 0;                         // tf32 [C][WP]
-  static constexpr int U = W + C * WP * 4;            // f32 [C][UP]   U' columns of this block
-  static constexpr int M = U + C * UP * 4;            // tf32 [C][AP]
-  static constexpr int Q = M + C * AP * 4;            // 16-bit [C][KP]
-  static constexpr int K = Q + C * KP * 2;            // 16-bit [C][KP]
-  static constexpr int G = K + C * KP * 2;            // f32 [C] gamma, [C] Gam
-  static constexpr int BUF = G + 2 * C * 4;
+  static constexpr int M = W + (WS_M - WS_W) * 4;     // tf32 [C][AP]
+  static constexpr int G = W + (WS_G - WS_W) * 4;     // f32 [C] gamma, [C] Gam
+  static constexpr int U = W + (WS_U - WS_W) * 4;     // f32 [C][UP]   U' columns of this block
+  // Q and K tiles as the tiled TMA lands them: two boxes of [64 positions][64 columns] (128-byte rows, 128-byte
+  // swizzle: the 16-byte piece j of row r sits at piece j ^ (r % 8)), 1024-byte aligned
+  static constexpr int QK_TILE = 2 * C * 64 * 2;
+  static constexpr int Q = (U + C * UP * 4 + 1023) / 1024 * 1024;
+  static constexpr int K = Q + QK_TILE;
+  static constexpr int BUF = K + QK_TILE;
   // persistent
   static constexpr int ST = 2 * BUF;                  // tf32 [DVB][WP] the state slice, rounded for the MMAs
-  static constexpr int UB = ST + DVB * WP * 4;        // tf32 [C][UQ] this chunk's U
-  static constexpr int UD = UB + C * UQ * 4;          // tf32 [C][UQ] diag(exp(gamma_C - gamma)) U
-  static constexpr int BYTES = UD + C * UQ * 4;
+  static constexpr int UB = ST + DVB * WP * 4;        // tf32 [DVB][UQ] this chunk's U, transposed
+  static constexpr int UD = UB + DVB * UQ * 4;        // tf32 [DVB][UQ] (diag(exp(gamma_C - gamma)) U)^T
+  static constexpr int BAR = UD + DVB * UQ * 4;       // 2 mbarriers: buffer b's copies landed
+  static constexpr int BYTES = BAR + 16 + 1024;  // (+ alignment of the dynamic shared memory base to 1024)
 };
+static_assert(ScanSmem::BUF % 1024 == 0 && ScanSmem::U % 16 == 0 && ScanSmem::Q % 1024 == 0, "copy alignment");
 static_assert(ScanSmem::BYTES <= 232448, "scan shared memory");
 
-// A 16-bit value's exact TF32 bit pattern (bf16 and fp16 mantissas fit TF32's 10 bits).
+// Element (row, col) of a Q / K tile (see ScanSmem) as its exact TF32 bit pattern.
 template <typename T>
-__device__ __forceinline__ uint32_t tf32_of(T x) {
-  return __float_as_uint(to_f<T>(x));
+__device__ __forceinline__ uint32_t qk_tf32(const uint8_t* tile, int row, int col) {
+  const int off = (col >> 6) * (C * 128) + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) << 4) + ((col & 7) << 1);
+  return tf32_of(*reinterpret_cast<const T*>(tile + off));
 }
 
-template <typename T>
-__device__ __forceinline__ void scan_prefetch(const Params& p, uint8_t* buf, int b, int h, int hk, int c, int dv0,
-                                              int tid) {
+// TF32 m16n8k8 fragments by ldmatrix (an 8 x 4 block of 32-bit values is an 8 x 8 block of 16-bit halves; thread
+// g * 4 + t receives the 32-bit value at row g, column t, the fragments' layout). `base` is the shared address of
+// element (0, 0) of a row-major fp32 / TF32 tile with `ld` values a row (ld * 4 % 128 == 16: conflict-free rows).
+// A: rows m0 .. m0 + 15, columns k0 .. k0 + 7.
+__device__ __forceinline__ void frag_a(uint32_t base, int ld, int m0, int k0, int lane, uint32_t* a) {
+  ldsm4(base + ((m0 + (lane & 7) + ((lane >> 3) & 1) * 8) * ld + k0 + (lane >> 4) * 4) * 4, a);
+}
+// B of two n-tiles from a tile stored n-major ([n][k]): n0 .. n0 + 15, k0 .. k0 + 7; b[0], b[1] for n-tile n0,
+// b[2], b[3] for n0 + 8.
+__device__ __forceinline__ void frag_b2(uint32_t base, int ld, int n0, int k0, int lane, uint32_t* b) {
+  ldsm4(base + ((n0 + (lane & 7) + (lane >> 4) * 8) * ld + k0 + ((lane >> 3) & 1) * 4) * 4, b);
+}
+
+
+// The tiles of chunk c into one buffer, completing on its mbarrier (thread 0 issues all): W, M and the gates in one
+// bulk copy, this block's U' slice in another, and the Q and K tiles by tiled TMA, two 64-column boxes each (rows
+// past T arrive as zeros).
+__device__ __forceinline__ void scan_prefetch(const Params& p, const CUtensorMap* qmap, const CUtensorMap* kmap,
+                                              uint8_t* buf, uint64_t* full, int b, int h, int hk, int c, int blk) {
   const float* u = unit_ptr(p, b, h, c);
-  float* W = reinterpret_cast<float*>(buf + ScanSmem::W);
-  float* U = reinterpret_cast<float*>(buf + ScanSmem::U);
-  float* M = reinterpret_cast<float*>(buf + ScanSmem::M);
-  T* Q = reinterpret_cast<T*>(buf + ScanSmem::Q);
-  T* K = reinterpret_cast<T*>(buf + ScanSmem::K);
-  float* G = reinterpret_cast<float*>(buf + ScanSmem::G);
+  fence_proxy_async_shared();  // the buffer's reads two chunks back precede these writes
+  mbar_arrive_expect_tx(full, uint32_t(WMG_BYTES + C * UP * 4 + 2 * ScanSmem::QK_TILE));
+  bulk_g2s(buf + ScanSmem::W, u + WS_W, WMG_BYTES, full);
+  bulk_g2s(buf + ScanSmem::U, u + WS_U + blk * C * UP, C * UP * 4, full);
 #pragma unroll
-  for (int e = tid; e < C * (DK / 4); e += SCAN_THREADS) {  // W: 64 rows x 32 pieces of 16 B
-    const int r = e >> 5, q = e & 31;
-    cp_async16(W + r * WP + q * 4, u + r * DK + q * 4);
-  }
-#pragma unroll
-  for (int e = tid; e < C * (DVB / 4); e += SCAN_THREADS) {  // U' columns dv0 .. dv0 + 31
-    const int r = e >> 3, q = e & 7;
-    cp_async16(U + r * UP + q * 4, u + C * DK + r * DV + dv0 + q * 4);
-  }
-#pragma unroll
-  for (int e = tid; e < C * (C / 4); e += SCAN_THREADS) {  // M
-    const int r = e >> 4, q = e & 15;
-    cp_async16(M + r * AP + q * 4, u + C * DK + C * DV + r * C + q * 4);
-  }
-  if (tid < 2 * C / 4) cp_async16(G + tid * 4, u + C * DK + C * DV + C * C + tid * 4);
-  const T* qg = static_cast<const T*>(p.q);
-  const T* kg = static_cast<const T*>(p.k);
-#pragma unroll
-  for (int e = tid; e < C * (DK / 8); e += SCAN_THREADS) {  // Q, K rows (zero past T)
-    const int r = e >> 4, q = e & 15;
-    const int pos = c * C + r;
-    if (pos < p.T) {
-      const int64_t off = ((int64_t(b) * p.T + pos) * p.Hk + hk) * DK + q * 8;
-      cp_async16(Q + r * KP + q * 8, qg + off);
-      cp_async16(K + r * KP + q * 8, kg + off);
-    } else {
-      *reinterpret_cast<uint4*>(Q + r * KP + q * 8) = make_uint4(0, 0, 0, 0);
-      *reinterpret_cast<uint4*>(K + r * KP + q * 8) = make_uint4(0, 0, 0, 0);
-    }
+  for (int db = 0; db < DK / 64; ++db) {
+    tma_load_4d(buf + ScanSmem::Q + db * C * 128, qmap, db * 64, c * C, hk, b, full);
+    tma_load_4d(buf + ScanSmem::K + db * C * 128, kmap, db * 64, c * C, hk, b, full);
   }
 }
 
@@ -417,16 +466,27 @@ __device__ __forceinline__ void scan_prefetch(const Params& p, uint8_t* buf, int
 // 4-7 form Gam Q S^T; (2) all warps update their state columns with U^T diag(exp(gamma_C - gamma)) K while warps
 // 4-7 add M U to Y and store it.
 template <typename T>
-__global__ void __launch_bounds__(SCAN_THREADS, 1) scan_kernel(const Params p) {
+__global__ void __launch_bounds__(SCAN_THREADS, 1) scan_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                                const __grid_constant__ CUtensorMap kmap,
+                                                                const Params p) {
   const int blk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int hk = h / (p.Hv / p.Hk);
   const int dv0 = blk * DVB;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int r = lane >> 2, cq = lane & 3;
-  extern __shared__ __align__(16) uint8_t sm[];
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint32_t* St = reinterpret_cast<uint32_t*>(sm + ScanSmem::ST);
   uint32_t* Ub = reinterpret_cast<uint32_t*>(sm + ScanSmem::UB);
   uint32_t* Ud = reinterpret_cast<uint32_t*>(sm + ScanSmem::UD);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + ScanSmem::BAR);
+  if (tid == 0) {
+    prefetch_tensormap(&qmap);
+    prefetch_tensormap(&kmap);
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    fence_barrier_init();
+  }
 
   // the state tile of this warp: rows mt * 16 + r (+ 8), columns 16 warp + 8 n + 2 cq (+ 1)
   float sreg[2][2][4];
@@ -444,20 +504,28 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) scan_kernel(const Params p) {
         St[i * WP + d] = tf32(v.x);
         St[i * WP + d + 1] = tf32(v.y);
       }
-  scan_prefetch<T>(p, sm, b, h, hk, 0, dv0, tid);
-  cp_async_commit();
+  __syncthreads();  // barriers initialised
+  if (p.nchunks > 0 && tid == 0) scan_prefetch(p, &qmap, &kmap, sm, &full[0], b, h, hk, 0, blk);
 
+  bool ok = true;
+  int issued = p.nchunks > 0 ? 1 : 0;  // chunks whose copies were issued
   for (int c = 0; c < p.nchunks; ++c) {
     uint8_t* buf = sm + (c & 1) * ScanSmem::BUF;
-    if (c + 1 < p.nchunks) scan_prefetch<T>(p, sm + ((c + 1) & 1) * ScanSmem::BUF, b, h, hk, c + 1, dv0, tid);
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
+    if (c + 1 < p.nchunks) {
+      if (tid == 0)
+        scan_prefetch(p, &qmap, &kmap, sm + ((c + 1) & 1) * ScanSmem::BUF, &full[(c + 1) & 1], b, h, hk, c + 1, blk);
+      issued = c + 2;
+    }
+    ok = mbar_wait(&full[c & 1], (c >> 1) & 1, 71);
+    if (__syncthreads_or(!ok)) {
+      ok = false;
+      break;
+    }
     const uint32_t* W = reinterpret_cast<const uint32_t*>(buf + ScanSmem::W);
     const float* U = reinterpret_cast<const float*>(buf + ScanSmem::U);
     const uint32_t* M = reinterpret_cast<const uint32_t*>(buf + ScanSmem::M);
-    const T* Q = reinterpret_cast<const T*>(buf + ScanSmem::Q);
-    const T* K = reinterpret_cast<const T*>(buf + ScanSmem::K);
+    const uint8_t* Q = buf + ScanSmem::Q;
+    const uint8_t* K = buf + ScanSmem::K;
     const float* G = reinterpret_cast<const float*>(buf + ScanSmem::G);
     const int m0 = (warp & 3) * 16;
 
@@ -470,11 +538,14 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) scan_kernel(const Params p) {
     if (warp < 4) {
 #pragma unroll 4
       for (int k0 = 0; k0 < DK; k0 += 8) {
-        const uint32_t a0 = W[(m0 + r) * WP + k0 + cq], a1 = W[(m0 + r + 8) * WP + k0 + cq];
-        const uint32_t a2 = W[(m0 + r) * WP + k0 + cq + 4], a3 = W[(m0 + r + 8) * WP + k0 + cq + 4];
-#pragma unroll
-        for (int n = 0; n < 4; ++n)
-          mma_tf32(acc[n], a0, a1, a2, a3, St[(n * 8 + r) * WP + k0 + cq], St[(n * 8 + r) * WP + k0 + cq + 4]);
+        uint32_t a[4], b01[4], b23[4];
+        frag_a(smem_u32(W), WP, m0, k0, lane, a);
+        frag_b2(smem_u32(St), WP, 0, k0, lane, b01);
+        frag_b2(smem_u32(St), WP, 16, k0, lane, b23);
+        mma_tf32(acc[0], a[0], a[1], a[2], a[3], b01[0], b01[1]);
+        mma_tf32(acc[1], a[0], a[1], a[2], a[3], b01[2], b01[3]);
+        mma_tf32(acc[2], a[0], a[1], a[2], a[3], b23[0], b23[1]);
+        mma_tf32(acc[3], a[0], a[1], a[2], a[3], b23[2], b23[3]);
       }
       // U = U' - W S^T, stored rounded for the products that read it, plain and scaled by exp(gamma_C - gamma_t)
       const float gl = G[C - 1];
@@ -485,18 +556,21 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) scan_kernel(const Params p) {
         for (int e = 0; e < 4; ++e) {
           const int t = m0 + r + 8 * (e >> 1), col = n * 8 + 2 * cq + (e & 1);
           const float u = U[t * UP + col] - acc[n][e];
-          Ub[t * UQ + col] = tf32(u);
-          Ud[t * UQ + col] = tf32((e >> 1 ? dh : dl) * u);
+          Ub[col * UQ + t] = tf32(u);
+          Ud[col * UQ + t] = tf32((e >> 1 ? dh : dl) * u);
         }
     } else {
 #pragma unroll 4
       for (int k0 = 0; k0 < DK; k0 += 8) {
-        const uint32_t a0 = tf32_of(Q[(m0 + r) * KP + k0 + cq]), a1 = tf32_of(Q[(m0 + r + 8) * KP + k0 + cq]);
-        const uint32_t a2 = tf32_of(Q[(m0 + r) * KP + k0 + cq + 4]);
-        const uint32_t a3 = tf32_of(Q[(m0 + r + 8) * KP + k0 + cq + 4]);
-#pragma unroll
-        for (int n = 0; n < 4; ++n)
-          mma_tf32(acc[n], a0, a1, a2, a3, St[(n * 8 + r) * WP + k0 + cq], St[(n * 8 + r) * WP + k0 + cq + 4]);
+        const uint32_t a0 = qk_tf32<T>(Q, m0 + r, k0 + cq), a1 = qk_tf32<T>(Q, m0 + r + 8, k0 + cq);
+        const uint32_t a2 = qk_tf32<T>(Q, m0 + r, k0 + cq + 4), a3 = qk_tf32<T>(Q, m0 + r + 8, k0 + cq + 4);
+        uint32_t b01[4], b23[4];
+        frag_b2(smem_u32(St), WP, 0, k0, lane, b01);
+        frag_b2(smem_u32(St), WP, 16, k0, lane, b23);
+        mma_tf32(acc[0], a0, a1, a2, a3, b01[0], b01[1]);
+        mma_tf32(acc[1], a0, a1, a2, a3, b01[2], b01[3]);
+        mma_tf32(acc[2], a0, a1, a2, a3, b23[0], b23[1]);
+        mma_tf32(acc[3], a0, a1, a2, a3, b23[2], b23[3]);
       }
       const float gl = G[C + m0 + r], gh = G[C + m0 + r + 8];
 #pragma unroll
@@ -522,16 +596,11 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) scan_kernel(const Params p) {
       for (int k0 = 0; k0 < C; k0 += 8) {
         uint32_t a[2][4];
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-          a[mt][0] = Ud[(k0 + cq) * UQ + mt * 16 + r];
-          a[mt][1] = Ud[(k0 + cq) * UQ + mt * 16 + r + 8];
-          a[mt][2] = Ud[(k0 + cq + 4) * UQ + mt * 16 + r];
-          a[mt][3] = Ud[(k0 + cq + 4) * UQ + mt * 16 + r + 8];
-        }
+        for (int mt = 0; mt < 2; ++mt) frag_a(smem_u32(Ud), UQ, mt * 16, k0, lane, a[mt]);
 #pragma unroll
         for (int n = 0; n < 2; ++n) {
           const int col = warp * 16 + n * 8 + r;
-          const uint32_t b0 = tf32_of(K[(k0 + cq) * KP + col]), b1 = tf32_of(K[(k0 + cq + 4) * KP + col]);
+          const uint32_t b0 = qk_tf32<T>(K, k0 + cq, col), b1 = qk_tf32<T>(K, k0 + cq + 4, col);
 #pragma unroll
           for (int mt = 0; mt < 2; ++mt) mma_tf32(sreg[mt][n], a[mt][0], a[mt][1], a[mt][2], a[mt][3], b0, b1);
         }
@@ -550,11 +619,14 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) scan_kernel(const Params p) {
     // (3) warps 4-7: Y = Gam Q S^T + M U (M lower triangular: k < m0 + 16), stored
     if (warp >= 4) {
       for (int k0 = 0; k0 < m0 + 16; k0 += 8) {
-        const uint32_t a0 = M[(m0 + r) * AP + k0 + cq], a1 = M[(m0 + r + 8) * AP + k0 + cq];
-        const uint32_t a2 = M[(m0 + r) * AP + k0 + cq + 4], a3 = M[(m0 + r + 8) * AP + k0 + cq + 4];
-#pragma unroll
-        for (int n = 0; n < 4; ++n)
-          mma_tf32(acc[n], a0, a1, a2, a3, Ub[(k0 + cq) * UQ + n * 8 + r], Ub[(k0 + cq + 4) * UQ + n * 8 + r]);
+        uint32_t a[4], b01[4], b23[4];
+        frag_a(smem_u32(M), AP, m0, k0, lane, a);
+        frag_b2(smem_u32(Ub), UQ, 0, k0, lane, b01);
+        frag_b2(smem_u32(Ub), UQ, 16, k0, lane, b23);
+        mma_tf32(acc[0], a[0], a[1], a[2], a[3], b01[0], b01[1]);
+        mma_tf32(acc[1], a[0], a[1], a[2], a[3], b01[2], b01[3]);
+        mma_tf32(acc[2], a[0], a[1], a[2], a[3], b23[0], b23[1]);
+        mma_tf32(acc[3], a[0], a[1], a[2], a[3], b23[2], b23[3]);
       }
       T* yg = static_cast<T*>(p.y);
 #pragma unroll
@@ -571,6 +643,10 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) scan_kernel(const Params p) {
       }
     }
     __syncthreads();  // the state copy complete and this chunk's buffer free before the next prefetch
+  }
+  if (!ok) {  // a wait gave up (status word set): let the copies still in flight land (bounded), write nothing
+    for (int c2 = max(0, issued - 2); c2 < issued; ++c2) mbar_wait(&full[c2 & 1], (c2 >> 1) & 1, 72);
+    return;
   }
   float* sout = p.s_out + (int64_t(b) * p.Hv + h) * DV * DK;
 #pragma unroll

@@ -1,6 +1,7 @@
 // larder_b200: the C-ABI library. One translation unit (so the device status word is one symbol) that includes
 // every kernel header and implements the entry points declared in include/larder_b200.h.
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 #include <string>
 
@@ -590,6 +591,16 @@ int lb2_gdn_chunked(const void* q, const void* k, int qdt, const void* v, int vd
   LB2_CHECK_ARG(((uintptr_t(state_in) | uintptr_t(state_out)) & 7) == 0, "gdn_chunked: states 8-byte aligned");
   gdnchunk::Params p{q, k, v, g, beta, qdt, vdt, gdt, bdt, state_in, state_out, y, B, T, Hk, Hv,
                      (T + gdnchunk::C - 1) / gdnchunk::C, static_cast<float*>(workspace)};
+  // Q and K tiles of the scan: [B, T, Hk, Dk] contiguous, 64-column boxes of 64 positions (rows past T read as 0)
+  CUtensorMap qm, km;
+  std::memset(&qm, 0, sizeof(qm));
+  std::memset(&km, 0, sizeof(km));
+  if (T > 0) {
+    const int64_t qk_st[3] = {int64_t(T) * Hk * Dk, Dk, int64_t(Hk) * Dk};
+    int rc = prefill::map4(&qm, q, qk_st, B, Hk, T, Dk, qdt, gdnchunk::C);
+    if (!rc) rc = prefill::map4(&km, k, qk_st, B, Hk, T, Dk, qdt, gdnchunk::C);
+    if (rc) return rc;
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   static int attr_dev = -1;
   int dev = 0;
@@ -608,10 +619,10 @@ int lb2_gdn_chunked(const void* q, const void* k, int qdt, const void* v, int vd
   const dim3 gp(unsigned(p.nchunks), unsigned(Hv), unsigned(B)), gs(gdnchunk::DV / gdnchunk::DVB, Hv, B);
   if (qdt == LB2_BF16) {
     if (p.nchunks > 0) gdnchunk::prep_kernel<__nv_bfloat16><<<gp, 128, gdnchunk::PrepSmem::BYTES, st>>>(p);
-    gdnchunk::scan_kernel<__nv_bfloat16><<<gs, gdnchunk::SCAN_THREADS, gdnchunk::ScanSmem::BYTES, st>>>(p);
+    gdnchunk::scan_kernel<__nv_bfloat16><<<gs, gdnchunk::SCAN_THREADS, gdnchunk::ScanSmem::BYTES, st>>>(qm, km, p);
   } else {
     if (p.nchunks > 0) gdnchunk::prep_kernel<__half><<<gp, 128, gdnchunk::PrepSmem::BYTES, st>>>(p);
-    gdnchunk::scan_kernel<__half><<<gs, gdnchunk::SCAN_THREADS, gdnchunk::ScanSmem::BYTES, st>>>(p);
+    gdnchunk::scan_kernel<__half><<<gs, gdnchunk::SCAN_THREADS, gdnchunk::ScanSmem::BYTES, st>>>(qm, km, p);
   }
   LB2_CUDA(cudaGetLastError());
   return LB2_OK;
