@@ -382,7 +382,8 @@ def bench_sharded(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, 
                         "roofline": {"bound": "tensor", "achieved": round(flop / (ms_p * 1e-3) / 1e12, 2),
                                      "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
                                      "frac": round(flop / (ms_p * 1e-3) / 1e12 / pk["bf16_tflops_sustained"], 4),
-                                     "peak_kind": "sustained (long step)"}},
+                                     "peak_kind": "sustained (long step)",
+                                     "kernel": "lb2::prefill2::fmha2_kernel<bf16,128>"}},
             "decode": {"value": round(world * kv_bytes / (ms_d * 1e-3) / 1e9, 1), "unit": "GB/s",
                        "ms_per_step": round(ms_d, 5), "context": n_local * world,
                        "per_rank": f"B=64 x {n_local} local keys; partial (o, lse) all-gathered over NCCL",
@@ -470,7 +471,7 @@ def bench_gdn(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_
                       "launch": "the K steps as one CUDA graph, replayed once",
                       "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                                    "frac": round(gbs / pk["hbm_gbs"], 4),
-                                   "kernel": "lb2::gdnrec::recurrent_kernel<bf16,4>"},
+                                   "kernel": "lb2::gdnrec::recurrent_kernel<bf16,4,8>"},
                       "clocks": clk.summary()}}
     return res
 
