@@ -74,8 +74,14 @@ def check(rc, what):
 
 
 _I64N = [ctypes.c_int64 * n for n in range(5)]
+_I64_CACHE = {}  # value tuple -> array: strides repeat from call to call, and the library only reads them
 
 
 def i64(*vals):
-    """An int64 array argument (strides, shapes) from Python ints."""
-    return _I64N[len(vals)](*vals) if len(vals) < 5 else (ctypes.c_int64 * len(vals))(*vals)
+    """An int64 array argument (strides, shapes) from Python ints. The library reads it during the call only."""
+    a = _I64_CACHE.get(vals)
+    if a is None:
+        a = _I64N[len(vals)](*vals) if len(vals) < 5 else (ctypes.c_int64 * len(vals))(*vals)
+        if len(_I64_CACHE) < 4096:
+            _I64_CACHE[vals] = a
+    return a

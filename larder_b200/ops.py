@@ -33,14 +33,15 @@ _raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
 
 
 def _stream(t):
-    """The caller's current CUDA stream on t's device, as the cudaStream_t handle the C ABI takes."""
+    """The caller's current CUDA stream on t's device, as the cudaStream_t handle (an int) the C ABI takes."""
     if _raw_stream is not None:
-        return ctypes.c_void_p(_raw_stream(t.device.index))
-    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+        return _raw_stream(t.device.index)
+    return torch.cuda.current_stream(t.device).cuda_stream
 
 
 def _ptr(t):
-    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+    """A tensor's device address as the C ABI's void* (None for NULL); the argtypes convert plain ints."""
+    return None if t is None else t.data_ptr()
 
 
 def _unit_last(t, name):
@@ -111,11 +112,11 @@ def decode_rows_limit(D):
     return 16 if D == 256 else 32
 
 
-_DECODE_WS = {}  # (B, Hq, Hkv, T, N, D, split, device) -> workspace bytes
+_DECODE_WS = {}  # (B, Hq, Hkv, T, N, D, split, device index) -> workspace bytes (the plan depends on the SM count)
 
 
-def _decode_ws_bytes(B, Hq, Hkv, T, N, D, split):
-    key = (B, Hq, Hkv, T, N, D, split, torch.cuda.current_device())
+def _decode_ws_bytes(B, Hq, Hkv, T, N, D, split, dev):
+    key = (B, Hq, Hkv, T, N, D, split, dev)
     n = _DECODE_WS.get(key)
     if n is None:
         n = _DECODE_WS[key] = lib().lb2_attn_decode_workspace_size(B, Hq, Hkv, T, N, D, split)
@@ -132,7 +133,7 @@ def attn_decode(q, k, v, scale, causal=False, kv_len=None, split=0, out=None):
     Hkv, N = k.shape[1], k.shape[2]
     if out is None:
         out = torch.empty((B, Hq, T, D), dtype=q.dtype, device=q.device)
-    ws = workspace(q.device, _decode_ws_bytes(B, Hq, Hkv, T, N, D, split), "decode")
+    ws = workspace(q.device, _decode_ws_bytes(B, Hq, Hkv, T, N, D, split, q.device.index), "decode")
     if kv_len is not None and (kv_len.dtype != torch.int32 or kv_len.numel() != B):
         raise ValueError("kv_len must be int32 [B]")
     rc = lib().lb2_attn_decode(_ptr(q), i64(*q.stride()[:3]), _ptr(k), i64(*k.stride()[:3]), _ptr(v),
@@ -150,7 +151,7 @@ def attn_decode_partial(q, k, v, scale, kv_len=None, split=0):
     Hkv, N = k.shape[1], k.shape[2]
     part_o = torch.empty((B, Hq, T, D), dtype=torch.float32, device=q.device)
     part_lse = torch.empty((B, Hq, T), dtype=torch.float32, device=q.device)
-    ws = workspace(q.device, _decode_ws_bytes(B, Hq, Hkv, T, N, D, split), "decode_partial")
+    ws = workspace(q.device, _decode_ws_bytes(B, Hq, Hkv, T, N, D, split, q.device.index), "decode_partial")
     rc = lib().lb2_attn_decode_partial(_ptr(q), i64(*q.stride()[:3]), _ptr(k), i64(*k.stride()[:3]), _ptr(v),
                                        i64(*v.stride()[:3]), _ptr(part_o), _ptr(part_lse), _ptr(kv_len), B, Hq, Hkv,
                                        T, N, D, dtype_code(q), float(scale), int(split), _ptr(ws), ws.numel(),
