@@ -128,6 +128,14 @@ int lb2_attn_decode_noalloc(const void* q, const int64_t* q_st, const void* k, c
 int lb2_attn_combine(const float* part_o, const float* part_lse, int R, int B, int Hq, int T, int D, void* o,
                      const int64_t* o_st, int dtype, void* stream);
 
+/* lb2_attn_combine over the buffer an all-gather of packed partials produces: for each of the R ranks, its o rows
+ * (rows * D floats) then its lse values (rows floats), the ranks' blocks back to back (rows * (D + 1) floats
+ * each). A rank packs its partial in place (lb2_attn_decode_partial into the two parts of one buffer), so the
+ * exchange is one all-gather and the merge reads the gathered buffer as it lands, with no copy between. Same
+ * merge and reference as lb2_attn_combine. */
+int lb2_attn_combine_packed(const float* packed, int R, int B, int Hq, int T, int D, void* o, const int64_t* o_st,
+                            int dtype, void* stream);
+
 /* ------------------------------------------------------------------------------------------------------------
  * Gated-DeltaNet recurrence, one position at a time (decode steps, short verify passes).
  *

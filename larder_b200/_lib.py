@@ -31,6 +31,7 @@ SIGNATURES = {
     "lb2_attn_decode_noalloc": ([_p, _i64p, _p, _i64p, _p, _i64p, _p, _i64p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _i,
                                  _i, _p], _i),
     "lb2_attn_combine": ([_p, _p, _i, _i, _i, _i, _i, _p, _i64p, _i, _p], _i),
+    "lb2_attn_combine_packed": ([_p, _i, _i, _i, _i, _i, _p, _i64p, _i, _p], _i),
     "lb2_gdn_recurrent": ([_p, _p, _i, _p, _i, _p, _i, _i, _p, _i, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p], _i),
     "lb2_gdn_chunked_workspace_size": ([_i, _i, _i, _i, _i, _i], _sz),
     "lb2_gdn_chunked": ([_p, _p, _i, _p, _i, _p, _i, _p, _i, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p, _sz, _p], _i),

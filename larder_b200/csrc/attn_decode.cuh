@@ -698,25 +698,27 @@ __global__ void __launch_bounds__(256) split_combine_kernel(const Params p) {
   }
 }
 
-// Merges R rank partials (normalised o, natural-log lse) row by row: one warp per row.
+// Merges R rank partials (normalised o, natural-log lse) row by row: one warp per row. Partial r's o rows start at
+// part_o + r so, its lse values at part_lse + r sl (floats).
 template <typename T>
 __global__ void combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse, int R,
-                               int rows, int Hq, int Tq, int D, void* o, int64_t o0, int64_t o1, int64_t o2) {
+                               int64_t so, int64_t sl, int rows, int Hq, int Tq, int D, void* o, int64_t o0,
+                               int64_t o1, int64_t o2) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   float M = -INFINITY;
-  for (int r = 0; r < R; ++r) M = fmaxf(M, part_lse[size_t(r) * rows + row]);
+  for (int r = 0; r < R; ++r) M = fmaxf(M, part_lse[r * sl + row]);
   const float Mu = M == -INFINITY ? 0.f : M;
   float wsum = 0.f;
-  for (int r = 0; r < R; ++r) wsum += __expf(part_lse[size_t(r) * rows + row] - Mu);
+  for (int r = 0; r < R; ++r) wsum += __expf(part_lse[r * sl + row] - Mu);
   const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
   const int t = row % Tq, h = (row / Tq) % Hq, b = row / (Tq * Hq);
   T* orow = reinterpret_cast<T*>(o) + b * o0 + int64_t(h) * o1 + int64_t(t) * o2;
   for (int d = lane; d < D; d += 32) {
     float x = 0.f;
     for (int r = 0; r < R; ++r)
-      x += __expf(part_lse[size_t(r) * rows + row] - Mu) * part_o[(size_t(r) * rows + row) * D + d];
+      x += __expf(part_lse[r * sl + row] - Mu) * part_o[r * so + int64_t(row) * D + d];
     orow[d] = from_f<T>(x * inv);
   }
 }

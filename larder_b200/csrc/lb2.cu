@@ -477,26 +477,40 @@ int lb2_attn_decode_noalloc(const void* q, const int64_t* q_st, const void* k, c
                      causal, split, ws, LB2_NOALLOC_SCRATCH_BYTES, stream);
 }
 
-int lb2_attn_combine(const float* part_o, const float* part_lse, int R, int B, int Hq, int T, int D, void* o,
-                     const int64_t* o_st, int dtype, void* stream) {
+static int combine_partials(const float* part_o, int64_t so, const float* part_lse, int64_t sl, int R, int B, int Hq,
+                            int T, int D, void* o, const int64_t* o_st, int dtype, void* stream) {
   LB2_CHECK_ARG(R > 0 && B > 0 && Hq > 0 && T > 0 && D > 0, "combine: empty shape");
+  LB2_CHECK_ARG(int64_t(B) * Hq * T < (int64_t(1) << 31), "combine: too many rows");
   const int rows = B * Hq * T;
   const int warps = 8;
   dim3 grid((rows + warps - 1) / warps);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == LB2_BF16)
-    decode::combine_kernel<__nv_bfloat16><<<grid, warps * 32, 0, st>>>(part_o, part_lse, R, rows, Hq, T, D, o,
+    decode::combine_kernel<__nv_bfloat16><<<grid, warps * 32, 0, st>>>(part_o, part_lse, R, so, sl, rows, Hq, T, D, o,
                                                                        o_st[0], o_st[1], o_st[2]);
   else if (dtype == LB2_F16)
-    decode::combine_kernel<__half><<<grid, warps * 32, 0, st>>>(part_o, part_lse, R, rows, Hq, T, D, o, o_st[0],
-                                                                o_st[1], o_st[2]);
+    decode::combine_kernel<__half><<<grid, warps * 32, 0, st>>>(part_o, part_lse, R, so, sl, rows, Hq, T, D, o,
+                                                                o_st[0], o_st[1], o_st[2]);
   else if (dtype == LB2_F32)
-    decode::combine_kernel<float><<<grid, warps * 32, 0, st>>>(part_o, part_lse, R, rows, Hq, T, D, o, o_st[0],
-                                                               o_st[1], o_st[2]);
+    decode::combine_kernel<float><<<grid, warps * 32, 0, st>>>(part_o, part_lse, R, so, sl, rows, Hq, T, D, o,
+                                                               o_st[0], o_st[1], o_st[2]);
   else
     return fail(LB2_EINVAL, "combine: dtype");
   LB2_CUDA(cudaGetLastError());
   return LB2_OK;
+}
+
+int lb2_attn_combine(const float* part_o, const float* part_lse, int R, int B, int Hq, int T, int D, void* o,
+                     const int64_t* o_st, int dtype, void* stream) {
+  const int64_t rows = int64_t(B) * Hq * T;
+  return combine_partials(part_o, rows * D, part_lse, rows, R, B, Hq, T, D, o, o_st, dtype, stream);
+}
+
+int lb2_attn_combine_packed(const float* packed, int R, int B, int Hq, int T, int D, void* o, const int64_t* o_st,
+                            int dtype, void* stream) {
+  const int64_t rows = int64_t(B) * Hq * T;
+  return combine_partials(packed, rows * (D + 1), packed + rows * D, rows * (D + 1), R, B, Hq, T, D, o, o_st, dtype,
+                          stream);
 }
 
 

@@ -144,13 +144,21 @@ def attn_decode(q, k, v, scale, causal=False, kv_len=None, split=0, out=None):
     return out
 
 
-def attn_decode_partial(q, k, v, scale, kv_len=None, split=0):
-    """This KV range's normalised partial output (fp32 [B, Hq, T, D]) and log-sum-exp (fp32 [B, Hq, T])."""
+def attn_decode_partial(q, k, v, scale, kv_len=None, split=0, out=None):
+    """This KV range's normalised partial output (fp32 [B, Hq, T, D]) and log-sum-exp (fp32 [B, Hq, T]); `out`, a
+    pair of contiguous fp32 tensors of those shapes (for instance the two parts of one packed exchange buffer),
+    receives them when given."""
     _cuda(q, k, v, kv_len)
     B, Hq, T, D = q.shape
     Hkv, N = k.shape[1], k.shape[2]
-    part_o = torch.empty((B, Hq, T, D), dtype=torch.float32, device=q.device)
-    part_lse = torch.empty((B, Hq, T), dtype=torch.float32, device=q.device)
+    if out is None:
+        part_o = torch.empty((B, Hq, T, D), dtype=torch.float32, device=q.device)
+        part_lse = torch.empty((B, Hq, T), dtype=torch.float32, device=q.device)
+    else:
+        part_o, part_lse = out
+        for t, shp in ((part_o, (B, Hq, T, D)), (part_lse, (B, Hq, T))):
+            if t.dtype != torch.float32 or tuple(t.shape) != shp or not t.is_contiguous() or t.device != q.device:
+                raise ValueError(f"attn_decode_partial: out must be contiguous fp32 {shp} on q's device")
     ws = workspace(q.device, _decode_ws_bytes(B, Hq, Hkv, T, N, D, split, q.device.index), "decode_partial")
     rc = lib().lb2_attn_decode_partial(_ptr(q), i64(*q.stride()[:3]), _ptr(k), i64(*k.stride()[:3]), _ptr(v),
                                        i64(*v.stride()[:3]), _ptr(part_o), _ptr(part_lse), _ptr(kv_len), B, Hq, Hkv,
@@ -170,6 +178,19 @@ def attn_combine(part_o, part_lse, dtype, out=None):
     rc = lib().lb2_attn_combine(_ptr(part_o), _ptr(part_lse), R, B, Hq, T, D, _ptr(out), i64(*out.stride()[:3]),
                                 dtype_code(out), _stream(part_o))
     check(rc, "attn_combine")
+    return out
+
+
+def attn_combine_packed(gathered, R, B, Hq, T, D, dtype, out=None):
+    """Merge R partials from an all-gathered packed buffer: R blocks of [o rows (B Hq T D) | lse (B Hq T)] fp32."""
+    _cuda(gathered)
+    if gathered.dtype != torch.float32 or not gathered.is_contiguous() or gathered.numel() != R * B * Hq * T * (D + 1):
+        raise ValueError("attn_combine_packed: gathered must be contiguous fp32 of R * B * Hq * T * (D + 1) values")
+    if out is None:
+        out = torch.empty((B, Hq, T, D), dtype=dtype, device=gathered.device)
+    rc = lib().lb2_attn_combine_packed(_ptr(gathered), R, B, Hq, T, D, _ptr(out), i64(*out.stride()[:3]),
+                                       dtype_code(out), _stream(gathered))
+    check(rc, "attn_combine_packed")
     return out
 
 

@@ -6,13 +6,15 @@ The reference is single-process and single-GPU (no collective exists in it); the
     kernel on it locally -- no exchange at all (weak scaling). `sequence_shard` gives the share.
   * long-context decode by KV range: each sequence's KV cache is cut into R contiguous ranges, one per rank,
     resident on that rank. Each rank computes its range's normalised partial output and log-sum-exp
-    (lb2_attn_decode_partial), the ranks exchange them with one all-gather of a packed [o | lse] buffer (about
-    B * Hq * T * (D + 1) * 4 bytes a rank), and every rank merges them with the log-sum-exp combine kernel
-    (lb2_attn_combine): o = sum_r exp(lse_r - lse*) o_r / sum_r exp(lse_r - lse*), the merge of foldattn_merge
+    (lb2_attn_decode_partial, written straight into a packed [o rows | lse] buffer), the ranks exchange them with one
+    all-gather of that buffer (about B * Hq * T * (D + 1) * 4 bytes a rank), and every rank merges the gathered
+    blocks in place with the log-sum-exp combine kernel (lb2_attn_combine_packed): o = sum_r exp(lse_r - lse*) o_r / sum_r exp(lse_r - lse*), the merge of foldattn_merge
     (foldattn.py:188-211) and cpu_kern.cpp:607-628 taken across GPUs.
 
-`partial_fn` / `combine_fn` default to this package's CUDA entry points; tests on CPU ranks (gloo) pass the CPU
-oracle instead, as the checker of the exchange itself.
+`partial_fn(q, k, v, scale, kv_len, part_o, part_lse)` fills a rank's partial into the two parts of its packed buffer
+and `combine_fn(gathered [world, rows * (D + 1)], (B, Hq, T, D), dtype)` merges the gathered blocks in place; both
+default to this package's CUDA entry points (lb2_attn_decode_partial, lb2_attn_combine_packed). Tests on CPU ranks
+(gloo) pass the CPU oracle instead, as the checker of the exchange itself.
 """
 import datetime
 
@@ -46,12 +48,13 @@ def kv_range(n_keys, rank, world):
     return sequence_shard(n_keys, rank, world)
 
 
-def _cuda_partial(q, k, v, scale, kv_len):
-    return ops.attn_decode_partial(q, k, v, scale, kv_len=kv_len)
+def _cuda_partial(q, k, v, scale, kv_len, part_o, part_lse):
+    ops.attn_decode_partial(q, k, v, scale, kv_len=kv_len, out=(part_o, part_lse))
 
 
-def _cuda_combine(part_o, part_lse, dtype):
-    return ops.attn_combine(part_o, part_lse, dtype)
+def _cuda_combine(gathered, shape, dtype):
+    B, Hq, T, D = shape
+    return ops.attn_combine_packed(gathered, gathered.shape[0], B, Hq, T, D, dtype)
 
 
 def kv_sharded_decode(q, k_local, v_local, scale, kv_len_local=None, group=None, partial_fn=None, combine_fn=None,
@@ -65,15 +68,14 @@ def kv_sharded_decode(q, k_local, v_local, scale, kv_len_local=None, group=None,
     combine_fn = combine_fn or _cuda_combine
     world = dist.get_world_size(group)
     B, Hq, T, D = q.shape
-    part_o, part_lse = partial_fn(q, k_local, v_local, scale, kv_len_local)
     rows = B * Hq * T
-    packed = torch.cat([part_o.reshape(rows, D), part_lse.reshape(rows, 1)], dim=1).contiguous()
-    gathered = torch.empty((world * rows, D + 1), dtype=packed.dtype, device=packed.device)
+    # the partial lands packed in one buffer, [o rows | lse], the all-gather's input as it stands
+    packed = torch.empty(rows * (D + 1), dtype=torch.float32, device=q.device)
+    partial_fn(q, k_local, v_local, scale, kv_len_local, packed[:rows * D].view(B, Hq, T, D),
+               packed[rows * D:].view(B, Hq, T))
+    gathered = torch.empty(world * rows * (D + 1), dtype=torch.float32, device=q.device)
     dist.all_gather_into_tensor(gathered, packed, group=group)
-    gathered = gathered.view(world, rows, D + 1)
-    go = gathered[:, :, :D].reshape(world, B, Hq, T, D)
-    gl = gathered[:, :, D].reshape(world, B, Hq, T)
-    return combine_fn(go, gl, out_dtype or q.dtype)
+    return combine_fn(gathered.view(world, rows * (D + 1)), (B, Hq, T, D), out_dtype or q.dtype)
 
 
 def sharded_prefill(q, k, v, scale, mask="causal", gate=None, rank=None, world=None):

@@ -32,8 +32,9 @@ def _free_port():
     return port
 
 
-def _oracle_partial(q, k, v, scale, kv_len):
-    """Per-range normalised output and natural-log LSE, from the f64 reference (test checker)."""
+def _oracle_partial(q, k, v, scale, kv_len, part_o, part_lse):
+    """Per-range normalised output and natural-log LSE, from the f64 reference (test checker), into the packed
+    buffer's two parts."""
     qn, kn, vn = (t.double().numpy() for t in (q, k, v))
     G = qn.shape[1] // kn.shape[1]
     kr, vr = np.repeat(kn, G, 1), np.repeat(vn, G, 1)
@@ -42,10 +43,15 @@ def _oracle_partial(q, k, v, scale, kv_len):
     p = np.exp(s - m)
     lse = (m + np.log(p.sum(-1, keepdims=True)))[..., 0]
     o = (p / p.sum(-1, keepdims=True)) @ vr
-    return torch.from_numpy(o).float(), torch.from_numpy(lse).float()
+    part_o.copy_(torch.from_numpy(o).float())
+    part_lse.copy_(torch.from_numpy(lse).float())
 
 
-def _torch_combine(po, pl, dtype):
+def _torch_combine(gathered, shape, dtype):
+    B, Hq, T, D = shape
+    world, rows = gathered.shape[0], B * Hq * T
+    po = gathered[:, :rows * D].reshape(world, B, Hq, T, D)
+    pl = gathered[:, rows * D:].reshape(world, B, Hq, T)
     w = torch.softmax(pl, dim=0)
     return (w[..., None] * po).sum(0).to(dtype)
 
