@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Benchmark of the attention / Gated-DeltaNet hot path on B200, one JSON line on rank 0.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--section decode,prefill,gdn]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--section decode,prefill,gdn,sharded,glue]
 
 Headline (`value`): decode KV-read GB/s on BASELINE.json's configs[1] -- batch 16, 32 query / 4 KV heads x 128,
 bf16 KV cache with per-sequence lengths uniform in [1024, 8192], one query token each. A step is one split-KV decode
@@ -191,6 +191,11 @@ def run_ours(args):
             out["gdn"] = bench_gdn(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_over_ranks)
         except Exception as e:
             out["gdn"] = {"error": f"{type(e).__name__}: {e}"}
+    if "glue" in sections:
+        try:
+            out["glue"] = bench_glue(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_over_ranks)
+        except Exception as e:
+            out["glue"] = {"error": f"{type(e).__name__}: {e}"}
     st = ops.status(local)
     out["device_status"] = st
 
@@ -443,6 +448,55 @@ def bench_sharded(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, 
             "scaling": "weak", "workload": "configs[4] share of one rank (exactly configs[4] at 8 GPUs)"}
 
 
+def bench_glue(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_over_ranks):
+    """The attention layer's glue (layer_glue.py:578-619) over configs[2]'s 8192 prefill rows (16q/2kv x 256, a
+    quarter of each head rotated): q / k RMSNorm + RoPE, then the output gate; HBM streams, so GB/s of the bytes
+    each kernel must move. Two input sets alternate so that consecutive steps miss L2 (each set > 126 MB)."""
+    from larder_b200 import layer_glue
+    g = torch.Generator(device=dev).manual_seed(7000 + rank)
+    B, S, NQ, NK, D, R = 1, 8192, 16, 2, 256, 64
+    sets = []
+    for _ in range(2):
+        qg = torch.randn(B, S, NQ * 2 * D, generator=g, device=dev).to(torch.bfloat16)
+        kr = torch.randn(B, S, NK * D, generator=g, device=dev).to(torch.bfloat16)
+        o = torch.randn(B, S, NQ * D, generator=g, device=dev).to(torch.bfloat16)
+        sets.append((qg, kr, o))
+    qw = (1 + 0.1 * torch.randn(D, generator=g, device=dev)).to(torch.bfloat16)
+    kw = (1 + 0.1 * torch.randn(D, generator=g, device=dev)).to(torch.bfloat16)
+    pos = torch.arange(S, device=dev, dtype=torch.float64)[:, None]
+    ang = pos * 10000.0 ** (-torch.arange(R // 2, device=dev, dtype=torch.float64) * 2 / R)[None]
+    ang = torch.cat([ang, ang], 1)
+    cos, sin = ang.cos().float(), ang.sin().float()
+    gated = torch.empty(B, S, NQ * D, dtype=torch.bfloat16, device=dev)
+
+    def qk(i):
+        qg, kr, _ = sets[i % 2]
+        layer_glue.qk_norm_rope(qg, kr, qw, kw, 1e-6, cos, sin, NQ, NK)
+
+    def gate(i):
+        qg, _, o = sets[i % 2]
+        layer_glue.out_gate(o, qg, NQ, result=gated)
+
+    res = {}
+    # bytes each must move: qk reads the query halves of qg, kr, cos / sin and writes q, k; the gate reads o and the
+    # gate halves of qg and writes the result
+    qk_bytes = B * S * (NQ * D + NK * D) * 2 * 2 + S * R * 4 * 2
+    gate_bytes = B * S * NQ * D * 2 * 3
+    for name, fn, nbytes, kern in (("qk_norm_rope", qk, qk_bytes, "lb2::aglue::qk_norm_rope_kernel<256>"),
+                                   ("out_gate", gate, gate_bytes, "lb2::aglue::out_gate_kernel<256>")):
+        for i in range(args.warmup):
+            fn(i)
+        barrier_sync()
+        ms = max_over_ranks(cuda_time(torch, fn, args.steps, stream)) / args.steps
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        res[name] = {"value": round(world * gbs, 1), "unit": "GB/s", "ms_per_step": round(ms, 5),
+                     "bytes_per_step": nbytes, "gpu_launches_per_step": 1,
+                     "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                  "frac": round(gbs / pk["hbm_gbs"], 4), "kernel": kern}}
+    res["workload"] = "configs[2]'s 8192 prefill rows, 16q/2kv x 256, RoPE over the first 64 dims, bf16"
+    return res
+
+
 def bench_gdn(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_over_ranks):
     """the GDN decode step at B = 16 (state GB/s) and the 8192-token chunked prefill."""
     g = torch.Generator(device=dev).manual_seed(4000 + rank)
@@ -610,7 +664,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--section", default="decode,prefill,gdn,sharded")
+    ap.add_argument("--section", default="decode,prefill,gdn,sharded,glue")
     ap.add_argument("--split", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()

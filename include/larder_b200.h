@@ -201,6 +201,28 @@ int lb2_gdn_step_glue(const void* conv, const void* a, const void* b, const floa
 int lb2_gdn_norm_gate(const void* x, const void* z, const void* w, void* out, int64_t R, int D, int dtype, float eps,
                       void* stream);
 
+/* ------------------------------------------------------------------------------------------------------------
+ * The attention layer's glue on either side of the SDPA (bf16 rows).
+ *
+ * q / k RMSNorm + rotate-half RoPE: for each row (b, s) and each of the NQ query and NK key heads, x = the head's D
+ * values (query head h: columns [2hD, 2hD + D) of q_proj's output qg [B, S, NQ * 2D], whose other half is the output
+ * gate; key head h: columns [hD, hD + D) of k_proj's output kr [B, S, NK * D]):
+ *   inv = 1 / sqrt(sum(x^2) / D + eps) (fp32), o_j = bf16(w_j * bf16(x_j * inv)),
+ *   j < R: r_j = bf16(bf16(o_j * bf16(cos_j)) + bf16(rot_j * bf16(sin_j))), rot_j = -o_{j+R/2} (j < R/2) else
+ *   o_{j-R/2}; j >= R: r_j = o_j,
+ * into q [B, NQ, S, D] and k [B, NK, S, D]. cos / sin [S, R] contiguous, cs_dtype LB2_F32 / BF16 / F16; norm weights
+ * [D] bf16. D in {128, 256, 512}, R even and <= D. Rows, outputs and weights 16-byte aligned, contiguous.
+ * Replaces: the qk kernel of layer_glue.py:241-286 as attn_step calls it (layer_glue.py:592-597). */
+int lb2_attn_qk_norm_rope(const void* qg, const void* kr, const void* q_norm_w, const void* k_norm_w, float eps,
+                          const void* cos, const void* sin, int cs_dtype, void* q, void* k, int B, int S, int NQ,
+                          int NK, int D, int R, int dtype, void* stream);
+
+/* Output gate: out[r, hD + j] = bf16(o[r, hD + j] * bf16(sigmoid(qg[r, 2hD + D + j]))) over `rows` rows of NQ heads
+ * (o, out [rows, NQ * D], qg [rows, NQ * 2D], bf16, contiguous, 16-byte aligned; out may be o).
+ * Replaces: the agate kernel of layer_glue.py:288-296 (attn_step, layer_glue.py:614-617), whose sigmoid is a
+ * table of bf16(sigmoid(x)) for every bf16 pattern x. */
+int lb2_attn_out_gate(const void* o, const void* qg, void* out, int64_t rows, int NQ, int D, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

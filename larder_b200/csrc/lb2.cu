@@ -12,6 +12,7 @@
 #include "attn_prefill2.cuh"
 #include "gdn_chunked.cuh"
 #include "attn_f32.cuh"
+#include "attn_glue.cuh"
 #include "kv_gather.cuh"
 #include "gdn_glue.cuh"
 
@@ -813,6 +814,60 @@ int lb2_gdn_norm_gate(const void* x, const void* z, const void* w, void* out, in
     glue::norm_gate_kernel<float><<<grid, 128, 0, st>>>(static_cast<const float*>(x), static_cast<const float*>(z),
                                                         static_cast<const float*>(w), static_cast<float*>(out), R, D,
                                                         eps);
+  LB2_CUDA(cudaGetLastError());
+  return LB2_OK;
+}
+
+int lb2_attn_qk_norm_rope(const void* qg, const void* kr, const void* q_norm_w, const void* k_norm_w, float eps,
+                          const void* cos, const void* sin, int cs_dtype, void* q, void* k, int B, int S, int NQ,
+                          int NK, int D, int R, int dtype, void* stream) {
+  LB2_CHECK_ARG(B >= 0 && S >= 0 && NQ > 0 && NK > 0, "qk_norm_rope: shape");
+  LB2_CHECK_ARG(dtype == LB2_BF16, "qk_norm_rope: bf16 rows only (the reference's path)");
+  LB2_CHECK_ARG(cs_dtype >= LB2_F32 && cs_dtype <= LB2_F16, "qk_norm_rope: cos / sin dtype");
+  LB2_CHECK_ARG(D == 128 || D == 256 || D == 512, "qk_norm_rope: head dim 128, 256 or 512");
+  LB2_CHECK_ARG(R >= 0 && R <= D && R % 2 == 0, "qk_norm_rope: rope dims must be even and at most the head dim");
+  for (const void* ptr : {qg, kr, q_norm_w, k_norm_w, static_cast<const void*>(q), static_cast<const void*>(k)})
+    LB2_CHECK_ARG(aligned16(ptr), "qk_norm_rope: rows and weights 16-byte aligned");
+  const int64_t items = int64_t(B) * S * (NQ + NK);
+  if (items == 0) return LB2_OK;
+  LB2_CHECK_ARG(R == 0 || (cos && sin), "qk_norm_rope: cos / sin missing");
+  LB2_CHECK_ARG(int64_t(B) * S < (int64_t(1) << 31), "qk_norm_rope: too many rows");
+  aglue::QkParams p{static_cast<const __nv_bfloat16*>(qg), static_cast<const __nv_bfloat16*>(kr),
+                    static_cast<const __nv_bfloat16*>(q_norm_w), static_cast<const __nv_bfloat16*>(k_norm_w), cos, sin,
+                    cs_dtype, eps, static_cast<__nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(k), B, S, NQ, NK, R};
+  const dim3 grid(unsigned((int64_t(B) * S + aglue::ROWS - 1) / aglue::ROWS),
+                  unsigned((NQ + NK + aglue::WARPS - 1) / aglue::WARPS));
+  LB2_CHECK_ARG(grid.y < 65536, "qk_norm_rope: too many heads");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (D == 128)
+    aglue::qk_norm_rope_kernel<128><<<grid, aglue::WARPS * 32, 0, st>>>(p);
+  else if (D == 256)
+    aglue::qk_norm_rope_kernel<256><<<grid, aglue::WARPS * 32, 0, st>>>(p);
+  else
+    aglue::qk_norm_rope_kernel<512><<<grid, aglue::WARPS * 32, 0, st>>>(p);
+  LB2_CUDA(cudaGetLastError());
+  return LB2_OK;
+}
+
+int lb2_attn_out_gate(const void* o, const void* qg, void* out, int64_t rows, int NQ, int D, int dtype, void* stream) {
+  LB2_CHECK_ARG(rows >= 0 && NQ > 0, "out_gate: shape");
+  LB2_CHECK_ARG(dtype == LB2_BF16, "out_gate: bf16 rows only (the reference's path)");
+  LB2_CHECK_ARG(D == 128 || D == 256 || D == 512, "out_gate: head dim 128, 256 or 512");
+  LB2_CHECK_ARG(aligned16(o) && aligned16(qg) && aligned16(out), "out_gate: rows 16-byte aligned");
+  const int64_t items = rows * NQ;
+  if (items == 0) return LB2_OK;
+  LB2_CHECK_ARG(rows < (int64_t(1) << 31), "out_gate: too many rows");
+  aglue::GateParams p{static_cast<const __nv_bfloat16*>(o), static_cast<const __nv_bfloat16*>(qg),
+                      static_cast<__nv_bfloat16*>(out), rows, NQ};
+  const dim3 grid(unsigned(rows), unsigned((NQ + aglue::WARPS - 1) / aglue::WARPS));
+  LB2_CHECK_ARG(grid.y < 65536, "out_gate: too many heads");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (D == 128)
+    aglue::out_gate_kernel<128><<<grid, aglue::WARPS * 32, 0, st>>>(p);
+  else if (D == 256)
+    aglue::out_gate_kernel<256><<<grid, aglue::WARPS * 32, 0, st>>>(p);
+  else
+    aglue::out_gate_kernel<512><<<grid, aglue::WARPS * 32, 0, st>>>(p);
   LB2_CUDA(cudaGetLastError());
   return LB2_OK;
 }

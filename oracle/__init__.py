@@ -207,3 +207,51 @@ def compute_g(A_log, a, dt_bias):
 
 def sigmoid(x):
     return (1.0 / (1.0 + np.exp(-np.asarray(x, dtype=np.float64)))).astype(np.float32)
+
+
+# ---------------------------------------------------------------------------------------------- attention glue
+
+def _bf(x):
+    """float32 values rounded to bf16 (nearest even), kept as float32."""
+    return bf16_to_f32(f32_to_bf16(np.asarray(x, dtype=np.float32)))
+
+
+def qk_norm_rope(qg, kr, qw, kw, eps, cs, sn, NQ, NK):
+    """The reference's qk kernel (layer_glue.py:241-286) restated on the CPU, bf16 as uint16 bits.
+
+    qg [B, S, NQ * 2D] (each query head's D values, then its D gate values), kr [B, S, NK * D], qw / kw [D];
+    cs / sn [S, R] float32 (the kernel casts them to bf16). For each head row x: inv = 1 / sqrt(sum(x^2) / D + eps),
+    o = bf16(w * bf16(x * inv)); on the first R dims r = bf16(bf16(o * bf16(cos)) + bf16(rot * bf16(sin))) with
+    rot = (-o[R/2:R], o[:R/2]). Returns q [B, NQ, S, D] and k [B, NK, S, D] bf16 bits. The sum of squares runs in
+    float64 here, the reference's in an fp32 tree: where x * inv sits on a bf16 rounding boundary the two can
+    differ by one bf16 step."""
+    qg, kr = np.asarray(qg, np.uint16), np.asarray(kr, np.uint16)
+    B, S = qg.shape[:2]
+    D = qg.shape[-1] // (2 * NQ)
+    cs, sn = np.asarray(cs, np.float32).reshape(S, -1), np.asarray(sn, np.float32).reshape(S, -1)
+    R = cs.shape[-1]
+    c, s_ = _bf(cs)[None, :, None, :], _bf(sn)[None, :, None, :]
+
+    def rows(x, w):
+        ms = (x.astype(np.float64) ** 2).sum(-1, keepdims=True) / D
+        inv = (np.float32(1) / np.sqrt((ms.astype(np.float32) + np.float32(eps)).astype(np.float32))).astype(np.float32)
+        o = _bf(bf16_to_f32(w) * _bf(x * inv))
+        if R:
+            rot = np.concatenate([-o[..., R // 2:R], o[..., :R // 2]], axis=-1)
+            o = o.copy()
+            o[..., :R] = _bf(_bf(o[..., :R] * c) + _bf(rot * s_))
+        return np.ascontiguousarray(o.transpose(0, 2, 1, 3))
+
+    xq = bf16_to_f32(qg).reshape(B, S, NQ, 2 * D)[..., :D]
+    xk = bf16_to_f32(kr).reshape(B, S, NK, D)
+    return f32_to_bf16(rows(xq, qw)), f32_to_bf16(rows(xk, kw))
+
+
+def out_gate(o, qg, NQ):
+    """The reference's agate kernel (layer_glue.py:288-296) restated: out = bf16(o * bf16(sigmoid(gate))), gate the
+    second half of each head's 2D columns of qg; o [..., NQ * D], qg [..., NQ * 2D], bf16 bits."""
+    o, qg = np.asarray(o, np.uint16), np.asarray(qg, np.uint16)
+    D = o.shape[-1] // NQ
+    g = bf16_to_f32(qg).reshape(-1, NQ, 2 * D)[..., D:]
+    sig = _bf(sigmoid(g))
+    return f32_to_bf16(bf16_to_f32(o).reshape(-1, NQ, D) * sig).reshape(o.shape)

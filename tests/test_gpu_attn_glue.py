@@ -1,0 +1,96 @@
+"""The attention layer's glue on the GPU (layer_glue.py:241-296, attn_step :578-619): q / k RMSNorm + rotate-half
+RoPE and the output gate, against the CPU restatement of the reference's kernels with its bf16 rounding points.
+
+The bar is the reference's own for its 16-bit CUDA paths (test_qsa_cuda.py:144, :163-164): at least 99 % of the
+outputs bit-equal and none more than one bf16 step away (the sums of squares run in different fp32 orders)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from gpu_util import to_np, to_torch
+from larder_b200 import layer_glue, ops
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _status_clean():
+    yield
+    assert ops.status() == 0, "a device wait gave up"
+
+
+def rope_tables(S, R, offset=0, base=10000.0):
+    """cos / sin [S, R] of positions offset .. offset + S - 1 (rotate-half layout: both halves repeat the angles)."""
+    pos = np.arange(offset, offset + S, dtype=np.float64)[:, None]
+    ang = pos * base ** (-np.arange(R // 2) * 2.0 / R)[None]
+    ang = np.concatenate([ang, ang], axis=1)
+    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+def assert_bf16_close(got, ref):
+    """got / ref bf16 bit patterns: >= 99 % equal, every other one a single bf16 step away."""
+    g, r = got.astype(np.int32).ravel(), ref.astype(np.int32).ravel()
+    same = g == r
+    assert same.mean() >= 0.99, f"only {same.mean():.4f} bit-equal"
+    gf, rf = oracle.bf16_to_f32(got).ravel(), oracle.bf16_to_f32(ref).ravel()
+    step = np.abs(oracle.bf16_to_f32((r & 0xFFFF).astype(np.uint16) ^ 1) - rf)  # one ulp at ref's magnitude
+    assert np.all(np.abs(gf - rf) <= step * 1.0001 + 1e-30), float(np.max(np.abs(gf - rf)))
+
+
+def inputs(B, S, NQ, NK, D, R, seed, offset=0):
+    rng = np.random.default_rng(seed)
+    qg = oracle.f32_to_bf16(rng.standard_normal((B, S, NQ * 2 * D)).astype(np.float32) * 3)
+    kr = oracle.f32_to_bf16(rng.standard_normal((B, S, NK * D)).astype(np.float32) * 3)
+    qw = oracle.f32_to_bf16((1 + 0.2 * rng.standard_normal(D)).astype(np.float32))
+    kw = oracle.f32_to_bf16((1 + 0.2 * rng.standard_normal(D)).astype(np.float32))
+    cs, sn = rope_tables(S, R, offset)
+    return qg, kr, qw, kw, cs, sn
+
+
+@pytest.mark.parametrize("B, S, NQ, NK, D, R, cs_dt", [
+    (1, 1, 16, 2, 256, 64, oracle.F32),     # a decode row of configs[2]'s model (partial rope, a quarter)
+    (2, 37, 16, 2, 256, 64, oracle.BF16),   # prefill rows, batch of two, bf16 tables
+    (1, 5, 32, 4, 128, 128, oracle.F32),    # configs[4]'s heads, full rope
+    (1, 3, 4, 1, 512, 0, oracle.F32),       # no rope
+])
+def test_qk_norm_rope_matches_oracle(B, S, NQ, NK, D, R, cs_dt):
+    qg, kr, qw, kw, cs, sn = inputs(B, S, NQ, NK, D, R, seed=B * 100 + S, offset=4093)
+    rq, rk = oracle.qk_norm_rope(qg, kr, qw, kw, 1e-6, oracle.bf16_to_f32(oracle.f32_to_bf16(cs))
+                                 if cs_dt == oracle.BF16 else cs,
+                                 oracle.bf16_to_f32(oracle.f32_to_bf16(sn)) if cs_dt == oracle.BF16 else sn, NQ, NK)
+    dt = torch.bfloat16 if cs_dt == oracle.BF16 else torch.float32
+    q, k = layer_glue.qk_norm_rope(to_torch(qg, oracle.BF16), to_torch(kr, oracle.BF16), to_torch(qw, oracle.BF16),
+                                   to_torch(kw, oracle.BF16), 1e-6, torch.from_numpy(cs).to(dt).cuda(),
+                                   torch.from_numpy(sn).to(dt).cuda(), NQ, NK)
+    assert tuple(q.shape) == (B, NQ, S, D) and tuple(k.shape) == (B, NK, S, D)
+    assert_bf16_close(to_np(q), rq)
+    assert_bf16_close(to_np(k), rk)
+
+
+def test_qk_norm_rope_empty_and_rejects():
+    qg, kr, qw, kw, cs, sn = inputs(1, 0, 4, 1, 128, 64, seed=3)
+    t = lambda a: to_torch(a, oracle.BF16)
+    q, k = layer_glue.qk_norm_rope(t(qg), t(kr), t(qw), t(kw), 1e-6, torch.from_numpy(cs).cuda(),
+                                   torch.from_numpy(sn).cuda(), 4, 1)
+    assert q.shape == (1, 4, 0, 128) and k.shape == (1, 1, 0, 128)
+    qg, kr, qw, kw, cs, sn = inputs(1, 2, 4, 1, 128, 64, seed=4)
+    with pytest.raises(ValueError):  # odd rope width
+        layer_glue.qk_norm_rope(t(qg), t(kr), t(qw), t(kw), 1e-6, torch.from_numpy(cs[:, :63]).cuda(),
+                                torch.from_numpy(sn[:, :63]).cuda(), 4, 1)
+    with pytest.raises(ValueError):  # fp16 rows: the reference's path is bf16
+        layer_glue.qk_norm_rope(t(qg).half(), t(kr).half(), t(qw), t(kw), 1e-6, torch.from_numpy(cs).cuda(),
+                                torch.from_numpy(sn).cuda(), 4, 1)
+
+
+@pytest.mark.parametrize("rows, NQ, D", [(1, 16, 256), (4099, 16, 256), (33, 32, 128)])
+def test_out_gate_matches_oracle_and_in_place(rows, NQ, D):
+    rng = np.random.default_rng(rows)
+    o = oracle.f32_to_bf16(rng.standard_normal((rows, NQ * D)).astype(np.float32))
+    qg = oracle.f32_to_bf16((rng.standard_normal((rows, NQ * 2 * D)) * 4).astype(np.float32))
+    ref = oracle.out_gate(o, qg, NQ)
+    ot, qt = to_torch(o, oracle.BF16), to_torch(qg, oracle.BF16)
+    got = layer_glue.out_gate(ot, qt, NQ)
+    assert_bf16_close(to_np(got), ref)
+    layer_glue.out_gate(ot, qt, NQ, result=ot)  # in place
+    assert np.array_equal(to_np(ot), to_np(got))

@@ -86,3 +86,39 @@ def test_fully_masked_leading_block_is_finite():
     ref = oracle.attn_ref64(q, k, v, 0.125, m)
     assert np.isfinite(o).all()
     checks.attn_close(o, ref, oracle.F32)
+
+
+def test_glue_oracle_against_float64_definitions():
+    """The CPU restatement of the reference's qk / agate kernels against the plain definitions in float64 (RMSNorm
+    with weight, rotate-half RoPE on the first R dims, sigmoid gate), the restatement's bf16 roundings being the only
+    difference."""
+    rng = np.random.default_rng(11)
+    B, S, NQ, NK, D, R = 2, 4, 3, 2, 128, 64
+    qg = oracle.f32_to_bf16(rng.standard_normal((B, S, NQ * 2 * D)).astype(np.float32))
+    kr = oracle.f32_to_bf16(rng.standard_normal((B, S, NK * D)).astype(np.float32))
+    w = oracle.f32_to_bf16((1 + 0.1 * rng.standard_normal(D)).astype(np.float32))
+    ang = np.arange(S)[:, None] * 10000.0 ** (-np.arange(R // 2) * 2.0 / R)[None]
+    cs, sn = np.cos(np.concatenate([ang, ang], 1)), np.sin(np.concatenate([ang, ang], 1))
+    q, k = oracle.qk_norm_rope(qg, kr, w, w, 1e-6, cs.astype(np.float32), sn.astype(np.float32), NQ, NK)
+
+    def ref(x, heads):
+        """(result, the magnitude the roundings scale with: each RoPE product is rounded before the sum)."""
+        x = x.reshape(B, S, heads, -1)[..., :D].astype(np.float64)
+        o = x / np.sqrt((x * x).mean(-1, keepdims=True) + 1e-6) * oracle.bf16_to_f32(w).astype(np.float64)
+        rot = np.concatenate([-o[..., R // 2:R], o[..., :R // 2]], -1)
+        mag = np.abs(o).copy()
+        mag[..., :R] = np.abs(o[..., :R] * cs[None, :, None]) + np.abs(rot * sn[None, :, None])
+        o[..., :R] = o[..., :R] * cs[None, :, None] + rot * sn[None, :, None]
+        return o.transpose(0, 2, 1, 3), mag.transpose(0, 2, 1, 3)
+
+    for got, x, heads in ((q, oracle.bf16_to_f32(qg), NQ), (k, oracle.bf16_to_f32(kr), NK)):
+        r, mag = ref(x, heads)
+        # up to five bf16 roundings stack (x inv, w, cos / sin, each product, the sum): a semantic pin (norm formula,
+        # rotate-half pairing), which a wrong convention misses by order one
+        assert np.all(np.abs(oracle.bf16_to_f32(got) - r) <= 8 * 2.0 ** -8 * mag + 1e-6)
+    o = oracle.f32_to_bf16(rng.standard_normal((S, NQ * D)).astype(np.float32))
+    g = oracle.f32_to_bf16(rng.standard_normal((S, NQ * 2 * D)).astype(np.float32))
+    gate = oracle.bf16_to_f32(g).reshape(S, NQ, 2 * D)[..., D:].astype(np.float64)
+    want = oracle.bf16_to_f32(o).reshape(S, NQ, D) / (1 + np.exp(-gate))
+    got = oracle.bf16_to_f32(oracle.out_gate(o, g, NQ)).reshape(S, NQ, D)
+    assert np.all(np.abs(got - want) <= 2 * 2.0 ** -8 * np.abs(want) + 1e-30)
