@@ -336,18 +336,19 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
     }
   }
   __syncthreads();
-  // 5. U' = T diag(beta) V, then W = T diag(beta Gam) K (TF32 mma), rows 16 w .. 16 w + 15: warp w scales its own
-  // rows of T by the column factors (beta, then Gam on top), so the B fragments are the 16-bit tiles' exact TF32
-  // values. T is lower triangular, so only k < 16 (w + 1) contributes.
+  // 5. U' = T diag(beta) V, then W = T diag(beta Gam) K (TF32 mma). Warp w takes output columns 32 w .. 32 w + 31 of
+  // all four 16-row blocks (T is lower triangular, so row block m reads k < 16 (m + 1): split by rows, the last
+  // warp would do four times the first's work). The column factors (beta, then Gam on top) are folded into T first,
+  // warp w scaling rows 16 w .., so that the B fragments are the 16-bit tiles' exact TF32 values.
   {
     float* Wg = unit_ptr(p, b, h, c) + WS_W;
     float* Ug = unit_ptr(p, b, h, c) + WS_U;
-    const int r = lane >> 2, cq = lane & 3, m0 = warp * 16;
+    const int r = lane >> 2, cq = lane & 3, nw = warp * 32;
 #pragma unroll 1
     for (int which = 1; which >= 0; --which) {
       const T* R = which ? Vb : Kb;
-      __syncwarp();
-      {  // lane l scales columns l and l + 32 of the warp's rows (the lower triangle: columns < m0 + 16)
+      {  // lane l scales columns l and l + 32 of rows 16 w .. 16 w + 15 (the lower triangle: columns < 16 w + 16)
+        const int m0 = warp * 16;
         const float f0 = which ? bet[lane] : Gam[lane], f1 = which ? bet[lane + 32] : Gam[lane + 32];
 #pragma unroll
         for (int rr = 0; rr < 16; ++rr) {
@@ -355,36 +356,38 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
           if (m0 >= 16) Af[(m0 + rr) * AP + lane + 32] *= f1;
         }
       }
-      __syncwarp();
+      __syncthreads();
 #pragma unroll 1
-      for (int nh = 0; nh < 2; ++nh) {  // two halves of 64 columns, to bound registers
-        float acc[8][4];
+      for (int mt = 0; mt < 4; ++mt) {
+        const int m0 = mt * 16;
+        float acc[4][4];
 #pragma unroll
-        for (int n = 0; n < 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
-        for (int k0 = 0; k0 < 16 * (warp + 1); k0 += 8) {
+        for (int n = 0; n < 4; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+        for (int k0 = 0; k0 < m0 + 16; k0 += 8) {
           const uint32_t a0 = tf32(Af[(m0 + r) * AP + k0 + cq]), a1 = tf32(Af[(m0 + r + 8) * AP + k0 + cq]);
           const uint32_t a2 = tf32(Af[(m0 + r) * AP + k0 + cq + 4]), a3 = tf32(Af[(m0 + r + 8) * AP + k0 + cq + 4]);
 #pragma unroll
-          for (int n = 0; n < 8; ++n) {
-            const int n0 = nh * 64 + n * 8;
+          for (int n = 0; n < 4; ++n) {
+            const int n0 = nw + n * 8;
             mma_tf32(acc[n], a0, a1, a2, a3, tf32_of(R[(k0 + cq) * KP + n0 + r]),
                      tf32_of(R[(k0 + cq + 4) * KP + n0 + r]));
           }
         }
         if (!which)  // W is an MMA operand of the scan: stored rounded to TF32; U' stays fp32
 #pragma unroll
-          for (int n = 0; n < 8; ++n)
+          for (int n = 0; n < 4; ++n)
 #pragma unroll
             for (int e = 0; e < 4; ++e) acc[n][e] = __uint_as_float(tf32(acc[n][e]));
 #pragma unroll
-        for (int n = 0; n < 8; ++n) {  // W rows of stride WP; U' in slices of DVB columns, rows of stride UP
-          const int col = nh * 64 + n * 8 + 2 * cq;
+        for (int n = 0; n < 4; ++n) {  // W rows of stride WP; U' in slices of DVB columns, rows of stride UP
+          const int col = nw + n * 8 + 2 * cq;
           float* g0 = which ? Ug + ((col / DVB) * C + m0 + r) * UP + col % DVB : Wg + (m0 + r) * WP + col;
           float* g1 = g0 + 8 * (which ? UP : WP);
           *reinterpret_cast<float2*>(g0) = make_float2(acc[n][0], acc[n][1]);
           *reinterpret_cast<float2*>(g1) = make_float2(acc[n][2], acc[n][3]);
         }
       }
+      __syncthreads();  // every warp has read T before it is scaled again
     }
   }
   // 7. gamma and Gam for the scan
