@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Benchmark of the attention / Gated-DeltaNet hot path on B200, one JSON line on rank 0.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--section decode,prefill,gdn,sharded,glue]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--section decode,prefill,gdn,sharded,glue,qsa]
 
 Headline (`value`): decode KV-read GB/s on BASELINE.json's configs[1] -- batch 16, 32 query / 4 KV heads x 128,
 bf16 KV cache with per-sequence lengths uniform in [1024, 8192], one query token each. A step is one split-KV decode
@@ -191,6 +191,11 @@ def run_ours(args):
             out["gdn"] = bench_gdn(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_over_ranks)
         except Exception as e:
             out["gdn"] = {"error": f"{type(e).__name__}: {e}"}
+    if "qsa" in sections:
+        try:
+            out["qsa"] = bench_qsa(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_over_ranks)
+        except Exception as e:
+            out["qsa"] = {"error": f"{type(e).__name__}: {e}"}
     if "glue" in sections:
         try:
             out["glue"] = bench_glue(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_over_ranks)
@@ -448,6 +453,36 @@ def bench_sharded(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, 
             "scaling": "weak", "workload": "configs[4] share of one rank (exactly configs[4] at 8 GPUs)"}
 
 
+def bench_qsa(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_over_ranks):
+    """The QSA indexer's block selection (qwen4_exp_vendor.py:271-292) for decode rows of Flash-Next's indexer (4
+    heads x 128, compress ratio 4, budget 2048: the top 512 blocks) at 131072 tokens (32768 pooled blocks), 16 rows a
+    step, one sequence each: the scores stream every pooled key once (HBM), then a radix select a row on a cluster
+    of CTAs. Two input sets alternate so that consecutive steps miss L2."""
+    from larder_b200 import qsa
+    g = torch.Generator(device=dev).manual_seed(8000 + rank)
+    B, H, D, cr, nb, k = 16, 4, 128, 4, 32768, 512
+    sets = [(torch.randn(B, 1, H, D, generator=g, device=dev).to(torch.bfloat16),
+             torch.randn(B, nb, D, generator=g, device=dev).to(torch.bfloat16)) for _ in range(2)]
+    offset = nb * cr
+
+    def step(i):
+        q, pooled = sets[i % 2]
+        qsa.qsa_select(q, pooled, offset, cr, k)
+
+    for i in range(args.warmup):
+        step(i)
+    barrier_sync()
+    ms = max_over_ranks(cuda_time(torch, step, args.steps, stream)) / args.steps
+    nbytes = B * nb * D * 2 + B * H * D * 2 + B * nb * 4 * 2 + B * k * 4  # keys and q in; scores out and back; picks
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"value": round(world * gbs, 1), "unit": "GB/s", "ms_per_step": round(ms, 5), "bytes_per_step": nbytes,
+            "gpu_launches_per_step": 2,
+            "workload": "16 decode rows, Flash-Next indexer (4 x 128, CR 4, top 512) over 32768 pooled blocks each",
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / pk["hbm_gbs"], 4),
+                         "kernel": "lb2::qsasel::score_kernel<128> + topk_kernel<16>"}}
+
+
 def bench_glue(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_over_ranks):
     """The attention layer's glue (layer_glue.py:578-619) over configs[2]'s 8192 prefill rows (16q/2kv x 256, a
     quarter of each head rotated): q / k RMSNorm + RoPE, then the output gate; HBM streams, so GB/s of the bytes
@@ -664,7 +699,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--section", default="decode,prefill,gdn,sharded,glue")
+    ap.add_argument("--section", default="decode,prefill,gdn,sharded,glue,qsa")
     ap.add_argument("--split", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()

@@ -223,6 +223,22 @@ int lb2_attn_qk_norm_rope(const void* qg, const void* kr, const void* q_norm_w, 
  * table of bf16(sigmoid(x)) for every bf16 pattern x. */
 int lb2_attn_out_gate(const void* o, const void* qg, void* out, int64_t rows, int NQ, int D, int dtype, void* stream);
 
+/* ------------------------------------------------------------------------------------------------------------
+ * QSA indexer block selection: the top-k part of the indexer (qwen4_exp_vendor.py:271-292, stream_fast.py's
+ * `select`, :6243-6305), given its normalised and rotated q [B, S, H, D] and pooled block keys [B, ., D] (bf16,
+ * batch stride pool_bstride elements, rows 0 .. n_blocks - 1 used). For each row (b, s) at position offset + s:
+ *   score_n = sum_h max(q_h . pooled_n, 0) / div (fp32; the reference divides by sqrt(head_dim)),
+ *   -inf for n >= (offset + s + 1) / cr (blocks not yet complete),
+ * and top [B, S, k] int32: the indices of the k largest finite scores in ascending order (the order `tb` takes in
+ * stream_fast.py:6478-6491), ties at the threshold lowest index first (the reference's argpartition leaves ties
+ * unspecified), padded with n_blocks where fewer than k blocks are candidates (the reference's
+ * where(picked, top, n_blocks)). The workspace (lb2_qsa_select_workspace_size) holds each row's scores after the
+ * call, [B * S, n_blocks] fp32. H <= 8, D in {64, 128}, B * S < 65536. */
+size_t lb2_qsa_select_workspace_size(int B, int S, int n_blocks);
+int lb2_qsa_select(const void* q, const void* pooled, int64_t pool_bstride, int B, int S, int H, int D, int n_blocks,
+                   int64_t offset, int cr, int k, float div, void* workspace, size_t workspace_bytes, int32_t* top,
+                   void* stream);
+
 #ifdef __cplusplus
 }
 #endif

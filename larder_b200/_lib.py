@@ -42,6 +42,9 @@ SIGNATURES = {
     "lb2_gdn_norm_gate": ([_p, _p, _p, _p, ctypes.c_int64, _i, _i, _f, _p], _i),
     "lb2_attn_qk_norm_rope": ([_p, _p, _p, _p, _f, _p, _p, _i, _p, _p, _i, _i, _i, _i, _i, _i, _i, _p], _i),
     "lb2_attn_out_gate": ([_p, _p, _p, ctypes.c_int64, _i, _i, _i, _p], _i),
+    "lb2_qsa_select_workspace_size": ([_i, _i, _i], _sz),
+    "lb2_qsa_select": ([_p, _p, ctypes.c_int64, _i, _i, _i, _i, _i, ctypes.c_int64, _i, _i, _f, _p, _sz, _p, _p],
+                       _i),
 }
 
 _lib = None

@@ -74,23 +74,6 @@ struct Cfg {
 
 // ---------------------------------------------------------------------------------------------- cluster helpers
 
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-// Address of the same shared-memory word in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
 // Arrive on an mbarrier anywhere in the cluster. The arriving warps order their tcgen05 loads / stores before it
 // with tcgen05.fence::before_thread_sync, the MMA thread orders its MMAs after the wait with
 // tcgen05.fence::after_thread_sync.

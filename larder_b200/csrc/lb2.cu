@@ -13,6 +13,7 @@
 #include "gdn_chunked.cuh"
 #include "attn_f32.cuh"
 #include "attn_glue.cuh"
+#include "qsa_select.cuh"
 #include "kv_gather.cuh"
 #include "gdn_glue.cuh"
 
@@ -869,6 +870,94 @@ int lb2_attn_out_gate(const void* o, const void* qg, void* out, int64_t rows, in
   else
     aglue::out_gate_kernel<512><<<grid, aglue::WARPS * 32, 0, st>>>(p);
   LB2_CUDA(cudaGetLastError());
+  return LB2_OK;
+}
+
+size_t lb2_qsa_select_workspace_size(int B, int S, int n_blocks) {
+  if (B < 0 || S < 0 || n_blocks < 0) return 0;
+  return size_t(int64_t(B) * S * n_blocks * int64_t(sizeof(float))) + 256;
+}
+
+int lb2_qsa_select(const void* q, const void* pooled, int64_t pool_bstride, int B, int S, int H, int D, int n_blocks,
+                   int64_t offset, int cr, int k, float div, void* workspace, size_t workspace_bytes, int32_t* top,
+                   void* stream) {
+  LB2_CHECK_ARG(B >= 0 && S >= 0 && n_blocks >= 0 && k >= 0, "qsa_select: shape");
+  LB2_CHECK_ARG(H >= 1 && H <= 8, "qsa_select: 1 to 8 indexer heads");
+  LB2_CHECK_ARG(D == 64 || D == 128, "qsa_select: indexer head dim 64 or 128");
+  LB2_CHECK_ARG(cr >= 1 && div > 0.f, "qsa_select: compress ratio and divisor must be positive");
+  LB2_CHECK_ARG(int64_t(B) * S < 65536, "qsa_select: at most 65535 query rows a call");
+  LB2_CHECK_ARG(pool_bstride >= int64_t(n_blocks) * D, "qsa_select: pooled rows overlap across the batch");
+  LB2_CHECK_ARG(aligned16(pooled) && aligned16(q) && pool_bstride % 8 == 0, "qsa_select: q and pooled keys 16-byte aligned");
+  LB2_CHECK_ARG(workspace_bytes >= lb2_qsa_select_workspace_size(B, S, n_blocks) && aligned16(workspace),
+                "qsa_select: workspace too small or misaligned");
+  const int rows = B * S;
+  if (rows == 0 || k == 0) return LB2_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float* scores = static_cast<float*>(workspace);
+  if (n_blocks > 0) {
+    const int chunk = qsasel::SC_STAGE / (D * 2);
+    const int ipr = (n_blocks + chunk - 1) / chunk;
+    qsasel::ScoreParams p{static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(pooled),
+                          pool_bstride, scores, B, S, H, n_blocks, cr, ipr, int64_t(rows) * ipr, offset, div};
+    auto kern = D == 128 ? qsasel::score_kernel<128> : qsasel::score_kernel<64>;
+    // persistent: as many CTAs as are resident at once (cached per device and head dim)
+    static int res_dev[2] = {-1, -1}, resident[2] = {0, 0};
+    const int di = D == 128 ? 1 : 0;
+    int dev = 0;
+    LB2_CUDA(cudaGetDevice(&dev));
+    if (res_dev[di] != dev) {
+      int sms = 0, per_sm = 0;
+      LB2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, qsasel::SC_SMEM));
+      LB2_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+      LB2_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, qsasel::SC_THREADS, qsasel::SC_SMEM));
+      if (per_sm < 1) return fail(LB2_ECUDA, "qsa_select: the score kernel does not fit an SM");
+      resident[di] = sms * per_sm;
+      res_dev[di] = dev;
+    }
+    const int64_t grid = std::min<int64_t>(p.items, resident[di]);
+    kern<<<static_cast<unsigned>(grid), qsasel::SC_THREADS, qsasel::SC_SMEM, st>>>(p);
+    LB2_CUDA(cudaGetLastError());
+  }
+  // A cluster of CTAs a row: the size topk_cluster picks for the row length, halved while the rows' clusters would
+  // not all be resident at once and the halves still hold their scores in registers.
+  auto topk_for = [](int per) {
+    return per <= 8 ? qsasel::topk_kernel<8> : per <= 16 ? qsasel::topk_kernel<16> : qsasel::topk_kernel<qsasel::TK_PER>;
+  };
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(qsasel::TK_THREADS);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // overlaps the score grid's tail
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  int cl = qsasel::topk_cluster(n_blocks);
+  static int fit_dev = -1, fit[4][3];  // resident clusters of (size 1, 2, 4, 8) x (topk_kernel<8>, <16>, <32>)
+  int dev = 0;
+  LB2_CUDA(cudaGetDevice(&dev));
+  if (fit_dev != dev) {
+    for (int a = 0; a < 4; ++a)
+      for (int b = 0; b < 3; ++b) {
+        attr[0].val.clusterDim.x = 1u << a;
+        cfg.gridDim = dim3(1u << a);
+        cfg.numAttrs = 1;
+        LB2_CUDA(cudaOccupancyMaxActiveClusters(&fit[a][b], topk_for(8 << b), &cfg));
+      }
+    fit_dev = dev;
+  }
+  auto fits = [&](int c) {
+    const int per = qsasel::topk_per(n_blocks, c);
+    const int a = c == 1 ? 0 : c == 2 ? 1 : c == 4 ? 2 : 3, b = per <= 8 ? 0 : per <= 16 ? 1 : 2;
+    return rows <= fit[a][b];
+  };
+  while (cl > 1 && !fits(cl) && qsasel::topk_per(n_blocks, cl / 2) <= qsasel::TK_PER) cl /= 2;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(cl);
+  cfg.gridDim = dim3(static_cast<unsigned>(cl), static_cast<unsigned>(rows));
+  cfg.numAttrs = 2;
+  LB2_CUDA(cudaLaunchKernelEx(&cfg, topk_for(qsasel::topk_per(n_blocks, cl)), static_cast<const float*>(scores),
+                              n_blocks, k, top));
   return LB2_OK;
 }
 

@@ -255,3 +255,26 @@ def out_gate(o, qg, NQ):
     g = bf16_to_f32(qg).reshape(-1, NQ, 2 * D)[..., D:]
     sig = _bf(sigmoid(g))
     return f32_to_bf16(bf16_to_f32(o).reshape(-1, NQ, D) * sig).reshape(o.shape)
+
+
+# ---------------------------------------------------------------------------------------------- QSA block selection
+
+def qsa_select(q, pooled, offset, cr, k, div):
+    """The indexer's scores and top-k (qwen4_exp_vendor.py:271-292) in float64, bf16 inputs as uint16 bits: q
+    [B, S, H, D], pooled [B, n_blocks, D]. Returns (top [B, S, k] int ascending, ties lowest index first, padded
+    with n_blocks; scores [B, S, n_blocks] float64 with -inf for blocks not yet complete)."""
+    qf = bf16_to_f32(q).astype(np.float64)
+    pf = bf16_to_f32(pooled).astype(np.float64)
+    B, S, H, D = qf.shape
+    nb = pf.shape[1]
+    sc = np.maximum(np.einsum("bshd,bnd->bsnh", qf, pf), 0).sum(-1) / div
+    n_complete = np.maximum(offset + np.arange(S) + 1, 0) // cr
+    sc = np.where(np.arange(nb)[None, None, :] < n_complete[None, :, None], sc, -np.inf)
+    top = np.full((B, S, k), nb, dtype=np.int64)
+    for b in range(B):
+        for s in range(S):
+            fin = np.isfinite(sc[b, s])
+            kk = min(k, int(fin.sum()))
+            order = np.argsort(-sc[b, s], kind="stable")[:kk]
+            top[b, s, :kk] = np.sort(order)
+    return top, sc
