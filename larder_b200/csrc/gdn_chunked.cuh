@@ -400,7 +400,7 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
 
 // ------------------------------------------------------------------------------------------------ scan
 
-constexpr int SCAN_THREADS = 256;  // warps 0-3: U = U' - W S^T; warps 4-7: Q S^T and M U; all 8: the state update
+constexpr int SCAN_THREADS = 256;  // warps 0-3: U = U' - W S^T and the state update; warps 4-7: Q S^T and M U
 constexpr int UQ = 68;             // u32 row stride of the transposed U tiles [DVB][C] (conflict-free ldmatrix)
 
 struct ScanSmem {
@@ -463,11 +463,40 @@ __device__ __forceinline__ void scan_prefetch(const Params& p, const CUtensorMap
   }
 }
 
-// One CTA: value rows dv0 .. dv0 + 31 of one (batch, v-head), all chunks in order. The fp32 state slice lives in
-// registers, warp w owning key columns 16 w .. 16 w + 15 of all 32 rows; a TF32 copy in shared memory feeds the
-// products that read the whole slice. Per chunk: (1) warps 0-3 form U = U' - W S^T (16 positions each) while warps
-// 4-7 form Gam Q S^T; (2) all warps update their state columns with U^T diag(exp(gamma_C - gamma)) K while warps
-// 4-7 add M U to Y and store it.
+// Named barriers (ids 1-4; 0 is __syncthreads): wait until `count` threads arrived, or arrive without waiting. The
+// arriving threads' earlier shared-memory writes are visible to the threads that waited.
+__device__ __forceinline__ void nbar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void nbar_arrive(int id, int count) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+// bar.sync that also ORs a flag over the participating threads.
+__device__ __forceinline__ bool nbar_sync_or(int id, int count, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(uint32_t(v)), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+constexpr int BAR_A = 1;   // all 256: U of the chunk written, every read of the state copy done
+constexpr int BAR_S = 2;   // warps 0-3 arrive, warps 4-7 wait: the state copy updated
+constexpr int BAR_U = 3;   // warps 4-7 arrive, warps 0-3 wait: M U read the chunk's U and its buffer is done with
+constexpr int BAR_S0 = 4;  // warps 0-3: the state copy updated, before their next W S^T
+
+// One CTA: value rows dv0 .. dv0 + 31 of one (batch, v-head), all chunks in order. Two roles, so that Y stays off the
+// chain from one chunk's state to the next:
+//   warps 0-3 own the fp32 state slice in registers (warp w: key columns 32 w .. 32 w + 31 of all 32 rows; a TF32
+//     copy in shared memory feeds the products that read the whole slice). Per chunk: U = U' - W S^T (16 positions
+//     each), then the state update S <- Gam_C S + (diag(exp(gamma_C - gamma)) U)^T K on their columns;
+//   warps 4-7 form Gam Q S^T beside W S^T, then M U and the Y store while warps 0-3 update the state, and wait for
+//     the updated copy before the next chunk's Q S^T.
+// Barrier order a chunk: warps 0-3 wait BAR_U (M U of the chunk before is done, so U and that chunk's buffer are
+// free: the next chunk's copies are issued), W S^T, write U, BAR_A, update, arrive BAR_S, sync BAR_S0; warps 4-7 wait
+// BAR_S (the state copy of this chunk is complete), Q S^T, BAR_A, M U, store Y, arrive BAR_U. A wait that gave up in
+// any thread is ORed at BAR_A and every warp leaves the loop there.
 template <typename T>
 __global__ void __launch_bounds__(SCAN_THREADS, 1) scan_kernel(const __grid_constant__ CUtensorMap qmap,
                                                                 const __grid_constant__ CUtensorMap kmap,
@@ -491,54 +520,53 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) scan_kernel(const __grid_cons
     fence_barrier_init();
   }
 
-  // the state tile of this warp: rows mt * 16 + r (+ 8), columns 16 warp + 8 n + 2 cq (+ 1)
-  float sreg[2][2][4];
+  // warps 0-3: the state tile of this warp, rows mt * 16 + r (+ 8), columns 32 warp + 8 n + 2 cq (+ 1)
+  const bool chain = warp < 4;
+  float sreg[2][4][4];
   const float* sin = p.s_in + (int64_t(b) * p.Hv + h) * DV * DK;
+  if (chain) {
 #pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
+    for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-    for (int n = 0; n < 2; ++n)
+      for (int n = 0; n < 4; ++n)
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int i = mt * 16 + r + 8 * hh, d = warp * 16 + n * 8 + 2 * cq;
-        const float2 v = *reinterpret_cast<const float2*>(sin + int64_t(dv0 + i) * DK + d);
-        sreg[mt][n][2 * hh] = v.x;
-        sreg[mt][n][2 * hh + 1] = v.y;
-        St[i * WP + d] = tf32(v.x);
-        St[i * WP + d + 1] = tf32(v.y);
-      }
-  __syncthreads();  // barriers initialised
+        for (int hh = 0; hh < 2; ++hh) {
+          const int i = mt * 16 + r + 8 * hh, d = warp * 32 + n * 8 + 2 * cq;
+          const float2 v = *reinterpret_cast<const float2*>(sin + int64_t(dv0 + i) * DK + d);
+          sreg[mt][n][2 * hh] = v.x;
+          sreg[mt][n][2 * hh + 1] = v.y;
+          St[i * WP + d] = tf32(v.x);
+          St[i * WP + d + 1] = tf32(v.y);
+        }
+  }
+  __syncthreads();  // barriers initialised, the state copy written
   if (p.nchunks > 0 && tid == 0) scan_prefetch(p, &qmap, &kmap, sm, &full[0], b, h, hk, 0, blk);
 
   bool ok = true;
-  int issued = p.nchunks > 0 ? 1 : 0;  // chunks whose copies were issued
+  int issued = p.nchunks > 0 ? 1 : 0;  // chunks whose copies were issued (thread 0)
+  const int m0 = (warp & 3) * 16;
   for (int c = 0; c < p.nchunks; ++c) {
+    const bool last = c + 1 == p.nchunks;
     uint8_t* buf = sm + (c & 1) * ScanSmem::BUF;
-    if (c + 1 < p.nchunks) {
-      if (tid == 0)
-        scan_prefetch(p, &qmap, &kmap, sm + ((c + 1) & 1) * ScanSmem::BUF, &full[(c + 1) & 1], b, h, hk, c + 1, blk);
-      issued = c + 2;
-    }
-    ok = mbar_wait(&full[c & 1], (c >> 1) & 1, 71);
-    if (__syncthreads_or(!ok)) {
-      ok = false;
-      break;
-    }
     const uint32_t* W = reinterpret_cast<const uint32_t*>(buf + ScanSmem::W);
     const float* U = reinterpret_cast<const float*>(buf + ScanSmem::U);
     const uint32_t* M = reinterpret_cast<const uint32_t*>(buf + ScanSmem::M);
     const uint8_t* Q = buf + ScanSmem::Q;
     const uint8_t* K = buf + ScanSmem::K;
     const float* G = reinterpret_cast<const float*>(buf + ScanSmem::G);
-    const int m0 = (warp & 3) * 16;
-
-    // (1) warps 0-3: acc = W S^T; warps 4-7: acc = Q S^T. Rows m0 .. m0 + 15, all 32 value columns.
     float acc[4][4];
 #pragma unroll
     for (int n = 0; n < 4; ++n)
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
-    if (warp < 4) {
+    if (chain) {
+      if (c > 0) nbar_sync(BAR_U, SCAN_THREADS);  // M U of chunk c - 1 done: U and that chunk's buffer are free
+      if (!last && tid == 0) {
+        scan_prefetch(p, &qmap, &kmap, sm + ((c + 1) & 1) * ScanSmem::BUF, &full[(c + 1) & 1], b, h, hk, c + 1, blk);
+        issued = c + 2;
+      }
+      ok = mbar_wait(&full[c & 1], (c >> 1) & 1, 71);
+      // (1) acc = W S^T: rows m0 .. m0 + 15, all 32 value columns
 #pragma unroll 4
       for (int k0 = 0; k0 < DK; k0 += 8) {
         uint32_t a[4], b01[4], b23[4];
@@ -563,6 +591,9 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) scan_kernel(const __grid_cons
           Ud[col * UQ + t] = tf32((e >> 1 ? dh : dl) * u);
         }
     } else {
+      if (c > 0) nbar_sync(BAR_S, SCAN_THREADS);  // the state copy of chunk c is complete
+      ok = mbar_wait(&full[c & 1], (c >> 1) & 1, 71);
+      // (1) acc = Gam Q S^T: rows m0 .. m0 + 15, all 32 value columns
 #pragma unroll 4
       for (int k0 = 0; k0 < DK; k0 += 8) {
         const uint32_t a0 = qk_tf32<T>(Q, m0 + r, k0 + cq), a1 = qk_tf32<T>(Q, m0 + r + 8, k0 + cq);
@@ -584,15 +615,17 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) scan_kernel(const __grid_cons
         acc[n][3] *= gh;
       }
     }
-    __syncthreads();  // U complete; every read of the state copy done
-
-    // (2) S <- Gam_C S + (diag(dec) U)^T K on this warp's 16 key columns (all 32 value rows)
-    {
+    if (nbar_sync_or(BAR_A, SCAN_THREADS, !ok)) {  // U complete; every read of the state copy done
+      ok = false;
+      break;
+    }
+    if (chain) {
+      // (2) S <- Gam_C S + (diag(dec) U)^T K on this warp's 32 key columns (all 32 value rows)
       const float gc = G[C + C - 1];
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-        for (int n = 0; n < 2; ++n)
+        for (int n = 0; n < 4; ++n)
 #pragma unroll
           for (int e = 0; e < 4; ++e) sreg[mt][n][e] *= gc;
 #pragma unroll 2
@@ -601,8 +634,8 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) scan_kernel(const __grid_cons
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt) frag_a(smem_u32(Ud), UQ, mt * 16, k0, lane, a[mt]);
 #pragma unroll
-        for (int n = 0; n < 2; ++n) {
-          const int col = warp * 16 + n * 8 + r;
+        for (int n = 0; n < 4; ++n) {
+          const int col = warp * 32 + n * 8 + r;
           const uint32_t b0 = qk_tf32<T>(K, k0 + cq, col), b1 = qk_tf32<T>(K, k0 + cq + 4, col);
 #pragma unroll
           for (int mt = 0; mt < 2; ++mt) mma_tf32(sreg[mt][n], a[mt][0], a[mt][1], a[mt][2], a[mt][3], b0, b1);
@@ -611,16 +644,19 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) scan_kernel(const __grid_cons
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-        for (int n = 0; n < 2; ++n)
+        for (int n = 0; n < 4; ++n)
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
-            const int i = mt * 16 + r + 8 * hh, d = warp * 16 + n * 8 + 2 * cq;
+            const int i = mt * 16 + r + 8 * hh, d = warp * 32 + n * 8 + 2 * cq;
             St[i * WP + d] = tf32(sreg[mt][n][2 * hh]);
             St[i * WP + d + 1] = tf32(sreg[mt][n][2 * hh + 1]);
           }
-    }
-    // (3) warps 4-7: Y = Gam Q S^T + M U (M lower triangular: k < m0 + 16), stored
-    if (warp >= 4) {
+      if (!last) {
+        nbar_arrive(BAR_S, SCAN_THREADS);
+        nbar_sync(BAR_S0, 128);
+      }
+    } else {
+      // (3) Y = Gam Q S^T + M U (M lower triangular: k < m0 + 16), stored
       for (int k0 = 0; k0 < m0 + 16; k0 += 8) {
         uint32_t a[4], b01[4], b23[4];
         frag_a(smem_u32(M), AP, m0, k0, lane, a);
@@ -631,6 +667,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) scan_kernel(const __grid_cons
         mma_tf32(acc[2], a[0], a[1], a[2], a[3], b23[0], b23[1]);
         mma_tf32(acc[3], a[0], a[1], a[2], a[3], b23[2], b23[3]);
       }
+      if (!last) nbar_arrive(BAR_U, SCAN_THREADS);  // done with U and with this chunk's buffer
       T* yg = static_cast<T*>(p.y);
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
@@ -645,23 +682,25 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) scan_kernel(const __grid_cons
         }
       }
     }
-    __syncthreads();  // the state copy complete and this chunk's buffer free before the next prefetch
   }
   if (!ok) {  // a wait gave up (status word set): let the copies still in flight land (bounded), write nothing
-    for (int c2 = max(0, issued - 2); c2 < issued; ++c2) mbar_wait(&full[c2 & 1], (c2 >> 1) & 1, 72);
+    if (tid == 0)
+      for (int c2 = max(0, issued - 2); c2 < issued; ++c2) mbar_wait(&full[c2 & 1], (c2 >> 1) & 1, 72);
     return;
   }
-  float* sout = p.s_out + (int64_t(b) * p.Hv + h) * DV * DK;
+  if (chain) {
+    float* sout = p.s_out + (int64_t(b) * p.Hv + h) * DV * DK;
 #pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
+    for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-    for (int n = 0; n < 2; ++n)
+      for (int n = 0; n < 4; ++n)
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int i = mt * 16 + r + 8 * hh, d = warp * 16 + n * 8 + 2 * cq;
-        *reinterpret_cast<float2*>(sout + int64_t(dv0 + i) * DK + d) =
-            make_float2(sreg[mt][n][2 * hh], sreg[mt][n][2 * hh + 1]);
-      }
+        for (int hh = 0; hh < 2; ++hh) {
+          const int i = mt * 16 + r + 8 * hh, d = warp * 32 + n * 8 + 2 * cq;
+          *reinterpret_cast<float2*>(sout + int64_t(dv0 + i) * DK + d) =
+              make_float2(sreg[mt][n][2 * hh], sreg[mt][n][2 * hh + 1]);
+        }
+  }
 }
 
 }  // namespace gdnchunk
