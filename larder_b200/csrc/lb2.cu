@@ -895,11 +895,11 @@ int lb2_qsa_select(const void* q, const void* pooled, int64_t pool_bstride, int 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   float* scores = static_cast<float*>(workspace);
   if (n_blocks > 0) {
-    const int chunk = qsasel::SC_STAGE / (D * 2);
-    const int ipr = (n_blocks + chunk - 1) / chunk;
+    const int ipr = (n_blocks + qsasel::SC_KEYS - 1) / qsasel::SC_KEYS;
     qsasel::ScoreParams p{static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(pooled),
                           pool_bstride, scores, B, S, H, n_blocks, cr, ipr, int64_t(rows) * ipr, offset, div};
     auto kern = D == 128 ? qsasel::score_kernel<128> : qsasel::score_kernel<64>;
+    const int smem = D == 128 ? qsasel::sc_smem(128) : qsasel::sc_smem(64);
     // persistent: as many CTAs as are resident at once (cached per device and head dim)
     static int res_dev[2] = {-1, -1}, resident[2] = {0, 0};
     const int di = D == 128 ? 1 : 0;
@@ -907,15 +907,15 @@ int lb2_qsa_select(const void* q, const void* pooled, int64_t pool_bstride, int 
     LB2_CUDA(cudaGetDevice(&dev));
     if (res_dev[di] != dev) {
       int sms = 0, per_sm = 0;
-      LB2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, qsasel::SC_SMEM));
+      LB2_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
       LB2_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-      LB2_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, qsasel::SC_THREADS, qsasel::SC_SMEM));
+      LB2_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, qsasel::SC_THREADS, smem));
       if (per_sm < 1) return fail(LB2_ECUDA, "qsa_select: the score kernel does not fit an SM");
       resident[di] = sms * per_sm;
       res_dev[di] = dev;
     }
     const int64_t grid = std::min<int64_t>(p.items, resident[di]);
-    kern<<<static_cast<unsigned>(grid), qsasel::SC_THREADS, qsasel::SC_SMEM, st>>>(p);
+    kern<<<static_cast<unsigned>(grid), qsasel::SC_THREADS, smem, st>>>(p);
     LB2_CUDA(cudaGetLastError());
   }
   // A cluster of CTAs a row: the size topk_cluster picks for the row length, halved while the rows' clusters would

@@ -7,8 +7,8 @@
 // threshold taken lowest index first, and a row with fewer than k candidates is padded with n_blocks (the
 // reference's `where(picked, top, n_blocks)`).
 //
-// Two kernels: the scores (an HBM stream over the pooled keys, bulk-copied into shared-memory stages, 8 blocks a
-// warp tile on mma.sync with the heads as rows), then a radix select a row on a cluster of CTAs (four 8-bit passes
+// Two kernels: the scores (an HBM stream over the pooled keys, bulk-copied into shared-memory stages, 16 keys a
+// warp tile on mma.sync with the heads as columns), then a radix select a row on a cluster of CTAs (four 8-bit passes
 // over order-preserving integer keys held in registers, warp-aggregated histogram increments) and an ordered
 // compaction that writes the picks in index order.
 #pragma once
@@ -32,34 +32,35 @@ struct ScoreParams {
 
 constexpr int SC_WARPS = 8;                      // consumer warps
 constexpr int SC_THREADS = (SC_WARPS + 1) * 32;  // and one producer warp
-constexpr int SC_STAGE = 16384;                  // bytes a stage: one chunk of keys (64 of 128 dims, 128 of 64)
-constexpr int SC_NS = 4;                         // stages
-constexpr int SC_SMEM = SC_NS * SC_STAGE + 2 * SC_NS * 8;
+constexpr int SC_KEYS = 16 * SC_WARPS;           // keys a chunk: 16 a consumer warp
+constexpr int SC_NS = 3;                         // stages
+__host__ __device__ constexpr int sc_stage(int D) { return SC_KEYS * D * 2; }  // bytes a stage: one chunk's keys
+__host__ __device__ constexpr int sc_smem(int D) { return SC_NS * sc_stage(D) + 2 * SC_NS * 8; }
 
-__device__ __forceinline__ void mma_bf16(float* c, uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+// D += A B, m16n8k16, bf16 operands, fp32 accumulators (a0..a3 and b0, b1 in the PTX fragment order).
+__device__ __forceinline__ void mma_bf16x(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                          uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Persistent CTAs over the items (row, chunk of SC_STAGE bytes of keys), each CTA a contiguous range of them. The
-// producer warp streams the chunks' keys (contiguous rows of the pooled buffer) into SC_NS shared-memory stages with
-// 1-D bulk copies; the eight consumer warps score 8 blocks a tile on mma.sync m16n8k16 (bf16 products, fp32 sums):
-// rows = the H <= 8 heads (rows 8-15 zero), columns = the blocks, K = the head dim. Lane (g = lane / 4, t = lane % 4)
-// reads block g's key 16 bytes at a time (elements 32 L + 8 t .. + 8 for L < D / 32), so the K order of the MMAs is
-// permuted, the same way for the query fragments: MMA 2 L + u takes, as its K pairs (2 t, 2 t + 1) and
-// (2 t + 8, 2 t + 9), elements 32 L + 8 t + 4 u + {0, 1} and + {2, 3}. The sums are unchanged. Lane (g, t) ends with
-// head g's dots with blocks 2 t, 2 t + 1; relu, then the sum over heads across the lanes of equal t. A partial last
-// chunk leaves stale rows in its stage: their columns are computed and dropped.
+// Persistent CTAs over the items (row, chunk of SC_KEYS keys), each CTA a contiguous range of them. The producer
+// warp streams the chunks' keys (contiguous rows of the pooled buffer) into SC_NS shared-memory stages with 1-D bulk
+// copies; consumer warp w scores keys 16 w .. 16 w + 15 of a chunk on mma.sync m16n8k16 (bf16 products, fp32 sums)
+// with the keys as the 16 rows, the H <= 8 query heads as the 8 columns (heads past H zero) and the head dim as K.
+// Lane (g = lane / 4, t = lane % 4) reads rows g and g + 8 16 bytes at a time (elements 32 L + 8 t .. + 8 for
+// L < D / 32), so the K order of the MMAs is permuted, the same way for the query fragments: MMA 2 L + u takes, as
+// its K pairs (2 t, 2 t + 1) and (2 t + 8, 2 t + 9), elements 32 L + 8 t + 4 u + {0, 1} and + {2, 3}. The sums are
+// unchanged. Lane (g, t) ends with keys g and g + 8 against heads 2 t, 2 t + 1: relu, add, then the sum over the
+// four lanes of the group. A partial last chunk leaves stale rows in its stage: their rows are computed and dropped.
 template <int D>
 __global__ void __launch_bounds__(SC_THREADS) score_kernel(const ScoreParams p) {
-  constexpr int KL = D / 32;                   // 16-byte pieces a lane per block key
-  constexpr int CH = SC_STAGE / (D * 2);       // blocks a chunk
-  constexpr int NT = CH / (8 * SC_WARPS);      // 8-block tiles a consumer warp per chunk
-  static_assert(NT * 8 * SC_WARPS == CH, "chunk split");
+  constexpr int KL = D / 32;          // 16-byte pieces a lane per key row
+  constexpr int STAGE = sc_stage(D);
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + SC_NS * SC_STAGE);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + SC_NS * STAGE);
   uint64_t* empty = full + SC_NS;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int64_t j0 = p.items * blockIdx.x / gridDim.x, j1 = p.items * (blockIdx.x + 1) / gridDim.x;
@@ -82,10 +83,10 @@ __global__ void __launch_bounds__(SC_THREADS) score_kernel(const ScoreParams p) 
         if (j >= SC_NS && !mbar_wait(&empty[st], ((j / SC_NS) - 1) & 1, 81)) break;
         const int64_t it = j0 + j;
         const int row = int(it / p.ipr), ch = int(it - int64_t(row) * p.ipr);
-        const int base = ch * CH, nb = min(CH, p.n_blocks - base);
+        const int base = ch * SC_KEYS, nb = min(SC_KEYS, p.n_blocks - base);
         const uint32_t bytes = uint32_t(nb) * D * 2;
         mbar_arrive_expect_tx(&full[st], bytes);
-        bulk_g2s(smem + st * SC_STAGE, p.pooled + int64_t(row / p.S) * p.pool_bstride + int64_t(base) * D, bytes,
+        bulk_g2s(smem + st * STAGE, p.pooled + int64_t(row / p.S) * p.pool_bstride + int64_t(base) * D, bytes,
                  &full[st]);
       }
       // the copies still in flight land before the CTA ends
@@ -95,7 +96,7 @@ __global__ void __launch_bounds__(SC_THREADS) score_kernel(const ScoreParams p) 
     return;
   }
   int cur_row = -1, n_complete = 0;
-  uint4 qa[KL];  // A fragments of the query heads (rows g < H), in the permuted K order
+  uint4 qb[KL];  // B fragments of the query heads (column g < H), in the permuted K order
   float* out = nullptr;
   for (int j = 0; j < n; ++j) {
     const int st = j % SC_NS;
@@ -105,41 +106,41 @@ __global__ void __launch_bounds__(SC_THREADS) score_kernel(const ScoreParams p) 
       cur_row = row;
       const uint4* qr = reinterpret_cast<const uint4*>(p.q + (int64_t(row) * p.H + g) * D) + t;
 #pragma unroll
-      for (int l = 0; l < KL; ++l) qa[l] = g < p.H ? qr[4 * l] : make_uint4(0u, 0u, 0u, 0u);
+      for (int l = 0; l < KL; ++l) qb[l] = g < p.H ? qr[4 * l] : make_uint4(0u, 0u, 0u, 0u);
       const int64_t pos = p.offset + (row % p.S);
       const int64_t nc = pos + 1 <= 0 ? 0 : (pos + 1) / p.cr;
       n_complete = nc < p.n_blocks ? int(nc) : p.n_blocks;
       out = p.scores + int64_t(row) * p.n_blocks;
     }
     if (!mbar_wait(&full[st], (j / SC_NS) & 1, 83)) break;
-    const uint8_t* stage = smem + st * SC_STAGE;
+    const int r16 = warp * 16;  // the warp's first key in the chunk
+    const uint4* pa = reinterpret_cast<const uint4*>(smem + st * STAGE + (r16 + g) * (D * 2)) + t;
+    const uint4* pb = pa + 8 * (D * 2 / 16);  // row g + 8
+    uint4 ra[KL], rb[KL];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const int r8 = (warp * NT + nt) * 8;  // the tile's first block in the chunk
-      const uint4* pr = reinterpret_cast<const uint4*>(stage + (r8 + g) * (D * 2)) + t;
-      uint4 bv[KL];
-#pragma unroll
-      for (int l = 0; l < KL; ++l) bv[l] = pr[4 * l];
-      float c[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int l = 0; l < KL; ++l) {
-        mma_bf16(c, qa[l].x, qa[l].y, bv[l].x, bv[l].y);
-        mma_bf16(c, qa[l].z, qa[l].w, bv[l].z, bv[l].w);
-      }
-      float s0 = fmaxf(c[0], 0.f), s1 = fmaxf(c[1], 0.f);  // head g, blocks 2t, 2t + 1 of the tile
-#pragma unroll
-      for (int o = 4; o < 32; o <<= 1) {
-        s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-      }
-      if (g == 0) {
-        const int m = ch * CH + r8 + 2 * t;
-        if (m < p.n_blocks) out[m] = m < n_complete ? s0 / p.div : -INFINITY;
-        if (m + 1 < p.n_blocks) out[m + 1] = m + 1 < n_complete ? s1 / p.div : -INFINITY;
-      }
+    for (int l = 0; l < KL; ++l) {
+      ra[l] = pa[4 * l];
+      rb[l] = pb[4 * l];
     }
     __syncwarp();  // the warp's reads of the stage are done
     if (lane == 0) mbar_arrive(&empty[st]);
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int l = 0; l < KL; ++l) {
+      mma_bf16x(c, ra[l].x, rb[l].x, ra[l].y, rb[l].y, qb[l].x, qb[l].y);
+      mma_bf16x(c, ra[l].z, rb[l].z, ra[l].w, rb[l].w, qb[l].z, qb[l].w);
+    }
+    float s0 = fmaxf(c[0], 0.f) + fmaxf(c[1], 0.f);  // key g, heads 2 t and 2 t + 1
+    float s1 = fmaxf(c[2], 0.f) + fmaxf(c[3], 0.f);  // key g + 8
+#pragma unroll
+    for (int o = 1; o < 4; o <<= 1) {
+      s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+      s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+    }
+    if (t < 2) {
+      const int m = ch * SC_KEYS + r16 + g + 8 * t;
+      if (m < p.n_blocks) out[m] = m < n_complete ? (t ? s1 : s0) / p.div : -INFINITY;
+    }
   }
 }
 

@@ -53,6 +53,7 @@ def inputs(B, S, NQ, NK, D, R, seed, offset=0):
     (2, 37, 16, 2, 256, 64, oracle.BF16),   # prefill rows, batch of two, bf16 tables
     (1, 5, 32, 4, 128, 128, oracle.F32),    # configs[4]'s heads, full rope
     (1, 3, 4, 1, 512, 0, oracle.F32),       # no rope
+    (1, 4, 8, 2, 256, 24, oracle.F32),      # a width that is not a multiple of 16: RoPE through shared memory
 ])
 def test_qk_norm_rope_matches_oracle(B, S, NQ, NK, D, R, cs_dt):
     qg, kr, qw, kw, cs, sn = inputs(B, S, NQ, NK, D, R, seed=B * 100 + S, offset=4093)
