@@ -42,8 +42,9 @@ int lb2_abi_version(void);
  * mpc_error(): one message slot, entry points return a status. */
 const char* lb2_error(void);
 
-/* Synchronises `stream`, then returns and clears the current device's status word: LB2_OK, or
- * LB2_ETIMEOUT | (where << 8) for the first device wait that gave up since the last call. */
+/* Synchronises `stream`, then returns and clears the current device's status word: LB2_OK, or, for the first event
+ * since the last call, LB2_ETIMEOUT | (where << 8) when a device wait gave up, LB2_EINVAL | (where << 8) when a
+ * kernel skipped an out-of-range index it was given (the KV home's LRU entry points). */
 int lb2_status(void* stream);
 
 /* ------------------------------------------------------------------------------------------------------------
@@ -179,11 +180,32 @@ int lb2_kv_gather_picks(const void* k, const int64_t* k_st, const void* v, const
  * uint64 device table (device memory or pinned, GPU-mapped host memory). put writes s new positions pos0.. of
  * k / v [Hk, s, D] (strides) into the home; gather reads the picked rows (as lb2_kv_gather_picks) from it, with
  * cache-bypassing loads. Replaces: kv_host's layout and its put / gather kernels (kv_host.py:17-18, :36-41,
- * :64-291, decode :612-648) without the VRAM LRU. */
+ * :64-291, decode :612-648); the VRAM LRU in front of it follows. */
 int lb2_kvh_put(const uint64_t* table, const void* k, const int64_t* k_st, const void* v, const int64_t* v_st,
                 int64_t pos0, int s, int Hk, int D, int dtype, int logc, void* stream);
 int lb2_kvh_gather(const uint64_t* table, const int32_t* tb, int nsel, int cr, int n, void* kg, void* vg, int Hk,
                    int D, int dtype, int logc, void* stream);
+
+/* The VRAM LRU in front of the home: a pool of ns slots in device memory, slot x holding one picked block's cr
+ * positions [K/V][Hk][cr][D] (pool [ns, 2, Hk, cr, D], the home's dtype), and its int32 device state, owned by the
+ * caller: slot_of [max_blocks] (-1 at first), block_of [ns] (-1), stamp [ns] (-1), ref [ns] (0), meta [4] (0:
+ * CLOCK hand, token count, hits, misses).
+ * plan: one token's picks tb [nsel] (distinct, sorted, 1 <= nsel <= 1024, ns >= ceil32(nsel)) -> sl [nsel]: the
+ *   hit's slot, -2 - victim for a miss that takes the CLOCK victim, -1 for a miss read from the home uncached.
+ *   Replaces kv_host's plan kernel (kv_host.py:116-185).
+ * gather: with sl, the token's QSA rows as lb2_kvh_gather gives them for a sequence of n positions (the new one
+ *   included), read from the pool on a hit and from the home otherwise (a miss with a victim fills the victim's
+ *   slot), and the new position's row kn / vn [Hk, D] (strides head, dim) written into the home at n - 1 and used
+ *   wherever position n - 1 is gathered. Replaces kv_host's gather kernel (kv_host.py:187-257).
+ * inval: slots holding a block >= lim drop it (before positions from lim * cr on are rewritten). Replaces kv_host's
+ *   inval kernel (kv_host.py:259-276).
+ * Out-of-range picks or slots are skipped (zeros in their rows) and reported through lb2_status. */
+int lb2_kvh_lru_plan(const int32_t* tb, int nsel, int32_t* slot_of, int max_blocks, int32_t* block_of, int32_t* stamp,
+                     int32_t* ref, int32_t* meta, int ns, int32_t* sl, void* stream);
+int lb2_kvh_lru_gather(const uint64_t* table, void* pool, int ns, const int32_t* tb, const int32_t* sl, int nsel, int cr,
+                       int n, const void* kn, const int64_t* kn_st, const void* vn, const int64_t* vn_st, void* kg,
+                       void* vg, int Hk, int D, int dtype, int logc, void* stream);
+int lb2_kvh_lru_inval(int32_t* slot_of, int32_t* block_of, int32_t* ref, int ns, int lim, void* stream);
 
 /* ------------------------------------------------------------------------------------------------------------
  * Gated-DeltaNet decode-row glue.

@@ -38,6 +38,9 @@ SIGNATURES = {
     "lb2_kv_gather_picks": ([_p, _i64p, _p, _i64p, _p, _i, _i, _i, _p, _p, _i, _i, _i, _p], _i),
     "lb2_kvh_put": ([_p, _p, _i64p, _p, _i64p, ctypes.c_int64, _i, _i, _i, _i, _i, _p], _i),
     "lb2_kvh_gather": ([_p, _p, _i, _i, _i, _p, _p, _i, _i, _i, _i, _p], _i),
+    "lb2_kvh_lru_plan": ([_p, _i, _p, _i, _p, _p, _p, _p, _i, _p, _p], _i),
+    "lb2_kvh_lru_gather": ([_p, _p, _i, _p, _p, _i, _i, _i, _p, _i64p, _p, _i64p, _p, _p, _i, _i, _i, _i, _p], _i),
+    "lb2_kvh_lru_inval": ([_p, _p, _p, _i, _i, _p], _i),
     "lb2_gdn_step_glue": ([_p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _f, _f, _f, _p], _i),
     "lb2_gdn_norm_gate": ([_p, _p, _p, _p, ctypes.c_int64, _i, _i, _f, _p], _i),
     "lb2_attn_qk_norm_rope": ([_p, _p, _p, _p, _f, _p, _p, _i, _p, _p, _i, _i, _i, _i, _i, _i, _i, _p], _i),

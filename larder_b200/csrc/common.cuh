@@ -46,6 +46,11 @@ __device__ __forceinline__ void report_timeout(int where) {
   atomicCAS(&g_status, 0, (where << 8) | LB2_ETIMEOUT);
 }
 
+// An index a kernel found out of range and skipped (it wrote zeros or nothing in its place).
+__device__ __forceinline__ void report_bad_index(int where) {
+  atomicCAS(&g_status, 0, (where << 8) | LB2_EINVAL);
+}
+
 // ---------------------------------------------------------------------------------------------- small PTX helpers
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

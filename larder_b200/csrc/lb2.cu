@@ -773,6 +773,52 @@ int lb2_kvh_gather(const uint64_t* table, const int32_t* tb, int nsel, int cr, i
   return LB2_OK;
 }
 
+int lb2_kvh_lru_plan(const int32_t* tb, int nsel, int32_t* slot_of, int max_blocks, int32_t* block_of, int32_t* stamp,
+                     int32_t* ref, int32_t* meta, int ns, int32_t* sl, void* stream) {
+  LB2_CHECK_ARG(nsel >= 1 && nsel <= kvg::LRU_MAX_NSEL, "kvh_lru_plan: 1 to 1024 picks a token");
+  const int nt = (nsel + 31) / 32 * 32;
+  LB2_CHECK_ARG(ns >= nt, "kvh_lru_plan: the pool needs at least ceil32(nsel) slots");
+  LB2_CHECK_ARG(max_blocks >= 1, "kvh_lru_plan: max_blocks");
+  LB2_CHECK_ARG(tb && slot_of && block_of && stamp && ref && meta && sl, "kvh_lru_plan: null pointer");
+  kvg::lru_plan_kernel<<<1, nt, 0, static_cast<cudaStream_t>(stream)>>>(tb, nsel, slot_of, max_blocks, block_of,
+                                                                         stamp, ref, meta, ns, sl);
+  LB2_CUDA(cudaGetLastError());
+  return LB2_OK;
+}
+
+int lb2_kvh_lru_gather(const uint64_t* table, void* pool, int ns, const int32_t* tb, const int32_t* sl, int nsel, int cr,
+                       int n, const void* kn, const int64_t* kn_st, const void* vn, const int64_t* vn_st, void* kg,
+                       void* vg, int Hk, int D, int dtype, int logc, void* stream) {
+  LB2_CHECK_ARG(nsel >= 0 && cr > 0 && n >= 1 && ns >= 1 && Hk > 0 && D > 0 && logc > 0 && logc < 31,
+                "kvh_lru_gather: shape");
+  LB2_CHECK_ARG(dtype >= LB2_F32 && dtype <= LB2_F16, "kvh_lru_gather: dtype");
+  const int m = nsel * cr + n - n / cr * cr;
+  dim3 grid(unsigned((int64_t(m + 1) * 32 + 255) / 256), unsigned(Hk), 2);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define LB2_LRU_GATHER(T)                                                                                            \
+  kvg::lru_gather_kernel<T><<<grid, 256, 0, st>>>(table, static_cast<T*>(pool), ns, tb, sl, nsel, cr, n,             \
+                                                  static_cast<const T*>(kn), kn_st[0], kn_st[1],                     \
+                                                  static_cast<const T*>(vn), vn_st[0], vn_st[1], static_cast<T*>(kg), \
+                                                  static_cast<T*>(vg), Hk, D, logc)
+  if (dtype == LB2_BF16)
+    LB2_LRU_GATHER(__nv_bfloat16);
+  else if (dtype == LB2_F16)
+    LB2_LRU_GATHER(__half);
+  else
+    LB2_LRU_GATHER(float);
+#undef LB2_LRU_GATHER
+  LB2_CUDA(cudaGetLastError());
+  return LB2_OK;
+}
+
+int lb2_kvh_lru_inval(int32_t* slot_of, int32_t* block_of, int32_t* ref, int ns, int lim, void* stream) {
+  LB2_CHECK_ARG(ns >= 1 && lim >= 0, "kvh_lru_inval: shape");
+  kvg::lru_inval_kernel<<<unsigned((ns + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(slot_of, block_of,
+                                                                                                   ref, ns, lim);
+  LB2_CUDA(cudaGetLastError());
+  return LB2_OK;
+}
+
 // ------------------------------------------------------------------------------------------------ GDN glue
 
 int lb2_gdn_step_glue(const void* conv, const void* a, const void* b, const float* A_log, const float* dt_bias,

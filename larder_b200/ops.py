@@ -298,6 +298,48 @@ def kvh_gather(table, tb, cr, n, Hk, D, dtype, logc, device):
     return kg, vg
 
 
+def kvh_lru_plan(tb, lru):
+    """One token's plan over the LRU state `lru` (a kv_host.Lru): sl [nsel] int32 on the device, the state updated in
+    place (see lb2_kvh_lru_plan)."""
+    tb = tb.reshape(-1)
+    _cuda(tb, lru.slot_of)
+    if tb.dtype != torch.int32:
+        raise ValueError("kvh_lru_plan: tb must be int32")
+    sl = torch.empty(tb.numel(), dtype=torch.int32, device=tb.device)
+    rc = lib().lb2_kvh_lru_plan(_ptr(tb), tb.numel(), _ptr(lru.slot_of), lru.slot_of.numel(), _ptr(lru.block_of),
+                                _ptr(lru.stamp), _ptr(lru.ref), _ptr(lru.meta), lru.slots, _ptr(sl), _stream(tb))
+    check(rc, "kvh_lru_plan")
+    return sl
+
+
+def kvh_lru_gather(table, lru, tb, sl, cr, n, kn, vn, logc):
+    """The token's QSA rows kg, vg [1, Hk, m, D] of a sequence of n positions through the LRU (pool hits, home
+    misses filling their victims), and the new row kn / vn ([Hk, D], [1, Hk, 1, D] ...) written into the home at
+    n - 1 (see lb2_kvh_lru_gather)."""
+    tb = tb.reshape(-1)
+    Hk, D = lru.pool.shape[2], lru.pool.shape[4]
+    kn, vn = kn.reshape(Hk, D), vn.reshape(Hk, D)
+    _cuda(table, tb, sl, kn, vn)
+    if kn.dtype != lru.pool.dtype or vn.dtype != lru.pool.dtype:
+        raise ValueError("kvh_lru_gather: the new row must have the pool's dtype")
+    nsel = tb.numel()
+    m = nsel * cr + n - n // cr * cr
+    kg = torch.empty((1, Hk, m, D), dtype=kn.dtype, device=kn.device)
+    vg = torch.empty_like(kg)
+    rc = lib().lb2_kvh_lru_gather(_ptr(table), _ptr(lru.pool), lru.slots, _ptr(tb), _ptr(sl), nsel, int(cr), int(n),
+                                  _ptr(kn), i64(*kn.stride()), _ptr(vn), i64(*vn.stride()), _ptr(kg), _ptr(vg), Hk, D,
+                                  dtype_code(kg), int(logc), _stream(kg))
+    check(rc, "kvh_lru_gather")
+    return kg, vg
+
+
+def kvh_lru_inval(lru, lim):
+    """Slots of the LRU holding a block >= lim drop it."""
+    rc = lib().lb2_kvh_lru_inval(_ptr(lru.slot_of), _ptr(lru.block_of), _ptr(lru.ref), lru.slots, int(lim),
+                                 _stream(lru.slot_of))
+    check(rc, "kvh_lru_inval")
+
+
 # ---------------------------------------------------------------------------------------------------- GDN glue
 
 def _rounded(x, dtype):

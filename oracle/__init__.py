@@ -278,3 +278,104 @@ def qsa_select(q, pooled, offset, cr, k, div):
             order = np.argsort(-sc[b, s], kind="stable")[:kk]
             top[b, s, :kk] = np.sort(order)
     return top, sc
+
+
+# ---------------------------------------------------------------------------------------------- KV home's VRAM LRU
+
+def lru_plan(tb, slot_of, block_of, stamp, ref, meta, ns):
+    """One token's plan of the reference's LRU (kv_host.py:116-185), restated over its rounds; the int32 state arrays
+    are updated in place. Returns sl [nsel]: the hit's slot, -2 - victim, or -1.
+
+    Hits take this token's stamp t = meta[1] + 1 and their reference bit. Each round looks at NT = ceil32(nsel)
+    consecutive slots from hand + scanned: a slot is protected when stamped t, eligible when not protected and its
+    bit is clear. Eligible slots are taken in order while victims are still needed; if the round supplies the last
+    victim it ends there (cut = that slot's place), else it covers all NT slots; unprotected, non-eligible slots up to
+    the cut lose their bit. The scan stops when every miss has a victim or after 2 ns + NT slots. The i-th miss (in
+    pick order) takes the i-th victim, evicting the victim's block."""
+    tb = np.asarray(tb, np.int64)
+    nsel = tb.size
+    nt = (nsel + 31) // 32 * 32
+    t = int(meta[1]) + 1
+    s = slot_of[tb].astype(np.int64)
+    hit = s >= 0
+    stamp[s[hit]] = t
+    ref[s[hit]] = 1
+    miss = ~hit
+    M = int(miss.sum())
+    hand, found, scanned = int(meta[0]), 0, 0
+    victims = []
+    lanes = np.arange(nt)
+    while found < M and scanned < 2 * ns + nt:
+        xs = (hand + scanned + lanes) % ns
+        prot = stamp[xs] == t
+        elig = ~prot & (ref[xs] == 0)
+        need = M - found
+        idx = np.flatnonzero(elig)
+        take = min(idx.size, need)
+        cut = int(idx[take - 1]) if take == need else nt - 1
+        chosen = xs[idx[:take]]
+        victims.extend(int(x) for x in chosen)
+        stamp[chosen] = t
+        passed = (lanes <= cut) & ~prot & ~elig
+        ref[xs[passed]] = 0
+        found += take
+        scanned += cut + 1
+    sl = np.full(nsel, -1, np.int32)
+    r = 0
+    for j in range(nsel):
+        if hit[j]:
+            sl[j] = s[j]
+            continue
+        if r < found:
+            x = victims[r]
+            old = int(block_of[x])
+            if old >= 0:
+                slot_of[old] = -1
+            block_of[x] = tb[j]
+            slot_of[tb[j]] = x
+            ref[x] = 0
+            sl[j] = -2 - x
+        r += 1
+    meta[0] = (hand + scanned) % ns
+    meta[1] = t
+    meta[2] += nsel - M
+    meta[3] += M
+    return sl
+
+
+def lru_gather(k, v, pool, tb, sl, cr, n):
+    """The token's rows through the LRU (kv_host.py:187-257): k / v [Hk, >= n, D] hold the sequence's positions
+    (n - 1 the new one), pool [ns, 2, Hk, cr, D] is updated in place (a miss with a victim fills it). Row r < nsel cr
+    is position tb[r / cr] cr + r % cr, from the pool on a hit (sl >= 0), else from k / v; then the trailing partial
+    block. Returns kg, vg [Hk, m, D]."""
+    tb = np.asarray(tb, np.int64)
+    nsel = tb.size
+    own0 = n // cr * cr
+    m = nsel * cr + n - own0
+    Hk, D = k.shape[0], k.shape[2]
+    out = [np.zeros((Hk, m, D), k.dtype), np.zeros((Hk, m, D), k.dtype)]
+    for r in range(m):
+        slot = vic = -1
+        if r >= nsel * cr:
+            pos = own0 + r - nsel * cr
+        else:
+            pos = int(tb[r // cr]) * cr + r % cr
+            c = int(sl[r // cr])
+            slot = c if c >= 0 else -1
+            vic = -2 - c if c <= -2 else -1
+        for kv, src in enumerate((k, v)):
+            x = pool[slot, kv, :, r % cr] if (slot >= 0 and pos != n - 1) else src[:, pos]
+            out[kv][:, r] = x
+            if vic >= 0:
+                pool[vic, kv, :, r % cr] = x
+    return out[0], out[1]
+
+
+def lru_inval(slot_of, block_of, ref, lim):
+    """Slots holding a block >= lim drop it (kv_host.py:259-276), in place."""
+    for x in range(block_of.size):
+        b = int(block_of[x])
+        if b >= 0 and b >= lim:
+            slot_of[b] = -1
+            block_of[x] = -1
+            ref[x] = 0
