@@ -397,7 +397,8 @@ def bench_prefill(torch, ops, dev, rank, world, args, stream, pk, pk_kind, barri
 def bench_sharded(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_over_ranks):
     """configs[4] per rank (weak scaling: the 8-GPU share of each rank fixed): 8 independent 8192-token causal
     prefills (32q/4kv x 128), and a batch-64 decode over this rank's 4096-key range of every sequence merged across
-    ranks (NCCL all-gather of packed (o, lse), then the log-sum-exp combine). At 8 GPUs that is configs[4]."""
+    ranks (NCCL all-gather of packed (o, lse), then the log-sum-exp combine; at N > 1 also over NVLink peer
+    memory, `decode_peer`). At 8 GPUs that is configs[4]."""
     from larder_b200 import sharded
     g = torch.Generator(device=dev).manual_seed(5000 + rank)
     # prefill: 8 sequences a rank
@@ -436,6 +437,25 @@ def bench_sharded(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, 
     barrier_sync()
     ms_d = max_over_ranks(cuda_time(torch, dec, args.steps, stream)) / args.steps
     kv_bytes = B * n_local * Hkv * D * 2 * 2
+    peer = None
+    if world > 1:  # the same decode with the exchange over NVLink peer memory (no collective on the data path)
+        xch = sharded.PeerExchange(B, Hq, 1, D)
+        try:
+            def dec_peer(i):
+                kk, vv = kvs[i % copies]
+                xch.decode(dq, kk, vv, D ** -0.5)
+
+            for i in range(args.warmup):
+                dec_peer(i)
+            barrier_sync()
+            ms_pd = max_over_ranks(cuda_time(torch, dec_peer, args.steps, stream)) / args.steps
+            peer = {"value": round(world * kv_bytes / (ms_pd * 1e-3) / 1e9, 1), "unit": "GB/s",
+                    "ms_per_step": round(ms_pd, 5),
+                    "per_rank": f"B=64 x {n_local} local keys; partials read in place from the peers' exchange "
+                                "buffers over NVLink (lb2_attn_combine_peers)",
+                    "kernel": "lb2::decode::decode_kernel + lb2::xch::peer_combine_kernel"}
+        finally:
+            xch.close()
     return {"prefill": {"value": round(world * flop / (ms_p * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                         "ms_per_step": round(ms_p, 4), "per_rank": "8 x 8192 causal, 32q/4kv x 128, bf16",
                         "roofline": {"bound": "tensor", "achieved": round(flop / (ms_p * 1e-3) / 1e12, 2),
@@ -450,6 +470,7 @@ def bench_sharded(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, 
                        "roofline": {"bound": "hbm", "achieved": round(kv_bytes / (ms_d * 1e-3) / 1e9, 1),
                                     "peak": pk["hbm_gbs"], "frac": round(kv_bytes / (ms_d * 1e-3) / 1e9 /
                                                                          pk["hbm_gbs"], 4)}},
+            "decode_peer": peer,
             "scaling": "weak", "workload": "configs[4] share of one rank (exactly configs[4] at 8 GPUs)"}
 
 

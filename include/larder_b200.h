@@ -137,6 +137,25 @@ int lb2_attn_combine(const float* part_o, const float* part_lse, int R, int B, i
 int lb2_attn_combine_packed(const float* packed, int R, int B, int Hq, int T, int D, void* o, const int64_t* o_st,
                             int dtype, void* stream);
 
+/* The same exchange over NVLink peer memory instead of a collective (no counterpart in the reference, which is
+ * single-GPU: this is the B200 form of the KV-range merge, foldattn.py:188-211 across GPUs). Each rank allocates one
+ * exchange buffer (lb2_xch_alloc of lb2_xch_bytes(B, Hq, T, D) bytes, zeroed), exports it (lb2_xch_handle: 64
+ * bytes to send to the other ranks) and maps every peer's (lb2_xch_open; lb2_xch_close / lb2_xch_free at the end).
+ * Call e = 1, 2, ... of a rank: lb2_attn_decode_partial writes its partial into half e % 2 of its own buffer
+ * (part_o at float offset (e % 2) * B Hq T (D + 1), part_lse right after the o rows), then lb2_attn_combine_peers
+ * (bufs: host array of the R buffers as mapped in this process, its own at `rank`) publishes e to every peer, waits
+ * for every peer's e (bounded: 2 s, then lb2_status reports LB2_ETIMEOUT and o is not written) and merges the R
+ * partials read in place over NVLink into o [B, Hq, T, D] (strides o_st). Every rank makes the same calls in the
+ * same order; R <= 8 (one NVSwitch node). */
+size_t lb2_xch_bytes(int B, int Hq, int T, int D);
+int lb2_xch_alloc(size_t bytes, void** ptr);
+int lb2_xch_free(void* ptr);
+int lb2_xch_handle(void* ptr, void* handle);
+int lb2_xch_open(const void* handle, void** ptr);
+int lb2_xch_close(void* ptr);
+int lb2_attn_combine_peers(const uint64_t* bufs, int R, int rank, uint32_t epoch, int B, int Hq, int T, int D, void* o,
+                           const int64_t* o_st, int dtype, void* stream);
+
 /* ------------------------------------------------------------------------------------------------------------
  * Gated-DeltaNet recurrence, one position at a time (decode steps, short verify passes).
  *

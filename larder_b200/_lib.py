@@ -38,6 +38,13 @@ SIGNATURES = {
     "lb2_kv_gather_picks": ([_p, _i64p, _p, _i64p, _p, _i, _i, _i, _p, _p, _i, _i, _i, _p], _i),
     "lb2_kvh_put": ([_p, _p, _i64p, _p, _i64p, ctypes.c_int64, _i, _i, _i, _i, _i, _p], _i),
     "lb2_kvh_gather": ([_p, _p, _i, _i, _i, _p, _p, _i, _i, _i, _i, _p], _i),
+    "lb2_xch_bytes": ([_i, _i, _i, _i], _sz),
+    "lb2_xch_alloc": ([_sz, ctypes.POINTER(ctypes.c_void_p)], _i),
+    "lb2_xch_free": ([_p], _i),
+    "lb2_xch_handle": ([_p, _p], _i),
+    "lb2_xch_open": ([_p, ctypes.POINTER(ctypes.c_void_p)], _i),
+    "lb2_xch_close": ([_p], _i),
+    "lb2_attn_combine_peers": ([_p, _i, _i, ctypes.c_uint32, _i, _i, _i, _i, _p, _i64p, _i, _p], _i),
     "lb2_kvh_lru_plan": ([_p, _i, _p, _i, _p, _p, _p, _p, _i, _p, _p], _i),
     "lb2_kvh_lru_gather": ([_p, _p, _i, _p, _p, _i, _i, _i, _p, _i64p, _p, _i64p, _p, _p, _i, _i, _i, _i, _p], _i),
     "lb2_kvh_lru_inval": ([_p, _p, _p, _i, _i, _p], _i),

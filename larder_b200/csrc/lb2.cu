@@ -14,6 +14,7 @@
 #include "attn_f32.cuh"
 #include "attn_glue.cuh"
 #include "qsa_select.cuh"
+#include "peer_xch.cuh"
 #include "kv_gather.cuh"
 #include "gdn_glue.cuh"
 
@@ -515,6 +516,92 @@ int lb2_attn_combine_packed(const float* packed, int R, int B, int Hq, int T, in
                           stream);
 }
 
+
+// ------------------------------------------------------------------------------------------------ peer exchange
+
+size_t lb2_xch_bytes(int B, int Hq, int T, int D) {
+  if (B <= 0 || Hq <= 0 || T <= 0 || D <= 0) return 0;
+  const int64_t half = int64_t(B) * Hq * T * (D + 1);
+  return size_t(xch::flags_offset(half) * 4 + xch::XCH_MAX_RANKS * 4);
+}
+
+int lb2_xch_alloc(size_t bytes, void** ptr) {
+  LB2_CHECK_ARG(ptr && bytes > 0, "xch_alloc: size");
+  *ptr = nullptr;
+  LB2_CUDA(cudaMalloc(ptr, bytes));
+  const cudaError_t e = cudaMemset(*ptr, 0, bytes);  // flags start at 0: no call published yet
+  if (e != cudaSuccess) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return cuda_fail(e, "cudaMemset(exchange buffer)");
+  }
+  return LB2_OK;
+}
+
+int lb2_xch_free(void* ptr) {
+  if (ptr) LB2_CUDA(cudaFree(ptr));
+  return LB2_OK;
+}
+
+int lb2_xch_handle(void* ptr, void* handle) {
+  LB2_CHECK_ARG(ptr && handle, "xch_handle: null pointer");
+  cudaIpcMemHandle_t h;
+  LB2_CUDA(cudaIpcGetMemHandle(&h, ptr));
+  std::memcpy(handle, &h, sizeof(h));
+  return LB2_OK;
+}
+
+int lb2_xch_open(const void* handle, void** ptr) {
+  LB2_CHECK_ARG(ptr && handle, "xch_open: null pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  *ptr = nullptr;
+  LB2_CUDA(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return LB2_OK;
+}
+
+int lb2_xch_close(void* ptr) {
+  if (ptr) LB2_CUDA(cudaIpcCloseMemHandle(ptr));
+  return LB2_OK;
+}
+
+int lb2_attn_combine_peers(const uint64_t* bufs, int R, int rank, uint32_t epoch, int B, int Hq, int T, int D, void* o,
+                           const int64_t* o_st, int dtype, void* stream) {
+  LB2_CHECK_ARG(R >= 1 && R <= xch::XCH_MAX_RANKS && rank >= 0 && rank < R, "combine_peers: 1 to 8 ranks");
+  LB2_CHECK_ARG(B > 0 && Hq > 0 && T > 0 && D > 0 && int64_t(B) * Hq * T < (int64_t(1) << 31), "combine_peers: shape");
+  LB2_CHECK_ARG(epoch > 0, "combine_peers: calls count from 1");
+  xch::PeerParams p{};
+  for (int r = 0; r < R; ++r) {
+    LB2_CHECK_ARG(bufs[r] != 0, "combine_peers: a rank's buffer is missing");
+    p.bufs[r] = reinterpret_cast<const float*>(bufs[r]);
+  }
+  p.R = R;
+  p.rank = rank;
+  p.parity = int(epoch & 1u);
+  p.epoch = epoch;
+  p.rows = B * Hq * T;
+  p.half = int64_t(p.rows) * (D + 1);
+  p.Hq = Hq;
+  p.Tq = T;
+  p.D = D;
+  p.o = o;
+  p.o0 = o_st[0];
+  p.o1 = o_st[1];
+  p.o2 = o_st[2];
+  const int warps = 8;
+  dim3 grid(unsigned((p.rows + warps - 1) / warps));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == LB2_BF16)
+    xch::peer_combine_kernel<__nv_bfloat16><<<grid, warps * 32, 0, st>>>(p);
+  else if (dtype == LB2_F16)
+    xch::peer_combine_kernel<__half><<<grid, warps * 32, 0, st>>>(p);
+  else if (dtype == LB2_F32)
+    xch::peer_combine_kernel<float><<<grid, warps * 32, 0, st>>>(p);
+  else
+    return fail(LB2_EINVAL, "combine_peers: dtype");
+  LB2_CUDA(cudaGetLastError());
+  return LB2_OK;
+}
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 

@@ -1,0 +1,112 @@
+// KV-range-sharded decode's exchange over NVLink peer memory: the log-sum-exp merge of every rank's partial
+// (foldattn.py:188-211's merge taken across GPUs) reading the peers' partials in place, without a collective.
+//
+// Each rank owns one exchange buffer in its device memory, shared with the other ranks through CUDA IPC:
+//   [parity 0: o rows (rows x D fp32) | lse (rows fp32)] [parity 1: the same] [flags: XCH_MAX_RANKS uint32]
+// Call e (e = 1, 2, ...) of a rank writes its partial into half e % 2 of its own buffer (the decode-partial kernel,
+// before this one on the stream), then peer_combine_kernel
+//   1. publishes: every block's thread 0 stores e into flags[rank] of every peer's buffer (a release at system scope,
+//      so the partial's writes are visible to a peer that sees the flag; all blocks publish, so no block waits on a
+//      block that has not run);
+//   2. waits until its own flags[r] >= e for every peer r (acquire, bounded: 2 s of %globaltimer, then the status word
+//      is set and the block writes nothing);
+//   3. merges the R partials of its rows, reading the peers' halves e % 2 over NVLink (cache-bypassing loads).
+// A rank is at most one call ahead of any peer (its call e + 1 needs every peer's flag e + 1, set after the peer's
+// call e ended), so a half is rewritten (call e + 2) only after every peer has finished reading it (call e).
+#pragma once
+
+#include "common.cuh"
+
+namespace lb2 {
+namespace xch {
+
+constexpr int XCH_MAX_RANKS = 8;
+
+struct PeerParams {
+  const float* bufs[XCH_MAX_RANKS];  // every rank's exchange buffer as mapped in this process (bufs[rank]: its own)
+  int R, rank, parity;
+  uint32_t epoch;
+  int64_t half;  // floats in one parity half: rows * (D + 1)
+  int rows, Hq, Tq, D;
+  void* o;
+  int64_t o0, o1, o2;
+};
+
+__host__ __device__ constexpr int64_t flags_offset(int64_t half) { return 2 * half; }  // in floats
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) peer_combine_kernel(const __grid_constant__ PeerParams p) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    __threadfence_system();  // the partial (written before this kernel on the stream) ahead of the flags
+    for (int r = 0; r < p.R; ++r)
+      if (r != p.rank) {
+        uint32_t* f = reinterpret_cast<uint32_t*>(const_cast<float*>(p.bufs[r]) + flags_offset(p.half)) + p.rank;
+        st_release_sys(f, p.epoch);
+      }
+    const uint32_t* mine = reinterpret_cast<const uint32_t*>(p.bufs[p.rank] + flags_offset(p.half));
+    bool ok = true;
+    for (int r = 0; r < p.R && ok; ++r) {
+      if (r == p.rank) continue;
+      uint64_t t0 = 0;
+      for (uint32_t i = 1; int32_t(ld_acquire_sys(mine + r) - p.epoch) < 0; ++i) {
+        if ((i & 255u) == 0) {
+          const uint64_t now = globaltimer_ns();
+          if (t0 == 0) {
+            t0 = now;
+          } else if (now - t0 > kWaitNs) {
+            report_timeout(101);
+            ok = false;
+            break;
+          }
+        }
+      }
+    }
+    s_ok = ok;
+  }
+  __syncthreads();
+  if (!s_ok) return;
+  // one warp a row, as decode::combine_kernel, with rank r's partial at bufs[r] + parity * half
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= p.rows) return;
+  const int64_t base = int64_t(p.parity) * p.half;
+  const int64_t lse_at = base + int64_t(p.rows) * p.D + row;
+  float lse[XCH_MAX_RANKS];
+  float M = -INFINITY;
+#pragma unroll
+  for (int r = 0; r < XCH_MAX_RANKS; ++r) {
+    lse[r] = r < p.R ? __ldcv(p.bufs[r] + lse_at) : -INFINITY;
+    M = fmaxf(M, lse[r]);
+  }
+  const float Mu = M == -INFINITY ? 0.f : M;
+  float wsum = 0.f;
+#pragma unroll
+  for (int r = 0; r < XCH_MAX_RANKS; ++r) {
+    lse[r] = r < p.R ? __expf(lse[r] - Mu) : 0.f;  // the weights
+    wsum += lse[r];
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  const int t = row % p.Tq, h = (row / p.Tq) % p.Hq, b = row / (p.Tq * p.Hq);
+  T* orow = reinterpret_cast<T*>(p.o) + b * p.o0 + int64_t(h) * p.o1 + int64_t(t) * p.o2;
+  const int64_t o_at = base + int64_t(row) * p.D;
+  for (int d = lane; d < p.D; d += 32) {
+    float x = 0.f;
+#pragma unroll
+    for (int r = 0; r < XCH_MAX_RANKS; ++r)
+      if (r < p.R) x += lse[r] * __ldcv(p.bufs[r] + o_at + d);
+    orow[d] = from_f<T>(x * inv);
+  }
+}
+
+}  // namespace xch
+}  // namespace lb2

@@ -159,13 +159,21 @@ def attn_decode_partial(q, k, v, scale, kv_len=None, split=0, out=None):
         for t, shp in ((part_o, (B, Hq, T, D)), (part_lse, (B, Hq, T))):
             if t.dtype != torch.float32 or tuple(t.shape) != shp or not t.is_contiguous() or t.device != q.device:
                 raise ValueError(f"attn_decode_partial: out must be contiguous fp32 {shp} on q's device")
+    decode_partial_into(q, k, v, scale, kv_len, split, _ptr(part_o), _ptr(part_lse))
+    return part_o, part_lse
+
+
+def decode_partial_into(q, k, v, scale, kv_len, split, part_o_ptr, part_lse_ptr):
+    """attn_decode_partial into raw device addresses (contiguous fp32 [B, Hq, T, D] and [B, Hq, T]): the halves of
+    a peer-exchange buffer, which no tensor wraps."""
+    B, Hq, T, D = q.shape
+    Hkv, N = k.shape[1], k.shape[2]
     ws = workspace(q.device, _decode_ws_bytes(B, Hq, Hkv, T, N, D, split, q.device.index), "decode_partial")
     rc = lib().lb2_attn_decode_partial(_ptr(q), i64(*q.stride()[:3]), _ptr(k), i64(*k.stride()[:3]), _ptr(v),
-                                       i64(*v.stride()[:3]), _ptr(part_o), _ptr(part_lse), _ptr(kv_len), B, Hq, Hkv,
+                                       i64(*v.stride()[:3]), part_o_ptr, part_lse_ptr, _ptr(kv_len), B, Hq, Hkv,
                                        T, N, D, dtype_code(q), float(scale), int(split), _ptr(ws), ws.numel(),
                                        _stream(q))
     check(rc, "attn_decode_partial")
-    return part_o, part_lse
 
 
 def attn_combine(part_o, part_lse, dtype, out=None):

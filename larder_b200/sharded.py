@@ -11,17 +11,23 @@ The reference is single-process and single-GPU (no collective exists in it); the
     blocks in place with the log-sum-exp combine kernel (lb2_attn_combine_packed): o = sum_r exp(lse_r - lse*) o_r / sum_r exp(lse_r - lse*), the merge of foldattn_merge
     (foldattn.py:188-211) and cpu_kern.cpp:607-628 taken across GPUs.
 
+`PeerExchange` is the same decode without a collective on the data path: each rank's partial lands in its own
+exchange buffer, shared with the other ranks through CUDA IPC, and lb2_attn_combine_peers merges all ranks' partials
+read in place over NVLink, after a flag each rank publishes into every peer's buffer (bounded waits).
+
 `partial_fn(q, k, v, scale, kv_len, part_o, part_lse)` fills a rank's partial into the two parts of its packed buffer
 and `combine_fn(gathered [world, rows * (D + 1)], (B, Hq, T, D), dtype)` merges the gathered blocks in place; both
 default to this package's CUDA entry points (lb2_attn_decode_partial, lb2_attn_combine_packed). Tests on CPU ranks
 (gloo) pass the CPU oracle instead, as the checker of the exchange itself.
 """
+import ctypes
 import datetime
 
 import torch
 import torch.distributed as dist
 
 from . import ops
+from ._lib import check, i64, lib
 
 
 def init(backend="nccl", timeout_s=60, device=None):
@@ -86,3 +92,76 @@ def sharded_prefill(q, k, v, scale, mask="causal", gate=None, rank=None, world=N
     s0, s1 = sequence_shard(q.shape[0], rank, world)
     g = None if gate is None else gate[s0:s1]
     return s0, s1, ops.attn_prefill(q[s0:s1], k[s0:s1], v[s0:s1], scale, mask, gate=g)
+
+
+class PeerExchange:
+    """KV-range-sharded decode over NVLink peer memory for one decode shape (B, Hq, T, D) on the ranks of `group`
+    (at most 8, one GPU each, all on one NVSwitch node). Every rank builds it with the same shape, calls `decode` the
+    same number of times in the same order, and calls `close` at the end (all ranks)."""
+
+    def __init__(self, B, Hq, T, D, group=None):
+        self.group = group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        if self.world > 8:
+            raise ValueError("PeerExchange: at most 8 ranks")
+        self.shape = (B, Hq, T, D)
+        self.rows = B * Hq * T
+        self.half = self.rows * (D + 1)
+        L = lib()
+        ptr = ctypes.c_void_p()
+        check(L.lb2_xch_alloc(L.lb2_xch_bytes(B, Hq, T, D), ctypes.byref(ptr)), "xch_alloc")
+        self.base = ptr.value
+        handle = ctypes.create_string_buffer(64)
+        check(L.lb2_xch_handle(ctypes.c_void_p(self.base), handle), "xch_handle")
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self.opened, bufs, err = [], [], ""
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                bufs.append(self.base)
+                continue
+            p = ctypes.c_void_p()
+            rc = L.lb2_xch_open(ctypes.create_string_buffer(h, 64), ctypes.byref(p))
+            if rc:
+                err = L.lb2_error().decode()
+                break
+            self.opened.append(p.value)
+            bufs.append(p.value)
+        # every rank mapped every peer, or all give up together (none goes on to a step the others left)
+        ok = torch.tensor([0 if err else 1], dtype=torch.int32,
+                          device=torch.device("cuda", torch.cuda.current_device()))
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if not int(ok.item()):
+            for p in self.opened:
+                L.lb2_xch_close(ctypes.c_void_p(p))
+            L.lb2_xch_free(ctypes.c_void_p(self.base))
+            self.base, self.opened = None, []
+            raise RuntimeError(f"PeerExchange: a rank could not map its peers' buffers ({err or 'another rank'})")
+        self.bufs = (ctypes.c_uint64 * self.world)(*bufs)
+        self.epoch = 0
+
+    def decode(self, q, k_local, v_local, scale, kv_len_local=None, out_dtype=None):
+        """As kv_sharded_decode: o [B, Hq, T, D] on every rank, from this rank's key range k_local / v_local."""
+        B, Hq, T, D = q.shape
+        if (B, Hq, T, D) != self.shape:
+            raise ValueError(f"PeerExchange: built for {self.shape}, called with {(B, Hq, T, D)}")
+        self.epoch += 1
+        o_ptr = self.base + (self.epoch & 1) * self.half * 4
+        ops.decode_partial_into(q, k_local, v_local, scale, kv_len_local, 0, o_ptr, o_ptr + self.rows * D * 4)
+        o = torch.empty((B, Hq, T, D), dtype=out_dtype or q.dtype, device=q.device)
+        rc = lib().lb2_attn_combine_peers(self.bufs, self.world, self.rank, self.epoch, B, Hq, T, D, ops._ptr(o),
+                                          i64(*o.stride()[:3]), ops.dtype_code(o), ops._stream(o))
+        check(rc, "attn_combine_peers")
+        return o
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's, once every rank's kernels are done with them."""
+        if self.base is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for p in self.opened:
+            check(lib().lb2_xch_close(ctypes.c_void_p(p)), "xch_close")
+        dist.barrier(group=self.group)
+        check(lib().lb2_xch_free(ctypes.c_void_p(self.base)), "xch_free")
+        self.base, self.opened = None, []

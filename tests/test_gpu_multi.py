@@ -63,6 +63,57 @@ def test_kv_sharded_decode_nccl_equals_whole():
         assert st == 0 and err <= 2e-2, (rank, err, st)
 
 
+def _peer_worker(rank, port, rq):
+    import datetime
+    import torch.distributed as dist
+    from larder_b200 import ops, sharded
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    xch = None
+    try:
+        g = torch.Generator().manual_seed(19)
+        B, Hq, Hkv, D, N = 8, 32, 4, 128, 8192
+        k = torch.randn(B, Hkv, N, D, generator=g).to(torch.bfloat16).to(dev)
+        v = torch.randn(B, Hkv, N, D, generator=g).to(torch.bfloat16).to(dev)
+        s0, s1 = sharded.kv_range(N, rank, WORLD)
+        xch = sharded.PeerExchange(B, Hq, 1, D)
+        err, same = 0.0, True
+        for _ in range(5):  # both halves of the exchange buffer, each reused
+            q = torch.randn(B, Hq, 1, D, generator=g).to(torch.bfloat16).to(dev)
+            o = xch.decode(q, k[:, :, s0:s1], v[:, :, s0:s1], D ** -0.5)
+            whole = ops.attn_decode(q, k, v, D ** -0.5)
+            err = max(err, (o.float() - whole.float()).abs().max().item())
+            same &= torch.equal(o, sharded.kv_sharded_decode(q, k[:, :, s0:s1], v[:, :, s0:s1], D ** -0.5))
+        st = ops.status(rank)
+        rq.put((rank, err, same, st))
+    finally:
+        torch.cuda.synchronize(dev)
+        if xch is not None:
+            xch.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_kv_sharded_decode_peer_memory_equals_whole_and_nccl():
+    """The exchange over NVLink peer memory (PeerExchange): five calls in a row, each equal to one decode over the
+    whole cache (grading tolerance) and bit-equal to the NCCL path (same partials, same merge order)."""
+    ctx = mp.get_context("spawn")
+    rq = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, port, rq)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    res = [rq.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, err, same, st in res:
+        assert st == 0 and err <= 2e-2 and same, (rank, err, same, st)
+
+
 def test_sequence_sharded_prefill_matches_oracle():
     """The prefill share of each of 2 ranks (run here one after the other on one GPU: the share is independent work)."""
     import checks
