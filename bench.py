@@ -269,74 +269,39 @@ def bench_decode(torch, ops, dev, rank, world, args, stream, pk, pk_kind, barrie
     out["clocks"] = clk.summary()
     out["gpu_launches"] = 2 * args.steps  # a step: the persistent split-KV kernel and the split combine
 
-    # e2e through the public API: every step copies its q from pinned host memory and reads its o back into pinned
-    # host memory, and both copies are inside the timed region. As a serving loop issues them, the copies run on
-    # streams of their own (device buffers alternate between two sets, ordered by events), so step i's copies
-    # overlap the neighbouring steps' kernels instead of waiting behind them. The copies and events go straight to
-    # the CUDA runtime (cudaMemcpyAsync, cudaEventRecord, cudaStreamWaitEvent): a decode step is about 30 us of
-    # device work, and torch's stream context managers alone cost the host more than that.
-    from cuda.bindings import runtime as cudart
-
-    def rt(res):
-        err = res[0] if isinstance(res, tuple) else res
-        if err != cudart.cudaError_t.cudaSuccess:
-            raise RuntimeError(f"CUDA runtime call failed: {err}")
-        return res[1] if isinstance(res, tuple) and len(res) > 1 else None
-
+    # e2e through the public API with host buffers: every step hands the library its q in pinned host memory and
+    # gets o back into pinned host memory (lb2_attn_decode_host: q in, decode, o out, with the copies on the
+    # library's own streams so that they overlap the neighbouring steps' kernels). The copies are inside the timed
+    # region, the last ones included (lb2_attn_decode_host_drain before the closing event).
     q_host = [s[0].pin_memory() for s in sets]
     o_host = [torch.empty(B, Hq, 1, D, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
-    q_buf = [torch.empty(B, Hq, 1, D, dtype=torch.bfloat16, device=dev) for _ in range(2)]
-    o_buf = [torch.empty(B, Hq, 1, D, dtype=torch.bfloat16, device=dev) for _ in range(2)]
-    nbytes = q_host[0].numel() * 2
-    h2d_stream, d2h_stream = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    s_main, s_h2d, s_d2h = stream.cuda_stream, h2d_stream.cuda_stream, d2h_stream.cuda_stream
-    flags = cudart.cudaEventDisableTiming
-    h2d_done, dec_done, d2h_done = ([rt(cudart.cudaEventCreateWithFlags(flags)) for _ in range(2)] for _ in range(3))
-    for j in range(2):  # every event recorded once, so the first waits find them complete
-        for e in (h2d_done[j], dec_done[j], d2h_done[j]):
-            rt(cudart.cudaEventRecord(e, s_main))
-    H2D, D2H = cudart.cudaMemcpyKind.cudaMemcpyHostToDevice, cudart.cudaMemcpyKind.cudaMemcpyDeviceToHost
-    q_host_p = [t.data_ptr() for t in q_host]
-    o_host_p, q_buf_p, o_buf_p = ([t.data_ptr() for t in ts] for ts in (o_host, q_buf, o_buf))
 
     def dec_e2e(i):
-        j = i % 2
         _, k, v = sets[i % copies]
-        rt(cudart.cudaStreamWaitEvent(s_h2d, dec_done[j], 0))  # the decode two steps back has read q_buf[j]
-        rt(cudart.cudaMemcpyAsync(q_buf_p[j], q_host_p[i % copies], nbytes, H2D, s_h2d))
-        rt(cudart.cudaEventRecord(h2d_done[j], s_h2d))
-        rt(cudart.cudaStreamWaitEvent(s_main, h2d_done[j], 0))
-        rt(cudart.cudaStreamWaitEvent(s_main, d2h_done[j], 0))  # o_buf[j] of two steps back is read out
-        ops.attn_decode(q_buf[j], k, v, D ** -0.5, kv_len=kv_len, split=split, out=o_buf[j])
-        rt(cudart.cudaEventRecord(dec_done[j], s_main))
-        rt(cudart.cudaStreamWaitEvent(s_d2h, dec_done[j], 0))
-        rt(cudart.cudaMemcpyAsync(o_host_p[j], o_buf_p[j], nbytes, D2H, s_d2h))
-        rt(cudart.cudaEventRecord(d2h_done[j], s_d2h))
+        ops.attn_decode_host(q_host[i % copies], k, v, D ** -0.5, o_host[i % 2], kv_len=kv_len, split=split)
 
     def e2e_time(steps):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for i in range(steps):
             dec_e2e(i)
-        for j in range(2):  # the last reads back are inside the timed region
-            rt(cudart.cudaStreamWaitEvent(s_main, d2h_done[j], 0))
+        ops.attn_decode_host_drain(dev.index)
         e1.record(stream)
         e1.synchronize()
         return e0.elapsed_time(e1)
 
     for i in range(args.warmup):
         dec_e2e(i)
+    ops.attn_decode_host_drain(dev.index)
     torch.cuda.synchronize(dev)
     barrier_sync()
     ms_e2e = max_over_ranks(e2e_time(args.steps))
     barrier_sync()
-    for e in h2d_done + dec_done + d2h_done:
-        rt(cudart.cudaEventDestroy(e))
     per_e2e = ms_e2e / args.steps
     out["e2e"] = {"value": round(world * kv_bytes / (per_e2e * 1e-3) / 1e9, 1), "unit": "GB/s",
                   "h2d_bytes_per_step": q_host[0].numel() * 2, "d2h_bytes_per_step": o_host[0].numel() * 2,
-                  "ms_per_step": round(per_e2e, 5), "api": "larder_b200.ops.attn_decode",
-                  "copies": "q in and o out every step from / to pinned host memory, on their own streams"}
+                  "ms_per_step": round(per_e2e, 5), "api": "larder_b200.ops.attn_decode_host (lb2_attn_decode_host)",
+                  "copies": "q in and o out every step from / to pinned host memory, on the library's copy streams"}
     del sets, q_dev, graph
     torch.cuda.empty_cache()
 

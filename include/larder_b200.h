@@ -94,6 +94,21 @@ int lb2_attn_decode(const void* q, const int64_t* q_st, const void* k, const int
                     int T, int N, int D, int dtype, float scale, int causal, int split, void* workspace,
                     size_t workspace_bytes, void* stream);
 
+/* The same decode for a caller whose queries and outputs live in host memory (q_host, o_host: contiguous
+ * [B, Hq, T, D] of dtype, pinned for the copies to overlap): the call copies q in, decodes on `stream` and copies o
+ * out, and returns at once. The copies run on two streams of the library's own (one pair per device, made at the
+ * device's first call), through two staging slots in the workspace (lb2_attn_decode_host_workspace_size bytes,
+ * 256-byte aligned) used by alternate calls, so that a call's copies overlap the kernels of the calls either side.
+ * o_host of every call issued so far is complete once lb2_attn_decode_host_drain(stream) has been called and the
+ * stream has reached that point. One caller stream per device at a time (the slots and events are shared). The
+ * reference's decode takes arrays wherever MLX keeps them; this is its host-buffer form (stream_fast.py:6411-6441's
+ * attn_cuda for a caller that holds q and reads o on the host). */
+size_t lb2_attn_decode_host_workspace_size(int B, int Hq, int Hkv, int T, int N, int D, int dtype, int split);
+int lb2_attn_decode_host(const void* q_host, const void* k, const int64_t* k_st, const void* v, const int64_t* v_st,
+                         void* o_host, const int32_t* kv_len, int B, int Hq, int Hkv, int T, int N, int D, int dtype,
+                         float scale, int causal, int split, void* workspace, size_t workspace_bytes, void* stream);
+int lb2_attn_decode_host_drain(void* stream);
+
 /* The same decode over this rank's KV range only, emitting the range's normalised partial output and its
  * log-sum-exp instead of the final o: part_o fp32 [B, Hq, T, D] contiguous, part_lse fp32 [B, Hq, T] (natural
  * log; -inf for a row with no visible key). For KV-range shards across GPUs merged by lb2_attn_combine.

@@ -38,6 +38,10 @@ SIGNATURES = {
     "lb2_kv_gather_picks": ([_p, _i64p, _p, _i64p, _p, _i, _i, _i, _p, _p, _i, _i, _i, _p], _i),
     "lb2_kvh_put": ([_p, _p, _i64p, _p, _i64p, ctypes.c_int64, _i, _i, _i, _i, _i, _p], _i),
     "lb2_kvh_gather": ([_p, _p, _i, _i, _i, _p, _p, _i, _i, _i, _i, _p], _i),
+    "lb2_attn_decode_host_workspace_size": ([_i, _i, _i, _i, _i, _i, _i, _i], _sz),
+    "lb2_attn_decode_host": ([_p, _p, _i64p, _p, _i64p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _i, _i, _p, _sz, _p],
+                             _i),
+    "lb2_attn_decode_host_drain": ([_p], _i),
     "lb2_xch_bytes": ([_i, _i, _i, _i], _sz),
     "lb2_xch_alloc": ([_sz, ctypes.POINTER(ctypes.c_void_p)], _i),
     "lb2_xch_free": ([_p], _i),

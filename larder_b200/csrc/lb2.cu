@@ -517,6 +517,95 @@ int lb2_attn_combine_packed(const float* packed, int R, int B, int Hq, int T, in
 }
 
 
+// ------------------------------------------------------------------------------------------------ host-buffer decode
+
+namespace {
+
+// Per-device state of lb2_attn_decode_host: its two copy streams, the events that order two staging slots, and the
+// count of calls (slot = count % 2). Created on a device's first call, kept until exit.
+struct HostDecodeState {
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  cudaEvent_t h2d_done[2] = {}, dec_done[2] = {}, d2h_done[2] = {};
+  uint64_t calls = 0;
+  bool ready = false;
+};
+HostDecodeState g_host_decode[64];
+
+int host_decode_state(HostDecodeState** out) {
+  int dev = 0;
+  LB2_CUDA(cudaGetDevice(&dev));
+  LB2_CHECK_ARG(dev >= 0 && dev < 64, "decode_host: device index");
+  HostDecodeState& s = g_host_decode[dev];
+  if (!s.ready) {
+    LB2_CUDA(cudaStreamCreateWithFlags(&s.h2d, cudaStreamNonBlocking));
+    LB2_CUDA(cudaStreamCreateWithFlags(&s.d2h, cudaStreamNonBlocking));
+    for (int j = 0; j < 2; ++j)
+      for (cudaEvent_t* e : {&s.h2d_done[j], &s.dec_done[j], &s.d2h_done[j]})
+        LB2_CUDA(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
+    s.ready = true;
+  }
+  *out = &s;
+  return LB2_OK;
+}
+
+size_t host_stage_bytes(int B, int Hq, int T, int D, int dtype) {
+  const size_t row = size_t(B) * Hq * T * D * (dtype == LB2_F32 ? 4 : 2);
+  return (row + 255) / 256 * 256;  // one q or o image, 256-byte aligned
+}
+
+}  // namespace
+
+size_t lb2_attn_decode_host_workspace_size(int B, int Hq, int Hkv, int T, int N, int D, int dtype, int split) {
+  const size_t dec = lb2_attn_decode_workspace_size(B, Hq, Hkv, T, N, D, split);
+  if (dec == 0 || D <= 0) return 0;
+  return 4 * host_stage_bytes(B, Hq, T, D, dtype) + dec;
+}
+
+int lb2_attn_decode_host(const void* q_host, const void* k, const int64_t* k_st, const void* v, const int64_t* v_st,
+                         void* o_host, const int32_t* kv_len, int B, int Hq, int Hkv, int T, int N, int D, int dtype,
+                         float scale, int causal, int split, void* workspace, size_t workspace_bytes, void* stream) {
+  LB2_CHECK_ARG(q_host && o_host, "decode_host: host buffers missing");
+  LB2_CHECK_ARG(B > 0 && Hq > 0 && T > 0 && D > 0, "decode_host: shape");
+  const size_t need = lb2_attn_decode_host_workspace_size(B, Hq, Hkv, T, N, D, dtype, split);
+  LB2_CHECK_ARG(need > 0 && workspace_bytes >= need && (reinterpret_cast<uintptr_t>(workspace) & 255) == 0,
+                "decode_host: workspace too small or not 256-byte aligned");
+  HostDecodeState* s = nullptr;
+  if (const int rc = host_decode_state(&s)) return rc;
+  const size_t stage = host_stage_bytes(B, Hq, T, D, dtype);
+  const size_t bytes = size_t(B) * Hq * T * D * (dtype == LB2_F32 ? 4 : 2);
+  const int j = int(s->calls & 1);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  void* q_dev = ws + j * stage;
+  void* o_dev = ws + (2 + j) * stage;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // q in on the copy stream, once the decode two calls back has read this slot
+  LB2_CUDA(cudaStreamWaitEvent(s->h2d, s->dec_done[j], 0));
+  LB2_CUDA(cudaMemcpyAsync(q_dev, q_host, bytes, cudaMemcpyHostToDevice, s->h2d));
+  LB2_CUDA(cudaEventRecord(s->h2d_done[j], s->h2d));
+  // the decode on the caller's stream, once q is in and this slot's o of two calls back is out
+  LB2_CUDA(cudaStreamWaitEvent(st, s->h2d_done[j], 0));
+  LB2_CUDA(cudaStreamWaitEvent(st, s->d2h_done[j], 0));
+  const int64_t qs[3] = {int64_t(Hq) * T * D, int64_t(T) * D, D};
+  if (const int rc = lb2_attn_decode(q_dev, qs, k, k_st, v, v_st, o_dev, qs, kv_len, B, Hq, Hkv, T, N, D, dtype, scale,
+                                     causal, split, ws + 4 * stage, workspace_bytes - 4 * stage, stream))
+    return rc;
+  LB2_CUDA(cudaEventRecord(s->dec_done[j], st));
+  // o out on the other copy stream
+  LB2_CUDA(cudaStreamWaitEvent(s->d2h, s->dec_done[j], 0));
+  LB2_CUDA(cudaMemcpyAsync(o_host, o_dev, bytes, cudaMemcpyDeviceToHost, s->d2h));
+  LB2_CUDA(cudaEventRecord(s->d2h_done[j], s->d2h));
+  ++s->calls;
+  return LB2_OK;
+}
+
+int lb2_attn_decode_host_drain(void* stream) {
+  HostDecodeState* s = nullptr;
+  if (const int rc = host_decode_state(&s)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int j = 0; j < 2; ++j) LB2_CUDA(cudaStreamWaitEvent(st, s->d2h_done[j], 0));
+  return LB2_OK;
+}
+
 // ------------------------------------------------------------------------------------------------ peer exchange
 
 size_t lb2_xch_bytes(int B, int Hq, int T, int D) {

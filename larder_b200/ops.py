@@ -144,6 +144,41 @@ def attn_decode(q, k, v, scale, causal=False, kv_len=None, split=0, out=None):
     return out
 
 
+def attn_decode_host(q_host, k, v, scale, o_host, causal=False, kv_len=None, split=0):
+    """attn_decode for q and o in host memory (contiguous CPU tensors [B, Hq, T, D], pinned for the copies to
+    overlap): copies q in, decodes on the current stream, copies o out, without waiting. o_host (of this call and
+    the ones before) is complete after attn_decode_host_drain() and a synchronisation of the stream."""
+    _cuda(k, v, kv_len)
+    for t, n in ((q_host, "q_host"), (o_host, "o_host")):
+        if t.is_cuda or not t.is_contiguous():
+            raise ValueError(f"attn_decode_host: {n} must be a contiguous host tensor")
+    if q_host.shape != o_host.shape or q_host.dtype != o_host.dtype or q_host.dtype != k.dtype:
+        raise ValueError("attn_decode_host: q_host, o_host and the cache must share shape / dtype")
+    B, Hq, T, D = q_host.shape
+    Hkv, N = k.shape[1], k.shape[2]
+    if kv_len is not None and (kv_len.dtype != torch.int32 or kv_len.numel() != B):
+        raise ValueError("kv_len must be int32 [B]")
+    L = lib()
+    need = L.lb2_attn_decode_host_workspace_size(B, Hq, Hkv, T, N, D, dtype_code(k), int(split))
+    cur = _WS.get((k.device.index if k.device.index is not None else torch.cuda.current_device(), "decode_host"))
+    if cur is not None and cur.numel() < need:  # copies still in flight may use the old buffer: let them finish
+        attn_decode_host_drain(k.device.index)
+        torch.cuda.synchronize(k.device)
+    ws = workspace(k.device, need, "decode_host")
+    rc = L.lb2_attn_decode_host(q_host.data_ptr(), _ptr(k), i64(*k.stride()[:3]), _ptr(v), i64(*v.stride()[:3]),
+                                o_host.data_ptr(), _ptr(kv_len), B, Hq, Hkv, T, N, D, dtype_code(k), float(scale),
+                                int(bool(causal)), int(split), _ptr(ws), ws.numel(), _stream(k))
+    check(rc, "attn_decode_host")
+    return o_host
+
+
+def attn_decode_host_drain(device=None):
+    """Order the current stream after every outstanding attn_decode_host copy out."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+    check(lib().lb2_attn_decode_host_drain(ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)),
+          "attn_decode_host_drain")
+
+
 def attn_decode_partial(q, k, v, scale, kv_len=None, split=0, out=None):
     """This KV range's normalised partial output (fp32 [B, Hq, T, D]) and log-sum-exp (fp32 [B, Hq, T]); `out`, a
     pair of contiguous fp32 tensors of those shapes (for instance the two parts of one packed exchange buffer),
