@@ -6,7 +6,8 @@
   picked at times, a trim midway, a chunk boundary crossed): each step's gathered rows equal the oracle's (plan +
   gather over a CPU mirror of the home and the pool) and the rows of the whole cache at the picked positions; the
   pool and its state equal the mirror's at the end.
-* Picks out of range are skipped with zero rows and reported in the status word, without touching memory."""
+* Picks out of range are skipped with zero rows and reported in the status word, without touching memory.
+* Flash-Next's decode shapes (24/2 x 256, CR 4, 512 picks) through Home.decode, attention against the oracle."""
 import types
 
 import numpy as np
@@ -112,3 +113,38 @@ def test_out_of_range_pick_is_skipped_and_reported():
     assert ops.status() == (91 << 8) | 1  # LB2_EINVAL from the plan, the first report
     assert not kg[0, :, (nsel - 1) * cr:nsel * cr].any() and not vg[0, :, (nsel - 1) * cr:nsel * cr].any()
     assert torch.equal(kg[0, :, :4], kv[0, 0, :, :4]), "the valid picks are unaffected"
+
+
+def test_home_lru_flash_next_shapes():
+    """Flash-Next's decode through Home(lru=True).decode: 24/2 heads x 256, CR 4, 512 picks (a plan block of 512
+    threads over 2048 slots). Three tokens, the second keeping most of the first's picks (hits); each token's
+    attention over its picks against the oracle over the same rows of the whole cache."""
+    import checks
+    from gpu_util import f32, to_np
+    g = torch.Generator().manual_seed(43)
+    rng = np.random.default_rng(43)
+    Hq, Hk, D, cr, nsel, n0 = 24, 2, 256, 4, 512, 12000
+    rows = torch.randn(2, 1, Hk, n0 + 3, D, generator=g).to(torch.bfloat16).cuda()
+    home = kv_host.Home(Hk, D, torch.bfloat16, "cuda", lru=True)
+    home.put(rows[0, :, :, :n0], rows[1, :, :, :n0])
+    prev = None
+    for step in range(3):
+        n = n0 + step + 1
+        nb = n // cr
+        if step == 1:
+            keep = rng.choice(prev, 400, replace=False)
+            rest = np.setdiff1d(np.arange(nb), keep)
+            tb = np.sort(np.concatenate([keep, rng.choice(rest, nsel - 400, replace=False)]))
+        else:
+            tb = np.sort(rng.choice(nb, nsel, replace=False))
+        prev = tb
+        q = torch.randn(1, Hq, 1, D, generator=g).to(torch.bfloat16).cuda()
+        k1, v1 = rows[0, :, :, n - 1:n], rows[1, :, :, n - 1:n]
+        out = f32(home.decode(q, k1, v1, torch.from_numpy(tb.astype(np.int32)).cuda(), cr, D ** -0.5))
+        pos = np.concatenate([(tb[:, None] * cr + np.arange(cr)).reshape(-1), np.arange(nb * cr, n)])
+        pos_t = torch.from_numpy(pos).cuda()
+        ref = oracle.attn(to_np(q), to_np(rows[0, :, :, :n][:, :, pos_t]), to_np(rows[1, :, :, :n][:, :, pos_t]),
+                          D ** -0.5, oracle.BF16, out_dt=oracle.F32)
+        checks.grading_close(out, ref, what=f"token {step}")
+    rep = kv_host.report([home])
+    assert rep["hits"] >= 400 and rep["hits"] + rep["misses"] == 3 * nsel, rep
