@@ -32,6 +32,8 @@ def bf16(a):
     (2, 3, 8, 64, 1501, 4, 256, 3),     # verify rows, 8 heads x 64, a block count that is not a multiple of 4
     (1, 2, 4, 64, 40001, 4, 2048, 2),   # a cluster of 8 CTAs a row
     (1, 1, 4, 64, 140001, 4, 2048, 1),  # more blocks than a cluster holds in registers: the streamed passes
+    (3, 2, 2, 128, 5000, 4, 300, 0),    # two heads (MMA columns 2-7 zero), complete blocks only
+    (1, 4, 1, 64, 777, 8, 64, 5),       # one head, compress ratio 8
 ])
 def test_qsa_select_matches_oracle(B, S, H, D, nb, cr, k, offset_from_end):
     rng = np.random.default_rng(nb + S)
