@@ -128,8 +128,9 @@ class PeerExchange:
             self.opened.append(p.value)
             bufs.append(p.value)
         # every rank mapped every peer, or all give up together (none goes on to a step the others left)
-        ok = torch.tensor([0 if err else 1], dtype=torch.int32,
-                          device=torch.device("cuda", torch.cuda.current_device()))
+        dev = torch.device("cpu") if dist.get_backend(group) == "gloo" else \
+            torch.device("cuda", torch.cuda.current_device())
+        ok = torch.tensor([0 if err else 1], dtype=torch.int32, device=dev)
         dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
         if not int(ok.item()):
             for p in self.opened:
@@ -158,7 +159,8 @@ class PeerExchange:
         """Unmap the peers' buffers and free this rank's, once every rank's kernels are done with them."""
         if self.base is None:
             return
-        torch.cuda.synchronize()
+        if torch.cuda.is_available():
+            torch.cuda.synchronize()
         dist.barrier(group=self.group)
         for p in self.opened:
             check(lib().lb2_xch_close(ctypes.c_void_p(p)), "xch_close")

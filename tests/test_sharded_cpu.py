@@ -113,3 +113,88 @@ def test_dead_rank_is_an_error_not_a_hang():
     for p in procs:
         p.join(timeout=60)
     assert rank == 0 and what != "no error"
+
+
+class _FakeXchLib:
+    """The exchange's CUDA calls stood in for on CPU ranks: allocation, 64-byte handles and mappings as plain
+    numbers, every call recorded; the open of `fail_rank` fails."""
+
+    def __init__(self, rank, fail_rank):
+        self.rank, self.fail_rank, self.calls = rank, fail_rank, []
+
+    def lb2_xch_bytes(self, B, Hq, T, D):
+        return 2 * B * Hq * T * (D + 1) * 4 + 32
+
+    def lb2_xch_alloc(self, nbytes, pptr):
+        pptr._obj.value = 0x10000 * (self.rank + 1)
+        self.calls.append(("alloc", nbytes))
+        return 0
+
+    def lb2_xch_handle(self, ptr, buf):
+        import ctypes
+        ctypes.memmove(buf, (b"H%d" % self.rank).ljust(64, b"\0"), 64)
+        return 0
+
+    def lb2_xch_open(self, hbuf, pptr):
+        if self.rank == self.fail_rank:
+            return 1
+        peer = int(hbuf.raw[1:2])
+        pptr._obj.value = 0x900000 + peer
+        self.calls.append(("open", peer))
+        return 0
+
+    def lb2_xch_close(self, p):
+        self.calls.append(("close", p.value))
+        return 0
+
+    def lb2_xch_free(self, p):
+        self.calls.append(("free", p.value))
+        return 0
+
+    def lb2_error(self):
+        return b"mapping refused"
+
+
+def _xch_worker(rank, world, port, fail_rank, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        fake = _FakeXchLib(rank, fail_rank)
+        sharded.lib = lambda: fake
+        try:
+            xch = sharded.PeerExchange(2, 4, 1, 8)
+        except RuntimeError as e:
+            q.put((rank, "raised", str(e), fake.calls))
+            return
+        bufs = list(xch.bufs)
+        xch.close()
+        q.put((rank, "ok", bufs, fake.calls))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("fail_rank", [-1, 1])
+def test_peer_exchange_setup_all_or_nothing(fail_rank):
+    """PeerExchange on two CPU ranks with the CUDA calls faked: each rank maps the other's buffer and keeps its own
+    at its rank; close unmaps the peer before freeing its own. When one rank cannot map, both raise (neither goes on
+    to a step the other left), and each releases what it had set up."""
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_xch_worker, args=(r, world, port, fail_rank, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, status, info, calls in res:
+        base = 0x10000 * (rank + 1)
+        if fail_rank < 0:
+            assert status == "ok"
+            assert info[rank] == base and info[1 - rank] == 0x900000 + (1 - rank)
+            assert calls[-2:] == [("close", 0x900000 + (1 - rank)), ("free", base)]
+        else:
+            assert status == "raised" and "could not map" in info
+            assert calls[-1] == ("free", base)
+            assert (("close", 0x900000 + (1 - rank)) in calls) == (rank != fail_rank)
