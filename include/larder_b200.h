@@ -124,7 +124,8 @@ int lb2_attn_decode_partial(const void* q, const int64_t* q_st, const void* k, c
  * allocation would break the budget), or a caller on a latency-critical path where cudaMalloc's implicit device
  * synchronisation is not acceptable. This entry has no counterpart in the reference (whose decode runs inside MLX's
  * allocator); it exists for such callers of this library.
- * Arguments and results as lb2_attn_decode, without the workspace: the split partials live in a
+ * Arguments and results as lb2_attn_decode, without the workspace (dtype LB2_F32 runs the exact fp32 kernel, which
+ * needs no scratch, exactly as lb2_attn_decode does): the bf16 / f16 split partials live in a
  * file-scope device array of LB2_NOALLOC_SCRATCH_BYTES (8 MiB) that every GPU loading this library holds until the
  * process exits. A call whose workspace (lb2_attn_decode_workspace_size) exceeds that size returns LB2_EINVAL;
  * choose a larger `split` or use lb2_attn_decode. The first call on a device looks up the array's device address

@@ -465,6 +465,9 @@ int lb2_attn_decode_noalloc(const void* q, const int64_t* q_st, const void* k, c
                             int Hkv, int T, int N, int D, int dtype, float scale, int causal, int split,
                             void* stream) {
   LB2_CHECK_ARG(o != nullptr && o_st != nullptr, "decode_noalloc: output missing");
+  if (dtype == LB2_F32)  // the exact fp32 kernel uses no scratch at all, as in lb2_attn_decode
+    return lb2_attn_decode(q, q_st, k, k_st, v, v_st, o, o_st, kv_len, B, Hq, Hkv, T, N, D, dtype, scale, causal,
+                           split, nullptr, 0, stream);
   const size_t need = lb2_attn_decode_workspace_size(B, Hq, Hkv, T, N, D, split);
   LB2_CHECK_ARG(need > 0, "decode_noalloc: empty or unsupported shape");
   if (need > LB2_NOALLOC_SCRATCH_BYTES)
@@ -530,12 +533,14 @@ struct HostDecodeState {
   bool ready = false;
 };
 HostDecodeState g_host_decode[64];
+std::mutex g_host_decode_mu;  // guards the lazy creation: two threads' first calls on one device make one set
 
 int host_decode_state(HostDecodeState** out) {
   int dev = 0;
   LB2_CUDA(cudaGetDevice(&dev));
   LB2_CHECK_ARG(dev >= 0 && dev < 64, "decode_host: device index");
   HostDecodeState& s = g_host_decode[dev];
+  std::lock_guard<std::mutex> lock(g_host_decode_mu);
   if (!s.ready) {
     LB2_CUDA(cudaStreamCreateWithFlags(&s.h2d, cudaStreamNonBlocking));
     LB2_CUDA(cudaStreamCreateWithFlags(&s.d2h, cudaStreamNonBlocking));

@@ -7,8 +7,8 @@ NumPy arrays, and records every step of two seeded decode sequences: the picks (
 probability 0.6, as the reference test's `decode` does, test_kv_host_emu.py:336-347), the occasional trim, and
 the LRU state after each step.
 
-Run once, in a checkout where the reference sits at REFERENCE (default /root/reference); the fixture is committed:
-    python tests/golden/make_kvh_lru.py
+Run once, with REFERENCE naming a checkout of the reference repository; the fixture is committed:
+    REFERENCE=<checkout of IamCooller/larder> python tests/golden/make_kvh_lru.py
 """
 import ast
 import os
@@ -16,7 +16,6 @@ import sys
 
 import numpy as np
 
-REF = os.environ.get("REFERENCE", "/root/reference")
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "kvh_lru.npz")
 
 
@@ -33,8 +32,8 @@ class _Mx:
         pass
 
 
-def load_emulations():
-    src = open(os.path.join(REF, "tests", "test_kv_host_emu.py")).read()
+def load_emulations(ref):
+    src = open(os.path.join(ref, "tests", "test_kv_host_emu.py")).read()
     tree = ast.parse(src)
     keep = [n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name in ("inplace", "emu_plan", "emu_inval")]
     assert len(keep) == 3, "the reference's emulations moved"
@@ -78,7 +77,10 @@ def sequence(plan, inval, rng, nsel, cr, ns, max_blocks, steps, n0):
 
 
 def main():
-    plan, inval = load_emulations()
+    ref = os.environ.get("REFERENCE")
+    if not ref:
+        sys.exit("set REFERENCE to a checkout of the reference repository (its tests/ are read and executed)")
+    plan, inval = load_emulations(ref)
     rng = np.random.default_rng(2024)
     cases = [
         sequence(plan, inval, rng, nsel=16, cr=4, ns=32, max_blocks=160, steps=70, n0=200),   # the reference test's

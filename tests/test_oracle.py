@@ -1,6 +1,7 @@
-"""The CPU oracle (oracle/liboracle.so) pinned against the golden vectors: the reference tests' float64 oracles on
-the reference tests' own seeded inputs, with the reference tests' tolerances. Also: the generated inputs still hash
-to the digests stored with the goldens, and a mistake planted in the oracle is caught."""
+"""The CPU oracle (oracle/liboracle.so) pinned against the golden vectors: the reference tests' float64 oracles,
+executed from the reference's own source by tests/golden/make_golden.py, on the reference tests' own seeded inputs,
+with the reference tests' tolerances. Also: the generated inputs still hash to the digests stored with the goldens,
+the goldens record which reference source made them, and a mistake planted in the oracle is caught."""
 import numpy as np
 import pytest
 
@@ -12,6 +13,31 @@ import oracle
 @pytest.fixture(scope="module")
 def g():
     return checks.golden()
+
+
+def test_goldens_come_from_the_reference_source(g):
+    """The vectors were made by executing the reference tests' functions (not a restatement): the generator stores
+    the functions it ran and the sha256 of the files it took them from."""
+    assert "test_attn.ref" in str(g["source.functions"]) and "test_gdn_cuda.py:ref" in str(g["source.functions"])
+    for f in ("source.test_cpu_kern.sha256", "source.test_gdn_cuda.sha256"):
+        assert len(str(g[f])) == 64
+
+
+def test_float64_restatements_agree_with_the_goldens(g):
+    """oracle.attn_ref64 / gdn_ref64 (used by other tests as float64 checkers) give the same vectors as the
+    reference's executed functions, to float32 storage."""
+    for c in cases.attn_cases():
+        q, k, v = (cases.to64(c[n], c["dt"]) for n in ("q", "k", "v"))
+        for kind, m in (("none", None), ("causal", oracle.causal_mask(c["T"], c["N"])), ("array", c["rnd"])):
+            checks.golden_close(oracle.attn_ref64(q, k, v, c["scale"], m), f"attn{c['case']}.{kind}", 1e-7,
+                                what="attn_ref64")
+    for i in range(len(cases.GDN_CUDA_CASES)):
+        c = cases.gdn_cuda_case(i)
+        y, s = oracle.gdn_ref64(cases.to64(c["q"], c["dt"]), cases.to64(c["k"], c["dt"]),
+                                cases.to64(c["v"], c["dt"]), c["g"], cases.to64(c["beta"], c["b_dt"]), c["state"],
+                                c["mask"])
+        checks.golden_close(y, f"gdncuda{i}.y", 1e-7, what="gdn_ref64 y")
+        checks.golden_close(s, f"gdncuda{i}.s", 1e-7, what="gdn_ref64 state")
 
 
 def test_digests_match(g):
