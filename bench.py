@@ -30,9 +30,10 @@ sys.path.insert(0, ROOT)
 
 METRIC = "prefill attn TFLOP/s & decode KV-read GB/s at 8k ctx, 1/2/4/8 B200, % peak"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# dram__bytes_read.sum + dram__bytes_write.sum of one decode_kernel launch on this workload, from the ncu capture in
-# profiles/decode_kernel_config2.md (148.3 MB read + 4.5 MB written).
+# dram__bytes_read.sum + dram__bytes_write.sum of one decode_kernel launch on this workload, from an ncu capture of
+# decode_kernel on this command (148.3 MB read + 4.5 MB written).
 DECODE_TRAFFIC_BYTES = 152.1e6
+DECODE_WORKLOAD = "configs[1] GQA decode: B=16 per rank, 32q/4kv x 128, bf16 KV, lengths U[1024,8192]"
 
 
 def peaks():
@@ -160,10 +161,13 @@ def run_ours(args):
         torch.cuda.synchronize(dev)
 
     def max_over_ranks(x):
+        return reduce_over_ranks(x, "max")
+
+    def reduce_over_ranks(x, how):
         if world == 1:
             return x
         t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op={"max": dist.ReduceOp.MAX, "min": dist.ReduceOp.MIN, "sum": dist.ReduceOp.SUM}[how])
         return float(t.item())
 
     out = {"metric": METRIC, "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
@@ -172,7 +176,7 @@ def run_ours(args):
     # ---------------------------------------------------------------- decode (headline)
     if "decode" in sections:
         out.update(bench_decode(torch, ops, dev, rank, world, args, stream, pk, pk_kind, barrier_sync,
-                                max_over_ranks, local))
+                                reduce_over_ranks, local))
     # ---------------------------------------------------------------- prefill
     if "prefill" in sections:
         try:
@@ -183,7 +187,7 @@ def run_ours(args):
     if "sharded" in sections:
         try:
             out["sharded"] = bench_sharded(torch, ops, dev, rank, world, args, stream, pk, barrier_sync,
-                                           max_over_ranks)
+                                           reduce_over_ranks)
         except Exception as e:
             out["sharded"] = {"error": f"{type(e).__name__}: {e}"}
     if "gdn" in sections:
@@ -207,6 +211,10 @@ def run_ours(args):
     # ---------------------------------------------------------------- CPU baseline (rank 0, N=1 only)
     if world == 1 and rank == 0 and not args.no_cpu:
         out["cpu_baseline"] = cpu_decode_baseline(torch, args, reps=3)
+        if isinstance(out.get("prefill"), dict) and "error" not in out["prefill"]:
+            out["prefill"]["cpu_baseline"] = cpu_prefill_baseline()
+        if isinstance(out.get("gdn"), dict) and "error" not in out["gdn"]:
+            out["gdn"]["prefill"]["cpu_baseline"], out["gdn"]["decode"]["cpu_baseline"] = cpu_gdn_baseline()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -214,9 +222,14 @@ def run_ours(args):
         print(json.dumps(out))
 
 
-def bench_decode(torch, ops, dev, rank, world, args, stream, pk, pk_kind, barrier_sync, max_over_ranks, local):
-    """The headline: configs[1] decode, KV-read GB/s, with its roofline, clocks and end-to-end figure."""
+def bench_decode(torch, ops, dev, rank, world, args, stream, pk, pk_kind, barrier_sync, reduce_over_ranks, local):
+    """The headline: configs[1] decode, KV-read GB/s, with its roofline, clocks and end-to-end figure. Every rank draws
+    its own lengths, so the whole job's bytes are the sum over ranks, over the slowest rank's time."""
     out = {}
+
+    def max_over_ranks(x):
+        return reduce_over_ranks(x, "max")
+
     copies = 4
     lens, sets, (B, Hq, Hkv, D) = decode_inputs(torch, dev, 1000 + rank, copies)
     kv_len = lens.to(torch.int32).to(dev)
@@ -251,19 +264,22 @@ def bench_decode(torch, ops, dev, rank, world, args, stream, pk, pk_kind, barrie
         barrier_sync()
         ms = cuda_time(torch, replay, 1, stream)
     barrier_sync()
-    ms = max_over_ranks(ms)
+    ms_min, ms = reduce_over_ranks(ms, "min"), max_over_ranks(ms)
+    kv_bytes_all = reduce_over_ranks(kv_bytes, "sum")
     per = ms / args.steps
-    gbs = world * kv_bytes / (per * 1e-3) / 1e9
+    gbs = kv_bytes_all / (per * 1e-3) / 1e9
     kern_gbs = alg_bytes / (per * 1e-3) / 1e9
     out.update({"value": round(gbs, 1), "unit": "GB/s", "ms_per_step": round(per, 5)})
-    out["config"] = {"workload": "configs[1] GQA decode: B=16/rank, 32q/4kv x 128, bf16 KV, lengths U[1024,8192]",
+    out["config"] = {"workload": DECODE_WORKLOAD,
                      "global_batch": 16 * world, "kv_lens_sum_per_rank": int(lens.sum()), "parallelism": f"dp{world}",
+                     "kv_bytes_all_ranks_per_step": int(kv_bytes_all),
+                     "rank_ms_per_step": {"min": round(ms_min / args.steps, 5), "max": round(per, 5)},
                      "split": split or "auto", "l2": f"{copies} rotating KV caches ({copies} x "
                      f"{kv_bytes / 1e6:.0f} MB read) so consecutive steps miss L2",
                      "launch": "the K steps as one CUDA graph, replayed once; e2e is the eager API call"}
     out["roofline"] = {"bound": "hbm", "achieved": round(kern_gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                        "frac": round(kern_gbs / pk["hbm_gbs"], 4), "traffic": DECODE_TRAFFIC_BYTES,
-                       "traffic_source": "ncu, profiles/decode_kernel_config2.md", "peak_kind": pk_kind,
+                       "traffic_source": "ncu capture of decode_kernel on this workload", "peak_kind": pk_kind,
                        "kernel": "lb2::decode::decode_kernel<bf16,128,1>",
                        "algorithmic_bytes_per_launch": alg_bytes}
     out["clocks"] = clk.summary()
@@ -298,7 +314,7 @@ def bench_decode(torch, ops, dev, rank, world, args, stream, pk, pk_kind, barrie
     ms_e2e = max_over_ranks(e2e_time(args.steps))
     barrier_sync()
     per_e2e = ms_e2e / args.steps
-    out["e2e"] = {"value": round(world * kv_bytes / (per_e2e * 1e-3) / 1e9, 1), "unit": "GB/s",
+    out["e2e"] = {"value": round(kv_bytes_all / (per_e2e * 1e-3) / 1e9, 1), "unit": "GB/s",
                   "h2d_bytes_per_step": q_host[0].numel() * 2, "d2h_bytes_per_step": o_host[0].numel() * 2,
                   "ms_per_step": round(per_e2e, 5), "api": "larder_b200.ops.attn_decode_host (lb2_attn_decode_host)",
                   "copies": "q in and o out every step from / to pinned host memory, on the library's copy streams"}
@@ -359,12 +375,16 @@ def bench_prefill(torch, ops, dev, rank, world, args, stream, pk, pk_kind, barri
             "clocks": clk.summary()}
 
 
-def bench_sharded(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_over_ranks):
+def bench_sharded(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, reduce_over_ranks):
     """configs[4] per rank (weak scaling: the 8-GPU share of each rank fixed): 8 independent 8192-token causal
     prefills (32q/4kv x 128), and a batch-64 decode over this rank's 4096-key range of every sequence merged across
     ranks (NCCL all-gather of packed (o, lse), then the log-sum-exp combine; at N > 1 also over NVLink peer
     memory, `decode_peer`). At 8 GPUs that is configs[4]."""
     from larder_b200 import sharded
+
+    def max_over_ranks(x):
+        return reduce_over_ranks(x, "max")
+
     g = torch.Generator(device=dev).manual_seed(5000 + rank)
     # prefill: 8 sequences a rank
     S, Hq, Hkv, D, T = 8, 32, 4, 128, 8192
@@ -406,6 +426,12 @@ def bench_sharded(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, 
     if world > 1:  # the same decode with the exchange over NVLink peer memory (no collective on the data path)
         xch = sharded.PeerExchange(B, Hq, 1, D)
         try:
+            # before timing: the peer-memory exchange against the NCCL one on the same inputs (same partials, same
+            # merge order, so bit-equal), recorded per rank as the count of ranks that matched
+            kk, vv = kvs[0]
+            same = torch.equal(xch.decode(dq, kk, vv, D ** -0.5), sharded.kv_sharded_decode(dq, kk, vv, D ** -0.5))
+            ranks_equal = int(reduce_over_ranks(float(same), "sum"))
+
             def dec_peer(i):
                 kk, vv = kvs[i % copies]
                 xch.decode(dq, kk, vv, D ** -0.5)
@@ -418,15 +444,16 @@ def bench_sharded(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, 
                     "ms_per_step": round(ms_pd, 5),
                     "per_rank": f"B=64 x {n_local} local keys; partials read in place from the peers' exchange "
                                 "buffers over NVLink (lb2_attn_combine_peers)",
-                    "kernel": "lb2::decode::decode_kernel + lb2::xch::peer_combine_kernel"}
+                    "kernel": "lb2::decode::decode_kernel + lb2::xch::peer_combine_kernel",
+                    "ranks_bit_equal_to_nccl_path": ranks_equal}
         finally:
             xch.close()
     return {"prefill": {"value": round(world * flop / (ms_p * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                         "ms_per_step": round(ms_p, 4), "per_rank": "8 x 8192 causal, 32q/4kv x 128, bf16",
                         "roofline": {"bound": "tensor", "achieved": round(flop / (ms_p * 1e-3) / 1e12, 2),
-                                     "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
-                                     "frac": round(flop / (ms_p * 1e-3) / 1e12 / pk["bf16_tflops_sustained"], 4),
-                                     "peak_kind": "sustained (long step)",
+                                     "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                                     "frac": round(flop / (ms_p * 1e-3) / 1e12 / pk["bf16_tflops"], 4),
+                                     "peak_kind": "burst (one launch timed alone)",
                                      "kernel": "lb2::prefill2::fmha2_kernel<bf16,128>"}},
             "decode": {"value": round(world * kv_bytes / (ms_d * 1e-3) / 1e9, 1), "unit": "GB/s",
                        "ms_per_step": round(ms_d, 5), "context": n_local * world,
@@ -602,9 +629,33 @@ def bench_gdn(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_
 
 # ------------------------------------------------------------------------------------------------ CPU arms
 
+def cpu_topology():
+    """Host CPU as lscpu reports it, and the thread count the CPU arms use: one a physical core the process may run
+    on (the reference's CPU path takes physical cores, cpu_kernels.py:14-22, :91)."""
+    info = {}
+    try:
+        txt = subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout
+        for line in txt.splitlines():
+            key, _, val = line.partition(":")
+            info[key.strip()] = val.strip()
+    except (OSError, subprocess.SubprocessError):
+        pass
+
+    def num(k, d):
+        try:
+            return int(info.get(k, d))
+        except ValueError:
+            return d
+    logical = len(os.sched_getaffinity(0))
+    sockets, cores, tpc = num("Socket(s)", 1), num("Core(s) per socket", logical), num("Thread(s) per core", 1)
+    threads = max(1, min(sockets * cores, logical // max(tpc, 1) if tpc > 1 else logical))
+    return threads, {"sockets": sockets, "cores_per_socket": cores, "threads_per_core": tpc,
+                     "logical_cpus_available": logical, "model": info.get("Model name", "")}
+
+
 def cpu_decode_baseline(torch, args, reps=3, sample_seqs=16):
     """Config 2 through the CPU oracle (the restated reference CPU kernel), one call per sequence as the reference's
-    CPU attention requires (mask leading dims 1, cpu_kern.cpp:653), all host cores."""
+    CPU attention requires (mask leading dims 1, cpu_kern.cpp:653), one thread a physical core."""
     import numpy as np
 
     import oracle
@@ -619,7 +670,7 @@ def cpu_decode_baseline(torch, args, reps=3, sample_seqs=16):
         k = oracle.f32_to_bf16(rng.normal(0, 1, (1, Hkv, n, D)).astype(np.float32))
         v = oracle.f32_to_bf16(rng.normal(0, 1, (1, Hkv, n, D)).astype(np.float32))
         seqs.append((q, k, v, n))
-    threads = oracle.default_threads()
+    threads, topo = cpu_topology()
     times = []
     for r in range(reps + 1):
         t0 = time.perf_counter()
@@ -629,9 +680,82 @@ def cpu_decode_baseline(torch, args, reps=3, sample_seqs=16):
             times.append(time.perf_counter() - t0)
     t = sorted(times)[len(times) // 2]
     kv = sum(n for *_, n in seqs) * Hkv * D * 2 * 2
-    return {"value": round(kv / t / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+    return {"value": round(kv / t / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port", "lscpu": topo,
             "sample": f"configs[1] decode, {len(seqs)} sequences (sum len {sum(n for *_, n in seqs)}), one oracle call "
                       f"each, median of {reps} after one warm-up", "seconds": round(t, 3)}
+
+
+def cpu_prefill_baseline():
+    """configs[2] through the CPU oracle (CpuAttn restated), as the reference's loop issues it: four 2048-row chunk
+    calls over keys 0 .. 2048(c + 1), causal; the gate is elementwise and not timed. Bounded sample: the 8 query
+    heads of one KV head (half the heads), all four chunks, one thread a physical core; TFLOP/s over the causal pairs
+    of the heads run."""
+    import numpy as np
+
+    import oracle
+    threads, topo = cpu_topology()
+    rng = np.random.default_rng(3)
+    Hq, Hkv, D, T, W = 8, 1, 256, 8192, 2048
+    q = oracle.f32_to_bf16(rng.normal(0, 1, (1, Hq, T, D)).astype(np.float32))
+    k = oracle.f32_to_bf16(rng.normal(0, 1, (1, Hkv, T, D)).astype(np.float32))
+    v = oracle.f32_to_bf16(rng.normal(0, 1, (1, Hkv, T, D)).astype(np.float32))
+    oracle.attn(q[:, :1, :256], k[:, :, :256], v[:, :, :256], D ** -0.5, oracle.BF16, oracle.MASK_CAUSAL,
+                threads=threads)  # warm-up
+    t0 = time.perf_counter()
+    for c in range(T // W):
+        oracle.attn(q[:, :, c * W:(c + 1) * W], k[:, :, :(c + 1) * W], v[:, :, :(c + 1) * W], D ** -0.5, oracle.BF16,
+                    oracle.MASK_CAUSAL, threads=threads)
+    t = time.perf_counter() - t0
+    flop = 4.0 * D * Hq * (T * (T + 1) / 2)
+    return {"value": round(flop / t / 1e12, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port", "lscpu": topo,
+            "sample": "configs[2] wide cut, 8 of the 16 query heads (one KV head), all four 2048-row chunks as four "
+                      "oracle calls, one pass after a warm-up call", "seconds": round(t, 3)}
+
+
+def cpu_gdn_baseline(reps=3):
+    """configs[3] through the CPU oracle (CpuGdn restated, scalar gate, no mask, as cpu_kernels.py:55-56 calls it):
+    the 8192-token prefill at B = 1 (one pass; TFLOP/s of the recurrence's 7 T Hv Dk Dv) and one decode step at
+    B = 16 (state GB/s, median of `reps`), one thread a physical core."""
+    import numpy as np
+
+    import oracle
+    threads, topo = cpu_topology()
+    rng = np.random.default_rng(4)
+    Hk, Hv, D = 16, 32, 128
+
+    def inputs(B, T):
+        def unit(*s):
+            x = rng.normal(0, 1, s).astype(np.float32)
+            return oracle.f32_to_bf16(x / np.linalg.norm(x, axis=-1, keepdims=True))
+        q, k = unit(B, T, Hk, D), unit(B, T, Hk, D)
+        v = oracle.f32_to_bf16(rng.normal(0, 1, (B, T, Hv, D)).astype(np.float32))
+        beta = oracle.f32_to_bf16((1 / (1 + np.exp(-rng.normal(0, 1, (B, T, Hv))))).astype(np.float32))
+        g = np.exp(-np.log1p(np.exp(rng.normal(0, 1, (B, T, Hv))))).astype(np.float32)
+        return q, k, v, g, beta, np.zeros((B, Hv, D, D), np.float32)
+
+    T = 8192
+    q, k, v, g, beta, s0 = inputs(1, T)
+    oracle.gdn(q[:, :64], k[:, :64], v[:, :64], g[:, :64], beta[:, :64], s0, oracle.BF16, g_dt=oracle.F32,
+               b_dt=oracle.BF16, threads=threads)  # warm-up
+    t0 = time.perf_counter()
+    oracle.gdn(q, k, v, g, beta, s0, oracle.BF16, g_dt=oracle.F32, b_dt=oracle.BF16, threads=threads)
+    tp = time.perf_counter() - t0
+    flop = 7.0 * T * Hv * D * D
+    q, k, v, g, beta, s0 = inputs(16, 1)
+    times = []
+    for r in range(reps + 1):
+        t0 = time.perf_counter()
+        oracle.gdn(q, k, v, g, beta, s0, oracle.BF16, g_dt=oracle.F32, b_dt=oracle.BF16, threads=threads)
+        if r:
+            times.append(time.perf_counter() - t0)
+    td = sorted(times)[len(times) // 2]
+    state_bytes = 16 * Hv * D * D * 4 * 2
+    pre = {"value": round(flop / tp / 1e12, 5), "unit": "TFLOP/s (recurrence FLOP)", "cores": threads, "kind": "port",
+           "lscpu": topo, "sample": "configs[3] prefill, B=1, all 8192 tokens, one pass after a 64-token warm-up",
+           "seconds": round(tp, 3), "ms_per_step": round(tp * 1e3, 2)}
+    dec = {"value": round(state_bytes / td / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port", "lscpu": topo,
+           "sample": f"configs[3] decode step, B=16, median of {reps} after one warm-up", "seconds": round(td, 4)}
+    return pre, dec
 
 
 def run_reference(args):
@@ -654,7 +778,7 @@ def run_reference(args):
         seqs.append((oracle.f32_to_bf16(rng.normal(0, 1, (1, Hq, 1, D)).astype(np.float32)),
                      oracle.f32_to_bf16(rng.normal(0, 1, (1, Hkv, n, D)).astype(np.float32)),
                      oracle.f32_to_bf16(rng.normal(0, 1, (1, Hkv, n, D)).astype(np.float32)), n))
-    threads = oracle.default_threads()
+    threads, topo = cpu_topology()
 
     def step():
         for q, k, v, n in seqs:
@@ -672,9 +796,8 @@ def run_reference(args):
                       "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
                       "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
                       "data": "synthetic (seeded N(0,1), config shapes)",
-                      "config": {"workload": "configs[1] GQA decode: B=16, 32q/4kv x 128, bf16 KV, lengths "
-                                             "U[1024,8192]", "global_batch": 16, "parallelism": "cpu"},
-                      "cpu_baseline": {"value": val, "unit": "GB/s", "cores": threads, "kind": "port",
+                      "config": {"workload": DECODE_WORKLOAD, "global_batch": 16, "parallelism": "cpu"},
+                      "cpu_baseline": {"value": val, "unit": "GB/s", "cores": threads, "kind": "port", "lscpu": topo,
                                        "sample": "the full configs[1] batch a step, one oracle call per sequence"},
                       "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
 
