@@ -205,14 +205,16 @@ int lb2_gdn_chunked(const void* q, const void* k, int qdt, const void* v, int vd
  * Gathers the rows the reference's QSA decode attends to: the sorted picked blocks tb (int32 [nsel], block size cr)
  * and the sequence's trailing partial block; row r < nsel*cr is position tb[r/cr]*cr + r%cr, row r >= nsel*cr is
  * position own0 + r - nsel*cr with own0 = n/cr*cr, m = nsel*cr + n - own0 rows. kg / vg [Hk, m, D] contiguous.
- * k / v: [Hk, n, D] views (one sequence) with strides k_st / v_st (head, position, dim).
+ * k / v: [Hk, n, D] views (one sequence) with strides k_st / v_st (head, position, dim). A picked block reaching
+ * outside [0, n) is not read: its rows come back as zeros and lb2_status reports LB2_EINVAL.
  * Replaces: stream_fast._qsa_gather (stream_fast.py:6448-6491); attn_cuda then runs the decode over kg / vg
  * (stream_fast.py:6411-6441), here lb2_attn_decode. */
 int lb2_kv_gather_picks(const void* k, const int64_t* k_st, const void* v, const int64_t* v_st, const int32_t* tb,
                         int nsel, int cr, int n, void* kg, void* vg, int Hk, int D, int dtype, void* stream);
 
 /* The paged home: positions in chunks of 2^logc, each chunk [K/V][Hk][2^logc][D] contiguous, chunk addresses in a
- * uint64 device table (device memory or pinned, GPU-mapped host memory). put writes s new positions pos0.. of
+ * uint64 device table (device memory or pinned, GPU-mapped host memory; each chunk 16-byte aligned, 2^logc a
+ * multiple of cr). put writes s new positions pos0.. of
  * k / v [Hk, s, D] (strides) into the home; gather reads the picked rows (as lb2_kv_gather_picks) from it, with
  * cache-bypassing loads. Replaces: kv_host's layout and its put / gather kernels (kv_host.py:17-18, :36-41,
  * :64-291, decode :612-648); the VRAM LRU in front of it follows. */

@@ -2,8 +2,11 @@
 // every kernel header and implements the entry points declared in include/larder_b200.h.
 #include <algorithm>
 #include <cstring>
+#include <initializer_list>
 #include <mutex>
 #include <string>
+#include <type_traits>
+#include <utility>
 
 #include "common.cuh"
 #include "attn_decode.cuh"
@@ -15,7 +18,7 @@
 #include "attn_glue.cuh"
 #include "qsa_select.cuh"
 #include "peer_xch.cuh"
-#include "kv_gather.cuh"
+#include "kv_runs.cuh"
 #include "gdn_glue.cuh"
 
 namespace lb2 {
@@ -884,29 +887,69 @@ int lb2_gdn_recurrent(const void* q, const void* k, int qdt, const void* v, int 
 
 // ------------------------------------------------------------------------------------------------ gathers
 
+}  // extern "C"
+
+namespace {
+
+// How a run-gather moves data: 16-byte units when every base is 16-byte aligned, rows are contiguous and every
+// stride is a whole number of units; else one element a unit (raw bits).
+struct RunUnits {
+  bool vec;
+  int esz, per;  // element bytes; elements a unit
+};
+
+// views: (strides, count) pairs, each the element strides of one view with the dim stride last.
+RunUnits run_units(int dtype, int D, std::initializer_list<const void*> bases,
+                   std::initializer_list<std::pair<const int64_t*, int>> views) {
+  RunUnits u{true, dtype == LB2_F32 ? 4 : 2, 0};
+  const int per = 16 / u.esz;
+  if ((int64_t(D) * u.esz) % 16) u.vec = false;
+  for (const void* b : bases)
+    if (reinterpret_cast<uintptr_t>(b) & 15) u.vec = false;
+  for (const auto& v : views) {
+    const int64_t* st = v.first;
+    if (st[v.second - 1] != 1) u.vec = false;
+    for (int i = 0; i + 1 < v.second; ++i)
+      if (st[i] % per) u.vec = false;
+  }
+  u.per = u.vec ? per : 1;
+  return u;
+}
+
+template <typename U>
+kvr::Rows<U> rows_of(const void* base, int64_t hs, int64_t rs, int64_t ds, int per) {
+  return kvr::Rows<U>{static_cast<const U*>(base), hs / per, rs / per, per > 1 ? 1 : ds};
+}
+
+// Calls f with a value of the unit type: uint4 for 16-byte units, else the element's raw-bits type.
+template <typename F>
+int with_units(const RunUnits& u, F&& f) {
+  if (u.vec) return f(uint4{});
+  if (u.esz == 4) return f(0u);
+  return f(static_cast<unsigned short>(0));
+}
+
+}  // namespace
+
+extern "C" {
+
 int lb2_kv_gather_picks(const void* k, const int64_t* k_st, const void* v, const int64_t* v_st, const int32_t* tb,
                         int nsel, int cr, int n, void* kg, void* vg, int Hk, int D, int dtype, void* stream) {
   LB2_CHECK_ARG(nsel >= 0 && cr > 0 && n >= 0 && Hk > 0 && D > 0, "kv_gather_picks: shape");
   LB2_CHECK_ARG(dtype >= LB2_F32 && dtype <= LB2_F16, "kv_gather_picks: dtype");
   const int m = nsel * cr + n - n / cr * cr;
   if (m == 0) return LB2_OK;
-  dim3 grid(unsigned((int64_t(m) * 32 + 255) / 256), unsigned(Hk), 2);
+  const RunUnits ru = run_units(dtype, D, {k, v, kg, vg}, {{k_st, 3}, {v_st, 3}});
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == LB2_BF16)
-    kvg::gather_picks_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(k), k_st[0], k_st[1], k_st[2], static_cast<const __nv_bfloat16*>(v),
-        v_st[0], v_st[1], v_st[2], tb, nsel, cr, n, static_cast<__nv_bfloat16*>(kg), static_cast<__nv_bfloat16*>(vg),
-        Hk, D);
-  else if (dtype == LB2_F16)
-    kvg::gather_picks_kernel<__half><<<grid, 256, 0, st>>>(
-        static_cast<const __half*>(k), k_st[0], k_st[1], k_st[2], static_cast<const __half*>(v), v_st[0], v_st[1],
-        v_st[2], tb, nsel, cr, n, static_cast<__half*>(kg), static_cast<__half*>(vg), Hk, D);
-  else
-    kvg::gather_picks_kernel<float><<<grid, 256, 0, st>>>(
-        static_cast<const float*>(k), k_st[0], k_st[1], k_st[2], static_cast<const float*>(v), v_st[0], v_st[1],
-        v_st[2], tb, nsel, cr, n, static_cast<float*>(kg), static_cast<float*>(vg), Hk, D);
-  LB2_CUDA(cudaGetLastError());
-  return LB2_OK;
+  const dim3 grid(unsigned(nsel + 1), 2);
+  return with_units(ru, [&](auto unit) {
+    using U = decltype(unit);
+    kvr::view_runs_kernel<U><<<grid, kvr::RUN_THREADS, 0, st>>>(
+        rows_of<U>(k, k_st[0], k_st[1], k_st[2], ru.per), rows_of<U>(v, v_st[0], v_st[1], v_st[2], ru.per), tb, nsel,
+        cr, n, static_cast<U*>(kg), static_cast<U*>(vg), Hk, D / ru.per);
+    LB2_CUDA(cudaGetLastError());
+    return LB2_OK;
+  });
 }
 
 int lb2_kvh_put(const uint64_t* table, const void* k, const int64_t* k_st, const void* v, const int64_t* v_st,
@@ -914,55 +957,47 @@ int lb2_kvh_put(const uint64_t* table, const void* k, const int64_t* k_st, const
   LB2_CHECK_ARG(s >= 0 && pos0 >= 0 && Hk > 0 && D > 0 && logc > 0 && logc < 31, "kvh_put: shape");
   LB2_CHECK_ARG(dtype >= LB2_F32 && dtype <= LB2_F16, "kvh_put: dtype");
   if (s == 0) return LB2_OK;
-  dim3 grid(unsigned((int64_t(s) * 32 + 255) / 256), unsigned(Hk), 2);
+  const RunUnits ru = run_units(dtype, D, {k, v}, {{k_st, 3}, {v_st, 3}});
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == LB2_BF16)
-    kvg::home_put_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(table, static_cast<const __nv_bfloat16*>(k), k_st[0],
-                                                              k_st[1], k_st[2], static_cast<const __nv_bfloat16*>(v),
-                                                              v_st[0], v_st[1], v_st[2], pos0, s, Hk, D, logc);
-  else if (dtype == LB2_F16)
-    kvg::home_put_kernel<__half><<<grid, 256, 0, st>>>(table, static_cast<const __half*>(k), k_st[0], k_st[1],
-                                                       k_st[2], static_cast<const __half*>(v), v_st[0], v_st[1],
-                                                       v_st[2], pos0, s, Hk, D, logc);
-  else
-    kvg::home_put_kernel<float><<<grid, 256, 0, st>>>(table, static_cast<const float*>(k), k_st[0], k_st[1], k_st[2],
-                                                      static_cast<const float*>(v), v_st[0], v_st[1], v_st[2], pos0, s,
-                                                      Hk, D, logc);
-  LB2_CUDA(cudaGetLastError());
-  return LB2_OK;
+  const dim3 grid(unsigned((s + 31) / 32), 2);
+  return with_units(ru, [&](auto unit) {
+    using U = decltype(unit);
+    kvr::home_put_kernel<U><<<grid, kvr::RUN_THREADS, 0, st>>>(
+        table, rows_of<U>(k, k_st[0], k_st[1], k_st[2], ru.per), rows_of<U>(v, v_st[0], v_st[1], v_st[2], ru.per),
+        pos0, s, Hk, D / ru.per, logc);
+    LB2_CUDA(cudaGetLastError());
+    return LB2_OK;
+  });
 }
 
 int lb2_kvh_gather(const uint64_t* table, const int32_t* tb, int nsel, int cr, int n, void* kg, void* vg, int Hk,
                    int D, int dtype, int logc, void* stream) {
   LB2_CHECK_ARG(nsel >= 0 && cr > 0 && n >= 0 && Hk > 0 && D > 0 && logc > 0 && logc < 31, "kvh_gather: shape");
   LB2_CHECK_ARG(dtype >= LB2_F32 && dtype <= LB2_F16, "kvh_gather: dtype");
+  LB2_CHECK_ARG((int64_t(1) << logc) % cr == 0, "kvh_gather: the block size must divide the chunk size");
   const int m = nsel * cr + n - n / cr * cr;
   if (m == 0) return LB2_OK;
-  dim3 grid(unsigned((int64_t(m) * 32 + 255) / 256), unsigned(Hk), 2);
+  const RunUnits ru = run_units(dtype, D, {kg, vg}, {});
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == LB2_BF16)
-    kvg::home_gather_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(table, tb, nsel, cr, n,
-                                                                 static_cast<__nv_bfloat16*>(kg),
-                                                                 static_cast<__nv_bfloat16*>(vg), Hk, D, logc);
-  else if (dtype == LB2_F16)
-    kvg::home_gather_kernel<__half><<<grid, 256, 0, st>>>(table, tb, nsel, cr, n, static_cast<__half*>(kg),
-                                                          static_cast<__half*>(vg), Hk, D, logc);
-  else
-    kvg::home_gather_kernel<float><<<grid, 256, 0, st>>>(table, tb, nsel, cr, n, static_cast<float*>(kg),
-                                                         static_cast<float*>(vg), Hk, D, logc);
-  LB2_CUDA(cudaGetLastError());
-  return LB2_OK;
+  const dim3 grid(unsigned(nsel + 1), 2);
+  return with_units(ru, [&](auto unit) {
+    using U = decltype(unit);
+    kvr::home_runs_kernel<U><<<grid, kvr::RUN_THREADS, 0, st>>>(table, tb, nsel, cr, n, static_cast<U*>(kg),
+                                                                static_cast<U*>(vg), Hk, D / ru.per, logc);
+    LB2_CUDA(cudaGetLastError());
+    return LB2_OK;
+  });
 }
 
 int lb2_kvh_lru_plan(const int32_t* tb, int nsel, int32_t* slot_of, int max_blocks, int32_t* block_of, int32_t* stamp,
                      int32_t* ref, int32_t* meta, int ns, int32_t* sl, void* stream) {
-  LB2_CHECK_ARG(nsel >= 1 && nsel <= kvg::LRU_MAX_NSEL, "kvh_lru_plan: 1 to 1024 picks a token");
+  LB2_CHECK_ARG(nsel >= 1 && nsel <= kvr::LRU_MAX_NSEL, "kvh_lru_plan: 1 to 1024 picks a token");
   const int nt = (nsel + 31) / 32 * 32;
   LB2_CHECK_ARG(ns >= nt, "kvh_lru_plan: the pool needs at least ceil32(nsel) slots");
   LB2_CHECK_ARG(max_blocks >= 1, "kvh_lru_plan: max_blocks");
   LB2_CHECK_ARG(tb && slot_of && block_of && stamp && ref && meta && sl, "kvh_lru_plan: null pointer");
-  kvg::lru_plan_kernel<<<1, nt, 0, static_cast<cudaStream_t>(stream)>>>(tb, nsel, slot_of, max_blocks, block_of,
-                                                                         stamp, ref, meta, ns, sl);
+  kvr::lru_plan_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(tb, nsel, slot_of, max_blocks, block_of, stamp,
+                                                                        ref, meta, ns, sl);
   LB2_CUDA(cudaGetLastError());
   return LB2_OK;
 }
@@ -973,29 +1008,24 @@ int lb2_kvh_lru_gather(const uint64_t* table, void* pool, int ns, const int32_t*
   LB2_CHECK_ARG(nsel >= 0 && cr > 0 && n >= 1 && ns >= 1 && Hk > 0 && D > 0 && logc > 0 && logc < 31,
                 "kvh_lru_gather: shape");
   LB2_CHECK_ARG(dtype >= LB2_F32 && dtype <= LB2_F16, "kvh_lru_gather: dtype");
-  const int m = nsel * cr + n - n / cr * cr;
-  dim3 grid(unsigned((int64_t(m + 1) * 32 + 255) / 256), unsigned(Hk), 2);
+  LB2_CHECK_ARG((int64_t(1) << logc) % cr == 0, "kvh_lru_gather: the block size must divide the chunk size");
+  const RunUnits ru = run_units(dtype, D, {pool, kn, vn, kg, vg}, {{kn_st, 2}, {vn_st, 2}});
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-#define LB2_LRU_GATHER(T)                                                                                            \
-  kvg::lru_gather_kernel<T><<<grid, 256, 0, st>>>(table, static_cast<T*>(pool), ns, tb, sl, nsel, cr, n,             \
-                                                  static_cast<const T*>(kn), kn_st[0], kn_st[1],                     \
-                                                  static_cast<const T*>(vn), vn_st[0], vn_st[1], static_cast<T*>(kg), \
-                                                  static_cast<T*>(vg), Hk, D, logc)
-  if (dtype == LB2_BF16)
-    LB2_LRU_GATHER(__nv_bfloat16);
-  else if (dtype == LB2_F16)
-    LB2_LRU_GATHER(__half);
-  else
-    LB2_LRU_GATHER(float);
-#undef LB2_LRU_GATHER
-  LB2_CUDA(cudaGetLastError());
-  return LB2_OK;
+  const dim3 grid(unsigned(nsel + 1), 2);
+  return with_units(ru, [&](auto unit) {
+    using U = decltype(unit);
+    kvr::lru_runs_kernel<U><<<grid, kvr::RUN_THREADS, 0, st>>>(
+        table, static_cast<U*>(pool), ns, tb, sl, nsel, cr, n, rows_of<U>(kn, kn_st[0], 0, kn_st[1], ru.per),
+        rows_of<U>(vn, vn_st[0], 0, vn_st[1], ru.per), static_cast<U*>(kg), static_cast<U*>(vg), Hk, D / ru.per,
+        logc);
+    LB2_CUDA(cudaGetLastError());
+    return LB2_OK;
+  });
 }
 
 int lb2_kvh_lru_inval(int32_t* slot_of, int32_t* block_of, int32_t* ref, int ns, int lim, void* stream) {
   LB2_CHECK_ARG(ns >= 1 && lim >= 0, "kvh_lru_inval: shape");
-  kvg::lru_inval_kernel<<<unsigned((ns + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(slot_of, block_of,
-                                                                                                   ref, ns, lim);
+  kvr::lru_trim_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(slot_of, block_of, ref, ns, lim);
   LB2_CUDA(cudaGetLastError());
   return LB2_OK;
 }
@@ -1008,16 +1038,29 @@ int lb2_gdn_step_glue(const void* conv, const void* a, const void* b, const floa
   LB2_CHECK_ARG(NR >= 0 && Hk > 0 && Hv > 0 && Dv > 0 && Hv % Hk == 0, "gdn_step_glue: shape");
   LB2_CHECK_ARG(Dk == 64 || Dk == 128, "gdn_step_glue: Dk must be 64 or 128");
   LB2_CHECK_ARG(dtype == LB2_BF16 || dtype == LB2_F16, "gdn_step_glue: dtype must be bf16 or f16");
-  glue::StepParams p{conv, a, b, A_log, dt_bias, state_in, state_out, y, NR, Hk, Hv, Dv, sq, sk, eps};
-  constexpr int RB = 16;
-  dim3 grid(unsigned((Dv + RB - 1) / RB), unsigned(Hv));
+  gdnrec::GlueParams p{conv, a, b, A_log, dt_bias, state_in, state_out, y, NR, Hk, Hv, Dv, sq, sk, eps};
+  if (NR == 0) return LB2_OK;
+  const int R = Dv % 8 == 0 ? 8 : Dv % 4 == 0 ? 4 : Dv % 2 == 0 ? 2 : 1;  // value rows a warp
+  const dim3 grid(unsigned((Dv / R + 3) / 4), unsigned(Hv));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto launch = [&](auto t_tag, auto npt_tag) {
+    using T = decltype(t_tag);
+    constexpr int NPT = decltype(npt_tag)::value;
+    switch (R) {
+      case 8: gdnrec::glue_step_kernel<T, NPT, 8><<<grid, 128, 0, st>>>(p); break;
+      case 4: gdnrec::glue_step_kernel<T, NPT, 4><<<grid, 128, 0, st>>>(p); break;
+      case 2: gdnrec::glue_step_kernel<T, NPT, 2><<<grid, 128, 0, st>>>(p); break;
+      default: gdnrec::glue_step_kernel<T, NPT, 1><<<grid, 128, 0, st>>>(p); break;
+    }
+  };
+  using N4 = std::integral_constant<int, 4>;
+  using N2 = std::integral_constant<int, 2>;
   if (dtype == LB2_BF16) {
-    if (Dk == 128) glue::step_glue_kernel<__nv_bfloat16, 4, RB><<<grid, RB * 32, 0, st>>>(p);
-    else glue::step_glue_kernel<__nv_bfloat16, 2, RB><<<grid, RB * 32, 0, st>>>(p);
+    if (Dk == 128) launch(__nv_bfloat16{}, N4{});
+    else launch(__nv_bfloat16{}, N2{});
   } else {
-    if (Dk == 128) glue::step_glue_kernel<__half, 4, RB><<<grid, RB * 32, 0, st>>>(p);
-    else glue::step_glue_kernel<__half, 2, RB><<<grid, RB * 32, 0, st>>>(p);
+    if (Dk == 128) launch(__half{}, N4{});
+    else launch(__half{}, N2{});
   }
   LB2_CUDA(cudaGetLastError());
   return LB2_OK;
