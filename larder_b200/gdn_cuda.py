@@ -7,6 +7,8 @@ multiplied by g, gdn_cuda.py:43). Long passes with a scalar gate and no mask run
 (lb2_gdn_chunked, chunks of 64 positions); everything else -- decode steps, short verify passes, vector gates,
 masks -- runs the position-by-position kernel (lb2_gdn_recurrent). Both are CUDA; there is no ops-loop fallback.
 
+install_glue(rows) routes a GatedDeltaNet layer's decode rows through step_glue + norm_gate (gdn_cuda.py:271-315).
+
 gated_delta_update keeps mlx_lm 0.32's parameter list (gdn_cuda.py:318-319) and its gating: beta = sigmoid(b)
 (doubled with allow_neg_eigval), g = compute_g(A_log, a, dt_bias) = exp(-exp(A_log) * softplus(a + dt_bias))
 (the expression gdn_cuda.py:146-149 spells out), a zero state when none is given.
@@ -69,6 +71,53 @@ def norm_gate(x, z, weight, eps):
     if z.shape != x.shape or weight.dtype != x.dtype:
         raise ValueError("norm_gate: z must match x and weight x's dtype")
     return ops.gdn_norm_gate(x, z, weight, eps)
+
+
+def install_glue(rows=1, cls=None):
+    """Route a GatedDeltaNet layer's decode rows -- and passes of up to `rows` positions -- through step_glue and
+    norm_gate, every other call through the layer's own __call__ (gdn_cuda.py:271-315). `cls` is the layer class
+    (default: mlx_lm.models.qwen3_5.GatedDeltaNet when that module is loaded); its instances carry qwen3_5's
+    attributes (in_proj_qkv, in_proj_z, in_proj_a, in_proj_b, conv1d taking channels-last [B, L, C] and returning the
+    conv output before silu, A_log, dt_bias, norm with weight / eps, out_proj, num_k_heads, head_k_dim, num_v_heads,
+    head_v_dim, conv_kernel_size, conv_dim) and the cache holds [conv_state, recurrent state] with advance(S). The
+    fused path is taken for B = 1, S <= rows, no mask, a cache whose state exists, bf16 activations and norm weight,
+    Dk in {64, 128} and Hv a multiple of Hk; the rest falls to the layer's own lines, as in the reference."""
+    if cls is None:
+        mod = sys.modules.get("mlx_lm.models.qwen3_5")
+        if mod is None:
+            raise ValueError("install_glue: give the GatedDeltaNet class (mlx_lm.models.qwen3_5 is not loaded)")
+        cls = mod.GatedDeltaNet
+    if getattr(cls, "_gdn_glue", False):
+        return cls
+    orig = cls.__call__
+
+    def __call__(self, inputs, mask=None, cache=None):
+        B, S, _ = inputs.shape
+        if not (B == 1 and S <= rows and mask is None and cache is not None and cache[1] is not None
+                and getattr(cache, "lengths", None) is None and not getattr(self, "training", False)
+                and inputs.dtype == torch.bfloat16 and inputs.is_cuda and self.head_k_dim in (64, 128)
+                and self.num_v_heads % self.num_k_heads == 0 and self.norm.weight.dtype == torch.bfloat16):
+            return orig(self, inputs, mask, cache)
+        qkv = self.in_proj_qkv(inputs)
+        z = self.in_proj_z(inputs).reshape(B, S, self.num_v_heads, self.head_v_dim)
+        b = self.in_proj_b(inputs)
+        a = self.in_proj_a(inputs)
+        conv_state = cache[0] if cache[0] is not None else torch.zeros(
+            (B, self.conv_kernel_size - 1, self.conv_dim), dtype=inputs.dtype, device=inputs.device)
+        conv_input = torch.cat([conv_state, qkv], dim=1)
+        cache[0] = conv_input[:, -(self.conv_kernel_size - 1):, :].contiguous()
+        conv = self.conv1d(conv_input)
+        out, state = step_glue(conv, a, b, self.A_log, self.dt_bias, cache[1], self.num_k_heads, self.head_k_dim,
+                               self.num_v_heads, self.head_v_dim)
+        cache[1] = state
+        cache.advance(S)
+        out = norm_gate(out, z, self.norm.weight, self.norm.eps)
+        return self.out_proj(out.reshape(B, S, -1))
+
+    cls.__call__ = __call__
+    cls._gdn_glue = True
+    cls._gdn_glue_orig = orig
+    return cls
 
 
 def install(modules=None):
