@@ -23,6 +23,9 @@
 //        stored already rounded to TF32 by prep.
 #pragma once
 
+#include <type_traits>
+
+#include "attn_prefill.cuh"
 #include "common.cuh"
 
 namespace lb2 {
@@ -32,21 +35,29 @@ constexpr int C = 64;
 constexpr int DK = 128;
 constexpr int DV = 128;
 constexpr int DVB = 32;   // value rows a scan CTA owns
-constexpr int KP = 136;   // bf16 row stride of K / Q tiles (conflict-free ldmatrix and scalar reads)
-constexpr int AP = 68;    // fp32 row stride of A / T / M tiles
-constexpr int RP = 136;   // fp32 row stride of 128-wide fp32 tiles (B operands)
-constexpr int WP = 132;   // fp32 row stride of W / S tiles (A operands and S^T reads)
-constexpr int UP = 36;    // fp32 row stride of 32-wide U tiles
-// Workspace of one (batch, head, chunk) in floats, laid out as the scan's shared-memory tiles (padded rows included)
-// so that a scan CTA fetches a chunk with two bulk copies: W [C][WP] and M [C][AP] (TF32 values) and gamma, Gam
-// [2 C] as one block, then U' as DV / DVB slices [C][UP] of 32 value columns each.
-constexpr int WS_W = 0;
-constexpr int WS_M = WS_W + C * WP;
-constexpr int WS_G = WS_M + C * AP;
-constexpr int WS_U = WS_G + 2 * C;
-constexpr int UNIT = WS_U + (DV / DVB) * C * UP;
-constexpr int WMG_BYTES = WS_U * 4;  // W, M and the gates: one copy
-static_assert(WS_M % 4 == 0 && WS_G % 4 == 0 && WS_U % 4 == 0 && UNIT % 4 == 0, "16-byte aligned workspace tiles");
+constexpr int KP = 136;   // bf16 row stride of prep's K / Q tiles (conflict-free ldmatrix and scalar reads)
+constexpr int AP = 68;    // fp32 row stride of prep's A / T tiles
+constexpr int UP = 36;    // fp32 row stride of the U' slices (32 value columns)
+// Workspace of one (batch, head, chunk), in bytes, laid out as the scan's shared-memory operands so that a chunk
+// arrives by four bulk copies. W and M are stored as 16-bit hi / lo pairs (hi = round(x), lo = round(x - hi): their
+// sum carries about 16 mantissa bits) in the tensor cores' 128-byte-swizzled K-major form: row r of a 64-column
+// block at r * 128 bytes, its 16-byte piece j at piece j ^ (r % 8).
+//   W_hi, W_lo [64 positions][128 keys]: two column blocks of 8 KB each;  M_hi, M_lo [64][64]: 8 KB each;
+//   gamma, Gam [64] fp32;  U' as DV / DVB slices [64][UP] fp32 of 32 value columns each.
+constexpr int WS_WHI = 0;
+constexpr int WS_WLO = WS_WHI + 2 * C * 128;
+constexpr int WS_MHI = WS_WLO + 2 * C * 128;
+constexpr int WS_MLO = WS_MHI + C * 128;
+constexpr int WS_G = WS_MLO + C * 128;
+constexpr int WS_U = WS_G + 2 * C * 4;
+constexpr int USLICE = C * UP * 4;
+constexpr int UNIT_BYTES = WS_U + (DV / DVB) * USLICE;
+static_assert(WS_G % 16 == 0 && WS_U % 16 == 0 && UNIT_BYTES % 16 == 0, "16-byte aligned workspace pieces");
+
+// Byte offset of 16-bit element (row, col) of a 64-column block in the 128-byte swizzle (col < 64).
+__host__ __device__ __forceinline__ int sw128(int row, int col) {
+  return row * 128 + ((((col >> 3) ^ row) & 7) << 4) + ((col & 7) << 1);
+}
 
 struct Params {
   const void* q;
@@ -147,9 +158,17 @@ __device__ __forceinline__ void mma3_tile(const float* Lp, int ldl, const float*
   }
 }
 
-// Workspace tiles of one (batch, head, chunk).
-__device__ __forceinline__ float* unit_ptr(const Params& p, int b, int h, int c) {
-  return p.ws + ((int64_t(b) * p.Hv + h) * p.nchunks + c) * UNIT;
+// Workspace of one (batch, head, chunk).
+__device__ __forceinline__ uint8_t* unit_ptr(const Params& p, int b, int h, int c) {
+  return reinterpret_cast<uint8_t*>(p.ws) + ((int64_t(b) * p.Hv + h) * p.nchunks + c) * int64_t(UNIT_BYTES);
+}
+
+// The 16-bit hi / lo split of two adjacent values, stored at the swizzled offset of the first in `hi` and `lo`.
+template <typename T>
+__device__ __forceinline__ void store_split2(uint8_t* hi, uint8_t* lo, int off, float x0, float x1) {
+  const float h0 = to_f<T>(from_f<T>(x0)), h1 = to_f<T>(from_f<T>(x1));
+  *reinterpret_cast<uint32_t*>(hi + off) = pack2<T>(h0, h1);
+  *reinterpret_cast<uint32_t*>(lo + off) = pack2<T>(x0 - h0, x1 - h1);
 }
 
 // ------------------------------------------------------------------------------------------------ prep
@@ -250,7 +269,8 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
         mma_16816<T>(qk[2 * np + 1], aq, bk[2], bk[3]);
       }
     }
-    float* Mg = unit_ptr(p, b, h, c) + WS_M;
+    uint8_t* Mhi = unit_ptr(p, b, h, c) + WS_MHI;
+    uint8_t* Mlo = unit_ptr(p, b, h, c) + WS_MLO;
 #pragma unroll
     for (int n = 0; n < 8; ++n)
 #pragma unroll
@@ -260,9 +280,7 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
         const float d0 = j <= t ? __expf(gam[t] - gam[j]) : 0.f, d1 = j + 1 <= t ? __expf(gam[t] - gam[j + 1]) : 0.f;
         *reinterpret_cast<float2*>(&Af[t * AP + j]) =
             make_float2(j < t ? bet[t] * d0 * kk[n][2 * hh] : 0.f, j + 1 < t ? bet[t] * d1 * kk[n][2 * hh + 1] : 0.f);
-        // an MMA operand of the scan: rounded once here
-        *reinterpret_cast<float2*>(&Mg[t * AP + j]) = make_float2(__uint_as_float(tf32(d0 * qk[n][2 * hh])),
-                                                                  __uint_as_float(tf32(d1 * qk[n][2 * hh + 1])));
+        store_split2<T>(Mhi, Mlo, sw128(t, j), d0 * qk[n][2 * hh], d1 * qk[n][2 * hh + 1]);  // a scan operand
       }
   }
   __syncthreads();
@@ -341,8 +359,7 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
   // warp would do four times the first's work). The column factors (beta, then Gam on top) are folded into T first,
   // warp w scaling rows 16 w .., so that the B fragments are the 16-bit tiles' exact TF32 values.
   {
-    float* Wg = unit_ptr(p, b, h, c) + WS_W;
-    float* Ug = unit_ptr(p, b, h, c) + WS_U;
+    uint8_t* unit = unit_ptr(p, b, h, c);
     const int r = lane >> 2, cq = lane & 3, nw = warp * 32;
 #pragma unroll 1
     for (int which = 1; which >= 0; --which) {
@@ -373,18 +390,19 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
                      tf32_of(R[(k0 + cq + 4) * KP + n0 + r]));
           }
         }
-        if (!which)  // W is an MMA operand of the scan: stored rounded to TF32; U' stays fp32
 #pragma unroll
-          for (int n = 0; n < 4; ++n)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc[n][e] = __uint_as_float(tf32(acc[n][e]));
-#pragma unroll
-        for (int n = 0; n < 4; ++n) {  // W rows of stride WP; U' in slices of DVB columns, rows of stride UP
+        for (int n = 0; n < 4; ++n) {  // U' fp32 in slices of DVB columns (rows of stride UP); W as hi / lo pairs
           const int col = nw + n * 8 + 2 * cq;
-          float* g0 = which ? Ug + ((col / DVB) * C + m0 + r) * UP + col % DVB : Wg + (m0 + r) * WP + col;
-          float* g1 = g0 + 8 * (which ? UP : WP);
-          *reinterpret_cast<float2*>(g0) = make_float2(acc[n][0], acc[n][1]);
-          *reinterpret_cast<float2*>(g1) = make_float2(acc[n][2], acc[n][3]);
+          if (which) {
+            float* g0 = reinterpret_cast<float*>(unit + WS_U) + ((col / DVB) * C + m0 + r) * UP + col % DVB;
+            *reinterpret_cast<float2*>(g0) = make_float2(acc[n][0], acc[n][1]);
+            *reinterpret_cast<float2*>(g0 + 8 * UP) = make_float2(acc[n][2], acc[n][3]);
+          } else {
+            uint8_t* hi = unit + WS_WHI + (col >> 6) * (C * 128);
+            uint8_t* lo = unit + WS_WLO + (col >> 6) * (C * 128);
+            store_split2<T>(hi, lo, sw128(m0 + r, col & 63), acc[n][0], acc[n][1]);
+            store_split2<T>(hi, lo, sw128(m0 + r + 8, col & 63), acc[n][2], acc[n][3]);
+          }
         }
       }
       __syncthreads();  // every warp has read T before it is scaled again
@@ -392,314 +410,346 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
   }
   // 7. gamma and Gam for the scan
   if (tid < C) {
-    float* gg = unit_ptr(p, b, h, c) + WS_G;
+    float* gg = reinterpret_cast<float*>(unit_ptr(p, b, h, c) + WS_G);
     gg[tid] = gam[tid];
     gg[C + tid] = Gam[tid];
   }
 }
 
 // ------------------------------------------------------------------------------------------------ scan
+//
+// One CTA: value columns dv0 .. dv0 + 31 of one (batch, v-head), all chunks in order, every product on the tensor
+// cores (tcgen05.mma kind::f16, accumulators in TMEM). The state slice S [32 value rows x 128 keys] is kept in fp32
+// registers of the epilogue warps (thread k holds column k: S[0 .. 31][k]) and given to the MMAs as a 16-bit hi / lo
+// pair in shared memory. Per chunk:
+//   P1  D1 = [W_hi ; Q] (S_hi + S_lo)^T   (M = 128: rows 0-63 W, rows 64-127 Q; N = 32; K = 128)
+//       D4 = W_lo S_hi^T                   (rows 0-63 used)                 -> W S^T = D1[0:64] + D4[0:64]
+//   E-U U = U' - W S^T (warps 0-1, thread = position), Ud = diag(exp(gamma_C - gamma)) U, both as hi / lo pairs
+//   P2  D2 = K^T (Ud_hi + Ud_lo)           (M = 128 keys, A = the K tile as the TMA loads it, MN-major; K = 64)
+//   P3  D3 = M_hi (U_hi + U_lo) + M_lo U_hi (rows 64-127 used)
+//   E-S S <- Gam_C S + D2 (all four warps, thread = key)                    -> the next P1's operand
+//   E-Y Y = Gam (D1[64:128]) + D3[64:128] (warps 2-3, thread = position)    -> y
+// The chain from one chunk to the next is P1 -> E-U -> P2 -> E-S; P3 and E-Y run beside it (D1 / D3 / D4 are
+// double-buffered by chunk parity, so E-Y may lag a chunk). Chunk c's W, M, gates and U' slice arrive by bulk copies
+// and its Q and K tiles by tiled TMA, into one of two buffers, a chunk ahead.
+//
+// Rows past T in the last chunk: Q and K arrive as zeros and prep left W, U' zero there, so they add nothing; their
+// y is not stored.
 
-constexpr int SCAN_THREADS = 256;  // warps 0-3: U = U' - W S^T and the state update; warps 4-7: Q S^T and M U
-constexpr int UQ = 68;             // u32 row stride of the transposed U tiles [DVB][C] (conflict-free ldmatrix)
+constexpr int TC_THREADS = 192;  // warps 0-3 epilogue (TMEM lane quarters), warp 4 loads, warp 5 MMA
+constexpr int TC_TMEM_COLS = 256;
 
-struct ScanSmem {
-  // one prefetch buffer; W, M and G in the workspace's order (one bulk copy)
-  static constexpr int W = 0;                         // tf32 [C][WP]
-  static constexpr int M = W + (WS_M - WS_W) * 4;     // tf32 [C][AP]
-  static constexpr int G = W + (WS_G - WS_W) * 4;     // f32 [C] gamma, [C] Gam
-  static constexpr int U = W + (WS_U - WS_W) * 4;     // f32 [C][UP]   U' columns of this block
-  // Q and K tiles as the tiled TMA lands them: two boxes of [64 positions][64 columns] (128-byte rows, 128-byte
-  // swizzle: the 16-byte piece j of row r sits at piece j ^ (r % 8)), 1024-byte aligned
-  static constexpr int QK_TILE = 2 * C * 64 * 2;
-  static constexpr int Q = (U + C * UP * 4 + 1023) / 1024 * 1024;
-  static constexpr int K = Q + QK_TILE;
-  static constexpr int BUF = K + QK_TILE;
-  // persistent
-  static constexpr int ST = 2 * BUF;                  // tf32 [DVB][WP] the state slice, rounded for the MMAs
-  static constexpr int UB = ST + DVB * WP * 4;        // tf32 [DVB][UQ] this chunk's U, transposed
-  static constexpr int UD = UB + DVB * UQ * 4;        // tf32 [DVB][UQ] (diag(exp(gamma_C - gamma)) U)^T
-  static constexpr int BAR = UD + DVB * UQ * 4;       // 2 mbarriers: buffer b's copies landed
-  static constexpr int BYTES = BAR + 16 + 1024;  // (+ alignment of the dynamic shared memory base to 1024)
+struct TcSmem {
+  // one chunk buffer (two of them): the shared-memory images of the workspace pieces, each operand 1024-aligned
+  static constexpr int A1 = 0;                 // [W_hi kb0 | Q kb0 | W_hi kb1 | Q kb1], 8 KB each: P1's A
+  static constexpr int WLO = 4 * C * 128;      // W_lo kb0, kb1 (8 KB each); then M_hi, M_lo, gates in workspace order
+  static constexpr int MHI = WLO + 2 * C * 128;
+  static constexpr int MLO = MHI + C * 128;
+  static constexpr int G = MLO + C * 128;      // gamma [64], Gam [64] fp32
+  static constexpr int U = G + 2 * C * 4;      // U' slice [64][UP] fp32
+  static constexpr int K = (U + USLICE + 1023) / 1024 * 1024;  // K tile: two TMA boxes [64 positions][64 keys]
+  static constexpr int BUF = K + 2 * C * 128;
+  // persistent operands (16-bit, 128-byte swizzle, K-major)
+  static constexpr int SHI = 2 * BUF;          // S_hi [32 value rows][128 keys]: two 4 KB blocks
+  static constexpr int SLO = SHI + 2 * DVB * 128;
+  static constexpr int UDHI = SLO + 2 * DVB * 128;  // Ud_hi [32 value rows][64 positions]
+  static constexpr int UDLO = UDHI + DVB * 128;
+  static constexpr int UHI = UDLO + DVB * 128;
+  static constexpr int ULO = UHI + DVB * 128;
+  static constexpr int BAR = ULO + DVB * 128;  // mbarriers
+  static constexpr int NBAR = 16;
+  static constexpr int SLOT = BAR + NBAR * 8;  // TMEM base address; abort flag
+  static constexpr int BYTES = SLOT + 16 + 1024;  // (+ alignment of the dynamic shared memory base)
+  // bytes that land in a buffer a chunk
+  static constexpr uint32_t TX = 2 * C * 128 + (WS_U - WS_WLO) + USLICE + 4 * C * 128;
 };
-static_assert(ScanSmem::BUF % 1024 == 0 && ScanSmem::U % 16 == 0 && ScanSmem::Q % 1024 == 0, "copy alignment");
-static_assert(ScanSmem::BYTES <= 232448, "scan shared memory");
+static_assert(TcSmem::WLO - TcSmem::A1 == 4 * 8192 && TcSmem::G - TcSmem::WLO == WS_G - WS_WLO, "copy layout");
+static_assert(TcSmem::BUF % 1024 == 0 && TcSmem::SHI % 1024 == 0 && TcSmem::BYTES <= 232448, "scan shared memory");
 
-// Element (row, col) of a Q / K tile (see ScanSmem) as its exact TF32 bit pattern.
+// barrier slots
+constexpr int B_FULL = 0;     // [2] a buffer's copies landed
+constexpr int B_EMPTY = 2;    // [2] a buffer is free: its MMAs committed and the four epilogue warps done with it
+constexpr int B_SREADY = 4;   // the state operand of the next chunk written (four warps)
+constexpr int B_D1 = 5;       // [2] P1 done
+constexpr int B_UREADY = 7;   // U / Ud operands written (warps 0-1)
+constexpr int B_D2 = 8;       // P2 done
+constexpr int B_D3 = 9;       // [2] P3 done
+constexpr int B_YDONE = 11;   // [2] E-Y read D1 / D3 of that parity (warps 2-3)
+constexpr int B_DRAIN = 13;   // every MMA issued has completed (the MMA thread's exit)
+
+// TMEM columns
+constexpr uint32_t T_D1 = 0, T_D4 = 64, T_D3 = 128, T_D2 = 192;  // D1, D4, D3: two 32-column buffers each
+
+// The chunk's 16-bit operand pair of value x: (hi, lo) of the activation type.
 template <typename T>
-__device__ __forceinline__ uint32_t qk_tf32(const uint8_t* tile, int row, int col) {
-  const int off = (col >> 6) * (C * 128) + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) << 4) + ((col & 7) << 1);
-  return tf32_of(*reinterpret_cast<const T*>(tile + off));
+__device__ __forceinline__ void split_pair(float x, uint16_t& hi, uint16_t& lo) {
+  const T h = from_f<T>(x);
+  const T l = from_f<T>(x - to_f<T>(h));
+  hi = *reinterpret_cast<const uint16_t*>(&h);
+  lo = *reinterpret_cast<const uint16_t*>(&l);
 }
 
-// TF32 m16n8k8 fragments by ldmatrix (an 8 x 4 block of 32-bit values is an 8 x 8 block of 16-bit halves; thread
-// g * 4 + t receives the 32-bit value at row g, column t, the fragments' layout). `base` is the shared address of
-// element (0, 0) of a row-major fp32 / TF32 tile with `ld` values a row (ld * 4 % 128 == 16: conflict-free rows).
-// A: rows m0 .. m0 + 15, columns k0 .. k0 + 7.
-__device__ __forceinline__ void frag_a(uint32_t base, int ld, int m0, int k0, int lane, uint32_t* a) {
-  ldsm4(base + ((m0 + (lane & 7) + ((lane >> 3) & 1) * 8) * ld + k0 + (lane >> 4) * 4) * 4, a);
-}
-// B of two n-tiles from a tile stored n-major ([n][k]): n0 .. n0 + 15, k0 .. k0 + 7; b[0], b[1] for n-tile n0,
-// b[2], b[3] for n0 + 8.
-__device__ __forceinline__ void frag_b2(uint32_t base, int ld, int n0, int k0, int lane, uint32_t* b) {
-  ldsm4(base + ((n0 + (lane & 7) + (lane >> 4) * 8) * ld + k0 + ((lane >> 3) & 1) * 4) * 4, b);
-}
-
-
-// The tiles of chunk c into one buffer, completing on its mbarrier (thread 0 issues all): W, M and the gates in one
-// bulk copy, this block's U' slice in another, and the Q and K tiles by tiled TMA, two 64-column boxes each (rows
-// past T arrive as zeros).
-__device__ __forceinline__ void scan_prefetch(const Params& p, const CUtensorMap* qmap, const CUtensorMap* kmap,
-                                              uint8_t* buf, uint64_t* full, int b, int h, int hk, int c, int blk) {
-  const float* u = unit_ptr(p, b, h, c);
-  fence_proxy_async_shared();  // the buffer's reads two chunks back precede these writes
-  mbar_arrive_expect_tx(full, uint32_t(WMG_BYTES + C * UP * 4 + 2 * ScanSmem::QK_TILE));
-  bulk_g2s(buf + ScanSmem::W, u + WS_W, WMG_BYTES, full);
-  bulk_g2s(buf + ScanSmem::U, u + WS_U + blk * C * UP, C * UP * 4, full);
+// Writes column `col` (a key or a position) of a [32 rows][cols] 16-bit K-major operand pair: row j gets x[j].
+template <typename T>
+__device__ __forceinline__ void put_column(uint8_t* hi, uint8_t* lo, int col, const float* x) {
+  uint8_t* bh = hi + (col >> 6) * (DVB * 128);
+  uint8_t* bl = lo + (col >> 6) * (DVB * 128);
 #pragma unroll
-  for (int db = 0; db < DK / 64; ++db) {
-    tma_load_4d(buf + ScanSmem::Q + db * C * 128, qmap, db * 64, c * C, hk, b, full);
-    tma_load_4d(buf + ScanSmem::K + db * C * 128, kmap, db * 64, c * C, hk, b, full);
+  for (int j = 0; j < DVB; ++j) {
+    uint16_t h, l;
+    split_pair<T>(x[j], h, l);
+    const int off = sw128(j, col & 63);
+    *reinterpret_cast<uint16_t*>(bh + off) = h;
+    *reinterpret_cast<uint16_t*>(bl + off) = l;
   }
 }
 
-// Named barriers (ids 1-4; 0 is __syncthreads): wait until `count` threads arrived, or arrive without waiting. The
-// arriving threads' earlier shared-memory writes are visible to the threads that waited.
-__device__ __forceinline__ void nbar_sync(int id, int count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-__device__ __forceinline__ void nbar_arrive(int id, int count) {
-  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-// bar.sync that also ORs a flag over the participating threads.
-__device__ __forceinline__ bool nbar_sync_or(int id, int count, bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"(uint32_t(v)), "r"(id), "r"(count)
-      : "memory");
-  return r != 0;
-}
-constexpr int BAR_A = 1;   // all 256: U of the chunk written, every read of the state copy done
-constexpr int BAR_S = 2;   // warps 0-3 arrive, warps 4-7 wait: the state copy updated
-constexpr int BAR_U = 3;   // warps 4-7 arrive, warps 0-3 wait: M U read the chunk's U and its buffer is done with
-constexpr int BAR_S0 = 4;  // warps 0-3: the state copy updated, before their next W S^T
-
-// One CTA: value rows dv0 .. dv0 + 31 of one (batch, v-head), all chunks in order. Two roles, so that Y stays off the
-// chain from one chunk's state to the next:
-//   warps 0-3 own the fp32 state slice in registers (warp w: key columns 32 w .. 32 w + 31 of all 32 rows; a TF32
-//     copy in shared memory feeds the products that read the whole slice). Per chunk: U = U' - W S^T (16 positions
-//     each), then the state update S <- Gam_C S + (diag(exp(gamma_C - gamma)) U)^T K on their columns;
-//   warps 4-7 form Gam Q S^T beside W S^T, then M U and the Y store while warps 0-3 update the state, and wait for
-//     the updated copy before the next chunk's Q S^T.
-// Barrier order a chunk: warps 0-3 wait BAR_U (M U of the chunk before is done, so U and that chunk's buffer are
-// free: the next chunk's copies are issued), W S^T, write U, BAR_A, update, arrive BAR_S, sync BAR_S0; warps 4-7 wait
-// BAR_S (the state copy of this chunk is complete), Q S^T, BAR_A, M U, store Y, arrive BAR_U. A wait that gave up in
-// any thread is ORed at BAR_A and every warp leaves the loop there.
 template <typename T>
-__global__ void __launch_bounds__(SCAN_THREADS, 1) scan_kernel(const __grid_constant__ CUtensorMap qmap,
-                                                                const __grid_constant__ CUtensorMap kmap,
-                                                                const Params p) {
+__global__ void __launch_bounds__(TC_THREADS, 1) scan_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                              const __grid_constant__ CUtensorMap kmap,
+                                                              const Params p) {
+  constexpr uint32_t AB = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+  constexpr uint32_t IDESC_K = prefill::idesc_f16(AB, 0, 0, 128, DVB);   // A K-major
+  constexpr uint32_t IDESC_MN = prefill::idesc_f16(AB, 1, 0, 128, DVB);  // A MN-major (the K tile as K^T)
   const int blk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int hk = h / (p.Hv / p.Hk);
   const int dv0 = blk * DVB;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int r = lane >> 2, cq = lane & 3;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = p.nchunks;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint32_t* St = reinterpret_cast<uint32_t*>(sm + ScanSmem::ST);
-  uint32_t* Ub = reinterpret_cast<uint32_t*>(sm + ScanSmem::UB);
-  uint32_t* Ud = reinterpret_cast<uint32_t*>(sm + ScanSmem::UD);
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + ScanSmem::BAR);
-  if (tid == 0) {
-    prefetch_tensormap(&qmap);
-    prefetch_tensormap(&kmap);
-    mbar_init(&full[0], 1);
-    mbar_init(&full[1], 1);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + TcSmem::BAR);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(sm + TcSmem::SLOT);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + TcSmem::SLOT + 4);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar[B_FULL + i], 1);
+      mbar_init(&bar[B_EMPTY + i], 5);  // the MMA commit + one arrive per epilogue warp
+      mbar_init(&bar[B_D1 + i], 1);
+      mbar_init(&bar[B_D3 + i], 1);
+      mbar_init(&bar[B_YDONE + i], 2);
+    }
+    mbar_init(&bar[B_SREADY], 4);
+    mbar_init(&bar[B_UREADY], 2);
+    mbar_init(&bar[B_D2], 1);
+    mbar_init(&bar[B_DRAIN], 1);
+    *abort_flag = 0;
     fence_barrier_init();
   }
-
-  // warps 0-3: the state tile of this warp, rows mt * 16 + r (+ 8), columns 32 warp + 8 n + 2 cq (+ 1)
-  const bool chain = warp < 4;
-  float sreg[2][4][4];
-  const float* sin = p.s_in + (int64_t(b) * p.Hv + h) * DV * DK;
-  if (chain) {
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-      for (int n = 0; n < 4; ++n)
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const int i = mt * 16 + r + 8 * hh, d = warp * 32 + n * 8 + 2 * cq;
-          const float2 v = *reinterpret_cast<const float2*>(sin + int64_t(dv0 + i) * DK + d);
-          sreg[mt][n][2 * hh] = v.x;
-          sreg[mt][n][2 * hh + 1] = v.y;
-          St[i * WP + d] = tf32(v.x);
-          St[i * WP + d + 1] = tf32(v.y);
-        }
+  if (warp == 5) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+                 "r"(TC_TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
-  __syncthreads();  // barriers initialised, the state copy written
-  if (p.nchunks > 0 && tid == 0) scan_prefetch(p, &qmap, &kmap, sm, &full[0], b, h, hk, 0, blk);
+  prefill::tc_fence_before();
+  __syncthreads();
+  prefill::tc_fence_after();
+  const uint32_t tmem = *slot;
 
-  bool ok = true;
-  int issued = p.nchunks > 0 ? 1 : 0;  // chunks whose copies were issued (thread 0)
-  const int m0 = (warp & 3) * 16;
-  for (int c = 0; c < p.nchunks; ++c) {
-    const bool last = c + 1 == p.nchunks;
-    uint8_t* buf = sm + (c & 1) * ScanSmem::BUF;
-    const uint32_t* W = reinterpret_cast<const uint32_t*>(buf + ScanSmem::W);
-    const float* U = reinterpret_cast<const float*>(buf + ScanSmem::U);
-    const uint32_t* M = reinterpret_cast<const uint32_t*>(buf + ScanSmem::M);
-    const uint8_t* Q = buf + ScanSmem::Q;
-    const uint8_t* K = buf + ScanSmem::K;
-    const float* G = reinterpret_cast<const float*>(buf + ScanSmem::G);
-    float acc[4][4];
+  if (warp < 4) {
+    // ------------------------------------------------------------------------------------ epilogue warps
+    const int k = 32 * warp + lane;                // this thread's key column of S
+    const uint32_t lq = uint32_t(32 * warp) << 16;  // the warp's TMEM lane quarter
+    float s[DVB];
+    const float* sin = p.s_in + (int64_t(b) * p.Hv + h) * DV * DK + int64_t(dv0) * DK + k;
 #pragma unroll
-    for (int n = 0; n < 4; ++n)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
-    if (chain) {
-      if (c > 0) nbar_sync(BAR_U, SCAN_THREADS);  // M U of chunk c - 1 done: U and that chunk's buffer are free
-      if (!last && tid == 0) {
-        scan_prefetch(p, &qmap, &kmap, sm + ((c + 1) & 1) * ScanSmem::BUF, &full[(c + 1) & 1], b, h, hk, c + 1, blk);
-        issued = c + 2;
-      }
-      ok = mbar_wait(&full[c & 1], (c >> 1) & 1, 71);
-      // (1) acc = W S^T: rows m0 .. m0 + 15, all 32 value columns
-#pragma unroll 4
-      for (int k0 = 0; k0 < DK; k0 += 8) {
-        uint32_t a[4], b01[4], b23[4];
-        frag_a(smem_u32(W), WP, m0, k0, lane, a);
-        frag_b2(smem_u32(St), WP, 0, k0, lane, b01);
-        frag_b2(smem_u32(St), WP, 16, k0, lane, b23);
-        mma_tf32(acc[0], a[0], a[1], a[2], a[3], b01[0], b01[1]);
-        mma_tf32(acc[1], a[0], a[1], a[2], a[3], b01[2], b01[3]);
-        mma_tf32(acc[2], a[0], a[1], a[2], a[3], b23[0], b23[1]);
-        mma_tf32(acc[3], a[0], a[1], a[2], a[3], b23[2], b23[3]);
-      }
-      // U = U' - W S^T, stored rounded for the products that read it, plain and scaled by exp(gamma_C - gamma_t)
-      const float gl = G[C - 1];
-      const float dl = __expf(gl - G[m0 + r]), dh = __expf(gl - G[m0 + r + 8]);
-#pragma unroll
-      for (int n = 0; n < 4; ++n)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int t = m0 + r + 8 * (e >> 1), col = n * 8 + 2 * cq + (e & 1);
-          const float u = U[t * UP + col] - acc[n][e];
-          Ub[col * UQ + t] = tf32(u);
-          Ud[col * UQ + t] = tf32((e >> 1 ? dh : dl) * u);
-        }
-    } else {
-      if (c > 0) nbar_sync(BAR_S, SCAN_THREADS);  // the state copy of chunk c is complete
-      ok = mbar_wait(&full[c & 1], (c >> 1) & 1, 71);
-      // (1) acc = Gam Q S^T: rows m0 .. m0 + 15, all 32 value columns
-#pragma unroll 4
-      for (int k0 = 0; k0 < DK; k0 += 8) {
-        const uint32_t a0 = qk_tf32<T>(Q, m0 + r, k0 + cq), a1 = qk_tf32<T>(Q, m0 + r + 8, k0 + cq);
-        const uint32_t a2 = qk_tf32<T>(Q, m0 + r, k0 + cq + 4), a3 = qk_tf32<T>(Q, m0 + r + 8, k0 + cq + 4);
-        uint32_t b01[4], b23[4];
-        frag_b2(smem_u32(St), WP, 0, k0, lane, b01);
-        frag_b2(smem_u32(St), WP, 16, k0, lane, b23);
-        mma_tf32(acc[0], a0, a1, a2, a3, b01[0], b01[1]);
-        mma_tf32(acc[1], a0, a1, a2, a3, b01[2], b01[3]);
-        mma_tf32(acc[2], a0, a1, a2, a3, b23[0], b23[1]);
-        mma_tf32(acc[3], a0, a1, a2, a3, b23[2], b23[3]);
-      }
-      const float gl = G[C + m0 + r], gh = G[C + m0 + r + 8];
-#pragma unroll
-      for (int n = 0; n < 4; ++n) {
-        acc[n][0] *= gl;
-        acc[n][1] *= gl;
-        acc[n][2] *= gh;
-        acc[n][3] *= gh;
-      }
+    for (int j = 0; j < DVB; ++j) s[j] = sin[int64_t(j) * DK];
+    if (n > 0) {
+      put_column<T>(sm + TcSmem::SHI, sm + TcSmem::SLO, k, s);
+      fence_proxy_async_shared();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[B_SREADY]);
     }
-    if (nbar_sync_or(BAR_A, SCAN_THREADS, !ok)) {  // U complete; every read of the state copy done
-      ok = false;
-      break;
-    }
-    if (chain) {
-      // (2) S <- Gam_C S + (diag(dec) U)^T K on this warp's 32 key columns (all 32 value rows)
-      const float gc = G[C + C - 1];
+    bool ok = true;
+    for (int c = 0; c < n && ok; ++c) {
+      const int par = c & 1;
+      uint8_t* buf = sm + par * TcSmem::BUF;
+      const float* gam = reinterpret_cast<const float*>(buf + TcSmem::G);
+      const float* Gam = gam + C;
+      if (warp < 2) {  // E-U: positions t = k (0 .. 63)
+        ok = __all_sync(0xffffffffu, mbar_wait(&bar[B_D1 + par], (c >> 1) & 1, 81) && !*abort_flag);
+        if (!ok) break;
+        prefill::tc_fence_after();
+        float d[DVB], d4[DVB];
+        prefill::tmem_ld32(tmem + lq + T_D1 + par * 32, d);
+        prefill::tmem_ld32(tmem + lq + T_D4 + par * 32, d4);
+        prefill::tmem_wait_ld();
+        const int t = k;
+        const float dec = __expf(gam[C - 1] - gam[t]);
+        const float4* up = reinterpret_cast<const float4*>(buf + TcSmem::U + t * UP * 4);
+        float u[DVB], ud[DVB];
 #pragma unroll
-      for (int mt = 0; mt < 2; ++mt)
+        for (int q4 = 0; q4 < DVB / 4; ++q4) {
+          const float4 x = up[q4];
+          const float xs[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
-        for (int n = 0; n < 4; ++n)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) sreg[mt][n][e] *= gc;
-#pragma unroll 2
-      for (int k0 = 0; k0 < C; k0 += 8) {
-        uint32_t a[2][4];
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt) frag_a(smem_u32(Ud), UQ, mt * 16, k0, lane, a[mt]);
-#pragma unroll
-        for (int n = 0; n < 4; ++n) {
-          const int col = warp * 32 + n * 8 + r;
-          const uint32_t b0 = qk_tf32<T>(K, k0 + cq, col), b1 = qk_tf32<T>(K, k0 + cq + 4, col);
-#pragma unroll
-          for (int mt = 0; mt < 2; ++mt) mma_tf32(sreg[mt][n], a[mt][0], a[mt][1], a[mt][2], a[mt][3], b0, b1);
-        }
-      }
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-        for (int n = 0; n < 4; ++n)
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const int i = mt * 16 + r + 8 * hh, d = warp * 32 + n * 8 + 2 * cq;
-            St[i * WP + d] = tf32(sreg[mt][n][2 * hh]);
-            St[i * WP + d + 1] = tf32(sreg[mt][n][2 * hh + 1]);
+          for (int e = 0; e < 4; ++e) {
+            const int j = 4 * q4 + e;
+            u[j] = xs[e] - (d[j] + d4[j]);
+            ud[j] = dec * u[j];
           }
-      if (!last) {
-        nbar_arrive(BAR_S, SCAN_THREADS);
-        nbar_sync(BAR_S0, 128);
+        }
+        put_column<T>(sm + TcSmem::UHI, sm + TcSmem::ULO, t, u);
+        put_column<T>(sm + TcSmem::UDHI, sm + TcSmem::UDLO, t, ud);
+        fence_proxy_async_shared();
+        prefill::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar[B_UREADY]);
       }
-    } else {
-      // (3) Y = Gam Q S^T + M U (M lower triangular: k < m0 + 16), stored
-      for (int k0 = 0; k0 < m0 + 16; k0 += 8) {
-        uint32_t a[4], b01[4], b23[4];
-        frag_a(smem_u32(M), AP, m0, k0, lane, a);
-        frag_b2(smem_u32(Ub), UQ, 0, k0, lane, b01);
-        frag_b2(smem_u32(Ub), UQ, 16, k0, lane, b23);
-        mma_tf32(acc[0], a[0], a[1], a[2], a[3], b01[0], b01[1]);
-        mma_tf32(acc[1], a[0], a[1], a[2], a[3], b01[2], b01[3]);
-        mma_tf32(acc[2], a[0], a[1], a[2], a[3], b23[0], b23[1]);
-        mma_tf32(acc[3], a[0], a[1], a[2], a[3], b23[2], b23[3]);
-      }
-      if (!last) nbar_arrive(BAR_U, SCAN_THREADS);  // done with U and with this chunk's buffer
-      T* yg = static_cast<T*>(p.y);
+      // E-S: S <- Gam_C S + K^T Ud on this thread's key column
+      ok = __all_sync(0xffffffffu, mbar_wait(&bar[B_D2], c & 1, 82) && !*abort_flag);
+      if (!ok) break;
+      prefill::tc_fence_after();
+      {
+        float d2[DVB];
+        prefill::tmem_ld32(tmem + lq + T_D2, d2);
+        prefill::tmem_wait_ld();
+        const float gc = Gam[C - 1];
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int t = m0 + r + 8 * hh, pos = c * C + t;
+        for (int j = 0; j < DVB; ++j) s[j] = fmaf(gc, s[j], d2[j]);
+      }
+      if (c + 1 < n) {
+        put_column<T>(sm + TcSmem::SHI, sm + TcSmem::SLO, k, s);
+        fence_proxy_async_shared();
+      }
+      prefill::tc_fence_before();
+      __syncwarp();
+      if (lane == 0 && c + 1 < n) mbar_arrive(&bar[B_SREADY]);
+      if (warp >= 2) {  // E-Y: positions t = k - 64
+        ok = __all_sync(0xffffffffu, mbar_wait(&bar[B_D3 + par], (c >> 1) & 1, 83) && !*abort_flag);
+        if (!ok) break;
+        prefill::tc_fence_after();
+        float qs[DVB], mu[DVB];
+        prefill::tmem_ld32(tmem + lq + T_D1 + par * 32, qs);
+        prefill::tmem_ld32(tmem + lq + T_D3 + par * 32, mu);
+        prefill::tmem_wait_ld();
+        const int t = k - C;
+        const int pos = c * C + t;
+        const float gt = Gam[t];
+        prefill::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar[B_YDONE + par]);
         if (pos < p.T) {
-          T* yr = yg + ((int64_t(b) * p.T + pos) * p.Hv + h) * DV + dv0;
+          uint4* yr = reinterpret_cast<uint4*>(static_cast<T*>(p.y) + ((int64_t(b) * p.T + pos) * p.Hv + h) * DV + dv0);
 #pragma unroll
-          for (int n = 0; n < 4; ++n) {
-            yr[n * 8 + 2 * cq] = from_f<T>(acc[n][2 * hh]);
-            yr[n * 8 + 2 * cq + 1] = from_f<T>(acc[n][2 * hh + 1]);
+          for (int q8 = 0; q8 < DVB / 8; ++q8) {
+            uint32_t w4[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int j = 8 * q8 + 2 * e;
+              w4[e] = pack2<T>(fmaf(gt, qs[j], mu[j]), fmaf(gt, qs[j + 1], mu[j + 1]));
+            }
+            yr[q8] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
           }
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[B_EMPTY + par]);  // this warp is done with the chunk's buffer
     }
-  }
-  if (!ok) {  // a wait gave up (status word set): let the copies still in flight land (bounded), write nothing
-    if (tid == 0)
-      for (int c2 = max(0, issued - 2); c2 < issued; ++c2) mbar_wait(&full[c2 & 1], (c2 >> 1) & 1, 72);
-    return;
-  }
-  if (chain) {
-    float* sout = p.s_out + (int64_t(b) * p.Hv + h) * DV * DK;
+    if (!ok) {
+      *abort_flag = 1;
+    } else {
+      float* sout = p.s_out + (int64_t(b) * p.Hv + h) * DV * DK + int64_t(dv0) * DK + k;
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-      for (int n = 0; n < 4; ++n)
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const int i = mt * 16 + r + 8 * hh, d = warp * 32 + n * 8 + 2 * cq;
-          *reinterpret_cast<float2*>(sout + int64_t(dv0 + i) * DK + d) =
-              make_float2(sreg[mt][n][2 * hh], sreg[mt][n][2 * hh + 1]);
+      for (int j = 0; j < DVB; ++j) sout[int64_t(j) * DK] = s[j];
+    }
+  } else if (warp == 4) {
+    // ------------------------------------------------------------------------------------ loads
+    if (lane == 0 && n > 0) {
+      prefetch_tensormap(&qmap);
+      prefetch_tensormap(&kmap);
+      int issued = 0;
+      for (int c = 0; c < n; ++c) {
+        const int par = c & 1;
+        if (c >= 2 && !mbar_wait(&bar[B_EMPTY + par], ((c >> 1) - 1) & 1, 84)) {
+          *abort_flag = 1;
+          break;
         }
+        if (*abort_flag) break;
+        uint8_t* buf = sm + par * TcSmem::BUF;
+        const uint8_t* u = unit_ptr(p, b, h, c);
+        fence_proxy_async_shared();
+        mbar_arrive_expect_tx(&bar[B_FULL + par], TcSmem::TX);
+        bulk_g2s(buf + TcSmem::A1, u + WS_WHI, C * 128, &bar[B_FULL + par]);
+        bulk_g2s(buf + TcSmem::A1 + 2 * C * 128, u + WS_WHI + C * 128, C * 128, &bar[B_FULL + par]);
+        bulk_g2s(buf + TcSmem::WLO, u + WS_WLO, WS_U - WS_WLO, &bar[B_FULL + par]);
+        bulk_g2s(buf + TcSmem::U, u + WS_U + blk * USLICE, USLICE, &bar[B_FULL + par]);
+#pragma unroll
+        for (int db = 0; db < DK / 64; ++db) {
+          tma_load_4d(buf + TcSmem::A1 + db * 2 * C * 128 + C * 128, &qmap, db * 64, c * C, hk, b, &bar[B_FULL + par]);
+          tma_load_4d(buf + TcSmem::K + db * C * 128, &kmap, db * 64, c * C, hk, b, &bar[B_FULL + par]);
+        }
+        issued = c + 1;
+      }
+      // what was issued has landed before the CTA may leave (bounded)
+      for (int c = max(0, issued - 2); c < issued; ++c) mbar_wait(&bar[B_FULL + (c & 1)], (c >> 1) & 1, 85);
+    }
+  } else {
+    // ------------------------------------------------------------------------------------ MMA issuer
+    if (elect_one() && n > 0) {
+      bool ok = true;
+      const uint32_t shi = smem_u32(sm + TcSmem::SHI), slo = smem_u32(sm + TcSmem::SLO);
+      const uint32_t uhi = smem_u32(sm + TcSmem::UHI), ulo = smem_u32(sm + TcSmem::ULO);
+      const uint32_t udhi = smem_u32(sm + TcSmem::UDHI), udlo = smem_u32(sm + TcSmem::UDLO);
+      for (int c = 0; c < n && ok; ++c) {
+        const int par = c & 1;
+        const uint32_t base = smem_u32(sm + par * TcSmem::BUF);
+        ok = mbar_wait(&bar[B_FULL + par], (c >> 1) & 1, 86) && mbar_wait(&bar[B_SREADY], c & 1, 87) &&
+             (c < 2 || mbar_wait(&bar[B_YDONE + par], ((c >> 1) - 1) & 1, 88)) && !*abort_flag;
+        if (!ok) break;
+        prefill::tc_fence_after();
+        // P1: D1 = [W_hi ; Q] (S_hi + S_lo)^T, D4 = W_lo S_hi^T (K = 128 keys: two 64-key blocks of 4 steps)
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint32_t acc = (kb | ks) ? 1u : 0u;
+            const uint64_t a = prefill::sdesc(base + TcSmem::A1 + kb * 2 * C * 128 + ks * 32, 16, 1024);
+            const uint64_t al = prefill::sdesc(base + TcSmem::WLO + kb * C * 128 + ks * 32, 16, 1024);
+            const uint64_t bh = prefill::sdesc(shi + kb * DVB * 128 + ks * 32, 16, 1024);
+            const uint64_t bl = prefill::sdesc(slo + kb * DVB * 128 + ks * 32, 16, 1024);
+            prefill::umma_ss(tmem + T_D1 + par * 32, a, bh, IDESC_K, acc);
+            prefill::umma_ss(tmem + T_D1 + par * 32, a, bl, IDESC_K, 1u);
+            prefill::umma_ss(tmem + T_D4 + par * 32, al, bh, IDESC_K, acc);
+          }
+        prefill::umma_commit(&bar[B_D1 + par]);
+        ok = mbar_wait(&bar[B_UREADY], c & 1, 89) && !*abort_flag;
+        if (!ok) break;
+        prefill::tc_fence_after();
+        // P2: D2 = K^T (Ud_hi + Ud_lo): A = the K tile [64 positions][128 keys] read as M = keys (MN-major: the two
+        // 64-key boxes 8 KB apart), K = positions in steps of 16 rows
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint64_t a = prefill::sdesc(base + TcSmem::K + ks * 16 * 128, C * 128, 1024);
+          prefill::umma_ss(tmem + T_D2, a, prefill::sdesc(udhi + ks * 32, 16, 1024), IDESC_MN, ks ? 1u : 0u);
+          prefill::umma_ss(tmem + T_D2, a, prefill::sdesc(udlo + ks * 32, 16, 1024), IDESC_MN, 1u);
+        }
+        prefill::umma_commit(&bar[B_D2]);
+        // P3: D3[64:128] = M_hi (U_hi + U_lo) + M_lo U_hi; A rows 0-63 are whatever precedes (D3 rows 0-63 unused)
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint64_t ahi = prefill::sdesc(base + TcSmem::MHI - C * 128 + ks * 32, 16, 1024);
+          const uint64_t alo = prefill::sdesc(base + TcSmem::MHI + ks * 32, 16, 1024);
+          prefill::umma_ss(tmem + T_D3 + par * 32, ahi, prefill::sdesc(uhi + ks * 32, 16, 1024), IDESC_K,
+                           ks ? 1u : 0u);
+          prefill::umma_ss(tmem + T_D3 + par * 32, ahi, prefill::sdesc(ulo + ks * 32, 16, 1024), IDESC_K, 1u);
+          prefill::umma_ss(tmem + T_D3 + par * 32, alo, prefill::sdesc(uhi + ks * 32, 16, 1024), IDESC_K, 1u);
+        }
+        prefill::umma_commit(&bar[B_D3 + par]);
+        prefill::umma_commit(&bar[B_EMPTY + par]);
+      }
+      if (!ok) *abort_flag = 1;
+      prefill::umma_commit(&bar[B_DRAIN]);  // every MMA issued has completed before TMEM is freed
+      mbar_wait(&bar[B_DRAIN], 0, 90);
+    }
+    __syncwarp();
+  }
+  prefill::tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    prefill::tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS));
   }
 }
 

@@ -773,7 +773,7 @@ size_t lb2_gdn_chunked_workspace_size(int B, int T, int Hk, int Hv, int Dk, int 
   (void)Hk;
   if (B <= 0 || T < 0 || Hv <= 0 || Dk != gdnchunk::DK || Dv != gdnchunk::DV) return 0;
   const int64_t nchunks = (int64_t(T) + gdnchunk::C - 1) / gdnchunk::C;
-  return size_t(int64_t(B) * Hv * nchunks * gdnchunk::UNIT * int64_t(sizeof(float))) + 256;
+  return size_t(int64_t(B) * Hv * nchunks * gdnchunk::UNIT_BYTES) + 256;
 }
 
 int lb2_gdn_chunked(const void* q, const void* k, int qdt, const void* v, int vdt, const void* g, int gdt,
@@ -811,18 +811,18 @@ int lb2_gdn_chunked(const void* q, const void* k, int qdt, const void* v, int vd
     LB2_CUDA(cudaFuncSetAttribute(gdnchunk::prep_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   gdnchunk::PrepSmem::BYTES));
     LB2_CUDA(cudaFuncSetAttribute(gdnchunk::scan_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  gdnchunk::ScanSmem::BYTES));
+                                  gdnchunk::TcSmem::BYTES));
     LB2_CUDA(cudaFuncSetAttribute(gdnchunk::scan_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  gdnchunk::ScanSmem::BYTES));
+                                  gdnchunk::TcSmem::BYTES));
     attr_dev = dev;
   }
   const dim3 gp(unsigned(p.nchunks), unsigned(Hv), unsigned(B)), gs(gdnchunk::DV / gdnchunk::DVB, Hv, B);
   if (qdt == LB2_BF16) {
     if (p.nchunks > 0) gdnchunk::prep_kernel<__nv_bfloat16><<<gp, 128, gdnchunk::PrepSmem::BYTES, st>>>(p);
-    gdnchunk::scan_kernel<__nv_bfloat16><<<gs, gdnchunk::SCAN_THREADS, gdnchunk::ScanSmem::BYTES, st>>>(qm, km, p);
+    gdnchunk::scan_kernel<__nv_bfloat16><<<gs, gdnchunk::TC_THREADS, gdnchunk::TcSmem::BYTES, st>>>(qm, km, p);
   } else {
     if (p.nchunks > 0) gdnchunk::prep_kernel<__half><<<gp, 128, gdnchunk::PrepSmem::BYTES, st>>>(p);
-    gdnchunk::scan_kernel<__half><<<gs, gdnchunk::SCAN_THREADS, gdnchunk::ScanSmem::BYTES, st>>>(qm, km, p);
+    gdnchunk::scan_kernel<__half><<<gs, gdnchunk::TC_THREADS, gdnchunk::TcSmem::BYTES, st>>>(qm, km, p);
   }
   LB2_CUDA(cudaGetLastError());
   return LB2_OK;
