@@ -471,11 +471,12 @@ constexpr int B_FULL = 0;     // [2] a buffer's copies landed
 constexpr int B_EMPTY = 2;    // [2] a buffer is free: its MMAs committed and the four epilogue warps done with it
 constexpr int B_SREADY = 4;   // the state operand of the next chunk written (four warps)
 constexpr int B_D1 = 5;       // [2] P1 done
-constexpr int B_UREADY = 7;   // U / Ud operands written (warps 0-1)
+constexpr int B_UREADY = 7;   // U operands written (warps 0-1)
 constexpr int B_D2 = 8;       // P2 done
 constexpr int B_D3 = 9;       // [2] P3 done
 constexpr int B_YDONE = 11;   // [2] E-Y read D1 / D3 of that parity (warps 2-3)
 constexpr int B_DRAIN = 13;   // every MMA issued has completed (the MMA thread's exit)
+constexpr int B_UDREADY = 14; // Ud operands written (warps 0-1): P2 may start
 
 // TMEM columns
 constexpr uint32_t T_D1 = 0, T_D4 = 64, T_D3 = 128, T_D2 = 192;  // D1, D4, D3: two 32-column buffers each
@@ -532,6 +533,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) scan_kernel(const __grid_consta
     }
     mbar_init(&bar[B_SREADY], 4);
     mbar_init(&bar[B_UREADY], 2);
+    mbar_init(&bar[B_UDREADY], 2);
     mbar_init(&bar[B_D2], 1);
     mbar_init(&bar[B_DRAIN], 1);
     *abort_flag = 0;
@@ -567,36 +569,48 @@ __global__ void __launch_bounds__(TC_THREADS, 1) scan_kernel(const __grid_consta
       uint8_t* buf = sm + par * TcSmem::BUF;
       const float* gam = reinterpret_cast<const float*>(buf + TcSmem::G);
       const float* Gam = gam + C;
+      // the chunk's buffer has landed (it did before P1 could run): gates and U' are read off the chain
+      ok = __all_sync(0xffffffffu, mbar_wait(&bar[B_FULL + par], (c >> 1) & 1, 80) && !*abort_flag);
+      if (!ok) break;
       if (warp < 2) {  // E-U: positions t = k (0 .. 63)
+        const int t = k;
+        const float dec = __expf(gam[C - 1] - gam[t]);
+        float u[DVB];
+        {
+          const float4* up = reinterpret_cast<const float4*>(buf + TcSmem::U + t * UP * 4);
+#pragma unroll
+          for (int q4 = 0; q4 < DVB / 4; ++q4) {
+            const float4 x = up[q4];
+            u[4 * q4] = x.x, u[4 * q4 + 1] = x.y, u[4 * q4 + 2] = x.z, u[4 * q4 + 3] = x.w;
+          }
+        }
         ok = __all_sync(0xffffffffu, mbar_wait(&bar[B_D1 + par], (c >> 1) & 1, 81) && !*abort_flag);
         if (!ok) break;
         prefill::tc_fence_after();
-        float d[DVB], d4[DVB];
-        prefill::tmem_ld32(tmem + lq + T_D1 + par * 32, d);
-        prefill::tmem_ld32(tmem + lq + T_D4 + par * 32, d4);
-        prefill::tmem_wait_ld();
-        const int t = k;
-        const float dec = __expf(gam[C - 1] - gam[t]);
-        const float4* up = reinterpret_cast<const float4*>(buf + TcSmem::U + t * UP * 4);
-        float u[DVB], ud[DVB];
+        {
+          float d[DVB], d4[DVB];
+          prefill::tmem_ld32(tmem + lq + T_D1 + par * 32, d);
+          prefill::tmem_ld32(tmem + lq + T_D4 + par * 32, d4);
+          prefill::tmem_wait_ld();
 #pragma unroll
-        for (int q4 = 0; q4 < DVB / 4; ++q4) {
-          const float4 x = up[q4];
-          const float xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int j = 4 * q4 + e;
-            u[j] = xs[e] - (d[j] + d4[j]);
-            ud[j] = dec * u[j];
-          }
+          for (int j = 0; j < DVB; ++j) u[j] -= d[j] + d4[j];
         }
-        put_column<T>(sm + TcSmem::UHI, sm + TcSmem::ULO, t, u);
-        put_column<T>(sm + TcSmem::UDHI, sm + TcSmem::UDLO, t, ud);
-        fence_proxy_async_shared();
         prefill::tc_fence_before();
+        {  // Ud first: the state update (P2) waits for it; U (P3, off the chain) after
+          float ud[DVB];
+#pragma unroll
+          for (int j = 0; j < DVB; ++j) ud[j] = dec * u[j];
+          put_column<T>(sm + TcSmem::UDHI, sm + TcSmem::UDLO, t, ud);
+        }
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar[B_UDREADY]);
+        put_column<T>(sm + TcSmem::UHI, sm + TcSmem::ULO, t, u);
+        fence_proxy_async_shared();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bar[B_UREADY]);
       }
+      const float gc = Gam[C - 1];  // read before the wait: the buffer stays until this warp releases it
       // E-S: S <- Gam_C S + K^T Ud on this thread's key column
       ok = __all_sync(0xffffffffu, mbar_wait(&bar[B_D2], c & 1, 82) && !*abort_flag);
       if (!ok) break;
@@ -605,7 +619,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) scan_kernel(const __grid_consta
         float d2[DVB];
         prefill::tmem_ld32(tmem + lq + T_D2, d2);
         prefill::tmem_wait_ld();
-        const float gc = Gam[C - 1];
 #pragma unroll
         for (int j = 0; j < DVB; ++j) s[j] = fmaf(gc, s[j], d2[j]);
       }
@@ -714,7 +727,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) scan_kernel(const __grid_consta
             prefill::umma_ss(tmem + T_D4 + par * 32, al, bh, IDESC_K, acc);
           }
         prefill::umma_commit(&bar[B_D1 + par]);
-        ok = mbar_wait(&bar[B_UREADY], c & 1, 89) && !*abort_flag;
+        ok = mbar_wait(&bar[B_UDREADY], c & 1, 89) && !*abort_flag;
         if (!ok) break;
         prefill::tc_fence_after();
         // P2: D2 = K^T (Ud_hi + Ud_lo): A = the K tile [64 positions][128 keys] read as M = keys (MN-major: the two
@@ -726,6 +739,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) scan_kernel(const __grid_consta
           prefill::umma_ss(tmem + T_D2, a, prefill::sdesc(udlo + ks * 32, 16, 1024), IDESC_MN, 1u);
         }
         prefill::umma_commit(&bar[B_D2]);
+        ok = mbar_wait(&bar[B_UREADY], c & 1, 91) && !*abort_flag;
+        if (!ok) break;
+        prefill::tc_fence_after();
         // P3: D3[64:128] = M_hi (U_hi + U_lo) + M_lo U_hi; A rows 0-63 are whatever precedes (D3 rows 0-63 unused)
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
