@@ -69,6 +69,19 @@ int lb2_attn_prefill(const void* q, const int64_t* q_st, const void* k, const in
                      const uint8_t* mask, const int64_t* m_st, int B, int Hq, int Hkv, int T, int N, int D, int dtype,
                      float scale, int mask_kind, void* stream);
 
+/* The same prefill for an array mask, with tile skipping: the mask's kept tiles are listed first (for each block of
+ * query rows the kernel takes together -- 256 rows on CTA pairs, else 128 -- the key tiles holding a key one of its
+ * rows keeps), and the kernel reads only those tiles' K / V and issues only their products. Same result as
+ * lb2_attn_prefill with LB2_MASK_ARRAY (every element is still masked as given); the work falls with the mask's
+ * tile density. workspace: lb2_attn_prefill_tiled_workspace_size(T, N, D) bytes, 16-byte aligned, any contents.
+ * Replaces: qsa_tiles.chunked / tile_chunk (qsa_tiles.py:216-292), which run each 16-row group's products over only
+ * the 16-key tiles it keeps. */
+size_t lb2_attn_prefill_tiled_workspace_size(int T, int N, int D);
+int lb2_attn_prefill_tiled(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
+                           const int64_t* v_st, void* o, const int64_t* o_st, const void* gate, const int64_t* g_st,
+                           const uint8_t* mask, const int64_t* m_st, int B, int Hq, int Hkv, int T, int N, int D,
+                           int dtype, float scale, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------------------------------------------
  * Split-KV decode attention (few query rows over a long KV cache; HBM-bandwidth bound).
  *

@@ -23,6 +23,9 @@ SIGNATURES = {
     "lb2_status": ([_p], _i),
     "lb2_attn_prefill": ([_p, _i64p, _p, _i64p, _p, _i64p, _p, _i64p, _p, _i64p, _p, _i64p,
                           _i, _i, _i, _i, _i, _i, _i, _f, _i, _p], _i),
+    "lb2_attn_prefill_tiled_workspace_size": ([_i, _i, _i], _sz),
+    "lb2_attn_prefill_tiled": ([_p, _i64p, _p, _i64p, _p, _i64p, _p, _i64p, _p, _i64p, _p, _i64p,
+                                _i, _i, _i, _i, _i, _i, _i, _f, _p, _sz, _p], _i),
     "lb2_attn_decode_workspace_size": ([_i, _i, _i, _i, _i, _i, _i], _sz),
     "lb2_attn_decode": ([_p, _i64p, _p, _i64p, _p, _i64p, _p, _i64p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _i, _i,
                          _p, _sz, _p], _i),

@@ -68,7 +68,16 @@ struct Params {
   int mask_kind;
   int mtiles;  // ceil(T / BM)
   float scale_log2;
+  // Optional key-tile lists (array masks): row block m reads tl[m * tl_ld + 0 .. tn[m]) instead of every tile up to
+  // its horizon -- the tiles in which some row of the block keeps a key (a block is BM rows here, 2 BM rows in the
+  // CTA-pair kernel). NULL: every tile.
+  const int32_t* tl;
+  const int32_t* tn;
+  int tl_ld;
 };
+
+// The index of the j-th key tile row block m reads.
+__device__ __forceinline__ int key_tile(const Params& p, int m, int j) { return p.tl ? p.tl[int64_t(m) * p.tl_ld + j] : j; }
 
 // ---------------------------------------------------------------------------------------------- tcgen05 helpers
 
@@ -160,6 +169,7 @@ __device__ __forceinline__ float ex2f(float x) {
 template <int D>
 __device__ __forceinline__ int kv_tiles(const Params& p, int mt) {
   constexpr int BN = Cfg<D>::BN;
+  if (p.tn) return p.tn[mt];
   int last = p.N;  // keys [0, last) may be visible to some row of the tile
   if (p.mask_kind == LB2_MASK_CAUSAL) {
     const int rmax = min(p.T, (mt + 1) * BM) - 1;
@@ -266,7 +276,8 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_kernel(const __grid_constant_
         mbar_arrive_expect_tx(&fullb[st], C::KBYTES);
 #pragma unroll
         for (int db = 0; db < D / 64; ++db)
-          tma_load_4d(sm + off + st * C::KBYTES + db * BN * 128, map, db * 64, j * BN, hk, b, &fullb[st]);
+          tma_load_4d(sm + off + st * C::KBYTES + db * BN * 128, map, db * 64, key_tile(p, mt, j) * BN, hk, b,
+                      &fullb[st]);
         issued = j + 1;
       }
       // Drain: every load this lane issued has landed before the CTA may finish (already true normally).
@@ -385,8 +396,9 @@ __global__ void __launch_bounds__(THREADS, 1) fmha_kernel(const __grid_constant_
         for (int c = 0; c < HC; ++c) s[c] = -INFINITY;
       }
 
-      const int key0 = j * BN + hf * HC;
-      const bool full_tile = j * BN + BN - 1 <= lim && j * BN + BN <= p.N && !mrow;
+      const int kt = key_tile(p, mt, j);
+      const int key0 = kt * BN + hf * HC;
+      const bool full_tile = kt * BN + BN - 1 <= lim && kt * BN + BN <= p.N && !mrow;
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
       if (full_tile) {
 #pragma unroll

@@ -164,6 +164,7 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
 template <int D>
 __device__ __forceinline__ int kv_tiles2(const Params& p, int mt2) {
   constexpr int BN = Cfg<D>::BN;
+  if (p.tn) return p.tn[mt2];
   int last = p.N;
   if (p.mask_kind == LB2_MASK_CAUSAL) {
     const int rmax = min(p.T, (mt2 + 1) * 2 * BM) - 1;
@@ -175,7 +176,7 @@ __device__ __forceinline__ int kv_tiles2(const Params& p, int mt2) {
 // Work item k of a pass, heaviest first; heads vary fastest so that neighbouring clusters share their KV head's
 // tiles in L2: the 256-row pair mt2 of (batch, query head) b, h.
 struct Item {
-  int b, h, hk, r0, ntiles;
+  int b, h, hk, r0, ntiles, mt2;
 };
 
 template <int D>
@@ -188,6 +189,7 @@ __device__ __forceinline__ Item item_of(const Params& p, int k, uint32_t rank) {
   it.hk = it.h / p.G;
   it.r0 = mt2 * 2 * BM + int(rank) * BM;  // this CTA's first row
   it.ntiles = kv_tiles2<D>(p, mt2);
+  it.mt2 = mt2;
   return it;
 }
 
@@ -319,13 +321,13 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
             uint8_t* dst = sm + C::K_OFF + st * C::KHBYTES;
 #pragma unroll
             for (int db = 0; db < D / 64; ++db)
-              tma_load_4d_pair(dst + db * HN * 128, &kmap, db * 64, j * BN + int(rank) * HN, itm.hk, itm.b,
+              tma_load_4d_pair(dst + db * HN * 128, &kmap, db * 64, prefill::key_tile(p, itm.mt2, j) * BN + int(rank) * HN, itm.hk, itm.b,
                                &fullb[st]);
           } else {  // keys [j BN, + BN), columns [rank HD, + HD): HD / 64 boxes of (64, BN)
             uint8_t* dst = sm + C::V_OFF + st * C::VHBYTES;
 #pragma unroll
             for (int db = 0; db < HD / 64; ++db)
-              tma_load_4d_pair(dst + db * BN * 128, &vmap, int(rank) * HD + db * 64, j * BN, itm.hk, itm.b,
+              tma_load_4d_pair(dst + db * BN * 128, &vmap, int(rank) * HD + db * 64, prefill::key_tile(p, itm.mt2, j) * BN, itm.hk, itm.b,
                                &fullb[st]);
           }
         }
@@ -475,8 +477,9 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
 #pragma unroll
           for (int c = 0; c < HC; ++c) s[c] = -INFINITY;
         }
-        const int key0 = j * BN + grp * HC;
-        const bool full_tile = j * BN + BN - 1 <= lim && j * BN + BN <= p.N && !mrow;
+        const int kt = prefill::key_tile(p, itm.mt2, j);
+        const int key0 = kt * BN + grp * HC;
+        const bool full_tile = kt * BN + BN - 1 <= lim && kt * BN + BN <= p.N && !mrow;
         if (!full_tile) {
 #pragma unroll
           for (int c = 0; c < HC; ++c) {

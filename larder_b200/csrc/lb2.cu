@@ -19,6 +19,7 @@
 #include "qsa_select.cuh"
 #include "peer_xch.cuh"
 #include "kv_runs.cuh"
+#include "attn_tiles.cuh"
 #include "gdn_glue.cuh"
 
 namespace lb2 {
@@ -702,10 +703,29 @@ int lb2_attn_combine_peers(const uint64_t* bufs, int R, int rank, uint32_t epoch
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-int lb2_attn_prefill(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
-                     const int64_t* v_st, void* o, const int64_t* o_st, const void* gate, const int64_t* g_st,
-                     const uint8_t* mask, const int64_t* m_st, int B, int Hq, int Hkv, int T, int N, int D, int dtype,
-                     float scale, int mask_kind, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// The prefill on the kernel its shape takes: CTA pairs for head dims 128 / 256 over more than one row tile, else the
+// single-CTA kernel. `tiled`: the array mask's kept-tile lists are built in `ws` first and the kernel reads only
+// those tiles.
+bool prefill_pair(int D, int T) { return (D == 128 || D == 256) && T > prefill::BM; }
+int prefill_rows(int D, int T) { return prefill_pair(D, T) ? 2 * prefill::BM : prefill::BM; }
+int prefill_bn(int D, int T) {
+  return prefill_pair(D, T) ? prefill2::Cfg<256>::BN : D == 256 ? prefill::Cfg<256>::BN
+                                                     : D == 128 ? prefill::Cfg<128>::BN : prefill::Cfg<64>::BN;
+}
+size_t tiles_bytes(int T, int N, int D) {
+  const int64_t nrb = (T + prefill_rows(D, T) - 1) / prefill_rows(D, T), nkt = (N + prefill_bn(D, T) - 1) /
+                                                                              prefill_bn(D, T);
+  return size_t((nrb * nkt + 255) / 256 * 256 + nrb * nkt * 4 + nrb * 4 + 256);
+}
+
+int prefill_run(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
+                const int64_t* v_st, void* o, const int64_t* o_st, const void* gate, const int64_t* g_st,
+                const uint8_t* mask, const int64_t* m_st, int B, int Hq, int Hkv, int T, int N, int D, int dtype,
+                float scale, int mask_kind, bool tiled, void* ws, size_t ws_bytes, void* stream) {
   LB2_CHECK_ARG(B > 0 && Hq > 0 && Hkv > 0 && T > 0 && N > 0, "prefill: empty shape");
   LB2_CHECK_ARG(Hq % Hkv == 0, "prefill: Hq must be a multiple of Hkv");
   if (dtype == LB2_F32)  // exact fp32 on CUDA cores (the tensor-core kernel takes 16-bit operands)
@@ -752,6 +772,22 @@ int lb2_attn_prefill(const void* q, const int64_t* q_st, const void* k, const in
   p.mtiles = pair ? (T + 2 * prefill::BM - 1) / (2 * prefill::BM) : (T + prefill::BM - 1) / prefill::BM;
   p.scale_log2 = scale * 1.4426950408889634f;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (tiled && p.mask) {
+    LB2_CHECK_ARG(ws != nullptr && ws_bytes >= tiles_bytes(T, N, D) && (reinterpret_cast<uintptr_t>(ws) & 15) == 0,
+                  "prefill_tiled: workspace too small or not 16-byte aligned");
+    const int RB = prefill_rows(D, T), TBN = prefill_bn(D, T);
+    const int nrb = (T + RB - 1) / RB, nkt = (N + TBN - 1) / TBN;
+    uint8_t* flags = static_cast<uint8_t*>(ws);
+    int32_t* list = reinterpret_cast<int32_t*>(flags + (int64_t(nrb) * nkt + 255) / 256 * 256);
+    int32_t* count = list + int64_t(nrb) * nkt;
+    tiles::flag_kernel<<<dim3(unsigned(nkt), unsigned(nrb)), 256, 0, st>>>(mask, m_st[0], m_st[1], T, N, RB, TBN,
+                                                                             nkt, flags);
+    tiles::compact_kernel<<<unsigned((nrb + 3) / 4), 128, 0, st>>>(flags, nrb, nkt, list, count);
+    LB2_CUDA(cudaGetLastError());
+    p.tl = list;
+    p.tn = count;
+    p.tl_ld = nkt;
+  }
   if (pair) {
     if (D == 128)
       return dtype == LB2_BF16 ? prefill2::launch<__nv_bfloat16, 128>(qm, km, vm, p, st)
@@ -767,6 +803,32 @@ int lb2_attn_prefill(const void* q, const int64_t* q_st, const void* k, const in
   if (D == 64) return prefill::launch<__half, 64>(qm, km, vm, p, st);
   if (D == 128) return prefill::launch<__half, 128>(qm, km, vm, p, st);
   return prefill::launch<__half, 256>(qm, km, vm, p, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int lb2_attn_prefill(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
+                     const int64_t* v_st, void* o, const int64_t* o_st, const void* gate, const int64_t* g_st,
+                     const uint8_t* mask, const int64_t* m_st, int B, int Hq, int Hkv, int T, int N, int D, int dtype,
+                     float scale, int mask_kind, void* stream) {
+  return prefill_run(q, q_st, k, k_st, v, v_st, o, o_st, gate, g_st, mask, m_st, B, Hq, Hkv, T, N, D, dtype, scale,
+                     mask_kind, false, nullptr, 0, stream);
+}
+
+size_t lb2_attn_prefill_tiled_workspace_size(int T, int N, int D) {
+  if (T <= 0 || N <= 0) return 0;
+  return tiles_bytes(T, N, D);
+}
+
+int lb2_attn_prefill_tiled(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
+                           const int64_t* v_st, void* o, const int64_t* o_st, const void* gate, const int64_t* g_st,
+                           const uint8_t* mask, const int64_t* m_st, int B, int Hq, int Hkv, int T, int N, int D,
+                           int dtype, float scale, void* workspace, size_t workspace_bytes, void* stream) {
+  LB2_CHECK_ARG(mask != nullptr && m_st != nullptr, "prefill_tiled: an array mask is required");
+  return prefill_run(q, q_st, k, k_st, v, v_st, o, o_st, gate, g_st, mask, m_st, B, Hq, Hkv, T, N, D, dtype, scale,
+                     LB2_MASK_ARRAY, true, workspace, workspace_bytes, stream);
 }
 
 size_t lb2_gdn_chunked_workspace_size(int B, int T, int Hk, int Hv, int Dk, int Dv) {

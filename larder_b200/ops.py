@@ -107,6 +107,36 @@ def attn_prefill(q, k, v, scale, mask=None, gate=None, out=None):
     return out
 
 
+def attn_prefill_tiled(q, k, v, scale, mask, gate=None, out=None):
+    """attn_prefill with a bool array mask [..., T, N] and tile skipping: only the key tiles that some row of a row
+    block keeps are read and multiplied (lb2_attn_prefill_tiled). Same result as attn_prefill(..., mask)."""
+    _cuda(q, k, v, gate, mask)
+    for t, n in ((q, "q"), (k, "k"), (v, "v")):
+        _unit_last(t, n)
+    B, Hq, T, D = q.shape
+    Hkv, N = k.shape[1], k.shape[2]
+    if k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("q, k, v must share a dtype")
+    if mask.dtype != torch.bool or tuple(mask.shape[-2:]) != (T, N) or any(d != 1 for d in mask.shape[:-2]):
+        raise ValueError("array masks must be bool [..., T, N] with leading dims of 1")
+    m = mask.reshape(T, N).to(torch.uint8)
+    if out is None:
+        out = torch.empty((B, Hq, T, D), dtype=q.dtype, device=q.device)
+    gst = i64(0, 0, 0)
+    if gate is not None:
+        if gate.shape != (B, Hq, T, D) or gate.dtype != q.dtype:
+            raise ValueError("gate must be [B, Hq, T, D] in q's dtype")
+        _unit_last(gate, "gate")
+        gst = i64(*gate.stride()[:3])
+    ws = workspace(q.device, lib().lb2_attn_prefill_tiled_workspace_size(T, N, D), "prefill_tiled")
+    rc = lib().lb2_attn_prefill_tiled(_ptr(q), i64(*q.stride()[:3]), _ptr(k), i64(*k.stride()[:3]), _ptr(v),
+                                      i64(*v.stride()[:3]), _ptr(out), i64(*out.stride()[:3]), _ptr(gate), gst,
+                                      _ptr(m), i64(m.stride(0), m.stride(1)), B, Hq, Hkv, T, N, D, dtype_code(q),
+                                      float(scale), _ptr(ws), ws.numel(), _stream(q))
+    check(rc, "attn_prefill_tiled")
+    return out
+
+
 def decode_rows_limit(D):
     """Folded rows (G*T) the split-KV decode kernel takes at head dim D."""
     return 16 if D == 256 else 32

@@ -84,3 +84,20 @@ def test_install_glue_leaves_other_calls_on_the_layer():
 def test_install_glue_needs_a_class_when_mlx_lm_is_absent():
     with pytest.raises(ValueError, match="GatedDeltaNet class"):
         gdn_cuda.install_glue()
+
+
+def test_qsa_tiles_install_is_off_unless_asked():
+    from larder_b200 import chunkattn, ops, qsa_tiles
+    assert not qsa_tiles.install(on=False)
+    assert chunkattn.chunked is not qsa_tiles.chunked and chunkattn.array_prefill is ops.attn_prefill
+
+
+def test_qsa_tiles_flags_and_plan_on_cpu_tensors():
+    from larder_b200 import qsa_tiles
+    m = torch.zeros(300, 700, dtype=torch.bool)
+    m[10, 5] = True       # row block 0 (256 rows at D=256), key tile 0 (128 keys)
+    m[299, 699] = True    # row block 1, key tile 5
+    f = qsa_tiles.group_flags(m, 256)
+    assert f.shape == (2, 6) and f.sum().item() == 2 and f[0, 0] and f[1, 5]
+    assert qsa_tiles.plan(f) == [(0, [0]), (1, [5])]
+    assert qsa_tiles.tile_shape(100, 256) == (128, 64) and qsa_tiles.tile_shape(300, 64) == (128, 128)
