@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Benchmark of the attention / Gated-DeltaNet hot path on B200, one JSON line on rank 0.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--section decode,prefill,gdn,sharded,glue,qsa]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--section decode,prefill,gdn,sharded,glue,qsa,tiles]
 
 Headline (`value`): decode KV-read GB/s on BASELINE.json's configs[1] -- batch 16, 32 query / 4 KV heads x 128,
 bf16 KV cache with per-sequence lengths uniform in [1024, 8192], one query token each. A step is one split-KV decode
@@ -200,6 +200,12 @@ def run_ours(args):
             out["qsa"] = bench_qsa(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_over_ranks)
         except Exception as e:
             out["qsa"] = {"error": f"{type(e).__name__}: {e}"}
+    if "tiles" in sections:
+        try:
+            out["qsa_tiles"] = bench_tiles(torch, ops, dev, rank, world, args, stream, pk, barrier_sync,
+                                           reduce_over_ranks)
+        except Exception as e:
+            out["qsa_tiles"] = {"error": f"{type(e).__name__}: {e}"}
     if "glue" in sections:
         try:
             out["glue"] = bench_glue(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_over_ranks)
@@ -494,6 +500,55 @@ def bench_qsa(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": round(gbs / pk["hbm_gbs"], 4),
                          "kernel": "lb2::qsasel::score_kernel<128> + topk_kernel<16>"}}
+
+
+def bench_tiles(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, reduce_over_ranks):
+    """Array-masked prefill with tile skipping (qsa_tiles.py's role) at Flash-Next's attention shape (24q/2kv x 256):
+    one 2048-row chunk over 16384 keys, masks of falling density -- the causal rule alone, QSA-style masks (a
+    64-key local window plus randomly picked 16-key blocks per 16-row group) and tile-aligned random 128 x 128 blocks.
+    Time of the tile-skipping kernel (lb2_attn_prefill_tiled, its listing pass included) beside the masked kernel
+    that visits every tile (lb2_attn_prefill, array mask); TFLOP/s over the kept (row, key) pairs."""
+    from larder_b200 import qsa_tiles
+    g = torch.Generator(device=dev).manual_seed(9000 + rank)
+    Hq, Hkv, D, T, N = 24, 2, 256, 2048, 16384
+    q = torch.randn(1, Hq, T, D, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn(1, Hkv, N, D, generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn(1, Hkv, N, D, generator=g, device=dev).to(torch.bfloat16)
+    r = torch.arange(T, device=dev)[:, None]
+    c = torch.arange(N, device=dev)[None, :]
+    causal = c <= N - T + r
+    cases = [("causal", causal)]
+    for dens in (0.05, 0.01):
+        picks = torch.rand(T // 16, N // 16, generator=g, device=dev) < dens
+        blocks = picks.repeat_interleave(16, 0).repeat_interleave(16, 1)
+        cases.append((f"qsa blocks {dens}", causal & ((c > N - T + r - 64) | blocks)))
+    for dens in (0.25, 0.1):
+        picks = torch.rand(T // 256, N // 128, generator=g, device=dev) < dens
+        blocks = picks.repeat_interleave(256, 0).repeat_interleave(128, 1)
+        cases.append((f"tiles {dens}", causal & ((c > N - T + r - 64) | blocks)))
+    res = {}
+    for name, m in cases:
+        kept = int(m.sum())
+        tile_density = float(qsa_tiles.group_flags(m, D).float().mean())
+
+        def tiled(i, m=m):
+            ops.attn_prefill_tiled(q, k, v, D ** -0.5, m)
+
+        def dense(i, m=m):
+            ops.attn_prefill(q, k, v, D ** -0.5, m)
+
+        for i in range(args.warmup):
+            tiled(i)
+            dense(i)
+        barrier_sync()
+        ms_t = reduce_over_ranks(cuda_time(torch, tiled, args.steps, stream), "max") / args.steps
+        ms_d = reduce_over_ranks(cuda_time(torch, dense, args.steps, stream), "max") / args.steps
+        res[name] = {"tile_density": round(tile_density, 4), "kept_pairs": kept, "tiled_ms": round(ms_t, 4),
+                     "masked_ms": round(ms_d, 4),
+                     "tiled_tflops_kept": round(4.0 * D * Hq * kept / (ms_t * 1e-3) / 1e12, 1)}
+    res["workload"] = "24q/2kv x 256, bf16, one 2048-row chunk over 16384 keys (the last chunk of a 16k prompt)"
+    res["gpu_launches_per_step"] = 3
+    return res
 
 
 def bench_glue(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_over_ranks):
@@ -808,7 +863,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--section", default="decode,prefill,gdn,sharded,glue,qsa")
+    ap.add_argument("--section", default="decode,prefill,gdn,sharded,glue,qsa,tiles")
     ap.add_argument("--split", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()

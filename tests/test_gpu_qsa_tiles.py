@@ -55,8 +55,8 @@ def test_tiled_matches_oracle_and_masked_kernel(Hq, Hkv, D, T, N, density):
                       out_dt=oracle.F32)
     checks.grading_close(f32(out), ref, what=f"tiled {Hq}/{Hkv}x{D} T={T} N={N}")
     assert not f32(out)[0, :, 3].any(), "a row that keeps nothing gives zeros"
-    flags = qsa_tiles.group_flags(m, D)
-    assert flags.float().mean().item() < 1.0  # tiles were skipped
+    if density <= 0.05:  # sparse enough that whole tiles were skipped
+        assert qsa_tiles.group_flags(m, D).float().mean().item() < 1.0
 
 
 def test_whole_row_blocks_without_keys_and_the_gate():
