@@ -386,6 +386,8 @@ def bench_sharded(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, 
     prefills (32q/4kv x 128), and a batch-64 decode over this rank's 4096-key range of every sequence merged across
     ranks (NCCL all-gather of packed (o, lse), then the log-sum-exp combine; at N > 1 also over NVLink peer
     memory, `decode_peer`). At 8 GPUs that is configs[4]."""
+    import torch.distributed as dist
+
     from larder_b200 import sharded
 
     def max_over_ranks(x):
@@ -428,6 +430,51 @@ def bench_sharded(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, 
     barrier_sync()
     ms_d = max_over_ranks(cuda_time(torch, dec, args.steps, stream)) / args.steps
     kv_bytes = B * n_local * Hkv * D * 2 * 2
+    breakdown = split = None
+    if world > 1:
+        # where a step's time goes, each part timed alone on every rank (min and max over ranks): this rank's partial,
+        # the all-gather of the packed partials, the merge; then the split merge (all-to-all, 1/R of the rows a rank,
+        # all-gather of the merged rows), checked against the all-gather path first
+        rows = B * Hq
+        packed = torch.empty(rows * (D + 1), dtype=torch.float32, device=dev)
+        gathered = torch.empty(world * rows * (D + 1), dtype=torch.float32, device=dev)
+
+        def part(i):
+            kk, vv = kvs[i % copies]
+            ops.attn_decode_partial(dq, kk, vv, D ** -0.5,
+                                    out=(packed[:rows * D].view(B, Hq, 1, D), packed[rows * D:].view(B, Hq, 1)))
+
+        def gath(i):
+            dist.all_gather_into_tensor(gathered, packed)
+
+        def comb(i):
+            ops.attn_combine_packed(gathered.view(world, -1), world, B, Hq, 1, D, torch.bfloat16)
+
+        breakdown = {}
+        for name, fn in (("partial", part), ("all_gather", gath), ("combine", comb)):
+            for i in range(args.warmup):
+                fn(i)
+            barrier_sync()
+            t = cuda_time(torch, fn, args.steps, stream) / args.steps
+            breakdown[name] = {"ms_min": round(reduce_over_ranks(t, "min"), 5),
+                               "ms_max": round(reduce_over_ranks(t, "max"), 5)}
+        kk, vv = kvs[0]
+        same = torch.equal(sharded.kv_sharded_decode_split(dq, kk, vv, D ** -0.5),
+                           sharded.kv_sharded_decode(dq, kk, vv, D ** -0.5))
+
+        def dec_split(i):
+            kk, vv = kvs[i % copies]
+            sharded.kv_sharded_decode_split(dq, kk, vv, D ** -0.5)
+
+        for i in range(args.warmup):
+            dec_split(i)
+        barrier_sync()
+        ms_s = max_over_ranks(cuda_time(torch, dec_split, args.steps, stream)) / args.steps
+        split = {"value": round(world * kv_bytes / (ms_s * 1e-3) / 1e9, 1), "unit": "GB/s",
+                 "ms_per_step": round(ms_s, 5), "ranks_bit_equal_to_all_gather_path": int(reduce_over_ranks(
+                     float(same), "sum")),
+                 "per_rank": f"B=64 x {n_local} local keys; all-to-all of 1/R of the partials, merge of B/R "
+                             "sequences, all-gather of the merged rows"}
     peer = None
     if world > 1:  # the same decode with the exchange over NVLink peer memory (no collective on the data path)
         xch = sharded.PeerExchange(B, Hq, 1, D)
@@ -468,7 +515,7 @@ def bench_sharded(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, 
                        "roofline": {"bound": "hbm", "achieved": round(kv_bytes / (ms_d * 1e-3) / 1e9, 1),
                                     "peak": pk["hbm_gbs"], "frac": round(kv_bytes / (ms_d * 1e-3) / 1e9 /
                                                                          pk["hbm_gbs"], 4)}},
-            "decode_peer": peer,
+            "decode_peer": peer, "decode_split": split, "decode_breakdown": breakdown,
             "scaling": "weak", "workload": "configs[4] share of one rank (exactly configs[4] at 8 GPUs)"}
 
 

@@ -84,6 +84,39 @@ def kv_sharded_decode(q, k_local, v_local, scale, kv_len_local=None, group=None,
     return combine_fn(gathered.view(world, rows * (D + 1)), (B, Hq, T, D), out_dtype or q.dtype)
 
 
+def _cuda_merge(part_o, part_lse, dtype):
+    return ops.attn_combine(part_o, part_lse, dtype)
+
+
+def kv_sharded_decode_split(q, k_local, v_local, scale, kv_len_local=None, group=None, partial_fn=None,
+                            merge_fn=None, out_dtype=None):
+    """kv_sharded_decode with the merge split by sequences instead of repeated on every rank: rank r merges only the
+    sequences [r B / R, (r + 1) B / R) (the same log-sum-exp merge), then the merged rows are all-gathered. The
+    exchange is an all-to-all of the partials (each rank receives 1/R of every peer's partial: about
+    B Hq T (D + 1) 4 (R - 1) / R bytes, against (R - 1) times the whole partial for the all-gather) and an all-gather
+    of the output rows in q's dtype. B must be a multiple of the group's size. `partial_fn` as kv_sharded_decode's;
+    `merge_fn(part_o [R, B / R, Hq, T, D], part_lse [R, B / R, Hq, T], dtype)` defaults to lb2_attn_combine."""
+    partial_fn = partial_fn or _cuda_partial
+    merge_fn = merge_fn or _cuda_merge
+    world = dist.get_world_size(group)
+    B, Hq, T, D = q.shape
+    if B % world:
+        raise ValueError("kv_sharded_decode_split: the batch must be a multiple of the ranks")
+    rows = B * Hq * T
+    part_o = torch.empty(rows * D, dtype=torch.float32, device=q.device)
+    part_lse = torch.empty(rows, dtype=torch.float32, device=q.device)
+    partial_fn(q, k_local, v_local, scale, kv_len_local, part_o.view(B, Hq, T, D), part_lse.view(B, Hq, T))
+    got_o = torch.empty_like(part_o)
+    got_lse = torch.empty_like(part_lse)
+    dist.all_to_all_single(got_o, part_o, group=group)      # block r of each rank: the sequences rank r merges
+    dist.all_to_all_single(got_lse, part_lse, group=group)
+    b = B // world
+    mine = merge_fn(got_o.view(world, b, Hq, T, D), got_lse.view(world, b, Hq, T), out_dtype or q.dtype)
+    o = torch.empty((B, Hq, T, D), dtype=mine.dtype, device=q.device)
+    dist.all_gather_into_tensor(o, mine, group=group)
+    return o
+
+
 def sharded_prefill(q, k, v, scale, mask="causal", gate=None, rank=None, world=None):
     """Prefill of a batch of independent sequences, this rank's share only: q [B, Hq, T, D], k / v [B, Hkv, N, D]
     (the whole batch's views; only this rank's rows are read). Returns (start, stop, o_local)."""

@@ -198,3 +198,43 @@ def test_peer_exchange_setup_all_or_nothing(fail_rank):
             assert status == "raised" and "could not map" in info
             assert calls[-1] == ("free", base)
             assert (("close", 0x900000 + (1 - rank)) in calls) == (rank != fail_rank)
+
+
+
+def _split_worker(rank, world, port, q, k, v, scale, result_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=__import__("datetime").timedelta(seconds=30))
+    try:
+        s0, s1 = sharded.kv_range(k.shape[2], rank, world)
+
+        def merge(po, pl, dtype):
+            w = torch.softmax(pl, dim=0)
+            return (w[..., None] * po).sum(0).to(dtype)
+        o = sharded.kv_sharded_decode_split(q, k[:, :, s0:s1], v[:, :, s0:s1], scale, partial_fn=_oracle_partial,
+                                            merge_fn=merge, out_dtype=torch.float32)
+        result_q.put((rank, o.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_split_merge_two_gloo_ranks_equals_whole():
+    """The split merge's plumbing (all-to-all of the partials, each rank merging B / R sequences, all-gather of the
+    merged rows) on two CPU ranks, the f64 partial and a torch merge in place of the CUDA kernels."""
+    g = torch.Generator().manual_seed(6)
+    B, Hq, Hkv, D, N = 4, 4, 2, 64, 200
+    q = torch.randn(B, Hq, 1, D, generator=g)
+    k = torch.randn(B, Hkv, N, D, generator=g)
+    v = torch.randn(B, Hkv, N, D, generator=g)
+    ctx = mp.get_context("spawn")
+    rq = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_split_worker, args=(r, 2, port, q, k, v, D ** -0.5, rq)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [rq.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    ref = oracle.attn_ref64(q.numpy(), k.numpy(), v.numpy(), D ** -0.5)
+    for rank, o in res:
+        assert np.abs(o - ref).max() < 1e-4, rank
