@@ -480,15 +480,7 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
         const int kt = prefill::key_tile(p, itm.mt2, j);
         const int key0 = kt * BN + grp * HC;
         const bool full_tile = kt * BN + BN - 1 <= lim && kt * BN + BN <= p.N && !mrow;
-        if (!full_tile) {
-#pragma unroll
-          for (int c = 0; c < HC; ++c) {
-            const int key = key0 + c;
-            bool vis = key <= lim && key < p.N;
-            if (mrow && vis) vis = mrow[int64_t(key) * p.m_st[1]] != 0;
-            s[c] = vis ? s[c] : -INFINITY;
-          }
-        }
+        if (!full_tile) prefill::mask_scores<HC>(s, mrow, p.m_st[1], key0, lim, p.N);
         // P_j with the running max. The running max moves only when a row's tile max exceeds it by more than 2^8,
         // i.e. when some P of the row exceeds 2^8; P >= 0, so a thread whose P sum is at most 2^8 has no such
         // element and skips the max altogether. Otherwise (or before the row's first key) the exact check below
