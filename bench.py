@@ -475,7 +475,7 @@ def bench_sharded(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, 
                      float(same), "sum")),
                  "per_rank": f"B=64 x {n_local} local keys; all-to-all of 1/R of the partials, merge of B/R "
                              "sequences, all-gather of the merged rows"}
-    peer = None
+    peer = push = None
     if world > 1:  # the same decode with the exchange over NVLink peer memory (no collective on the data path)
         xch = sharded.PeerExchange(B, Hq, 1, D)
         try:
@@ -501,6 +501,27 @@ def bench_sharded(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, 
                     "ranks_bit_equal_to_nccl_path": ranks_equal}
         finally:
             xch.close()
+        xch = sharded.PeerExchange(B, Hq, 1, D, push=True)
+        try:  # the push form: partials stored into every rank's buffer by the decode, the merge reads local memory
+            kk, vv = kvs[0]
+            same = torch.equal(xch.decode(dq, kk, vv, D ** -0.5), sharded.kv_sharded_decode(dq, kk, vv, D ** -0.5))
+
+            def dec_push(i):
+                kk, vv = kvs[i % copies]
+                xch.decode(dq, kk, vv, D ** -0.5)
+
+            for i in range(args.warmup):
+                dec_push(i)
+            barrier_sync()
+            ms_pp = max_over_ranks(cuda_time(torch, dec_push, args.steps, stream)) / args.steps
+            push = {"value": round(world * kv_bytes / (ms_pp * 1e-3) / 1e9, 1), "unit": "GB/s",
+                    "ms_per_step": round(ms_pp, 5),
+                    "per_rank": f"B=64 x {n_local} local keys; the decode's epilogue stores the partial into every "
+                                "rank's exchange buffer over NVLink, the merge reads local memory",
+                    "kernel": "lb2::decode::decode_kernel (push) + lb2::xch::peer_combine_kernel (pushed)",
+                    "ranks_bit_equal_to_nccl_path": int(reduce_over_ranks(float(same), "sum"))}
+        finally:
+            xch.close()
     return {"prefill": {"value": round(world * flop / (ms_p * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                         "ms_per_step": round(ms_p, 4), "per_rank": "8 x 8192 causal, 32q/4kv x 128, bf16",
                         "roofline": {"bound": "tensor", "achieved": round(flop / (ms_p * 1e-3) / 1e12, 2),
@@ -515,7 +536,7 @@ def bench_sharded(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, 
                        "roofline": {"bound": "hbm", "achieved": round(kv_bytes / (ms_d * 1e-3) / 1e9, 1),
                                     "peak": pk["hbm_gbs"], "frac": round(kv_bytes / (ms_d * 1e-3) / 1e9 /
                                                                          pk["hbm_gbs"], 4)}},
-            "decode_peer": peer, "decode_split": split, "decode_breakdown": breakdown,
+            "decode_peer": peer, "decode_push": push, "decode_split": split, "decode_breakdown": breakdown,
             "scaling": "weak", "workload": "configs[4] share of one rank (exactly configs[4] at 8 GPUs)"}
 
 

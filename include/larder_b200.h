@@ -185,6 +185,20 @@ int lb2_xch_close(void* ptr);
 int lb2_attn_combine_peers(const uint64_t* bufs, int R, int rank, uint32_t epoch, int B, int Hq, int T, int D, void* o,
                            const int64_t* o_st, int dtype, void* stream);
 
+/* The same exchange in push form (no counterpart in the reference either): every rank's buffer holds all R partials
+ * (lb2_xch_push_bytes(R, B, Hq, T, D) bytes, from lb2_xch_alloc, shared as above). Call e = 1, 2, ... of a rank:
+ * lb2_attn_decode_push computes this rank's range partial and its epilogue stores it straight into slot `rank` of
+ * half e % 2 of EVERY rank's buffer (bufs: the R buffers as mapped here; peer stores over NVLink, fenced at system
+ * scope), then lb2_attn_combine_pushed publishes e, waits (bounded, 2 s) for every peer's e and merges the R slots of
+ * its OWN buffer, so the merge reads local memory only. kv_len / workspace / split as lb2_attn_decode_partial. */
+size_t lb2_xch_push_bytes(int R, int B, int Hq, int T, int D);
+int lb2_attn_decode_push(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
+                         const int64_t* v_st, const int32_t* kv_len, int B, int Hq, int Hkv, int T, int N, int D,
+                         int dtype, float scale, int split, void* workspace, size_t workspace_bytes,
+                         const uint64_t* bufs, int R, int rank, uint32_t epoch, void* stream);
+int lb2_attn_combine_pushed(const uint64_t* bufs, int R, int rank, uint32_t epoch, int B, int Hq, int T, int D, void* o,
+                            const int64_t* o_st, int dtype, void* stream);
+
 /* ------------------------------------------------------------------------------------------------------------
  * Gated-DeltaNet recurrence, one position at a time (decode steps, short verify passes).
  *

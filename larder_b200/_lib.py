@@ -52,6 +52,10 @@ SIGNATURES = {
     "lb2_xch_open": ([_p, ctypes.POINTER(ctypes.c_void_p)], _i),
     "lb2_xch_close": ([_p], _i),
     "lb2_attn_combine_peers": ([_p, _i, _i, ctypes.c_uint32, _i, _i, _i, _i, _p, _i64p, _i, _p], _i),
+    "lb2_xch_push_bytes": ([_i, _i, _i, _i, _i], _sz),
+    "lb2_attn_decode_push": ([_p, _i64p, _p, _i64p, _p, _i64p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _i, _p, _sz, _p,
+                              _i, _i, ctypes.c_uint32, _p], _i),
+    "lb2_attn_combine_pushed": ([_p, _i, _i, ctypes.c_uint32, _i, _i, _i, _i, _p, _i64p, _i, _p], _i),
     "lb2_kvh_lru_plan": ([_p, _i, _p, _i, _p, _p, _p, _p, _i, _p, _p], _i),
     "lb2_kvh_lru_gather": ([_p, _p, _i, _p, _p, _i, _i, _i, _p, _i64p, _p, _i64p, _p, _p, _i, _i, _i, _i, _p], _i),
     "lb2_kvh_lru_inval": ([_p, _p, _p, _i, _i, _p], _i),

@@ -74,6 +74,11 @@ struct Params {
   int grid;         // CTAs of the decode grid (the balanced schedule's run count)
   int causal, emit;
   float scale_log2;  // softmax scale * log2(e)
+  // push mode (npush > 0): the emitted partial goes to npush places at once -- this rank's slot in every rank's
+  // exchange buffer, peers' through NVLink -- instead of part_o / part_lse (same offsets in each)
+  int npush;
+  float* push_o[8];
+  float* push_lse[8];
 };
 
 template <typename T>
@@ -685,8 +690,17 @@ __global__ void __launch_bounds__(256) split_combine_kernel(const Params p) {
       const float4 v = make_float4(acc[j].x * inv, acc[j].y * inv, acc[j].z * inv, acc[j].w * inv);
       if (p.emit) {
         const size_t ro = (size_t(b) * p.Hq + h) * p.T + t;
-        reinterpret_cast<float4*>(p.part_o + ro * D)[c] = v;
-        if (c == 0) p.part_lse[ro] = L > 0.f ? (M + __log2f(L)) * 0.69314718055994531f : -INFINITY;
+        const float lse = L > 0.f ? (M + __log2f(L)) * 0.69314718055994531f : -INFINITY;
+        if (p.npush) {
+#pragma unroll 1
+          for (int i = 0; i < p.npush; ++i) {
+            reinterpret_cast<float4*>(p.push_o[i] + ro * D)[c] = v;
+            if (c == 0) p.push_lse[i][ro] = lse;
+          }
+        } else {
+          reinterpret_cast<float4*>(p.part_o + ro * D)[c] = v;
+          if (c == 0) p.part_lse[ro] = lse;
+        }
       } else {
         T* dst = reinterpret_cast<T*>(p.o) + b * p.o_st[0] + int64_t(h) * p.o_st[1] + int64_t(t) * p.o_st[2] + 4 * c;
         dst[0] = from_f<T>(v.x);
@@ -695,6 +709,7 @@ __global__ void __launch_bounds__(256) split_combine_kernel(const Params p) {
         dst[3] = from_f<T>(v.w);
       }
     }
+    if (p.npush) __threadfence_system();  // the pushed rows reach the peers before this rank publishes its call
   }
 }
 

@@ -209,7 +209,8 @@ static int kv_map(CUtensorMap* m, const void* base, const int64_t* st, int B, in
 static int run(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
                const int64_t* v_st, void* o, const int64_t* o_st, float* part_o, float* part_lse,
                const int32_t* kv_len, int B, int Hq, int Hkv, int T, int N, int D, int dtype, float scale, int causal,
-               int split, void* workspace, size_t workspace_bytes, void* stream) {
+               int split, void* workspace, size_t workspace_bytes, void* stream, int npush = 0,
+               float* const* push_o = nullptr, float* const* push_lse = nullptr) {
   LB2_CHECK_ARG(B > 0 && Hq > 0 && Hkv > 0 && T > 0 && N > 0, "decode: empty shape");
   LB2_CHECK_ARG(Hq % Hkv == 0, "decode: Hq must be a multiple of Hkv");
   LB2_CHECK_ARG(D == 64 || D == 128 || D == 256, "decode: head dim must be 64, 128 or 256");
@@ -245,7 +246,12 @@ static int run(const void* q, const int64_t* q_st, const void* k, const int64_t*
   p.o = o;
   p.part_o = part_o;
   p.part_lse = part_lse;
-  p.emit = part_o != nullptr;
+  p.emit = part_o != nullptr || npush > 0;
+  p.npush = npush;
+  for (int i = 0; i < npush; ++i) {
+    p.push_o[i] = push_o[i];
+    p.push_lse[i] = push_lse[i];
+  }
   p.kv_len = kv_len;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   p.ws_ml = reinterpret_cast<float*>(ws + w.ml);
@@ -697,6 +703,70 @@ int lb2_attn_combine_peers(const uint64_t* bufs, int R, int rank, uint32_t epoch
     xch::peer_combine_kernel<float><<<grid, warps * 32, 0, st>>>(p);
   else
     return fail(LB2_EINVAL, "combine_peers: dtype");
+  LB2_CUDA(cudaGetLastError());
+  return LB2_OK;
+}
+
+size_t lb2_xch_push_bytes(int R, int B, int Hq, int T, int D) {
+  if (R < 1 || R > xch::XCH_MAX_RANKS || B <= 0 || Hq <= 0 || T <= 0 || D <= 0) return 0;
+  const int64_t half = int64_t(R) * B * Hq * T * (D + 1);
+  return size_t(xch::flags_offset(half) * 4 + xch::XCH_MAX_RANKS * 4);
+}
+
+int lb2_attn_decode_push(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
+                         const int64_t* v_st, const int32_t* kv_len, int B, int Hq, int Hkv, int T, int N, int D,
+                         int dtype, float scale, int split, void* workspace, size_t workspace_bytes,
+                         const uint64_t* bufs, int R, int rank, uint32_t epoch, void* stream) {
+  LB2_CHECK_ARG(R >= 1 && R <= xch::XCH_MAX_RANKS && rank >= 0 && rank < R, "decode_push: 1 to 8 ranks");
+  LB2_CHECK_ARG(epoch > 0, "decode_push: calls count from 1");
+  const int64_t rows = int64_t(B) * Hq * T, slot = rows * (D + 1), half = R * slot;
+  float* po[xch::XCH_MAX_RANKS];
+  float* pl[xch::XCH_MAX_RANKS];
+  for (int r = 0; r < R; ++r) {
+    LB2_CHECK_ARG(bufs[r] != 0 && (bufs[r] & 15) == 0, "decode_push: a rank's buffer is missing or misaligned");
+    po[r] = reinterpret_cast<float*>(bufs[r]) + int64_t(epoch & 1u) * half + rank * slot;
+    pl[r] = po[r] + rows * D;
+  }
+  return decode::run(q, q_st, k, k_st, v, v_st, nullptr, nullptr, nullptr, nullptr, kv_len, B, Hq, Hkv, T, N, D, dtype,
+                     scale, 0, split, workspace, workspace_bytes, stream, R, po, pl);
+}
+
+int lb2_attn_combine_pushed(const uint64_t* bufs, int R, int rank, uint32_t epoch, int B, int Hq, int T, int D, void* o,
+                            const int64_t* o_st, int dtype, void* stream) {
+  LB2_CHECK_ARG(R >= 1 && R <= xch::XCH_MAX_RANKS && rank >= 0 && rank < R, "combine_pushed: 1 to 8 ranks");
+  LB2_CHECK_ARG(B > 0 && Hq > 0 && T > 0 && D > 0 && int64_t(B) * Hq * T < (int64_t(1) << 31),
+                "combine_pushed: shape");
+  LB2_CHECK_ARG(epoch > 0, "combine_pushed: calls count from 1");
+  xch::PeerParams p{};
+  for (int r = 0; r < R; ++r) {
+    LB2_CHECK_ARG(bufs[r] != 0, "combine_pushed: a rank's buffer is missing");
+    p.bufs[r] = reinterpret_cast<const float*>(bufs[r]);
+  }
+  p.R = R;
+  p.rank = rank;
+  p.parity = int(epoch & 1u);
+  p.epoch = epoch;
+  p.rows = B * Hq * T;
+  p.half = int64_t(R) * p.rows * (D + 1);
+  p.pushed = 1;
+  p.Hq = Hq;
+  p.Tq = T;
+  p.D = D;
+  p.o = o;
+  p.o0 = o_st[0];
+  p.o1 = o_st[1];
+  p.o2 = o_st[2];
+  const int warps = 8;
+  dim3 grid(unsigned((p.rows + warps - 1) / warps));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == LB2_BF16)
+    xch::peer_combine_kernel<__nv_bfloat16><<<grid, warps * 32, 0, st>>>(p);
+  else if (dtype == LB2_F16)
+    xch::peer_combine_kernel<__half><<<grid, warps * 32, 0, st>>>(p);
+  else if (dtype == LB2_F32)
+    xch::peer_combine_kernel<float><<<grid, warps * 32, 0, st>>>(p);
+  else
+    return fail(LB2_EINVAL, "combine_pushed: dtype");
   LB2_CUDA(cudaGetLastError());
   return LB2_OK;
 }

@@ -13,6 +13,12 @@
 //   3. merges the R partials of its rows, reading the peers' halves e % 2 over NVLink (cache-bypassing loads).
 // A rank is at most one call ahead of any peer (its call e + 1 needs every peer's flag e + 1, set after the peer's
 // call e ended), so a half is rewritten (call e + 2) only after every peer has finished reading it (call e).
+//
+// Push mode: a rank's buffer holds every rank's partial (R slots a half), and the decode partial of call e writes
+// this rank's rows into slot `rank` of half e % 2 of EVERY rank's buffer (peer stores over NVLink, fenced at system
+// scope). The combine then publishes and waits exactly as above, and merges the R slots of its OWN buffer -- local
+// reads only. A peer writes half e % 2 of this buffer for call e + 2 only after it has seen this rank's flag e + 1,
+// published when this rank's merge of call e was done.
 #pragma once
 
 #include "common.cuh"
@@ -26,7 +32,8 @@ struct PeerParams {
   const float* bufs[XCH_MAX_RANKS];  // every rank's exchange buffer as mapped in this process (bufs[rank]: its own)
   int R, rank, parity;
   uint32_t epoch;
-  int64_t half;  // floats in one parity half: rows * (D + 1)
+  int64_t half;  // floats in one parity half: rows * (D + 1), or R slots of that in push mode
+  int pushed;    // push mode: every rank's partial is in this rank's own buffer, slot r at parity half + r rows (D + 1)
   int rows, Hq, Tq, D;
   void* o;
   int64_t o0, o1, o2;
@@ -75,17 +82,23 @@ __global__ void __launch_bounds__(256) peer_combine_kernel(const __grid_constant
   }
   __syncthreads();
   if (!s_ok) return;
-  // one warp a row, as decode::combine_kernel, with rank r's partial at bufs[r] + parity * half
+  // one warp a row, as decode::combine_kernel, with rank r's partial at bufs[r] + parity * half (pull mode: read over
+  // NVLink) or in this rank's own buffer, slot r (push mode: the peers wrote it here)
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= p.rows) return;
   const int64_t base = int64_t(p.parity) * p.half;
-  const int64_t lse_at = base + int64_t(p.rows) * p.D + row;
+  const int64_t slot = int64_t(p.rows) * (p.D + 1);
+  const float* src[XCH_MAX_RANKS];
+#pragma unroll
+  for (int r = 0; r < XCH_MAX_RANKS; ++r)
+    src[r] = r < p.R ? (p.pushed ? p.bufs[p.rank] + base + r * slot : p.bufs[r] + base) : nullptr;
+  const int64_t lse_at = int64_t(p.rows) * p.D + row;
   float lse[XCH_MAX_RANKS];
   float M = -INFINITY;
 #pragma unroll
   for (int r = 0; r < XCH_MAX_RANKS; ++r) {
-    lse[r] = r < p.R ? __ldcv(p.bufs[r] + lse_at) : -INFINITY;
+    lse[r] = r < p.R ? __ldcv(src[r] + lse_at) : -INFINITY;
     M = fmaxf(M, lse[r]);
   }
   const float Mu = M == -INFINITY ? 0.f : M;
@@ -98,12 +111,12 @@ __global__ void __launch_bounds__(256) peer_combine_kernel(const __grid_constant
   const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
   const int t = row % p.Tq, h = (row / p.Tq) % p.Hq, b = row / (p.Tq * p.Hq);
   T* orow = reinterpret_cast<T*>(p.o) + b * p.o0 + int64_t(h) * p.o1 + int64_t(t) * p.o2;
-  const int64_t o_at = base + int64_t(row) * p.D;
+  const int64_t o_at = int64_t(row) * p.D;
   for (int d = lane; d < p.D; d += 32) {
     float x = 0.f;
 #pragma unroll
     for (int r = 0; r < XCH_MAX_RANKS; ++r)
-      if (r < p.R) x += lse[r] * __ldcv(p.bufs[r] + o_at + d);
+      if (r < p.R) x += lse[r] * __ldcv(src[r] + o_at + d);
     orow[d] = from_f<T>(x * inv);
   }
 }

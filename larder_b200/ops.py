@@ -241,6 +241,19 @@ def decode_partial_into(q, k, v, scale, kv_len, split, part_o_ptr, part_lse_ptr)
     check(rc, "attn_decode_partial")
 
 
+def decode_push(q, k, v, scale, kv_len, split, bufs, R, rank, epoch):
+    """This rank's KV-range partial stored into slot `rank` of half epoch % 2 of every rank's push-exchange buffer
+    (bufs: a ctypes uint64 array of the R buffers as mapped here), lb2_attn_decode_push."""
+    B, Hq, T, D = q.shape
+    Hkv, N = k.shape[1], k.shape[2]
+    ws = workspace(q.device, _decode_ws_bytes(B, Hq, Hkv, T, N, D, split, q.device.index), "decode_partial")
+    rc = lib().lb2_attn_decode_push(_ptr(q), i64(*q.stride()[:3]), _ptr(k), i64(*k.stride()[:3]), _ptr(v),
+                                    i64(*v.stride()[:3]), _ptr(kv_len), B, Hq, Hkv, T, N, D, dtype_code(q),
+                                    float(scale), int(split), _ptr(ws), ws.numel(), bufs, int(R), int(rank),
+                                    int(epoch), _stream(q))
+    check(rc, "attn_decode_push")
+
+
 def attn_combine(part_o, part_lse, dtype, out=None):
     """Merge R partials part_o [R, B, Hq, T, D], part_lse [R, B, Hq, T] (fp32) by log-sum-exp."""
     _cuda(part_o, part_lse)

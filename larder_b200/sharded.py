@@ -132,17 +132,22 @@ class PeerExchange:
     (at most 8, one GPU each, all on one NVSwitch node). Every rank builds it with the same shape, calls `decode` the
     same number of times in the same order, and calls `close` at the end (all ranks)."""
 
-    def __init__(self, B, Hq, T, D, group=None):
+    def __init__(self, B, Hq, T, D, group=None, push=False):
+        """push=True: every rank's partial is stored straight into every rank's buffer by its decode kernel
+        (lb2_attn_decode_push) and the merge reads only local memory (lb2_attn_combine_pushed); else each rank
+        keeps its partial and the merge reads the peers' over NVLink (lb2_attn_combine_peers)."""
         self.group = group
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
         if self.world > 8:
             raise ValueError("PeerExchange: at most 8 ranks")
         self.shape = (B, Hq, T, D)
+        self.push = push
         self.rows = B * Hq * T
         self.half = self.rows * (D + 1)
         L = lib()
         ptr = ctypes.c_void_p()
-        check(L.lb2_xch_alloc(L.lb2_xch_bytes(B, Hq, T, D), ctypes.byref(ptr)), "xch_alloc")
+        nbytes = L.lb2_xch_push_bytes(self.world, B, Hq, T, D) if push else L.lb2_xch_bytes(B, Hq, T, D)
+        check(L.lb2_xch_alloc(nbytes, ctypes.byref(ptr)), "xch_alloc")
         self.base = ptr.value
         handle = ctypes.create_string_buffer(64)
         check(L.lb2_xch_handle(ctypes.c_void_p(self.base), handle), "xch_handle")
@@ -180,9 +185,15 @@ class PeerExchange:
         if (B, Hq, T, D) != self.shape:
             raise ValueError(f"PeerExchange: built for {self.shape}, called with {(B, Hq, T, D)}")
         self.epoch += 1
+        o = torch.empty((B, Hq, T, D), dtype=out_dtype or q.dtype, device=q.device)
+        if self.push:
+            ops.decode_push(q, k_local, v_local, scale, kv_len_local, 0, self.bufs, self.world, self.rank, self.epoch)
+            rc = lib().lb2_attn_combine_pushed(self.bufs, self.world, self.rank, self.epoch, B, Hq, T, D,
+                                               ops._ptr(o), i64(*o.stride()[:3]), ops.dtype_code(o), ops._stream(o))
+            check(rc, "attn_combine_pushed")
+            return o
         o_ptr = self.base + (self.epoch & 1) * self.half * 4
         ops.decode_partial_into(q, k_local, v_local, scale, kv_len_local, 0, o_ptr, o_ptr + self.rows * D * 4)
-        o = torch.empty((B, Hq, T, D), dtype=out_dtype or q.dtype, device=q.device)
         rc = lib().lb2_attn_combine_peers(self.bufs, self.world, self.rank, self.epoch, B, Hq, T, D, ops._ptr(o),
                                           i64(*o.stride()[:3]), ops.dtype_code(o), ops._stream(o))
         check(rc, "attn_combine_peers")

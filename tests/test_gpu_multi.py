@@ -63,7 +63,7 @@ def test_kv_sharded_decode_nccl_equals_whole():
         assert st == 0 and err <= 2e-2, (rank, err, st)
 
 
-def _peer_worker(rank, port, rq):
+def _peer_worker(rank, port, rq, push=False):
     import datetime
     import torch.distributed as dist
     from larder_b200 import ops, sharded
@@ -79,7 +79,7 @@ def _peer_worker(rank, port, rq):
         k = torch.randn(B, Hkv, N, D, generator=g).to(torch.bfloat16).to(dev)
         v = torch.randn(B, Hkv, N, D, generator=g).to(torch.bfloat16).to(dev)
         s0, s1 = sharded.kv_range(N, rank, WORLD)
-        xch = sharded.PeerExchange(B, Hq, 1, D)
+        xch = sharded.PeerExchange(B, Hq, 1, D, push=push)
         err, same = 0.0, True
         for _ in range(5):  # both halves of the exchange buffer, each reused
             q = torch.randn(B, Hq, 1, D, generator=g).to(torch.bfloat16).to(dev)
@@ -104,6 +104,24 @@ def test_kv_sharded_decode_peer_memory_equals_whole_and_nccl():
     rq = ctx.Queue()
     port = _port()
     procs = [ctx.Process(target=_peer_worker, args=(r, port, rq)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    res = [rq.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, err, same, st in res:
+        assert st == 0 and err <= 2e-2 and same, (rank, err, same, st)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_kv_sharded_decode_push_equals_whole_and_nccl():
+    """The push form (each rank's decode stores its partial into every rank's buffer; the merge reads local memory):
+    five calls in a row, equal to one whole-cache decode and bit-equal to the NCCL path."""
+    ctx = mp.get_context("spawn")
+    rq = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, port, rq, True)) for r in range(WORLD)]
     for p in procs:
         p.start()
     res = [rq.get(timeout=300) for _ in procs]
