@@ -189,8 +189,9 @@ int lb2_attn_combine_peers(const uint64_t* bufs, int R, int rank, uint32_t epoch
  * (lb2_xch_push_bytes(R, B, Hq, T, D) bytes, from lb2_xch_alloc, shared as above). Call e = 1, 2, ... of a rank:
  * lb2_attn_decode_push computes this rank's range partial and its epilogue stores it straight into slot `rank` of
  * half e % 2 of EVERY rank's buffer (bufs: the R buffers as mapped here; peer stores over NVLink, fenced at system
- * scope), then lb2_attn_combine_pushed publishes e, waits (bounded, 2 s) for every peer's e and merges the R slots of
- * its OWN buffer, so the merge reads local memory only. kv_len / workspace / split as lb2_attn_decode_partial. */
+ * scope); its last block to finish announces e to every rank. lb2_attn_combine_pushed then waits (bounded, 2 s) for
+ * every peer's e and merges the R slots of its OWN buffer, so the merge reads local memory only. kv_len / workspace /
+ * split as lb2_attn_decode_partial; every call of an exchange has the same shape. */
 size_t lb2_xch_push_bytes(int R, int B, int Hq, int T, int D);
 int lb2_attn_decode_push(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
                          const int64_t* v_st, const int32_t* kv_len, int B, int Hq, int Hkv, int T, int N, int D,

@@ -79,6 +79,11 @@ struct Params {
   int npush;
   float* push_o[8];
   float* push_lse[8];
+  // and the call is announced by the block that finishes last: it stores push_epoch into every rank's flag of this
+  // rank (push_flag[i]), once push_count (this rank's, in its own buffer) shows every block done
+  uint32_t* push_count;
+  uint32_t* push_flag[8];
+  uint32_t push_epoch;
 };
 
 template <typename T>
@@ -709,7 +714,18 @@ __global__ void __launch_bounds__(256) split_combine_kernel(const Params p) {
         dst[3] = from_f<T>(v.w);
       }
     }
-    if (p.npush) __threadfence_system();  // the pushed rows reach the peers before this rank publishes its call
+  }
+  if (p.npush) {  // the last block to finish announces the call to every rank (release at system scope)
+    __threadfence_system();  // this thread's pushed rows reach the peers before the call is announced
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const uint32_t done = atomicAdd(p.push_count, 1u) + 1u;
+      if (done == p.push_epoch * gridDim.x) {
+        __threadfence_system();
+        for (int i = 0; i < p.npush; ++i)
+          asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.push_flag[i]), "r"(p.push_epoch) : "memory");
+      }
+    }
   }
 }
 

@@ -210,7 +210,8 @@ static int run(const void* q, const int64_t* q_st, const void* k, const int64_t*
                const int64_t* v_st, void* o, const int64_t* o_st, float* part_o, float* part_lse,
                const int32_t* kv_len, int B, int Hq, int Hkv, int T, int N, int D, int dtype, float scale, int causal,
                int split, void* workspace, size_t workspace_bytes, void* stream, int npush = 0,
-               float* const* push_o = nullptr, float* const* push_lse = nullptr) {
+               float* const* push_o = nullptr, float* const* push_lse = nullptr, uint32_t* push_count = nullptr,
+               uint32_t* const* push_flag = nullptr, uint32_t push_epoch = 0) {
   LB2_CHECK_ARG(B > 0 && Hq > 0 && Hkv > 0 && T > 0 && N > 0, "decode: empty shape");
   LB2_CHECK_ARG(Hq % Hkv == 0, "decode: Hq must be a multiple of Hkv");
   LB2_CHECK_ARG(D == 64 || D == 128 || D == 256, "decode: head dim must be 64, 128 or 256");
@@ -251,7 +252,10 @@ static int run(const void* q, const int64_t* q_st, const void* k, const int64_t*
   for (int i = 0; i < npush; ++i) {
     p.push_o[i] = push_o[i];
     p.push_lse[i] = push_lse[i];
+    p.push_flag[i] = push_flag[i];
   }
+  p.push_count = push_count;
+  p.push_epoch = push_epoch;
   p.kv_len = kv_len;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   p.ws_ml = reinterpret_cast<float*>(ws + w.ml);
@@ -669,6 +673,38 @@ int lb2_xch_close(void* ptr) {
   return LB2_OK;
 }
 
+}  // extern "C"
+
+namespace {
+
+// The peer merge as a programmatic dependent of the decode partial before it (its launch overlaps that grid's tail;
+// the kernel waits on the grid dependency first).
+int xch_combine_launch(const xch::PeerParams& p, int dtype, void* stream) {
+  const int warps = 8;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned((p.rows + warps - 1) / warps));
+  cfg.blockDim = dim3(warps * 32);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (dtype == LB2_BF16)
+    LB2_CUDA(cudaLaunchKernelEx(&cfg, xch::peer_combine_kernel<__nv_bfloat16>, p));
+  else if (dtype == LB2_F16)
+    LB2_CUDA(cudaLaunchKernelEx(&cfg, xch::peer_combine_kernel<__half>, p));
+  else if (dtype == LB2_F32)
+    LB2_CUDA(cudaLaunchKernelEx(&cfg, xch::peer_combine_kernel<float>, p));
+  else
+    return fail(LB2_EINVAL, "combine_peers: dtype");
+  return LB2_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
 int lb2_attn_combine_peers(const uint64_t* bufs, int R, int rank, uint32_t epoch, int B, int Hq, int T, int D, void* o,
                            const int64_t* o_st, int dtype, void* stream) {
   LB2_CHECK_ARG(R >= 1 && R <= xch::XCH_MAX_RANKS && rank >= 0 && rank < R, "combine_peers: 1 to 8 ranks");
@@ -692,25 +728,13 @@ int lb2_attn_combine_peers(const uint64_t* bufs, int R, int rank, uint32_t epoch
   p.o0 = o_st[0];
   p.o1 = o_st[1];
   p.o2 = o_st[2];
-  const int warps = 8;
-  dim3 grid(unsigned((p.rows + warps - 1) / warps));
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == LB2_BF16)
-    xch::peer_combine_kernel<__nv_bfloat16><<<grid, warps * 32, 0, st>>>(p);
-  else if (dtype == LB2_F16)
-    xch::peer_combine_kernel<__half><<<grid, warps * 32, 0, st>>>(p);
-  else if (dtype == LB2_F32)
-    xch::peer_combine_kernel<float><<<grid, warps * 32, 0, st>>>(p);
-  else
-    return fail(LB2_EINVAL, "combine_peers: dtype");
-  LB2_CUDA(cudaGetLastError());
-  return LB2_OK;
+  return xch_combine_launch(p, dtype, stream);
 }
 
 size_t lb2_xch_push_bytes(int R, int B, int Hq, int T, int D) {
   if (R < 1 || R > xch::XCH_MAX_RANKS || B <= 0 || Hq <= 0 || T <= 0 || D <= 0) return 0;
   const int64_t half = int64_t(R) * B * Hq * T * (D + 1);
-  return size_t(xch::flags_offset(half) * 4 + xch::XCH_MAX_RANKS * 4);
+  return size_t(xch::flags_offset(half) * 4 + xch::XCH_MAX_RANKS * 4 + 16);  // flags, then the rank's block count
 }
 
 int lb2_attn_decode_push(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
@@ -722,13 +746,17 @@ int lb2_attn_decode_push(const void* q, const int64_t* q_st, const void* k, cons
   const int64_t rows = int64_t(B) * Hq * T, slot = rows * (D + 1), half = R * slot;
   float* po[xch::XCH_MAX_RANKS];
   float* pl[xch::XCH_MAX_RANKS];
+  uint32_t* flag[xch::XCH_MAX_RANKS];
   for (int r = 0; r < R; ++r) {
     LB2_CHECK_ARG(bufs[r] != 0 && (bufs[r] & 15) == 0, "decode_push: a rank's buffer is missing or misaligned");
     po[r] = reinterpret_cast<float*>(bufs[r]) + int64_t(epoch & 1u) * half + rank * slot;
     pl[r] = po[r] + rows * D;
+    flag[r] = reinterpret_cast<uint32_t*>(reinterpret_cast<float*>(bufs[r]) + xch::flags_offset(half)) + rank;
   }
+  uint32_t* count = reinterpret_cast<uint32_t*>(reinterpret_cast<float*>(bufs[rank]) + xch::flags_offset(half)) +
+                    xch::XCH_MAX_RANKS;
   return decode::run(q, q_st, k, k_st, v, v_st, nullptr, nullptr, nullptr, nullptr, kv_len, B, Hq, Hkv, T, N, D, dtype,
-                     scale, 0, split, workspace, workspace_bytes, stream, R, po, pl);
+                     scale, 0, split, workspace, workspace_bytes, stream, R, po, pl, count, flag, epoch);
 }
 
 int lb2_attn_combine_pushed(const uint64_t* bufs, int R, int rank, uint32_t epoch, int B, int Hq, int T, int D, void* o,
@@ -756,19 +784,7 @@ int lb2_attn_combine_pushed(const uint64_t* bufs, int R, int rank, uint32_t epoc
   p.o0 = o_st[0];
   p.o1 = o_st[1];
   p.o2 = o_st[2];
-  const int warps = 8;
-  dim3 grid(unsigned((p.rows + warps - 1) / warps));
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == LB2_BF16)
-    xch::peer_combine_kernel<__nv_bfloat16><<<grid, warps * 32, 0, st>>>(p);
-  else if (dtype == LB2_F16)
-    xch::peer_combine_kernel<__half><<<grid, warps * 32, 0, st>>>(p);
-  else if (dtype == LB2_F32)
-    xch::peer_combine_kernel<float><<<grid, warps * 32, 0, st>>>(p);
-  else
-    return fail(LB2_EINVAL, "combine_pushed: dtype");
-  LB2_CUDA(cudaGetLastError());
-  return LB2_OK;
+  return xch_combine_launch(p, dtype, stream);
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }

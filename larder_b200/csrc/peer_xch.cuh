@@ -53,9 +53,13 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 template <typename T>
 __global__ void __launch_bounds__(256) peer_combine_kernel(const __grid_constant__ PeerParams p) {
   __shared__ int s_ok;
+  // launched as a programmatic dependent: the next kernel may begin its launch now, and this one waits for the
+  // stream's previous kernel (the decode partial) to complete before anything below
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (threadIdx.x == 0) {
-    __threadfence_system();  // the partial (written before this kernel on the stream) ahead of the flags
-    for (int r = 0; r < p.R; ++r)
+    if (!p.pushed) __threadfence_system();  // the partial (written before this kernel on the stream) ahead of the flags
+    for (int r = 0; r < p.R && !p.pushed; ++r)  // (push mode: the decode's last block announced the call)
       if (r != p.rank) {
         uint32_t* f = reinterpret_cast<uint32_t*>(const_cast<float*>(p.bufs[r]) + flags_offset(p.half)) + p.rank;
         st_release_sys(f, p.epoch);
