@@ -187,7 +187,8 @@ int lb2_attn_combine_peers(const uint64_t* bufs, int R, int rank, uint32_t epoch
 
 /* The same exchange in push form (no counterpart in the reference either): every rank's buffer holds all R partials
  * (lb2_xch_push_bytes(R, B, Hq, T, D) bytes, from lb2_xch_alloc, shared as above). Call e = 1, 2, ... of a rank:
- * lb2_attn_decode_push computes this rank's range partial and its epilogue stores it straight into slot `rank` of
+ * lb2_attn_decode_push computes this rank's range partial (o rows in bf16, lse in fp32) and its epilogue stores it
+ * straight into slot `rank` of
  * half e % 2 of EVERY rank's buffer (bufs: the R buffers as mapped here; peer stores over NVLink, fenced at system
  * scope); its last block to finish announces e to every rank. lb2_attn_combine_pushed then waits (bounded, 2 s) for
  * every peer's e and merges the R slots of its OWN buffer, so the merge reads local memory only. kv_len / workspace /

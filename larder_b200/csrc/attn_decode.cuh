@@ -75,7 +75,8 @@ struct Params {
   int causal, emit;
   float scale_log2;  // softmax scale * log2(e)
   // push mode (npush > 0): the emitted partial goes to npush places at once -- this rank's slot in every rank's
-  // exchange buffer, peers' through NVLink -- instead of part_o / part_lse (same offsets in each)
+  // exchange buffer, peers' through NVLink -- instead of part_o / part_lse (same offsets in each; the o rows as
+  // bf16 at the start of the o area)
   int npush;
   float* push_o[8];
   float* push_lse[8];
@@ -699,7 +700,11 @@ __global__ void __launch_bounds__(256) split_combine_kernel(const Params p) {
         if (p.npush) {
 #pragma unroll 1
           for (int i = 0; i < p.npush; ++i) {
-            reinterpret_cast<float4*>(p.push_o[i] + ro * D)[c] = v;
+            // o rows travel as bf16 (half the NVLink bytes; the merged output is 16-bit anyway), lse as fp32
+            uint2 h;
+            h.x = pack2<__nv_bfloat16>(v.x, v.y);
+            h.y = pack2<__nv_bfloat16>(v.z, v.w);
+            reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.push_o[i]) + ro * D)[c] = h;
             if (c == 0) p.push_lse[i][ro] = lse;
           }
         } else {

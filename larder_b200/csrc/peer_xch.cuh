@@ -14,8 +14,8 @@
 // A rank is at most one call ahead of any peer (its call e + 1 needs every peer's flag e + 1, set after the peer's
 // call e ended), so a half is rewritten (call e + 2) only after every peer has finished reading it (call e).
 //
-// Push mode: a rank's buffer holds every rank's partial (R slots a half), and the decode partial of call e writes
-// this rank's rows into slot `rank` of half e % 2 of EVERY rank's buffer (peer stores over NVLink, fenced at system
+// Push mode: a rank's buffer holds every rank's partial (R slots a half; o rows as bf16, half the bytes over NVLink),
+// and the decode partial of call e writes this rank's rows into slot `rank` of half e % 2 of EVERY rank's buffer (peer stores over NVLink, fenced at system
 // scope). The combine then publishes and waits exactly as above, and merges the R slots of its OWN buffer -- local
 // reads only. A peer writes half e % 2 of this buffer for call e + 2 only after it has seen this rank's flag e + 1,
 // published when this rank's merge of call e was done.
@@ -120,7 +120,10 @@ __global__ void __launch_bounds__(256) peer_combine_kernel(const __grid_constant
     float x = 0.f;
 #pragma unroll
     for (int r = 0; r < XCH_MAX_RANKS; ++r)
-      if (r < p.R) x += lse[r] * __ldcv(src[r] + o_at + d);
+      if (r < p.R)
+        x += lse[r] * (p.pushed ? __bfloat162float(__ushort_as_bfloat16(__ldcv(
+                                      reinterpret_cast<const unsigned short*>(src[r]) + o_at + d)))
+                                : __ldcv(src[r] + o_at + d));
     orow[d] = from_f<T>(x * inv);
   }
 }

