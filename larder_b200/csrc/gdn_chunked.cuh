@@ -11,16 +11,13 @@
 // Decay ratios are always formed as exp(gamma_t - gamma_j) with j <= t (never a division by a small Gam), so no
 // intermediate overflows however strong the decay.
 //
-// Two launches:
-//   prep (grid: chunks x v-heads x batch, independent): K K^T and Q K^T on bf16 mma.sync (fp32 accumulate), the
-//        decay / beta weighting, T by blocked inversion (16 x 16 diagonal blocks by substitution, then 32 and 64
-//        by the 2 x 2 block formula) in fp32, and W, U' on TF32 mma.sync with their B operands (beta Gam K,
-//        beta V) formed from the 16-bit tiles on the fly; writes W, U', M, gamma, Gam to the workspace.
-//   scan (grid: Dv / 32 value-row blocks x v-heads x batch, 8 warps): the state slice S[32 x 128] in fp32
-//        registers (a TF32 copy in shared memory for the products that read all of it), chunks in order, each
-//        chunk's tiles prefetched by bulk copies (the workspace is laid out as the shared-memory tiles) while the
-//        previous chunk computes; U, Y and the state update on TF32 mma.sync with fp32 accumulation. W and M are
-//        stored already rounded to TF32 by prep.
+// Two launches, every product on the tcgen05 tensor cores (kind::f16, fp32 accumulators in TMEM), fp32 values that
+// feed a product passed as a 16-bit hi / lo pair (hi = round(x), lo = round(x - hi): about 16 mantissa bits):
+//   prep (grid: chunks x v-heads x batch, independent): K K^T and Q K^T, the decay / beta weighting, T by blocked
+//        inversion in fp32 on the CUDA cores, then W and U'; writes W, U', M, gamma, Gam to the workspace in the
+//        scan's shared-memory layout.
+//   scan (grid: Dv / 32 value columns x v-heads x batch): the state slice in fp32 registers, chunks in order, each
+//        chunk's workspace pieces and Q / K tiles prefetched a chunk ahead; U, Y and the state update per chunk.
 #pragma once
 
 #include <type_traits>
@@ -81,142 +78,121 @@ __device__ __forceinline__ float ldf(const void* p, int64_t i, int dt) {
   }
 }
 
-__device__ __forceinline__ uint32_t tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
-}
-
-// A 16-bit value's exact TF32 bit pattern (bf16 and fp16 mantissas fit TF32's 10 bits).
-template <typename T>
-__device__ __forceinline__ uint32_t tf32_of(T x) {
-  return __float_as_uint(to_f<T>(x));
-}
-
-__device__ __forceinline__ void mma_tf32(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                         uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-template <typename T>
-__device__ __forceinline__ void mma_16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1);
-template <>
-__device__ __forceinline__ void mma_16816<__nv_bfloat16>(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-template <>
-__device__ __forceinline__ void mma_16816<__half>(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ void ldsm4(uint32_t addr, uint32_t* r) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
-
-// 16-byte cp.async, zero-filling the destination when `in` is false (nothing is read then).
-__device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, bool in) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(in ? 16 : 0)
-               : "memory");
-}
-
-// acc (a 16 x 8 m16n8k8 accumulator) += L R over K = 8 ksteps, with L's rows at Lp (row stride ldl, columns from
-// Lp) and R's rows k at Rp + k ldr, in three TF32 products per step (hi hi + hi lo + lo hi of each fp32 operand
-// split into TF32 high and low parts), so that the block products of the inversion keep close to fp32 accuracy.
-__device__ __forceinline__ void mma3_tile(const float* Lp, int ldl, const float* Rp, int ldr, int ksteps, float* acc,
-                                          int lane) {
-  const int r = lane >> 2, cq = lane & 3;
-  for (int ks = 0; ks < ksteps; ++ks) {
-    const int k0 = ks * 8;
-    const float a[4] = {Lp[r * ldl + k0 + cq], Lp[(r + 8) * ldl + k0 + cq], Lp[r * ldl + k0 + cq + 4],
-                        Lp[(r + 8) * ldl + k0 + cq + 4]};
-    const float bb[2] = {Rp[(k0 + cq) * ldr + r], Rp[(k0 + cq + 4) * ldr + r]};
-    uint32_t ah[4], al[4], bh[2], bl[2];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      ah[i] = tf32(a[i]);
-      al[i] = tf32(a[i] - __uint_as_float(ah[i]));
-    }
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      bh[i] = tf32(bb[i]);
-      bl[i] = tf32(bb[i] - __uint_as_float(bh[i]));
-    }
-    mma_tf32(acc, al[0], al[1], al[2], al[3], bh[0], bh[1]);
-    mma_tf32(acc, ah[0], ah[1], ah[2], ah[3], bl[0], bl[1]);
-    mma_tf32(acc, ah[0], ah[1], ah[2], ah[3], bh[0], bh[1]);
-  }
-}
-
 // Workspace of one (batch, head, chunk).
 __device__ __forceinline__ uint8_t* unit_ptr(const Params& p, int b, int h, int c) {
   return reinterpret_cast<uint8_t*>(p.ws) + ((int64_t(b) * p.Hv + h) * p.nchunks + c) * int64_t(UNIT_BYTES);
 }
 
-// The 16-bit hi / lo split of two adjacent values, stored at the swizzled offset of the first in `hi` and `lo`.
-template <typename T>
-__device__ __forceinline__ void store_split2(uint8_t* hi, uint8_t* lo, int off, float x0, float x1) {
-  const float h0 = to_f<T>(from_f<T>(x0)), h1 = to_f<T>(from_f<T>(x1));
-  *reinterpret_cast<uint32_t*>(hi + off) = pack2<T>(h0, h1);
-  *reinterpret_cast<uint32_t*>(lo + off) = pack2<T>(x0 - h0, x1 - h1);
-}
-
 // ------------------------------------------------------------------------------------------------ prep
+//
+// One CTA of 4 warps a (chunk, v-head), its products on tcgen05 (kind::f16, accumulators in TMEM, M = 64 MMAs: an
+// accumulator's row m sits in TMEM lane m % 16 + 32 (m / 16) from the lane the MMA names, so two M = 64 products
+// written at lane 0 and lane 16 share 32 x 4 lanes, and warp w's lanes 0-15 read rows 16 w .. of the first and its
+// lanes 16-31 rows 16 w .. of the second):
+//   P_A  K K^T (lane 0) and Q K^T (lane 16), N = 64, from the K / Q tiles as TMA lands them;
+//   A = diag(beta) (decay x K K^T) strictly below the diagonal, M = decay x Q K^T on and below it (M as a hi / lo pair
+//   straight to the workspace); T = (I + A)^{-1} in fp32 on the CUDA cores (16 x 16 diagonal blocks by substitution,
+//   then the 2 x 2 block formula at 32 and 64);
+//   P_W  W = (T diag(beta Gam)) K (lane 0) and U' = (T diag(beta)) V (lane 16), N = 128: A = the scaled T as a hi / lo
+//   pair, B = the K / V tile read MN-major (positions are the products' K).
+
+constexpr int PREP_TMEM_COLS = 128;
+constexpr int XP = 40;  // row stride of the inversion scratch
 
 struct PrepSmem {
-  static constexpr int KB = 0;                              // bf16 [C][KP]
-  static constexpr int QB = KB + C * KP * 2;                // bf16 [C][KP]
-  static constexpr int VB = QB + C * KP * 2;                // bf16 [C][KP]
-  static constexpr int AF = VB + C * KP * 2;                // f32 [C][AP]  A, then T
-  static constexpr int XS = AF + C * AP * 4;                // f32 [32][XP] inversion scratch
-  static constexpr int GAM = XS + 32 * 40 * 4;              // f32 [C] gamma, [C] Gam, [C] beta
-  static constexpr int BYTES = GAM + 3 * C * 4;
+  static constexpr int K0 = 0;                  // K tile: two TMA boxes [64 positions][64 keys], 8 KB each
+  static constexpr int Q0 = K0 + 2 * C * 128;   // Q tile, the same
+  static constexpr int V0 = Q0 + 2 * C * 128;   // V tile, the same (64 value columns a box)
+  static constexpr int TBG = V0 + 2 * C * 128;  // T diag(beta Gam) as hi, lo: [64][64] 16-bit, 8 KB each
+  static constexpr int TB = TBG + 2 * C * 128;  // T diag(beta) as hi, lo
+  static constexpr int AF = TB + 2 * C * 128;   // f32 [C][AP]: A, then T
+  static constexpr int XS = AF + C * AP * 4;    // f32 [32][XP] inversion scratch
+  static constexpr int GAM = XS + 32 * XP * 4;  // f32 [C] gamma, [C] Gam, [C] beta
+  static constexpr int BAR = GAM + 3 * C * 4;   // 2 mbarriers: loads landed, MMAs done
+  static constexpr int SLOT = BAR + 16;         // TMEM base address
+  static constexpr int BYTES = SLOT + 16 + 1024;
 };
+static_assert(PrepSmem::AF % 1024 == 0 && PrepSmem::BYTES <= 116 * 1024, "two prep CTAs an SM");
+
+// acc (a 16 x 8 tile in the m16n8 fragment layout: lane (r = lane / 4, q = lane % 4) holds (r, 2q), (r, 2q + 1),
+// (r + 8, 2q), (r + 8, 2q + 1)) += L R over K = 8 ksteps, fp32 on the CUDA cores: L's rows at Lp (stride ldl), R's
+// row k at Rp + k ldr.
+__device__ __forceinline__ void fma_tile(const float* Lp, int ldl, const float* Rp, int ldr, int ksteps, float* acc,
+                                         int lane) {
+  const int r = lane >> 2, cq = lane & 3;
+  for (int k = 0; k < 8 * ksteps; ++k) {
+    const float l0 = Lp[r * ldl + k], l1 = Lp[(r + 8) * ldl + k];
+    const float2 rr = *reinterpret_cast<const float2*>(Rp + k * ldr + 2 * cq);
+    acc[0] = fmaf(l0, rr.x, acc[0]);
+    acc[1] = fmaf(l0, rr.y, acc[1]);
+    acc[2] = fmaf(l1, rr.x, acc[2]);
+    acc[3] = fmaf(l1, rr.y, acc[3]);
+  }
+}
+
+// Writes 64 values of row `row` of a 16-bit K-major operand pair (128-byte swizzle) as hi / lo: eight 16-byte pieces.
+template <typename T>
+__device__ __forceinline__ void put_row_pair(uint8_t* hi, uint8_t* lo, int row, const float* x) {
+#pragma unroll
+  for (int j8 = 0; j8 < 8; ++j8) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float a = x[8 * j8 + 2 * e], bb = x[8 * j8 + 2 * e + 1];
+      const float ha = to_f<T>(from_f<T>(a)), hb = to_f<T>(from_f<T>(bb));
+      h[e] = pack2<T>(ha, hb);
+      l[e] = pack2<T>(a - ha, bb - hb);
+    }
+    const int off = row * 128 + (((j8 ^ row) & 7) << 4);
+    *reinterpret_cast<uint4*>(hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(lo + off) = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
 
 template <typename T>
-__global__ void __launch_bounds__(128) prep_kernel(const Params p) {
+__global__ void __launch_bounds__(128) prep_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                   const __grid_constant__ CUtensorMap kmap,
+                                                   const __grid_constant__ CUtensorMap vmap, const Params p) {
+  constexpr uint32_t AB = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+  constexpr uint32_t IDESC_A = prefill::idesc_f16(AB, 0, 0, 64, 64);   // K K^T, Q K^T
+  constexpr uint32_t IDESC_W = prefill::idesc_f16(AB, 0, 1, 64, 128);  // W, U' (B: the K / V tile, MN-major)
+  constexpr uint32_t LANE16 = 16u << 16;
   const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int hk = h / (p.Hv / p.Hk);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = c * C;
-  extern __shared__ __align__(16) uint8_t sm[];
-  T* Kb = reinterpret_cast<T*>(sm + PrepSmem::KB);
-  T* Qb = reinterpret_cast<T*>(sm + PrepSmem::QB);
-  T* Vb = reinterpret_cast<T*>(sm + PrepSmem::VB);
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* Af = reinterpret_cast<float*>(sm + PrepSmem::AF);
   float* Xs = reinterpret_cast<float*>(sm + PrepSmem::XS);
   float* gam = reinterpret_cast<float*>(sm + PrepSmem::GAM);
   float* Gam = gam + C;
   float* bet = Gam + C;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + PrepSmem::BAR);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(sm + PrepSmem::SLOT);
+  uint8_t* unit = unit_ptr(p, b, h, c);
 
-  // 1. K, Q and V tiles (16-bit) by cp.async, zero past T: they land while the gates are formed
-  {
-    const T* kg = static_cast<const T*>(p.k);
-    const T* qg = static_cast<const T*>(p.q);
-    const T* vg = static_cast<const T*>(p.v);
+  // 1. the K, Q, V tiles by TMA (rows past T land as zeros) while the gates are formed; TMEM
+  if (tid == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    fence_barrier_init();
+    prefetch_tensormap(&qmap);
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
+    mbar_arrive_expect_tx(&bar[0], 3 * 2 * C * 128);
 #pragma unroll
-    for (int i = 0; i < C * (DK / 8) / 128; ++i) {
-      const int e = tid + 128 * i, r = e / (DK / 8), u = e % (DK / 8);
-      const bool in = t0 + r < p.T;
-      const int64_t row = int64_t(b) * p.T + (in ? t0 + r : 0);  // (a row of the sequence even when not read)
-      cp_async16_zfill(Kb + r * KP + u * 8, kg + (row * p.Hk + hk) * DK + u * 8, in);
-      cp_async16_zfill(Qb + r * KP + u * 8, qg + (row * p.Hk + hk) * DK + u * 8, in);
-      cp_async16_zfill(Vb + r * KP + u * 8, vg + (row * p.Hv + h) * DV + u * 8, in);
+    for (int db = 0; db < 2; ++db) {
+      tma_load_4d(sm + PrepSmem::K0 + db * C * 128, &kmap, db * 64, t0, hk, b, &bar[0]);
+      tma_load_4d(sm + PrepSmem::Q0 + db * C * 128, &qmap, db * 64, t0, hk, b, &bar[0]);
+      tma_load_4d(sm + PrepSmem::V0 + db * C * 128, &vmap, db * 64, t0, h, b, &bar[0]);
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
   }
-  // 2. gates: gamma = inclusive prefix sum of log g over the chunk (positions past T: g = 1, beta = 0)
   if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+                 "r"(PREP_TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    // gates: gamma = inclusive prefix sum of log g over the chunk (positions past T: g = 1, beta = 0)
     float x[2], bt[2];
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
@@ -241,51 +217,65 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
       bet[lane + 32 * u] = bt[u];
     }
   }
-  asm volatile("cp.async.wait_all;" ::: "memory");
+  prefill::tc_fence_before();
   __syncthreads();
+  prefill::tc_fence_after();
+  const uint32_t tmem = *slot;
+  const uint32_t lq = uint32_t(32 * warp) << 16;
+  bool ok = mbar_wait(&bar[0], 0, 75);
 
-  // 3. K K^T and Q K^T for rows 16 w .. 16 w + 15 (bf16 mma, fp32 accumulate), then decay / beta weighting
-  {
-    float kk[8][4], qk[8][4];
+  // 2. P_A: K K^T (lane 0) and Q K^T (lane 16), K = 128 keys in two 64-key blocks of four steps
+  if (tid == 0 && ok) {
+    prefill::tc_fence_after();
+    const uint32_t k0 = smem_u32(sm + PrepSmem::K0), q0 = smem_u32(sm + PrepSmem::Q0);
 #pragma unroll
-    for (int n = 0; n < 8; ++n)
+    for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) kk[n][e] = qk[n][e] = 0.f;
-    const uint32_t kb_addr = smem_u32(Kb), qb_addr = smem_u32(Qb);
-#pragma unroll
-    for (int ks = 0; ks < DK / 16; ++ks) {
-      uint32_t ak[4], aq[4];
-      const int ar = warp * 16 + (lane & 15), ac = ks * 16 + (lane >> 4) * 8;
-      ldsm4(kb_addr + (ar * KP + ac) * 2, ak);
-      ldsm4(qb_addr + (ar * KP + ac) * 2, aq);
-#pragma unroll
-      for (int np = 0; np < 4; ++np) {
-        uint32_t bk[4];
-        const int br = np * 16 + (lane & 7) + 8 * (lane >> 4), bc = ks * 16 + ((lane >> 3) & 1) * 8;
-        ldsm4(kb_addr + (br * KP + bc) * 2, bk);
-        mma_16816<T>(kk[2 * np], ak, bk[0], bk[1]);
-        mma_16816<T>(kk[2 * np + 1], ak, bk[2], bk[3]);
-        mma_16816<T>(qk[2 * np], aq, bk[0], bk[1]);
-        mma_16816<T>(qk[2 * np + 1], aq, bk[2], bk[3]);
+      for (int ks = 0; ks < 4; ++ks) {
+        const uint64_t ak = prefill::sdesc(k0 + kb * C * 128 + ks * 32, 16, 1024);
+        const uint64_t aq = prefill::sdesc(q0 + kb * C * 128 + ks * 32, 16, 1024);
+        prefill::umma_ss(tmem, ak, ak, IDESC_A, (kb | ks) ? 1u : 0u);
+        prefill::umma_ss(tmem + LANE16, aq, ak, IDESC_A, (kb | ks) ? 1u : 0u);
       }
-    }
-    uint8_t* Mhi = unit_ptr(p, b, h, c) + WS_MHI;
-    uint8_t* Mlo = unit_ptr(p, b, h, c) + WS_MLO;
-#pragma unroll
-    for (int n = 0; n < 8; ++n)
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {  // columns j, j + 1 of row t
-        const int t = warp * 16 + (lane >> 2) + 8 * hh;
-        const int j = n * 8 + 2 * (lane & 3);
-        const float d0 = j <= t ? __expf(gam[t] - gam[j]) : 0.f, d1 = j + 1 <= t ? __expf(gam[t] - gam[j + 1]) : 0.f;
-        *reinterpret_cast<float2*>(&Af[t * AP + j]) =
-            make_float2(j < t ? bet[t] * d0 * kk[n][2 * hh] : 0.f, j + 1 < t ? bet[t] * d1 * kk[n][2 * hh + 1] : 0.f);
-        store_split2<T>(Mhi, Mlo, sw128(t, j), d0 * qk[n][2 * hh], d1 * qk[n][2 * hh + 1]);  // a scan operand
-      }
+    prefill::umma_commit(&bar[1]);
   }
+  ok = __all_sync(0xffffffffu, ok && mbar_wait(&bar[1], 0, 76));
+  // 3. A (lanes 0-15: row t of K K^T) into shared memory; M (lanes 16-31: row t of Q K^T) to the workspace
+  {
+    const int t = 16 * warp + (lane & 15);
+    float x[C];
+    if (ok) {
+      prefill::tc_fence_after();
+      prefill::tmem_ld32(tmem + lq, x);
+      prefill::tmem_ld32(tmem + lq + 32, x + 32);
+      prefill::tmem_wait_ld();
+    } else {
+#pragma unroll
+      for (int j = 0; j < C; ++j) x[j] = 0.f;
+    }
+    const float gt = gam[t];
+    if (lane < 16) {
+      const float bt = bet[t];
+#pragma unroll
+      for (int j = 0; j < C; j += 4) {
+        float4 a;
+        a.x = j < t ? bt * __expf(gt - gam[j]) * x[j] : 0.f;
+        a.y = j + 1 < t ? bt * __expf(gt - gam[j + 1]) * x[j + 1] : 0.f;
+        a.z = j + 2 < t ? bt * __expf(gt - gam[j + 2]) * x[j + 2] : 0.f;
+        a.w = j + 3 < t ? bt * __expf(gt - gam[j + 3]) * x[j + 3] : 0.f;
+        *reinterpret_cast<float4*>(Af + t * AP + j) = a;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < C; ++j) x[j] = j <= t ? __expf(gt - gam[j]) * x[j] : 0.f;
+      put_row_pair<T>(unit + WS_MHI, unit + WS_MLO, t, x);
+    }
+  }
+  prefill::tc_fence_before();
   __syncthreads();
 
-  // 4. T = (I + A)^{-1}, in place over A's lower triangle (diagonal 1, upper 0)
+
+  // 4. T = (I + A)^{-1}, in place over A's lower triangle (diagonal 1, upper 0), fp32 on the CUDA cores
   // level 0: each warp inverts its 16 x 16 diagonal block by forward substitution, lane i holding column i
   {
     const int base = warp * 16;
@@ -293,10 +283,10 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
     const int i = lane & 15;
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
-      float s = 0.f;
+      float sum = 0.f;
 #pragma unroll
-      for (int j = 0; j < r; ++j) s = fmaf(Af[(base + r) * AP + base + j], tc[j], s);
-      tc[r] = i < r ? -s : (i == r ? 1.f : 0.f);
+      for (int j = 0; j < r; ++j) sum = fmaf(Af[(base + r) * AP + base + j], tc[j], sum);
+      tc[r] = i < r ? -sum : (i == r ? 1.f : 0.f);
     }
     __syncwarp();
     if (lane < 16)
@@ -304,27 +294,26 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
       for (int r = 0; r < 16; ++r) Af[(base + r) * AP + base + i] = tc[r];
   }
   __syncthreads();
-  // level 1: T[hi][lo] = -T[hi][hi] A[hi][lo] T[lo][lo] for the block pairs (0, 1) and (2, 3) (16 x 16 blocks):
-  // warp w takes pair w / 2 and output columns 8 (w % 2) .. + 7, first of X = A[hi][lo] T[lo][lo], then of the block
-  constexpr int XP = 40;  // row stride of the scratch X (conflict-free B fragment reads)
+  // level 1: T[hi][lo] = -T[hi][hi] A[hi][lo] T[lo][lo] for the 16 x 16 block pairs (0, 1) and (2, 3): warp w takes
+  // pair w / 2 and output columns 8 (w % 2) .. + 7, first of X = A[hi][lo] T[lo][lo], then of the block
   {
     const int pr = warp >> 1, n0 = (warp & 1) * 8;
     const int lo = 32 * pr, hi = lo + 16;
     float* X = Xs + pr * 16 * XP;
     const int r = lane >> 2, cq = lane & 3;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    mma3_tile(Af + hi * AP + lo, AP, Af + lo * AP + lo + n0, AP, 2, acc, lane);
+    fma_tile(Af + hi * AP + lo, AP, Af + lo * AP + lo + n0, AP, 2, acc, lane);
     X[r * XP + n0 + 2 * cq] = acc[0];
     X[r * XP + n0 + 2 * cq + 1] = acc[1];
     X[(r + 8) * XP + n0 + 2 * cq] = acc[2];
     X[(r + 8) * XP + n0 + 2 * cq + 1] = acc[3];
     __syncthreads();
-    float t[4] = {0.f, 0.f, 0.f, 0.f};
-    mma3_tile(Af + hi * AP + hi, AP, X + n0, XP, 2, t, lane);
-    Af[(hi + r) * AP + lo + n0 + 2 * cq] = -t[0];
-    Af[(hi + r) * AP + lo + n0 + 2 * cq + 1] = -t[1];
-    Af[(hi + r + 8) * AP + lo + n0 + 2 * cq] = -t[2];
-    Af[(hi + r + 8) * AP + lo + n0 + 2 * cq + 1] = -t[3];
+    float t4[4] = {0.f, 0.f, 0.f, 0.f};
+    fma_tile(Af + hi * AP + hi, AP, X + n0, XP, 2, t4, lane);
+    Af[(hi + r) * AP + lo + n0 + 2 * cq] = -t4[0];
+    Af[(hi + r) * AP + lo + n0 + 2 * cq + 1] = -t4[1];
+    Af[(hi + r + 8) * AP + lo + n0 + 2 * cq] = -t4[2];
+    Af[(hi + r + 8) * AP + lo + n0 + 2 * cq + 1] = -t4[3];
   }
   __syncthreads();
   // level 2: T[32:64][0:32] = -T[32:64][32:64] A[32:64][0:32] T[0:32][0:32] (32 x 32 blocks): warp w takes the two
@@ -335,7 +324,7 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
     for (int u = 0; u < 2; ++u) {
       const int ti = warp * 2 + u, m0 = (ti >> 2) * 16, n0 = (ti & 3) * 8;
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      mma3_tile(Af + (32 + m0) * AP, AP, Af + n0, AP, 4, acc, lane);
+      fma_tile(Af + (32 + m0) * AP, AP, Af + n0, AP, 4, acc, lane);
       Xs[(m0 + r) * XP + n0 + 2 * cq] = acc[0];
       Xs[(m0 + r) * XP + n0 + 2 * cq + 1] = acc[1];
       Xs[(m0 + r + 8) * XP + n0 + 2 * cq] = acc[2];
@@ -345,74 +334,96 @@ __global__ void __launch_bounds__(128) prep_kernel(const Params p) {
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const int ti = warp * 2 + u, m0 = (ti >> 2) * 16, n0 = (ti & 3) * 8;
-      float t[4] = {0.f, 0.f, 0.f, 0.f};
-      mma3_tile(Af + (32 + m0) * AP + 32, AP, Xs + n0, XP, 4, t, lane);
-      Af[(32 + m0 + r) * AP + n0 + 2 * cq] = -t[0];
-      Af[(32 + m0 + r) * AP + n0 + 2 * cq + 1] = -t[1];
-      Af[(32 + m0 + r + 8) * AP + n0 + 2 * cq] = -t[2];
-      Af[(32 + m0 + r + 8) * AP + n0 + 2 * cq + 1] = -t[3];
+      float t4[4] = {0.f, 0.f, 0.f, 0.f};
+      fma_tile(Af + (32 + m0) * AP + 32, AP, Xs + n0, XP, 4, t4, lane);
+      Af[(32 + m0 + r) * AP + n0 + 2 * cq] = -t4[0];
+      Af[(32 + m0 + r) * AP + n0 + 2 * cq + 1] = -t4[1];
+      Af[(32 + m0 + r + 8) * AP + n0 + 2 * cq] = -t4[2];
+      Af[(32 + m0 + r + 8) * AP + n0 + 2 * cq + 1] = -t4[3];
     }
   }
   __syncthreads();
-  // 5. U' = T diag(beta) V, then W = T diag(beta Gam) K (TF32 mma). Warp w takes output columns 32 w .. 32 w + 31 of
-  // all four 16-row blocks (T is lower triangular, so row block m reads k < 16 (m + 1): split by rows, the last
-  // warp would do four times the first's work). The column factors (beta, then Gam on top) are folded into T first,
-  // warp w scaling rows 16 w .., so that the B fragments are the 16-bit tiles' exact TF32 values.
+  // 5. the P_W operands: thread r < 64 writes row r of T diag(beta Gam), thread 64 + r row r of T diag(beta), as
+  // hi / lo pairs
   {
-    uint8_t* unit = unit_ptr(p, b, h, c);
-    const int r = lane >> 2, cq = lane & 3, nw = warp * 32;
-#pragma unroll 1
-    for (int which = 1; which >= 0; --which) {
-      const T* R = which ? Vb : Kb;
-      {  // lane l scales columns l and l + 32 of rows 16 w .. 16 w + 15 (the lower triangle: columns < 16 w + 16)
-        const int m0 = warp * 16;
-        const float f0 = which ? bet[lane] : Gam[lane], f1 = which ? bet[lane + 32] : Gam[lane + 32];
+    const int r = tid & 63;
+    const bool vb = tid >= 64;
+    float x[C];
 #pragma unroll
-        for (int rr = 0; rr < 16; ++rr) {
-          Af[(m0 + rr) * AP + lane] *= f0;
-          if (m0 >= 16) Af[(m0 + rr) * AP + lane + 32] *= f1;
+    for (int j = 0; j < C; j += 4) {
+      const float4 a = *reinterpret_cast<const float4*>(Af + r * AP + j);
+      const float f[4] = {bet[j] * (vb ? 1.f : Gam[j]), bet[j + 1] * (vb ? 1.f : Gam[j + 1]),
+                          bet[j + 2] * (vb ? 1.f : Gam[j + 2]), bet[j + 3] * (vb ? 1.f : Gam[j + 3])};
+      x[j] = a.x * f[0];
+      x[j + 1] = a.y * f[1];
+      x[j + 2] = a.z * f[2];
+      x[j + 3] = a.w * f[3];
+    }
+    uint8_t* dst = sm + (vb ? PrepSmem::TB : PrepSmem::TBG);
+    put_row_pair<T>(dst, dst + C * 128, r, x);
+  }
+  fence_proxy_async_shared();
+  prefill::tc_fence_before();
+  __syncthreads();
+  // 6. P_W: W (lane 0) = T diag(beta Gam) K, U' (lane 16) = T diag(beta) V; K = 64 positions in four steps of 16 rows
+  // of the K / V tile (B MN-major: its two 64-column boxes 8 KB apart)
+  if (tid == 0 && ok) {
+    prefill::tc_fence_after();
+    const uint32_t k0 = smem_u32(sm + PrepSmem::K0), v0 = smem_u32(sm + PrepSmem::V0);
+    const uint32_t tg = smem_u32(sm + PrepSmem::TBG), tb = smem_u32(sm + PrepSmem::TB);
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      const uint64_t bk = prefill::sdesc(k0 + ks * 16 * 128, C * 128, 1024);
+      const uint64_t bv = prefill::sdesc(v0 + ks * 16 * 128, C * 128, 1024);
+      prefill::umma_ss(tmem, prefill::sdesc(tg + ks * 32, 16, 1024), bk, IDESC_W, ks ? 1u : 0u);
+      prefill::umma_ss(tmem, prefill::sdesc(tg + C * 128 + ks * 32, 16, 1024), bk, IDESC_W, 1u);
+      prefill::umma_ss(tmem + LANE16, prefill::sdesc(tb + ks * 32, 16, 1024), bv, IDESC_W, ks ? 1u : 0u);
+      prefill::umma_ss(tmem + LANE16, prefill::sdesc(tb + C * 128 + ks * 32, 16, 1024), bv, IDESC_W, 1u);
+    }
+    prefill::umma_commit(&bar[1]);
+  }
+  ok = __all_sync(0xffffffffu, ok && mbar_wait(&bar[1], 1, 77));
+  // 7. W (lanes 0-15: row t) as hi / lo pairs, U' (lanes 16-31: row t) in fp32 slices, to the workspace; 64 columns
+  // at a time
+  {
+    const int t = 16 * warp + (lane & 15);
+    if (ok) prefill::tc_fence_after();
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {
+      float x[C];
+      if (ok) {
+        prefill::tmem_ld32(tmem + lq + half * C, x);
+        prefill::tmem_ld32(tmem + lq + half * C + 32, x + 32);
+        prefill::tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int j = 0; j < C; ++j) x[j] = 0.f;
+      }
+      if (lane < 16) {
+        put_row_pair<T>(unit + WS_WHI + half * C * 128, unit + WS_WLO + half * C * 128, t, x);
+      } else {
+#pragma unroll
+        for (int s2 = 0; s2 < 2; ++s2) {  // value columns half 64 + s2 32 .. : slice 2 half + s2
+          float4* g = reinterpret_cast<float4*>(unit + WS_U + (2 * half + s2) * USLICE + t * UP * 4);
+#pragma unroll
+          for (int q4 = 0; q4 < DVB / 4; ++q4)
+            g[q4] = make_float4(x[32 * s2 + 4 * q4], x[32 * s2 + 4 * q4 + 1], x[32 * s2 + 4 * q4 + 2],
+                                x[32 * s2 + 4 * q4 + 3]);
         }
       }
-      __syncthreads();
-#pragma unroll 1
-      for (int mt = 0; mt < 4; ++mt) {
-        const int m0 = mt * 16;
-        float acc[4][4];
-#pragma unroll
-        for (int n = 0; n < 4; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
-        for (int k0 = 0; k0 < m0 + 16; k0 += 8) {
-          const uint32_t a0 = tf32(Af[(m0 + r) * AP + k0 + cq]), a1 = tf32(Af[(m0 + r + 8) * AP + k0 + cq]);
-          const uint32_t a2 = tf32(Af[(m0 + r) * AP + k0 + cq + 4]), a3 = tf32(Af[(m0 + r + 8) * AP + k0 + cq + 4]);
-#pragma unroll
-          for (int n = 0; n < 4; ++n) {
-            const int n0 = nw + n * 8;
-            mma_tf32(acc[n], a0, a1, a2, a3, tf32_of(R[(k0 + cq) * KP + n0 + r]),
-                     tf32_of(R[(k0 + cq + 4) * KP + n0 + r]));
-          }
-        }
-#pragma unroll
-        for (int n = 0; n < 4; ++n) {  // U' fp32 in slices of DVB columns (rows of stride UP); W as hi / lo pairs
-          const int col = nw + n * 8 + 2 * cq;
-          if (which) {
-            float* g0 = reinterpret_cast<float*>(unit + WS_U) + ((col / DVB) * C + m0 + r) * UP + col % DVB;
-            *reinterpret_cast<float2*>(g0) = make_float2(acc[n][0], acc[n][1]);
-            *reinterpret_cast<float2*>(g0 + 8 * UP) = make_float2(acc[n][2], acc[n][3]);
-          } else {
-            uint8_t* hi = unit + WS_WHI + (col >> 6) * (C * 128);
-            uint8_t* lo = unit + WS_WLO + (col >> 6) * (C * 128);
-            store_split2<T>(hi, lo, sw128(m0 + r, col & 63), acc[n][0], acc[n][1]);
-            store_split2<T>(hi, lo, sw128(m0 + r + 8, col & 63), acc[n][2], acc[n][3]);
-          }
-        }
-      }
-      __syncthreads();  // every warp has read T before it is scaled again
     }
   }
-  // 7. gamma and Gam for the scan
+  // 8. gamma and Gam for the scan
   if (tid < C) {
-    float* gg = reinterpret_cast<float*>(unit_ptr(p, b, h, c) + WS_G);
+    float* gg = reinterpret_cast<float*>(unit + WS_G);
     gg[tid] = gam[tid];
     gg[C + tid] = Gam[tid];
+  }
+  prefill::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    prefill::tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(PREP_TMEM_COLS));
   }
 }
 

@@ -940,13 +940,16 @@ int lb2_gdn_chunked(const void* q, const void* k, int qdt, const void* v, int vd
   gdnchunk::Params p{q, k, v, g, beta, qdt, vdt, gdt, bdt, state_in, state_out, y, B, T, Hk, Hv,
                      (T + gdnchunk::C - 1) / gdnchunk::C, static_cast<float*>(workspace)};
   // Q and K tiles of the scan: [B, T, Hk, Dk] contiguous, 64-column boxes of 64 positions (rows past T read as 0)
-  CUtensorMap qm, km;
+  CUtensorMap qm, km, vm;
   std::memset(&qm, 0, sizeof(qm));
   std::memset(&km, 0, sizeof(km));
+  std::memset(&vm, 0, sizeof(vm));
   if (T > 0) {
     const int64_t qk_st[3] = {int64_t(T) * Hk * Dk, Dk, int64_t(Hk) * Dk};
+    const int64_t v_st[3] = {int64_t(T) * Hv * Dv, Dv, int64_t(Hv) * Dv};
     int rc = prefill::map4(&qm, q, qk_st, B, Hk, T, Dk, qdt, gdnchunk::C);
     if (!rc) rc = prefill::map4(&km, k, qk_st, B, Hk, T, Dk, qdt, gdnchunk::C);
+    if (!rc) rc = prefill::map4(&vm, v, v_st, B, Hv, T, Dv, vdt, gdnchunk::C);
     if (rc) return rc;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -966,10 +969,11 @@ int lb2_gdn_chunked(const void* q, const void* k, int qdt, const void* v, int vd
   }
   const dim3 gp(unsigned(p.nchunks), unsigned(Hv), unsigned(B)), gs(gdnchunk::DV / gdnchunk::DVB, Hv, B);
   if (qdt == LB2_BF16) {
-    if (p.nchunks > 0) gdnchunk::prep_kernel<__nv_bfloat16><<<gp, 128, gdnchunk::PrepSmem::BYTES, st>>>(p);
+    if (p.nchunks > 0)
+      gdnchunk::prep_kernel<__nv_bfloat16><<<gp, 128, gdnchunk::PrepSmem::BYTES, st>>>(qm, km, vm, p);
     gdnchunk::scan_kernel<__nv_bfloat16><<<gs, gdnchunk::TC_THREADS, gdnchunk::TcSmem::BYTES, st>>>(qm, km, p);
   } else {
-    if (p.nchunks > 0) gdnchunk::prep_kernel<__half><<<gp, 128, gdnchunk::PrepSmem::BYTES, st>>>(p);
+    if (p.nchunks > 0) gdnchunk::prep_kernel<__half><<<gp, 128, gdnchunk::PrepSmem::BYTES, st>>>(qm, km, vm, p);
     gdnchunk::scan_kernel<__half><<<gs, gdnchunk::TC_THREADS, gdnchunk::TcSmem::BYTES, st>>>(qm, km, p);
   }
   LB2_CUDA(cudaGetLastError());
