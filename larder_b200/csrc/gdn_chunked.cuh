@@ -93,26 +93,28 @@ __device__ __forceinline__ uint8_t* unit_ptr(const Params& p, int b, int h, int 
 //   A = diag(beta) (decay x K K^T) strictly below the diagonal, M = decay x Q K^T on and below it (M as a hi / lo pair
 //   straight to the workspace); T = (I + A)^{-1} in fp32 on the CUDA cores (16 x 16 diagonal blocks by substitution,
 //   then the 2 x 2 block formula at 32 and 64);
-//   P_W  W = (T diag(beta Gam)) K (lane 0) and U' = (T diag(beta)) V (lane 16), N = 128: A = the scaled T as a hi / lo
-//   pair, B = the K / V tile read MN-major (positions are the products' K).
+//   P_W  W = (T diag(beta Gam)) K (lane 0), then U' = (T diag(beta)) V (lane 16), N = 128: A = the scaled T as a hi /
+//   lo pair, B = the K / V tile read MN-major (positions are the products' K).
 
 constexpr int PREP_TMEM_COLS = 128;
 constexpr int XP = 40;  // row stride of the inversion scratch
 
+// 16 KB regions reused as the steps go, so that three CTAs fit an SM: the Q tile is dead after P_A (its region then
+// holds the inversion scratch, then T diag(beta Gam)); the K tile after W's products (then T diag(beta)).
 struct PrepSmem {
-  static constexpr int K0 = 0;                  // K tile: two TMA boxes [64 positions][64 keys], 8 KB each
-  static constexpr int Q0 = K0 + 2 * C * 128;   // Q tile, the same
-  static constexpr int V0 = Q0 + 2 * C * 128;   // V tile, the same (64 value columns a box)
-  static constexpr int TBG = V0 + 2 * C * 128;  // T diag(beta Gam) as hi, lo: [64][64] 16-bit, 8 KB each
-  static constexpr int TB = TBG + 2 * C * 128;  // T diag(beta) as hi, lo
-  static constexpr int AF = TB + 2 * C * 128;   // f32 [C][AP]: A, then T
-  static constexpr int XS = AF + C * AP * 4;    // f32 [32][XP] inversion scratch
-  static constexpr int GAM = XS + 32 * XP * 4;  // f32 [C] gamma, [C] Gam, [C] beta
+  static constexpr int K0 = 0;                  // K tile: two TMA boxes [64 positions][64 keys]; later T diag(beta)
+  static constexpr int V0 = K0 + 2 * C * 128;   // V tile, the same (64 value columns a box)
+  static constexpr int Q0 = V0 + 2 * C * 128;   // Q tile; later the inversion scratch, then T diag(beta Gam)
+  static constexpr int TBG = Q0;                // hi, lo: [64][64] 16-bit, 8 KB each
+  static constexpr int TB = K0;
+  static constexpr int XS = Q0;                 // f32 [32][XP]
+  static constexpr int AF = Q0 + 2 * C * 128;   // f32 [C][AP]: A, then T
+  static constexpr int GAM = AF + C * AP * 4;   // f32 [C] gamma, [C] Gam, [C] beta
   static constexpr int BAR = GAM + 3 * C * 4;   // 2 mbarriers: loads landed, MMAs done
   static constexpr int SLOT = BAR + 16;         // TMEM base address
   static constexpr int BYTES = SLOT + 16 + 1024;
 };
-static_assert(PrepSmem::AF % 1024 == 0 && PrepSmem::BYTES <= 116 * 1024, "two prep CTAs an SM");
+static_assert(PrepSmem::AF % 1024 == 0 && PrepSmem::BYTES <= 75 * 1024, "three prep CTAs an SM");
 
 // acc (a 16 x 8 tile in the m16n8 fragment layout: lane (r = lane / 4, q = lane % 4) holds (r, 2q), (r, 2q + 1),
 // (r + 8, 2q), (r + 8, 2q + 1)) += L R over K = 8 ksteps, fp32 on the CUDA cores: L's rows at Lp (stride ldl), R's
@@ -343,75 +345,96 @@ __global__ void __launch_bounds__(128) prep_kernel(const __grid_constant__ CUten
     }
   }
   __syncthreads();
-  // 5. the P_W operands: thread r < 64 writes row r of T diag(beta Gam), thread 64 + r row r of T diag(beta), as
-  // hi / lo pairs
-  {
-    const int r = tid & 63;
-    const bool vb = tid >= 64;
+  // 5. W = T diag(beta Gam) K (lane 0): threads 0-63 write row t of its A operand (a hi / lo pair) where the Q tile
+  // was; K = 64 positions in four steps of 16 rows of the K tile (B MN-major: its two 64-key boxes 8 KB apart)
+  if (tid < C) {
     float x[C];
 #pragma unroll
     for (int j = 0; j < C; j += 4) {
-      const float4 a = *reinterpret_cast<const float4*>(Af + r * AP + j);
-      const float f[4] = {bet[j] * (vb ? 1.f : Gam[j]), bet[j + 1] * (vb ? 1.f : Gam[j + 1]),
-                          bet[j + 2] * (vb ? 1.f : Gam[j + 2]), bet[j + 3] * (vb ? 1.f : Gam[j + 3])};
-      x[j] = a.x * f[0];
-      x[j + 1] = a.y * f[1];
-      x[j + 2] = a.z * f[2];
-      x[j + 3] = a.w * f[3];
+      const float4 a = *reinterpret_cast<const float4*>(Af + tid * AP + j);
+      x[j] = a.x * bet[j] * Gam[j];
+      x[j + 1] = a.y * bet[j + 1] * Gam[j + 1];
+      x[j + 2] = a.z * bet[j + 2] * Gam[j + 2];
+      x[j + 3] = a.w * bet[j + 3] * Gam[j + 3];
     }
-    uint8_t* dst = sm + (vb ? PrepSmem::TB : PrepSmem::TBG);
-    put_row_pair<T>(dst, dst + C * 128, r, x);
+    put_row_pair<T>(sm + PrepSmem::TBG, sm + PrepSmem::TBG + C * 128, tid, x);
   }
   fence_proxy_async_shared();
   prefill::tc_fence_before();
   __syncthreads();
-  // 6. P_W: W (lane 0) = T diag(beta Gam) K, U' (lane 16) = T diag(beta) V; K = 64 positions in four steps of 16 rows
-  // of the K / V tile (B MN-major: its two 64-column boxes 8 KB apart)
   if (tid == 0 && ok) {
     prefill::tc_fence_after();
-    const uint32_t k0 = smem_u32(sm + PrepSmem::K0), v0 = smem_u32(sm + PrepSmem::V0);
-    const uint32_t tg = smem_u32(sm + PrepSmem::TBG), tb = smem_u32(sm + PrepSmem::TB);
+    const uint32_t k0 = smem_u32(sm + PrepSmem::K0), tg = smem_u32(sm + PrepSmem::TBG);
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) {
       const uint64_t bk = prefill::sdesc(k0 + ks * 16 * 128, C * 128, 1024);
-      const uint64_t bv = prefill::sdesc(v0 + ks * 16 * 128, C * 128, 1024);
       prefill::umma_ss(tmem, prefill::sdesc(tg + ks * 32, 16, 1024), bk, IDESC_W, ks ? 1u : 0u);
       prefill::umma_ss(tmem, prefill::sdesc(tg + C * 128 + ks * 32, 16, 1024), bk, IDESC_W, 1u);
+    }
+    prefill::umma_commit(&bar[1]);
+  }
+  ok = __all_sync(0xffffffffu, ok && mbar_wait(&bar[1], 1, 77));
+  // 6. U' = T diag(beta) V (lane 16): threads 64-127 write its A operand where the K tile was (W's products are done
+  // with it), then while those MMAs run every warp takes W out of TMEM (lanes 0-15: row t) as hi / lo pairs
+  if (tid >= C) {
+    const int r = tid - C;
+    float x[C];
+#pragma unroll
+    for (int j = 0; j < C; j += 4) {
+      const float4 a = *reinterpret_cast<const float4*>(Af + r * AP + j);
+      x[j] = a.x * bet[j];
+      x[j + 1] = a.y * bet[j + 1];
+      x[j + 2] = a.z * bet[j + 2];
+      x[j + 3] = a.w * bet[j + 3];
+    }
+    put_row_pair<T>(sm + PrepSmem::TB, sm + PrepSmem::TB + C * 128, r, x);
+  }
+  fence_proxy_async_shared();
+  prefill::tc_fence_before();
+  __syncthreads();
+  if (tid == 0 && ok) {
+    prefill::tc_fence_after();
+    const uint32_t v0 = smem_u32(sm + PrepSmem::V0), tb = smem_u32(sm + PrepSmem::TB);
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      const uint64_t bv = prefill::sdesc(v0 + ks * 16 * 128, C * 128, 1024);
       prefill::umma_ss(tmem + LANE16, prefill::sdesc(tb + ks * 32, 16, 1024), bv, IDESC_W, ks ? 1u : 0u);
       prefill::umma_ss(tmem + LANE16, prefill::sdesc(tb + C * 128 + ks * 32, 16, 1024), bv, IDESC_W, 1u);
     }
     prefill::umma_commit(&bar[1]);
   }
-  ok = __all_sync(0xffffffffu, ok && mbar_wait(&bar[1], 1, 77));
-  // 7. W (lanes 0-15: row t) as hi / lo pairs, U' (lanes 16-31: row t) in fp32 slices, to the workspace; 64 columns
-  // at a time
-  {
-    const int t = 16 * warp + (lane & 15);
-    if (ok) prefill::tc_fence_after();
+  const int t = 16 * warp + (lane & 15);
+  if (ok) prefill::tc_fence_after();
 #pragma unroll 1
-    for (int half = 0; half < 2; ++half) {
-      float x[C];
-      if (ok) {
-        prefill::tmem_ld32(tmem + lq + half * C, x);
-        prefill::tmem_ld32(tmem + lq + half * C + 32, x + 32);
-        prefill::tmem_wait_ld();
-      } else {
-#pragma unroll
-        for (int j = 0; j < C; ++j) x[j] = 0.f;
-      }
-      if (lane < 16) {
-        put_row_pair<T>(unit + WS_WHI + half * C * 128, unit + WS_WLO + half * C * 128, t, x);
-      } else {
-#pragma unroll
-        for (int s2 = 0; s2 < 2; ++s2) {  // value columns half 64 + s2 32 .. : slice 2 half + s2
-          float4* g = reinterpret_cast<float4*>(unit + WS_U + (2 * half + s2) * USLICE + t * UP * 4);
-#pragma unroll
-          for (int q4 = 0; q4 < DVB / 4; ++q4)
-            g[q4] = make_float4(x[32 * s2 + 4 * q4], x[32 * s2 + 4 * q4 + 1], x[32 * s2 + 4 * q4 + 2],
-                                x[32 * s2 + 4 * q4 + 3]);
-        }
-      }
+  for (int half = 0; half < 2; ++half) {  // W, 64 key columns at a time
+    float x[C];
+    if (ok) {
+      prefill::tmem_ld32(tmem + lq + half * C, x);
+      prefill::tmem_ld32(tmem + lq + half * C + 32, x + 32);
+      prefill::tmem_wait_ld();
     }
+    if (lane < 16 && ok) put_row_pair<T>(unit + WS_WHI + half * C * 128, unit + WS_WLO + half * C * 128, t, x);
+  }
+  // 7. U' (lanes 16-31: row t) in fp32 slices of 32 value columns
+  ok = __all_sync(0xffffffffu, ok && mbar_wait(&bar[1], 0, 78));
+  if (ok) prefill::tc_fence_after();
+#pragma unroll 1
+  for (int half = 0; half < 2; ++half) {
+    float x[C];
+    if (ok) {
+      prefill::tmem_ld32(tmem + lq + half * C, x);
+      prefill::tmem_ld32(tmem + lq + half * C + 32, x + 32);
+      prefill::tmem_wait_ld();
+    }
+    if (lane >= 16 && ok)
+#pragma unroll
+      for (int s2 = 0; s2 < 2; ++s2) {  // value columns 64 half + 32 s2 ..: slice 2 half + s2
+        float4* g = reinterpret_cast<float4*>(unit + WS_U + (2 * half + s2) * USLICE + t * UP * 4);
+#pragma unroll
+        for (int q4 = 0; q4 < DVB / 4; ++q4)
+          g[q4] = make_float4(x[32 * s2 + 4 * q4], x[32 * s2 + 4 * q4 + 1], x[32 * s2 + 4 * q4 + 2],
+                              x[32 * s2 + 4 * q4 + 3]);
+      }
   }
   // 8. gamma and Gam for the scan
   if (tid < C) {
