@@ -454,15 +454,18 @@ __global__ void __launch_bounds__(128) prep_kernel(const __grid_constant__ CUten
 //
 // One CTA: value columns dv0 .. dv0 + 31 of one (batch, v-head), all chunks in order, every product on the tensor
 // cores (tcgen05.mma kind::f16, accumulators in TMEM). The state slice S [32 value rows x 128 keys] is kept in fp32
-// registers of the epilogue warps (thread k holds column k: S[0 .. 31][k]) and given to the MMAs as a 16-bit hi / lo
-// pair in shared memory. Per chunk:
-//   P1  D1 = [W_hi ; Q] (S_hi + S_lo)^T   (M = 128: rows 0-63 W, rows 64-127 Q; N = 32; K = 128)
-//       D4 = W_lo S_hi^T                   (rows 0-63 used)                 -> W S^T = D1[0:64] + D4[0:64]
-//   E-U U = U' - W S^T (warps 0-1, thread = position), Ud = diag(exp(gamma_C - gamma)) U, both as hi / lo pairs
-//   P2  D2 = K^T (Ud_hi + Ud_lo)           (M = 128 keys, A = the K tile as the TMA loads it, MN-major; K = 64)
-//   P3  D3 = M_hi (U_hi + U_lo) + M_lo U_hi (rows 64-127 used)
-//   E-S S <- Gam_C S + D2 (all four warps, thread = key)                    -> the next P1's operand
-//   E-Y Y = Gam (D1[64:128]) + D3[64:128] (warps 2-3, thread = position)    -> y
+// registers of the eight epilogue warps (two threads a key k, one with S[0 .. 15][k], one with S[16 .. 31][k]) and
+// given to the MMAs as a 16-bit hi / lo pair in shared memory. Every B operand is MN-major with N = 64: the 32 value
+// rows' hi halves, then their lo halves, so one MMA reads its A tile once for both halves and an epilogue thread writes
+// its row with four 16-byte stores. Per chunk:
+//   P1  D1 = [W_hi ; Q] [S_hi | S_lo]^T   (M = 128: rows 0-63 W, rows 64-127 Q; K = 128)
+//       D4 = W_lo [S_hi | S_lo]^T           (rows 0-63 used)      -> W S^T = D1[0:64] + D4[0:64], both halves summed
+//   E-U U = U' - W S^T (TMEM lanes 0-63: thread = position, half the columns), Ud = diag(exp(gamma_C - gamma)) U,
+//       both as hi / lo pairs
+//   P2  D2 = K^T [Ud_hi | Ud_lo]           (M = 128 keys, A = the K tile as the TMA loads it, MN-major; K = 64)
+//   P3  D3 = (M_hi + M_lo) [U_hi | U_lo]^T  (rows 64-127 used)
+//   E-S S <- Gam_C S + D2 (all eight warps, thread = key, half the columns) -> the next P1's operand
+//   E-Y Y = Gam (D1[64:128]) + D3[64:128] (lanes 64-127: thread = position) -> y
 // The chain from one chunk to the next is P1 -> E-U -> P2 -> E-S; P3 and E-Y run beside it (D1 / D3 / D4 are
 // double-buffered by chunk parity, so E-Y may lag a chunk). Chunk c's W, M, gates and U' slice arrive by bulk copies
 // and its Q and K tiles by tiled TMA, into one of two buffers, a chunk ahead.
@@ -470,8 +473,12 @@ __global__ void __launch_bounds__(128) prep_kernel(const __grid_constant__ CUten
 // Rows past T in the last chunk: Q and K arrive as zeros and prep left W, U' zero there, so they add nothing; their
 // y is not stored.
 
-constexpr int TC_THREADS = 192;  // warps 0-3 epilogue (TMEM lane quarters), warp 4 loads, warp 5 MMA
-constexpr int TC_TMEM_COLS = 256;
+// warps 0-7 epilogue: warp w reads TMEM lane quarter w % 4 and takes value columns 16 (w / 4) .. + 15 of the
+// slice; warp 8 loads, warp 9 issues the MMAs
+constexpr int TC_EPI = 8, TC_LOAD = 8, TC_MMA = 9;
+constexpr int TC_THREADS = 320;
+constexpr int VH = DVB / 2;      // value columns a thread
+constexpr int TC_TMEM_COLS = 512;
 
 struct TcSmem {
   // one chunk buffer (two of them): the shared-memory images of the workspace pieces, each operand 1024-aligned
@@ -484,13 +491,12 @@ struct TcSmem {
   static constexpr int K = (U + USLICE + 1023) / 1024 * 1024;  // K tile: two TMA boxes [64 positions][64 keys]
   static constexpr int BUF = K + 2 * C * 128;
   // persistent operands (16-bit, 128-byte swizzle, K-major)
-  static constexpr int SHI = 2 * BUF;          // S_hi [32 value rows][128 keys]: two 4 KB blocks
-  static constexpr int SLO = SHI + 2 * DVB * 128;
-  static constexpr int UDHI = SLO + 2 * DVB * 128;  // Ud_hi [32 value rows][64 positions]
-  static constexpr int UDLO = UDHI + DVB * 128;
-  static constexpr int UHI = UDLO + DVB * 128;
-  static constexpr int ULO = UHI + DVB * 128;
-  static constexpr int BAR = ULO + DVB * 128;  // mbarriers
+  // B operands of the chain, MN-major (N = 64: the 32 value rows' hi halves, then their lo halves, a 128-byte row):
+  // S^T [128 keys][hi 32 | lo 32] (16 KB), Ud [64 positions][hi 32 | lo 32] (8 KB), U the same
+  static constexpr int SOP = 2 * BUF;
+  static constexpr int UDOP = SOP + DK * 128;
+  static constexpr int UOP = UDOP + C * 128;
+  static constexpr int BAR = UOP + C * 128;    // mbarriers
   static constexpr int NBAR = 16;
   static constexpr int SLOT = BAR + NBAR * 8;  // TMEM base address; abort flag
   static constexpr int BYTES = SLOT + 16 + 1024;  // (+ alignment of the dynamic shared memory base)
@@ -498,22 +504,24 @@ struct TcSmem {
   static constexpr uint32_t TX = 2 * C * 128 + (WS_U - WS_WLO) + USLICE + 4 * C * 128;
 };
 static_assert(TcSmem::WLO - TcSmem::A1 == 4 * 8192 && TcSmem::G - TcSmem::WLO == WS_G - WS_WLO, "copy layout");
-static_assert(TcSmem::BUF % 1024 == 0 && TcSmem::SHI % 1024 == 0 && TcSmem::BYTES <= 232448, "scan shared memory");
+static_assert(TcSmem::BUF % 1024 == 0 && TcSmem::SOP % 1024 == 0 && TcSmem::BYTES <= 232448, "scan shared memory");
 
 // barrier slots
 constexpr int B_FULL = 0;     // [2] a buffer's copies landed
-constexpr int B_EMPTY = 2;    // [2] a buffer is free: its MMAs committed and the four epilogue warps done with it
-constexpr int B_SREADY = 4;   // the state operand of the next chunk written (four warps)
+constexpr int B_EMPTY = 2;    // [2] a buffer is free: its MMAs committed and the eight epilogue warps done with it
+constexpr int B_SREADY = 4;   // the state operand of the next chunk written (eight warps)
 constexpr int B_D1 = 5;       // [2] P1 done
-constexpr int B_UREADY = 7;   // U operands written (warps 0-1)
+constexpr int B_UREADY = 7;   // U operands written (warps 0, 1, 4, 5)
 constexpr int B_D2 = 8;       // P2 done
 constexpr int B_D3 = 9;       // [2] P3 done
-constexpr int B_YDONE = 11;   // [2] E-Y read D1 / D3 of that parity (warps 2-3)
+constexpr int B_YDONE = 11;   // [2] E-Y read D1 / D3 of that parity (warps 2, 3, 6, 7)
 constexpr int B_DRAIN = 13;   // every MMA issued has completed (the MMA thread's exit)
-constexpr int B_UDREADY = 14; // Ud operands written (warps 0-1): P2 may start
+constexpr int B_UDREADY = 14; // Ud operands written (warps 0, 1, 4, 5): P2 may start
 
 // TMEM columns
-constexpr uint32_t T_D1 = 0, T_D4 = 64, T_D3 = 128, T_D2 = 192;  // D1, D4, D3: two 32-column buffers each
+// D1 = [W_hi ; Q] [S_hi | S_lo]^T, D4 = W_lo [S_hi | S_lo]^T and D3 = (M_hi + M_lo) [U_hi | U_lo]^T: two 64-column
+// buffers each (the products with the hi and the lo halves side by side); D2 = K^T [Ud_hi | Ud_lo]: 64 columns
+constexpr uint32_t T_D1 = 0, T_D3 = 128, T_D4 = 256, T_D2 = 384;
 
 // The chunk's 16-bit operand pair of value x: (hi, lo) of the activation type.
 template <typename T>
@@ -524,19 +532,34 @@ __device__ __forceinline__ void split_pair(float x, uint16_t& hi, uint16_t& lo) 
   lo = *reinterpret_cast<const uint16_t*>(&l);
 }
 
-// Writes column `col` (a key or a position) of a [32 rows][cols] 16-bit K-major operand pair: row j gets x[j].
+// Writes the 16 values x (value rows r0 .. r0 + 15) into row `row` (a key or a position) of an MN-major operand
+// [rows][hi 32 | lo 32]: the hi halves at elements r0 .., the lo halves at 32 + r0 .., four 16-byte stores.
 template <typename T>
-__device__ __forceinline__ void put_column(uint8_t* hi, uint8_t* lo, int col, const float* x) {
-  uint8_t* bh = hi + (col >> 6) * (DVB * 128);
-  uint8_t* bl = lo + (col >> 6) * (DVB * 128);
+__device__ __forceinline__ void put_row16(uint8_t* op, int row, int r0, const float* x) {
+  uint32_t h[8], l[8];
 #pragma unroll
-  for (int j = 0; j < DVB; ++j) {
-    uint16_t h, l;
-    split_pair<T>(x[j], h, l);
-    const int off = sw128(j, col & 63);
-    *reinterpret_cast<uint16_t*>(bh + off) = h;
-    *reinterpret_cast<uint16_t*>(bl + off) = l;
+  for (int e = 0; e < 8; ++e) {
+    uint16_t h0, l0, h1, l1;
+    split_pair<T>(x[2 * e], h0, l0);
+    split_pair<T>(x[2 * e + 1], h1, l1);
+    h[e] = uint32_t(h0) | (uint32_t(h1) << 16);
+    l[e] = uint32_t(l0) | (uint32_t(l1) << 16);
   }
+  uint8_t* r = op + row * 128;
+  const int c0 = r0 >> 3, sw = row & 7;
+  *reinterpret_cast<uint4*>(r + (((c0) ^ sw) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+  *reinterpret_cast<uint4*>(r + (((c0 + 1) ^ sw) << 4)) = make_uint4(h[4], h[5], h[6], h[7]);
+  *reinterpret_cast<uint4*>(r + (((c0 + 4) ^ sw) << 4)) = make_uint4(l[0], l[1], l[2], l[3]);
+  *reinterpret_cast<uint4*>(r + (((c0 + 5) ^ sw) << 4)) = make_uint4(l[4], l[5], l[6], l[7]);
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
 }
 
 template <typename T>
@@ -544,8 +567,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) scan_kernel(const __grid_consta
                                                               const __grid_constant__ CUtensorMap kmap,
                                                               const Params p) {
   constexpr uint32_t AB = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
-  constexpr uint32_t IDESC_K = prefill::idesc_f16(AB, 0, 0, 128, DVB);   // A K-major
-  constexpr uint32_t IDESC_MN = prefill::idesc_f16(AB, 1, 0, 128, DVB);  // A MN-major (the K tile as K^T)
+  // B always MN-major [K rows][hi 32 | lo 32] (N = 64); A K-major, or MN-major for the K tile read as K^T
+  constexpr uint32_t IDESC_K2 = prefill::idesc_f16(AB, 0, 1, 128, 2 * DVB);
+  constexpr uint32_t IDESC_MN2 = prefill::idesc_f16(AB, 1, 1, 128, 2 * DVB);
   const int blk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int hk = h / (p.Hv / p.Hk);
   const int dv0 = blk * DVB;
@@ -560,20 +584,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1) scan_kernel(const __grid_consta
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar[B_FULL + i], 1);
-      mbar_init(&bar[B_EMPTY + i], 5);  // the MMA commit + one arrive per epilogue warp
+      mbar_init(&bar[B_EMPTY + i], 1 + TC_EPI);  // the MMA commit + one arrive per epilogue warp
       mbar_init(&bar[B_D1 + i], 1);
       mbar_init(&bar[B_D3 + i], 1);
-      mbar_init(&bar[B_YDONE + i], 2);
+      mbar_init(&bar[B_YDONE + i], TC_EPI / 2);
     }
-    mbar_init(&bar[B_SREADY], 4);
-    mbar_init(&bar[B_UREADY], 2);
-    mbar_init(&bar[B_UDREADY], 2);
+    mbar_init(&bar[B_SREADY], TC_EPI);
+    mbar_init(&bar[B_UREADY], TC_EPI / 2);
+    mbar_init(&bar[B_UDREADY], TC_EPI / 2);
     mbar_init(&bar[B_D2], 1);
     mbar_init(&bar[B_DRAIN], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == TC_MMA) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
                  "r"(TC_TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -583,16 +607,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) scan_kernel(const __grid_consta
   prefill::tc_fence_after();
   const uint32_t tmem = *slot;
 
-  if (warp < 4) {
+  if (warp < TC_EPI) {
     // ------------------------------------------------------------------------------------ epilogue warps
-    const int k = 32 * warp + lane;                // this thread's key column of S
-    const uint32_t lq = uint32_t(32 * warp) << 16;  // the warp's TMEM lane quarter
-    float s[DVB];
-    const float* sin = p.s_in + (int64_t(b) * p.Hv + h) * DV * DK + int64_t(dv0) * DK + k;
+    const int quarter = warp & 3, vh = warp >> 2;
+    const int k = 32 * quarter + lane;                // this thread's key column of S (and TMEM lane)
+    const int r0 = VH * vh;                           // its value rows r0 .. r0 + 15 of the slice
+    const uint32_t lq = uint32_t(32 * quarter) << 16;  // the warp's TMEM lane quarter
+    float s[VH];
+    const float* sin = p.s_in + (int64_t(b) * p.Hv + h) * DV * DK + int64_t(dv0 + r0) * DK + k;
 #pragma unroll
-    for (int j = 0; j < DVB; ++j) s[j] = sin[int64_t(j) * DK];
+    for (int j = 0; j < VH; ++j) s[j] = sin[int64_t(j) * DK];
     if (n > 0) {
-      put_column<T>(sm + TcSmem::SHI, sm + TcSmem::SLO, k, s);
+      put_row16<T>(sm + TcSmem::SOP, k, r0, s);
       fence_proxy_async_shared();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[B_SREADY]);
@@ -606,14 +632,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) scan_kernel(const __grid_consta
       // the chunk's buffer has landed (it did before P1 could run): gates and U' are read off the chain
       ok = __all_sync(0xffffffffu, mbar_wait(&bar[B_FULL + par], (c >> 1) & 1, 80) && !*abort_flag);
       if (!ok) break;
-      if (warp < 2) {  // E-U: positions t = k (0 .. 63)
+      if (quarter < 2) {  // E-U: positions t = k (0 .. 63)
         const int t = k;
         const float dec = __expf(gam[C - 1] - gam[t]);
-        float u[DVB];
+        float u[VH];
         {
-          const float4* up = reinterpret_cast<const float4*>(buf + TcSmem::U + t * UP * 4);
+          const float4* up = reinterpret_cast<const float4*>(buf + TcSmem::U + t * UP * 4 + r0 * 4);
 #pragma unroll
-          for (int q4 = 0; q4 < DVB / 4; ++q4) {
+          for (int q4 = 0; q4 < VH / 4; ++q4) {
             const float4 x = up[q4];
             u[4 * q4] = x.x, u[4 * q4 + 1] = x.y, u[4 * q4 + 2] = x.z, u[4 * q4 + 3] = x.w;
           }
@@ -622,24 +648,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1) scan_kernel(const __grid_consta
         if (!ok) break;
         prefill::tc_fence_after();
         {
-          float d[DVB], d4[DVB];
-          prefill::tmem_ld32(tmem + lq + T_D1 + par * 32, d);
-          prefill::tmem_ld32(tmem + lq + T_D4 + par * 32, d4);
+          float d[VH], dl[VH], d4[VH], d4l[VH];
+          tmem_ld16(tmem + lq + T_D1 + par * 64 + r0, d);
+          tmem_ld16(tmem + lq + T_D1 + par * 64 + DVB + r0, dl);
+          tmem_ld16(tmem + lq + T_D4 + par * 64 + r0, d4);
+          tmem_ld16(tmem + lq + T_D4 + par * 64 + DVB + r0, d4l);
           prefill::tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < DVB; ++j) u[j] -= d[j] + d4[j];
+          for (int j = 0; j < VH; ++j) u[j] -= (d[j] + dl[j]) + (d4[j] + d4l[j]);
         }
         prefill::tc_fence_before();
         {  // Ud first: the state update (P2) waits for it; U (P3, off the chain) after
-          float ud[DVB];
+          float ud[VH];
 #pragma unroll
-          for (int j = 0; j < DVB; ++j) ud[j] = dec * u[j];
-          put_column<T>(sm + TcSmem::UDHI, sm + TcSmem::UDLO, t, ud);
+          for (int j = 0; j < VH; ++j) ud[j] = dec * u[j];
+          put_row16<T>(sm + TcSmem::UDOP, t, r0, ud);
         }
         fence_proxy_async_shared();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bar[B_UDREADY]);
-        put_column<T>(sm + TcSmem::UHI, sm + TcSmem::ULO, t, u);
+        put_row16<T>(sm + TcSmem::UOP, t, r0, u);
         fence_proxy_async_shared();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bar[B_UREADY]);
@@ -650,27 +678,35 @@ __global__ void __launch_bounds__(TC_THREADS, 1) scan_kernel(const __grid_consta
       if (!ok) break;
       prefill::tc_fence_after();
       {
-        float d2[DVB];
-        prefill::tmem_ld32(tmem + lq + T_D2, d2);
+        float d2[VH], d2l[VH];
+        tmem_ld16(tmem + lq + T_D2 + r0, d2);
+        tmem_ld16(tmem + lq + T_D2 + DVB + r0, d2l);
         prefill::tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < DVB; ++j) s[j] = fmaf(gc, s[j], d2[j]);
+        for (int j = 0; j < VH; ++j) s[j] = fmaf(gc, s[j], d2[j] + d2l[j]);
       }
       if (c + 1 < n) {
-        put_column<T>(sm + TcSmem::SHI, sm + TcSmem::SLO, k, s);
+        put_row16<T>(sm + TcSmem::SOP, k, r0, s);
         fence_proxy_async_shared();
       }
       prefill::tc_fence_before();
       __syncwarp();
       if (lane == 0 && c + 1 < n) mbar_arrive(&bar[B_SREADY]);
-      if (warp >= 2) {  // E-Y: positions t = k - 64
+      if (quarter >= 2) {  // E-Y: positions t = k - 64
         ok = __all_sync(0xffffffffu, mbar_wait(&bar[B_D3 + par], (c >> 1) & 1, 83) && !*abort_flag);
         if (!ok) break;
         prefill::tc_fence_after();
-        float qs[DVB], mu[DVB];
-        prefill::tmem_ld32(tmem + lq + T_D1 + par * 32, qs);
-        prefill::tmem_ld32(tmem + lq + T_D3 + par * 32, mu);
-        prefill::tmem_wait_ld();
+        float qs[VH], mu[VH];
+        {
+          float ql[VH], ml[VH];
+          tmem_ld16(tmem + lq + T_D1 + par * 64 + r0, qs);
+          tmem_ld16(tmem + lq + T_D1 + par * 64 + DVB + r0, ql);
+          tmem_ld16(tmem + lq + T_D3 + par * 64 + r0, mu);
+          tmem_ld16(tmem + lq + T_D3 + par * 64 + DVB + r0, ml);
+          prefill::tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < VH; ++j) qs[j] += ql[j], mu[j] += ml[j];
+        }
         const int t = k - C;
         const int pos = c * C + t;
         const float gt = Gam[t];
@@ -678,9 +714,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) scan_kernel(const __grid_consta
         __syncwarp();
         if (lane == 0) mbar_arrive(&bar[B_YDONE + par]);
         if (pos < p.T) {
-          uint4* yr = reinterpret_cast<uint4*>(static_cast<T*>(p.y) + ((int64_t(b) * p.T + pos) * p.Hv + h) * DV + dv0);
+          uint4* yr = reinterpret_cast<uint4*>(static_cast<T*>(p.y) + ((int64_t(b) * p.T + pos) * p.Hv + h) * DV +
+                                               dv0 + r0);
 #pragma unroll
-          for (int q8 = 0; q8 < DVB / 8; ++q8) {
+          for (int q8 = 0; q8 < VH / 8; ++q8) {
             uint32_t w4[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
@@ -697,11 +734,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) scan_kernel(const __grid_consta
     if (!ok) {
       *abort_flag = 1;
     } else {
-      float* sout = p.s_out + (int64_t(b) * p.Hv + h) * DV * DK + int64_t(dv0) * DK + k;
+      float* sout = p.s_out + (int64_t(b) * p.Hv + h) * DV * DK + int64_t(dv0 + r0) * DK + k;
 #pragma unroll
-      for (int j = 0; j < DVB; ++j) sout[int64_t(j) * DK] = s[j];
+      for (int j = 0; j < VH; ++j) sout[int64_t(j) * DK] = s[j];
     }
-  } else if (warp == 4) {
+  } else if (warp == TC_LOAD) {
     // ------------------------------------------------------------------------------------ loads
     if (lane == 0 && n > 0) {
       prefetch_tensormap(&qmap);
@@ -736,9 +773,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) scan_kernel(const __grid_consta
     // ------------------------------------------------------------------------------------ MMA issuer
     if (elect_one() && n > 0) {
       bool ok = true;
-      const uint32_t shi = smem_u32(sm + TcSmem::SHI), slo = smem_u32(sm + TcSmem::SLO);
-      const uint32_t uhi = smem_u32(sm + TcSmem::UHI), ulo = smem_u32(sm + TcSmem::ULO);
-      const uint32_t udhi = smem_u32(sm + TcSmem::UDHI), udlo = smem_u32(sm + TcSmem::UDLO);
+      const uint32_t sop = smem_u32(sm + TcSmem::SOP);
+      const uint32_t uop = smem_u32(sm + TcSmem::UOP), udop = smem_u32(sm + TcSmem::UDOP);
       for (int c = 0; c < n && ok; ++c) {
         const int par = c & 1;
         const uint32_t base = smem_u32(sm + par * TcSmem::BUF);
@@ -746,7 +782,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) scan_kernel(const __grid_consta
              (c < 2 || mbar_wait(&bar[B_YDONE + par], ((c >> 1) - 1) & 1, 88)) && !*abort_flag;
         if (!ok) break;
         prefill::tc_fence_after();
-        // P1: D1 = [W_hi ; Q] (S_hi + S_lo)^T, D4 = W_lo S_hi^T (K = 128 keys: two 64-key blocks of 4 steps)
+        // P1: D1 = [W_hi ; Q] [S_hi | S_lo]^T, D4 = W_lo [S_hi | S_lo]^T (N = 64: each A tile read once for both
+        // halves; K = 128 keys: two 64-key blocks of A, 4 steps each, and 16 rows of S^T a step)
 #pragma unroll
         for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
@@ -754,37 +791,34 @@ __global__ void __launch_bounds__(TC_THREADS, 1) scan_kernel(const __grid_consta
             const uint32_t acc = (kb | ks) ? 1u : 0u;
             const uint64_t a = prefill::sdesc(base + TcSmem::A1 + kb * 2 * C * 128 + ks * 32, 16, 1024);
             const uint64_t al = prefill::sdesc(base + TcSmem::WLO + kb * C * 128 + ks * 32, 16, 1024);
-            const uint64_t bh = prefill::sdesc(shi + kb * DVB * 128 + ks * 32, 16, 1024);
-            const uint64_t bl = prefill::sdesc(slo + kb * DVB * 128 + ks * 32, 16, 1024);
-            prefill::umma_ss(tmem + T_D1 + par * 32, a, bh, IDESC_K, acc);
-            prefill::umma_ss(tmem + T_D1 + par * 32, a, bl, IDESC_K, 1u);
-            prefill::umma_ss(tmem + T_D4 + par * 32, al, bh, IDESC_K, acc);
+            const uint64_t bs = prefill::sdesc(sop + (kb * 4 + ks) * 16 * 128, DK * 128, 1024);
+            prefill::umma_ss(tmem + T_D1 + par * 64, a, bs, IDESC_K2, acc);
+            prefill::umma_ss(tmem + T_D4 + par * 64, al, bs, IDESC_K2, acc);
           }
         prefill::umma_commit(&bar[B_D1 + par]);
         ok = mbar_wait(&bar[B_UDREADY], c & 1, 89) && !*abort_flag;
         if (!ok) break;
         prefill::tc_fence_after();
-        // P2: D2 = K^T (Ud_hi + Ud_lo): A = the K tile [64 positions][128 keys] read as M = keys (MN-major: the two
+        // P2: D2 = K^T [Ud_hi | Ud_lo]: A = the K tile [64 positions][128 keys] read as M = keys (MN-major: the two
         // 64-key boxes 8 KB apart), K = positions in steps of 16 rows
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
           const uint64_t a = prefill::sdesc(base + TcSmem::K + ks * 16 * 128, C * 128, 1024);
-          prefill::umma_ss(tmem + T_D2, a, prefill::sdesc(udhi + ks * 32, 16, 1024), IDESC_MN, ks ? 1u : 0u);
-          prefill::umma_ss(tmem + T_D2, a, prefill::sdesc(udlo + ks * 32, 16, 1024), IDESC_MN, 1u);
+          prefill::umma_ss(tmem + T_D2, a, prefill::sdesc(udop + ks * 16 * 128, C * 128, 1024), IDESC_MN2, ks ? 1u : 0u);
         }
         prefill::umma_commit(&bar[B_D2]);
         ok = mbar_wait(&bar[B_UREADY], c & 1, 91) && !*abort_flag;
         if (!ok) break;
         prefill::tc_fence_after();
-        // P3: D3[64:128] = M_hi (U_hi + U_lo) + M_lo U_hi; A rows 0-63 are whatever precedes (D3 rows 0-63 unused)
+        // P3: D3[64:128] = (M_hi + M_lo) [U_hi | U_lo]^T; the A rows 0-63 are whatever precedes M_hi / M_lo in the
+        // buffer (D3 rows 0-63 unused)
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
           const uint64_t ahi = prefill::sdesc(base + TcSmem::MHI - C * 128 + ks * 32, 16, 1024);
           const uint64_t alo = prefill::sdesc(base + TcSmem::MHI + ks * 32, 16, 1024);
-          prefill::umma_ss(tmem + T_D3 + par * 32, ahi, prefill::sdesc(uhi + ks * 32, 16, 1024), IDESC_K,
-                           ks ? 1u : 0u);
-          prefill::umma_ss(tmem + T_D3 + par * 32, ahi, prefill::sdesc(ulo + ks * 32, 16, 1024), IDESC_K, 1u);
-          prefill::umma_ss(tmem + T_D3 + par * 32, alo, prefill::sdesc(uhi + ks * 32, 16, 1024), IDESC_K, 1u);
+          const uint64_t bu = prefill::sdesc(uop + ks * 16 * 128, C * 128, 1024);
+          prefill::umma_ss(tmem + T_D3 + par * 64, ahi, bu, IDESC_K2, ks ? 1u : 0u);
+          prefill::umma_ss(tmem + T_D3 + par * 64, alo, bu, IDESC_K2, 1u);
         }
         prefill::umma_commit(&bar[B_D3 + par]);
         prefill::umma_commit(&bar[B_EMPTY + par]);
@@ -797,7 +831,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) scan_kernel(const __grid_consta
   }
   prefill::tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == TC_MMA) {
     prefill::tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS));
   }
