@@ -133,6 +133,23 @@ __device__ __forceinline__ void fma_tile(const float* Lp, int ldl, const float* 
 }
 
 // Writes 64 values of row `row` of a 16-bit K-major operand pair (128-byte swizzle) as hi / lo: eight 16-byte pieces.
+// The 16-bit hi / lo pairs of two values (hi = round(x), lo = round(x - hi)), packed two a word, with one paired
+// conversion for the two hi halves and one for the two lo halves: the single-value conversions go through a narrow
+// pipe and were the largest cost of the scan's epilogues.
+template <typename T>
+__device__ __forceinline__ void split2(float a, float b, uint32_t& h, uint32_t& l);
+template <>
+__device__ __forceinline__ void split2<__nv_bfloat16>(float a, float b, uint32_t& h, uint32_t& l) {
+  h = pack2<__nv_bfloat16>(a, b);
+  l = pack2<__nv_bfloat16>(a - __uint_as_float(h << 16), b - __uint_as_float(h & 0xffff0000u));
+}
+template <>
+__device__ __forceinline__ void split2<__half>(float a, float b, uint32_t& h, uint32_t& l) {
+  h = pack2<__half>(a, b);
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
+  l = pack2<__half>(a - f.x, b - f.y);
+}
+
 template <typename T>
 __device__ __forceinline__ void put_row_pair(uint8_t* hi, uint8_t* lo, int row, const float* x) {
 #pragma unroll
@@ -140,10 +157,7 @@ __device__ __forceinline__ void put_row_pair(uint8_t* hi, uint8_t* lo, int row, 
     uint32_t h[4], l[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const float a = x[8 * j8 + 2 * e], bb = x[8 * j8 + 2 * e + 1];
-      const float ha = to_f<T>(from_f<T>(a)), hb = to_f<T>(from_f<T>(bb));
-      h[e] = pack2<T>(ha, hb);
-      l[e] = pack2<T>(a - ha, bb - hb);
+      split2<T>(x[8 * j8 + 2 * e], x[8 * j8 + 2 * e + 1], h[e], l[e]);
     }
     const int off = row * 128 + (((j8 ^ row) & 7) << 4);
     *reinterpret_cast<uint4*>(hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
@@ -523,14 +537,6 @@ constexpr int B_UDREADY = 14; // Ud operands written (warps 0, 1, 4, 5): P2 may 
 // buffers each (the products with the hi and the lo halves side by side); D2 = K^T [Ud_hi | Ud_lo]: 64 columns
 constexpr uint32_t T_D1 = 0, T_D3 = 128, T_D4 = 256, T_D2 = 384;
 
-// The chunk's 16-bit operand pair of value x: (hi, lo) of the activation type.
-template <typename T>
-__device__ __forceinline__ void split_pair(float x, uint16_t& hi, uint16_t& lo) {
-  const T h = from_f<T>(x);
-  const T l = from_f<T>(x - to_f<T>(h));
-  hi = *reinterpret_cast<const uint16_t*>(&h);
-  lo = *reinterpret_cast<const uint16_t*>(&l);
-}
 
 // Writes the 16 values x (value rows r0 .. r0 + 15) into row `row` (a key or a position) of an MN-major operand
 // [rows][hi 32 | lo 32]: the hi halves at elements r0 .., the lo halves at 32 + r0 .., four 16-byte stores.
@@ -538,13 +544,7 @@ template <typename T>
 __device__ __forceinline__ void put_row16(uint8_t* op, int row, int r0, const float* x) {
   uint32_t h[8], l[8];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    uint16_t h0, l0, h1, l1;
-    split_pair<T>(x[2 * e], h0, l0);
-    split_pair<T>(x[2 * e + 1], h1, l1);
-    h[e] = uint32_t(h0) | (uint32_t(h1) << 16);
-    l[e] = uint32_t(l0) | (uint32_t(l1) << 16);
-  }
+  for (int e = 0; e < 8; ++e) split2<T>(x[2 * e], x[2 * e + 1], h[e], l[e]);
   uint8_t* r = op + row * 128;
   const int c0 = r0 >> 3, sw = row & 7;
   *reinterpret_cast<uint4*>(r + (((c0) ^ sw) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
