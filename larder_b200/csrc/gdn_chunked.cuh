@@ -269,21 +269,34 @@ __global__ void __launch_bounds__(128) prep_kernel(const __grid_constant__ CUten
 #pragma unroll
       for (int j = 0; j < C; ++j) x[j] = 0.f;
     }
+    // the decays exp(gamma_t - gamma_j) (j <= t), shared by the lane pair (l, l ^ 16) that has row t: this lane forms
+    // those of the j with parity `half`, the other lane's come by a shuffle; columns past the warp's last row are zero
     const float gt = gam[t];
-    if (lane < 16) {
+    const int half = lane >> 4;
+    const int ilim = 8 * (warp + 1);  // j <= 16 warp + 15 covers every row of the warp
+#pragma unroll
+    for (int i = 0; i < C / 2; ++i) {
+      float own = 0.f;
+      if (i < ilim) {
+        const int j = 2 * i + half;
+        own = j <= t ? __expf(gt - gam[j]) : 0.f;
+      }
+      const float other = __shfl_xor_sync(0xffffffffu, own, 16);
+      x[2 * i] *= half ? other : own;
+      x[2 * i + 1] *= half ? own : other;
+    }
+    if (lane < 16) {  // A: strictly lower, weighted by beta_t
       const float bt = bet[t];
 #pragma unroll
       for (int j = 0; j < C; j += 4) {
         float4 a;
-        a.x = j < t ? bt * __expf(gt - gam[j]) * x[j] : 0.f;
-        a.y = j + 1 < t ? bt * __expf(gt - gam[j + 1]) * x[j + 1] : 0.f;
-        a.z = j + 2 < t ? bt * __expf(gt - gam[j + 2]) * x[j + 2] : 0.f;
-        a.w = j + 3 < t ? bt * __expf(gt - gam[j + 3]) * x[j + 3] : 0.f;
+        a.x = j < t ? bt * x[j] : 0.f;
+        a.y = j + 1 < t ? bt * x[j + 1] : 0.f;
+        a.z = j + 2 < t ? bt * x[j + 2] : 0.f;
+        a.w = j + 3 < t ? bt * x[j + 3] : 0.f;
         *reinterpret_cast<float4*>(Af + t * AP + j) = a;
       }
-    } else {
-#pragma unroll
-      for (int j = 0; j < C; ++j) x[j] = j <= t ? __expf(gt - gam[j]) * x[j] : 0.f;
+    } else {  // M: lower with the diagonal (the decay is zero above it)
       put_row_pair<T>(unit + WS_MHI, unit + WS_MLO, t, x);
     }
   }
