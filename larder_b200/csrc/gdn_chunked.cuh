@@ -97,7 +97,7 @@ __device__ __forceinline__ uint8_t* unit_ptr(const Params& p, int b, int h, int 
 //   lo pair, B = the K / V tile read MN-major (positions are the products' K).
 
 constexpr int PREP_TMEM_COLS = 128;
-constexpr int XP = 40;  // row stride of the inversion scratch
+constexpr int XP = 36;  // row stride of the inversion scratch (conflict-free float4 rows)
 
 // 16 KB regions reused as the steps go, so that three CTAs fit an SM: the Q tile is dead after P_A (its region then
 // holds the inversion scratch, then T diag(beta Gam)); the K tile after W's products (then T diag(beta)).
@@ -116,21 +116,6 @@ struct PrepSmem {
 };
 static_assert(PrepSmem::AF % 1024 == 0 && PrepSmem::BYTES <= 75 * 1024, "three prep CTAs an SM");
 
-// acc (a 16 x 8 tile in the m16n8 fragment layout: lane (r = lane / 4, q = lane % 4) holds (r, 2q), (r, 2q + 1),
-// (r + 8, 2q), (r + 8, 2q + 1)) += L R over K = 8 ksteps, fp32 on the CUDA cores: L's rows at Lp (stride ldl), R's
-// row k at Rp + k ldr.
-__device__ __forceinline__ void fma_tile(const float* Lp, int ldl, const float* Rp, int ldr, int ksteps, float* acc,
-                                         int lane) {
-  const int r = lane >> 2, cq = lane & 3;
-  for (int k = 0; k < 8 * ksteps; ++k) {
-    const float l0 = Lp[r * ldl + k], l1 = Lp[(r + 8) * ldl + k];
-    const float2 rr = *reinterpret_cast<const float2*>(Rp + k * ldr + 2 * cq);
-    acc[0] = fmaf(l0, rr.x, acc[0]);
-    acc[1] = fmaf(l0, rr.y, acc[1]);
-    acc[2] = fmaf(l1, rr.x, acc[2]);
-    acc[3] = fmaf(l1, rr.y, acc[3]);
-  }
-}
 
 // Writes 64 values of row `row` of a 16-bit K-major operand pair (128-byte swizzle) as hi / lo: eight 16-byte pieces.
 // The 16-bit hi / lo pairs of two values (hi = round(x), lo = round(x - hi)), packed two a word, with one paired
@@ -323,53 +308,92 @@ __global__ void __launch_bounds__(128) prep_kernel(const __grid_constant__ CUten
       for (int r = 0; r < 16; ++r) Af[(base + r) * AP + base + i] = tc[r];
   }
   __syncthreads();
-  // level 1: T[hi][lo] = -T[hi][hi] A[hi][lo] T[lo][lo] for the 16 x 16 block pairs (0, 1) and (2, 3): warp w takes
-  // pair w / 2 and output columns 8 (w % 2) .. + 7, first of X = A[hi][lo] T[lo][lo], then of the block
+  // level 1: T[hi][lo] = -T[hi][hi] (A[hi][lo] T[lo][lo]) for the 16 x 16 block pairs (lo, hi) = (0, 16), (32, 48):
+  // threads 64 p .. 64 p + 63 take pair p, the thread row r = (tid % 64) / 4 and columns c0 .. c0 + 3 of the block
+  // (float4 operands: a quarter warp reads two rows of A and four column groups of one row of T, conflict-free)
   {
-    const int pr = warp >> 1, n0 = (warp & 1) * 8;
+    const int pr = tid >> 6, r = (tid & 63) >> 2, c0 = (tid & 3) * 4;
     const int lo = 32 * pr, hi = lo + 16;
-    float* X = Xs + pr * 16 * XP;
-    const int r = lane >> 2, cq = lane & 3;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    fma_tile(Af + hi * AP + lo, AP, Af + lo * AP + lo + n0, AP, 2, acc, lane);
-    X[r * XP + n0 + 2 * cq] = acc[0];
-    X[r * XP + n0 + 2 * cq + 1] = acc[1];
-    X[(r + 8) * XP + n0 + 2 * cq] = acc[2];
-    X[(r + 8) * XP + n0 + 2 * cq + 1] = acc[3];
+#pragma unroll
+    for (int k = 0; k < 16; k += 4) {
+      const float4 a = *reinterpret_cast<const float4*>(Af + (hi + r) * AP + lo + k);
+      const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const float4 bq = *reinterpret_cast<const float4*>(Af + (lo + k + kk) * AP + lo + c0);
+        acc[0] = fmaf(av[kk], bq.x, acc[0]);
+        acc[1] = fmaf(av[kk], bq.y, acc[1]);
+        acc[2] = fmaf(av[kk], bq.z, acc[2]);
+        acc[3] = fmaf(av[kk], bq.w, acc[3]);
+      }
+    }
+    *reinterpret_cast<float4*>(Xs + (16 * pr + r) * XP + c0) = make_float4(acc[0], acc[1], acc[2], acc[3]);
     __syncthreads();
     float t4[4] = {0.f, 0.f, 0.f, 0.f};
-    fma_tile(Af + hi * AP + hi, AP, X + n0, XP, 2, t4, lane);
-    Af[(hi + r) * AP + lo + n0 + 2 * cq] = -t4[0];
-    Af[(hi + r) * AP + lo + n0 + 2 * cq + 1] = -t4[1];
-    Af[(hi + r + 8) * AP + lo + n0 + 2 * cq] = -t4[2];
-    Af[(hi + r + 8) * AP + lo + n0 + 2 * cq + 1] = -t4[3];
+#pragma unroll
+    for (int k = 0; k < 16; k += 4) {
+      const float4 a = *reinterpret_cast<const float4*>(Af + (hi + r) * AP + hi + k);
+      const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const float4 xq = *reinterpret_cast<const float4*>(Xs + (16 * pr + k + kk) * XP + c0);
+        t4[0] = fmaf(av[kk], xq.x, t4[0]);
+        t4[1] = fmaf(av[kk], xq.y, t4[1]);
+        t4[2] = fmaf(av[kk], xq.z, t4[2]);
+        t4[3] = fmaf(av[kk], xq.w, t4[3]);
+      }
+    }
+    *reinterpret_cast<float4*>(Af + (hi + r) * AP + lo + c0) = make_float4(-t4[0], -t4[1], -t4[2], -t4[3]);
   }
   __syncthreads();
-  // level 2: T[32:64][0:32] = -T[32:64][32:64] A[32:64][0:32] T[0:32][0:32] (32 x 32 blocks): warp w takes the two
-  // 16 x 8 output tiles 2 w, 2 w + 1 (row tile = index / 4, column tile = index % 4) of each product
+  // level 2: T[32:64][0:32] = -T[32:64][32:64] (A[32:64][0:32] T[0:32][0:32]) (32 x 32 blocks): thread row
+  // r = tid / 4, columns c0 .. c0 + 7
   {
-    const int r = lane >> 2, cq = lane & 3;
+    const int r = tid >> 2, c0 = (tid & 3) * 8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int ti = warp * 2 + u, m0 = (ti >> 2) * 16, n0 = (ti & 3) * 8;
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      fma_tile(Af + (32 + m0) * AP, AP, Af + n0, AP, 4, acc, lane);
-      Xs[(m0 + r) * XP + n0 + 2 * cq] = acc[0];
-      Xs[(m0 + r) * XP + n0 + 2 * cq + 1] = acc[1];
-      Xs[(m0 + r + 8) * XP + n0 + 2 * cq] = acc[2];
-      Xs[(m0 + r + 8) * XP + n0 + 2 * cq + 1] = acc[3];
+    for (int k = 0; k < 32; k += 4) {
+      const float4 a = *reinterpret_cast<const float4*>(Af + (32 + r) * AP + k);
+      const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const float4 b0 = *reinterpret_cast<const float4*>(Af + (k + kk) * AP + c0);
+        const float4 b1 = *reinterpret_cast<const float4*>(Af + (k + kk) * AP + c0 + 4);
+        acc[0] = fmaf(av[kk], b0.x, acc[0]);
+        acc[1] = fmaf(av[kk], b0.y, acc[1]);
+        acc[2] = fmaf(av[kk], b0.z, acc[2]);
+        acc[3] = fmaf(av[kk], b0.w, acc[3]);
+        acc[4] = fmaf(av[kk], b1.x, acc[4]);
+        acc[5] = fmaf(av[kk], b1.y, acc[5]);
+        acc[6] = fmaf(av[kk], b1.z, acc[6]);
+        acc[7] = fmaf(av[kk], b1.w, acc[7]);
+      }
     }
+    *reinterpret_cast<float4*>(Xs + r * XP + c0) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    *reinterpret_cast<float4*>(Xs + r * XP + c0 + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
     __syncthreads();
+    float t8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int ti = warp * 2 + u, m0 = (ti >> 2) * 16, n0 = (ti & 3) * 8;
-      float t4[4] = {0.f, 0.f, 0.f, 0.f};
-      fma_tile(Af + (32 + m0) * AP + 32, AP, Xs + n0, XP, 4, t4, lane);
-      Af[(32 + m0 + r) * AP + n0 + 2 * cq] = -t4[0];
-      Af[(32 + m0 + r) * AP + n0 + 2 * cq + 1] = -t4[1];
-      Af[(32 + m0 + r + 8) * AP + n0 + 2 * cq] = -t4[2];
-      Af[(32 + m0 + r + 8) * AP + n0 + 2 * cq + 1] = -t4[3];
+    for (int k = 0; k < 32; k += 4) {
+      const float4 a = *reinterpret_cast<const float4*>(Af + (32 + r) * AP + 32 + k);
+      const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const float4 x0 = *reinterpret_cast<const float4*>(Xs + (k + kk) * XP + c0);
+        const float4 x1 = *reinterpret_cast<const float4*>(Xs + (k + kk) * XP + c0 + 4);
+        t8[0] = fmaf(av[kk], x0.x, t8[0]);
+        t8[1] = fmaf(av[kk], x0.y, t8[1]);
+        t8[2] = fmaf(av[kk], x0.z, t8[2]);
+        t8[3] = fmaf(av[kk], x0.w, t8[3]);
+        t8[4] = fmaf(av[kk], x1.x, t8[4]);
+        t8[5] = fmaf(av[kk], x1.y, t8[5]);
+        t8[6] = fmaf(av[kk], x1.z, t8[6]);
+        t8[7] = fmaf(av[kk], x1.w, t8[7]);
+      }
     }
+    *reinterpret_cast<float4*>(Af + (32 + r) * AP + c0) = make_float4(-t8[0], -t8[1], -t8[2], -t8[3]);
+    *reinterpret_cast<float4*>(Af + (32 + r) * AP + c0 + 4) = make_float4(-t8[4], -t8[5], -t8[6], -t8[7]);
   }
   __syncthreads();
   // 5. W = T diag(beta Gam) K (lane 0): threads 0-63 write row t of its A operand (a hi / lo pair) where the Q tile
