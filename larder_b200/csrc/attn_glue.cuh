@@ -4,7 +4,7 @@
 // qk_norm_rope: for each row (b, s) and each of the NQ query heads and NK key heads, x = the head's D values (query
 // head h: columns [2 h D, 2 h D + D) of q_proj's output, whose other half is the output gate; key head h: columns
 // [h D, h D + D) of k_proj's output),
-//   inv = 1 / sqrt(sum(x^2) / D + eps)                         (fp32 sum of squares)
+//   inv = rsqrt(sum(x^2) / D + eps)        (fp32 sum of squares; rsqrtf, within 2 ulp of the reference's precise rsqrt)
 //   o_j = bf16(w_j * bf16(x_j * inv))                           (RMSNorm with the norm's bf16 weight)
 //   j < R:  r_j = bf16(bf16(o_j * bf16(cos_j)) + bf16(rot_j * bf16(sin_j))),  rot_j = -o_{j+R/2} (j < R/2),
 //           o_{j-R/2} (j >= R/2)                                 (rotate-half RoPE on the first R dims)
@@ -16,9 +16,10 @@
 // sig(g) = bf16(sigmoid(g)), the reference's per-bf16-pattern sigmoid table.
 //
 // Both are HBM-bound streams: D / 32 consecutive values a lane, 16-byte loads and stores; the grid's x index picks
-// the rows and its y index the warp's head group (no 64-bit index division per warp). A warp takes ROWS rows of
-// its head and issues their loads before any arithmetic; the RoPE phase runs on all 32 lanes over strided columns
-// (coalesced cos / sin reads), through shared memory.
+// the rows and its y index the warp's head group (no 64-bit index division per warp). A warp takes several rows of
+// its head and issues their loads before any arithmetic. For R in {0, 32, 64, 128} the lanes hold strided column pairs
+// and RoPE runs on every lane (qk_rope_pair_kernel); other widths go through shared memory over strided columns
+// (qk_norm_rope_kernel).
 #pragma once
 
 #include "common.cuh"
@@ -41,6 +42,29 @@ struct QkParams {
 };
 
 __device__ __forceinline__ float bf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// bf16-rounds two values in place: one paired conversion, then bit moves back to fp32.
+__device__ __forceinline__ void bf2(float& a, float& b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  const uint32_t u = *reinterpret_cast<const uint32_t*>(&h);
+  a = __uint_as_float(u << 16);
+  b = __uint_as_float(u & 0xffff0000u);
+}
+
+// Stores E bf16-exact fp32 values (their low 16 bits zero) as bf16: the high halves packed by bit moves.
+template <int E>
+__device__ __forceinline__ void st_row_exact(__nv_bfloat16* dst, const float* x) {
+  uint32_t w[E / 2];
+#pragma unroll
+  for (int i = 0; i < E / 2; ++i) w[i] = __byte_perm(__float_as_uint(x[2 * i]), __float_as_uint(x[2 * i + 1]), 0x7632);
+  if constexpr (E == 4) {
+    *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+  } else {
+#pragma unroll
+    for (int c = 0; c < E / 8; ++c)
+      *reinterpret_cast<uint4*>(dst + 8 * c) = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+  }
+}
 
 __device__ __forceinline__ float ld_any(const void* p, int64_t i, int dt) {
   switch (dt) {
@@ -125,7 +149,7 @@ __global__ void __launch_bounds__(WARPS * 32) qk_norm_rope_kernel(const QkParams
     for (int i = 0; i < E; ++i) acc = fmaf(x[r][i], x[r][i], acc);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    const float inv = 1.f / sqrtf(acc / float(D) + p.eps);
+    const float inv = rsqrtf(acc / float(D) + p.eps);
 #pragma unroll
     for (int i = 0; i < E; i += 4)  // (16-byte stores: a lane's E values are consecutive)
       *reinterpret_cast<float4*>(&part[warp][r][lane * E + i]) =
@@ -177,6 +201,119 @@ __global__ void __launch_bounds__(WARPS * 32) qk_norm_rope_kernel(const QkParams
   }
 }
 
+// qk_norm_rope in a pair-strided layout: lane l holds the column pairs (64 k + 2 l, 64 k + 2 l + 1), k < D / 64, so
+// the rotated columns of a row are spread over all 32 lanes, and a column's rotate-half partner is in lane
+// l ^ (R / 4), same pair (MODE 1: R = 32 or 64), or in this lane's other pair (MODE 2: R = 128); MODE 0 has no RoPE.
+// A block takes QROWS rows and WARPS heads (a warp a head); the rows' cos / sin are read once a block into shared
+// memory (rounded to bf16 as every use takes them, sin negated where the partner enters negated) while the warps' row
+// loads are in flight. Roundings go two values a paired conversion; the results, bf16-exact, are packed for the stores
+// by bit moves. The arithmetic and its roundings are those of qk_norm_rope_kernel.
+constexpr int QROWS = 4;
+
+template <int D, int MODE>
+__global__ void __launch_bounds__(WARPS * 32) qk_rope_pair_kernel(const QkParams p) {
+  constexpr int NP = D / 64;  // column pairs a lane
+  __shared__ __align__(16) float2 trig[2][QROWS][64];  // (cos, sin) pairs of the block's rows, R / 2 <= 64 pairs
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hd = blockIdx.y * WARPS + warp;  // query heads, then key heads
+  const bool live = hd < p.NQ + p.NK;
+  const bool isq = hd < p.NQ;
+  const int h = isq ? hd : hd - p.NQ;
+  const int nrows = p.B * p.S;  // < 2^31: checked by the launcher
+  const int row0 = blockIdx.x * QROWS;
+  const int64_t rstride = isq ? int64_t(p.NQ) * 2 * D : int64_t(p.NK) * D;
+  const __nv_bfloat16* src = (isq ? p.qg + int64_t(h) * 2 * D : p.kr + int64_t(h) * D) + 2 * lane;
+  uint32_t raw[QROWS][NP], wraw[NP];
+  if (live) {
+#pragma unroll
+    for (int r = 0; r < QROWS; ++r) {
+      const bool in = row0 + r < nrows;
+#pragma unroll
+      for (int k = 0; k < NP; ++k)
+        raw[r][k] = in ? *reinterpret_cast<const uint32_t*>(src + int64_t(row0 + r) * rstride + 64 * k) : 0u;
+    }
+    const __nv_bfloat16* w = (isq ? p.qw : p.kw) + 2 * lane;
+#pragma unroll
+    for (int k = 0; k < NP; ++k) wraw[k] = *reinterpret_cast<const uint32_t*>(w + 64 * k);
+  }
+  const int R = p.R;
+  if (MODE != 0) {
+#pragma unroll
+    for (int r = 0; r < QROWS; ++r) {
+      const int row = row0 + r < nrows ? row0 + r : row0;
+      const int64_t c0 = int64_t(row % p.S) * R;
+      for (int q = threadIdx.x; q < R; q += WARPS * 32) {  // q < R / 2: cos pairs, else sin pairs
+        const int w = 2 * q >= R, qq = q - w * (R >> 1);
+        float a = ld_any(w ? p.sn : p.cs, c0 + 2 * qq, p.csdt), b = ld_any(w ? p.sn : p.cs, c0 + 2 * qq + 1, p.csdt);
+        bf2(a, b);
+        if (w && 4 * qq < R) a = -a, b = -b;
+        trig[w][r][qq] = make_float2(a, b);
+      }
+    }
+  }
+  __syncthreads();
+  if (!live) return;
+  float wv[2 * NP];
+#pragma unroll
+  for (int k = 0; k < NP; ++k) wv[2 * k] = __uint_as_float(wraw[k] << 16), wv[2 * k + 1] = __uint_as_float(wraw[k] & 0xffff0000u);
+  int b = row0 / p.S, s = row0 - b * p.S;
+#pragma unroll
+  for (int r = 0; r < QROWS; ++r, ++s) {
+    if (s == p.S) s = 0, ++b;
+    float x[2 * NP];
+#pragma unroll
+    for (int k = 0; k < NP; ++k)
+      x[2 * k] = __uint_as_float(raw[r][k] << 16), x[2 * k + 1] = __uint_as_float(raw[r][k] & 0xffff0000u);
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < 2 * NP; ++i) acc = fmaf(x[i], x[i], acc);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    const float inv = rsqrtf(acc / float(D) + p.eps);
+#pragma unroll
+    for (int i = 0; i < 2 * NP; i += 2) {
+      float u = x[i] * inv, v = x[i + 1] * inv;
+      bf2(u, v);
+      u *= wv[i], v *= wv[i + 1];
+      bf2(u, v);
+      x[i] = u, x[i + 1] = v;
+    }
+    if (MODE == 1) {  // pair 0 of lanes 2 lane < R: partner in lane ^ (R / 4)
+      const float p0 = __shfl_xor_sync(0xffffffffu, x[0], R >> 2), p1 = __shfl_xor_sync(0xffffffffu, x[1], R >> 2);
+      if (2 * lane < R) {
+        const float2 c = trig[0][r][lane], sg = trig[1][r][lane];
+        float a0 = x[0] * c.x, a1 = x[1] * c.y, b0 = p0 * sg.x, b1 = p1 * sg.y;
+        bf2(a0, a1);
+        bf2(b0, b1);
+        a0 += b0, a1 += b1;
+        bf2(a0, a1);
+        x[0] = a0, x[1] = a1;
+      }
+    } else if (MODE == 2) {  // pairs 0 and 1 (R = 128): each the other's partner
+      float y[4];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const float2 c = trig[0][r][32 * k + lane], sg = trig[1][r][32 * k + lane];
+        float a0 = x[2 * k] * c.x, a1 = x[2 * k + 1] * c.y, b0 = x[2 * (1 - k)] * sg.x, b1 = x[2 * (1 - k) + 1] * sg.y;
+        bf2(a0, a1);
+        bf2(b0, b1);
+        a0 += b0, a1 += b1;
+        bf2(a0, a1);
+        y[2 * k] = a0, y[2 * k + 1] = a1;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) x[i] = y[i];
+    }
+    if (row0 + r < nrows) {
+      __nv_bfloat16* dst = (isq ? p.q + ((int64_t(b) * p.NQ + h) * p.S + s) * D
+                                 : p.k + ((int64_t(b) * p.NK + h) * p.S + s) * D) + 2 * lane;
+#pragma unroll
+      for (int k = 0; k < NP; ++k)
+        *reinterpret_cast<uint32_t*>(dst + 64 * k) = __byte_perm(__float_as_uint(x[2 * k]), __float_as_uint(x[2 * k + 1]), 0x7632);
+    }
+  }
+}
+
 struct GateParams {
   const __nv_bfloat16* o;   // [rows, NQ * D]
   const __nv_bfloat16* qg;  // [rows, NQ * 2 D]
@@ -197,8 +334,14 @@ __global__ void __launch_bounds__(WARPS * 32) out_gate_kernel(const GateParams p
   ld_row<E>(p.o + oo, x);
   ld_row<E>(p.qg + row * (int64_t(p.NQ) * 2 * D) + int64_t(h) * 2 * D + D + lane * E, g);
 #pragma unroll
-  for (int i = 0; i < E; ++i) x[i] = bf(x[i] * bf(1.f / (1.f + expf(-g[i]))));
-  st_row<E>(p.out + oo, x);
+  for (int i = 0; i < E; i += 2) {
+    float s0 = 1.f / (1.f + expf(-g[i])), s1 = 1.f / (1.f + expf(-g[i + 1]));
+    bf2(s0, s1);
+    float a = x[i] * s0, b = x[i + 1] * s1;
+    bf2(a, b);
+    x[i] = a, x[i + 1] = b;
+  }
+  st_row_exact<E>(p.out + oo, x);
 }
 
 }  // namespace aglue

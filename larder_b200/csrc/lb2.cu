@@ -1258,10 +1258,34 @@ int lb2_attn_qk_norm_rope(const void* qg, const void* kr, const void* q_norm_w, 
   aglue::QkParams p{static_cast<const __nv_bfloat16*>(qg), static_cast<const __nv_bfloat16*>(kr),
                     static_cast<const __nv_bfloat16*>(q_norm_w), static_cast<const __nv_bfloat16*>(k_norm_w), cos, sin,
                     cs_dtype, eps, static_cast<__nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(k), B, S, NQ, NK, R};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the pair-strided form for rope widths 0, 32, 64 and 128
+  const int mode = R == 0 ? 0 : (R == 32 || R == 64) ? 1 : R == 128 ? 2 : -1;
+  if (mode >= 0) {
+    const dim3 g1(unsigned((int64_t(B) * S + aglue::QROWS - 1) / aglue::QROWS),
+                  unsigned((NQ + NK + aglue::WARPS - 1) / aglue::WARPS));
+    LB2_CHECK_ARG(g1.y < 65536, "qk_norm_rope: too many heads");
+#define LB2_QK_PAIR(DD)                                                               \
+  if (mode == 0)                                                                      \
+    aglue::qk_rope_pair_kernel<DD, 0><<<g1, aglue::WARPS * 32, 0, st>>>(p);           \
+  else if (mode == 1)                                                                 \
+    aglue::qk_rope_pair_kernel<DD, 1><<<g1, aglue::WARPS * 32, 0, st>>>(p);           \
+  else                                                                                \
+    aglue::qk_rope_pair_kernel<DD, 2><<<g1, aglue::WARPS * 32, 0, st>>>(p)
+    if (D == 128) {
+      LB2_QK_PAIR(128);
+    } else if (D == 256) {
+      LB2_QK_PAIR(256);
+    } else {
+      LB2_QK_PAIR(512);
+    }
+#undef LB2_QK_PAIR
+    LB2_CUDA(cudaGetLastError());
+    return LB2_OK;
+  }
   const dim3 grid(unsigned((int64_t(B) * S + aglue::ROWS - 1) / aglue::ROWS),
                   unsigned((NQ + NK + aglue::WARPS - 1) / aglue::WARPS));
   LB2_CHECK_ARG(grid.y < 65536, "qk_norm_rope: too many heads");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (D == 128)
     aglue::qk_norm_rope_kernel<128><<<grid, aglue::WARPS * 32, 0, st>>>(p);
   else if (D == 256)
