@@ -26,9 +26,10 @@ ROW_CANDIDATES = (5, 8, 16, 32, 64, 128, 256)
 
 # (Hq, Hkv, D) -> (per_key_bytes, min_rows, key_floor), as the reference's table; calibrate() fills it.
 layout = {}
-# The kernel entry array-masked prefills take: ops.attn_prefill, or ops.attn_prefill_tiled (tile skipping) once
-# qsa_tiles.install has rebound it (the reference's qsa_tiles.install rebinds `chunked` the same way).
-array_prefill = ops.attn_prefill
+# The kernel entry array-masked prefills take: None for ops.attn_prefill (looked up at each call), or
+# ops.attn_prefill_tiled (tile skipping) once qsa_tiles.install has rebound it (the reference's qsa_tiles.install
+# rebinds `chunked` the same way).
+array_prefill = None
 
 
 def _cut(nk, n, floor):
@@ -61,7 +62,7 @@ def chunked(q, k, v, scale, rows, min_rows, floor=0, mask=None, fused=False, gat
     out = torch.empty((B, Hq, T, D), dtype=q.dtype, device=q.device)
     if mask is None:
         return ops.attn_prefill(q, k, v, scale, "causal", gate=gate, out=out)
-    return array_prefill(q, k, v, scale, mask.reshape(T, N), gate=gate, out=out)
+    return (array_prefill or ops.attn_prefill)(q, k, v, scale, mask.reshape(T, N), gate=gate, out=out)
 
 
 def _arr_mask(mask, T, N):
@@ -86,7 +87,7 @@ def attend(queries, keys, values, scale, mask=None):
     if few and (mask is None or causal):
         return ops.attn_decode(queries, keys, values, scale, causal=causal and T > 1)
     if mask is not None and not causal:
-        return array_prefill(queries, keys, values, scale, mask)
+        return (array_prefill or ops.attn_prefill)(queries, keys, values, scale, mask)
     return ops.attn_prefill(queries, keys, values, scale, mask)
 
 

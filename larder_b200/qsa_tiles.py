@@ -81,4 +81,4 @@ def install(cache_gb=0.05, on=None):
 
 def uninstall():
     chunkattn.chunked = _STOCK_CHUNKED
-    chunkattn.array_prefill = ops.attn_prefill
+    chunkattn.array_prefill = None

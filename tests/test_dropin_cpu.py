@@ -89,7 +89,7 @@ def test_install_glue_needs_a_class_when_mlx_lm_is_absent():
 def test_qsa_tiles_install_is_off_unless_asked():
     from larder_b200 import chunkattn, ops, qsa_tiles
     assert not qsa_tiles.install(on=False)
-    assert chunkattn.chunked is not qsa_tiles.chunked and chunkattn.array_prefill is ops.attn_prefill
+    assert chunkattn.chunked is not qsa_tiles.chunked and chunkattn.array_prefill is None
 
 
 def test_qsa_tiles_flags_and_plan_on_cpu_tensors():
