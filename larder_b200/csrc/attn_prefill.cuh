@@ -192,6 +192,23 @@ __device__ __forceinline__ float ex2f(float x) {
   return y;
 }
 
+// 2^x on the FMA and integer pipes instead of the multi-function unit, for a share of the softmax's exponentials
+// (the split FlashAttention-4 describes for Blackwell): x = j + f with j = round(x) through the 1.5 * 2^23 rounding
+// constant, 2^f by a degree-4 polynomial whose coefficients were fitted for relative error on [-1/2, 1/2] (at most
+// 2.7e-6, about 18.5 bits: finer than the bf16 rounding P gets), 2^j added into the exponent field. x below -125
+// gives 0 (as ex2.approx.ftz gives 0 below -126; masked scores are -inf).
+__device__ __forceinline__ float ex2_fma(float x) {
+  const float xc = fmaxf(x, -125.f);
+  const float t = xc + 12582912.f;
+  const float f = xc - (t - 12582912.f);
+  float p = fmaf(0.009570101276040077f, f, 0.05591785907745361f);
+  p = fmaf(p, f, 0.240247443318367f);
+  p = fmaf(p, f, 0.6931217908859253f);
+  p = fmaf(p, f, 0.9999992847442627f);
+  const float r = __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+  return x < -125.f ? 0.f : r;
+}
+
 // Number of BN-key tiles query tile mt reads.
 template <int D>
 __device__ __forceinline__ int kv_tiles(const Params& p, int mt) {
