@@ -563,12 +563,51 @@ def bench_qsa(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_
     ms = max_over_ranks(cuda_time(torch, step, args.steps, stream)) / args.steps
     nbytes = B * nb * D * 2 + B * H * D * 2 + B * nb * 4 * 2 + B * k * 4  # keys and q in; scores out and back; picks
     gbs = nbytes / (ms * 1e-3) / 1e9
-    return {"value": round(world * gbs, 1), "unit": "GB/s", "ms_per_step": round(ms, 5), "bytes_per_step": nbytes,
-            "gpu_launches_per_step": 2,
-            "workload": "16 decode rows, Flash-Next indexer (4 x 128, CR 4, top 512) over 32768 pooled blocks each",
-            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                         "frac": round(gbs / pk["hbm_gbs"], 4),
-                         "kernel": "lb2::qsasel::score_kernel<128> + topk_kernel<16>"}}
+    res = {"value": round(world * gbs, 1), "unit": "GB/s", "ms_per_step": round(ms, 5), "bytes_per_step": nbytes,
+           "gpu_launches_per_step": 2,
+           "workload": "16 decode rows, Flash-Next indexer (4 x 128, CR 4, top 512) over 32768 pooled blocks each",
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                        "frac": round(gbs / pk["hbm_gbs"], 4),
+                        "kernel": "lb2::qsasel::score_kernel<128> + topk_kernel<16>"}}
+    res["decode_over_picks"] = bench_qsa_decode(torch, ops, dev, rank, args, stream, pk, barrier_sync,
+                                                max_over_ranks)
+    return res
+
+
+def bench_qsa_decode(torch, ops, dev, rank, args, stream, pk, barrier_sync, max_over_ranks):
+    """One Flash-Next decode row (24q/2kv x 256) over its 512 picked 4-row blocks and the tail of a 131072-position
+    cache: the picked rows read in place by the decode kernel, against the gather kernel then the same decode. A
+    different pick list each step (16 of them, over a 268 MB cache) so that steps read cold rows; each form timed as
+    one CUDA graph of the K steps. Bytes: the picked K / V rows each must read, and q / o."""
+    from larder_b200 import qsa
+    g = torch.Generator(device=dev).manual_seed(8500 + rank)
+    Hq, Hk, D, cr, nsel, n = 24, 2, 256, 4, 512, 131072
+    k = torch.randn(1, Hk, n, D, generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn(1, Hk, n, D, generator=g, device=dev).to(torch.bfloat16)
+    q = torch.randn(1, Hq, 1, D, generator=g, device=dev).to(torch.bfloat16)
+    tbs = [torch.randperm(n // cr, generator=g, device=dev)[:nsel].sort().values.to(torch.int32) for _ in range(16)]
+    m = nsel * cr + n - n // cr * cr
+    nbytes = 2 * Hk * m * D * 2 + 2 * Hq * D * 2
+    forms = {"in_place": lambda i: ops.qsa_decode(q, k, v, tbs[i % 16], cr, D ** -0.5),
+             "gather_then_decode": lambda i: ops.attn_decode(q, *qsa.qsa_gather(k, v, tbs[i % 16], cr), D ** -0.5)}
+    res = {}
+    for name, fn in forms.items():
+        for i in range(args.warmup):
+            fn(i)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(args.steps):
+                fn(i)
+        graph.replay()
+        barrier_sync()
+        ms = max_over_ranks(cuda_time(torch, lambda _: graph.replay(), 1, stream)) / args.steps
+        del graph
+        res[name] = {"ms_per_step": round(ms, 5), "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1)}
+    res["bytes_per_step"] = nbytes
+    res["workload"] = "Flash-Next decode row, 24q/2kv x 256, 512 picks of CR 4 + tail, 131072-position cache"
+    res["launch"] = "each form's K steps as one CUDA graph, replayed once"
+    res["kernel"] = "lb2::decode::decode_kernel<bf16, 256, 2> (picks mode) + split_combine_kernel"
+    return res
 
 
 def bench_tiles(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, reduce_over_ranks):

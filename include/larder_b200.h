@@ -241,6 +241,18 @@ int lb2_gdn_chunked(const void* q, const void* k, int qdt, const void* v, int vd
 int lb2_kv_gather_picks(const void* k, const int64_t* k_st, const void* v, const int64_t* v_st, const int32_t* tb,
                         int nsel, int cr, int n, void* kg, void* vg, int Hk, int D, int dtype, void* stream);
 
+/* The QSA decode step with the gather inside the decode: one query row q [1, Hq, 1, D] (strides q_st: batch, head,
+ * row) attends to the rows lb2_kv_gather_picks would gather from the [Hk, n, D] views k / v (strides k_st / v_st,
+ * multiples of 8 elements, bases 16-byte aligned), read straight from the views by the split-KV decode kernel's
+ * threads; o [1, Hq, 1, D] (strides o_st). The result is bit-equal to gather + lb2_attn_decode (split = 0). bf16 / f16,
+ * D = 64, 128 or 256; the workspace (256-byte aligned) as lb2_qsa_decode_workspace_size says. A pick reaching
+ * outside [0, n) reads row 0 and lb2_status reports LB2_EINVAL.
+ * Replaces: stream_fast._qsa_gather + attn_cuda's attention (stream_fast.py:6411-6491). */
+size_t lb2_qsa_decode_workspace_size(int nsel, int cr, int n, int Hq, int Hk, int D);
+int lb2_qsa_decode(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
+                   const int64_t* v_st, void* o, const int64_t* o_st, const int32_t* tb, int nsel, int cr, int n, int Hq,
+                   int Hk, int D, int dtype, float scale, void* workspace, size_t workspace_bytes, void* stream);
+
 /* The paged home: positions in chunks of 2^logc, each chunk [K/V][Hk][2^logc][D] contiguous, chunk addresses in a
  * uint64 device table (device memory or pinned, GPU-mapped host memory; each chunk 16-byte aligned, 2^logc a
  * multiple of cr). put writes s new positions pos0.. of

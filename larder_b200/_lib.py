@@ -39,6 +39,9 @@ SIGNATURES = {
     "lb2_gdn_chunked_workspace_size": ([_i, _i, _i, _i, _i, _i], _sz),
     "lb2_gdn_chunked": ([_p, _p, _i, _p, _i, _p, _i, _p, _i, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p, _sz, _p], _i),
     "lb2_kv_gather_picks": ([_p, _i64p, _p, _i64p, _p, _i, _i, _i, _p, _p, _i, _i, _i, _p], _i),
+    "lb2_qsa_decode_workspace_size": ([_i, _i, _i, _i, _i, _i], _sz),
+    "lb2_qsa_decode": ([_p, _i64p, _p, _i64p, _p, _i64p, _p, _i64p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _p, _sz, _p],
+                       _i),
     "lb2_kvh_put": ([_p, _p, _i64p, _p, _i64p, ctypes.c_int64, _i, _i, _i, _i, _i, _p], _i),
     "lb2_kvh_gather": ([_p, _p, _i, _i, _i, _p, _p, _i, _i, _i, _i, _p], _i),
     "lb2_attn_decode_host_workspace_size": ([_i, _i, _i, _i, _i, _i, _i, _i], _sz),

@@ -85,7 +85,36 @@ struct Params {
   uint32_t* push_count;
   uint32_t* push_flag[8];
   uint32_t push_epoch;
+  // pick mode (picks != nullptr; one sequence): the call's keys are the gathered rows of a QSA decode step -- key g is
+  // row tb[g / cr] cr + g % cr of the cache view for g < nsel cr, then the view's trailing partial block -- read
+  // straight from the view (pk / pv, head and position strides in bytes, view length pick_n) by the producer warp
+  const int32_t* picks;
+  int nsel, cr, pick_n;
+  const uint8_t* pk;
+  const uint8_t* pv;
+  int64_t pk_hst, pk_pst, pv_hst, pv_pst;
 };
+
+// The cache-view row of gathered key g in pick mode (out-of-range picks read row 0, recorded in the status word).
+__device__ __forceinline__ int pick_row(const Params& p, int g) {
+  const int j = g / p.cr;
+  const int r = j < p.nsel ? p.picks[j] * p.cr + (g - j * p.cr) : p.pick_n / p.cr * p.cr + (g - p.nsel * p.cr);
+  if (r < 0 || r >= p.pick_n) {
+    report_bad_index(98);
+    return 0;
+  }
+  return r;
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+// Arrives on the mbarrier once this thread's earlier cp.async copies have landed (raising the phase's expected count
+// by one first, so the arrival is neutral to it).
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.shared.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 
 template <typename T>
 __device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1);
@@ -270,7 +299,98 @@ __global__ void __launch_bounds__(Cfg<D, NT>::THREADS, 1) decode_kernel(const __
   // this grid's completion before reading any partial.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
+  // Pick mode: every thread of the CTA copies the CTA's first tiles (as many as the ring holds) before the roles part,
+  // so that those loads have the whole CTA's copy capacity behind them (one warp's 16-byte copies keep too few bytes
+  // in flight); the producer goes on from the next tile. Each thread's arrival follows its copies; thread 0's plain
+  // arrival, after a barrier, completes each stage's phase once all of them have landed.
+  constexpr int CPR = D / 8;  // 16-byte chunks a K / V row
+  int pre = 0;
+  if (p.picks) {
+    Sched s0(p, prefix, lens);
+    Item i0;
+    while (pre < STAGES && s0.next(i0)) {
+      const int nt = i0.n1 > i0.n0 ? (i0.n1 - i0.n0 + BK - 1) / BK : 0;
+      const uint8_t* kh = p.pk + i0.hk * p.pk_hst;
+      const uint8_t* vh = p.pv + i0.hk * p.pv_hst;
+      for (int i = 0; i < nt && pre < STAGES; ++i, ++pre) {
+        const uint32_t kt = smem_u32(sm + pre * C::STAGE_BYTES), vt = kt + C::TILE_BYTES;
+        const int key0 = i0.n0 + i * BK;
+        for (int e = threadIdx.x; e < BK * CPR; e += THREADS) {
+          const int r = e / CPR, c = e - r * CPR;
+          const int src = pick_row(p, min(key0 + r, i0.len - 1));
+          const uint32_t off = swz(c >> 3, r, c & 7);
+          cp_async16(kt + off, kh + src * p.pk_pst + c * 16);
+          cp_async16(vt + off, vh + src * p.pv_pst + c * 16);
+        }
+        cp_async_arrive(&full[pre]);
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0)
+      for (int i = 0; i < pre; ++i) mbar_arrive(&full[i]);
+  }
+
   // ------------------------------------------------------------------ producer warp: Q tiles and K/V tiles
+  if (warp == C::PRODUCER && p.picks) {
+    // Pick mode: lane 0 loads the Q tiles by TMA as below; the whole warp fills each K / V tile with 16-byte cp.async
+    // copies of the gathered rows, into the layout the TMA boxes give (128-byte swizzle, [D / 64][BK][64]). Lane l
+    // resolves the rows l and l + 32 of a tile (rows past the call's length repeat its last row, which the consumers
+    // mask), and every lane's arrival on the stage's full barrier follows its copies. The CTA's first `pre` tiles
+    // were copied above by all its threads.
+    int gt = 0, uc = 0;
+    bool ok = true;
+    Sched sched(p, prefix, lens);
+    Item it;
+    for (; ok && sched.next(it); ++uc) {
+      const int b = it.b, hk = it.hk, n0 = it.n0;
+      const int ntiles = it.n1 > n0 ? (it.n1 - n0 + BK - 1) / BK : 0;
+      const int qs = uc & 1;
+      if (lane == 0) {
+        ok = uc < 2 || mbar_wait(&q_empty[qs], ((uc >> 1) - 1) & 1, 1);
+        if (ok) {
+          mbar_arrive_expect_tx(&q_full[qs], (D / 64) * p.rows * 128);
+#pragma unroll
+          for (int db = 0; db < D / 64; ++db)
+            tma_load_4d(sm + C::Q_OFF + qs * C::QSLOT + db * RP * 128, &qmap, db * 64, 0, hk * p.G, b, &q_full[qs]);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      const uint8_t* kh = p.pk + hk * p.pk_hst;
+      const uint8_t* vh = p.pv + hk * p.pv_hst;
+      for (int i = 0; ok && i < ntiles; ++i, ++gt) {
+        if (gt < pre) continue;
+        const int st = gt % STAGES;
+        bool w = true;
+        if (lane == 0 && gt >= STAGES) w = mbar_wait(&empty[st], ((gt / STAGES) - 1) & 1, 2);
+        if (!__shfl_sync(0xffffffffu, w, 0)) {
+          ok = false;
+          break;
+        }
+        const uint32_t kt = smem_u32(sm + st * C::STAGE_BYTES), vt = kt + C::TILE_BYTES;
+        const int key0 = n0 + i * BK;
+        const int row_lo = pick_row(p, min(key0 + lane, it.len - 1));
+        const int row_hi = pick_row(p, min(key0 + 32 + lane, it.len - 1));
+#pragma unroll 4
+        for (int t = 0; t < BK * CPR / 32; ++t) {
+          const int e = lane + 32 * t, r = e / CPR, c = e - r * CPR;
+          const int src = (32 * t) / CPR < 32 ? __shfl_sync(0xffffffffu, row_lo, r & 31)
+                                               : __shfl_sync(0xffffffffu, row_hi, r & 31);
+          const uint32_t off = swz(c >> 3, r, c & 7);
+          cp_async16(kt + off, kh + src * p.pk_pst + c * 16);
+          cp_async16(vt + off, vh + src * p.pv_pst + c * 16);
+        }
+        cp_async_arrive(&full[st]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[st]);
+      }
+    }
+    // Drain: the last copies issued have landed before the CTA may finish (normally already consumed).
+    if (lane == 0) {
+      for (int g2 = max(0, gt - STAGES); g2 < gt; ++g2) mbar_wait(&full[g2 % STAGES], (g2 / STAGES) & 1, 3);
+      for (int q2 = max(0, uc - 2); q2 < uc; ++q2) mbar_wait(&q_full[q2 & 1], (q2 >> 1) & 1, 4);
+    }
+    return;
+  }
   if (warp == C::PRODUCER) {
     if (lane == 0) {
       int gt = 0, uc = 0;

@@ -211,7 +211,8 @@ static int run(const void* q, const int64_t* q_st, const void* k, const int64_t*
                const int32_t* kv_len, int B, int Hq, int Hkv, int T, int N, int D, int dtype, float scale, int causal,
                int split, void* workspace, size_t workspace_bytes, void* stream, int npush = 0,
                float* const* push_o = nullptr, float* const* push_lse = nullptr, uint32_t* push_count = nullptr,
-               uint32_t* const* push_flag = nullptr, uint32_t push_epoch = 0) {
+               uint32_t* const* push_flag = nullptr, uint32_t push_epoch = 0, const int32_t* picks = nullptr,
+               int nsel = 0, int cr = 0, int pick_n = 0) {
   LB2_CHECK_ARG(B > 0 && Hq > 0 && Hkv > 0 && T > 0 && N > 0, "decode: empty shape");
   LB2_CHECK_ARG(Hq % Hkv == 0, "decode: Hq must be a multiple of Hkv");
   LB2_CHECK_ARG(D == 64 || D == 128 || D == 256, "decode: head dim must be 64, 128 or 256");
@@ -230,9 +231,10 @@ static int run(const void* q, const int64_t* q_st, const void* k, const int64_t*
   LB2_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "decode: workspace must be 256-byte aligned");
   LB2_CHECK_ARG(B <= MAX_B, "decode: at most 1024 sequences a call");
   CUtensorMap qm, km, vm;
-  int rc = kv_map(&km, k, k_st, B, Hkv, N, D, dtype);
+  // (pick mode reads K and V by copies of its own; the maps, over the cache view, go unused)
+  int rc = kv_map(&km, k, k_st, B, Hkv, picks ? pick_n : N, D, dtype);
   if (rc) return rc;
-  rc = kv_map(&vm, v, v_st, B, Hkv, N, D, dtype);
+  rc = kv_map(&vm, v, v_st, B, Hkv, picks ? pick_n : N, D, dtype);
   if (rc) return rc;
   {  // the folded Q tile of one KV head: a (64, T, G, 1) box of the (D, T, Hq, B) view of q
     const uint64_t dims[4] = {uint64_t(D), uint64_t(T), uint64_t(Hq), uint64_t(B)};
@@ -273,6 +275,21 @@ static int run(const void* q, const int64_t* q_st, const void* k, const int64_t*
   p.grid = pl.grid;
   p.causal = causal && T > 1;
   p.scale_log2 = scale * 1.4426950408889634f;
+  if (picks) {
+    LB2_CHECK_ARG(B == 1 && !causal && kv_len == nullptr, "decode: pick mode takes one sequence, no mask");
+    LB2_CHECK_ARG((reinterpret_cast<uintptr_t>(k) & 15) == 0 && (reinterpret_cast<uintptr_t>(v) & 15) == 0,
+                  "decode: k / v must be 16-byte aligned");
+    p.picks = picks;
+    p.nsel = nsel;
+    p.cr = cr;
+    p.pick_n = pick_n;
+    p.pk = static_cast<const uint8_t*>(k);
+    p.pv = static_cast<const uint8_t*>(v);
+    p.pk_hst = k_st[1] * 2;
+    p.pk_pst = k_st[2] * 2;
+    p.pv_hst = v_st[1] * 2;
+    p.pv_pst = v_st[2] * 2;
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return dtype == LB2_BF16 ? launch_d<__nv_bfloat16>(D, NT, qm, km, vm, p, st)
                            : launch_d<__half>(D, NT, qm, km, vm, p, st);
@@ -1102,6 +1119,24 @@ int lb2_kv_gather_picks(const void* k, const int64_t* k_st, const void* v, const
     LB2_CUDA(cudaGetLastError());
     return LB2_OK;
   });
+}
+
+size_t lb2_qsa_decode_workspace_size(int nsel, int cr, int n, int Hq, int Hk, int D) {
+  if (nsel < 0 || cr <= 0 || n < 0 || Hq <= 0 || Hk <= 0 || Hq % Hk) return 0;
+  const int m = nsel * cr + n - n / cr * cr;
+  return m > 0 ? lb2_attn_decode_workspace_size(1, Hq, Hk, 1, m, D, 0) : 0;
+}
+
+int lb2_qsa_decode(const void* q, const int64_t* q_st, const void* k, const int64_t* k_st, const void* v,
+                   const int64_t* v_st, void* o, const int64_t* o_st, const int32_t* tb, int nsel, int cr, int n, int Hq,
+                   int Hk, int D, int dtype, float scale, void* workspace, size_t workspace_bytes, void* stream) {
+  LB2_CHECK_ARG(nsel >= 0 && cr > 0 && n >= 0 && Hq > 0 && Hk > 0, "qsa_decode: shape");
+  LB2_CHECK_ARG(nsel == 0 || tb != nullptr, "qsa_decode: picks missing");
+  const int m = nsel * cr + n - n / cr * cr;
+  LB2_CHECK_ARG(m > 0, "qsa_decode: no key to attend to");
+  return decode::run(q, q_st, k, k_st, v, v_st, o, o_st, nullptr, nullptr, nullptr, 1, Hq, Hk, 1, m, D, dtype, scale,
+                     0, 0, workspace, workspace_bytes, stream, 0, nullptr, nullptr, nullptr, nullptr, 0, tb, nsel, cr,
+                     n);
 }
 
 int lb2_kvh_put(const uint64_t* table, const void* k, const int64_t* k_st, const void* v, const int64_t* v_st,

@@ -360,6 +360,36 @@ def kv_gather_picks(k, v, tb, cr, n=None):
     return kg, vg
 
 
+def qsa_decode(q, k, v, tb, cr, scale, n=None, out=None):
+    """One QSA decode row with the gather inside the decode kernel: q [1, Hq, 1, D] attends to the rows of k / v
+    [Hk, n, D] (or [1, Hk, n, D]) that kv_gather_picks(k, v, tb, cr) would return, read in place. Bit-equal to
+    attn_decode over kv_gather_picks' output."""
+    _cuda(q, k, v, tb)
+    if k.dim() == 4:
+        k, v = k[0], v[0]
+    for t, nm in ((q, "q"), (k, "k"), (v, "v")):
+        _unit_last(t, nm)
+    Hk, N, D = k.shape
+    n = N if n is None else int(n)
+    tb = tb.reshape(-1)
+    if tb.dtype != torch.int32:
+        raise ValueError("tb must be int32")
+    _, Hq, T, _ = q.shape
+    if q.shape[0] != 1 or T != 1:
+        raise ValueError("qsa_decode: one query row [1, Hq, 1, D]")
+    if out is None:
+        out = torch.empty_like(q)
+    nsel = tb.numel()
+    L = lib()
+    ws = workspace(q.device, L.lb2_qsa_decode_workspace_size(nsel, int(cr), n, Hq, Hk, D), "decode")
+    # (the views as [1, Hk, n, D]: a batch stride of Hk heads, for the tensor maps the kernel is given)
+    rc = L.lb2_qsa_decode(_ptr(q), i64(*q.stride()[:3]), _ptr(k), i64(Hk * k.stride(0), *k.stride()[:2]), _ptr(v),
+                          i64(Hk * v.stride(0), *v.stride()[:2]), _ptr(out), i64(*out.stride()[:3]), _ptr(tb), nsel,
+                          int(cr), n, Hq, Hk, D, dtype_code(q), float(scale), _ptr(ws), ws.numel(), _stream(q))
+    check(rc, "qsa_decode")
+    return out
+
+
 def kvh_put(table, k, v, pos0, logc):
     """Write k / v [Hk, s, D] (or [1, Hk, s, D]) as positions pos0 .. pos0 + s - 1 of the paged home `table`."""
     _cuda(table, k, v)

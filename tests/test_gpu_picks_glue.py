@@ -51,6 +51,31 @@ def test_qsa_gather_bit_exact_and_attend():
     checks.grading_close(out, full, what="picks vs masked pass")
 
 
+@pytest.mark.parametrize("Hq, Hk, D, cr, nsel, n, cap", [
+    (24, 2, 256, 4, 512, 10003, 10240),   # Flash-Next's decode shapes, a capacity-padded cache
+    (24, 2, 256, 8, 300, 4099, 4352),     # CR 8, a 3-row tail
+    (16, 2, 128, 1, 700, 2048, 2048),     # CR 1 (picked single rows), no tail
+    (8, 1, 64, 3, 50, 1001, 1024),        # a block size that does not divide the 64-key tile
+    (32, 4, 128, 16, 1, 40, 64),          # one pick and a tail: less than one tile
+])
+def test_qsa_decode_in_place_equals_gather_then_decode(Hq, Hk, D, cr, nsel, n, cap):
+    """The decode kernel reading the picked rows in place (the CTA's copies) is bit-equal to the gather kernel
+    followed by the same decode over the gathered rows; and both match the oracle over those rows."""
+    g = torch.Generator().manual_seed(30 + cr + D)
+    kb = torch.randn(1, Hk, cap, D, generator=g).to(torch.bfloat16).cuda()
+    vb = torch.randn(1, Hk, cap, D, generator=g).to(torch.bfloat16).cuda()
+    k, v = kb[:, :, :n], vb[:, :, :n]
+    tb, pos = picks(n, cr, nsel, g)
+    q = torch.randn(1, Hq, 1, D, generator=g).to(torch.bfloat16).cuda()
+    kg, vg = qsa.qsa_gather(k, v, tb.cuda(), cr)
+    two_step = ops.attn_decode(q, kg, vg, D ** -0.5)
+    fused = ops.qsa_decode(q, k, v, tb.cuda(), cr, D ** -0.5)
+    assert torch.equal(fused, two_step)
+    if nsel <= 64:
+        ref = oracle.attn(to_np(q), to_np(kg), to_np(vg), D ** -0.5, oracle.BF16, out_dt=oracle.F32)
+        checks.grading_close(f32(fused), ref, what="picks in place")
+
+
 @pytest.mark.parametrize("host", [False, True])
 def test_kv_home_put_gather_decode(host):
     """Rows appended in three puts across a chunk boundary (4096), then the picks gathered from the home equal the
