@@ -324,6 +324,19 @@ def bench_decode(torch, ops, dev, rank, world, args, stream, pk, pk_kind, barrie
                   "h2d_bytes_per_step": q_host[0].numel() * 2, "d2h_bytes_per_step": o_host[0].numel() * 2,
                   "ms_per_step": round(per_e2e, 5), "api": "larder_b200.ops.attn_decode_host (lb2_attn_decode_host)",
                   "copies": "q in and o out every step from / to pinned host memory, on the library's copy streams"}
+    # The output checked: the last e2e step and the graph's last step decoded the same inputs (they must be bit-equal),
+    # and sequence 0 of that step against torch's fp32 attention over the same bf16 values (GQA heads expanded).
+    last = (args.steps - 1) % copies
+    torch.cuda.synchronize(dev)
+    _, k_l, v_l = sets[last]
+    n0 = int(lens[0])
+    qf = q_dev[last][:1].float()
+    kf = k_l[:1, :, :n0].float().repeat_interleave(Hq // Hkv, dim=1)
+    vf = v_l[:1, :, :n0].float().repeat_interleave(Hq // Hkv, dim=1)
+    ref = torch.nn.functional.scaled_dot_product_attention(qf, kf, vf, scale=D ** -0.5)
+    out["check"] = {"e2e_bit_equal_to_graph_step": bool(torch.equal(o_host[last % 2].to(dev), o_dev)),
+                    "max_abs_diff_vs_torch_fp32_sdpa_seq0": round(float((o_dev[:1].float() - ref).abs().max()), 6),
+                    "seq0_keys": n0}
     del sets, q_dev, graph
     torch.cuda.empty_cache()
 

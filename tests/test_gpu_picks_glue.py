@@ -76,6 +76,20 @@ def test_qsa_decode_in_place_equals_gather_then_decode(Hq, Hk, D, cr, nsel, n, c
         checks.grading_close(f32(fused), ref, what="picks in place")
 
 
+def test_qsa_decode_in_place_reports_an_out_of_range_pick():
+    """A pick past the view's end is not read (the kernel takes row 0 in its place) and lb2_status reports LB2_EINVAL
+    from the pick-mode producer (where 98); the other rows attend as usual, so the output stays finite."""
+    g = torch.Generator().manual_seed(44)
+    Hq, Hk, D, cr, n = 8, 2, 128, 4, 400
+    k = torch.randn(1, Hk, n, D, generator=g).to(torch.bfloat16).cuda()
+    v = torch.randn(1, Hk, n, D, generator=g).to(torch.bfloat16).cuda()
+    q = torch.randn(1, Hq, 1, D, generator=g).to(torch.bfloat16).cuda()
+    tb = torch.tensor([0, 5, n // cr], dtype=torch.int32).cuda()  # block n // cr starts at row n: outside
+    out = ops.qsa_decode(q, k, v, tb, cr, D ** -0.5)
+    assert ops.status() == (98 << 8) | 1
+    assert torch.isfinite(out.float()).all()
+
+
 @pytest.mark.parametrize("host", [False, True])
 def test_kv_home_put_gather_decode(host):
     """Rows appended in three puts across a chunk boundary (4096), then the picks gathered from the home equal the
