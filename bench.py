@@ -379,6 +379,19 @@ def bench_prefill(torch, ops, dev, rank, world, args, stream, pk, pk_kind, barri
     ms = max_over_ranks(ms)
     ms_chunks = max_over_ranks(cuda_time(torch, step_per_chunk, args.steps, stream)) / args.steps
     barrier_sync()
+    # the output checked: the one-launch wide cut against the per-chunk launches, and the last 64 rows of head 0
+    # against torch's fp32 attention over their causal keys, times sigmoid(gate)
+    o1 = chunkattn.chunked(qv, k, v, D ** -0.5, W, W, gate=gv)
+    step_per_chunk(0)
+    rows = slice(T - 64, T)
+    qf, kf, vf = qv[0, 0, rows].float(), k[0, 0].float(), v[0, 0].float()
+    sc = (qf @ kf.t()) * D ** -0.5
+    sc = sc.masked_fill(torch.arange(T, device=dev)[None, :] > torch.arange(T - 64, T, device=dev)[:, None],
+                        float("-inf"))
+    ref = (torch.softmax(sc, -1) @ vf) * torch.sigmoid(gv[0, 0, rows].float())
+    prefill_check = {"one_launch_bit_equal_to_per_chunk": bool(torch.equal(o1, out)),
+                     "max_abs_diff_vs_torch_fp32_head0_last64": round(float((o1[0, 0, rows].float() - ref).abs().max()),
+                                                                     6)}
     per = ms / args.steps
     tf = flop / (per * 1e-3) / 1e12
     return {"value": round(world * tf, 2), "unit": "TFLOP/s", "ms_per_step": round(per, 4),
@@ -391,7 +404,7 @@ def bench_prefill(torch, ops, dev, rank, world, args, stream, pk, pk_kind, barri
             "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": round(tf / pk["bf16_tflops"], 4), "traffic": None, "peak_kind": pk_kind,
                          "kernel": "lb2::prefill2::fmha2_kernel<bf16,256>"},
-            "clocks": clk.summary()}
+            "check": prefill_check, "clocks": clk.summary()}
 
 
 def bench_sharded(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, reduce_over_ranks):
@@ -789,6 +802,11 @@ def bench_gdn(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_
     pre_rec(0)
     barrier_sync()
     ms_r = max_over_ranks(cuda_time(torch, pre_rec, max(2, args.steps // 10), stream)) / max(2, args.steps // 10)
+    # the output checked: the chunked scan against the position-by-position kernel (two algorithms of this library)
+    y_c, s_c = ops.gdn_chunked(pq, pk_, pv, pg, pb, s0)
+    y_r, s_r = ops.gdn_recurrent(pq, pk_, pv, pg, pb, s0)
+    gdn_check = {"chunked_vs_recurrent_y_max_abs": round(float((y_c.float() - y_r.float()).abs().max()), 6),
+                 "chunked_vs_recurrent_state_max_rel": round(float((s_c - s_r).abs().max() / s_r.abs().max()), 8)}
     flop = 7.0 * T * Hv * D * D
     pbytes = 2 * T * Hk * D * 2 + 2 * T * Hv * D * 2 + 2 * T * Hv * 4 + 2 * Hv * D * D * 4
     t_roof = max(flop / (pk["bf16_tflops"] * 1e12), pbytes / (pk["hbm_gbs"] * 1e9))
@@ -798,7 +816,7 @@ def bench_gdn(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_
                "flop_per_step": flop, "algorithmic_bytes": pbytes, "gpu_launches_per_step": 2,
                "roofline": {"bound": "max(tensor, hbm)", "roof_ms": round(t_roof * 1e3, 4),
                             "frac": round(t_roof * 1e3 / ms_p, 4), "unit": "time",
-                            "kernel": "lb2::gdnchunk::{prep_kernel, scan_kernel}"}}
+                            "kernel": "lb2::gdnchunk::{prep_kernel, scan_kernel}"}, "check": gdn_check}
     del graph
     res = {"prefill": prefill,
            "decode": {"value": round(world * gbs, 1), "unit": "GB/s", "ms_per_step": round(per, 5),
