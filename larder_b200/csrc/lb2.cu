@@ -738,6 +738,8 @@ int lb2_attn_combine_peers(const uint64_t* bufs, int R, int rank, uint32_t epoch
   p.epoch = epoch;
   p.rows = B * Hq * T;
   p.half = int64_t(p.rows) * (D + 1);
+  p.vec = p.rows % 4 == 0 && (D == 64 || D == 128 || D == 256);
+  for (int r = 0; r < R; ++r) p.vec = p.vec && (bufs[r] & 15) == 0;
   p.Hq = Hq;
   p.Tq = T;
   p.D = D;
@@ -794,6 +796,7 @@ int lb2_attn_combine_pushed(const uint64_t* bufs, int R, int rank, uint32_t epoc
   p.rows = B * Hq * T;
   p.half = int64_t(R) * p.rows * (D + 1);
   p.pushed = 1;
+  p.vec = p.rows % 4 == 0 && (D == 64 || D == 128 || D == 256) && (bufs[rank] & 15) == 0;
   p.Hq = Hq;
   p.Tq = T;
   p.D = D;
