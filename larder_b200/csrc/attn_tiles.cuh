@@ -15,15 +15,30 @@ namespace lb2 {
 namespace tiles {
 
 // flags[rb * nkt + kt] = 1 when a row of [rb RB, rb RB + RB) and a key of [kt BN, kt BN + BN) (clipped to T x N) are
-// kept. One CTA a (key tile, row block); each thread stops at its first kept element.
+// kept. One CTA a (key tile, row block); each thread stops at its first kept element. With `vec` (rows of unit key
+// stride, 16-byte aligned, BN a multiple of 16) a thread reads 16 keys a load; otherwise one byte at a time.
 __global__ void __launch_bounds__(256) flag_kernel(const uint8_t* mask, int64_t ms0, int64_t ms1, int T, int N, int RB,
-                                                   int BN, int nkt, uint8_t* flags) {
+                                                   int BN, int nkt, uint8_t* flags, int vec) {
   const int kt = blockIdx.x, rb = blockIdx.y;
   const int r0 = rb * RB, rows = min(T, r0 + RB) - r0, k0 = kt * BN, w = min(N, k0 + BN) - k0;
   int any = 0;
-  for (int i = threadIdx.x; i < rows * w && !any; i += blockDim.x) {
-    const int r = r0 + i / w, c = k0 + i % w;
-    any = mask[int64_t(r) * ms0 + int64_t(c) * ms1] != 0;
+  if (vec) {
+    const int cpr = (w + 15) >> 4;  // 16-byte pieces a row (the last may be short)
+    for (int i = threadIdx.x; i < rows * cpr && !any; i += blockDim.x) {
+      const int r = i / cpr, j = i - r * cpr;
+      const uint8_t* pc = mask + int64_t(r0 + r) * ms0 + k0 + 16 * j;
+      if (16 * j + 16 <= w) {
+        const uint4 u = *reinterpret_cast<const uint4*>(pc);
+        any = (u.x | u.y | u.z | u.w) != 0u;
+      } else {
+        for (int e = 0; e < w - 16 * j; ++e) any |= pc[e] != 0;
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < rows * w && !any; i += blockDim.x) {
+      const int r = r0 + i / w, c = k0 + i % w;
+      any = mask[int64_t(r) * ms0 + int64_t(c) * ms1] != 0;
+    }
   }
   any = __syncthreads_or(any);
   if (threadIdx.x == 0) flags[int64_t(rb) * nkt + kt] = uint8_t(any);

@@ -886,8 +886,9 @@ int prefill_run(const void* q, const int64_t* q_st, const void* k, const int64_t
     uint8_t* flags = static_cast<uint8_t*>(ws);
     int32_t* list = reinterpret_cast<int32_t*>(flags + (int64_t(nrb) * nkt + 255) / 256 * 256);
     int32_t* count = list + int64_t(nrb) * nkt;
+    const int vec = m_st[1] == 1 && m_st[0] % 16 == 0 && TBN % 16 == 0 && (reinterpret_cast<uintptr_t>(mask) & 15) == 0;
     tiles::flag_kernel<<<dim3(unsigned(nkt), unsigned(nrb)), 256, 0, st>>>(mask, m_st[0], m_st[1], T, N, RB, TBN,
-                                                                             nkt, flags);
+                                                                             nkt, flags, vec);
     tiles::compact_kernel<<<unsigned((nrb + 3) / 4), 128, 0, st>>>(flags, nrb, nkt, list, count);
     LB2_CUDA(cudaGetLastError());
     p.tl = list;

@@ -92,7 +92,7 @@ def attn_prefill(q, k, v, scale, mask=None, gate=None, out=None):
     elif mask is not None:
         if mask.dtype != torch.bool or tuple(mask.shape[-2:]) != (T, N) or any(d != 1 for d in mask.shape[:-2]):
             raise ValueError("array masks must be bool [..., T, N] with leading dims of 1")
-        m = mask.reshape(T, N).to(torch.uint8)
+        m = mask.reshape(T, N).view(torch.uint8)  # (bool and uint8 share a byte layout: no copy, strides kept)
         kind, mst = _lib.MASK_ARRAY, i64(m.stride(0), m.stride(1))
     gst = i64(0, 0, 0)
     if gate is not None:
@@ -119,7 +119,7 @@ def attn_prefill_tiled(q, k, v, scale, mask, gate=None, out=None):
         raise ValueError("q, k, v must share a dtype")
     if mask.dtype != torch.bool or tuple(mask.shape[-2:]) != (T, N) or any(d != 1 for d in mask.shape[:-2]):
         raise ValueError("array masks must be bool [..., T, N] with leading dims of 1")
-    m = mask.reshape(T, N).to(torch.uint8)
+    m = mask.reshape(T, N).view(torch.uint8)  # (no copy, strides kept)
     if out is None:
         out = torch.empty((B, Hq, T, D), dtype=q.dtype, device=q.device)
     gst = i64(0, 0, 0)

@@ -59,6 +59,20 @@ def test_tiled_matches_oracle_and_masked_kernel(Hq, Hkv, D, T, N, density):
         assert qsa_tiles.group_flags(m, D).float().mean().item() < 1.0
 
 
+def test_mask_view_with_padded_rows():
+    """A mask that is a column slice of a wider one (row stride 2016, a multiple of 16; N = 2001, not): the tile
+    listing reads 16 keys a load and the last tile's short piece bytewise."""
+    g = torch.Generator().manual_seed(6)
+    Hq, Hkv, D, T, N = 8, 2, 128, 300, 2001
+    q, k, v = rnd(g, 1, Hq, T, D), rnd(g, 1, Hkv, N, D), rnd(g, 1, Hkv, N, D)
+    wide = torch.zeros(T, 2016, dtype=torch.bool)
+    wide[:, :N] = qsa_mask(T, N, 0.1, g)
+    wide[:, N:] = True  # columns past N must not be read
+    m = wide.cuda()[:, :N]
+    out = ops.attn_prefill_tiled(q, k, v, D ** -0.5, m)
+    assert torch.equal(out, ops.attn_prefill(q, k, v, D ** -0.5, m))
+
+
 def test_whole_row_blocks_without_keys_and_the_gate():
     g = torch.Generator().manual_seed(5)
     Hq, Hkv, D, T, N = 16, 2, 256, 640, 2048
