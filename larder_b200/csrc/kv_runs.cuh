@@ -81,13 +81,19 @@ __global__ void __launch_bounds__(RUN_THREADS) view_runs_kernel(Rows<U> k, Rows<
   const bool inside = run.p0 >= 0 && run.p0 + run.len <= n;
   if (!inside && threadIdx.x == 0) report_bad_index(94);
   const int units = run.len * upr;
-  for (int h = 0; h < Hk; ++h) {
-    U* dst = out + (int64_t(h) * m + run.out0) * upr;
+  // up to HB heads' loads go out before any store (a store may alias a later load as far as the compiler knows, so
+  // a head-by-head loop would wait a round trip a head)
+  constexpr int HB = 4;
+  for (int h0 = 0; h0 < Hk; h0 += HB)
     for (int u = threadIdx.x; u < units; u += RUN_THREADS) {
       const int r = u / upr, c = u - r * upr;
-      dst[u] = inside ? *src.at(h, run.p0 + r, c) : U{};
+      U x[HB];
+#pragma unroll
+      for (int i = 0; i < HB; ++i) x[i] = (inside && h0 + i < Hk) ? *src.at(h0 + i, run.p0 + r, c) : U{};
+#pragma unroll
+      for (int i = 0; i < HB; ++i)
+        if (h0 + i < Hk) out[(int64_t(h0 + i) * m + run.out0) * upr + u] = x[i];
     }
-  }
 }
 
 // The same rows read from the paged home (table of chunk addresses), n = the sequence length.
