@@ -108,10 +108,20 @@ __global__ void __launch_bounds__(RUN_THREADS) home_runs_kernel(const uint64_t* 
   const bool inside = run.p0 >= 0 && run.p0 + run.len <= n;
   if (!inside && threadIdx.x == 0) report_bad_index(95);
   const int units = run.len * upr;
-  for (int h = 0; h < Hk; ++h) {
-    U* dst = out + (int64_t(h) * m + run.out0) * upr;
-    const U* src = inside && run.len ? home_run<U>(tbl, run.p0, kv, h, Hk, upr, logc, 96) : nullptr;  // one chunk
-    for (int u = threadIdx.x; u < units; u += RUN_THREADS) dst[u] = src ? ld_bypass(src + u) : U{};
+  constexpr int HB = 4;  // heads whose loads go out before any store, as view_runs_kernel
+  for (int h0 = 0; h0 < Hk; h0 += HB) {
+    const U* src[HB];
+#pragma unroll
+    for (int i = 0; i < HB; ++i)  // one chunk a run
+      src[i] = inside && run.len && h0 + i < Hk ? home_run<U>(tbl, run.p0, kv, h0 + i, Hk, upr, logc, 96) : nullptr;
+    for (int u = threadIdx.x; u < units; u += RUN_THREADS) {
+      U x[HB];
+#pragma unroll
+      for (int i = 0; i < HB; ++i) x[i] = src[i] ? ld_bypass(src[i] + u) : U{};
+#pragma unroll
+      for (int i = 0; i < HB; ++i)
+        if (h0 + i < Hk) out[(int64_t(h0 + i) * m + run.out0) * upr + u] = x[i];
+    }
   }
 }
 
