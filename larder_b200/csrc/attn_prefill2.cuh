@@ -72,11 +72,13 @@ struct Cfg {
   static_assert(D == 128 || D == 256, "the pair kernel is built for head dims 128 and 256");
 };
 
-// The softmax's exponential of column c of a thread's 32: a quarter of them (c % 8 in {6, 7}) on the FMA pipe, the rest
-// on the multi-function unit, whose 16 results a clock an SM would otherwise pace the tile at head dim 128 (one
-// exponential per 512 MMA flops there, about what the tensor cores do in the same time).
+// The softmax's exponential of column c of a thread's 32: at head dim 256 a quarter of them (c % 8 in {6, 7}) on the
+// FMA pipe, the rest on the multi-function unit. At head dim 128 all go to the multi-function unit: that kernel is
+// bound by instruction issue, and the polynomial's nine instructions cost more than the unit's queue (measured 2.7 %
+// slower with the split).
+template <int D>
 __device__ __forceinline__ float ex2_mix(int c, float x) {
-  return (c & 7) >= 6 ? prefill::ex2_fma(x) : prefill::ex2f(x);
+  return (D == 256 && (c & 7) >= 6) ? prefill::ex2_fma(x) : prefill::ex2f(x);
 }
 
 // ---------------------------------------------------------------------------------------------- cluster helpers
@@ -500,8 +502,8 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
         uint32_t pk[HC / 2];
 #pragma unroll
         for (int c = 0; c < HC; c += 2) {
-          const float e0 = ex2_mix(c, fmaf(s[c], p.scale_log2, nm));
-          const float e1 = ex2_mix(c, fmaf(s[c + 1], p.scale_log2, nm));
+          const float e0 = ex2_mix<D>(c, fmaf(s[c], p.scale_log2, nm));
+          const float e1 = ex2_mix<D>(c, fmaf(s[c + 1], p.scale_log2, nm));
           ls4[c & 3] += e0;
           ls4[(c + 1) & 3] += e1;
           pk[c / 2] = pack2<T>(e0, e1);
@@ -560,8 +562,8 @@ __global__ void __launch_bounds__(THREADS, 1) fmha2_kernel(const __grid_constant
             for (int c = 0; c < 4; ++c) ls4[c] = 0.f;
 #pragma unroll
             for (int c = 0; c < HC; c += 2) {
-              const float e0 = ex2_mix(c, fmaf(s[c], p.scale_log2, nm));
-              const float e1 = ex2_mix(c, fmaf(s[c + 1], p.scale_log2, nm));
+              const float e0 = ex2_mix<D>(c, fmaf(s[c], p.scale_log2, nm));
+              const float e1 = ex2_mix<D>(c, fmaf(s[c + 1], p.scale_log2, nm));
               ls4[c & 3] += e0;
               ls4[(c + 1) & 3] += e1;
               pk[c / 2] = pack2<T>(e0, e1);
