@@ -824,7 +824,7 @@ def bench_gdn(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_
                       "launch": "the K steps as one CUDA graph, replayed once",
                       "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                                    "frac": round(gbs / pk["hbm_gbs"], 4),
-                                   "kernel": "lb2::gdnrec::recurrent_kernel<bf16,4,8>"},
+                                   "kernel": "lb2::gdnrec::recurrent_kernel<bf16,4,4>"},
                       "clocks": clk.summary()}}
     return res
 

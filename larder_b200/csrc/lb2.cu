@@ -1018,9 +1018,9 @@ int lb2_gdn_recurrent(const void* q, const void* k, int qdt, const void* v, int 
   LB2_CHECK_ARG((reinterpret_cast<uintptr_t>(state_in) & 15) == 0 && (reinterpret_cast<uintptr_t>(state_out) & 15) == 0,
                 "gdn: state buffers must be 16-byte aligned");
   const int warps = 4;
-  // value rows a warp: several for a decode step (more state in flight, 32 fp32 values a lane), one for longer
-  // passes (more warps)
-  const int R = T > 1 ? 1 : (Dk == 256 ? 4 : (Dv % 8 == 0 ? 8 : 4));
+  // value rows a warp: four for a decode step (more state in flight; eight measured 2 % slower at Dk = 128), one for
+  // longer passes (more warps)
+  const int R = T > 1 ? 1 : 4;
   LB2_CHECK_ARG(int64_t(B) * Hv < 65536, "gdn: at most 65535 (sequence, head) pairs a call");
   dim3 grid(unsigned((Dv / R + warps - 1) / warps), unsigned(B * Hv));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -1032,18 +1032,12 @@ int lb2_gdn_recurrent(const void* q, const void* k, int qdt, const void* v, int 
       case 128: gdnrec::recurrent_kernel<QT, 4, 1><<<grid, warps * 32, 0, st>>>(p); break;           \
       default: gdnrec::recurrent_kernel<QT, 8, 1><<<grid, warps * 32, 0, st>>>(p); break;            \
     }                                                                                                \
-  } else if (R == 4) {                                                                              \
+  } else {                                                                                           \
     switch (Dk) {                                                                                    \
       case 32: gdnrec::recurrent_kernel<QT, 1, 4><<<grid, warps * 32, 0, st>>>(p); break;            \
       case 64: gdnrec::recurrent_kernel<QT, 2, 4><<<grid, warps * 32, 0, st>>>(p); break;            \
       case 128: gdnrec::recurrent_kernel<QT, 4, 4><<<grid, warps * 32, 0, st>>>(p); break;           \
       default: gdnrec::recurrent_kernel<QT, 8, 4><<<grid, warps * 32, 0, st>>>(p); break;            \
-    }                                                                                                \
-  } else {                                                                                           \
-    switch (Dk) {                                                                                    \
-      case 32: gdnrec::recurrent_kernel<QT, 1, 8><<<grid, warps * 32, 0, st>>>(p); break;            \
-      case 64: gdnrec::recurrent_kernel<QT, 2, 8><<<grid, warps * 32, 0, st>>>(p); break;            \
-      default: gdnrec::recurrent_kernel<QT, 4, 8><<<grid, warps * 32, 0, st>>>(p); break;            \
     }                                                                                                \
   }
   if (qdt == LB2_BF16) {
