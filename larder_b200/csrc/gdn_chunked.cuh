@@ -99,22 +99,25 @@ __device__ __forceinline__ uint8_t* unit_ptr(const Params& p, int b, int h, int 
 constexpr int PREP_TMEM_COLS = 128;
 constexpr int XP = 36;  // row stride of the inversion scratch (conflict-free float4 rows)
 
-// 16 KB regions reused as the steps go, so that three CTAs fit an SM: the Q tile is dead after P_A (its region then
-// holds the inversion scratch, then T diag(beta Gam)); the K tile after W's products (then T diag(beta)).
+// Regions reused as the steps go, so that four CTAs fit an SM (with 128 TMEM columns each, the SM's 512): the Q tile
+// is dead once P_A has committed, and its region then holds A and T (fp32, 1 KB more than the tile), then T diag(beta
+// Gam) once every thread has its row of T in registers; the K tile is dead once W's products have committed, and its
+// region then holds T diag(beta), kept in registers until then.
 struct PrepSmem {
   static constexpr int K0 = 0;                  // K tile: two TMA boxes [64 positions][64 keys]; later T diag(beta)
   static constexpr int V0 = K0 + 2 * C * 128;   // V tile, the same (64 value columns a box)
-  static constexpr int Q0 = V0 + 2 * C * 128;   // Q tile; later the inversion scratch, then T diag(beta Gam)
+  static constexpr int Q0 = V0 + 2 * C * 128;   // Q tile; later A / T, then T diag(beta Gam)
+  static constexpr int AF = Q0;                 // f32 [C][AP]: A, then T
   static constexpr int TBG = Q0;                // hi, lo: [64][64] 16-bit, 8 KB each
   static constexpr int TB = K0;
-  static constexpr int XS = Q0;                 // f32 [32][XP]
-  static constexpr int AF = Q0 + 2 * C * 128;   // f32 [C][AP]: A, then T
-  static constexpr int GAM = AF + C * AP * 4;   // f32 [C] gamma, [C] Gam, [C] beta
+  static constexpr int XS = AF + C * AP * 4;    // f32 [32][XP], the inversion scratch
+  static constexpr int GAM = XS + 32 * XP * 4;  // f32 [C] gamma, [C] Gam, [C] beta
   static constexpr int BAR = GAM + 3 * C * 4;   // 2 mbarriers: loads landed, MMAs done
   static constexpr int SLOT = BAR + 16;         // TMEM base address
   static constexpr int BYTES = SLOT + 16 + 1024;
 };
-static_assert(PrepSmem::AF % 1024 == 0 && PrepSmem::BYTES <= 75 * 1024, "three prep CTAs an SM");
+static_assert(PrepSmem::Q0 % 1024 == 0 && PrepSmem::XS % 16 == 0 && PrepSmem::BYTES + 1024 <= 228 * 1024 / 4,
+              "four prep CTAs an SM");
 
 
 // Writes 64 values of row `row` of a 16-bit K-major operand pair (128-byte swizzle) as hi / lo: eight 16-byte pieces.
@@ -151,7 +154,7 @@ __device__ __forceinline__ void put_row_pair(uint8_t* hi, uint8_t* lo, int row, 
 }
 
 template <typename T>
-__global__ void __launch_bounds__(128) prep_kernel(const __grid_constant__ CUtensorMap qmap,
+__global__ void __launch_bounds__(128, 4) prep_kernel(const __grid_constant__ CUtensorMap qmap,
                                                    const __grid_constant__ CUtensorMap kmap,
                                                    const __grid_constant__ CUtensorMap vmap, const Params p) {
   constexpr uint32_t AB = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
@@ -396,20 +399,25 @@ __global__ void __launch_bounds__(128) prep_kernel(const __grid_constant__ CUten
     *reinterpret_cast<float4*>(Af + (32 + r) * AP + c0 + 4) = make_float4(-t8[4], -t8[5], -t8[6], -t8[7]);
   }
   __syncthreads();
-  // 5. W = T diag(beta Gam) K (lane 0): threads 0-63 write row t of its A operand (a hi / lo pair) where the Q tile
-  // was; K = 64 positions in four steps of 16 rows of the K tile (B MN-major: its two 64-key boxes 8 KB apart)
-  if (tid < C) {
-    float x[C];
+  // 5. W = T diag(beta Gam) K (lane 0): every thread takes a row of T into registers (threads 0-63 row tid scaled by
+  // beta Gam, threads 64-127 row tid - 64 scaled by beta, for U'), then threads 0-63 write their row of W's A operand
+  // (a hi / lo pair) over T; K = 64 positions in four steps of 16 rows of the K tile (B MN-major: its two 64-key boxes
+  // 8 KB apart)
+  float tx[C];
+  {
+    const int r = tid & (C - 1);
+    const bool w_row = tid < C;
 #pragma unroll
     for (int j = 0; j < C; j += 4) {
-      const float4 a = *reinterpret_cast<const float4*>(Af + tid * AP + j);
-      x[j] = a.x * bet[j] * Gam[j];
-      x[j + 1] = a.y * bet[j + 1] * Gam[j + 1];
-      x[j + 2] = a.z * bet[j + 2] * Gam[j + 2];
-      x[j + 3] = a.w * bet[j + 3] * Gam[j + 3];
+      const float4 a = *reinterpret_cast<const float4*>(Af + r * AP + j);
+      tx[j] = a.x * (w_row ? bet[j] * Gam[j] : bet[j]);
+      tx[j + 1] = a.y * (w_row ? bet[j + 1] * Gam[j + 1] : bet[j + 1]);
+      tx[j + 2] = a.z * (w_row ? bet[j + 2] * Gam[j + 2] : bet[j + 2]);
+      tx[j + 3] = a.w * (w_row ? bet[j + 3] * Gam[j + 3] : bet[j + 3]);
     }
-    put_row_pair<T>(sm + PrepSmem::TBG, sm + PrepSmem::TBG + C * 128, tid, x);
   }
+  __syncthreads();  // T is read: its region takes T diag(beta Gam)
+  if (tid < C) put_row_pair<T>(sm + PrepSmem::TBG, sm + PrepSmem::TBG + C * 128, tid, tx);
   fence_proxy_async_shared();
   prefill::tc_fence_before();
   __syncthreads();
@@ -425,21 +433,10 @@ __global__ void __launch_bounds__(128) prep_kernel(const __grid_constant__ CUten
     prefill::umma_commit(&bar[1]);
   }
   ok = __all_sync(0xffffffffu, ok && mbar_wait(&bar[1], 1, 77));
-  // 6. U' = T diag(beta) V (lane 16): threads 64-127 write its A operand where the K tile was (W's products are done
-  // with it), then while those MMAs run every warp takes W out of TMEM (lanes 0-15: row t) as hi / lo pairs
-  if (tid >= C) {
-    const int r = tid - C;
-    float x[C];
-#pragma unroll
-    for (int j = 0; j < C; j += 4) {
-      const float4 a = *reinterpret_cast<const float4*>(Af + r * AP + j);
-      x[j] = a.x * bet[j];
-      x[j + 1] = a.y * bet[j + 1];
-      x[j + 2] = a.z * bet[j + 2];
-      x[j + 3] = a.w * bet[j + 3];
-    }
-    put_row_pair<T>(sm + PrepSmem::TB, sm + PrepSmem::TB + C * 128, r, x);
-  }
+  // 6. U' = T diag(beta) V (lane 16): threads 64-127 write its A operand from their registers where the K tile was
+  // (W's products are done with it), then while those MMAs run every warp takes W out of TMEM (lanes 0-15: row t) as
+  // hi / lo pairs
+  if (tid >= C) put_row_pair<T>(sm + PrepSmem::TB, sm + PrepSmem::TB + C * 128, tid - C, tx);
   fence_proxy_async_shared();
   prefill::tc_fence_before();
   __syncthreads();
