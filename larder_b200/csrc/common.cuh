@@ -188,6 +188,19 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// 1-D bulk copy shared -> global (both addresses 16-byte aligned, bytes % 16 == 0), in the issuing thread's bulk
+// async-group: bulk_commit() closes the group, bulk_wait_read() waits until every committed group has read its shared
+// memory (the source may then be overwritten), bulk_wait_all() until their writes are done. The writes of generic
+// stores to the source must be made visible to the async proxy first (fence_proxy_async_shared() and a barrier).
+__device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_u32(src)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // Tiled TMA load of a 4-D box (no multicast) into shared memory, completing on an mbarrier.
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
                                             uint64_t* bar) {

@@ -176,6 +176,8 @@ __global__ void __launch_bounds__(128, 4) prep_kernel(const __grid_constant__ CU
   uint32_t* slot = reinterpret_cast<uint32_t*>(sm + PrepSmem::SLOT);
   uint8_t* unit = unit_ptr(p, b, h, c);
 
+  // The scan (this grid's programmatic dependent) may launch once every prep CTA has started; it waits for this
+  // grid's completion before reading anything.
   // 1. the K, Q, V tiles by TMA (rows past T land as zeros) while the gates are formed; TMEM
   if (tid == 0) {
     mbar_init(&bar[0], 1);
@@ -451,21 +453,43 @@ __global__ void __launch_bounds__(128, 4) prep_kernel(const __grid_constant__ CU
     }
     prefill::umma_commit(&bar[1]);
   }
+  // W and U' leave through shared memory by bulk copies: written there by rows, they reach the workspace as whole
+  // lines (row-by-row 16-byte global stores touch sixteen lines a warp instruction and held the load / store unit).
+  // W, a half (64 key columns, hi and lo: 16 KB) at a time, is staged where T diag(beta Gam) was (free once W's
+  // products have committed).
   const int t = 16 * warp + (lane & 15);
+  uint8_t* wst = sm + PrepSmem::TBG;
   if (ok) prefill::tc_fence_after();
 #pragma unroll 1
-  for (int half = 0; half < 2; ++half) {  // W, 64 key columns at a time
+  for (int half = 0; half < 2; ++half) {
     float x[C];
     if (ok) {
       prefill::tmem_ld32(tmem + lq + half * C, x);
       prefill::tmem_ld32(tmem + lq + half * C + 32, x + 32);
       prefill::tmem_wait_ld();
     }
-    if (lane < 16 && ok) put_row_pair<T>(unit + WS_WHI + half * C * 128, unit + WS_WLO + half * C * 128, t, x);
+    if (half) {  // the first half's copies have read the stage
+      if (tid == 0) bulk_wait_read();
+      __syncthreads();
+    }
+    if (lane < 16 && ok) put_row_pair<T>(wst, wst + C * 128, t, x);
+    fence_proxy_async_shared();
+    __syncthreads();
+    if (tid == 0 && ok) {
+      bulk_s2g(unit + WS_WHI + half * C * 128, wst, C * 128);
+      bulk_s2g(unit + WS_WLO + half * C * 128, wst + C * 128, C * 128);
+      bulk_commit();
+    }
   }
-  // 7. U' (lanes 16-31: row t) in fp32 slices of 32 value columns
+  // 7. U' (lanes 16-31: row t) in fp32 slices of 32 value columns, staged as the workspace holds them (all four slices,
+  // 36 KB from the K tile's region on: free once U''s products have committed, and past W's stage once its copies
+  // have read it)
   ok = __all_sync(0xffffffffu, ok && mbar_wait(&bar[1], 0, 78));
   if (ok) prefill::tc_fence_after();
+  uint8_t* ust = sm + PrepSmem::K0;
+  static_assert(PrepSmem::K0 + (DV / DVB) * USLICE <= PrepSmem::XS, "U' stage inside the tile regions");
+  if (tid == 0) bulk_wait_read();
+  __syncthreads();
 #pragma unroll 1
   for (int half = 0; half < 2; ++half) {
     float x[C];
@@ -477,12 +501,18 @@ __global__ void __launch_bounds__(128, 4) prep_kernel(const __grid_constant__ CU
     if (lane >= 16 && ok)
 #pragma unroll
       for (int s2 = 0; s2 < 2; ++s2) {  // value columns 64 half + 32 s2 ..: slice 2 half + s2
-        float4* g = reinterpret_cast<float4*>(unit + WS_U + (2 * half + s2) * USLICE + t * UP * 4);
+        float4* g = reinterpret_cast<float4*>(ust + (2 * half + s2) * USLICE + t * UP * 4);
 #pragma unroll
         for (int q4 = 0; q4 < DVB / 4; ++q4)
           g[q4] = make_float4(x[32 * s2 + 4 * q4], x[32 * s2 + 4 * q4 + 1], x[32 * s2 + 4 * q4 + 2],
                               x[32 * s2 + 4 * q4 + 3]);
       }
+  }
+  fence_proxy_async_shared();
+  __syncthreads();
+  if (tid == 0 && ok) {
+    bulk_s2g(unit + WS_U, ust, (DV / DVB) * USLICE);
+    bulk_commit();
   }
   // 8. gamma and Gam for the scan
   if (tid < C) {
@@ -490,6 +520,7 @@ __global__ void __launch_bounds__(128, 4) prep_kernel(const __grid_constant__ CU
     gg[tid] = gam[tid];
     gg[C + tid] = Gam[tid];
   }
+  if (tid == 0) bulk_wait_all();  // the bulk copies have read their stages and written the workspace
   prefill::tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -640,6 +671,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) scan_kernel(const __grid_consta
   __syncthreads();
   prefill::tc_fence_after();
   const uint32_t tmem = *slot;
+  // Launched as a programmatic dependent of prep: the set-up above touched only this CTA's shared memory and TMEM;
+  // every global read below waits for prep's grid to complete.
 
   if (warp < TC_EPI) {
     // ------------------------------------------------------------------------------------ epilogue warps
