@@ -614,13 +614,14 @@ int lb2_attn_decode_host(const void* q_host, const void* k, const int64_t* k_st,
   void* q_dev = ws + j * stage;
   void* o_dev = ws + (2 + j) * stage;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // q in on the copy stream, once the decode two calls back has read this slot
-  LB2_CUDA(cudaStreamWaitEvent(s->h2d, s->dec_done[j], 0));
+  // q in on the copy stream, once this slot's o of two calls back is out (which followed that call's decode, so its
+  // q in this slot has been read too)
+  LB2_CUDA(cudaStreamWaitEvent(s->h2d, s->d2h_done[j], 0));
   LB2_CUDA(cudaMemcpyAsync(q_dev, q_host, bytes, cudaMemcpyHostToDevice, s->h2d));
   LB2_CUDA(cudaEventRecord(s->h2d_done[j], s->h2d));
-  // the decode on the caller's stream, once q is in and this slot's o of two calls back is out
+  // the decode on the caller's stream once q is in: one wait, which also orders it after the slot's o of two calls
+  // back has left (each wait on another stream's event costs the caller's stream device time)
   LB2_CUDA(cudaStreamWaitEvent(st, s->h2d_done[j], 0));
-  LB2_CUDA(cudaStreamWaitEvent(st, s->d2h_done[j], 0));
   const int64_t qs[3] = {int64_t(Hq) * T * D, int64_t(T) * D, D};
   if (const int rc = lb2_attn_decode(q_dev, qs, k, k_st, v, v_st, o_dev, qs, kv_len, B, Hq, Hkv, T, N, D, dtype, scale,
                                      causal, split, ws + 4 * stage, workspace_bytes - 4 * stage, stream))
