@@ -210,7 +210,20 @@ __global__ void __launch_bounds__(WARPS * 32) qk_norm_rope_kernel(const QkParams
 // by bit moves. The arithmetic and its roundings are those of qk_norm_rope_kernel.
 constexpr int QROWS = 4;
 
-template <int D, int MODE>
+// A table value as fp32 (cos / sin come as fp32, bf16 or f16).
+__device__ __forceinline__ float tab_f(float x) { return x; }
+__device__ __forceinline__ float tab_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ float tab_f(__half x) { return __half2float(x); }
+
+// The bf16 pair of two values, packed (low half a), and its two values back as fp32.
+__device__ __forceinline__ uint32_t bf2w(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ float lo_f(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float hi_f(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+template <int D, int MODE, typename CT>
 __global__ void __launch_bounds__(WARPS * 32) qk_rope_pair_kernel(const QkParams p) {
   constexpr int NP = D / 64;  // column pairs a lane
   __shared__ __align__(16) float2 trig[2][QROWS][64];  // (cos, sin) pairs of the block's rows, R / 2 <= 64 pairs
@@ -222,7 +235,8 @@ __global__ void __launch_bounds__(WARPS * 32) qk_rope_pair_kernel(const QkParams
   const int nrows = p.B * p.S;  // < 2^31: checked by the launcher
   const int row0 = blockIdx.x * QROWS;
   const int64_t rstride = isq ? int64_t(p.NQ) * 2 * D : int64_t(p.NK) * D;
-  const __nv_bfloat16* src = (isq ? p.qg + int64_t(h) * 2 * D : p.kr + int64_t(h) * D) + 2 * lane;
+  const __nv_bfloat16* src =
+      (isq ? p.qg + int64_t(h) * 2 * D : p.kr + int64_t(h) * D) + int64_t(row0) * rstride + 2 * lane;
   uint32_t raw[QROWS][NP], wraw[NP];
   if (live) {
 #pragma unroll
@@ -230,24 +244,31 @@ __global__ void __launch_bounds__(WARPS * 32) qk_rope_pair_kernel(const QkParams
       const bool in = row0 + r < nrows;
 #pragma unroll
       for (int k = 0; k < NP; ++k)
-        raw[r][k] = in ? *reinterpret_cast<const uint32_t*>(src + int64_t(row0 + r) * rstride + 64 * k) : 0u;
+        raw[r][k] = in ? *reinterpret_cast<const uint32_t*>(src + r * rstride + 64 * k) : 0u;
     }
     const __nv_bfloat16* w = (isq ? p.qw : p.kw) + 2 * lane;
 #pragma unroll
     for (int k = 0; k < NP; ++k) wraw[k] = *reinterpret_cast<const uint32_t*>(w + 64 * k);
   }
+  // the block's first row as (sequence, position); later rows step the position (rows past the end take the
+  // positions that follow, inside the table)
+  const int b0 = row0 / p.S, s0 = row0 - b0 * p.S;
   const int R = p.R;
   if (MODE != 0) {
+    const int q = threadIdx.x;  // q < R / 2: cos pairs, else sin pairs (R <= 128: one per thread)
+    if (q < R) {
+      const int w = 2 * q >= R, qq = q - w * (R >> 1);
+      const CT* tab = static_cast<const CT*>(w ? p.sn : p.cs) + 2 * qq;
+      const bool neg = w && 4 * qq < R;
+      int s = s0;
 #pragma unroll
-    for (int r = 0; r < QROWS; ++r) {
-      const int row = row0 + r < nrows ? row0 + r : row0;
-      const int64_t c0 = int64_t(row % p.S) * R;
-      for (int q = threadIdx.x; q < R; q += WARPS * 32) {  // q < R / 2: cos pairs, else sin pairs
-        const int w = 2 * q >= R, qq = q - w * (R >> 1);
-        float a = ld_any(w ? p.sn : p.cs, c0 + 2 * qq, p.csdt), b = ld_any(w ? p.sn : p.cs, c0 + 2 * qq + 1, p.csdt);
+      for (int r = 0; r < QROWS; ++r) {
+        const CT* e = tab + int64_t(s) * R;
+        float a = tab_f(e[0]), b = tab_f(e[1]);
         bf2(a, b);
-        if (w && 4 * qq < R) a = -a, b = -b;
+        if (neg) a = -a, b = -b;
         trig[w][r][qq] = make_float2(a, b);
+        if (++s == p.S) s = 0;
       }
     }
   }
@@ -255,61 +276,62 @@ __global__ void __launch_bounds__(WARPS * 32) qk_rope_pair_kernel(const QkParams
   if (!live) return;
   float wv[2 * NP];
 #pragma unroll
-  for (int k = 0; k < NP; ++k) wv[2 * k] = __uint_as_float(wraw[k] << 16), wv[2 * k + 1] = __uint_as_float(wraw[k] & 0xffff0000u);
-  int b = row0 / p.S, s = row0 - b * p.S;
+  for (int k = 0; k < NP; ++k) wv[2 * k] = lo_f(wraw[k]), wv[2 * k + 1] = hi_f(wraw[k]);
+  const int NH = isq ? p.NQ : p.NK;
+  __nv_bfloat16* const obase = (isq ? p.q : p.k) + 2 * lane;
+  int b = b0, s = s0;
+  int64_t orow = (int64_t(b) * NH + h) * p.S + s;  // output row of (b, h, s)
 #pragma unroll
-  for (int r = 0; r < QROWS; ++r, ++s) {
-    if (s == p.S) s = 0, ++b;
+  for (int r = 0; r < QROWS; ++r) {
     float x[2 * NP];
 #pragma unroll
-    for (int k = 0; k < NP; ++k)
-      x[2 * k] = __uint_as_float(raw[r][k] << 16), x[2 * k + 1] = __uint_as_float(raw[r][k] & 0xffff0000u);
+    for (int k = 0; k < NP; ++k) x[2 * k] = lo_f(raw[r][k]), x[2 * k + 1] = hi_f(raw[r][k]);
     float acc = 0.f;
 #pragma unroll
     for (int i = 0; i < 2 * NP; ++i) acc = fmaf(x[i], x[i], acc);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     const float inv = rsqrtf(acc / float(D) + p.eps);
+    // bf16(bf16(x inv) w), packed: the stored words of the pairs RoPE leaves alone
+    uint32_t ow[NP];
 #pragma unroll
-    for (int i = 0; i < 2 * NP; i += 2) {
-      float u = x[i] * inv, v = x[i + 1] * inv;
+    for (int k = 0; k < NP; ++k) {
+      float u = x[2 * k] * inv, v = x[2 * k + 1] * inv;
       bf2(u, v);
-      u *= wv[i], v *= wv[i + 1];
-      bf2(u, v);
-      x[i] = u, x[i + 1] = v;
+      ow[k] = bf2w(u * wv[2 * k], v * wv[2 * k + 1]);
     }
     if (MODE == 1) {  // pair 0 of lanes 2 lane < R: partner in lane ^ (R / 4)
-      const float p0 = __shfl_xor_sync(0xffffffffu, x[0], R >> 2), p1 = __shfl_xor_sync(0xffffffffu, x[1], R >> 2);
+      const float x0 = lo_f(ow[0]), x1 = hi_f(ow[0]);
+      const float p0 = __shfl_xor_sync(0xffffffffu, x0, R >> 2), p1 = __shfl_xor_sync(0xffffffffu, x1, R >> 2);
       if (2 * lane < R) {
         const float2 c = trig[0][r][lane], sg = trig[1][r][lane];
-        float a0 = x[0] * c.x, a1 = x[1] * c.y, b0 = p0 * sg.x, b1 = p1 * sg.y;
+        float a0 = x0 * c.x, a1 = x1 * c.y, q0 = p0 * sg.x, q1 = p1 * sg.y;
         bf2(a0, a1);
-        bf2(b0, b1);
-        a0 += b0, a1 += b1;
-        bf2(a0, a1);
-        x[0] = a0, x[1] = a1;
+        bf2(q0, q1);
+        ow[0] = bf2w(a0 + q0, a1 + q1);
       }
     } else if (MODE == 2) {  // pairs 0 and 1 (R = 128): each the other's partner
-      float y[4];
+      const float xs[4] = {lo_f(ow[0]), hi_f(ow[0]), lo_f(ow[1]), hi_f(ow[1])};
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
         const float2 c = trig[0][r][32 * k + lane], sg = trig[1][r][32 * k + lane];
-        float a0 = x[2 * k] * c.x, a1 = x[2 * k + 1] * c.y, b0 = x[2 * (1 - k)] * sg.x, b1 = x[2 * (1 - k) + 1] * sg.y;
+        float a0 = xs[2 * k] * c.x, a1 = xs[2 * k + 1] * c.y, q0 = xs[2 * (1 - k)] * sg.x,
+              q1 = xs[2 * (1 - k) + 1] * sg.y;
         bf2(a0, a1);
-        bf2(b0, b1);
-        a0 += b0, a1 += b1;
-        bf2(a0, a1);
-        y[2 * k] = a0, y[2 * k + 1] = a1;
+        bf2(q0, q1);
+        ow[k] = bf2w(a0 + q0, a1 + q1);
       }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) x[i] = y[i];
     }
     if (row0 + r < nrows) {
-      __nv_bfloat16* dst = (isq ? p.q + ((int64_t(b) * p.NQ + h) * p.S + s) * D
-                                 : p.k + ((int64_t(b) * p.NK + h) * p.S + s) * D) + 2 * lane;
+      __nv_bfloat16* dst = obase + orow * D;
 #pragma unroll
-      for (int k = 0; k < NP; ++k)
-        *reinterpret_cast<uint32_t*>(dst + 64 * k) = __byte_perm(__float_as_uint(x[2 * k]), __float_as_uint(x[2 * k + 1]), 0x7632);
+      for (int k = 0; k < NP; ++k) *reinterpret_cast<uint32_t*>(dst + 64 * k) = ow[k];
+    }
+    if (++s == p.S) {
+      s = 0, ++b;
+      orow = (int64_t(b) * NH + h) * p.S;
+    } else {
+      ++orow;
     }
   }
 }

@@ -1299,13 +1299,21 @@ int lb2_attn_qk_norm_rope(const void* qg, const void* kr, const void* q_norm_w, 
     const dim3 g1(unsigned((int64_t(B) * S + aglue::QROWS - 1) / aglue::QROWS),
                   unsigned((NQ + NK + aglue::WARPS - 1) / aglue::WARPS));
     LB2_CHECK_ARG(g1.y < 65536, "qk_norm_rope: too many heads");
+#define LB2_QK_PAIR_T(DD, MM)                                                                    \
+  if (cs_dtype == LB2_F32)                                                                       \
+    aglue::qk_rope_pair_kernel<DD, MM, float><<<g1, aglue::WARPS * 32, 0, st>>>(p);              \
+  else if (cs_dtype == LB2_BF16)                                                                 \
+    aglue::qk_rope_pair_kernel<DD, MM, __nv_bfloat16><<<g1, aglue::WARPS * 32, 0, st>>>(p);      \
+  else                                                                                           \
+    aglue::qk_rope_pair_kernel<DD, MM, __half><<<g1, aglue::WARPS * 32, 0, st>>>(p)
 #define LB2_QK_PAIR(DD)                                                               \
   if (mode == 0)                                                                      \
-    aglue::qk_rope_pair_kernel<DD, 0><<<g1, aglue::WARPS * 32, 0, st>>>(p);           \
-  else if (mode == 1)                                                                 \
-    aglue::qk_rope_pair_kernel<DD, 1><<<g1, aglue::WARPS * 32, 0, st>>>(p);           \
-  else                                                                                \
-    aglue::qk_rope_pair_kernel<DD, 2><<<g1, aglue::WARPS * 32, 0, st>>>(p)
+    aglue::qk_rope_pair_kernel<DD, 0, float><<<g1, aglue::WARPS * 32, 0, st>>>(p);    \
+  else if (mode == 1) {                                                               \
+    LB2_QK_PAIR_T(DD, 1);                                                             \
+  } else {                                                                            \
+    LB2_QK_PAIR_T(DD, 2);                                                             \
+  }
     if (D == 128) {
       LB2_QK_PAIR(128);
     } else if (D == 256) {
@@ -1314,6 +1322,7 @@ int lb2_attn_qk_norm_rope(const void* qg, const void* kr, const void* q_norm_w, 
       LB2_QK_PAIR(512);
     }
 #undef LB2_QK_PAIR
+#undef LB2_QK_PAIR_T
     LB2_CUDA(cudaGetLastError());
     return LB2_OK;
   }
