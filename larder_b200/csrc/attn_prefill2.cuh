@@ -102,22 +102,6 @@ __device__ __forceinline__ bool mbar_test_wait_cluster(uint64_t* bar, uint32_t p
   return ok != 0;
 }
 
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int where) {
-  uint64_t t0 = 0;
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_test_wait_cluster(bar, parity)) return true;
-    if ((i & 1023) == 0) {
-      const uint64_t now = globaltimer_ns();
-      if (t0 == 0) {
-        t0 = now;
-      } else if (now - t0 > kWaitNs) {
-        report_timeout(where);
-        return false;
-      }
-    }
-  }
-}
-
 // 4-D tiled TMA load into this CTA's shared memory, completing on the leader CTA's copy of the mbarrier (the 2-CTA
 // form of the copy, whose barrier may sit in either CTA of the pair).
 __device__ __forceinline__ void tma_load_4d_pair(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
@@ -161,12 +145,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
         "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
-               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
-               : "memory");
 }
 
 // Number of BN-key tiles the pair of row tiles mt2 (rows [256 mt2, 256 mt2 + 256)) reads.

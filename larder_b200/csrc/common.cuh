@@ -215,8 +215,6 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
 
-__device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31; }
-
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
   asm volatile(

@@ -32,7 +32,6 @@ constexpr int C = 64;
 constexpr int DK = 128;
 constexpr int DV = 128;
 constexpr int DVB = 32;   // value rows a scan CTA owns
-constexpr int KP = 136;   // bf16 row stride of prep's K / Q tiles (conflict-free ldmatrix and scalar reads)
 constexpr int AP = 68;    // fp32 row stride of prep's A / T tiles
 constexpr int UP = 36;    // fp32 row stride of the U' slices (32 value columns)
 // Workspace of one (batch, head, chunk), in bytes, laid out as the scan's shared-memory operands so that a chunk
@@ -50,11 +49,6 @@ constexpr int WS_U = WS_G + 2 * C * 4;
 constexpr int USLICE = C * UP * 4;
 constexpr int UNIT_BYTES = WS_U + (DV / DVB) * USLICE;
 static_assert(WS_G % 16 == 0 && WS_U % 16 == 0 && UNIT_BYTES % 16 == 0, "16-byte aligned workspace pieces");
-
-// Byte offset of 16-bit element (row, col) of a 64-column block in the 128-byte swizzle (col < 64).
-__host__ __device__ __forceinline__ int sw128(int row, int col) {
-  return row * 128 + ((((col >> 3) ^ row) & 7) << 4) + ((col & 7) << 1);
-}
 
 struct Params {
   const void* q;
