@@ -172,7 +172,8 @@ __global__ void __launch_bounds__(128, 4) prep_kernel(const __grid_constant__ CU
 
   // The scan (this grid's programmatic dependent) may launch once every prep CTA has started; it waits for this
   // grid's completion before reading anything.
-  // 1. the K, Q, V tiles by TMA (rows past T land as zeros) while the gates are formed; TMEM
+  // 1. the K and Q tiles by TMA (rows past T land as zeros) while the gates are formed; TMEM. (The V tile, read only
+  // by U''s products, comes after M has left through its region.)
   if (tid == 0) {
     mbar_init(&bar[0], 1);
     mbar_init(&bar[1], 1);
@@ -180,12 +181,11 @@ __global__ void __launch_bounds__(128, 4) prep_kernel(const __grid_constant__ CU
     prefetch_tensormap(&qmap);
     prefetch_tensormap(&kmap);
     prefetch_tensormap(&vmap);
-    mbar_arrive_expect_tx(&bar[0], 3 * 2 * C * 128);
+    mbar_arrive_expect_tx(&bar[0], 2 * 2 * C * 128);
 #pragma unroll
     for (int db = 0; db < 2; ++db) {
       tma_load_4d(sm + PrepSmem::K0 + db * C * 128, &kmap, db * 64, t0, hk, b, &bar[0]);
       tma_load_4d(sm + PrepSmem::Q0 + db * C * 128, &qmap, db * 64, t0, hk, b, &bar[0]);
-      tma_load_4d(sm + PrepSmem::V0 + db * C * 128, &vmap, db * 64, t0, h, b, &bar[0]);
     }
   }
   if (warp == 0) {
@@ -240,7 +240,8 @@ __global__ void __launch_bounds__(128, 4) prep_kernel(const __grid_constant__ CU
     prefill::umma_commit(&bar[1]);
   }
   ok = __all_sync(0xffffffffu, ok && mbar_wait(&bar[1], 0, 76));
-  // 3. A (lanes 0-15: row t of K K^T) into shared memory; M (lanes 16-31: row t of Q K^T) to the workspace
+  // 3. A (lanes 0-15: row t of K K^T) into shared memory; M (lanes 16-31: row t of Q K^T) staged in the V tile's
+  // region, then to the workspace by one bulk copy, after which the V tile is loaded there
   {
     const int t = 16 * warp + (lane & 15);
     float x[C];
@@ -281,11 +282,21 @@ __global__ void __launch_bounds__(128, 4) prep_kernel(const __grid_constant__ CU
         *reinterpret_cast<float4*>(Af + t * AP + j) = a;
       }
     } else {  // M: lower with the diagonal (the decay is zero above it)
-      put_row_pair<T>(unit + WS_MHI, unit + WS_MLO, t, x);
+      put_row_pair<T>(sm + PrepSmem::V0, sm + PrepSmem::V0 + C * 128, t, x);
     }
   }
+  fence_proxy_async_shared();
   prefill::tc_fence_before();
   __syncthreads();
+  if (tid == 0 && ok) {  // (M_hi, M_lo: 16 KB, adjacent in the workspace as in the stage)
+    bulk_s2g(unit + WS_MHI, sm + PrepSmem::V0, 2 * C * 128);
+    bulk_commit();
+    bulk_wait_read();
+    mbar_arrive_expect_tx(&bar[0], 2 * C * 128);
+#pragma unroll
+    for (int db = 0; db < 2; ++db)
+      tma_load_4d(sm + PrepSmem::V0 + db * C * 128, &vmap, db * 64, t0, h, b, &bar[0]);
+  }
 
 
   // 4. T = (I + A)^{-1}, in place over A's lower triangle (diagonal 1, upper 0), fp32 on the CUDA cores
@@ -433,6 +444,7 @@ __global__ void __launch_bounds__(128, 4) prep_kernel(const __grid_constant__ CU
   // (W's products are done with it), then while those MMAs run every warp takes W out of TMEM (lanes 0-15: row t) as
   // hi / lo pairs
   if (tid >= C) put_row_pair<T>(sm + PrepSmem::TB, sm + PrepSmem::TB + C * 128, tid - C, tx);
+  ok = __all_sync(0xffffffffu, ok && mbar_wait(&bar[0], 1, 79));  // the V tile has landed (long since)
   fence_proxy_async_shared();
   prefill::tc_fence_before();
   __syncthreads();

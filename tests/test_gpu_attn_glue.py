@@ -85,16 +85,21 @@ def inputs(B, S, NQ, NK, D, R, seed, offset=0):
     (1, 6, 4, 2, 128, 32, oracle.F32),      # a quarter of 128 rotated (the partner eight lanes away)
     (1, 3, 4, 2, 512, 128, oracle.BF16),    # 128 of 512 rotated (the partner in the lane's other column pair)
     (1, 4, 8, 2, 256, 24, oracle.F32),      # a width that is not a multiple of 16: RoPE through shared memory
+    (1, 7, 8, 2, 256, 64, oracle.F16),      # f16 tables
+    (1, 3, 4, 2, 128, 24, oracle.F16),      # f16 tables through shared memory
 ])
 def test_qk_norm_rope_matches_oracle(B, S, NQ, NK, D, R, cs_dt):
     qg, kr, qw, kw, cs, sn = inputs(B, S, NQ, NK, D, R, seed=B * 100 + S, offset=4093)
-    rq, rk = oracle.qk_norm_rope(qg, kr, qw, kw, 1e-6, oracle.bf16_to_f32(oracle.f32_to_bf16(cs))
-                                 if cs_dt == oracle.BF16 else cs,
-                                 oracle.bf16_to_f32(oracle.f32_to_bf16(sn)) if cs_dt == oracle.BF16 else sn, NQ, NK)
+    # the tables as the kernel reads them (each use rounds a table value to bf16, in the oracle too)
+    if cs_dt == oracle.BF16:
+        cs, sn = oracle.bf16_to_f32(oracle.f32_to_bf16(cs)), oracle.bf16_to_f32(oracle.f32_to_bf16(sn))
+    elif cs_dt == oracle.F16:
+        cs, sn = cs.astype(np.float16).astype(np.float32), sn.astype(np.float16).astype(np.float32)
+    rq, rk = oracle.qk_norm_rope(qg, kr, qw, kw, 1e-6, cs, sn, NQ, NK)
     nq, nk = oracle.qk_norm_rope(qg, kr, qw, kw, 1e-6, np.zeros((S, 0), np.float32), np.zeros((S, 0), np.float32),
                                  NQ, NK)
     cb, sb = oracle.bf16_to_f32(oracle.f32_to_bf16(cs)), oracle.bf16_to_f32(oracle.f32_to_bf16(sn))
-    dt = torch.bfloat16 if cs_dt == oracle.BF16 else torch.float32
+    dt = {oracle.BF16: torch.bfloat16, oracle.F16: torch.float16}.get(cs_dt, torch.float32)
     q, k = layer_glue.qk_norm_rope(to_torch(qg, oracle.BF16), to_torch(kr, oracle.BF16), to_torch(qw, oracle.BF16),
                                    to_torch(kw, oracle.BF16), 1e-6, torch.from_numpy(cs).to(dt).cuda(),
                                    torch.from_numpy(sn).to(dt).cuda(), NQ, NK)
