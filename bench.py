@@ -403,6 +403,9 @@ def bench_prefill(torch, ops, dev, rank, world, args, stream, pk, pk_kind, barri
             "flop_per_step": flop, "gpu_launches_per_step": 1,
             "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": round(tf / pk["bf16_tflops"], 4), "traffic": None, "peak_kind": pk_kind,
+                         # timed after the warm window, at the power cap: against cuBLAS held at the cap too
+                         "frac_of_sustained": round(tf / pk["bf16_tflops_sustained"], 4),
+                         "sustained_peak": pk["bf16_tflops_sustained"],
                          "kernel": "lb2::prefill2::fmha2_kernel<bf16,256>"},
             "check": prefill_check, "clocks": clk.summary()}
 
@@ -555,6 +558,9 @@ def bench_sharded(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, 
                                      "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                                      "frac": round(flop / (ms_p * 1e-3) / 1e12 / pk["bf16_tflops"], 4),
                                      "peak_kind": "burst (one launch timed alone)",
+                                     "frac_of_sustained": round(flop / (ms_p * 1e-3) / 1e12 /
+                                                                pk["bf16_tflops_sustained"], 4),
+                                     "sustained_peak": pk["bf16_tflops_sustained"],
                                      "kernel": "lb2::prefill2::fmha2_kernel<bf16,128>"}},
             "decode": {"value": round(world * kv_bytes / (ms_d * 1e-3) / 1e9, 1), "unit": "GB/s",
                        "ms_per_step": round(ms_d, 5), "context": n_local * world,
