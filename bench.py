@@ -824,7 +824,8 @@ def bench_gdn(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_
                             "frac": round(t_roof * 1e3 / ms_p, 4), "unit": "time",
                             "kernel": "lb2::gdnchunk::{prep_kernel, scan_kernel}"}, "check": gdn_check}
     del graph
-    res = {"prefill": prefill,
+    row_glue = bench_gdn_row_glue(torch, ops, dev, g, args, stream, pk, barrier_sync, max_over_ranks, Hk, Hv, D)
+    res = {"prefill": prefill, "decode_row_glue": row_glue,
            "decode": {"value": round(world * gbs, 1), "unit": "GB/s", "ms_per_step": round(per, 5),
                       "workload": "configs[3] decode step: B=16, Hk 16, Hv 32, 128x128 fp32 state read+written",
                       "launch": "the K steps as one CUDA graph, replayed once",
@@ -833,6 +834,55 @@ def bench_gdn(torch, ops, dev, rank, world, args, stream, pk, barrier_sync, max_
                                    "kernel": "lb2::gdnrec::recurrent_kernel<bf16,4,4>"},
                       "clocks": clk.summary()}}
     return res
+
+
+def bench_gdn_row_glue(torch, ops, dev, g, args, stream, pk, barrier_sync, max_over_ranks, Hk, Hv, D):
+    """One GDN decode token of one sequence as the reference's install_glue routes it (gdn_cuda.py:271-315): the fused
+    row glue and recurrence (step_glue) from the conv output, then the gated RMSNorm (norm_gate), at configs[3]'s
+    head shapes. The K steps are one CUDA graph over `copies` state copies (2 MB each, 128 MB together) so that
+    each step reads its state from HBM; a step is latency-bound, so the line gives microseconds a token beside the
+    state bytes' rate."""
+    from larder_b200 import gdn_cuda
+
+    copies = 64
+    cd = 2 * Hk * D + Hv * D
+    conv = torch.randn(1, 1, cd, generator=g, device=dev).to(torch.bfloat16)
+    a = torch.randn(1, 1, Hv, generator=g, device=dev).to(torch.bfloat16)
+    b = torch.randn(1, 1, Hv, generator=g, device=dev).to(torch.bfloat16)
+    A_log = torch.log(torch.rand(Hv, generator=g, device=dev) * 15 + 1)
+    dt_bias = torch.rand(Hv, generator=g, device=dev)
+    z = torch.randn(1, 1, Hv, D, generator=g, device=dev).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(D, generator=g, device=dev)).to(torch.bfloat16)
+    states = [0.05 * torch.randn(1, Hv, D, D, generator=g, device=dev) for _ in range(copies)]
+
+    def tok(i):
+        y, _ = gdn_cuda.step_glue(conv, a, b, A_log, dt_bias, states[i % copies], Hk, D, Hv, D)
+        gdn_cuda.norm_gate(y, z, w, 1e-6)
+
+    for i in range(args.warmup):
+        tok(i)
+    barrier_sync()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(args.steps):
+            tok(i)
+
+    def step(_):
+        graph.replay()
+
+    step(0)
+    barrier_sync()
+    per = max_over_ranks(cuda_time(torch, step, 1, stream)) / args.steps
+    del graph
+    state_bytes = Hv * D * D * 4 * 2
+    gbs = state_bytes / (per * 1e-3) / 1e9
+    return {"us_per_token": round(per * 1e3, 2), "state_gbs": round(gbs, 1), "bytes_per_step": state_bytes,
+            "gpu_launches_per_step": 2,
+            "workload": "one decode token, B=1, Hk 16, Hv 32, 128x128: gdn_cuda.step_glue + norm_gate",
+            "launch": f"the K steps as one CUDA graph, replayed once; {copies} state copies (past L2)",
+            "roofline": {"bound": "latency", "hbm_floor_us": round(state_bytes / (pk["hbm_gbs"] * 1e9) * 1e6, 2),
+                         "frac_of_hbm": round(gbs / pk["hbm_gbs"], 4),
+                         "kernel": "lb2::gdnrec::glue_step_kernel + lb2::glue::norm_gate_kernel"}}
 
 
 # ------------------------------------------------------------------------------------------------ CPU arms
