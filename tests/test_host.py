@@ -72,6 +72,27 @@ def test_wrapper_refuses_what_it_cannot_serve(spy):
     assert spy.calls == []
 
 
+def test_ops_refuse_host_tensors():
+    """No op has a CPU path: handed host tensors, each raises before it touches the library or allocates."""
+    from larder_b200 import layer_glue
+
+    bf = torch.bfloat16
+    q, kv = torch.zeros(1, 8, 4, 128, dtype=bf), torch.zeros(1, 2, 16, 128, dtype=bf)
+    g, beta = torch.ones(1, 4, 8), torch.ones(1, 4, 8, dtype=bf)
+    gq, gv = torch.zeros(1, 4, 4, 128, dtype=bf), torch.zeros(1, 4, 8, 128, dtype=bf)
+    calls = [
+        lambda: ops.attn_prefill(q, kv, kv, 0.1, "causal"),
+        lambda: ops.attn_decode(q[:, :, :1], kv, kv, 0.1),
+        lambda: ops.gdn_recurrent(gq, gq, gv, g, beta),
+        lambda: ops.gdn_chunked(gq, gq, gv, g, beta),
+        lambda: ops.kv_gather_picks(kv[0], kv[0], torch.zeros(2, dtype=torch.int32), 4),
+        lambda: layer_glue.out_gate(torch.zeros(1, 2, 256, dtype=bf), torch.zeros(1, 2, 512, dtype=bf), 2),
+    ]
+    for call in calls:
+        with pytest.raises(ValueError, match="CUDA"):
+            call()
+
+
 def test_chunked_runs_all_rows_in_one_launch(spy):
     """The fused kernel keeps no score buffer, so the wide cut's row chunks become one launch over all T rows and
     all N keys (bottom-right causal), whatever `rows`, `min_rows` and `floor` say."""
