@@ -1,5 +1,6 @@
 """CPU checks of the drop-in boundary: the C-ABI library loads, exports every symbol include/larder_b200.h declares,
 and the Python layer refuses CPU tensors and bad shapes loudly (no CPU fallback exists). No compute call runs."""
+import ctypes
 import os
 import re
 
@@ -24,6 +25,52 @@ def test_library_exports_every_declared_symbol():
     for n in names:
         assert hasattr(L, n), f"{n} declared in include/larder_b200.h but not exported"
     assert set(names) == set(_lib.SIGNATURES), "ctypes signatures out of step with the header"
+
+
+def declarations():
+    """{name: (return type, [parameter types])} of every entry point in include/larder_b200.h."""
+    text = open(os.path.join(ROOT, "include", "larder_b200.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    text = re.sub(r"//[^\n]*", "", text)
+    text = re.sub(r"^\s*#[^\n]*", "", text, flags=re.M)  # preprocessor lines
+    out = {}
+    for ret, name, params in re.findall(r"([A-Za-z_][\w\s\*]*?)\s*\b(lb2_\w+)\s*\(([^)]*)\)\s*;", text):
+        types = []
+        for prm in [x.strip() for x in params.split(",") if x.strip() and x.strip() != "void"]:
+            prm = re.sub(r"\s*\*\s*", "* ", prm)
+            types.append(" ".join(prm.replace("*", " * ").split()[:-1]).replace(" *", "*"))
+        out[name] = (" ".join(ret.split()), types)
+    return out
+
+
+def ctype_of(c_type):
+    """The ctypes type a C parameter or return type binds as."""
+    t = c_type.replace("const ", "").strip()
+    if t.count("*") == 2:
+        return ctypes.POINTER(ctypes.c_void_p)
+    if t == "int64_t*":
+        return _lib._i64p
+    if t == "char*":
+        return ctypes.c_char_p
+    if t.endswith("*"):
+        return ctypes.c_void_p
+    return {"int": ctypes.c_int, "float": ctypes.c_float, "size_t": ctypes.c_size_t, "int64_t": ctypes.c_int64,
+            "uint32_t": ctypes.c_uint32}[t]
+
+
+def test_ctypes_signatures_match_the_header():
+    """Each binding's argument list is the declaration's, type by type: a wrong count or width would pass every CPU
+    check and corrupt the call's arguments on a GPU."""
+    decl = declarations()
+    assert set(decl) == set(declared_symbols())
+    assert set(_lib.SIGNATURES) == set(decl), set(_lib.SIGNATURES) ^ set(decl)
+    for name, (ret, params) in decl.items():
+        args, res = _lib.SIGNATURES[name]
+        want = [ctype_of(p) for p in params]
+        assert len(args) == len(want), f"{name}: {len(args)} ctypes arguments, {len(want)} declared"
+        for i, (a, w) in enumerate(zip(args, want)):
+            assert a == w, f"{name} argument {i}: ctypes {a.__name__}, declared {params[i]}"
+        assert res == ctype_of(ret), f"{name}: returns {ret}"
 
 
 def test_abi_version_and_error_slot():
